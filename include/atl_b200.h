@@ -1,0 +1,164 @@
+/*
+ * atl_b200.h -- C ABI of libatlb200.so, the B200 (sm_100a) implementation of the anchored transport
+ * score path of KAVYANSHTYAGI/x (package `atl`).
+ *
+ * Conventions (the layout contract of the reference, csrc/atl_ops.h:3-8):
+ *   pos  (N,2) float32 [x, y], pixel centres at integers;  w (N) float32;  bidx (N) int64 in [0, B);
+ *   img  (B,H,W) float32.  All arrays are contiguous DEVICE pointers.  Events whose batch index lies
+ *   outside [0, B) or whose position is not finite touch no pixel (the reference read out of bounds).  Outputs are caller-allocated
+ *   and fully overwritten (the reference returned torch::zeros-initialised tensors).
+ * Every entry point returns 0 (ATLB_OK) or an error code; atlb_last_error() gives the message of the
+ * calling thread's last failure.  Work is enqueued on `stream`; an entry point documented as
+ * "synchronous" waits for `stream` because it must read a device result on the host (as the
+ * reference's torch code does with .item()-style reads).
+ * There is no CPU path: every entry point needs a CUDA device of compute capability 10.0.
+ */
+#ifndef ATL_B200_H
+#define ATL_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* atlb_stream_t; /* a cudaStream_t; NULL = legacy default stream */
+
+enum {
+  ATLB_OK = 0,
+  ATLB_ERR_ARG = 1,       /* invalid argument (null pointer, negative size, bad enum) */
+  ATLB_ERR_CUDA = 2,      /* a CUDA launch or runtime call failed */
+  ATLB_ERR_WORKSPACE = 3, /* workspace smaller than the matching *_workspace_bytes() */
+  ATLB_ERR_UNSORTED = 4,  /* events not sorted by (b, t); see atlb_window_counts */
+  ATLB_ERR_OVERFLOW = 5   /* a size does not fit the index types of the kernels */
+};
+
+/* Message of the calling thread's last non-zero status ("" if none). */
+const char* atlb_last_error(void);
+/* ABI version of this header (bumped on incompatible changes). */
+int atlb_abi_version(void);
+#define ATLB_ABI_VERSION 1
+/* Number of kernels this library has launched in the calling process (instrumentation; no reference
+ * counterpart). */
+uint64_t atlb_kernel_launches(void);
+/* Opt-in CUDA-event timing of the main kernels (instrumentation; no reference counterpart).  While
+ * enabled, each launch of a timed kernel ("k_pair_fwd", "k_pair_bwd", ...) is bracketed by events on
+ * its stream; atlb_timing_read waits for them and returns the summed milliseconds and launch count
+ * for `name` (reset != 0 forgets them). */
+int atlb_timing_enable(int on);
+int atlb_timing_read(const char* name, double* total_ms, int64_t* count, int reset);
+
+/* ----------------------------------------------------------------------------------------------
+ * Splat / gather / voxel.  Replace the reference's bound kernels
+ *   splat_bilinear_fwd/bwd  csrc/atl_cpu.cpp:38-76   (decl. csrc/atl_ops.h:20-21)
+ *   splat_gauss_fwd/bwd     csrc/atl_cpu.cpp:79-131  (decl. csrc/atl_ops.h:23-26)
+ *   gather_bilinear_fwd/bwd csrc/atl_cpu.cpp:134-172 (decl. csrc/atl_ops.h:28-29)
+ *   voxel_grid              csrc/atl_cpu.cpp:256-286 (decl. csrc/atl_ops.h:48-49)
+ * ---------------------------------------------------------------------------------------------- */
+int atlb_splat_bilinear_fwd(const float* pos, const float* w, const int64_t* bidx, int64_t N, int64_t B, int64_t H,
+                            int64_t W, float* img, atlb_stream_t stream);
+int atlb_splat_bilinear_bwd(const float* gimg, const float* pos, const float* w, const int64_t* bidx, int64_t N,
+                            int64_t B, int64_t H, int64_t W, float* gpos, float* gw, atlb_stream_t stream);
+int atlb_splat_gauss_fwd(const float* pos, const float* w, const int64_t* bidx, int64_t N, int64_t B, int64_t H,
+                         int64_t W, double sigma, int64_t radius, float* img, atlb_stream_t stream);
+int atlb_splat_gauss_bwd(const float* gimg, const float* pos, const float* w, const int64_t* bidx, int64_t N,
+                         int64_t B, int64_t H, int64_t W, double sigma, int64_t radius, float* gpos, float* gw,
+                         atlb_stream_t stream);
+int atlb_gather_bilinear_fwd(const float* img, const float* pos, const int64_t* bidx, int64_t N, int64_t B, int64_t H,
+                             int64_t W, float* out, atlb_stream_t stream);
+int atlb_gather_bilinear_bwd(const float* gval, const float* img, const float* pos, const int64_t* bidx, int64_t N,
+                             int64_t B, int64_t H, int64_t W, float* gimg, float* gpos, atlb_stream_t stream);
+int atlb_voxel_grid(const float* pos, const float* t, const float* p, const int64_t* bidx, int64_t N, int64_t B,
+                    int64_t C, int64_t H, int64_t W, float* vox, atlb_stream_t stream);
+
+/* ----------------------------------------------------------------------------------------------
+ * Pair plan: the device replacement of build_pair_plan (atl/ops/functional.py:132-178), in three
+ * calls because two sizes are only known on the device:
+ *   1. atlb_plan_geometry   vmax, anchor bounding box -> cell, origin, GW, GH    (synchronous)
+ *   2. atlb_plan_count      per-cell counts -> cell_start (B*S*GH*GW + 1), #entries (synchronous)
+ *   3. atlb_plan_fill       the sorted entries and the anchor cells               (asynchronous)
+ * Cell keys, CSR offsets, slice ranges and anchor cells are bit-identical to the reference's CPU
+ * path; entries inside one cell come in an unspecified order (the reference's argsort is unstable).
+ * ---------------------------------------------------------------------------------------------- */
+typedef struct {
+  double cell, ox, oy; /* cell size and grid origin (double, as the reference's Python computes them) */
+  int64_t GW, GH;      /* grid width / height in cells */
+  float vmax;          /* max_j |v_j| (torch's row norm) */
+  int32_t S;           /* number of slices */
+} atlb_plan_geom;
+
+/* x (N,2) positions, v (N,2) velocities, anchors (M) event indices, anchor_xy (M,2) the positions the
+ * anchors are evaluated at, or NULL for x[anchors].  scratch: device buffer of >= 32 bytes.  Fails with
+ * ATLB_ERR_ARG if an anchor index lies outside [0, N).  Replaces functional.py:136-149. */
+int atlb_plan_geometry(const float* x, const float* v, int64_t N, const int64_t* anchors, const float* anchor_xy,
+                       int64_t M, int64_t H, int64_t W, double h, double cut, int64_t S, void* scratch,
+                       atlb_plan_geom* geom_out, atlb_stream_t stream);
+size_t atlb_plan_workspace_bytes(int64_t ncell);
+/* cell_start: int64[ncell + 1] with ncell = B*S*GH*GW.  *n_entries_out receives cell_start[ncell].
+ * workspace must stay untouched until atlb_plan_fill.  Replaces functional.py:150-168. */
+int atlb_plan_count(const float* x, const float* t, const float* v, const int64_t* b, int64_t N, int64_t B, double tau,
+                    const atlb_plan_geom* geom, int64_t* cell_start, void* workspace, size_t workspace_bytes,
+                    int64_t* n_entries_out, atlb_stream_t stream);
+/* anchors (M) event indices; anchor_xy (M,2) or NULL (= x[anchors]).  Outputs as PairPlan
+ * (functional.py:114-129): src_y/src_v (Ns,2), src_t (Ns), src_id (Ns) int64, anc_x (M,2), anc_t (M),
+ * anc_cell (M,3) int64, anc_id (M) int64, slice_c (S).  Replaces functional.py:150-178. */
+int atlb_plan_fill(const float* x, const float* t, const float* v, const int64_t* b, int64_t N, int64_t B, double tau,
+                   const atlb_plan_geom* geom, const int64_t* anchors, const float* anchor_xy, int64_t M,
+                   const int64_t* cell_start, void* workspace, size_t workspace_bytes, float* src_y, float* src_v,
+                   float* src_t, int64_t* src_id, float* anc_x, float* anc_t, int64_t* anc_cell, int64_t* anc_id,
+                   float* slice_c, atlb_stream_t stream);
+
+/* ----------------------------------------------------------------------------------------------
+ * Anchored pair sums over a plan.  Replace ats_pair_fwd / ats_pair_bwd
+ *   csrc/atl_cpu.cpp:203-253 (decl. csrc/atl_ops.h:35-46; bound at csrc/atl_cpu.cpp:312-320).
+ * Arguments are the plan arrays in the reference's layout; ncell = length(cell_start) - 1 and
+ * Ns = cell_start[ncell].  The workspace holds the anchors bucketed by cell.
+ * ---------------------------------------------------------------------------------------------- */
+size_t atlb_pair_workspace_bytes(int64_t M, int64_t ncell);
+int atlb_ats_pair_fwd(const float* src_y, const float* src_v, const float* src_t, const int64_t* src_id,
+                      const int64_t* cell_start, const float* anc_x, const float* anc_t, const int64_t* anc_cell,
+                      const int64_t* anc_id, const float* slice_c, int64_t Ns, int64_t M, int64_t ncell, int64_t S,
+                      int64_t GH, int64_t GW, double h, double tau, double cut, float* out, void* workspace,
+                      size_t workspace_bytes, atlb_stream_t stream);
+/* gv (N,2): gradient of sum_i gS_i S_i w.r.t. the per-event velocities. */
+int atlb_ats_pair_bwd(const float* gS, const float* src_y, const float* src_v, const float* src_t,
+                      const int64_t* src_id, const int64_t* cell_start, const float* anc_x, const float* anc_t,
+                      const int64_t* anc_cell, const int64_t* anc_id, const float* slice_c, int64_t Ns, int64_t M,
+                      int64_t ncell, int64_t S, int64_t GH, int64_t GW, double h, double tau, double cut, int64_t N,
+                      float* gv, void* workspace, size_t workspace_bytes, atlb_stream_t stream);
+
+/* ----------------------------------------------------------------------------------------------
+ * window_counts (atl/ops/functional.py:210-217): out[q] = #{j != idx[q], same batch,
+ * |t_j - t_idx[q]| <= tau} through float64 keys b*4 + t.  Events must be sorted by (b, t) (the
+ * EventPacket invariant, atl/core/events.py:12); the call checks it on the device and returns
+ * ATLB_ERR_UNSORTED without a result otherwise (synchronous).  For unsorted events pass the sorted
+ * float64 keys instead to atlb_window_counts_keys.
+ * ---------------------------------------------------------------------------------------------- */
+int atlb_window_counts(const float* t, const int64_t* b, int64_t N, const int64_t* idx, int64_t M, double tau,
+                       float* out, void* scratch, atlb_stream_t stream);
+int atlb_window_counts_keys(const double* sorted_keys, int64_t N, const float* t, const int64_t* b,
+                            const int64_t* idx, int64_t M, double tau, float* out, atlb_stream_t stream);
+
+/* ----------------------------------------------------------------------------------------------
+ * Motion fields of stage 1 (velocity linear at the event) and the exposure correction.
+ *   kind 0 Translation  theta (B,2)        atl/motion/parametric.py:148-157
+ *   kind 1 Affine       theta (B,6)        atl/motion/parametric.py:207-217
+ *   kind 2 DenseLinearFlow grid (B,2,Hg,Wg) atl/motion/parametric.py:257-312 (sample_grid)
+ * ---------------------------------------------------------------------------------------------- */
+enum { ATLB_MOTION_TRANSLATION = 0, ATLB_MOTION_AFFINE = 1, ATLB_MOTION_DENSE = 2 };
+int atlb_velocity(int kind, const float* theta, int64_t B, int64_t Hg, int64_t Wg, int64_t H, int64_t W,
+                  const float* xy, const int64_t* b, int64_t N, float* v, atlb_stream_t stream);
+/* gtheta (same shape as theta) = d(sum_j gv_j . v_j)/d theta; overwritten. */
+int atlb_velocity_bwd(int kind, const float* gv, int64_t B, int64_t Hg, int64_t Wg, int64_t H, int64_t W,
+                      const float* xy, const int64_t* b, int64_t N, float* gtheta, atlb_stream_t stream);
+/* visible_fraction (atl/objectives/ats.py:31-50) for linear transport; scratch >= B*n_check*4 bytes. */
+int atlb_visible_fraction(int kind, const float* theta, int64_t B, int64_t Hg, int64_t Wg, int64_t H, int64_t W,
+                          const float* xa, const float* ta, const int64_t* ba, int64_t M, const float* t,
+                          const int64_t* b, int64_t N, double tau, int64_t n_check, float* out, void* scratch,
+                          atlb_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* ATL_B200_H */

@@ -1,0 +1,332 @@
+// extern "C" boundary of libatlb200.so (declarations and reference citations in include/atl_b200.h).
+// Validates arguments, forwards to the kernels' launchers and turns CUDA errors into status codes.
+#include <stdarg.h>
+#include <stdio.h>
+
+#include "common.cuh"
+#include "motion_math.cuh"
+#include "plan_math.cuh"
+
+namespace atlb {
+
+static thread_local char g_err[512] = "";
+std::atomic<unsigned long long> g_launches{0};
+
+void set_error(const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+}
+
+int launch_status(const char* what) {
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_error("%s: %s", what, cudaGetErrorString(e));
+    return ATLB_ERR_CUDA;
+  }
+  return ATLB_OK;
+}
+
+// launchers (plan.cu, pair.cu, splat.cu, motion.cu)
+int plan_geometry(const float*, const float*, long long, const long long*, const float*, long long, long long,
+                  long long, double, double, long long, void*, atlb_plan_geom*, cudaStream_t);
+size_t plan_workspace_bytes(long long ncell);
+int plan_count(const float*, const float*, const float*, const long long*, long long, long long, double,
+               const atlb_plan_geom*, long long*, void*, long long*, cudaStream_t);
+int plan_fill(const float*, const float*, const float*, const long long*, long long, long long, double,
+              const atlb_plan_geom*, const long long*, const float*, long long, const long long*, void*, float*,
+              float*, float*, long long*, float*, float*, long long*, long long*, float*, cudaStream_t);
+size_t pair_workspace_bytes(long long M, long long ncell);
+int pair_fwd(const float*, const float*, const float*, const long long*, const long long*, const float*, const float*,
+             const long long*, const long long*, const float*, long long, long long, long long, long long, long long,
+             double, double, double, float*, void*, cudaStream_t);
+int pair_bwd(const float*, const float*, const float*, const float*, const long long*, const long long*, const float*,
+             const float*, const long long*, const long long*, const float*, long long, long long, long long,
+             long long, long long, double, double, double, long long, float*, void*, cudaStream_t);
+int splat_bilinear_fwd(const float*, const float*, const long long*, long long, long long, long long, long long,
+                       float*, cudaStream_t);
+int splat_bilinear_bwd(const float*, const float*, const float*, const long long*, long long, long long, long long,
+                       long long, float*, float*, cudaStream_t);
+int splat_gauss_fwd(const float*, const float*, const long long*, long long, long long, long long, long long, double,
+                    long long, float*, cudaStream_t);
+int splat_gauss_bwd(const float*, const float*, const float*, const long long*, long long, long long, long long,
+                    long long, double, long long, float*, float*, cudaStream_t);
+int gather_fwd(const float*, const float*, const long long*, long long, long long, long long, long long, float*,
+               cudaStream_t);
+int gather_bwd(const float*, const float*, const float*, const long long*, long long, long long, long long, long long,
+               float*, float*, cudaStream_t);
+int voxel_grid(const float*, const float*, const float*, const long long*, long long, long long, long long, long long,
+               long long, float*, cudaStream_t);
+int velocity(const MotionView&, const float*, const long long*, long long, float*, cudaStream_t);
+int velocity_bwd(const MotionView&, const float*, const float*, const long long*, long long, float*, cudaStream_t);
+int visible_fraction(const MotionView&, const float*, const float*, const long long*, long long, const float*,
+                     const long long*, long long, double, long long, float*, void*, cudaStream_t);
+int window_counts(const float*, const long long*, long long, const long long*, long long, double, float*, void*,
+                  cudaStream_t);
+int window_counts_keys(const double*, long long, const float*, const long long*, const long long*, long long, double,
+                       float*, cudaStream_t);
+
+}  // namespace atlb
+
+using namespace atlb;
+
+#define LL(p) reinterpret_cast<const long long*>(p)
+#define LLW(p) reinterpret_cast<long long*>(p)
+#define STREAM(s) reinterpret_cast<cudaStream_t>(s)
+
+// A pointer may only be NULL when the array it stands for is empty.
+#define NEED(ptr, n)                                                        \
+  do {                                                                      \
+    if ((n) > 0 && (ptr) == nullptr) {                                      \
+      set_error("%s: %s is NULL for a non-empty array", __func__, #ptr);    \
+      return ATLB_ERR_ARG;                                                  \
+    }                                                                       \
+  } while (0)
+#define NONNEG(x)                                                           \
+  do {                                                                      \
+    if ((x) < 0) {                                                          \
+      set_error("%s: %s = %lld is negative", __func__, #x, (long long)(x)); \
+      return ATLB_ERR_ARG;                                                  \
+    }                                                                       \
+  } while (0)
+
+static int clear() {
+  g_err[0] = 0;
+  return ATLB_OK;
+}
+
+static int check_kind(int kind, const char* fn) {
+  if (kind != ATLB_MOTION_TRANSLATION && kind != ATLB_MOTION_AFFINE && kind != ATLB_MOTION_DENSE) {
+    set_error("%s: unknown motion kind %d", fn, kind);
+    return ATLB_ERR_ARG;
+  }
+  return ATLB_OK;
+}
+
+extern "C" {
+
+const char* atlb_last_error(void) { return g_err; }
+int atlb_abi_version(void) { return ATLB_ABI_VERSION; }
+uint64_t atlb_kernel_launches(void) { return g_launches.load(std::memory_order_relaxed); }
+
+int atlb_splat_bilinear_fwd(const float* pos, const float* w, const int64_t* bidx, int64_t N, int64_t B, int64_t H,
+                            int64_t W, float* img, atlb_stream_t stream) {
+  clear();
+  NONNEG(N); NONNEG(B); NONNEG(H); NONNEG(W);
+  NEED(pos, N); NEED(w, N); NEED(bidx, N); NEED(img, B * H * W);
+  return splat_bilinear_fwd(pos, w, LL(bidx), N, B, H, W, img, STREAM(stream));
+}
+
+int atlb_splat_bilinear_bwd(const float* gimg, const float* pos, const float* w, const int64_t* bidx, int64_t N,
+                            int64_t B, int64_t H, int64_t W, float* gpos, float* gw, atlb_stream_t stream) {
+  clear();
+  NONNEG(N); NONNEG(B); NONNEG(H); NONNEG(W);
+  NEED(gimg, N); NEED(pos, N); NEED(w, N); NEED(bidx, N); NEED(gpos, N); NEED(gw, N);
+  return splat_bilinear_bwd(gimg, pos, w, LL(bidx), N, B, H, W, gpos, gw, STREAM(stream));
+}
+
+int atlb_splat_gauss_fwd(const float* pos, const float* w, const int64_t* bidx, int64_t N, int64_t B, int64_t H,
+                         int64_t W, double sigma, int64_t radius, float* img, atlb_stream_t stream) {
+  clear();
+  NONNEG(N); NONNEG(B); NONNEG(H); NONNEG(W); NONNEG(radius);
+  NEED(pos, N); NEED(w, N); NEED(bidx, N); NEED(img, B * H * W);
+  return splat_gauss_fwd(pos, w, LL(bidx), N, B, H, W, sigma, radius, img, STREAM(stream));
+}
+
+int atlb_splat_gauss_bwd(const float* gimg, const float* pos, const float* w, const int64_t* bidx, int64_t N,
+                         int64_t B, int64_t H, int64_t W, double sigma, int64_t radius, float* gpos, float* gw,
+                         atlb_stream_t stream) {
+  clear();
+  NONNEG(N); NONNEG(B); NONNEG(H); NONNEG(W); NONNEG(radius);
+  NEED(gimg, N); NEED(pos, N); NEED(w, N); NEED(bidx, N); NEED(gpos, N); NEED(gw, N);
+  return splat_gauss_bwd(gimg, pos, w, LL(bidx), N, B, H, W, sigma, radius, gpos, gw, STREAM(stream));
+}
+
+int atlb_gather_bilinear_fwd(const float* img, const float* pos, const int64_t* bidx, int64_t N, int64_t B, int64_t H,
+                             int64_t W, float* out, atlb_stream_t stream) {
+  clear();
+  NONNEG(N); NONNEG(B); NONNEG(H); NONNEG(W);
+  NEED(img, N); NEED(pos, N); NEED(bidx, N); NEED(out, N);
+  return gather_fwd(img, pos, LL(bidx), N, B, H, W, out, STREAM(stream));
+}
+
+int atlb_gather_bilinear_bwd(const float* gval, const float* img, const float* pos, const int64_t* bidx, int64_t N,
+                             int64_t B, int64_t H, int64_t W, float* gimg, float* gpos, atlb_stream_t stream) {
+  clear();
+  NONNEG(N); NONNEG(B); NONNEG(H); NONNEG(W);
+  NEED(gval, N); NEED(img, N); NEED(pos, N); NEED(bidx, N); NEED(gimg, B * H * W); NEED(gpos, N);
+  return gather_bwd(gval, img, pos, LL(bidx), N, B, H, W, gimg, gpos, STREAM(stream));
+}
+
+int atlb_voxel_grid(const float* pos, const float* t, const float* p, const int64_t* bidx, int64_t N, int64_t B,
+                    int64_t C, int64_t H, int64_t W, float* vox, atlb_stream_t stream) {
+  clear();
+  NONNEG(N); NONNEG(B); NONNEG(C); NONNEG(H); NONNEG(W);
+  NEED(pos, N); NEED(t, N); NEED(p, N); NEED(bidx, N); NEED(vox, B * C * H * W);
+  return voxel_grid(pos, t, p, LL(bidx), N, B, C, H, W, vox, STREAM(stream));
+}
+
+int atlb_plan_geometry(const float* x, const float* v, int64_t N, const int64_t* anchors, const float* anchor_xy,
+                       int64_t M, int64_t H, int64_t W, double h, double cut, int64_t S, void* scratch,
+                       atlb_plan_geom* geom_out, atlb_stream_t stream) {
+  clear();
+  NONNEG(N); NONNEG(M); NONNEG(H); NONNEG(W);
+  NEED(x, N); NEED(v, N); NEED(anchors, M);
+  if (S < 1 || S > (1 << 20)) { set_error("atlb_plan_geometry: n_slices = %lld", (long long)S); return ATLB_ERR_ARG; }
+  if (!scratch || !geom_out) { set_error("atlb_plan_geometry: scratch / geom_out is NULL"); return ATLB_ERR_ARG; }
+  const int st = plan_geometry(x, v, N, LL(anchors), anchor_xy, M, H, W, h, cut, S, scratch, geom_out, STREAM(stream));
+  if (st) return st;
+  if (!(geom_out->cell > 0) || geom_out->GW <= 0 || geom_out->GH <= 0 || geom_out->GW > (1LL << 31) ||
+      geom_out->GH > (1LL << 31)) {
+    set_error("atlb_plan_geometry: degenerate grid (cell %g, %lld x %lld cells); non-finite inputs?", geom_out->cell,
+              (long long)geom_out->GW, (long long)geom_out->GH);
+    return ATLB_ERR_OVERFLOW;
+  }
+  return ATLB_OK;
+}
+
+size_t atlb_plan_workspace_bytes(int64_t ncell) { return plan_workspace_bytes(ncell < 0 ? 0 : ncell); }
+
+static int check_geom(const atlb_plan_geom* g, int64_t B, const char* fn) {
+  if (!g || g->S < 1 || g->GW <= 0 || g->GH <= 0) { set_error("%s: invalid geometry", fn); return ATLB_ERR_ARG; }
+  const double ncell = (double)B * g->S * (double)g->GH * (double)g->GW;
+  if (ncell > 2.0e9) {
+    set_error("%s: %.3g cells exceed the int32 cursor range", fn, ncell);
+    return ATLB_ERR_OVERFLOW;
+  }
+  return ATLB_OK;
+}
+
+int atlb_plan_count(const float* x, const float* t, const float* v, const int64_t* b, int64_t N, int64_t B, double tau,
+                    const atlb_plan_geom* geom, int64_t* cell_start, void* workspace, size_t workspace_bytes,
+                    int64_t* n_entries_out, atlb_stream_t stream) {
+  clear();
+  NONNEG(N); NONNEG(B);
+  NEED(x, N); NEED(t, N); NEED(v, N); NEED(b, N);
+  if (int st = check_geom(geom, B, __func__)) return st;
+  const long long ncell = B * (long long)geom->S * geom->GH * geom->GW;
+  if (!cell_start || !n_entries_out) { set_error("atlb_plan_count: NULL output"); return ATLB_ERR_ARG; }
+  if (!workspace || workspace_bytes < plan_workspace_bytes(ncell)) {
+    set_error("atlb_plan_count: workspace %zu < %zu bytes", workspace_bytes, plan_workspace_bytes(ncell));
+    return ATLB_ERR_WORKSPACE;
+  }
+  return plan_count(x, t, v, LL(b), N, B, tau, geom, LLW(cell_start), workspace, LLW(n_entries_out), STREAM(stream));
+}
+
+int atlb_plan_fill(const float* x, const float* t, const float* v, const int64_t* b, int64_t N, int64_t B, double tau,
+                   const atlb_plan_geom* geom, const int64_t* anchors, const float* anchor_xy, int64_t M,
+                   const int64_t* cell_start, void* workspace, size_t workspace_bytes, float* src_y, float* src_v,
+                   float* src_t, int64_t* src_id, float* anc_x, float* anc_t, int64_t* anc_cell, int64_t* anc_id,
+                   float* slice_c, atlb_stream_t stream) {
+  clear();
+  NONNEG(N); NONNEG(B); NONNEG(M);
+  NEED(x, N); NEED(t, N); NEED(v, N); NEED(b, N); NEED(anchors, M);
+  NEED(anc_x, M); NEED(anc_t, M); NEED(anc_cell, M); NEED(anc_id, M);
+  if (int st = check_geom(geom, B, __func__)) return st;
+  const long long ncell = B * (long long)geom->S * geom->GH * geom->GW;
+  if (!cell_start || !slice_c) { set_error("atlb_plan_fill: NULL cell_start / slice_c"); return ATLB_ERR_ARG; }
+  if (N > 0 && (!src_y || !src_v || !src_t || !src_id)) { set_error("atlb_plan_fill: NULL entry array"); return ATLB_ERR_ARG; }
+  if (!workspace || workspace_bytes < plan_workspace_bytes(ncell)) {
+    set_error("atlb_plan_fill: workspace %zu < %zu bytes", workspace_bytes, plan_workspace_bytes(ncell));
+    return ATLB_ERR_WORKSPACE;
+  }
+  return plan_fill(x, t, v, LL(b), N, B, tau, geom, LL(anchors), anchor_xy, M, LL(cell_start), workspace, src_y,
+                   src_v, src_t, LLW(src_id), anc_x, anc_t, LLW(anc_cell), LLW(anc_id), slice_c, STREAM(stream));
+}
+
+size_t atlb_pair_workspace_bytes(int64_t M, int64_t ncell) {
+  return pair_workspace_bytes(M < 0 ? 0 : M, ncell < 0 ? 0 : ncell);
+}
+
+static int check_pair(const int64_t* cell_start, const float* slice_c, int64_t Ns, int64_t M, int64_t ncell, int64_t S,
+                      int64_t GH, int64_t GW, void* ws, size_t ws_bytes, const char* fn) {
+  if (Ns < 0 || M < 0 || ncell < 0 || S < 1 || GH < 0 || GW < 0) { set_error("%s: negative size", fn); return ATLB_ERR_ARG; }
+  if (!cell_start || !slice_c) { set_error("%s: NULL cell_start / slice_c", fn); return ATLB_ERR_ARG; }
+  if (M > (1LL << 31) - 1 || ncell > (1LL << 31) - 2) { set_error("%s: too many anchors / cells", fn); return ATLB_ERR_OVERFLOW; }
+  if (!ws || ws_bytes < pair_workspace_bytes(M, ncell)) {
+    set_error("%s: workspace %zu < %zu bytes", fn, ws_bytes, pair_workspace_bytes(M, ncell));
+    return ATLB_ERR_WORKSPACE;
+  }
+  return ATLB_OK;
+}
+
+int atlb_ats_pair_fwd(const float* src_y, const float* src_v, const float* src_t, const int64_t* src_id,
+                      const int64_t* cell_start, const float* anc_x, const float* anc_t, const int64_t* anc_cell,
+                      const int64_t* anc_id, const float* slice_c, int64_t Ns, int64_t M, int64_t ncell, int64_t S,
+                      int64_t GH, int64_t GW, double h, double tau, double cut, float* out, void* workspace,
+                      size_t workspace_bytes, atlb_stream_t stream) {
+  clear();
+  if (int st = check_pair(cell_start, slice_c, Ns, M, ncell, S, GH, GW, workspace, workspace_bytes, __func__)) return st;
+  NEED(src_y, Ns); NEED(src_v, Ns); NEED(src_t, Ns); NEED(src_id, Ns);
+  NEED(anc_x, M); NEED(anc_t, M); NEED(anc_cell, M); NEED(anc_id, M); NEED(out, M);
+  return pair_fwd(src_y, src_v, src_t, LL(src_id), LL(cell_start), anc_x, anc_t, LL(anc_cell), LL(anc_id), slice_c, M,
+                  ncell, S, GH, GW, h, tau, cut, out, workspace, STREAM(stream));
+}
+
+int atlb_ats_pair_bwd(const float* gS, const float* src_y, const float* src_v, const float* src_t,
+                      const int64_t* src_id, const int64_t* cell_start, const float* anc_x, const float* anc_t,
+                      const int64_t* anc_cell, const int64_t* anc_id, const float* slice_c, int64_t Ns, int64_t M,
+                      int64_t ncell, int64_t S, int64_t GH, int64_t GW, double h, double tau, double cut, int64_t N,
+                      float* gv, void* workspace, size_t workspace_bytes, atlb_stream_t stream) {
+  clear();
+  if (int st = check_pair(cell_start, slice_c, Ns, M, ncell, S, GH, GW, workspace, workspace_bytes, __func__)) return st;
+  NONNEG(N);
+  NEED(gS, M); NEED(src_y, Ns); NEED(src_v, Ns); NEED(src_t, Ns); NEED(src_id, Ns);
+  NEED(anc_x, M); NEED(anc_t, M); NEED(anc_cell, M); NEED(anc_id, M); NEED(gv, N);
+  return pair_bwd(gS, src_y, src_v, src_t, LL(src_id), LL(cell_start), anc_x, anc_t, LL(anc_cell), LL(anc_id), slice_c,
+                  M, ncell, S, GH, GW, h, tau, cut, N, gv, workspace, STREAM(stream));
+}
+
+int atlb_window_counts(const float* t, const int64_t* b, int64_t N, const int64_t* idx, int64_t M, double tau,
+                       float* out, void* scratch, atlb_stream_t stream) {
+  clear();
+  NONNEG(N); NONNEG(M);
+  NEED(t, N); NEED(b, N); NEED(idx, M); NEED(out, M);
+  if (!scratch) { set_error("atlb_window_counts: scratch is NULL"); return ATLB_ERR_ARG; }
+  return window_counts(t, LL(b), N, LL(idx), M, tau, out, scratch, STREAM(stream));
+}
+
+int atlb_window_counts_keys(const double* sorted_keys, int64_t N, const float* t, const int64_t* b,
+                            const int64_t* idx, int64_t M, double tau, float* out, atlb_stream_t stream) {
+  clear();
+  NONNEG(N); NONNEG(M);
+  NEED(sorted_keys, N); NEED(t, N); NEED(b, N); NEED(idx, M); NEED(out, M);
+  return window_counts_keys(sorted_keys, N, t, LL(b), LL(idx), M, tau, out, STREAM(stream));
+}
+
+int atlb_velocity(int kind, const float* theta, int64_t B, int64_t Hg, int64_t Wg, int64_t H, int64_t W,
+                  const float* xy, const int64_t* b, int64_t N, float* v, atlb_stream_t stream) {
+  clear();
+  if (int st = check_kind(kind, __func__)) return st;
+  NONNEG(B); NONNEG(N);
+  if (kind == ATLB_MOTION_DENSE && (Hg < 1 || Wg < 1)) { set_error("atlb_velocity: empty grid"); return ATLB_ERR_ARG; }
+  NEED(theta, B); NEED(xy, N); NEED(b, N); NEED(v, N);
+  return velocity(make_motion_view(kind, theta, B, Hg, Wg, H, W), xy, LL(b), N, v, STREAM(stream));
+}
+
+int atlb_velocity_bwd(int kind, const float* gv, int64_t B, int64_t Hg, int64_t Wg, int64_t H, int64_t W,
+                      const float* xy, const int64_t* b, int64_t N, float* gtheta, atlb_stream_t stream) {
+  clear();
+  if (int st = check_kind(kind, __func__)) return st;
+  NONNEG(B); NONNEG(N);
+  if (kind == ATLB_MOTION_DENSE && (Hg < 1 || Wg < 1)) { set_error("atlb_velocity_bwd: empty grid"); return ATLB_ERR_ARG; }
+  NEED(gv, N); NEED(xy, N); NEED(b, N); NEED(gtheta, B);
+  return velocity_bwd(make_motion_view(kind, nullptr, B, Hg, Wg, H, W), gv, xy, LL(b), N, gtheta, STREAM(stream));
+}
+
+int atlb_visible_fraction(int kind, const float* theta, int64_t B, int64_t Hg, int64_t Wg, int64_t H, int64_t W,
+                          const float* xa, const float* ta, const int64_t* ba, int64_t M, const float* t,
+                          const int64_t* b, int64_t N, double tau, int64_t n_check, float* out, void* scratch,
+                          atlb_stream_t stream) {
+  clear();
+  if (int st = check_kind(kind, __func__)) return st;
+  NONNEG(B); NONNEG(M); NONNEG(N);
+  if (n_check < 1 || n_check > 4096) { set_error("atlb_visible_fraction: n_check = %lld", (long long)n_check); return ATLB_ERR_ARG; }
+  NEED(theta, B); NEED(xa, M); NEED(ta, M); NEED(ba, M); NEED(t, N); NEED(b, N); NEED(out, M);
+  if (!scratch) { set_error("atlb_visible_fraction: scratch is NULL"); return ATLB_ERR_ARG; }
+  return visible_fraction(make_motion_view(kind, theta, B, Hg, Wg, H, W), xa, ta, LL(ba), M, t, LL(b), N, tau, n_check,
+                          out, scratch, STREAM(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,48 @@
+// The pair test and kernel of the anchored sum (csrc/atl_cpu.cpp:181-196), rounding-exact.
+#pragma once
+#include "common.cuh"
+
+namespace atlb {
+
+struct PairConsts {
+  float tau;     // (float)tau
+  float r2max;   // cut*cut*h*h in fp32, left to right (atl_cpu.cpp:184)
+  float inv2h2;  // 1 / (2 h h) in fp32 (atl_cpu.cpp:184)
+  float invh2;   // 1 / (float)(h*h)   (atl_cpu.cpp:236)
+};
+
+inline PairConsts make_pair_consts(double h, double tau, double cut) {
+  const float hf = (float)h, cf = (float)cut;
+  PairConsts C;
+  C.tau = (float)tau;
+  volatile float r = cf * cf;  // volatile: keep the reference's left-to-right rounding order
+  r = r * hf;
+  r = r * hf;
+  C.r2max = r;
+  volatile float d = 2.f * hf;
+  d = d * hf;
+  C.inv2h2 = 1.f / d;
+  C.invh2 = 1.f / (float)(h * h);
+  return C;
+}
+
+// dt = t_i - t_j; r = x_i - (y_j + v_j (t_i - c_s)); accepted iff |dt| <= tau and |r|^2 <= r2max.
+// NaN inputs are accepted, as the reference's "skip if greater" tests accept them.
+__device__ __forceinline__ bool pair_test(const PairConsts& C, float xi, float yi, float ti, float dti, float2 sy,
+                                          float2 sv, float st, float* rx, float* ry, float* d2, float* dt) {
+  *dt = sub_rn(ti, st);
+  if (fabsf(*dt) > C.tau) return false;
+  *rx = sub_rn(xi, add_rn(sy.x, mul_rn(sv.x, dti)));
+  *ry = sub_rn(yi, add_rn(sy.y, mul_rn(sv.y, dti)));
+  *d2 = add_rn(mul_rn(*rx, *rx), mul_rn(*ry, *ry));
+  return !(*d2 > C.r2max);
+}
+
+__device__ __forceinline__ float pair_kernel(const PairConsts& C, float d2) { return expf(mul_rn(-d2, C.inv2h2)); }
+
+// f = gS_i * k * dt / h^2, in the reference's order (atl_cpu.cpp:244).
+__device__ __forceinline__ float pair_grad_factor(const PairConsts& C, float gi, float kern, float dt) {
+  return mul_rn(mul_rn(mul_rn(gi, kern), dt), C.invh2);
+}
+
+}  // namespace atlb

@@ -1,0 +1,118 @@
+// Exclusive prefix sum of per-cell int32 counts -> CSR offsets, in three launches:
+//   partials (one sum per 4096-item chunk) -> scan of the partials (one CTA) -> chunk scan + offset.
+// The counts are zeroed on the way so that the same array serves as the per-cell cursor of the
+// scatter pass that follows (pos = offset[key] + atomicAdd(&counts[key], 1)).
+#pragma once
+#include "common.cuh"
+
+namespace atlb {
+namespace {  // per translation unit: every .cu that scans gets its own copy of the kernels
+
+constexpr int kScanThreads = 1024;
+constexpr int kScanItems = 4;
+constexpr long long kScanChunk = (long long)kScanThreads * kScanItems;
+
+inline long long scan_nchunks(long long n) { return (n + kScanChunk - 1) / kScanChunk; }
+inline size_t scan_partials_bytes(long long n) { return (size_t)(scan_nchunks(n) + 1) * sizeof(long long); }
+
+__device__ __forceinline__ long long block_exclusive_scan(long long v, long long* smem_warp, long long* total) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  long long incl = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const long long u = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += u;
+  }
+  if (lane == 31) smem_warp[wid] = incl;
+  __syncthreads();
+  if (wid == 0) {
+    const int nw = blockDim.x >> 5;
+    long long w = lane < nw ? smem_warp[lane] : 0;
+    long long wi = w;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const long long u = __shfl_up_sync(0xffffffffu, wi, o);
+      if (lane >= o) wi += u;
+    }
+    if (lane < nw) smem_warp[lane] = wi - w;
+    if (lane == nw - 1) smem_warp[32] = wi;
+  }
+  __syncthreads();
+  const long long out = smem_warp[wid] + incl - v;
+  if (total) *total = smem_warp[32];
+  __syncthreads();
+  return out;
+}
+
+__global__ void __launch_bounds__(kScanThreads) k_scan_partials(const int* __restrict__ counts, long long n,
+                                                                long long* __restrict__ partials) {
+  __shared__ long long sw[33];
+  const long long base = blockIdx.x * kScanChunk;
+  long long s = 0;
+#pragma unroll
+  for (int q = 0; q < kScanItems; ++q) {
+    const long long i = base + (long long)q * kScanThreads + threadIdx.x;
+    if (i < n) s += counts[i];
+  }
+  long long tot;
+  block_exclusive_scan(s, sw, &tot);
+  if (threadIdx.x == 0) partials[blockIdx.x] = tot;
+}
+
+__global__ void __launch_bounds__(kScanThreads) k_scan_partials_scan(long long* __restrict__ partials, long long nchunks) {
+  __shared__ long long sw[33];
+  long long carry = 0;
+  for (long long base = 0; base < nchunks; base += kScanThreads) {
+    const long long i = base + threadIdx.x;
+    const long long v = i < nchunks ? partials[i] : 0;
+    long long tot;
+    const long long ex = block_exclusive_scan(v, sw, &tot);
+    if (i < nchunks) partials[i] = carry + ex;
+    carry += tot;
+  }
+  if (threadIdx.x == 0) partials[nchunks] = carry;
+}
+
+// offsets[i] = exclusive prefix (OutT = long long or int); offsets[n] = total; counts[i] = 0.
+template <typename OutT>
+__global__ void __launch_bounds__(kScanThreads) k_scan_final(int* __restrict__ counts, long long n,
+                                                             const long long* __restrict__ partials,
+                                                             OutT* __restrict__ offsets) {
+  __shared__ long long sw[33];
+  const long long base = blockIdx.x * kScanChunk + (long long)threadIdx.x * kScanItems;
+  long long v[kScanItems];
+  long long s = 0;
+#pragma unroll
+  for (int q = 0; q < kScanItems; ++q) {
+    const long long i = base + q;
+    v[q] = i < n ? counts[i] : 0;
+    s += v[q];
+  }
+  long long ex = block_exclusive_scan(s, sw, nullptr) + partials[blockIdx.x];
+#pragma unroll
+  for (int q = 0; q < kScanItems; ++q) {
+    const long long i = base + q;
+    if (i < n) {
+      offsets[i] = (OutT)ex;
+      counts[i] = 0;
+    }
+    ex += v[q];
+  }
+  if (blockIdx.x == 0 && threadIdx.x == 0) offsets[n] = (OutT)partials[gridDim.x];
+}
+
+// counts[0..n) -> offsets[0..n] (exclusive, offsets[n] = total); counts zeroed.
+template <typename OutT>
+inline void exclusive_scan(int* counts, long long n, long long* partials, OutT* offsets, cudaStream_t s) {
+  const long long nch = scan_nchunks(n);
+  if (nch == 0) {
+    cudaMemsetAsync(offsets, 0, sizeof(OutT), s);
+    return;
+  }
+  launch(k_scan_partials, (unsigned)nch, kScanThreads, 0, s, counts, n, partials);
+  launch(k_scan_partials_scan, 1, kScanThreads, 0, s, partials, nch);
+  launch(k_scan_final<OutT>, (unsigned)nch, kScanThreads, 0, s, counts, n, partials, offsets);
+}
+
+}  // namespace
+}  // namespace atlb

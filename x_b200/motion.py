@@ -1,0 +1,214 @@
+"""Motion models of stage 1 -- mirror of atl/motion/{base,parametric}.py for the models on the path.
+
+``Translation``, ``Affine`` and ``DenseLinearFlow`` evaluate their velocity field (and its gradient
+w.r.t. ``theta`` / the flow grid) in libatlb200 kernels that round exactly like the reference's torch
+CPU ops, so the pair plan built from the velocities is bit-identical.  ``transport`` in
+``mode="linear"`` is x + v(x) (t' - t); ``mode="exact"`` keeps the reference's closed-form matrix
+exponential (affine fields) or RK4 (dense fields) in torch ops on the device.
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+from torch import nn
+
+from . import _lib as L
+
+
+def as_time(t_dst, like: torch.Tensor) -> torch.Tensor:
+    """Broadcast a scalar or tensor target time to the shape of ``like`` (atl/motion/base.py:57-61)."""
+    if torch.is_tensor(t_dst):
+        return t_dst.to(like.dtype).expand_as(like) if t_dst.dim() == 0 else t_dst.to(like.dtype)
+    return torch.full_like(like, float(t_dst))
+
+
+class Motion(nn.Module):
+    """Base class (atl/motion/base.py:21-54)."""
+    linear_at_event: bool = False
+
+    def transport(self, xy, t, t_dst, b):
+        raise NotImplementedError
+
+    def velocity(self, xy, t, b):
+        raise NotImplementedError(f"{type(self).__name__} has no per-event velocity")
+
+    def transport_logdet(self, xy, t, t_dst, b, delta: float = 0.5):
+        """Transport plus log|det d transport / d xy| by central differences (base.py:43-50)."""
+        y = self.transport(xy, t, t_dst, b)
+        ex = xy.new_tensor([delta, 0.0]); ey = xy.new_tensor([0.0, delta])
+        jx = (self.transport(xy + ex, t, t_dst, b) - self.transport(xy - ex, t, t_dst, b)) / (2 * delta)
+        jy = (self.transport(xy + ey, t, t_dst, b) - self.transport(xy - ey, t, t_dst, b)) / (2 * delta)
+        det = jx[:, 0] * jy[:, 1] - jx[:, 1] * jy[:, 0]
+        return y, torch.log(det.abs().clamp(min=1e-12))
+
+
+class _VelocityFn(torch.autograd.Function):
+    """v = field(xy; theta) on the device; gradient w.r.t. theta only (event positions are data)."""
+
+    @staticmethod
+    def forward(ctx, theta, xy, b, kind, H, W):
+        if xy.requires_grad:
+            raise RuntimeError("x_b200 motion fields give no gradient w.r.t. event positions")
+        if not theta.is_cuda:
+            raise RuntimeError("x_b200 motion models need CUDA parameters (there is no CPU path)")
+        th = theta.detach().float().contiguous()
+        xyc = xy.detach().float().contiguous()
+        bl = b.contiguous().long()
+        B = th.shape[0]
+        Hg, Wg = (th.shape[-2], th.shape[-1]) if kind == L.MOTION_DENSE else (1, 1)
+        v = torch.empty(xyc.shape[0], 2, dtype=torch.float32, device=xyc.device)
+        L.check(L.lib().atlb_velocity(kind, L.ptr(th), B, Hg, Wg, H, W, L.ptr(xyc), L.ptr(bl), xyc.shape[0], L.ptr(v),
+                                      L.stream()), "velocity")
+        ctx.save_for_backward(xyc, bl)
+        ctx.meta = (kind, tuple(th.shape), B, Hg, Wg, H, W, theta.dtype)
+        return v
+
+    @staticmethod
+    def backward(ctx, gv):
+        xyc, bl = ctx.saved_tensors
+        kind, shape, B, Hg, Wg, H, W, dtype = ctx.meta
+        g = torch.empty(shape, dtype=torch.float32, device=xyc.device)
+        L.check(L.lib().atlb_velocity_bwd(kind, L.ptr(gv.contiguous().float()), B, Hg, Wg, H, W, L.ptr(xyc), L.ptr(bl),
+                                          xyc.shape[0], L.ptr(g), L.stream()), "velocity_bwd")
+        return g.to(dtype), None, None, None, None, None
+
+
+class VectorFieldMotion(Motion):
+    """Autonomous velocity field v(x; theta) (parametric.py:84-145)."""
+    n_params: int = 0
+    kind: int = -1
+
+    @property
+    def linear_at_event(self) -> bool:
+        return self.mode == "linear"
+
+    def __init__(self, batch_size: int, height: int, width: int, mode: str = "linear", rk4_steps: int = 8,
+                 init: Optional[torch.Tensor] = None):
+        super().__init__()
+        self.H, self.W, self.mode, self.rk4_steps = height, width, mode, rk4_steps
+        self.c = torch.tensor([(width - 1) / 2.0, (height - 1) / 2.0])
+        theta = torch.zeros(batch_size, self.n_params) if init is None else init.clone().float()
+        self.theta = nn.Parameter(theta)
+
+    def field(self, xy: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+        return _VelocityFn.apply(self.theta, xy, b, self.kind, self.H, self.W)
+
+    def velocity(self, xy, t, b):
+        return self.field(xy, b)
+
+    def affine_parts(self, b):
+        return None
+
+    def transport(self, xy, t, t_dst, b):
+        """parametric.py:114-139: linear warp, closed-form affine flow, or RK4."""
+        dt = as_time(t_dst, t) - t
+        if self.mode == "linear":
+            return xy + self.field(xy, b) * dt[:, None]
+        parts = self.affine_parts(b)
+        if parts is not None:
+            A, tr = parts
+            c = self.c.to(xy)
+            n = A.shape[0]
+            Z = torch.zeros(n, 3, 3, device=xy.device, dtype=xy.dtype)
+            Z[:, :2, :2] = A
+            Z[:, :2, 2] = tr
+            E = torch.linalg.matrix_exp(Z * dt[:, None, None])
+            return c + torch.bmm(E[:, :2, :2], (xy - c)[..., None])[..., 0] + E[:, :2, 2]
+        n = self.rk4_steps
+        h = dt / n
+        x = xy
+        for _ in range(n):
+            k1 = self._field_any(x, b)
+            k2 = self._field_any(x + 0.5 * h[:, None] * k1, b)
+            k3 = self._field_any(x + 0.5 * h[:, None] * k2, b)
+            k4 = self._field_any(x + h[:, None] * k3, b)
+            x = x + h[:, None] * (k1 + 2 * k2 + 2 * k3 + k4) / 6
+        return x
+
+    def _field_any(self, xy, b):
+        """Field at positions that may carry autograd history (RK4 stages): evaluated with torch ops."""
+        return self.field(xy, b) if not xy.requires_grad else self.field_torch(xy, b)
+
+    def field_torch(self, xy, b):
+        raise NotImplementedError
+
+
+class Translation(VectorFieldMotion):
+    """v = (tx, ty) (parametric.py:148-157)."""
+    n_params = 2
+    kind = L.MOTION_TRANSLATION
+
+    def field_torch(self, xy, b):
+        return self.theta[b]
+
+    def affine_parts(self, b):
+        z = self.theta.new_zeros(b.numel(), 2, 2)
+        return z, self.theta[b]
+
+
+class Affine(VectorFieldMotion):
+    """v = A (x - c) + t, theta = (tx, ty, a11, a12, a21, a22) (parametric.py:207-217)."""
+    n_params = 6
+    kind = L.MOTION_AFFINE
+
+    def affine_parts(self, b):
+        th = self.theta[b]
+        return th[:, 2:6].view(-1, 2, 2), th[:, :2]
+
+    def field_torch(self, xy, b):
+        A, tr = self.affine_parts(b)
+        return tr + torch.bmm(A, (xy - self.c.to(xy))[..., None])[..., 0]
+
+
+class DenseLinearFlow(VectorFieldMotion):
+    """Dense velocity grid (B, 2, Hg, Wg) bilinearly interpolated over the image (parametric.py:257-293)."""
+    kind = L.MOTION_DENSE
+
+    def __init__(self, batch_size, height, width, grid=(1, 1), mode="linear", init=None, rk4_steps=4):
+        Motion.__init__(self)
+        self.H, self.W, self.mode, self.rk4_steps = height, width, mode, rk4_steps
+        self.c = torch.tensor([(width - 1) / 2.0, (height - 1) / 2.0])
+        g = torch.zeros(batch_size, 2, *grid) if init is None else init.clone().float()
+        self.grid = nn.Parameter(g)
+
+    @property
+    def theta(self):
+        return self.grid
+
+    def field_torch(self, xy, b):
+        Hg, Wg = self.grid.shape[-2:]
+        gx = xy[:, 0] / max(self.W - 1, 1) * (Wg - 1)
+        gy = xy[:, 1] / max(self.H - 1, 1) * (Hg - 1)
+        return sample_grid(self.grid, torch.stack([gx, gy], 1), b)
+
+    def upsample(self, factor: int = 2):
+        """Refine the velocity grid by ``factor`` (parametric.py:282-289)."""
+        with torch.no_grad():
+            Hg, Wg = self.grid.shape[-2:]
+            new = torch.nn.functional.interpolate(self.grid, size=(Hg * factor, Wg * factor), mode="bilinear",
+                                                  align_corners=True)
+        self.grid = nn.Parameter(new)
+        return self
+
+
+def sample_grid(field: torch.Tensor, gpos: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """Bilinear sample of a (B, C, Hg, Wg) field at grid coordinates, border clamp (parametric.py:296-312).
+    Torch ops; used for positions that carry autograd history (RK4 stages of ``mode='exact'``)."""
+    B, C, Hg, Wg = field.shape
+    gx = gpos[:, 0].clamp(0, Wg - 1)
+    gy = gpos[:, 1].clamp(0, Hg - 1)
+    x0 = torch.floor(gx).clamp(max=max(Wg - 2, 0)); y0 = torch.floor(gy).clamp(max=max(Hg - 2, 0))
+    ax, ay = gx - x0, gy - y0
+    x0, y0 = x0.long(), y0.long()
+    x1, y1 = (x0 + 1).clamp(max=Wg - 1), (y0 + 1).clamp(max=Hg - 1)
+    f = field.permute(0, 2, 3, 1).reshape(-1, C)
+    base = b * (Hg * Wg)
+
+    def at(yy, xx):
+        return f[base + yy * Wg + xx]
+    return (at(y0, x0) * ((1 - ax) * (1 - ay))[:, None] + at(y0, x1) * (ax * (1 - ay))[:, None] +
+            at(y1, x0) * ((1 - ax) * ay)[:, None] + at(y1, x1) * (ax * ay)[:, None])
+
+
+MODELS = {"translation": Translation, "affine": Affine, "dense": DenseLinearFlow}

@@ -1,0 +1,257 @@
+"""Anchored transport score on B200 -- mirror of atl/objectives/ats.py (AnchoredExact, AnchoredSliced).
+
+    S(theta) = mean_i log( eps + rho_{-i}(x_i) ),
+    rho_{-i}(x) = (1 / W_i) sum_{j != i, |t_i - t_j| <= tau} K_h( x - Phi_{t_j -> t_i}(x_j) )
+
+Same constructors, same random draws (the objective's CPU ``torch.Generator``) and same outputs as
+the reference.  Stage kernels come from libatlb200 through x_b200.functional; the exposure
+correction runs as one fused kernel for the motion models of x_b200.motion.  ``log_scores`` also
+accepts pre-drawn noise (``noise=(u, z)``), which is how the benchmark keeps the host RNG out of a
+device-resident step.
+"""
+from __future__ import annotations
+
+import math
+from typing import Optional
+
+import torch
+
+from . import _lib as L
+from .events import EventPacket
+from .functional import ats_pair_sums, gather, splat, window_counts
+from .motion import VectorFieldMotion
+
+
+def _fused_kind(motion) -> int:
+    """libatlb200 motion kind if the motion's transport is the linear warp of a fused field, else -1."""
+    if isinstance(motion, VectorFieldMotion) and motion.kind >= 0 and motion.mode == "linear":
+        return motion.kind
+    return -1
+
+
+@torch.no_grad()
+def visible_fraction(motion, xa, ta, ba, ev: EventPacket, tau: float, n_check: int = 16) -> torch.Tensor:
+    """Exposure correction (atl/objectives/ats.py:31-50): fraction of the anchor's source mass recorded
+    while its scene point was inside the image, checked at ``n_check`` slice centres."""
+    kind = _fused_kind(motion)
+    if kind >= 0 and xa.is_cuda:
+        th = motion.theta.detach().float().contiguous()
+        Hg, Wg = (th.shape[-2], th.shape[-1]) if kind == L.MOTION_DENSE else (1, 1)
+        xac, tac, bac = xa.detach().float().contiguous(), ta.detach().float().contiguous(), ba.contiguous().long()
+        out = torch.empty(tac.shape[0], dtype=torch.float32, device=xa.device)
+        scratch = torch.empty(ev.batch_size * n_check * 4 + 16, dtype=torch.uint8, device=xa.device)
+        tf, bl = ev.t.float().contiguous(), ev.b.contiguous().long()
+        L.check(L.lib().atlb_visible_fraction(kind, L.ptr(th), th.shape[0], Hg, Wg, ev.height, ev.width, L.ptr(xac),
+                                              L.ptr(tac), L.ptr(bac), tac.shape[0], L.ptr(tf), L.ptr(bl), tf.shape[0],
+                                              float(tau), int(n_check), L.ptr(out), L.ptr(scratch), L.stream()),
+                "visible_fraction")
+        return out.to(ta.dtype)
+    # other motion models: the same computation with the motion's own transport (torch ops on the device)
+    edges = torch.linspace(0, 1, n_check + 1, device=ev.device)
+    centres = 0.5 * (edges[:-1] + edges[1:])
+    sl = torch.clamp((ev.t * n_check).long(), 0, n_check - 1)
+    counts = torch.zeros(ev.batch_size, n_check, device=ev.device)
+    counts.index_put_((ev.b, sl), torch.ones_like(ev.t), accumulate=True)
+    vis = torch.zeros_like(ta); tot = torch.zeros_like(ta)
+    for k in range(n_check):
+        c = float(centres[k])
+        near = ((ta - c).abs() <= tau).to(ta.dtype)
+        y = motion.transport(xa, ta, c, ba)
+        inside = ((y[:, 0] >= 0) & (y[:, 0] <= ev.width - 1) & (y[:, 1] >= 0) & (y[:, 1] <= ev.height - 1)).to(ta.dtype)
+        w = counts[ba, k] * near
+        vis += w * inside; tot += w
+    return (vis / tot.clamp(min=1)).clamp(min=1e-3)
+
+
+def _pick_anchors(ev: EventPacket, n_anchors: Optional[int], gen: Optional[torch.Generator]) -> torch.Tensor:
+    """ats.py:53-57."""
+    if n_anchors is None or n_anchors >= ev.n:
+        return torch.arange(ev.n, device=ev.device)
+    idx = torch.randperm(ev.n, generator=gen, device="cpu")[:n_anchors].to(ev.device)
+    return torch.sort(idx).values
+
+
+class Objective:
+    """Callable ``(events, motion) -> {'loss': ...}`` (atl/objectives/base.py:18-27)."""
+    name = "objective"
+    reference_frame = True
+
+    def __call__(self, ev: EventPacket, motion) -> dict:
+        raise NotImplementedError
+
+
+class AnchoredExact(Objective):
+    """Anchored transport score with the exact pair kernel (ats.py:60-105); motion linear at the event."""
+    name = "ats_exact"
+    reference_frame = False
+
+    def __init__(self, h: float = 1.0, tau: float = 1.0, eps_frac: float = 1e-2, n_anchors: Optional[int] = 20000,
+                 n_slices: int = 16, cut: float = 3.0, seed: Optional[int] = None, smooth_anchors: bool = True,
+                 dequantize: bool = True, visibility: bool = True, anchor_margin: float = 0.0):
+        self.visibility, self.anchor_margin = visibility, anchor_margin
+        self.h, self.tau, self.eps_frac, self.n_anchors, self.n_slices, self.cut = h, tau, eps_frac, n_anchors, n_slices, cut
+        self.smooth_anchors, self.dequantize = smooth_anchors, dequantize
+        self.gen = torch.Generator().manual_seed(seed) if seed is not None else None
+
+    def draw(self, ev: EventPacket, anchors: Optional[torch.Tensor] = None):
+        """The objective's random draws (ats.py:79-88), in the reference's order: anchors, dequantisation
+        jitter u ~ U[0,1)^2 per event, smoothing noise z ~ N(0, I) per anchor.  Returns (anchors, u, z)
+        with u / z on the events' device (None when the option is off)."""
+        if anchors is None:
+            anchors = _pick_anchors(ev, self.n_anchors, self.gen)
+            if self.anchor_margin > 0:
+                anchors = anchors[ev.inside(ev.xy[anchors], margin=-self.anchor_margin)]
+        u = torch.rand(ev.xy.shape, generator=self.gen).to(ev.xy) if self.dequantize else None
+        z = torch.randn((anchors.numel(), 2), generator=self.gen).to(ev.xy) if self.smooth_anchors else None
+        return anchors, u, z
+
+    def log_scores(self, ev: EventPacket, motion, anchors: Optional[torch.Tensor] = None, noise=None):
+        """Per-anchor log predictive densities and the anchor indices (ats.py:75-96).  ``noise`` =
+        (anchors, u, z) as returned by :meth:`draw` replaces the generator draws."""
+        if not getattr(motion, "linear_at_event", False):
+            raise ValueError("AnchoredExact needs a motion that is linear at the event; use AnchoredSliced")
+        anchors, u, z = self.draw(ev, anchors) if noise is None else noise
+        xs = ev.xy
+        if self.dequantize:
+            xs = xs + (u - 0.5)
+        xa = xs[anchors]
+        if self.smooth_anchors:
+            xa = xa + self.h * z
+        v = motion.velocity(xs, ev.t, ev.b)
+        S = ats_pair_sums(xs, ev.t, v, ev.b, ev.batch_size, ev.height, ev.width, anchors, self.h, self.tau,
+                          self.cut, self.n_slices, anchor_xy=xa)
+        Wn = window_counts(ev.t, ev.b, anchors, self.tau).clamp(min=1)
+        if self.visibility:
+            Wn = Wn * visible_fraction(motion, xa.detach(), ev.t[anchors], ev.b[anchors], ev, self.tau)
+        eps = self.eps_frac / (ev.height * ev.width)
+        return torch.log(eps + S / (Wn * 2 * math.pi * self.h ** 2)), anchors
+
+    def set_bandwidth(self, h: float):
+        self.h = float(h)
+
+    def __call__(self, ev, motion, noise=None):
+        ls, _ = self.log_scores(ev, motion, noise=noise)
+        s = ls.mean()
+        return {"loss": -s, "score": s.detach()}
+
+
+class AnchoredSliced(Objective):
+    """Anchored transport score for any motion model (ats.py:108-183): Gaussian splats at slice centres,
+    anchors moved by the small step t_i -> c_s with the exact finite-difference log|det|."""
+    name = "ats_sliced"
+    reference_frame = False
+
+    def __init__(self, n_slices: int = 10, slices_per_step: Optional[int] = None, sigma: float = 1.0,
+                 tau: float = 1.0, eps_frac: float = 1e-2, n_anchors_per_slice: Optional[int] = None,
+                 logdet: bool = True, seed: Optional[int] = None, smooth_anchors: bool = True,
+                 dequantize: bool = True, visibility: bool = True):
+        self.smooth_anchors, self.dequantize, self.visibility = smooth_anchors, dequantize, visibility
+        self.S, self.sps, self.sigma, self.tau, self.eps_frac = n_slices, slices_per_step, sigma, tau, eps_frac
+        self.nap, self.logdet = n_anchors_per_slice, logdet
+        self.gen = torch.Generator().manual_seed(seed) if seed is not None else None
+
+    def log_scores(self, ev: EventPacket, motion, anchor_mask: Optional[torch.Tensor] = None,
+                   source_mask: Optional[torch.Tensor] = None):
+        S, dev = self.S, ev.device
+        delta = 1.0 / S
+        sl = torch.clamp(torch.floor(ev.t / delta), 0, S - 1).long()
+        slices = list(range(S))
+        if self.sps is not None and self.sps < S:
+            slices = torch.randperm(S, generator=self.gen)[: self.sps].tolist()
+        eps = self.eps_frac / (ev.height * ev.width)
+        xs = ev.xy
+        if self.dequantize:
+            xs = xs + (torch.rand(xs.shape, generator=self.gen).to(xs) - 0.5)
+        xsm = xs + self.sigma * torch.randn(xs.shape, generator=self.gen).to(xs) if self.smooth_anchors else xs
+        out, idx_all = [], []
+        for s in slices:
+            c = (s + 0.5) * delta
+            src = (ev.t - c).abs() <= self.tau + delta / 2
+            if source_mask is not None:
+                src = src & source_mask
+            anc = sl == s
+            if anchor_mask is not None:
+                anc = anc & anchor_mask
+            ai = torch.nonzero(anc).squeeze(1)
+            if ai.numel() == 0:
+                continue
+            if self.nap is not None and ai.numel() > self.nap:
+                ai = ai[torch.randperm(ai.numel(), generator=self.gen)[: self.nap].to(dev)]
+            si = torch.nonzero(src).squeeze(1)
+            y = motion.transport(xs[si], ev.t[si], c, ev.b[si])
+            img = splat(y, torch.ones_like(ev.t[si]), ev.b[si], ev.batch_size, ev.height, ev.width,
+                        kernel="gauss", sigma=self.sigma)
+            if self.logdet:
+                a, ld = motion.transport_logdet(xsm[ai], ev.t[ai], c, ev.b[ai])
+            else:
+                a, ld = motion.transport(xsm[ai], ev.t[ai], c, ev.b[ai]), 0.0
+            val = gather(img, a, ev.b[ai])
+            if self.smooth_anchors:
+                y_own = motion.transport(xs[ai], ev.t[ai], c, ev.b[ai])
+                own = src[ai].to(val.dtype) * _cross_term(a, y_own, self.sigma, ev.height, ev.width)
+            else:
+                own = src[ai].to(val.dtype) * _self_term(a, self.sigma, ev.height, ev.width)
+            nsrc = torch.bincount(ev.b[si], minlength=ev.batch_size).to(val.dtype)[ev.b[ai]] - src[ai].to(val.dtype)
+            if self.visibility:
+                nsrc = nsrc * visible_fraction(motion, xsm[ai].detach(), ev.t[ai], ev.b[ai], ev, self.tau)
+            rho = (val - own).clamp(min=0) / nsrc.clamp(min=1)
+            out.append(torch.log(eps + rho) + ld)
+            idx_all.append(ai)
+        if not out:
+            z = ev.t.new_zeros(0)
+            return z, z.long()
+        return torch.cat(out), torch.cat(idx_all)
+
+    def set_bandwidth(self, h: float):
+        self.sigma = float(h)
+
+    def __call__(self, ev, motion):
+        ls, _ = self.log_scores(ev, motion)
+        s = ls.mean() if ls.numel() else ev.t.new_zeros(())
+        return {"loss": -s, "score": s.detach()}
+
+
+def _cross_term(a: torch.Tensor, y: torch.Tensor, sigma: float, H: int, W: int) -> torch.Tensor:
+    """Bilinear look-up at ``a`` of the truncated Gaussian splat centred at ``y`` (ats.py:186-200)."""
+    R = int(math.ceil(3 * sigma))
+    cy0, cx0 = torch.round(y[:, 1]), torch.round(y[:, 0])
+    x0, y0 = torch.floor(a[:, 0]), torch.floor(a[:, 1])
+    ax, ay = a[:, 0] - x0, a[:, 1] - y0
+    s = torch.zeros_like(ax)
+    norm = 1.0 / (2 * math.pi * sigma * sigma)
+    for dy, wy in ((0, 1 - ay), (1, ay)):
+        for dx, wx in ((0, 1 - ax), (1, ax)):
+            px, py = x0 + dx, y0 + dy
+            ok = ((px >= 0) & (px < W) & (py >= 0) & (py < H) & ((px - cx0).abs() <= R) & ((py - cy0).abs() <= R))
+            d2 = (px - y[:, 0]) ** 2 + (py - y[:, 1]) ** 2
+            s = s + wx * wy * ok.to(a.dtype) * norm * torch.exp(-d2 / (2 * sigma * sigma))
+    return s
+
+
+def _self_term(y: torch.Tensor, sigma: float, H: int, W: int) -> torch.Tensor:
+    """Own Gaussian splat seen by the bilinear look-up at its own position (atl/objectives/cmax.py:125-137)."""
+    x0, y0 = torch.floor(y[:, 0]), torch.floor(y[:, 1])
+    ax, ay = y[:, 0] - x0, y[:, 1] - y0
+    s = torch.zeros_like(ax)
+    norm = 1.0 / (2 * math.pi * sigma * sigma)
+    for dy, wy in ((0, 1 - ay), (1, ay)):
+        for dx, wx in ((0, 1 - ax), (1, ax)):
+            cx, cy = x0 + dx, y0 + dy
+            inside = ((cx >= 0) & (cx < W) & (cy >= 0) & (cy < H)).to(y.dtype)
+            d2 = (cx - y[:, 0]) ** 2 + (cy - y[:, 1]) ** 2
+            s = s + wx * wy * inside * norm * torch.exp(-d2 / (2 * sigma * sigma))
+    return s
+
+
+def build(name: str, **kw) -> Objective:
+    """Registry of the anchored objectives (atl/objectives/__init__.py:10-35, 'ats_exact' / 'ats_sliced')."""
+    reg = {
+        "ats_exact": lambda: AnchoredExact(**{k: v for k, v in kw.items() if k in (
+            "h", "tau", "eps_frac", "n_anchors", "n_slices", "seed", "smooth_anchors", "dequantize", "visibility",
+            "anchor_margin")}),
+        "ats_sliced": lambda: AnchoredSliced(**{k: v for k, v in kw.items() if k in (
+            "n_slices", "slices_per_step", "sigma", "tau", "eps_frac", "n_anchors_per_slice", "seed")}),
+    }
+    if name not in reg:
+        raise KeyError(f"unknown objective {name}; available: {sorted(reg)}")
+    return reg[name]()
