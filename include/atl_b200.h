@@ -158,6 +158,41 @@ int atlb_visible_fraction(int kind, const float* theta, int64_t B, int64_t Hg, i
                           const int64_t* b, int64_t N, double tau, int64_t n_check, float* out, void* scratch,
                           atlb_stream_t stream);
 
+/* ----------------------------------------------------------------------------------------------
+ * Fused anchored score: AnchoredExact.log_scores (atl/objectives/ats.py:75-96) for the motion kinds
+ * above, with its backward.  Three calls:
+ *   atlb_exact_prepare   dequantised positions xs = xy + (u - 1/2) (u NULL: none), velocities v(xs),
+ *                        anchor positions xa = xs[a] + h z (z NULL: none; anchors NULL: all events),
+ *                        grid geometry.  Writes ev4 (N,4) = (xs, v) and anc4 (M,4) = (xa, t_a, a bits),
+ *                        anc_b (M).  Synchronous.  ATLB_ERR_UNSORTED if events are not (b, t) sorted.
+ *   atlb_exact_forward   plan, window counts (ats.py:92), exposure correction (ats.py:93-94), pair
+ *                        sums; S (M), den (M) = W * vis * 2 pi h^2 and ls (M) = log(eps + S / den).
+ *   atlb_exact_backward  from dL/dls (M): gv (N,2) = dL/dv and gtheta = dL/dtheta (overwritten).
+ * The workspace (atlb_exact_workspace_bytes) carries the plan from forward to backward.
+ * ---------------------------------------------------------------------------------------------- */
+typedef struct {
+  int32_t kind;          /* ATLB_MOTION_* */
+  const float* theta;    /* motion parameters / flow grid */
+  int64_t Bt, Hg, Wg;    /* parameter batch; flow grid height / width (dense) */
+  int64_t B, H, W;       /* event batch size; sensor height / width */
+  double h, tau, cut, eps_frac;
+  int64_t S;             /* n_slices */
+  int32_t visibility;    /* exposure correction on (1) / off (0) */
+  int64_t n_check;       /* slices of the exposure check (16 in the reference) */
+} atlb_exact_cfg;
+
+int atlb_exact_prepare(const atlb_exact_cfg* cfg, const float* xy, const float* u, const float* t, const int64_t* b,
+                       int64_t N, const int64_t* anchors, const float* z, int64_t M, float* ev4, float* anc4,
+                       int64_t* anc_b, void* scratch, atlb_plan_geom* geom_out, atlb_stream_t stream);
+size_t atlb_exact_workspace_bytes(const atlb_exact_cfg* cfg, int64_t N, int64_t M, const atlb_plan_geom* geom);
+int atlb_exact_forward(const atlb_exact_cfg* cfg, const float* t, const int64_t* b, int64_t N, int64_t M,
+                       const float* ev4, const float* anc4, const int64_t* anc_b, const atlb_plan_geom* geom,
+                       void* workspace, size_t workspace_bytes, float* S_out, float* den_out, float* ls_out,
+                       atlb_stream_t stream);
+int atlb_exact_backward(const atlb_exact_cfg* cfg, const float* grad_ls, const int64_t* b, int64_t N, int64_t M,
+                        const float* ev4, const atlb_plan_geom* geom, void* workspace, size_t workspace_bytes,
+                        const float* S, const float* den, float* gv, float* gtheta, atlb_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -28,6 +28,14 @@ class PlanGeom(ctypes.Structure):
                 ("GW", ctypes.c_int64), ("GH", ctypes.c_int64), ("vmax", ctypes.c_float), ("S", ctypes.c_int32)]
 
 
+class ExactCfg(ctypes.Structure):
+    _fields_ = [("kind", ctypes.c_int32), ("theta", ctypes.c_void_p), ("Bt", ctypes.c_int64), ("Hg", ctypes.c_int64),
+                ("Wg", ctypes.c_int64), ("B", ctypes.c_int64), ("H", ctypes.c_int64), ("W", ctypes.c_int64),
+                ("h", ctypes.c_double), ("tau", ctypes.c_double), ("cut", ctypes.c_double),
+                ("eps_frac", ctypes.c_double), ("S", ctypes.c_int64), ("visibility", ctypes.c_int32),
+                ("n_check", ctypes.c_int64)]
+
+
 # name -> (restype, argtypes)
 _SIGS = {
     "atlb_last_error": (ctypes.c_char_p, []),
@@ -59,6 +67,13 @@ _SIGS = {
     "atlb_velocity_bwd": (_int, [_int, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _vp, _i64, _vp, _vp]),
     "atlb_visible_fraction": (_int, [_int, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _i64, _vp, _vp, _i64,
                                      _dbl, _i64, _vp, _vp, _vp]),
+    "atlb_exact_prepare": (_int, [ctypes.POINTER(ExactCfg), _vp, _vp, _vp, _vp, _i64, _vp, _vp, _i64, _vp, _vp, _vp,
+                                  _vp, ctypes.POINTER(PlanGeom), _vp]),
+    "atlb_exact_workspace_bytes": (_size, [ctypes.POINTER(ExactCfg), _i64, _i64, ctypes.POINTER(PlanGeom)]),
+    "atlb_exact_forward": (_int, [ctypes.POINTER(ExactCfg), _vp, _vp, _i64, _i64, _vp, _vp, _vp,
+                                  ctypes.POINTER(PlanGeom), _vp, _size, _vp, _vp, _vp, _vp]),
+    "atlb_exact_backward": (_int, [ctypes.POINTER(ExactCfg), _vp, _vp, _i64, _i64, _vp, ctypes.POINTER(PlanGeom), _vp,
+                                   _size, _vp, _vp, _vp, _vp, _vp]),
 }
 
 _LIB = None

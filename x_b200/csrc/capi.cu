@@ -67,6 +67,15 @@ int window_counts(const float*, const long long*, long long, const long long*, l
 int window_counts_keys(const double*, long long, const float*, const long long*, const long long*, long long, double,
                        float*, cudaStream_t);
 
+size_t exact_workspace_bytes(const atlb_exact_cfg&, long long, long long, const atlb_plan_geom&);
+int exact_prepare(const atlb_exact_cfg&, const float*, const float*, const float*, const long long*, long long,
+                  const long long*, const float*, long long, float*, float*, long long*, void*, atlb_plan_geom*,
+                  cudaStream_t);
+int exact_forward(const atlb_exact_cfg&, const float*, const long long*, long long, long long, const float*,
+                  const float*, const long long*, const atlb_plan_geom&, void*, float*, float*, float*, cudaStream_t);
+int exact_backward(const atlb_exact_cfg&, const float*, const long long*, long long, long long, const float*,
+                   const atlb_plan_geom&, void*, const float*, const float*, float*, float*, cudaStream_t);
+
 }  // namespace atlb
 
 using namespace atlb;
@@ -327,6 +336,84 @@ int atlb_visible_fraction(int kind, const float* theta, int64_t B, int64_t Hg, i
   if (!scratch) { set_error("atlb_visible_fraction: scratch is NULL"); return ATLB_ERR_ARG; }
   return visible_fraction(make_motion_view(kind, theta, B, Hg, Wg, H, W), xa, ta, LL(ba), M, t, LL(b), N, tau, n_check,
                           out, scratch, STREAM(stream));
+}
+
+static int check_exact_cfg(const atlb_exact_cfg* c, const char* fn) {
+  if (!c) { set_error("%s: cfg is NULL", fn); return ATLB_ERR_ARG; }
+  if (int st = check_kind(c->kind, fn)) return st;
+  if (!c->theta || c->Bt < 1 || c->B < 1 || c->H < 1 || c->W < 1 || c->S < 1 || c->S > 65535 || c->n_check < 1 ||
+      c->n_check > 4096 || (c->kind == ATLB_MOTION_DENSE && (c->Hg < 1 || c->Wg < 1))) {
+    set_error("%s: invalid configuration", fn);
+    return ATLB_ERR_ARG;
+  }
+  return ATLB_OK;
+}
+
+static int check_exact_sizes(const atlb_exact_cfg* c, int64_t N, int64_t M, const atlb_plan_geom* g, const char* fn) {
+  if (N < 0 || M < 0) { set_error("%s: negative size", fn); return ATLB_ERR_ARG; }
+  if (N * c->S > (1LL << 31) - 1 || M > (1LL << 31) - 1) {
+    set_error("%s: N * n_slices = %lld entries exceed the int32 plan index", fn, (long long)(N * c->S));
+    return ATLB_ERR_OVERFLOW;
+  }
+  if (g && (g->S != c->S || g->GW < 1 || g->GH < 1 || (double)c->B * g->S * (double)g->GH * g->GW > 2.0e9)) {
+    set_error("%s: invalid geometry", fn);
+    return ATLB_ERR_OVERFLOW;
+  }
+  return ATLB_OK;
+}
+
+int atlb_exact_prepare(const atlb_exact_cfg* cfg, const float* xy, const float* u, const float* t, const int64_t* b,
+                       int64_t N, const int64_t* anchors, const float* z, int64_t M, float* ev4, float* anc4,
+                       int64_t* anc_b, void* scratch, atlb_plan_geom* geom_out, atlb_stream_t stream) {
+  clear();
+  if (int st = check_exact_cfg(cfg, __func__)) return st;
+  if (int st = check_exact_sizes(cfg, N, M, nullptr, __func__)) return st;
+  NEED(xy, N); NEED(t, N); NEED(b, N); NEED(ev4, N); NEED(anc4, M); NEED(anc_b, M);
+  if (!anchors && M != N) { set_error("atlb_exact_prepare: anchors NULL needs M == N"); return ATLB_ERR_ARG; }
+  if (!scratch || !geom_out) { set_error("atlb_exact_prepare: scratch / geom_out NULL"); return ATLB_ERR_ARG; }
+  const int st = exact_prepare(*cfg, xy, u, t, LL(b), N, LL(anchors), z, M, ev4, anc4, LLW(anc_b), scratch, geom_out,
+                               STREAM(stream));
+  if (st) return st;
+  return check_exact_sizes(cfg, N, M, geom_out, __func__);
+}
+
+size_t atlb_exact_workspace_bytes(const atlb_exact_cfg* cfg, int64_t N, int64_t M, const atlb_plan_geom* geom) {
+  if (!cfg || !geom || N < 0 || M < 0) return 0;
+  return exact_workspace_bytes(*cfg, N, M, *geom);
+}
+
+int atlb_exact_forward(const atlb_exact_cfg* cfg, const float* t, const int64_t* b, int64_t N, int64_t M,
+                       const float* ev4, const float* anc4, const int64_t* anc_b, const atlb_plan_geom* geom,
+                       void* workspace, size_t workspace_bytes, float* S_out, float* den_out, float* ls_out,
+                       atlb_stream_t stream) {
+  clear();
+  if (int st = check_exact_cfg(cfg, __func__)) return st;
+  if (!geom) { set_error("atlb_exact_forward: geom NULL"); return ATLB_ERR_ARG; }
+  if (int st = check_exact_sizes(cfg, N, M, geom, __func__)) return st;
+  NEED(t, N); NEED(b, N); NEED(ev4, N); NEED(anc4, M); NEED(anc_b, M); NEED(S_out, M); NEED(den_out, M);
+  NEED(ls_out, M);
+  if (!workspace || workspace_bytes < exact_workspace_bytes(*cfg, N, M, *geom)) {
+    set_error("atlb_exact_forward: workspace too small");
+    return ATLB_ERR_WORKSPACE;
+  }
+  return exact_forward(*cfg, t, LL(b), N, M, ev4, anc4, LL(anc_b), *geom, workspace, S_out, den_out, ls_out,
+                       STREAM(stream));
+}
+
+int atlb_exact_backward(const atlb_exact_cfg* cfg, const float* grad_ls, const int64_t* b, int64_t N, int64_t M,
+                        const float* ev4, const atlb_plan_geom* geom, void* workspace, size_t workspace_bytes,
+                        const float* S, const float* den, float* gv, float* gtheta, atlb_stream_t stream) {
+  clear();
+  if (int st = check_exact_cfg(cfg, __func__)) return st;
+  if (!geom) { set_error("atlb_exact_backward: geom NULL"); return ATLB_ERR_ARG; }
+  if (int st = check_exact_sizes(cfg, N, M, geom, __func__)) return st;
+  NEED(grad_ls, M); NEED(b, N); NEED(ev4, N); NEED(S, M); NEED(den, M); NEED(gv, N);
+  if (!gtheta) { set_error("atlb_exact_backward: gtheta NULL"); return ATLB_ERR_ARG; }
+  if (!workspace || workspace_bytes < exact_workspace_bytes(*cfg, N, M, *geom)) {
+    set_error("atlb_exact_backward: workspace too small");
+    return ATLB_ERR_WORKSPACE;
+  }
+  return exact_backward(*cfg, grad_ls, LL(b), N, M, ev4, *geom, workspace, S, den, gv, gtheta, STREAM(stream));
 }
 
 }  // extern "C"

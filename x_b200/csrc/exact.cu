@@ -1,0 +1,550 @@
+// Fused AnchoredExact (atl/objectives/ats.py:75-96) for the motion fields of motion_math.cuh.
+//
+// The reference runs ~40 torch ops and four extension calls per score evaluation, with the plan built
+// by host-orchestrated torch ops.  Here one score is:
+//   prepare   one pass over the events: dequantised position xs = xy + (u - 1/2), velocity v(xs),
+//             packed (xs, v) record, vmax and (b, t)-order checks; one pass over the anchors:
+//             xa = xs[a] + h z and the anchors' bounding box                       [1 host read]
+//   forward   slice-major count + scan + scatter of the (source, slice) entries into a compact
+//             24-byte layout, anchors bucketed by cell, per-anchor normaliser W_i * vis_i * 2 pi h^2
+//             (window count + exposure correction fused), pair sums with the log score written
+//             directly (log(eps + S / den)).
+//   backward  dL/dS from the upstream dL/dls, source-centric pair gradient, velocity-field gradient.
+// Every step keeps the reference's rounding, so scores match it to float accuracy and the plan's
+// cells are the reference's cells.
+#include "common.cuh"
+#include "motion_math.cuh"
+#include "pair_kernels.cuh"
+#include "pair_tiled.cuh"
+#include "plan_math.cuh"
+#include "scan.cuh"
+
+namespace atlb {
+
+void plan_geometry_host(float vmax, bool have_anchors, float mnx, float mny, float mxx, float mxy, long long H,
+                        long long W, double h, double cut, long long S, atlb_plan_geom* g);
+PlanConsts make_plan_consts(const atlb_plan_geom& g, double tau, long long B);
+dim3 slice_grid(long long N, int S);
+
+namespace {
+
+constexpr int kThreads = 256;
+inline int grid_for(long long n) { return clamp_grid(blocks_for(n, kThreads)); }
+
+// scratch ints: [0] vmax bits, [1..4] anchor bbox (ordered ints), [5] bad anchor index,
+// [6] events not sorted by (b, t), [7] batch index outside [0, B)
+__global__ void k_exact_init(int* r) {
+  if (threadIdx.x == 0) {
+    r[0] = 0;
+    r[1] = 0x7fffffff; r[2] = 0x7fffffff;
+    r[3] = (int)0x80000000; r[4] = (int)0x80000000;
+    r[5] = 0; r[6] = 0; r[7] = 0;
+  }
+}
+
+__global__ void __launch_bounds__(kThreads) k_exact_events(MotionView Mv, const float2* __restrict__ xy,
+                                                           const float2* __restrict__ u, const float* __restrict__ t,
+                                                           const long long* __restrict__ b, long long N, long long B,
+                                                           float4* __restrict__ ev4, int* r) {
+  float vm = 0.f;
+  int unsorted = 0, badb = 0;
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long j = blockIdx.x * (long long)blockDim.x + threadIdx.x; j < N; j += stride) {
+    float2 p = xy[j];
+    if (u) {  // ats.py:84-85: xs = xy + (u - 0.5)
+      const float2 q = u[j];
+      p = make_float2(add_rn(p.x, sub_rn(q.x, 0.5f)), add_rn(p.y, sub_rn(q.y, 0.5f)));
+    }
+    const long long bj = b[j];
+    float2 v;
+    if (bj >= 0 && bj < B && bj < Mv.B) {
+      v = motion_field(Mv, p.x, p.y, bj);
+    } else {
+      v = make_float2(__int_as_float(0x7fc00000), __int_as_float(0x7fc00000));
+      badb = 1;
+    }
+    ev4[j] = make_float4(p.x, p.y, v.x, v.y);
+    const float n = row_norm(v.x, v.y);
+    vm = (n > vm || n != n) ? n : vm;
+    if (j + 1 < N) {
+      const double k0 = (double)bj * 4.0 + (double)t[j], k1 = (double)b[j + 1] * 4.0 + (double)t[j + 1];
+      if (!(k0 <= k1)) unsorted = 1;
+    }
+  }
+  int vb = __float_as_int(vm);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    vb = max(vb, __shfl_xor_sync(0xffffffffu, vb, o));
+    unsorted |= __shfl_xor_sync(0xffffffffu, unsorted, o);
+    badb |= __shfl_xor_sync(0xffffffffu, badb, o);
+  }
+  if ((threadIdx.x & 31) == 0) {
+    atomicMax(r + 0, vb);
+    if (unsorted) atomicOr(r + 6, 1);
+    if (badb) atomicOr(r + 7, 1);
+  }
+}
+
+__global__ void __launch_bounds__(kThreads) k_exact_anchors(const float4* __restrict__ ev4,
+                                                            const float* __restrict__ t,
+                                                            const long long* __restrict__ b, long long N,
+                                                            const long long* __restrict__ anchors,
+                                                            const float2* __restrict__ z, float h_f, long long M,
+                                                            float4* __restrict__ anc4, long long* __restrict__ anc_b,
+                                                            int* r) {
+  int mnx = 0x7fffffff, mny = 0x7fffffff, mxx = (int)0x80000000, mxy = (int)0x80000000, bad = 0;
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < M; i += stride) {
+    const long long a = anchors ? anchors[i] : i;
+    if (a < 0 || a >= N) {
+      bad = 1;
+      anc4[i] = make_float4(0.f, 0.f, 0.f, __int_as_float(-1));
+      anc_b[i] = -1;
+      continue;
+    }
+    const float4 e = ev4[a];
+    float xa = e.x, ya = e.y;
+    if (z) {  // ats.py:87-88: xa = xs[a] + h * z
+      const float2 q = z[i];
+      xa = add_rn(xa, mul_rn(h_f, q.x));
+      ya = add_rn(ya, mul_rn(h_f, q.y));
+    }
+    anc4[i] = make_float4(xa, ya, t[a], __int_as_float((int)a));
+    anc_b[i] = b[a];
+    const int ox = float_to_ordered(xa), oy = float_to_ordered(ya);
+    mnx = min(mnx, ox); mny = min(mny, oy); mxx = max(mxx, ox); mxy = max(mxy, oy);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    mnx = min(mnx, __shfl_xor_sync(0xffffffffu, mnx, o));
+    mny = min(mny, __shfl_xor_sync(0xffffffffu, mny, o));
+    mxx = max(mxx, __shfl_xor_sync(0xffffffffu, mxx, o));
+    mxy = max(mxy, __shfl_xor_sync(0xffffffffu, mxy, o));
+    bad |= __shfl_xor_sync(0xffffffffu, bad, o);
+  }
+  if ((threadIdx.x & 31) == 0) {
+    atomicMin(r + 1, mnx); atomicMin(r + 2, mny);
+    atomicMax(r + 3, mxx); atomicMax(r + 4, mxy);
+    if (bad) atomicOr(r + 5, 1);
+  }
+}
+
+// ---- compact plan -------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(kThreads) k_fast_count(PlanConsts P, const float4* __restrict__ ev4,
+                                                         const float* __restrict__ t, const long long* __restrict__ b,
+                                                         long long N, int* __restrict__ counts) {
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (int s = blockIdx.y; s < P.S; s += gridDim.y) {
+    for (long long j = blockIdx.x * (long long)blockDim.x + threadIdx.x; j < N; j += stride) {
+      const float tj = t[j];
+      int s_lo, s_hi;
+      slice_range(P, tj, &s_lo, &s_hi);
+      if (s < s_lo || s > s_hi) continue;
+      const float4 e = ev4[j];
+      float yx, yy;
+      const long long key = source_key(P, e.x, e.y, e.z, e.w, tj, b[j], s, &yx, &yy);
+      if (key >= 0) atomicAdd(counts + key, 1);
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kThreads) k_fast_scatter(PlanConsts P, const float4* __restrict__ ev4,
+                                                           const float* __restrict__ t, const long long* __restrict__ b,
+                                                           long long N, const int* __restrict__ start,
+                                                           int* __restrict__ cursor, float4* __restrict__ YV,
+                                                           float2* __restrict__ TI) {
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (int s = blockIdx.y; s < P.S; s += gridDim.y) {
+    for (long long j = blockIdx.x * (long long)blockDim.x + threadIdx.x; j < N; j += stride) {
+      const float tj = t[j];
+      int s_lo, s_hi;
+      slice_range(P, tj, &s_lo, &s_hi);
+      if (s < s_lo || s > s_hi) continue;
+      const float4 e = ev4[j];
+      float yx, yy;
+      const long long key = source_key(P, e.x, e.y, e.z, e.w, tj, b[j], s, &yx, &yy);
+      if (key < 0) continue;
+      const int p = start[key] + atomicAdd(cursor + key, 1);
+      YV[p] = make_float4(yx, yy, e.z, e.w);
+      TI[p] = make_float2(tj, __int_as_float((int)j));
+    }
+  }
+}
+
+__device__ __forceinline__ long long fast_anchor_key(const PlanConsts& P, float4 a, long long ba) {
+  if (__float_as_int(a.w) < 0 || ba < 0 || ba >= P.B) return -1;
+  long long g, cx, cy;
+  anchor_cell(P, a.x, a.y, a.z, ba, &g, &cx, &cy);
+  return (g * P.GH + cy) * P.GW + cx;
+}
+
+__global__ void __launch_bounds__(kThreads) k_fast_anchor_count(PlanConsts P, const float4* __restrict__ anc4,
+                                                                const long long* __restrict__ anc_b, long long M,
+                                                                int* __restrict__ counts) {
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < M; i += stride) {
+    const long long key = fast_anchor_key(P, anc4[i], anc_b[i]);
+    if (key >= 0) atomicAdd(counts + key, 1);
+  }
+}
+
+__global__ void __launch_bounds__(kThreads) k_fast_anchor_scatter(PlanConsts P, const float4* __restrict__ anc4,
+                                                                  const long long* __restrict__ anc_b, long long M,
+                                                                  const int* __restrict__ start,
+                                                                  int* __restrict__ cursor, float4* __restrict__ XT,
+                                                                  int* __restrict__ BI) {
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < M; i += stride) {
+    const float4 a = anc4[i];
+    const long long key = fast_anchor_key(P, a, anc_b[i]);
+    if (key < 0) continue;
+    const int p = start[key] + atomicAdd(cursor + key, 1);
+    XT[p] = a;
+    BI[p] = (int)i;
+  }
+}
+
+// ---- per-anchor normaliser: den = W * vis * 2 pi h^2 (ats.py:92-96, functional.py:210-217) ----------
+__device__ __forceinline__ double ev_key(const float* t, const long long* b, long long j) {
+  return (double)b[j] * 4.0 + (double)t[j];
+}
+
+__device__ __forceinline__ long long key_search(const float* t, const long long* b, long long N, double q, bool right) {
+  long long lo = 0, hi = N;
+  while (lo < hi) {
+    const long long m = (lo + hi) >> 1;
+    const double k = ev_key(t, b, m);
+    if (right ? (k <= q) : (k < q)) lo = m + 1; else hi = m;
+  }
+  return lo;
+}
+
+struct NormConsts {
+  double tau;
+  float tau_f, pi_f, h2_f, wmax, hmax;
+  int n_check, visibility;
+};
+
+__global__ void __launch_bounds__(kThreads) k_exact_norm(MotionView Mv, NormConsts K, const float4* __restrict__ anc4,
+                                                         const long long* __restrict__ anc_b, long long M,
+                                                         const float* __restrict__ t, const long long* __restrict__ b,
+                                                         long long N, const int* __restrict__ counts,
+                                                         float* __restrict__ den) {
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < M; i += stride) {
+    const float4 a = anc4[i];
+    const int ai = __float_as_int(a.w);
+    const long long ba = anc_b[i];
+    if (ai < 0 || ba < 0 || ba >= Mv.B) {
+      den[i] = __int_as_float(0x7fc00000);
+      continue;
+    }
+    const double ki = ev_key(t, b, ai);
+    const long long c = key_search(t, b, N, ki + K.tau, true) - key_search(t, b, N, ki - K.tau, false) - 1;
+    float wn = (float)(c > 0 ? c : 0);
+    wn = wn < 1.f ? 1.f : wn;  // .clamp(min=1)
+    if (K.visibility)
+      wn = mul_rn(wn, visible_fraction_one(Mv, a.x, a.y, a.z, ba, counts + ba * K.n_check, K.n_check, K.tau_f,
+                                           K.wmax, K.hmax));
+    den[i] = mul_rn(mul_rn(mul_rn(wn, 2.f), K.pi_f), K.h2_f);  // Wn * 2 * math.pi * h ** 2
+  }
+}
+
+struct FusedOut {
+  float* S;
+  float* ls;
+  const float* den;
+  const int* idx;
+  float eps;
+  __device__ __forceinline__ void operator()(int p, double v) const {
+    const int i = idx[p];
+    const float s = (float)v;
+    S[i] = s;
+    ls[i] = logf(add_rn(eps, div_rn(s, den[i])));  // log(eps + S / den)
+  }
+};
+
+// dL/dS in bucket order from the upstream dL/dls (torch's LogBackward then DivBackward).
+__global__ void __launch_bounds__(kThreads) k_exact_gs(const int* __restrict__ BI, long long M,
+                                                       const float* __restrict__ grad_ls, const float* __restrict__ S,
+                                                       const float* __restrict__ den, float eps,
+                                                       float* __restrict__ gSb) {
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long p = blockIdx.x * (long long)blockDim.x + threadIdx.x; p < M; p += stride) {
+    const int i = BI[p];
+    const float q = div_rn(S[i], den[i]);
+    gSb[p] = div_rn(div_rn(grad_ls[i], add_rn(eps, q)), den[i]);
+  }
+}
+
+__global__ void __launch_bounds__(kThreads) k_slice_hist(const float* __restrict__ t, const long long* __restrict__ b,
+                                                         long long N, long long B, int n_check,
+                                                         int* __restrict__ counts) {
+  __shared__ int hist[4096];
+  const long long nbins = B * n_check;
+  const bool sm = nbins <= 4096;
+  if (sm)
+    for (long long i = threadIdx.x; i < nbins; i += blockDim.x) hist[i] = 0;
+  __syncthreads();
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long j = blockIdx.x * (long long)blockDim.x + threadIdx.x; j < N; j += stride) {
+    const long long bj = b[j];
+    if (bj < 0 || bj >= B) continue;
+    long long s = (long long)mul_rn(t[j], (float)n_check);
+    s = s < 0 ? 0 : (s > n_check - 1 ? n_check - 1 : s);
+    if (sm) atomicAdd(hist + bj * n_check + s, 1);
+    else atomicAdd(counts + bj * n_check + s, 1);
+  }
+  __syncthreads();
+  if (sm)
+    for (long long i = threadIdx.x; i < nbins; i += blockDim.x)
+      if (hist[i]) atomicAdd(counts + i, hist[i]);
+}
+
+__global__ void k_slice_centres(PlanConsts P, float* sc) {
+  const int s = blockIdx.x * blockDim.x + threadIdx.x;
+  if (s < P.S) sc[s] = slice_centre(P, s);
+}
+
+// velocity-field gradient at the dequantised positions stored in ev4 (x, y in the first two lanes)
+__global__ void __launch_bounds__(kThreads) k_exact_vbwd_dense(MotionView Mv, const float2* __restrict__ gv,
+                                                               const float4* __restrict__ ev4,
+                                                               const long long* __restrict__ b, long long N,
+                                                               float* __restrict__ ggrid) {
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  const long long plane = Mv.Hg * Mv.Wg;
+  for (long long j = blockIdx.x * (long long)blockDim.x + threadIdx.x; j < N; j += stride) {
+    const float2 g = gv[j];
+    if ((g.x == 0.f && g.y == 0.f) || b[j] < 0 || b[j] >= Mv.B) continue;
+    const float4 e = ev4[j];
+    DenseTaps T;
+    dense_taps(Mv, e.x, e.y, &T);
+    float* G = ggrid + b[j] * 2 * plane;
+    const long long idx[4] = {T.y0 * Mv.Wg + T.x0, T.y0 * Mv.Wg + T.x1, T.y1 * Mv.Wg + T.x0, T.y1 * Mv.Wg + T.x1};
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      if (T.w[q] == 0.f) continue;
+      red_add_f1(G + idx[q], g.x * T.w[q]);
+      red_add_f1(G + plane + idx[q], g.y * T.w[q]);
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kThreads) k_exact_vbwd_param(MotionView Mv, const float2* __restrict__ gv,
+                                                               const float4* __restrict__ ev4,
+                                                               const long long* __restrict__ b, long long N,
+                                                               float* __restrict__ gtheta) {
+  // per-warp partial sums for batch 0..B-1 are rare to mix: accumulate per event with atomics on the
+  // (B, 2|6) parameters after a warp reduction over runs of equal batch index
+  const int np = Mv.kind == ATLB_MOTION_TRANSLATION ? 2 : 6;
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long j0 = blockIdx.x * (long long)blockDim.x; j0 < N; j0 += stride) {
+    const long long j = j0 + threadIdx.x;
+    float c[6] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    long long bj = -1;
+    if (j < N) {
+      bj = b[j];
+      const float2 g = gv[j];
+      const float4 e = ev4[j];
+      const float d0 = sub_rn(e.x, Mv.cx), d1 = sub_rn(e.y, Mv.cy);
+      c[0] = g.x; c[1] = g.y; c[2] = g.x * d0; c[3] = g.x * d1; c[4] = g.y * d0; c[5] = g.y * d1;
+      if (bj < 0 || bj >= Mv.B) bj = -1;
+    }
+    const long long b0 = __shfl_sync(0xffffffffu, bj, 0);
+    const bool uniform = __all_sync(0xffffffffu, bj == b0);
+    if (uniform) {
+      for (int q = 0; q < np; ++q) c[q] = warp_sum(c[q]);
+      if ((threadIdx.x & 31) == 0 && b0 >= 0)
+        for (int q = 0; q < np; ++q) atomicAdd(gtheta + b0 * np + q, c[q]);
+    } else if (bj >= 0) {
+      for (int q = 0; q < np; ++q) atomicAdd(gtheta + bj * np + q, c[q]);
+    }
+  }
+}
+
+struct ExactWs {
+  int* counts;
+  int* start;
+  long long* partials;
+  float4* YV;
+  float2* TI;
+  int* acounts;
+  int* astart;
+  float4* XT;
+  int* BI;
+  float* gSb;
+  int* slice_hist;
+  float* SC;
+  int* scratch;
+};
+
+size_t ws_layout(long long N, long long M, long long ncell, long long S, long long B, long long n_check,
+                 ExactWs* w, void* base) {
+  const long long nent = N * S;
+  size_t off = 0;
+  char* p = (char*)align_ptr(base ? base : (void*)256);
+  auto take = [&](size_t bytes) {
+    char* q = p + off;
+    off += align_up(bytes);
+    return (void*)q;
+  };
+  ExactWs x;
+  x.counts = (int*)take((size_t)ncell * 4);
+  x.start = (int*)take((size_t)(ncell + 1) * 4);
+  x.partials = (long long*)take(scan_partials_bytes(ncell));
+  x.YV = (float4*)take((size_t)nent * 16);
+  x.TI = (float2*)take((size_t)nent * 8);
+  x.acounts = (int*)take((size_t)ncell * 4);
+  x.astart = (int*)take((size_t)(ncell + 1) * 4);
+  x.XT = (float4*)take((size_t)M * 16);
+  x.BI = (int*)take((size_t)M * 4);
+  x.gSb = (float*)take((size_t)M * 4);
+  x.slice_hist = (int*)take((size_t)(B * n_check) * 4);
+  x.SC = (float*)take((size_t)S * 4);
+  x.scratch = (int*)take(64);
+  if (w) *w = x;
+  return off + 256;
+}
+
+int warp_grid(long long nwarps) { return clamp_grid(blocks_for(nwarps * 32, kThreads)); }
+
+}  // namespace
+
+size_t exact_workspace_bytes(const atlb_exact_cfg& c, long long N, long long M, const atlb_plan_geom& g) {
+  const long long ncell = c.B * (long long)g.S * g.GH * g.GW;
+  return ws_layout(N, M, ncell, g.S, c.B, c.n_check, nullptr, nullptr);
+}
+
+static MotionView motion_of(const atlb_exact_cfg& c) {
+  return make_motion_view(c.kind, c.theta, c.Bt, c.Hg, c.Wg, c.H, c.W);
+}
+
+int exact_prepare(const atlb_exact_cfg& c, const float* xy, const float* u, const float* t, const long long* b,
+                  long long N, const long long* anchors, const float* z, long long M, float* ev4, float* anc4,
+                  long long* anc_b, void* scratch, atlb_plan_geom* geom, cudaStream_t s) {
+  int* r = (int*)scratch;
+  launch(k_exact_init, 1, 32, 0, s, r);
+  const MotionView Mv = motion_of(c);
+  if (N > 0)
+    launch(k_exact_events, grid_for(N), kThreads, 0, s, Mv, (const float2*)xy, (const float2*)u, t, b, N, c.B,
+           (float4*)ev4, r);
+  if (M > 0)
+    launch(k_exact_anchors, grid_for(M), kThreads, 0, s, (const float4*)ev4, t, b, N, anchors, (const float2*)z,
+           (float)c.h, M, (float4*)anc4, anc_b, r);
+  int host[8];
+  if (cudaMemcpyAsync(host, r, sizeof(host), cudaMemcpyDeviceToHost, s) != cudaSuccess)
+    return launch_status("exact_prepare copy");
+  if (cudaStreamSynchronize(s) != cudaSuccess) return launch_status("exact_prepare sync");
+  if (int st = launch_status("exact_prepare")) return st;
+  if (host[5]) { set_error("exact_prepare: an anchor index lies outside [0, %lld)", N); return ATLB_ERR_ARG; }
+  if (host[7]) { set_error("exact_prepare: a batch index lies outside [0, %lld)", (long long)c.B); return ATLB_ERR_ARG; }
+  if (host[6]) { set_error("exact_prepare: events are not sorted by (b, t)"); return ATLB_ERR_UNSORTED; }
+  float vmax;
+  memcpy(&vmax, &host[0], 4);
+  plan_geometry_host(N > 0 ? vmax : 0.f, M > 0, ordered_to_float(host[1]), ordered_to_float(host[2]),
+                     ordered_to_float(host[3]), ordered_to_float(host[4]), c.H, c.W, c.h, c.cut, c.S, geom);
+  return ATLB_OK;
+}
+
+int exact_forward(const atlb_exact_cfg& c, const float* t, const long long* b, long long N, long long M,
+                  const float* ev4, const float* anc4, const long long* anc_b, const atlb_plan_geom& g, void* ws,
+                  float* S_out, float* den_out, float* ls_out, cudaStream_t s) {
+  const long long ncell = c.B * (long long)g.S * g.GH * g.GW;
+  ExactWs w;
+  ws_layout(N, M, ncell, g.S, c.B, c.n_check, &w, ws);
+  const PlanConsts P = make_plan_consts(g, c.tau, c.B);
+  // slice centres, entries and anchors
+  launch(k_slice_centres, (unsigned)((g.S + 127) / 128), 128, 0, s, P, w.SC);
+  cudaMemsetAsync(w.counts, 0, (size_t)ncell * 4, s);
+  cudaMemsetAsync(w.acounts, 0, (size_t)ncell * 4, s);
+  if (N > 0) launch(k_fast_count, slice_grid(N, P.S), kThreads, 0, s, P, (const float4*)ev4, t, b, N, w.counts);
+  if (M > 0) launch(k_fast_anchor_count, grid_for(M), kThreads, 0, s, P, (const float4*)anc4, anc_b, M, w.acounts);
+  exclusive_scan<int>(w.counts, ncell, w.partials, w.start, s);
+  if (N > 0)
+    launch(k_fast_scatter, slice_grid(N, P.S), kThreads, 0, s, P, (const float4*)ev4, t, b, N, (const int*)w.start,
+           w.counts, w.YV, w.TI);
+  exclusive_scan<int>(w.acounts, ncell, w.partials, w.astart, s);
+  if (M > 0)
+    launch(k_fast_anchor_scatter, grid_for(M), kThreads, 0, s, P, (const float4*)anc4, anc_b, M,
+           (const int*)w.astart, w.acounts, w.XT, w.BI);
+  // normaliser
+  const MotionView Mv = motion_of(c);
+  NormConsts K;
+  K.tau = c.tau;
+  K.tau_f = (float)c.tau;
+  K.pi_f = (float)M_PI;
+  K.h2_f = (float)(c.h * c.h);
+  K.wmax = (float)(c.W - 1);
+  K.hmax = (float)(c.H - 1);
+  K.n_check = (int)c.n_check;
+  K.visibility = c.visibility;
+  cudaMemsetAsync(w.slice_hist, 0, (size_t)(c.B * c.n_check) * 4, s);
+  if (c.visibility && N > 0)
+    launch(k_slice_hist, clamp_grid(blocks_for(N, kThreads * 16)), kThreads, 0, s, t, b, N, c.B, (int)c.n_check,
+           w.slice_hist);
+  if (M > 0)
+    launch(k_exact_norm, grid_for(M), kThreads, 0, s, Mv, K, (const float4*)anc4, anc_b, M, t, b, N,
+           (const int*)w.slice_hist, den_out);
+  // pair sums + log scores
+  const FastEntries E{w.YV, w.TI};
+  const FastAnchors A{w.XT, w.BI};
+  const CellGrid G{g.GW, g.GH, g.S, ncell};
+  const PairConsts C = make_pair_consts(c.h, c.tau, c.cut);
+  const float eps = (float)(c.eps_frac / (double)(c.H * c.W));
+  if (M > 0 && ncell > 0) {
+    static bool attr = false;
+    if (!attr) {
+      cudaFuncSetAttribute(k_pair_fwd_tiled<FusedOut>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)sizeof(TileSmemFwd));
+      attr = true;
+    }
+    const dim3 grid((unsigned)(((g.GW + kTileX - 1) / kTileX) * ((g.GH + kTileY - 1) / kTileY)),
+                    (unsigned)(c.B * g.S), 1);
+    cudaEvent_t e0 = timing_begin(s);
+    launch(k_pair_fwd_tiled<FusedOut>, grid, kTileThreads, sizeof(TileSmemFwd), s, E, A, (const int*)w.astart,
+           (const int*)w.start, G, (const float*)w.SC, C, FusedOut{S_out, ls_out, den_out, w.BI, eps});
+    timing_end("k_pair_fwd", s, e0);
+  }
+  return launch_status("exact_forward");
+}
+
+int exact_backward(const atlb_exact_cfg& c, const float* grad_ls, const long long* b, long long N, long long M,
+                   const float* ev4, const atlb_plan_geom& g, void* ws, const float* S, const float* den, float* gv,
+                   float* gtheta, cudaStream_t s) {
+  const long long ncell = c.B * (long long)g.S * g.GH * g.GW;
+  ExactWs w;
+  ws_layout(N, M, ncell, g.S, c.B, c.n_check, &w, ws);
+  const float eps = (float)(c.eps_frac / (double)(c.H * c.W));
+  cudaMemsetAsync(gv, 0, (size_t)N * 2 * sizeof(float), s);
+  const FastEntries E{w.YV, w.TI};
+  const FastAnchors A{w.XT, w.BI};
+  const CellGrid G{g.GW, g.GH, g.S, ncell};
+  const PairConsts C = make_pair_consts(c.h, c.tau, c.cut);
+  if (M > 0 && ncell > 0) {
+    launch(k_exact_gs, grid_for(M), kThreads, 0, s, (const int*)w.BI, M, grad_ls, S, den, eps, w.gSb);
+    static bool attr = false;
+    if (!attr) {
+      cudaFuncSetAttribute(k_pair_bwd_tiled, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(TileSmemBwd));
+      attr = true;
+    }
+    const dim3 grid((unsigned)(((g.GW + kTileX - 1) / kTileX) * ((g.GH + kTileY - 1) / kTileY)),
+                    (unsigned)(c.B * g.S), 1);
+    cudaEvent_t e0 = timing_begin(s);
+    launch(k_pair_bwd_tiled, grid, kTileThreads, sizeof(TileSmemBwd), s, E, A, (const int*)w.astart,
+           (const float*)w.gSb, (const int*)w.start, G, (const float*)w.SC, C, N, gv);
+    timing_end("k_pair_bwd", s, e0);
+  }
+  const MotionView Mv = motion_of(c);
+  const size_t nth = c.kind == ATLB_MOTION_DENSE ? (size_t)(c.Bt * 2 * c.Hg * c.Wg)
+                                                 : (size_t)(c.Bt * (c.kind == ATLB_MOTION_TRANSLATION ? 2 : 6));
+  cudaMemsetAsync(gtheta, 0, nth * sizeof(float), s);
+  if (N > 0) {
+    if (c.kind == ATLB_MOTION_DENSE)
+      launch(k_exact_vbwd_dense, grid_for(N), kThreads, 0, s, Mv, (const float2*)gv, (const float4*)ev4, b, N, gtheta);
+    else
+      launch(k_exact_vbwd_param, grid_for(N), kThreads, 0, s, Mv, (const float2*)gv, (const float4*)ev4, b, N, gtheta);
+  }
+  return launch_status("exact_backward");
+}
+
+}  // namespace atlb

@@ -76,16 +76,30 @@ __global__ void __launch_bounds__(kThreads) k_velocity_bwd_dense(MotionView Mv, 
   }
 }
 
+// Per-(batch, slice) event counts (ats.py:39-41).  Events are time-sorted, so neighbouring threads hit
+// the same counter: counts are aggregated in shared memory first (one global atomic per bin per CTA).
+constexpr int kMaxSmemBins = 8192;
 __global__ void __launch_bounds__(kThreads) k_slice_counts(const float* __restrict__ t,
                                                            const long long* __restrict__ b, long long N, long long B,
                                                            int n_check, int* __restrict__ counts) {
+  __shared__ int hist[kMaxSmemBins];
+  const long long nbins = B * n_check;
+  const bool use_smem = nbins <= kMaxSmemBins;
+  if (use_smem)
+    for (long long i = threadIdx.x; i < nbins; i += blockDim.x) hist[i] = 0;
+  __syncthreads();
   const long long stride = (long long)gridDim.x * blockDim.x;
   for (long long j = blockIdx.x * (long long)blockDim.x + threadIdx.x; j < N; j += stride) {
     if (b[j] < 0 || b[j] >= B) continue;
     long long s = (long long)mul_rn(t[j], (float)n_check);  // (ev.t * n_check).long(): truncation
     s = s < 0 ? 0 : (s > n_check - 1 ? n_check - 1 : s);
-    atomicAdd(counts + b[j] * n_check + s, 1);
+    if (use_smem) atomicAdd(hist + b[j] * n_check + s, 1);
+    else atomicAdd(counts + b[j] * n_check + s, 1);
   }
+  __syncthreads();
+  if (use_smem)
+    for (long long i = threadIdx.x; i < nbins; i += blockDim.x)
+      if (hist[i]) atomicAdd(counts + i, hist[i]);
 }
 
 __global__ void __launch_bounds__(kThreads) k_visible_fraction(MotionView Mv, const float2* __restrict__ xa,
@@ -186,7 +200,7 @@ int visible_fraction(const MotionView& Mv, const float* xa, const float* ta, con
                      void* scratch, cudaStream_t s) {
   int* counts = (int*)scratch;
   cudaMemsetAsync(counts, 0, (size_t)(Mv.B * n_check) * sizeof(int), s);
-  if (N > 0) launch(k_slice_counts, grid_for(N), kThreads, 0, s, t, b, N, Mv.B, (int)n_check, counts);
+  if (N > 0) launch(k_slice_counts, clamp_grid(blocks_for(N, kThreads * 16)), kThreads, 0, s, t, b, N, Mv.B, (int)n_check, counts);
   if (M > 0)
     launch(k_visible_fraction, grid_for(M), kThreads, 0, s, Mv, (const float2*)xa, ta, ba, M, counts, (int)n_check,
                                                         (float)tau, (float)(Mv.W - 1), (float)(Mv.H - 1), out);

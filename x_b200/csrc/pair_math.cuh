@@ -9,6 +9,7 @@ struct PairConsts {
   float r2max;   // cut*cut*h*h in fp32, left to right (atl_cpu.cpp:184)
   float inv2h2;  // 1 / (2 h h) in fp32 (atl_cpu.cpp:184)
   float invh2;   // 1 / (float)(h*h)   (atl_cpu.cpp:236)
+  float k2;      // log2(e) / (2 h h): exp(-d2 / 2h^2) = 2^(-d2 * k2)
 };
 
 inline PairConsts make_pair_consts(double h, double tau, double cut) {
@@ -23,6 +24,7 @@ inline PairConsts make_pair_consts(double h, double tau, double cut) {
   d = d * hf;
   C.inv2h2 = 1.f / d;
   C.invh2 = 1.f / (float)(h * h);
+  C.k2 = (float)(1.4426950408889634 / (2.0 * h * h));
   return C;
 }
 
@@ -39,6 +41,27 @@ __device__ __forceinline__ bool pair_test(const PairConsts& C, float xi, float y
 }
 
 __device__ __forceinline__ float pair_kernel(const PairConsts& C, float d2) { return expf(mul_rn(-d2, C.inv2h2)); }
+
+// 2^x with the SFU (PTX ex2.approx: relative error below 2^-22).  exp(-d2 / 2h^2) as 2^(-d2 k2) differs
+// from expf by < 1e-6 relative for the kernel's range d2 <= (cut h)^2.
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Branch-free pair evaluation for the fused kernels: the same acceptance test as pair_test (exact
+// rounding of r and d^2), the kernel value selected to 0 for rejected pairs.
+__device__ __forceinline__ float pair_eval(const PairConsts& C, float xi, float yi, float ti, float dti, float2 sy,
+                                           float2 sv, float st, bool same, float* rx, float* ry, float* dt) {
+  *dt = sub_rn(ti, st);
+  *rx = sub_rn(xi, add_rn(sy.x, mul_rn(sv.x, dti)));
+  *ry = sub_rn(yi, add_rn(sy.y, mul_rn(sv.y, dti)));
+  const float d2 = add_rn(mul_rn(*rx, *rx), mul_rn(*ry, *ry));
+  const bool ok = !(fabsf(*dt) > C.tau) && !(d2 > C.r2max) && !same;
+  const float e = ex2_approx(-d2 * C.k2);
+  return ok ? e : 0.f;
+}
 
 // f = gS_i * k * dt / h^2, in the reference's order (atl_cpu.cpp:244).
 __device__ __forceinline__ float pair_grad_factor(const PairConsts& C, float gi, float kern, float dt) {

@@ -71,21 +71,22 @@ __global__ void __launch_bounds__(kThreads) k_geom_reduce(const float2* __restri
   }
 }
 
+// Slice-major passes: blockIdx.y walks the slices, so at any moment the writes of the scatter pass
+// land in one slice's part of the plan (~1/S of it), which stays in L2 until its sectors are full.
 __global__ void __launch_bounds__(kThreads) k_plan_count(PlanConsts P, const float2* __restrict__ x,
                                                          const float* __restrict__ t, const float2* __restrict__ v,
                                                          const long long* __restrict__ b, long long N,
                                                          int* __restrict__ counts) {
   const long long stride = (long long)gridDim.x * blockDim.x;
-  for (long long j = blockIdx.x * (long long)blockDim.x + threadIdx.x; j < N; j += stride) {
-    const float tj = t[j];
-    int s_lo, s_hi;
-    slice_range(P, tj, &s_lo, &s_hi);
-    if (s_lo > s_hi) continue;
-    const float2 xj = x[j], vj = v[j];
-    const long long bj = b[j];
-    for (int s = s_lo; s <= s_hi; ++s) {
+  for (int s = blockIdx.y; s < P.S; s += gridDim.y) {
+    for (long long j = blockIdx.x * (long long)blockDim.x + threadIdx.x; j < N; j += stride) {
+      const float tj = t[j];
+      int s_lo, s_hi;
+      slice_range(P, tj, &s_lo, &s_hi);
+      if (s < s_lo || s > s_hi) continue;
+      const float2 xj = x[j], vj = v[j];
       float yx, yy;
-      const long long key = source_key(P, xj.x, xj.y, vj.x, vj.y, tj, bj, s, &yx, &yy);
+      const long long key = source_key(P, xj.x, xj.y, vj.x, vj.y, tj, b[j], s, &yx, &yy);
       if (key >= 0) atomicAdd(counts + key, 1);
     }
   }
@@ -99,16 +100,15 @@ __global__ void __launch_bounds__(kThreads) k_plan_scatter(PlanConsts P, const f
                                                            float2* __restrict__ src_v, float* __restrict__ src_t,
                                                            long long* __restrict__ src_id) {
   const long long stride = (long long)gridDim.x * blockDim.x;
-  for (long long j = blockIdx.x * (long long)blockDim.x + threadIdx.x; j < N; j += stride) {
-    const float tj = t[j];
-    int s_lo, s_hi;
-    slice_range(P, tj, &s_lo, &s_hi);
-    if (s_lo > s_hi) continue;
-    const float2 xj = x[j], vj = v[j];
-    const long long bj = b[j];
-    for (int s = s_lo; s <= s_hi; ++s) {
+  for (int s = blockIdx.y; s < P.S; s += gridDim.y) {
+    for (long long j = blockIdx.x * (long long)blockDim.x + threadIdx.x; j < N; j += stride) {
+      const float tj = t[j];
+      int s_lo, s_hi;
+      slice_range(P, tj, &s_lo, &s_hi);
+      if (s < s_lo || s > s_hi) continue;
+      const float2 xj = x[j], vj = v[j];
       float yx, yy;
-      const long long key = source_key(P, xj.x, xj.y, vj.x, vj.y, tj, bj, s, &yx, &yy);
+      const long long key = source_key(P, xj.x, xj.y, vj.x, vj.y, tj, b[j], s, &yx, &yy);
       if (key < 0) continue;
       const long long p = cell_start[key] + atomicAdd(cursor + key, 1);
       src_y[p] = make_float2(yx, yy);
@@ -151,6 +151,16 @@ __global__ void __launch_bounds__(kThreads) k_plan_anchors(PlanConsts P, const f
 }
 
 }  // namespace
+
+// (x over events, y over slices): enough CTAs to fill the GPU, slices striding by gridDim.y.
+dim3 slice_grid(long long N, int S) {
+  const long long bx = blocks_for(N, kThreads);
+  const long long by = S < 65535 ? S : 65535;
+  const long long cap = 148LL * 32;
+  long long gx = bx;
+  if (gx * by > cap) gx = (cap + by - 1) / by;
+  return dim3((unsigned)(gx < 1 ? 1 : gx), (unsigned)by, 1);
+}
 
 // Host-side geometry, functional.py:139-149, in double exactly as the reference's Python computes it.
 void plan_geometry_host(float vmax, bool have_anchors, float mnx, float mny, float mxx, float mxy, long long H,
@@ -225,9 +235,7 @@ int plan_count(const float* x, const float* t, const float* v, const long long* 
   long long* partials = (long long*)(p + align_up((size_t)ncell * sizeof(int)));
   cudaMemsetAsync(counts, 0, (size_t)ncell * sizeof(int), s);
   const PlanConsts P = make_plan_consts(*g, tau, B);
-  if (N > 0)
-    launch(k_plan_count, clamp_grid(blocks_for(N, kThreads)), kThreads, 0, s, P, (const float2*)x, t, (const float2*)v, b,
-                                                                        N, counts);
+  if (N > 0) launch(k_plan_count, slice_grid(N, P.S), kThreads, 0, s, P, (const float2*)x, t, (const float2*)v, b, N, counts);
   exclusive_scan<long long>(counts, ncell, partials, cell_start, s);
   if (cudaMemcpyAsync(n_entries, cell_start + ncell, sizeof(long long), cudaMemcpyDeviceToHost, s) != cudaSuccess)
     return launch_status("plan_count copy");
@@ -243,9 +251,8 @@ int plan_fill(const float* x, const float* t, const float* v, const long long* b
   int* cursor = (int*)p;  // zeroed by the scan of plan_count
   const PlanConsts P = make_plan_consts(*g, tau, B);
   if (N > 0)
-    launch(k_plan_scatter, clamp_grid(blocks_for(N, kThreads)), kThreads, 0, s, 
-        P, (const float2*)x, t, (const float2*)v, b, N, cell_start, cursor, (float2*)src_y, (float2*)src_v, src_t,
-        src_id);
+    launch(k_plan_scatter, slice_grid(N, P.S), kThreads, 0, s, P, (const float2*)x, t, (const float2*)v, b, N,
+           cell_start, cursor, (float2*)src_y, (float2*)src_v, src_t, src_id);
   const long long na = M > P.S ? M : P.S;
   launch(k_plan_anchors, clamp_grid(blocks_for(na, kThreads)), kThreads, 0, s, 
       P, (const float2*)x, t, b, anchors, (const float2*)anchor_xy, M, N, (float2*)anc_x, anc_t, anc_cell, anc_id,

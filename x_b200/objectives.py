@@ -11,6 +11,7 @@ device-resident step.
 """
 from __future__ import annotations
 
+import ctypes
 import math
 from typing import Optional
 
@@ -63,6 +64,59 @@ def visible_fraction(motion, xa, ta, ba, ev: EventPacket, tau: float, n_check: i
     return (vis / tot.clamp(min=1)).clamp(min=1e-3)
 
 
+class _FusedExact(torch.autograd.Function):
+    """AnchoredExact.log_scores (ats.py:84-96) as one libatlb200 pipeline (atlb_exact_*), differentiable
+    w.r.t. the motion parameters."""
+
+    @staticmethod
+    def forward(ctx, theta, xy, t, b, anchors, u, z, spec):
+        kind, B, H, W, h, tau, cut, eps_frac, S, visibility, n_check = spec
+        lib = L.lib()
+        dev = xy.device
+        th = theta.detach().float().contiguous()
+        Hg, Wg = (th.shape[-2], th.shape[-1]) if kind == L.MOTION_DENSE else (1, 1)
+        cfg = L.ExactCfg(kind, th.data_ptr(), th.shape[0], Hg, Wg, B, H, W, float(h), float(tau), float(cut),
+                         float(eps_frac), int(S), int(bool(visibility)), int(n_check))
+        xyc, tc, bc = xy.detach().float().contiguous(), t.detach().float().contiguous(), b.contiguous().long()
+        N = tc.shape[0]
+        anc = None if anchors is None else anchors.contiguous().long()
+        M = N if anc is None else anc.shape[0]
+        uc = None if u is None else u.detach().float().contiguous()
+        zc = None if z is None else z.detach().float().contiguous()
+        ev4 = torch.empty(N, 4, dtype=torch.float32, device=dev)
+        anc4 = torch.empty(M, 4, dtype=torch.float32, device=dev)
+        anc_b = torch.empty(M, dtype=torch.int64, device=dev)
+        scratch = torch.empty(64, dtype=torch.uint8, device=dev)
+        geom = L.PlanGeom()
+        L.check(lib.atlb_exact_prepare(ctypes.byref(cfg), L.ptr(xyc), L.ptr(uc), L.ptr(tc), L.ptr(bc), N, L.ptr(anc),
+                                       L.ptr(zc), M, L.ptr(ev4), L.ptr(anc4), L.ptr(anc_b), L.ptr(scratch),
+                                       ctypes.byref(geom), L.stream()), "exact_prepare")
+        nb = lib.atlb_exact_workspace_bytes(ctypes.byref(cfg), N, M, ctypes.byref(geom))
+        ws = L.workspace(nb, dev)
+        Sv = torch.empty(M, dtype=torch.float32, device=dev)
+        den = torch.empty(M, dtype=torch.float32, device=dev)
+        ls = torch.empty(M, dtype=torch.float32, device=dev)
+        L.check(lib.atlb_exact_forward(ctypes.byref(cfg), L.ptr(tc), L.ptr(bc), N, M, L.ptr(ev4), L.ptr(anc4),
+                                       L.ptr(anc_b), ctypes.byref(geom), L.ptr(ws), nb, L.ptr(Sv), L.ptr(den),
+                                       L.ptr(ls), L.stream()), "exact_forward")
+        ctx.save_for_backward(th, bc, ev4, ws, Sv, den)
+        ctx.meta = (cfg, geom, nb, N, M, theta.dtype, tuple(theta.shape))
+        ctx.S, ctx.den = Sv, den
+        return ls
+
+    @staticmethod
+    def backward(ctx, grad_ls):
+        th, bc, ev4, ws, Sv, den = ctx.saved_tensors
+        cfg, geom, nb, N, M, dtype, shape = ctx.meta
+        cfg.theta = th.data_ptr()
+        gv = torch.empty(N, 2, dtype=torch.float32, device=ev4.device)
+        gth = torch.empty(shape, dtype=torch.float32, device=ev4.device)
+        L.check(L.lib().atlb_exact_backward(ctypes.byref(cfg), L.ptr(grad_ls.contiguous().float()), L.ptr(bc), N, M,
+                                            L.ptr(ev4), ctypes.byref(geom), L.ptr(ws), nb, L.ptr(Sv), L.ptr(den),
+                                            L.ptr(gv), L.ptr(gth), L.stream()), "exact_backward")
+        return gth.to(dtype), None, None, None, None, None, None, None
+
+
 def _pick_anchors(ev: EventPacket, n_anchors: Optional[int], gen: Optional[torch.Generator]) -> torch.Tensor:
     """ats.py:53-57."""
     if n_anchors is None or n_anchors >= ev.n:
@@ -87,8 +141,9 @@ class AnchoredExact(Objective):
 
     def __init__(self, h: float = 1.0, tau: float = 1.0, eps_frac: float = 1e-2, n_anchors: Optional[int] = 20000,
                  n_slices: int = 16, cut: float = 3.0, seed: Optional[int] = None, smooth_anchors: bool = True,
-                 dequantize: bool = True, visibility: bool = True, anchor_margin: float = 0.0):
+                 dequantize: bool = True, visibility: bool = True, anchor_margin: float = 0.0, fused: bool = True):
         self.visibility, self.anchor_margin = visibility, anchor_margin
+        self.fused = fused  # one libatlb200 pipeline for the motion fields it implements
         self.h, self.tau, self.eps_frac, self.n_anchors, self.n_slices, self.cut = h, tau, eps_frac, n_anchors, n_slices, cut
         self.smooth_anchors, self.dequantize = smooth_anchors, dequantize
         self.gen = torch.Generator().manual_seed(seed) if seed is not None else None
@@ -111,6 +166,18 @@ class AnchoredExact(Objective):
         if not getattr(motion, "linear_at_event", False):
             raise ValueError("AnchoredExact needs a motion that is linear at the event; use AnchoredSliced")
         anchors, u, z = self.draw(ev, anchors) if noise is None else noise
+        kind = _fused_kind(motion)
+        if self.fused and kind >= 0 and ev.xy.is_cuda:
+            spec = (kind, ev.batch_size, ev.height, ev.width, self.h, self.tau, self.cut, self.eps_frac,
+                    self.n_slices, self.visibility, 16)
+            try:
+                ls = _FusedExact.apply(motion.theta, ev.xy, ev.t, ev.b, anchors, u if self.dequantize else None,
+                                       z if self.smooth_anchors else None, spec)
+                return ls, anchors
+            except RuntimeError as e:
+                if "not sorted" not in str(e):
+                    raise
+                # unsorted events: the stage-by-stage path below sorts the window keys like the reference
         xs = ev.xy
         if self.dequantize:
             xs = xs + (u - 0.5)
