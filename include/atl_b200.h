@@ -38,7 +38,7 @@ enum {
 const char* atlb_last_error(void);
 /* ABI version of this header (bumped on incompatible changes). */
 int atlb_abi_version(void);
-#define ATLB_ABI_VERSION 1
+#define ATLB_ABI_VERSION 2
 /* Number of kernels this library has launched in the calling process (instrumentation; no reference
  * counterpart). */
 uint64_t atlb_kernel_launches(void);
@@ -86,6 +86,7 @@ typedef struct {
   int64_t GW, GH;      /* grid width / height in cells */
   float vmax;          /* max_j |v_j| (torch's row norm) */
   int32_t S;           /* number of slices */
+  float t_lo, t_hi;    /* event time range (atlb_exact_prepare; NaN when not computed) */
 } atlb_plan_geom;
 
 /* x (N,2) positions, v (N,2) velocities, anchors (M) event indices, anchor_xy (M,2) the positions the

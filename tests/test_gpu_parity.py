@@ -273,3 +273,29 @@ def test_fused_matches_stagewise_unsorted_fallback():
     ref = O.anchored_exact("translation", g["theta"], xs, g["t"][perm], g["b"][perm], B, H, W, np_(anchors), xa,
                            with_grad=False)
     np.testing.assert_allclose(np_(ls), ref["ls"], rtol=RTOL, atol=RTOL)
+
+
+@pytest.mark.parametrize("n,box", [(20000, 6.0), (6000, 40.0)])
+def test_fused_dense_clusters_vs_oracle(n, box):
+    """Events packed into a few pixels: tiles overflow their shared-memory staging (global-memory paths of
+    the tiled forward/backward and the overflow pass) and still match the oracle."""
+    from x_b200 import motion as Mo
+    from x_b200.events import EventPacket
+    from x_b200.objectives import AnchoredExact
+    rng = np.random.default_rng(5)
+    H, W = 64, 96
+    xy = np.stack([rng.integers(40, 40 + int(box), n), rng.integers(20, 20 + int(box), n)], 1).astype(np.float32)
+    t = np.sort(rng.uniform(0, 1, n)).astype(np.float32)
+    b = np.zeros(n, np.int64)
+    th = np.array([[3.0, -2.0]], np.float32)
+    ev = EventPacket(T(xy), T(t), torch.ones(n, device=DEV), T(b), 1, H, W)
+    m = Mo.Translation(1, H, W, init=T(th)).to(DEV)
+    obj = AnchoredExact(h=1.0, n_anchors=None, seed=9)
+    anchors, u, z = obj.draw(ev)
+    ls, _ = obj.log_scores(ev, m, noise=(anchors, u, z))
+    (-ls.mean()).backward()
+    xs = (xy + (np_(u) - np.float32(0.5))).astype(np.float32)
+    xa = (xs[np_(anchors)] + np_(z)).astype(np.float32)
+    ref = O.anchored_exact("translation", th, xs, t, b, 1, H, W, np_(anchors), xa)
+    np.testing.assert_allclose(np_(ls), ref["ls"], rtol=RTOL, atol=RTOL)
+    np.testing.assert_allclose(np_(m.theta.grad), ref["grad_theta"], rtol=1e-3, atol=1e-4 * np.abs(ref["grad_theta"]).max())

@@ -25,7 +25,8 @@ MOTION_TRANSLATION, MOTION_AFFINE, MOTION_DENSE = 0, 1, 2
 
 class PlanGeom(ctypes.Structure):
     _fields_ = [("cell", ctypes.c_double), ("ox", ctypes.c_double), ("oy", ctypes.c_double),
-                ("GW", ctypes.c_int64), ("GH", ctypes.c_int64), ("vmax", ctypes.c_float), ("S", ctypes.c_int32)]
+                ("GW", ctypes.c_int64), ("GH", ctypes.c_int64), ("vmax", ctypes.c_float), ("S", ctypes.c_int32),
+                ("t_lo", ctypes.c_float), ("t_hi", ctypes.c_float)]
 
 
 class ExactCfg(ctypes.Structure):

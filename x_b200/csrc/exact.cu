@@ -12,6 +12,8 @@
 //   backward  dL/dS from the upstream dL/dls, source-centric pair gradient, velocity-field gradient.
 // Every step keeps the reference's rounding, so scores match it to float accuracy and the plan's
 // cells are the reference's cells.
+#include <cstddef>
+
 #include "common.cuh"
 #include "motion_math.cuh"
 #include "pair_kernels.cuh"
@@ -32,13 +34,14 @@ constexpr int kThreads = 256;
 inline int grid_for(long long n) { return clamp_grid(blocks_for(n, kThreads)); }
 
 // scratch ints: [0] vmax bits, [1..4] anchor bbox (ordered ints), [5] bad anchor index,
-// [6] events not sorted by (b, t), [7] batch index outside [0, B)
+// [6] events not sorted by (b, t), [7] batch index outside [0, B), [8] / [9] min / max t (ordered ints)
 __global__ void k_exact_init(int* r) {
   if (threadIdx.x == 0) {
     r[0] = 0;
     r[1] = 0x7fffffff; r[2] = 0x7fffffff;
     r[3] = (int)0x80000000; r[4] = (int)0x80000000;
     r[5] = 0; r[6] = 0; r[7] = 0;
+    r[8] = 0x7fffffff; r[9] = (int)0x80000000;
   }
 }
 
@@ -47,9 +50,12 @@ __global__ void __launch_bounds__(kThreads) k_exact_events(MotionView Mv, const 
                                                            const long long* __restrict__ b, long long N, long long B,
                                                            float4* __restrict__ ev4, int* r) {
   float vm = 0.f;
-  int unsorted = 0, badb = 0;
+  int unsorted = 0, badb = 0, tmn = 0x7fffffff, tmx = (int)0x80000000;
   const long long stride = (long long)gridDim.x * blockDim.x;
   for (long long j = blockIdx.x * (long long)blockDim.x + threadIdx.x; j < N; j += stride) {
+    const int ot = float_to_ordered(t[j]);
+    tmn = min(tmn, ot);
+    tmx = max(tmx, ot);
     float2 p = xy[j];
     if (u) {  // ats.py:84-85: xs = xy + (u - 0.5)
       const float2 q = u[j];
@@ -77,11 +83,29 @@ __global__ void __launch_bounds__(kThreads) k_exact_events(MotionView Mv, const 
     vb = max(vb, __shfl_xor_sync(0xffffffffu, vb, o));
     unsorted |= __shfl_xor_sync(0xffffffffu, unsorted, o);
     badb |= __shfl_xor_sync(0xffffffffu, badb, o);
+    tmn = min(tmn, __shfl_xor_sync(0xffffffffu, tmn, o));
+    tmx = max(tmx, __shfl_xor_sync(0xffffffffu, tmx, o));
   }
+  // one atomic per CTA and quantity (warp results combined in shared memory first)
+  __shared__ int red[5];
+  if (threadIdx.x == 0) {
+    red[0] = 0; red[1] = 0; red[2] = 0; red[3] = 0x7fffffff; red[4] = (int)0x80000000;
+  }
+  __syncthreads();
   if ((threadIdx.x & 31) == 0) {
-    atomicMax(r + 0, vb);
-    if (unsorted) atomicOr(r + 6, 1);
-    if (badb) atomicOr(r + 7, 1);
+    atomicMax(red + 0, vb);
+    atomicOr(red + 1, unsorted);
+    atomicOr(red + 2, badb);
+    atomicMin(red + 3, tmn);
+    atomicMax(red + 4, tmx);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    atomicMax(r + 0, red[0]);
+    if (red[1]) atomicOr(r + 6, 1);
+    if (red[2]) atomicOr(r + 7, 1);
+    atomicMin(r + 8, red[3]);
+    atomicMax(r + 9, red[4]);
   }
 }
 
@@ -122,10 +146,21 @@ __global__ void __launch_bounds__(kThreads) k_exact_anchors(const float4* __rest
     mxy = max(mxy, __shfl_xor_sync(0xffffffffu, mxy, o));
     bad |= __shfl_xor_sync(0xffffffffu, bad, o);
   }
+  __shared__ int red[5];
+  if (threadIdx.x == 0) {
+    red[0] = 0x7fffffff; red[1] = 0x7fffffff; red[2] = (int)0x80000000; red[3] = (int)0x80000000; red[4] = 0;
+  }
+  __syncthreads();
   if ((threadIdx.x & 31) == 0) {
-    atomicMin(r + 1, mnx); atomicMin(r + 2, mny);
-    atomicMax(r + 3, mxx); atomicMax(r + 4, mxy);
-    if (bad) atomicOr(r + 5, 1);
+    atomicMin(red + 0, mnx); atomicMin(red + 1, mny);
+    atomicMax(red + 2, mxx); atomicMax(red + 3, mxy);
+    atomicOr(red + 4, bad);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    atomicMin(r + 1, red[0]); atomicMin(r + 2, red[1]);
+    atomicMax(r + 3, red[2]); atomicMax(r + 4, red[3]);
+    if (red[4]) atomicOr(r + 5, 1);
   }
 }
 
@@ -148,6 +183,10 @@ __global__ void __launch_bounds__(kThreads) k_fast_count(PlanConsts P, const flo
   }
 }
 
+// Four (source, slice) entries per thread and round: their cursor atomics are independent, so four are
+// in flight before the first result is needed (a single returning atomic per thread leaves the SM
+// waiting on L2 latency).
+constexpr int kScatterILP = 4;
 __global__ void __launch_bounds__(kThreads) k_fast_scatter(PlanConsts P, const float4* __restrict__ ev4,
                                                            const float* __restrict__ t, const long long* __restrict__ b,
                                                            long long N, const int* __restrict__ start,
@@ -155,18 +194,37 @@ __global__ void __launch_bounds__(kThreads) k_fast_scatter(PlanConsts P, const f
                                                            float2* __restrict__ TI) {
   const long long stride = (long long)gridDim.x * blockDim.x;
   for (int s = blockIdx.y; s < P.S; s += gridDim.y) {
-    for (long long j = blockIdx.x * (long long)blockDim.x + threadIdx.x; j < N; j += stride) {
-      const float tj = t[j];
-      int s_lo, s_hi;
-      slice_range(P, tj, &s_lo, &s_hi);
-      if (s < s_lo || s > s_hi) continue;
-      const float4 e = ev4[j];
-      float yx, yy;
-      const long long key = source_key(P, e.x, e.y, e.z, e.w, tj, b[j], s, &yx, &yy);
-      if (key < 0) continue;
-      const int p = start[key] + atomicAdd(cursor + key, 1);
-      YV[p] = make_float4(yx, yy, e.z, e.w);
-      TI[p] = make_float2(tj, __int_as_float((int)j));
+    for (long long j0 = blockIdx.x * (long long)blockDim.x + threadIdx.x; j0 < N; j0 += stride * kScatterILP) {
+      long long key[kScatterILP];
+      float4 rec[kScatterILP];
+      float tt[kScatterILP];
+#pragma unroll
+      for (int q = 0; q < kScatterILP; ++q) {
+        const long long j = j0 + q * stride;
+        key[q] = -1;
+        if (j < N) {
+          const float tj = t[j];
+          int s_lo, s_hi;
+          slice_range(P, tj, &s_lo, &s_hi);
+          if (s >= s_lo && s <= s_hi) {
+            const float4 e = ev4[j];
+            float yx, yy;
+            key[q] = source_key(P, e.x, e.y, e.z, e.w, tj, b[j], s, &yx, &yy);
+            rec[q] = make_float4(yx, yy, e.z, e.w);
+            tt[q] = tj;
+          }
+        }
+      }
+      int pos[kScatterILP];
+#pragma unroll
+      for (int q = 0; q < kScatterILP; ++q) pos[q] = key[q] >= 0 ? atomicAdd(cursor + key[q], 1) : 0;
+#pragma unroll
+      for (int q = 0; q < kScatterILP; ++q) {
+        if (key[q] < 0) continue;
+        const int p = start[key[q]] + pos[q];
+        YV[p] = rec[q];
+        TI[p] = make_float2(tt[q], __int_as_float((int)(j0 + q * stride)));
+      }
     }
   }
 }
@@ -250,19 +308,59 @@ __global__ void __launch_bounds__(kThreads) k_exact_norm(MotionView Mv, NormCons
   }
 }
 
+// Writes S_i and the log score log(eps + S_i / den_i) of original anchor i.
 struct FusedOut {
   float* S;
   float* ls;
   const float* den;
-  const int* idx;
   float eps;
-  __device__ __forceinline__ void operator()(int p, double v) const {
-    const int i = idx[p];
+  __device__ __forceinline__ void operator()(int i, double v) const {
     const float s = (float)v;
     S[i] = s;
     ls[i] = logf(add_rn(eps, div_rn(s, den[i])));  // log(eps + S / den)
   }
 };
+
+// Bucket index -> original anchor index, for the untiled kernel of pair_kernels.cuh.
+struct BucketOut {
+  FusedOut o;
+  const int* idx;
+  __device__ __forceinline__ void operator()(int p, double v) const { o(idx[p], v); }
+};
+
+// Cells of tiles that held more anchors than the tiled kernel stages: one warp per such cell, candidates
+// from global memory (the untiled forward of pair_kernels.cuh, restricted to those cells).
+__global__ void __launch_bounds__(kThreads) k_fwd_overflow(FastEntries E, FastAnchors A, const int* __restrict__ astart,
+                                                           const int* __restrict__ cstart, TileGrid T, CellGrid G,
+                                                           const float* __restrict__ SC, PairConsts C, BucketOut out,
+                                                           const int* __restrict__ overflow) {
+  if (*overflow == 0) return;
+  const int lane = threadIdx.x & 31;
+  const long long nwarps = ((long long)gridDim.x * blockDim.x) >> 5;
+  for (long long c = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5; c < G.ncell; c += nwarps) {
+    const int a0 = astart[c], a1 = astart[c + 1];
+    if (a0 == a1) continue;
+    long long cx, cy, g;
+    cell_coords<int>(c, G, &cx, &cy, &g);
+    // the cell's tile and its anchor count (as the tiled kernel saw it)
+    const int tx0 = (int)(cx >> kTileXLog) << kTileXLog, ty0 = (int)(cy / kTileY) * kTileY;
+    const int tx1 = min(tx0 + kTileX, T.GW), ty1 = min(ty0 + kTileY, T.GH);
+    const long long gbase = g * G.GH * G.GW;
+    int na = 0;
+    for (int y = ty0; y < ty1; ++y) na += astart[gbase + (long long)y * G.GW + tx1] - astart[gbase + (long long)y * G.GW + tx0];
+    if (na <= kTileAncCap) continue;
+    const float cs = __ldg(SC + g % G.S);
+    const long long xlo = cx > 0 ? cx - 1 : 0, xhi = cx + 1 < G.GW ? cx + 1 : G.GW - 1;
+    const long long ylo = cy > 0 ? cy - 1 : 0, yhi = cy + 1 < G.GH ? cy + 1 : G.GH - 1;
+    for (int base = a0; base < a1; base += 4) {
+      const int n = min(4, a1 - base);
+      if (n == 4) fwd_group<4>(E, A, base, cstart, gbase, G.GW, ylo, yhi, xlo, xhi, cs, C, out, lane);
+      else if (n == 3) fwd_group<3>(E, A, base, cstart, gbase, G.GW, ylo, yhi, xlo, xhi, cs, C, out, lane);
+      else if (n == 2) fwd_group<2>(E, A, base, cstart, gbase, G.GW, ylo, yhi, xlo, xhi, cs, C, out, lane);
+      else fwd_group<1>(E, A, base, cstart, gbase, G.GW, ylo, yhi, xlo, xhi, cs, C, out, lane);
+    }
+  }
+}
 
 // dL/dS in bucket order from the upstream dL/dls (torch's LogBackward then DivBackward).
 __global__ void __launch_bounds__(kThreads) k_exact_gs(const int* __restrict__ BI, long long M,
@@ -408,6 +506,13 @@ size_t ws_layout(long long N, long long M, long long ncell, long long S, long lo
 
 int warp_grid(long long nwarps) { return clamp_grid(blocks_for(nwarps * 32, kThreads)); }
 
+// Every pair passes |t_i - t_j| <= tau when tau covers the events' time range: fl(t_i - t_j) never exceeds
+// fl(t_hi - t_lo) (rounding is monotonic).  NaN bounds (unknown range) fail the test.
+bool tau_covers(const atlb_plan_geom& g, double tau) {
+  const float span = g.t_hi - g.t_lo;
+  return span <= (float)tau;
+}
+
 }  // namespace
 
 size_t exact_workspace_bytes(const atlb_exact_cfg& c, long long N, long long M, const atlb_plan_geom& g) {
@@ -431,7 +536,7 @@ int exact_prepare(const atlb_exact_cfg& c, const float* xy, const float* u, cons
   if (M > 0)
     launch(k_exact_anchors, grid_for(M), kThreads, 0, s, (const float4*)ev4, t, b, N, anchors, (const float2*)z,
            (float)c.h, M, (float4*)anc4, anc_b, r);
-  int host[8];
+  int host[10];
   if (cudaMemcpyAsync(host, r, sizeof(host), cudaMemcpyDeviceToHost, s) != cudaSuccess)
     return launch_status("exact_prepare copy");
   if (cudaStreamSynchronize(s) != cudaSuccess) return launch_status("exact_prepare sync");
@@ -443,6 +548,10 @@ int exact_prepare(const atlb_exact_cfg& c, const float* xy, const float* u, cons
   memcpy(&vmax, &host[0], 4);
   plan_geometry_host(N > 0 ? vmax : 0.f, M > 0, ordered_to_float(host[1]), ordered_to_float(host[2]),
                      ordered_to_float(host[3]), ordered_to_float(host[4]), c.H, c.W, c.h, c.cut, c.S, geom);
+  if (N > 0) {
+    geom->t_lo = ordered_to_float(host[8]);
+    geom->t_hi = ordered_to_float(host[9]);
+  }
   return ATLB_OK;
 }
 
@@ -492,18 +601,32 @@ int exact_forward(const atlb_exact_cfg& c, const float* t, const long long* b, l
   const PairConsts C = make_pair_consts(c.h, c.tau, c.cut);
   const float eps = (float)(c.eps_frac / (double)(c.H * c.W));
   if (M > 0 && ncell > 0) {
+    // the entry times (last member) are only staged when tau does not cover the window
+    const size_t smem_all = sizeof(TileSmemFwd), smem_no_t = offsetof(TileSmemFwd, ti);
     static bool attr = false;
     if (!attr) {
-      cudaFuncSetAttribute(k_pair_fwd_tiled<FusedOut>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           (int)sizeof(TileSmemFwd));
+      cudaFuncSetAttribute(k_pair_fwd_tiled<true, FusedOut>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)smem_no_t);
+      cudaFuncSetAttribute(k_pair_fwd_tiled<false, FusedOut>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)smem_all);
       attr = true;
     }
-    const dim3 grid((unsigned)(((g.GW + kTileX - 1) / kTileX) * ((g.GH + kTileY - 1) / kTileY)),
-                    (unsigned)(c.B * g.S), 1);
+    const dim3 grid((unsigned)((g.GW + kTileX - 1) / kTileX), (unsigned)((g.GH + kTileY - 1) / kTileY),
+                    (unsigned)g.S);
+    const TileGrid T{(int)g.GW, (int)g.GH, (int)g.S, (int)c.B};
+    const FusedOut out{S_out, ls_out, den_out, eps};
+    cudaMemsetAsync(w.scratch, 0, sizeof(int), s);
     cudaEvent_t e0 = timing_begin(s);
-    launch(k_pair_fwd_tiled<FusedOut>, grid, kTileThreads, sizeof(TileSmemFwd), s, E, A, (const int*)w.astart,
-           (const int*)w.start, G, (const float*)w.SC, C, FusedOut{S_out, ls_out, den_out, w.BI, eps});
+    if (tau_covers(g, c.tau))
+      launch(k_pair_fwd_tiled<true, FusedOut>, grid, kTileThreads, smem_no_t, s, E, A, (const int*)w.astart,
+             (const int*)w.start, T, (const float*)w.SC, C, P, (const float4*)ev4, out, w.scratch);
+    else
+      launch(k_pair_fwd_tiled<false, FusedOut>, grid, kTileThreads, smem_all, s, E, A,
+             (const int*)w.astart, (const int*)w.start, T, (const float*)w.SC, C, P, (const float4*)ev4, out,
+             w.scratch);
     timing_end("k_pair_fwd", s, e0);
+    launch(k_fwd_overflow, warp_grid(ncell), kThreads, 0, s, E, A, (const int*)w.astart, (const int*)w.start, T, G,
+           (const float*)w.SC, C, BucketOut{out, w.BI}, (const int*)w.scratch);
   }
   return launch_status("exact_forward");
 }
@@ -524,14 +647,22 @@ int exact_backward(const atlb_exact_cfg& c, const float* grad_ls, const long lon
     launch(k_exact_gs, grid_for(M), kThreads, 0, s, (const int*)w.BI, M, grad_ls, S, den, eps, w.gSb);
     static bool attr = false;
     if (!attr) {
-      cudaFuncSetAttribute(k_pair_bwd_tiled, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(TileSmemBwd));
+      cudaFuncSetAttribute(k_pair_bwd_tiled<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)sizeof(TileSmemBwd));
+      cudaFuncSetAttribute(k_pair_bwd_tiled<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)sizeof(TileSmemBwd));
       attr = true;
     }
-    const dim3 grid((unsigned)(((g.GW + kTileX - 1) / kTileX) * ((g.GH + kTileY - 1) / kTileY)),
-                    (unsigned)(c.B * g.S), 1);
+    const dim3 grid((unsigned)((g.GW + kTileX - 1) / kTileX), (unsigned)((g.GH + kTileY - 1) / kTileY),
+                    (unsigned)g.S);
+    const TileGrid T{(int)g.GW, (int)g.GH, (int)g.S, (int)c.B};
     cudaEvent_t e0 = timing_begin(s);
-    launch(k_pair_bwd_tiled, grid, kTileThreads, sizeof(TileSmemBwd), s, E, A, (const int*)w.astart,
-           (const float*)w.gSb, (const int*)w.start, G, (const float*)w.SC, C, N, gv);
+    if (tau_covers(g, c.tau))
+      launch(k_pair_bwd_tiled<true>, grid, kTileThreads, sizeof(TileSmemBwd), s, E, A, (const int*)w.astart,
+             (const float*)w.gSb, (const int*)w.start, T, (const float*)w.SC, C, N, gv);
+    else
+      launch(k_pair_bwd_tiled<false>, grid, kTileThreads, sizeof(TileSmemBwd), s, E, A, (const int*)w.astart,
+             (const float*)w.gSb, (const int*)w.start, T, (const float*)w.SC, C, N, gv);
     timing_end("k_pair_bwd", s, e0);
   }
   const MotionView Mv = motion_of(c);

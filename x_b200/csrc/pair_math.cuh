@@ -68,4 +68,41 @@ __device__ __forceinline__ float pair_grad_factor(const PairConsts& C, float gi,
   return mul_rn(mul_rn(mul_rn(gi, kern), dt), C.invh2);
 }
 
+// ---- packed fp32x2 arithmetic (sm_100: add/sub/mul .rn.f32x2, each lane rounded like the scalar op) ----
+typedef unsigned long long f32x2;
+__device__ __forceinline__ f32x2 pk2(float a, float b) {
+  f32x2 r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ float2 upk2(f32x2 r) {
+  float2 d;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(d.x), "=f"(d.y) : "l"(r));
+  return d;
+}
+__device__ __forceinline__ f32x2 mul2(f32x2 a, f32x2 b) {
+  f32x2 r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ f32x2 add2(f32x2 a, f32x2 b) {
+  f32x2 r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ f32x2 sub2(f32x2 a, f32x2 b) {
+  f32x2 r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+
+// r = x_i - (y_j + v_j * dti) for both components, each op rounded as the reference's scalar code
+// (atl_cpu.cpp:192-193); returns d^2 = rx*rx + ry*ry (atl_cpu.cpp:194) and r in *r.
+__device__ __forceinline__ float residual2(f32x2 xi, f32x2 dti2, f32x2 y, f32x2 v, float2* r) {
+  const f32x2 rr = sub2(xi, add2(y, mul2(v, dti2)));
+  *r = upk2(rr);
+  const float2 sq = upk2(mul2(rr, rr));
+  return add_rn(sq.x, sq.y);
+}
+
 }  // namespace atlb

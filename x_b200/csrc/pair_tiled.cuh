@@ -1,47 +1,92 @@
 // Shared-memory tiled pair kernels of the fused path (compact entry layout).
 //
-// A CTA owns a tile of TX x TY cells of one slice grid g.
-//   forward : the entries of the (TX+2) x (TY+2) cells around the tile are staged once in shared memory
-//             with cp.async (each row of cells is one contiguous CSR range); the warps then walk the
-//             tile's anchor cells: a cell's anchors in register groups of NA, the candidate rows of its
-//             3x3 neighbourhood read from shared memory.  A tile whose neighbourhood does not fit reads
-//             its candidates from global memory instead (same code, other pointer).
+// Grid: (tile column, tile row, slice); each CTA walks the batches of its slice.  A tile is TX x TY cells.
+//   forward : the entries of the (TX+2) x (TY+2) cells around the tile and the anchors of the tile are
+//             staged in shared memory with cp.async (every row of cells is one contiguous CSR range);
+//             the anchors' leave-one-out terms are evaluated while staging.  Warps then walk the tile's
+//             anchor cells: a cell's anchors in register groups of up to 4, the candidates of its 3x3
+//             neighbourhood streamed by the lanes.  A tile whose neighbourhood does not fit reads its
+//             candidates from global memory instead (same loop, global pointer).
 //   backward: the anchors (and their dL/dS) of the (TX+2) x (TY+2) cells are staged; each lane takes one
 //             source entry of the tile and sums its gradient over the staged anchors of its 3x3 cells.
-// The prologue (row offsets of the staged cells) is computed by one warp in parallel; several CTAs per
-// SM overlap one CTA's staging with another's arithmetic.
+// Index arithmetic is 32-bit and division-free (power-of-two tile width, one grid axis per coordinate):
+// per-thread integer divisions by runtime values cost more than the pair arithmetic they surround.
 #pragma once
 #include "common.cuh"
 #include "pair_kernels.cuh"
 #include "pair_math.cuh"
+#include "plan_math.cuh"
 
 namespace atlb {
 
-constexpr int kTileX = 8;
+constexpr int kTileXLog = 3;
+constexpr int kTileX = 1 << kTileXLog;  // 8
 constexpr int kTileY = 4;
 constexpr int kTileThreads = 512;
-constexpr int kStageCap = 3584;  // staged entries per CTA (forward): 3584 * 24 B = 84 KB -> 2 CTAs / SM
-constexpr int kAncCap = 1536;    // staged anchors per CTA (backward): 1536 * 20 B = 30 KB
+constexpr int kStageCap = 3456;   // staged entries per CTA (forward): 3456 * 16 B = 54 KB (+ 8 B each for t)
+constexpr int kTileAncCap = 768;  // staged anchors per CTA (forward): 768 * 24 B = 18 KB
+constexpr int kAncCap = 1536;     // staged anchors per CTA (backward): 1536 * 24 B = 36 KB
 
 constexpr int kSR = kTileY + 2;  // staged rows
 constexpr int kSC = kTileX + 2;  // staged columns
 
+// Per-CTA work list: items (cell << 16 | part) sorted by decreasing cost, handed to warps by an atomic
+// counter (longest-processing-time-first: the cost of a cell's work varies by ~40x across a tile).
+constexpr int kMaxItems = 256;
+struct WorkQueue {
+  int item[kMaxItems];
+  int cost[kMaxItems];
+  int sorted[kMaxItems];
+  int n, next;
+};
+
+// Sorts wq.item[0..n) by decreasing cost into wq.sorted (rank sort; n <= kMaxItems).  Whole CTA.
+__device__ __forceinline__ void sort_items(WorkQueue& wq) {
+  const int n = wq.n;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const int ci = wq.cost[i];
+    int rank = 0;
+    for (int j = 0; j < n; ++j) {
+      const int cj = wq.cost[j];
+      rank += (cj > ci) || (cj == ci && j < i);
+    }
+    wq.sorted[rank] = wq.item[i];
+  }
+  if (threadIdx.x == 0) wq.next = 0;
+}
+
+// Next item for this warp (-1 when done).
+__device__ __forceinline__ int next_item(WorkQueue& wq, int lane) {
+  int k = 0;
+  if (lane == 0) k = atomicAdd(&wq.next, 1);
+  k = __shfl_sync(0xffffffffu, k, 0);
+  return k < wq.n ? wq.sorted[k] : -1;
+}
+
 struct TileSmemFwd {
   float4 yv[kStageCap];
-  float2 ti[kStageCap];
-  int cell_off[kSR][kSC + 1];  // staged offset of each cell of a staged row (+ end)
+  float4 anc[kTileAncCap];      // (x, y, t, a bits)
+  int aidx[kTileAncCap];        // original anchor index
+  int cell_off[kSR][kSC + 1];   // staged entry offset of each cell of a staged row (+ end)
   int row_k0[kSR];
   int row_base[kSR];
-  int total, any;
+  int acell_off[kTileY][kTileX + 1];
+  int arow_p0[kTileY];
+  int arow_base[kTileY];
+  int total, atotal;
+  WorkQueue wq;
+  float2 ti[kStageCap];  // entry times: staged only when tau does not cover the window (last member: the
+                         // launch omits it from the dynamic shared memory otherwise)
 };
 
 struct TileSmemBwd {
-  float4 xt[kAncCap];
-  float gs[kAncCap];
+  float4 xa[kAncCap];  // (x, y, t - c_s, t - c_s)
+  float2 tg[kAncCap];  // (t, dL/dS / h^2)
   int cell_off[kSR][kSC + 1];
   int row_p0[kSR];
   int row_base[kSR];
   int total;
+  WorkQueue wq;
 };
 
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
@@ -59,42 +104,54 @@ __device__ __forceinline__ void cp_async4(void* smem, const void* gmem) {
 __device__ __forceinline__ void cp_async_wait_all() {
   asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
 }
+__device__ __forceinline__ unsigned smem_addr(const void* p) { return (unsigned)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ float4 lds128(unsigned a) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ float2 lds64(unsigned a) {
+  float2 v;
+  asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(a));
+  return v;
+}
 
-// Tile geometry shared by both kernels.
+// 32-bit grid shape of the tiled kernels (ncell < 2^31 is checked by the API).
+struct TileGrid {
+  int GW, GH, S, B;
+};
+
 struct TileGeo {
   int tx0, tx1, ty0, ty1;  // tile cells [tx0, tx1) x [ty0, ty1)
   int sx0, sx1, sy0, sy1;  // staged cells (tile + 1-cell halo, clipped)
-  long long gbase;         // first cell of grid g
 };
 
-__device__ __forceinline__ TileGeo tile_geo(const CellGrid& G) {
+__device__ __forceinline__ TileGeo tile_geo(const TileGrid& G) {
   TileGeo t;
-  const int tiles_x = (int)((G.GW + kTileX - 1) / kTileX);
-  t.tx0 = (blockIdx.x % tiles_x) * kTileX;
-  t.ty0 = (blockIdx.x / tiles_x) * kTileY;
-  t.tx1 = (int)min((long long)t.tx0 + kTileX, G.GW);
-  t.ty1 = (int)min((long long)t.ty0 + kTileY, G.GH);
-  t.sx0 = t.tx0 > 0 ? t.tx0 - 1 : 0;
-  t.sx1 = t.tx1 < G.GW ? t.tx1 + 1 : (int)G.GW;
-  t.sy0 = t.ty0 > 0 ? t.ty0 - 1 : 0;
-  t.sy1 = t.ty1 < G.GH ? t.ty1 + 1 : (int)G.GH;
-  t.gbase = (long long)blockIdx.y * G.GH * G.GW;
+  t.tx0 = (int)blockIdx.x << kTileXLog;
+  t.ty0 = (int)blockIdx.y * kTileY;
+  t.tx1 = min(t.tx0 + kTileX, G.GW);
+  t.ty1 = min(t.ty0 + kTileY, G.GH);
+  t.sx0 = max(t.tx0 - 1, 0);
+  t.sx1 = min(t.tx1 + 1, G.GW);
+  t.sy0 = max(t.ty0 - 1, 0);
+  t.sy1 = min(t.ty1 + 1, G.GH);
   return t;
 }
 
-// Offsets (relative to a compact staging buffer) of every staged cell, from a CSR array:
-// off[r][c] for staged row r and column c in [0, nsc]; row0[r] = CSR index of the row's first cell;
-// rbase[r] = the row's first slot in the buffer.  Executed by one full warp; *total = staged count.
-template <typename CSR>
-__device__ __forceinline__ void stage_offsets(const TileGeo& t, long long GW, const CSR* __restrict__ csr,
-                                              int (*off)[kSC + 1], int* row0, int* rbase, int* total) {
+// Buffer offsets of a block of cells (rows [y0, y1), columns [x0, x1)) from a CSR array: off[r][c] = slot of
+// cell (y0 + r, x0 + c) (c = x1 - x0 gives the row end), row0[r] = CSR index of the row's first cell,
+// rbase[r] = the row's first slot.  Executed by one full warp; *total = the block's entries.
+template <int NC>
+__device__ __forceinline__ void block_offsets(const int* __restrict__ csr, int gbase, int GW, int y0, int y1, int x0,
+                                              int x1, int (*off)[NC + 1], int* row0, int* rbase, int* total) {
   const int lane = threadIdx.x & 31;
-  const int nsr = t.sy1 - t.sy0, nsc = t.sx1 - t.sx0;
+  const int nr = y1 - y0, nc = x1 - x0;
   int len = 0, k0 = 0;
-  if (lane < nsr) {
-    const long long row = t.gbase + (long long)(t.sy0 + lane) * GW;
-    k0 = (int)csr[row + t.sx0];
-    len = (int)csr[row + t.sx1] - k0;
+  if (lane < nr) {
+    const int row = gbase + (y0 + lane) * GW;
+    k0 = csr[row + x0];
+    len = csr[row + x1] - k0;
   }
   int incl = len;
 #pragma unroll
@@ -102,205 +159,367 @@ __device__ __forceinline__ void stage_offsets(const TileGeo& t, long long GW, co
     const int u = __shfl_up_sync(0xffffffffu, incl, o);
     if (lane >= o) incl += u;
   }
-  const int tot = __shfl_sync(0xffffffffu, incl, nsr > 0 ? nsr - 1 : 0);
-  if (lane < nsr) {
+  const int tot = __shfl_sync(0xffffffffu, incl, nr > 0 ? nr - 1 : 0);
+  if (lane < nr) {
     row0[lane] = k0;
     rbase[lane] = incl - len;
   }
-  if (lane == 0) *total = nsr > 0 ? tot : 0;
+  if (lane == 0) *total = nr > 0 ? tot : 0;
   __syncwarp();
-  for (int i = lane; i < nsr * (nsc + 1); i += 32) {
-    const int r = i / (nsc + 1), c = i % (nsc + 1);
-    const long long row = t.gbase + (long long)(t.sy0 + r) * GW;
-    off[r][c] = (int)csr[row + t.sx0 + c] - row0[r] + rbase[r];
+  for (int r = 0; r < nr; ++r) {
+    const int row = gbase + (y0 + r) * GW;
+    for (int c = lane; c <= nc; c += 32) off[r][c] = csr[row + x0 + c] - row0[r] + rbase[r];
   }
   __syncwarp();
 }
 
-// 3x3 neighbourhood of tile cell (cx, cy) as up to 3 ranges [lo, hi) of a staged buffer (or of the global
-// CSR when not staged).
-template <typename CSR>
-__device__ __forceinline__ int neighbour_rows(const TileGeo& t, long long GW, long long GH, int cx, int cy,
-                                              bool staged, const int (*off)[kSC + 1],
-                                              const CSR* __restrict__ csr, int* lo, int* hi) {
+// The 3x3 neighbourhood of tile cell (cx, cy) as up to 3 ranges [lo, hi) of the staged rows (or of the
+// global CSR when not staged).
+__device__ __forceinline__ int neighbour_rows(const TileGeo& t, int gbase, int GW, int GH, int cx, int cy, bool staged,
+                                              const int (*off)[kSC + 1], const int* __restrict__ csr, int* lo,
+                                              int* hi) {
   int nrows = 0;
-  const int xl = (cx > 0 ? cx - 1 : 0) - t.sx0, xh = (cx + 1 < GW ? cx + 1 : (int)GW - 1) - t.sx0 + 1;
-  for (int y = (cy > 0 ? cy - 1 : 0); y <= cy + 1 && y < GH; ++y) {
-    const int r = y - t.sy0;
+  const int xl = max(cx - 1, 0), xh = min(cx + 1, GW - 1) + 1;
+  for (int y = max(cy - 1, 0); y <= cy + 1 && y < GH; ++y) {
     if (staged) {
-      lo[nrows] = off[r][xl];
-      hi[nrows] = off[r][xh];
+      lo[nrows] = off[y - t.sy0][xl - t.sx0];
+      hi[nrows] = off[y - t.sy0][xh - t.sx0];
     } else {
-      const long long row = t.gbase + (long long)y * GW;
-      lo[nrows] = (int)csr[row + t.sx0 + xl];
-      hi[nrows] = (int)csr[row + t.sx0 + xh];
+      const int row = gbase + y * GW;
+      lo[nrows] = csr[row + xl];
+      hi[nrows] = csr[row + xh];
     }
     ++nrows;
   }
   return nrows;
 }
 
-// Candidate reads from shared memory (staged) or global memory (overflow tiles).
-struct CandView {
-  const float4* yv;
-  const float2* ti;
-};
+// Leave-one-out: anchor a's own event appears among the candidates iff its entry of slice s exists and its
+// cell lies in the anchor's 3x3 cells; returns that entry's (bit-identical) kernel value, else 0.
+__device__ __forceinline__ float self_term(const PlanConsts& P, const PairConsts& C, const float4* __restrict__ ev4,
+                                           int a, float xi, float yi, float ti, float dti, int b, int s, int cx,
+                                           int cy) {
+  int s_lo, s_hi;
+  slice_range(P, ti, &s_lo, &s_hi);
+  if (s < s_lo || s > s_hi || b < 0 || b >= P.B) return 0.f;
+  const float4 e = __ldg(ev4 + a);
+  const float dtc = sub_rn(slice_centre(P, s), ti);
+  const float yx = add_rn(e.x, mul_rn(e.z, dtc)), yy = add_rn(e.y, mul_rn(e.w, dtc));
+  const float qx = floorf(div_rn(sub_rn(yx, P.ox_f), P.cell_f));
+  const float qy = floorf(div_rn(sub_rn(yy, P.oy_f), P.cell_f));
+  if (!(qx >= 0.f && qx < (float)P.GW && qy >= 0.f && qy < (float)P.GH)) return 0.f;
+  const int ex = (int)qx, ey = (int)qy;
+  if (ex < cx - 1 || ex > cx + 1 || ey < cy - 1 || ey > cy + 1) return 0.f;
+  float2 r;
+  const float d2 = residual2(pk2(xi, yi), pk2(dti, dti), pk2(yx, yy), pk2(e.z, e.w), &r);
+  const float k = ex2_approx(-d2 * C.k2);
+  return (d2 > C.r2max) ? 0.f : k;  // dt = 0: inside any tau
+}
 
-template <int NA, class Out>
-__device__ __forceinline__ void fwd_group_tile(const FastAnchors& anc, int base, const CandView& cv,
-                                               const int* lo, const int* hi, int nrows, float cs,
-                                               const PairConsts& C, Out& out, int lane) {
-  float ax[NA], ay[NA], at[NA], adt[NA], acc[NA];
-  int aid[NA];
+// ---- forward -----------------------------------------------------------------------------------------
+template <int NA, bool TAU_ALL, bool STAGED, class Out>
+__device__ __forceinline__ void fwd_group_tile(const TileSmemFwd& sm, int p, const float4* __restrict__ yv,
+                                               const float2* __restrict__ ti, const int* lo, const int* hi, int nrows,
+                                               float cs, const PairConsts& C, const PlanConsts& P,
+                                               const float4* __restrict__ ev4, int b, int s, int cx, int cy, Out& out,
+                                               int lane) {
+  f32x2 axy[NA], adt2[NA];
+  float at[NA], acc[NA];
+  // lane q < NA evaluates anchor q's leave-one-out term; its latency overlaps the candidate loop
+  float self_k = 0.f;
+  if (lane < NA) {
+    const float4 a = sm.anc[p + lane];
+    self_k = self_term(P, C, ev4, __float_as_int(a.w), a.x, a.y, a.z, sub_rn(a.z, cs), b, s, cx, cy);
+  }
 #pragma unroll
   for (int q = 0; q < NA; ++q) {
-    anc.load(base + q, ax[q], ay[q], at[q], aid[q]);
-    adt[q] = sub_rn(at[q], cs);
+    const float4 a = sm.anc[p + q];
+    const float adt = sub_rn(a.z, cs);
+    axy[q] = pk2(a.x, a.y);
+    adt2[q] = pk2(adt, adt);
+    at[q] = a.z;
     acc[q] = 0.f;
   }
+  const unsigned yv_s = STAGED ? smem_addr(yv) : 0u, ti_s = STAGED ? smem_addr(ti) : 0u;
   for (int r = 0; r < nrows; ++r) {
     const int k1 = hi[r];
     for (int k = lo[r] + lane; k < k1; k += 32) {
-      const float4 e = cv.yv[k];
-      const float2 f = cv.ti[k];
-      const float2 sy = make_float2(e.x, e.y), sv = make_float2(e.z, e.w);
-      const int sid = __float_as_int(f.y);
+      float4 e;
+      float st = 0.f;
+      if (STAGED) {
+        e = lds128(yv_s + 16u * (unsigned)k);
+        if (!TAU_ALL) st = lds64(ti_s + 8u * (unsigned)k).x;
+      } else {
+        e = __ldg(yv + k);
+        if (!TAU_ALL) st = __ldg(ti + k).x;
+      }
+      const f32x2 y = pk2(e.x, e.y), v = pk2(e.z, e.w);
 #pragma unroll
       for (int q = 0; q < NA; ++q) {
-        float rx, ry, dt;
-        acc[q] += pair_eval(C, ax[q], ay[q], at[q], adt[q], sy, sv, f.x, sid == aid[q], &rx, &ry, &dt);
+        float2 rr;
+        const float d2 = residual2(axy[q], adt2[q], y, v, &rr);
+        bool ok = !(d2 > C.r2max);
+        if (!TAU_ALL) ok = ok && !(fabsf(sub_rn(at[q], st)) > C.tau);
+        const float kv = ex2_approx(-d2 * C.k2);
+        acc[q] += ok ? kv : 0.f;
       }
     }
   }
 #pragma unroll
   for (int q = 0; q < NA; ++q) {
-    const float s = warp_sum(acc[q]);
-    if (lane == 0) out(base + q, (double)s);
+    const float sum = warp_sum(acc[q]);
+    const float self_q = __shfl_sync(0xffffffffu, self_k, q);
+    if (lane == 0) out(sm.aidx[p + q], (double)(sum - self_q));
   }
 }
 
-template <class Out>
+// out(i, S_i) with i the original anchor index.  A tile with more than kTileAncCap anchors sets *overflow
+// and leaves its anchors to the caller's untiled pass.
+template <bool TAU_ALL, class Out>
 __global__ void __launch_bounds__(kTileThreads) k_pair_fwd_tiled(FastEntries ent, FastAnchors anc,
                                                                  const int* __restrict__ astart,
-                                                                 const int* __restrict__ cstart, CellGrid G,
-                                                                 const float* __restrict__ SC, PairConsts C, Out out) {
+                                                                 const int* __restrict__ cstart, TileGrid G,
+                                                                 const float* __restrict__ SC, PairConsts C,
+                                                                 PlanConsts P, const float4* __restrict__ ev4,
+                                                                 Out out, int* __restrict__ overflow) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   TileSmemFwd& sm = *reinterpret_cast<TileSmemFwd*>(smem_raw);
   const TileGeo t = tile_geo(G);
-  const long long GW = G.GW, GH = G.GH;
+  const int GW = G.GW, GH = G.GH, s = (int)blockIdx.z;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  const float cs = __ldg(SC + s);
+  const int nsc = t.sx1 - t.sx0, ntx = t.tx1 - t.tx0, nty = t.ty1 - t.ty0;
 
-  if (warp == 0) {
-    // anchors in the tile? (lane r < TY: one row of the tile each)
-    int na = 0;
-    if (lane < t.ty1 - t.ty0) {
-      const long long row = t.gbase + (long long)(t.ty0 + lane) * GW;
-      na = astart[row + t.tx1] - astart[row + t.tx0];
+  for (int b = 0; b < G.B; ++b) {
+    const int gbase = (b * G.S + s) * GH * GW;
+    if (warp == 0) {
+      block_offsets<kTileX>(astart, gbase, GW, t.ty0, t.ty1, t.tx0, t.tx1, sm.acell_off, sm.arow_p0, sm.arow_base,
+                            &sm.atotal);
+      block_offsets<kSC>(cstart, gbase, GW, t.sy0, t.sy1, t.sx0, t.sx1, sm.cell_off, sm.row_k0, sm.row_base,
+                         &sm.total);
     }
-    na = __reduce_add_sync(0xffffffffu, na);
-    if (na > 0) stage_offsets(t, GW, cstart, sm.cell_off, sm.row_k0, sm.row_base, &sm.total);
-    if (lane == 0) sm.any = na;
-  }
-  __syncthreads();
-  if (sm.any == 0) return;
-  const int nsr = t.sy1 - t.sy0, nsc = t.sx1 - t.sx0;
-  const bool staged = sm.total <= kStageCap;
-  if (staged) {
-    for (int r = 0; r < nsr; ++r) {
-      const int k0 = sm.row_k0[r], b0 = sm.cell_off[r][0], n = sm.cell_off[r][nsc] - b0;
+    __syncthreads();
+    const int na = sm.atotal;
+    const bool staged = sm.total <= kStageCap;
+    if (na == 0 || na > kTileAncCap) {  // CTA-uniform
+      if (na > kTileAncCap && threadIdx.x == 0) atomicOr(overflow, 1);
+      __syncthreads();
+      continue;
+    }
+    // stage the tile's anchors (contiguous per tile row) and, if they fit, the neighbourhood's entries
+    for (int r = 0; r < nty; ++r) {
+      const int p0 = sm.arow_p0[r], b0 = sm.acell_off[r][0], n = sm.acell_off[r][ntx] - b0;
       for (int i = threadIdx.x; i < n; i += blockDim.x) {
-        cp_async16(&sm.yv[b0 + i], ent.YV + k0 + i);
-        cp_async8(&sm.ti[b0 + i], ent.TI + k0 + i);
+        cp_async16(&sm.anc[b0 + i], anc.XT + p0 + i);
+        cp_async4(&sm.aidx[b0 + i], anc.idx + p0 + i);
       }
     }
-    cp_async_wait_all();
-  }
-  __syncthreads();
-
-  const float cs = __ldg(SC + blockIdx.y % G.S);
-  const int ncx = t.tx1 - t.tx0, ncells = ncx * (t.ty1 - t.ty0);
-  const CandView cv = staged ? CandView{sm.yv, sm.ti} : CandView{ent.YV, ent.TI};
-  for (int ci = warp; ci < ncells; ci += nwarps) {
-    const int cx = t.tx0 + ci % ncx, cy = t.ty0 + ci / ncx;
-    const long long c = t.gbase + (long long)cy * GW + cx;
-    const int a0 = astart[c], a1 = astart[c + 1];
-    if (a0 == a1) continue;
-    int lo[3], hi[3];
-    const int nrows = neighbour_rows(t, GW, GH, cx, cy, staged, sm.cell_off, cstart, lo, hi);
-    int base = a0;
-    for (; base + 4 <= a1; base += 4) fwd_group_tile<4>(anc, base, cv, lo, hi, nrows, cs, C, out, lane);
-    switch (a1 - base) {
-      case 3: fwd_group_tile<3>(anc, base, cv, lo, hi, nrows, cs, C, out, lane); break;
-      case 2: fwd_group_tile<2>(anc, base, cv, lo, hi, nrows, cs, C, out, lane); break;
-      case 1: fwd_group_tile<1>(anc, base, cv, lo, hi, nrows, cs, C, out, lane); break;
-      default: break;
+    if (staged) {
+      for (int r = 0; r < t.sy1 - t.sy0; ++r) {
+        const int k0 = sm.row_k0[r], b0 = sm.cell_off[r][0], n = sm.cell_off[r][nsc] - b0;
+        for (int i = threadIdx.x; i < n; i += blockDim.x) {
+          cp_async16(&sm.yv[b0 + i], ent.YV + k0 + i);
+          if (!TAU_ALL) cp_async8(&sm.ti[b0 + i], ent.TI + k0 + i);
+        }
+      }
     }
+    // work items: (cell, group of <= 4 anchors), cost = anchors x candidates
+    if (warp == 0) {
+      int ng = 0, cand = 0, p0 = 0;
+      const int cxo = lane & (kTileX - 1), cyo = lane >> kTileXLog;
+      if (lane < kTileX * kTileY && cxo < ntx && cyo < nty) {
+        p0 = sm.acell_off[cyo][cxo];
+        ng = (sm.acell_off[cyo][cxo + 1] - p0 + 3) >> 2;
+        int lo[3], hi[3];
+        const int nr = neighbour_rows(t, gbase, GW, GH, t.tx0 + cxo, t.ty0 + cyo, staged, sm.cell_off, cstart, lo, hi);
+        for (int r = 0; r < nr; ++r) cand += hi[r] - lo[r];
+      }
+      int incl = ng;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int u = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += u;
+      }
+      const int total_items = __shfl_sync(0xffffffffu, incl, 31);
+      const int p1 = lane < kTileX * kTileY && cxo < ntx && cyo < nty ? sm.acell_off[cyo][cxo + 1] : 0;
+      for (int gi = 0; gi < ng; ++gi) {
+        const int slot = incl - ng + gi;
+        if (slot < kMaxItems) {
+          sm.wq.item[slot] = (lane << 16) | gi;
+          sm.wq.cost[slot] = min(4, p1 - (p0 + 4 * gi)) * cand;
+        }
+      }
+      if (lane == 0) sm.wq.n = min(total_items, kMaxItems);
+    }
+    cp_async_wait_all();
+    __syncthreads();
+    sort_items(sm.wq);
+    __syncthreads();
+    for (int it = next_item(sm.wq, lane); it >= 0; it = next_item(sm.wq, lane)) {
+      const int ci = it >> 16, gi = it & 0xffff;
+      const int cxo = ci & (kTileX - 1), cyo = ci >> kTileXLog;
+      const int p = sm.acell_off[cyo][cxo] + 4 * gi, p1 = sm.acell_off[cyo][cxo + 1];
+      int lo[3], hi[3];
+      const int nrows = neighbour_rows(t, gbase, GW, GH, t.tx0 + cxo, t.ty0 + cyo, staged, sm.cell_off, cstart, lo, hi);
+      const int na_g = min(4, p1 - p);
+      const int cx = t.tx0 + cxo, cy = t.ty0 + cyo;
+#define ATLB_GROUP(n, st, yvp, tip) \
+  fwd_group_tile<n, TAU_ALL, st>(sm, p, yvp, tip, lo, hi, nrows, cs, C, P, ev4, b, s, cx, cy, out, lane)
+      if (staged) {
+        switch (na_g) {
+          case 4: ATLB_GROUP(4, true, sm.yv, sm.ti); break;
+          case 3: ATLB_GROUP(3, true, sm.yv, sm.ti); break;
+          case 2: ATLB_GROUP(2, true, sm.yv, sm.ti); break;
+          default: ATLB_GROUP(1, true, sm.yv, sm.ti); break;
+        }
+      } else {
+        switch (na_g) {
+          case 4: ATLB_GROUP(4, false, ent.YV, ent.TI); break;
+          case 3: ATLB_GROUP(3, false, ent.YV, ent.TI); break;
+          case 2: ATLB_GROUP(2, false, ent.YV, ent.TI); break;
+          default: ATLB_GROUP(1, false, ent.YV, ent.TI); break;
+        }
+      }
+#undef ATLB_GROUP
+    }
+    __syncthreads();  // the next batch reuses the shared buffers
   }
 }
 
-// Backward: source entries of the tile, anchors of the (TX+2) x (TY+2) cells staged.
+// ---- backward ----------------------------------------------------------------------------------------
+// Source entries of the tile; anchors of the (TX+2) x (TY+2) cells staged as (x, y, t - c_s) and
+// (t, dL/dS / h^2).  The self pair has dt = 0 and contributes nothing, so no leave-one-out test.
+template <bool TAU_ALL>
 __global__ void __launch_bounds__(kTileThreads) k_pair_bwd_tiled(FastEntries ent, FastAnchors anc,
                                                                  const int* __restrict__ astart,
                                                                  const float* __restrict__ gSb,
-                                                                 const int* __restrict__ cstart, CellGrid G,
+                                                                 const int* __restrict__ cstart, TileGrid G,
                                                                  const float* __restrict__ SC, PairConsts C,
                                                                  long long N, float* __restrict__ gv) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   TileSmemBwd& sm = *reinterpret_cast<TileSmemBwd*>(smem_raw);
   const TileGeo t = tile_geo(G);
-  const long long GW = G.GW, GH = G.GH;
+  const int GW = G.GW, GH = G.GH, s = (int)blockIdx.z;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  const float cs = __ldg(SC + s);
+  const int nsc = t.sx1 - t.sx0, ntx = t.tx1 - t.tx0, nty = t.ty1 - t.ty0;
+  const unsigned xa_s = smem_addr(sm.xa), tg_s = smem_addr(sm.tg);
 
-  if (warp == 0) stage_offsets(t, GW, astart, sm.cell_off, sm.row_p0, sm.row_base, &sm.total);
-  __syncthreads();
-  const int nsr = t.sy1 - t.sy0, nsc = t.sx1 - t.sx0;
-  const bool staged = sm.total <= kAncCap;
-  if (staged) {
-    for (int r = 0; r < nsr; ++r) {
-      const int p0 = sm.row_p0[r], b0 = sm.cell_off[r][0], n = sm.cell_off[r][nsc] - b0;
-      for (int i = threadIdx.x; i < n; i += blockDim.x) {
-        cp_async16(&sm.xt[b0 + i], anc.XT + p0 + i);
-        cp_async4(&sm.gs[b0 + i], gSb + p0 + i);
-      }
-    }
-    cp_async_wait_all();
-  }
-  __syncthreads();
-
-  const float cs = __ldg(SC + blockIdx.y % G.S);
-  const int ncx = t.tx1 - t.tx0, ncells = ncx * (t.ty1 - t.ty0);
-  const float4* XT = staged ? sm.xt : anc.XT;
-  const float* GS = staged ? sm.gs : gSb;
-  for (int ci = warp; ci < ncells; ci += nwarps) {
-    const int cx = t.tx0 + ci % ncx, cy = t.ty0 + ci / ncx;
-    const long long c = t.gbase + (long long)cy * GW + cx;
-    const int k0 = cstart[c], k1 = cstart[c + 1];
-    if (k0 == k1) continue;
-    int lo[3], hi[3];
-    const int nrows = neighbour_rows(t, GW, GH, cx, cy, staged, sm.cell_off, astart, lo, hi);
-    for (int kb = k0; kb < k1; kb += 32) {
-      const int k = kb + lane;
-      const bool valid = k < k1;
-      float2 sy, sv;
-      float st;
-      int sid;
-      ent.load(valid ? k : k0, sy, sv, st, sid);
-      float gx = 0.f, gy = 0.f;
-      for (int r = 0; r < nrows; ++r) {
-        for (int p = lo[r]; p < hi[r]; ++p) {
-          const float4 a = XT[p];
-          const float gi = GS[p];
-          float rx, ry, dt;
-          const float e = pair_eval(C, a.x, a.y, a.z, sub_rn(a.z, cs), sy, sv, st, sid == __float_as_int(a.w),
-                                    &rx, &ry, &dt);
-          const float f = mul_rn(mul_rn(mul_rn(gi, e), dt), C.invh2);  // gS k dt / h^2 (atl_cpu.cpp:244)
-          const bool hit = e != 0.f;
-          gx += hit ? f * rx : 0.f;
-          gy += hit ? f * ry : 0.f;
+  for (int b = 0; b < G.B; ++b) {
+    const int gbase = (b * G.S + s) * GH * GW;
+    if (warp == 0)
+      block_offsets<kSC>(astart, gbase, GW, t.sy0, t.sy1, t.sx0, t.sx1, sm.cell_off, sm.row_p0, sm.row_base,
+                         &sm.total);
+    __syncthreads();
+    const bool staged = sm.total <= kAncCap;
+    if (staged) {
+      for (int r = 0; r < t.sy1 - t.sy0; ++r) {
+        const int p0 = sm.row_p0[r], b0 = sm.cell_off[r][0], n = sm.cell_off[r][nsc] - b0;
+        for (int i = threadIdx.x; i < n; i += blockDim.x) {
+          const float4 a = __ldg(anc.XT + p0 + i);
+          const float adt = sub_rn(a.z, cs);
+          sm.xa[b0 + i] = make_float4(a.x, a.y, adt, adt);
+          sm.tg[b0 + i] = make_float2(a.z, __ldg(gSb + p0 + i) * C.invh2);
         }
       }
-      if (valid && (gx != 0.f || gy != 0.f) && sid >= 0 && sid < N) red_add_f2(gv + 2 * (long long)sid, gx, gy);
     }
+    __syncthreads();
+    // work items: (cell, chunk of 32 source entries), cost = sources x staged anchors of the 3x3 cells
+    if (warp == 0) {
+      int nch = 0, nanc = 0, k0 = 0, k1 = 0;
+      const int cxo = lane & (kTileX - 1), cyo = lane >> kTileXLog;
+      if (lane < kTileX * kTileY && cxo < ntx && cyo < nty) {
+        const int c = gbase + (t.ty0 + cyo) * GW + t.tx0 + cxo;
+        k0 = cstart[c];
+        k1 = cstart[c + 1];
+        nch = (k1 - k0 + 31) >> 5;
+        int lo[3], hi[3];
+        const int nr = neighbour_rows(t, gbase, GW, GH, t.tx0 + cxo, t.ty0 + cyo, staged, sm.cell_off, astart, lo, hi);
+        for (int r = 0; r < nr; ++r) nanc += hi[r] - lo[r];
+      }
+      if (nanc == 0) nch = 0;  // no anchor in reach: nothing to add
+      int incl = nch;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int u = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += u;
+      }
+      const int total_items = __shfl_sync(0xffffffffu, incl, 31);
+      for (int q = 0; q < nch; ++q) {
+        const int slot = incl - nch + q;
+        if (slot < kMaxItems) {
+          sm.wq.item[slot] = (lane << 16) | q;
+          sm.wq.cost[slot] = min(32, k1 - (k0 + 32 * q)) * nanc;
+        }
+      }
+      if (lane == 0) sm.wq.n = total_items;
+    }
+    __syncthreads();
+    const int nitems = sm.wq.n;
+    if (nitems <= kMaxItems) sort_items(sm.wq);
+    __syncthreads();
+    for (int w = warp;; w += nwarps) {
+      int it;
+      if (nitems <= kMaxItems) {
+        it = next_item(sm.wq, lane);
+      } else {  // more chunks than the list holds: static walk over (cell, chunk)
+        it = -1;
+        int acc = 0;
+        for (int ci = 0; ci < kTileX * kTileY && it < 0; ++ci) {
+          const int cxo = ci & (kTileX - 1), cyo = ci >> kTileXLog;
+          if (cxo >= ntx || cyo >= nty) continue;
+          const int c = gbase + (t.ty0 + cyo) * GW + t.tx0 + cxo;
+          const int nch = (cstart[c + 1] - cstart[c] + 31) >> 5;
+          if (w < acc + nch) it = (ci << 16) | (w - acc);
+          acc += nch;
+        }
+      }
+      if (it < 0) break;
+      const int ci = it >> 16, q = it & 0xffff;
+      const int cxo = ci & (kTileX - 1), cyo = ci >> kTileXLog;
+      const int cx = t.tx0 + cxo, cy = t.ty0 + cyo;
+      const int c = gbase + cy * GW + cx;
+      const int k0 = cstart[c], k1 = cstart[c + 1];
+      int lo[3], hi[3];
+      const int nrows = neighbour_rows(t, gbase, GW, GH, cx, cy, staged, sm.cell_off, astart, lo, hi);
+      {
+        const int kb = k0 + 32 * q;
+        const int k = kb + lane;
+        const bool valid = k < k1;
+        float2 sy, sv;
+        float st;
+        int sid;
+        ent.load(valid ? k : k0, sy, sv, st, sid);
+        const f32x2 y = pk2(sy.x, sy.y), v = pk2(sv.x, sv.y);
+        float gx = 0.f, gy = 0.f;
+        for (int r = 0; r < nrows; ++r) {
+          const int p1 = hi[r];
+          for (int p = lo[r]; p < p1; ++p) {
+            float4 a;
+            float2 tg;
+            if (staged) {
+              a = lds128(xa_s + 16u * (unsigned)p);
+              tg = lds64(tg_s + 8u * (unsigned)p);
+            } else {
+              const float4 qa = __ldg(anc.XT + p);
+              const float adt = sub_rn(qa.z, cs);
+              a = make_float4(qa.x, qa.y, adt, adt);
+              tg = make_float2(qa.z, __ldg(gSb + p) * C.invh2);
+            }
+            float2 rr;
+            const float d2 = residual2(pk2(a.x, a.y), pk2(a.z, a.w), y, v, &rr);
+            const float dt = sub_rn(tg.x, st);
+            bool ok = !(d2 > C.r2max);
+            if (!TAU_ALL) ok = ok && !(fabsf(dt) > C.tau);
+            const float f = ok ? tg.y * ex2_approx(-d2 * C.k2) * dt : 0.f;  // gS k dt / h^2
+            gx = fmaf(f, rr.x, gx);
+            gy = fmaf(f, rr.y, gy);
+          }
+        }
+        if (valid && (gx != 0.f || gy != 0.f) && sid >= 0 && sid < N) red_add_f2(gv + 2 * (long long)sid, gx, gy);
+      }
+    }
+    __syncthreads();  // the next batch reuses the shared buffers
   }
 }
 

@@ -162,6 +162,12 @@ dim3 slice_grid(long long N, int S) {
   return dim3((unsigned)(gx < 1 ? 1 : gx), (unsigned)by, 1);
 }
 
+static inline float __int_as_float_host(int i) {
+  float f;
+  memcpy(&f, &i, 4);
+  return f;
+}
+
 // Host-side geometry, functional.py:139-149, in double exactly as the reference's Python computes it.
 void plan_geometry_host(float vmax, bool have_anchors, float mnx, float mny, float mxx, float mxy, long long H,
                         long long W, double h, double cut, long long S, atlb_plan_geom* g) {
@@ -180,6 +186,8 @@ void plan_geometry_host(float vmax, bool have_anchors, float mnx, float mny, flo
   g->GH = (int64_t)std::ceil((ey - oy) / cell) + 1;
   g->vmax = vmax;
   g->S = (int32_t)S;
+  g->t_lo = __int_as_float_host(0x7fc00000);
+  g->t_hi = __int_as_float_host(0x7fc00000);
 }
 
 PlanConsts make_plan_consts(const atlb_plan_geom& g, double tau, long long B) {
