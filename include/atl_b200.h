@@ -122,6 +122,23 @@ int atlb_ats_pair_fwd(const float* src_y, const float* src_v, const float* src_t
                       const int64_t* anc_id, const float* slice_c, int64_t Ns, int64_t M, int64_t ncell, int64_t S,
                       int64_t GH, int64_t GW, double h, double tau, double cut, float* out, void* workspace,
                       size_t workspace_bytes, atlb_stream_t stream);
+/* atlb_ats_pair_fwd without a workspace argument: the same sums, for callers that cannot allocate
+ * device memory when they need them (code running inside someone else's stream capture, hosts that give
+ * the library a fixed memory budget, FFI layers without a device allocator).  No counterpart in the
+ * reference: it is an addition of this library.  The anchor buckets live in one file-scope device
+ * array of ATLB_PAIR_NOALLOC_SCRATCH_BYTES, which every device that loads the library holds until the
+ * process exits; the call allocates nothing.  Sizes with atlb_pair_workspace_bytes(M, ncell) above
+ * that limit fail with ATLB_ERR_WORKSPACE before any device work.  The first call on a device looks up
+ * the array's device address (cudaGetSymbolAddress, with that device current), so make that first
+ * call before any stream capture.  All calls share the array: calls whose work overlaps on the GPU
+ * (other streams or host threads) race; calls ordered on one stream do not.  Not covered by
+ * atlb_timing_*. */
+#define ATLB_PAIR_NOALLOC_SCRATCH_BYTES ((size_t)16 << 20)
+int atlb_ats_pair_fwd_noalloc(const float* src_y, const float* src_v, const float* src_t, const int64_t* src_id,
+                              const int64_t* cell_start, const float* anc_x, const float* anc_t,
+                              const int64_t* anc_cell, const int64_t* anc_id, const float* slice_c, int64_t Ns,
+                              int64_t M, int64_t ncell, int64_t S, int64_t GH, int64_t GW, double h, double tau,
+                              double cut, float* out, atlb_stream_t stream);
 /* gv (N,2): gradient of sum_i gS_i S_i w.r.t. the per-event velocities. */
 int atlb_ats_pair_bwd(const float* gS, const float* src_y, const float* src_v, const float* src_t,
                       const int64_t* src_id, const int64_t* cell_start, const float* anc_x, const float* anc_t,

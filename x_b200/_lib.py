@@ -61,6 +61,7 @@ _SIGS = {
                               _vp, _size, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "atlb_pair_workspace_bytes": (_size, [_i64, _i64]),
     "atlb_ats_pair_fwd": (_int, [_vp] * 10 + [_i64] * 6 + [_dbl] * 3 + [_vp, _vp, _size, _vp]),
+    "atlb_ats_pair_fwd_noalloc": (_int, [_vp] * 10 + [_i64] * 6 + [_dbl] * 3 + [_vp, _vp]),
     "atlb_ats_pair_bwd": (_int, [_vp] * 11 + [_i64] * 6 + [_dbl] * 3 + [_i64, _vp, _vp, _size, _vp]),
     "atlb_window_counts": (_int, [_vp, _vp, _i64, _vp, _i64, _dbl, _vp, _vp, _vp]),
     "atlb_window_counts_keys": (_int, [_vp, _i64, _vp, _vp, _vp, _i64, _dbl, _vp, _vp]),

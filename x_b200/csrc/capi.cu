@@ -44,6 +44,9 @@ int pair_fwd(const float*, const float*, const float*, const long long*, const l
 int pair_bwd(const float*, const float*, const float*, const float*, const long long*, const long long*, const float*,
              const float*, const long long*, const long long*, const float*, long long, long long, long long,
              long long, long long, double, double, double, long long, float*, void*, cudaStream_t);
+int pair_fwd_noalloc(const float*, const float*, const float*, const long long*, const long long*, const float*,
+                     const float*, const long long*, const long long*, const float*, long long, long long, long long,
+                     long long, long long, double, double, double, float*, cudaStream_t);
 int splat_bilinear_fwd(const float*, const float*, const long long*, long long, long long, long long, long long,
                        float*, cudaStream_t);
 int splat_bilinear_bwd(const float*, const float*, const float*, const long long*, long long, long long, long long,
@@ -271,6 +274,21 @@ int atlb_ats_pair_fwd(const float* src_y, const float* src_v, const float* src_t
   NEED(anc_x, M); NEED(anc_t, M); NEED(anc_cell, M); NEED(anc_id, M); NEED(out, M);
   return pair_fwd(src_y, src_v, src_t, LL(src_id), LL(cell_start), anc_x, anc_t, LL(anc_cell), LL(anc_id), slice_c, M,
                   ncell, S, GH, GW, h, tau, cut, out, workspace, STREAM(stream));
+}
+
+int atlb_ats_pair_fwd_noalloc(const float* src_y, const float* src_v, const float* src_t, const int64_t* src_id,
+                              const int64_t* cell_start, const float* anc_x, const float* anc_t,
+                              const int64_t* anc_cell, const int64_t* anc_id, const float* slice_c, int64_t Ns,
+                              int64_t M, int64_t ncell, int64_t S, int64_t GH, int64_t GW, double h, double tau,
+                              double cut, float* out, atlb_stream_t stream) {
+  clear();
+  if (Ns < 0 || M < 0 || ncell < 0 || S < 1 || GH < 0 || GW < 0) { set_error("%s: negative size", __func__); return ATLB_ERR_ARG; }
+  if (!cell_start || !slice_c) { set_error("%s: NULL cell_start / slice_c", __func__); return ATLB_ERR_ARG; }
+  if (M > (1LL << 31) - 1 || ncell > (1LL << 31) - 2) { set_error("%s: too many anchors / cells", __func__); return ATLB_ERR_OVERFLOW; }
+  NEED(src_y, Ns); NEED(src_v, Ns); NEED(src_t, Ns); NEED(src_id, Ns);
+  NEED(anc_x, M); NEED(anc_t, M); NEED(anc_cell, M); NEED(anc_id, M); NEED(out, M);
+  return pair_fwd_noalloc(src_y, src_v, src_t, LL(src_id), LL(cell_start), anc_x, anc_t, LL(anc_cell), LL(anc_id),
+                          slice_c, M, ncell, S, GH, GW, h, tau, cut, out, STREAM(stream));
 }
 
 int atlb_ats_pair_bwd(const float* gS, const float* src_y, const float* src_v, const float* src_t,

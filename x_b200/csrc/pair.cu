@@ -12,6 +12,8 @@
 //     two atomics per pair.
 // The pair test (|dt| <= tau, d^2 <= (cut h)^2, leave-one-out by id) is evaluated with the exact
 // rounding sequence of the reference, so the set of contributing pairs is identical.
+#include <mutex>
+
 #include "common.cuh"
 #include "pair_kernels.cuh"
 #include "pair_math.cuh"
@@ -173,6 +175,78 @@ int pair_bwd(const float* gS, const float* SY, const float* SV, const float* ST,
     timing_end("k_pair_bwd", s, e0);
   }
   return launch_status("ats_pair_bwd");
+}
+
+// ---- allocation-free forward ---------------------------------------------------------------------
+// Some callers cannot call cudaMalloc at the point where they need the pair sums: code running while
+// a stream is being captured into a CUDA graph by someone else, hosts that hand the library a fixed
+// device-memory budget (a custom allocator, an embedded runtime, a real-time loop that forbids
+// allocation after start-up), or FFI layers with no device allocator of their own.  For them the
+// forward's anchor buckets live in this file-scope device array instead of a caller workspace.  Every
+// device that loads the library holds these bytes until the process exits.  In host code the array's
+// name is a stand-in for the symbol, not a device address: its address on the current device comes
+// from cudaGetSymbolAddress, looked up once per device on that device's first call.
+constexpr size_t kNoAllocScratchBytes = ATLB_PAIR_NOALLOC_SCRATCH_BYTES;
+static __device__ __align__(256) unsigned char g_pair_scratch[kNoAllocScratchBytes];
+
+namespace {
+constexpr int kMaxDevices = 64;
+std::mutex g_scratch_mu;
+void* g_scratch_ptr[kMaxDevices] = {};
+
+// Device address of g_pair_scratch on the current device (looked up on the first call per device).
+int pair_scratch_address(void** out) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    set_error("ats_pair_fwd_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
+    return ATLB_ERR_CUDA;
+  }
+  if (dev < 0 || dev >= kMaxDevices) {
+    set_error("ats_pair_fwd_noalloc: device ordinal %d beyond the %d supported", dev, kMaxDevices);
+    return ATLB_ERR_ARG;
+  }
+  std::lock_guard<std::mutex> lk(g_scratch_mu);
+  if (!g_scratch_ptr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_pair_scratch);
+    if (e != cudaSuccess || !p) {
+      set_error("ats_pair_fwd_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+      return ATLB_ERR_CUDA;
+    }
+    g_scratch_ptr[dev] = p;
+  }
+  *out = g_scratch_ptr[dev];
+  return ATLB_OK;
+}
+}  // namespace
+
+// Same kernels and result as pair_fwd; the workspace is g_pair_scratch.  The per-cell counters are
+// zeroed on the stream by every call (bucket_anchors), and every other byte used is written before it
+// is read, so what an earlier call left in the array does not matter.  Calls whose work overlaps on the
+// GPU (two streams, or two host threads) share the array and race.  Not timed by atlb_timing_*, whose
+// events would be created here.
+int pair_fwd_noalloc(const float* SY, const float* SV, const float* ST, const long long* SID, const long long* CS,
+                     const float* AX, const float* AT, const long long* AC, const long long* AID, const float* SC,
+                     long long M, long long ncell, long long S, long long GH, long long GW, double h, double tau,
+                     double cut, float* out, cudaStream_t s) {
+  const size_t need = pair_workspace_bytes(M, ncell);
+  if (need > kNoAllocScratchBytes) {
+    set_error("atlb_ats_pair_fwd_noalloc: %lld anchors over %lld cells need %zu scratch bytes, above the fixed %zu",
+              M, ncell, need, kNoAllocScratchBytes);
+    return ATLB_ERR_WORKSPACE;
+  }
+  void* ws = nullptr;
+  if (int st = pair_scratch_address(&ws)) return st;
+  const PairWs w = carve(ws, M, ncell);
+  const RefAnchors A = bucket_anchors(w, AC, AX, AT, AID, M, S, GH, GW, ncell, out, s);
+  const RefEntries E{(const float2*)SY, (const float2*)SV, ST, SID};
+  const CellGrid G{GW, GH, S, ncell};
+  const PairConsts C = make_pair_consts(h, tau, cut);
+  if (M > 0 && ncell > 0)
+    launch(k_pair_fwd_t<RefEntries, RefAnchors, long long, RefOut>, warp_grid(ncell), kThreads, 0, s, E, A,
+           (const int*)w.start, CS, G, SC, C, RefOut{out, w.idx});
+  return launch_status("ats_pair_fwd_noalloc");
 }
 
 }  // namespace atlb
