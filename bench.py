@@ -40,8 +40,8 @@ WORKLOAD = ("config2: AnchoredExact(h=1, tau=1, n_anchors=None, n_slices=16, vis
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
-    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--events", type=int, default=N_EVENTS)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -145,26 +145,39 @@ def cpu_baseline(ev, flow, n):
 
 # ------------------------------------------------------------------------------------------------ clocks
 class ClockSampler:
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    """nvidia-smi samples every 20 ms while the timed region runs; ``mark()`` brackets the region and
+    ``summary()`` keeps the samples whose own timestamps fall inside it (the nearest one if none does)."""
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, gpu_index):
         self.proc, self.path, self.gpu = None, None, gpu_index
+        self.t0 = self.t1 = None
 
     def __enter__(self):
         try:
             fd, self.path = tempfile.mkstemp(suffix=".csv")
             os.close(fd)
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "20"],
                                          stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+            deadline = time.time() + 5.0  # wait for the first sample so the region is covered
+            while time.time() < deadline and os.path.getsize(self.path) == 0:
+                time.sleep(0.02)
         except Exception:
             self.proc = None
         return self
 
+    def mark(self, end=False):
+        if end:
+            self.t1 = time.time()
+        else:
+            self.t0 = time.time()
+
     def __exit__(self, *exc):
         if self.proc is not None:
+            time.sleep(0.05)
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
@@ -172,29 +185,57 @@ class ClockSampler:
                 self.proc.kill()
 
     def summary(self):
+        import datetime
         if not self.path or not os.path.exists(self.path):
             return None
         rows = []
         for line in open(self.path):
             f = [x.strip() for x in line.split(",")]
-            if len(f) >= 9:
-                rows.append(f)
+            if len(f) >= 10:
+                try:
+                    ts = datetime.datetime.strptime(f[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                except ValueError:
+                    continue
+                rows.append((ts, f[1:]))
         os.unlink(self.path)
         if not rows:
             return None
-        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        t0 = self.t0 if self.t0 is not None else rows[0][0]
+        t1 = self.t1 if self.t1 is not None else rows[-1][0]
+        inside = [r for ts, r in rows if t0 <= ts <= t1]
+        if not inside:
+            inside = [min(rows, key=lambda x: abs(x[0] - 0.5 * (t0 + t1)))[1]]
+        num = lambda v: v.replace(".", "", 1).isdigit()  # noqa: E731
+        sm = [float(r[1]) for r in inside if num(r[1])]
+        mx = [float(r[2]) for r in inside if num(r[2])]
         reasons = set()
         names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
-        for r in rows:
+        for r in inside:
             for name, val in zip(names, r[5:9]):
                 if val.lower().startswith("active"):
                     reasons.add(name)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": sorted(reasons), "samples": len(rows)}
+                "reasons": sorted(reasons), "samples": len(inside), "region_s": round(t1 - t0, 4)}
 
 
 # ------------------------------------------------------------------------------------------------ ours
+PROFILE_SUMMARY = ROOT / "profiles" / "pair_kernels.config2_1M.md"
+
+
+def profiled_traffic(kernel):
+    """DRAM bytes (read + write) per launch of ``kernel`` from the committed ncu summary of this workload
+    (a line ``traffic <kernel> <bytes>``), or None."""
+    import re
+    try:
+        for line in open(PROFILE_SUMMARY):
+            m_ = re.match(r"\s*[-*]?\s*traffic\s+(\w+)\s+(\d+)", line)
+            if m_ and m_.group(1) == kernel:
+                return int(m_.group(2))
+    except OSError:
+        pass
+    return None
+
+
 def measured_peak():
     try:
         d = json.load(open(ROOT / "MEASURED_PEAKS.json"))
@@ -252,12 +293,14 @@ def ours_arm(args):
     torch.cuda.synchronize()
     launches0 = L.atlb_kernel_launches()
     with ClockSampler(local) as clk:
+        clk.mark()
         for i in range(args.steps):
             flush.zero_()
             starts[i].record()
             step(ev, noise)
             ends[i].record()
         torch.cuda.synchronize()
+        clk.mark(end=True)
         barrier()
     launches = L.atlb_kernel_launches() - launches0
     ktime = {k: _lib.timing_read(k, reset=True) for k in ("k_pair_fwd", "k_pair_bwd")}
@@ -297,7 +340,10 @@ def ours_arm(args):
 
     if rank != 0:
         return
-    # ---- roofline of the dominant kernel (algorithmic bytes: plan entries + anchors + outputs)
+    # ---- roofline of the dominant kernel.  Algorithmic bytes of the fused path's compact layout:
+    # forward (tau covering the window): per plan entry its (y, v) float4; per anchor its (x, y, t, id)
+    # float4, its event's (x, v) float4 for the self term and S out.  Backward: per plan entry (y, v) +
+    # (t, id) = 24 B; per anchor (x, y, t, id) + dL/dS = 20 B; per event its (gx, gy) out.
     dom = max(ktime, key=lambda k: ktime[k][0])
     dom_ms, dom_n = ktime[dom]
     with torch.no_grad():
@@ -307,12 +353,13 @@ def ours_arm(args):
         v = m.velocity(xs, ev.t, ev.b)
         plan = F.build_pair_plan(xs, ev.t, v, ev.b, 1, H, W, anchors, 1.0, 1.0, 3.0, 16, anchor_xy=xa)
         Ns, M = plan.src_y.shape[0], plan.anc_x.shape[0]
-    entry_b = 8 + 8 + 4 + 8          # src_y, src_v, src_t, src_id
-    anchor_b = 8 + 4 + 8 + 4 + 4     # bucketed xy, t, id, index + output / gS
-    alg_bytes = Ns * entry_b + M * anchor_b
+        del plan
+    alg = {"k_pair_fwd": Ns * 16 + M * (16 + 16 + 4), "k_pair_bwd": Ns * 24 + M * 20 + args.events * 8}
+    alg_bytes = alg[dom]
     avg_ms = dom_ms / max(dom_n, 1)
     peak, peak_kind = measured_peak()
     achieved = alg_bytes / (avg_ms / 1000) / 1e9
+    traffic = profiled_traffic(dom)
     cores = os.cpu_count()
     cpu = None if (args.no_cpu_baseline or world > 1) else cpu_baseline(ev_cpu, flow_cpu, args.events)
     line = {
@@ -323,8 +370,8 @@ def ours_arm(args):
                    "anchors_per_window": M, "plan_entries": Ns, "l2": "flushed (256 MB write) before every step",
                    "parallelism": f"replicas x{world}"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "traffic": None, "kernel": dom, "avg_launch_ms": avg_ms, "algorithmic_bytes": alg_bytes,
-                     "peak_source": peak_kind},
+                     "traffic": traffic, "kernel": dom, "avg_launch_ms": avg_ms, "algorithmic_bytes": alg_bytes,
+                     "peak_source": peak_kind, "traffic_source": PROFILE_SUMMARY.name if traffic else None},
         "kernels_ms_per_step": {k: v[0] / max(v[1], 1) for k, v in ktime.items()},
         "e2e": {"value": world * args.events / (e2e_ms / 1000), "unit": "events/s", "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4},

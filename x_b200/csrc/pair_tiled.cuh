@@ -175,23 +175,31 @@ __device__ __forceinline__ void block_offsets(const int* __restrict__ csr, int g
 
 // The 3x3 neighbourhood of tile cell (cx, cy) as up to 3 ranges [lo, hi) of the staged rows (or of the
 // global CSR when not staged).
+// The CSR ranges of the 3 cell rows (cy-1 .. cy+1, each spanning cells cx-1 .. cx+1 clipped to the grid)
+// around cell (cx, cy); a row outside the grid gets an empty range.  Always 3 rows, so that callers
+// unroll their row loops and lo/hi stay in registers.
 __device__ __forceinline__ int neighbour_rows(const TileGeo& t, int gbase, int GW, int GH, int cx, int cy, bool staged,
                                               const int (*off)[kSC + 1], const int* __restrict__ csr, int* lo,
                                               int* hi) {
-  int nrows = 0;
   const int xl = max(cx - 1, 0), xh = min(cx + 1, GW - 1) + 1;
-  for (int y = max(cy - 1, 0); y <= cy + 1 && y < GH; ++y) {
-    if (staged) {
-      lo[nrows] = off[y - t.sy0][xl - t.sx0];
-      hi[nrows] = off[y - t.sy0][xh - t.sx0];
-    } else {
-      const int row = gbase + y * GW;
-      lo[nrows] = csr[row + xl];
-      hi[nrows] = csr[row + xh];
+#pragma unroll
+  for (int r = 0; r < 3; ++r) {
+    const int y = cy - 1 + r;
+    int l = 0, h = 0;
+    if (y >= 0 && y < GH) {
+      if (staged) {
+        l = off[y - t.sy0][xl - t.sx0];
+        h = off[y - t.sy0][xh - t.sx0];
+      } else {
+        const int row = gbase + y * GW;
+        l = csr[row + xl];
+        h = csr[row + xh];
+      }
     }
-    ++nrows;
+    lo[r] = l;
+    hi[r] = h;
   }
-  return nrows;
+  return 3;
 }
 
 // Leave-one-out: anchor a's own event appears among the candidates iff its entry of slice s exists and its
@@ -241,7 +249,8 @@ __device__ __forceinline__ void fwd_group_tile(const TileSmemFwd& sm, int p, con
     acc[q] = 0.f;
   }
   const unsigned yv_s = STAGED ? smem_addr(yv) : 0u, ti_s = STAGED ? smem_addr(ti) : 0u;
-  for (int r = 0; r < nrows; ++r) {
+#pragma unroll
+  for (int r = 0; r < 3; ++r) {
     const int k1 = hi[r];
     for (int k = lo[r] + lane; k < k1; k += 32) {
       float4 e;
@@ -332,7 +341,8 @@ __global__ void __launch_bounds__(kTileThreads) k_pair_fwd_tiled(FastEntries ent
         ng = (sm.acell_off[cyo][cxo + 1] - p0 + 3) >> 2;
         int lo[3], hi[3];
         const int nr = neighbour_rows(t, gbase, GW, GH, t.tx0 + cxo, t.ty0 + cyo, staged, sm.cell_off, cstart, lo, hi);
-        for (int r = 0; r < nr; ++r) cand += hi[r] - lo[r];
+#pragma unroll
+        for (int r = 0; r < 3; ++r) cand += hi[r] - lo[r];
       }
       int incl = ng;
 #pragma unroll
@@ -387,6 +397,52 @@ __global__ void __launch_bounds__(kTileThreads) k_pair_fwd_tiled(FastEntries ent
 }
 
 // ---- backward ----------------------------------------------------------------------------------------
+// One chunk of (up to) 32 source entries [kb, min(kb + 32, k1)) of one cell, lane = entry, against the
+// anchors of the 3 neighbouring cell rows (warp-uniform ranges lo/hi): staged anchors come from shared
+// memory, otherwise from global memory.  STAGED is a template parameter so that the inner loop holds
+// only the path it takes.
+template <bool TAU_ALL, bool STAGED>
+__device__ __forceinline__ void bwd_chunk(const FastEntries& ent, const FastAnchors& anc,
+                                          const float* __restrict__ gSb, unsigned xa_s, unsigned tg_s,
+                                          const int* lo, const int* hi, int kb, int k1, float cs,
+                                          const PairConsts& C, long long N, float* __restrict__ gv, int lane) {
+  const int k = kb + lane;
+  const bool valid = k < k1;
+  float2 sy, sv;
+  float st;
+  int sid;
+  ent.load(valid ? k : kb, sy, sv, st, sid);
+  const f32x2 y = pk2(sy.x, sy.y), v = pk2(sv.x, sv.y);
+  float gx = 0.f, gy = 0.f;
+#pragma unroll
+  for (int r = 0; r < 3; ++r) {
+    const int p1 = hi[r];
+    for (int p = lo[r]; p < p1; ++p) {
+      float4 a;
+      float2 tg;
+      if (STAGED) {
+        a = lds128(xa_s + 16u * (unsigned)p);
+        tg = lds64(tg_s + 8u * (unsigned)p);
+      } else {
+        const float4 qa = __ldg(anc.XT + p);
+        const float adt = sub_rn(qa.z, cs);
+        a = make_float4(qa.x, qa.y, adt, adt);
+        tg = make_float2(qa.z, __ldg(gSb + p) * C.invh2);
+      }
+      float2 rr;
+      const float d2 = residual2(pk2(a.x, a.y), pk2(a.z, a.w), y, v, &rr);
+      const float dt = sub_rn(tg.x, st);
+      bool ok = !(d2 > C.r2max);
+      if (!TAU_ALL) ok = ok && !(fabsf(dt) > C.tau);
+      const float f = ok ? tg.y * ex2_approx(-d2 * C.k2) * dt : 0.f;  // gS k dt / h^2
+      gx = fmaf(f, rr.x, gx);
+      gy = fmaf(f, rr.y, gy);
+    }
+  }
+  if (valid && (gx != 0.f || gy != 0.f) && sid >= 0 && sid < N) red_add_f2(gv + 2 * (long long)sid, gx, gy);
+}
+
+
 // Source entries of the tile; anchors of the (TX+2) x (TY+2) cells staged as (x, y, t - c_s) and
 // (t, dL/dS / h^2).  The self pair has dt = 0 and contributes nothing, so no leave-one-out test.
 template <bool TAU_ALL>
@@ -435,7 +491,8 @@ __global__ void __launch_bounds__(kTileThreads) k_pair_bwd_tiled(FastEntries ent
         nch = (k1 - k0 + 31) >> 5;
         int lo[3], hi[3];
         const int nr = neighbour_rows(t, gbase, GW, GH, t.tx0 + cxo, t.ty0 + cyo, staged, sm.cell_off, astart, lo, hi);
-        for (int r = 0; r < nr; ++r) nanc += hi[r] - lo[r];
+#pragma unroll
+        for (int r = 0; r < 3; ++r) nanc += hi[r] - lo[r];
       }
       if (nanc == 0) nch = 0;  // no anchor in reach: nothing to add
       int incl = nch;
@@ -481,43 +538,11 @@ __global__ void __launch_bounds__(kTileThreads) k_pair_bwd_tiled(FastEntries ent
       const int c = gbase + cy * GW + cx;
       const int k0 = cstart[c], k1 = cstart[c + 1];
       int lo[3], hi[3];
-      const int nrows = neighbour_rows(t, gbase, GW, GH, cx, cy, staged, sm.cell_off, astart, lo, hi);
-      {
-        const int kb = k0 + 32 * q;
-        const int k = kb + lane;
-        const bool valid = k < k1;
-        float2 sy, sv;
-        float st;
-        int sid;
-        ent.load(valid ? k : k0, sy, sv, st, sid);
-        const f32x2 y = pk2(sy.x, sy.y), v = pk2(sv.x, sv.y);
-        float gx = 0.f, gy = 0.f;
-        for (int r = 0; r < nrows; ++r) {
-          const int p1 = hi[r];
-          for (int p = lo[r]; p < p1; ++p) {
-            float4 a;
-            float2 tg;
-            if (staged) {
-              a = lds128(xa_s + 16u * (unsigned)p);
-              tg = lds64(tg_s + 8u * (unsigned)p);
-            } else {
-              const float4 qa = __ldg(anc.XT + p);
-              const float adt = sub_rn(qa.z, cs);
-              a = make_float4(qa.x, qa.y, adt, adt);
-              tg = make_float2(qa.z, __ldg(gSb + p) * C.invh2);
-            }
-            float2 rr;
-            const float d2 = residual2(pk2(a.x, a.y), pk2(a.z, a.w), y, v, &rr);
-            const float dt = sub_rn(tg.x, st);
-            bool ok = !(d2 > C.r2max);
-            if (!TAU_ALL) ok = ok && !(fabsf(dt) > C.tau);
-            const float f = ok ? tg.y * ex2_approx(-d2 * C.k2) * dt : 0.f;  // gS k dt / h^2
-            gx = fmaf(f, rr.x, gx);
-            gy = fmaf(f, rr.y, gy);
-          }
-        }
-        if (valid && (gx != 0.f || gy != 0.f) && sid >= 0 && sid < N) red_add_f2(gv + 2 * (long long)sid, gx, gy);
-      }
+      neighbour_rows(t, gbase, GW, GH, cx, cy, staged, sm.cell_off, astart, lo, hi);
+      if (staged)
+        bwd_chunk<TAU_ALL, true>(ent, anc, gSb, xa_s, tg_s, lo, hi, k0 + 32 * q, k1, cs, C, N, gv, lane);
+      else
+        bwd_chunk<TAU_ALL, false>(ent, anc, gSb, xa_s, tg_s, lo, hi, k0 + 32 * q, k1, cs, C, N, gv, lane);
     }
     __syncthreads();  // the next batch reuses the shared buffers
   }
