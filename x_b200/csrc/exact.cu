@@ -165,65 +165,117 @@ __global__ void __launch_bounds__(kThreads) k_exact_anchors(const float4* __rest
 }
 
 // ---- compact plan -------------------------------------------------------------------------------------
-__global__ void __launch_bounds__(kThreads) k_fast_count(PlanConsts P, const float4* __restrict__ ev4,
-                                                         const float* __restrict__ t, const long long* __restrict__ b,
-                                                         long long N, int* __restrict__ counts) {
+// ---- spatial order of the events for the plan passes ------------------------------------------------
+// The count and scatter passes walk the events in the order of their cell at the middle slice, i.e. of
+// where each event sits at mid-window under its own motion.  Under a smooth motion field, events that
+// share that cell stay within a few cells of one another at every slice, so the 32 lanes of a warp fall
+// into a handful of cells: one cursor atomic per distinct cell (warp-aggregated with match.any), and the
+// lanes of one cell write consecutive slots.  The order only decides where inside a cell an entry lands;
+// the cell keys themselves come from source_key, unchanged.
+__device__ __forceinline__ int order_key(const PlanConsts& P, float4 e, float t, int b) {
+  const float dtc = slice_centre(P, P.S / 2) - t;
+  const float qx = floorf((e.x + e.z * dtc - P.ox_f) / P.cell_f);
+  const float qy = floorf((e.y + e.w * dtc - P.oy_f) / P.cell_f);
+  const int cx = (int)fminf(fmaxf(qx, 0.f), (float)(P.GW - 1));  // NaN -> 0
+  const int cy = (int)fminf(fmaxf(qy, 0.f), (float)(P.GH - 1));
+  const int bb = (b >= 0 && b < P.B) ? b : 0;
+  return (bb * (int)P.GH + cy) * (int)P.GW + cx;
+}
+
+__global__ void __launch_bounds__(kThreads) k_order_count(PlanConsts P, const float4* __restrict__ ev4,
+                                                          const float* __restrict__ t,
+                                                          const long long* __restrict__ b, long long N,
+                                                          int* __restrict__ ocount) {
   const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long j = blockIdx.x * (long long)blockDim.x + threadIdx.x; j < N; j += stride)
+    atomicAdd(ocount + order_key(P, ev4[j], t[j], (int)b[j]), 1);
+}
+
+// XVo[i] = (x, y, vx, vy) and TBo[i] = (t bits, b, original index, 0) of the i-th event in that order.
+__global__ void __launch_bounds__(kThreads) k_order_scatter(PlanConsts P, const float4* __restrict__ ev4,
+                                                            const float* __restrict__ t,
+                                                            const long long* __restrict__ b, long long N,
+                                                            const int* __restrict__ ostart,
+                                                            int* __restrict__ ocursor, float4* __restrict__ XVo,
+                                                            int4* __restrict__ TBo) {
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long j = blockIdx.x * (long long)blockDim.x + threadIdx.x; j < N; j += stride) {
+    const float4 e = ev4[j];
+    const float tj = t[j];
+    const int bj = (int)b[j];
+    const int key = order_key(P, e, tj, bj);
+    const int pos = ostart[key] + atomicAdd(ocursor + key, 1);
+    XVo[pos] = e;
+    TBo[pos] = make_int4(__float_as_int(tj), bj, (int)j, 0);
+  }
+}
+
+// Plan entry counts over the ordered events; one atomic per distinct cell of a warp.  Keys fit in int
+// (the cell count is checked against the int32 range by the caller).
+__global__ void __launch_bounds__(kThreads) k_fast_count_ordered(PlanConsts P, const float4* __restrict__ XVo,
+                                                                 const int4* __restrict__ TBo, long long N,
+                                                                 int* __restrict__ counts) {
+  const int lane = threadIdx.x & 31;
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  const long long first = blockIdx.x * (long long)blockDim.x + (threadIdx.x & ~31);
   for (int s = blockIdx.y; s < P.S; s += gridDim.y) {
-    for (long long j = blockIdx.x * (long long)blockDim.x + threadIdx.x; j < N; j += stride) {
-      const float tj = t[j];
-      int s_lo, s_hi;
-      slice_range(P, tj, &s_lo, &s_hi);
-      if (s < s_lo || s > s_hi) continue;
-      const float4 e = ev4[j];
-      float yx, yy;
-      const long long key = source_key(P, e.x, e.y, e.z, e.w, tj, b[j], s, &yx, &yy);
-      if (key >= 0) atomicAdd(counts + key, 1);
+    for (long long i0 = first; i0 < N; i0 += stride) {  // warp-uniform loop
+      const long long i = i0 + lane;
+      int key = -1;
+      if (i < N) {
+        const int4 tb = TBo[i];
+        const float tj = __int_as_float(tb.x);
+        int s_lo, s_hi;
+        slice_range(P, tj, &s_lo, &s_hi);
+        if (s >= s_lo && s <= s_hi) {
+          const float4 e = XVo[i];
+          float yx, yy;
+          key = (int)source_key(P, e.x, e.y, e.z, e.w, tj, tb.y, s, &yx, &yy);
+        }
+      }
+      const unsigned grp = __match_any_sync(0xffffffffu, key);
+      if (key >= 0 && lane == __ffs(grp) - 1) atomicAdd(counts + key, __popc(grp));
     }
   }
 }
 
-// Four (source, slice) entries per thread and round: their cursor atomics are independent, so four are
-// in flight before the first result is needed (a single returning atomic per thread leaves the SM
-// waiting on L2 latency).
-constexpr int kScatterILP = 4;
-__global__ void __launch_bounds__(kThreads) k_fast_scatter(PlanConsts P, const float4* __restrict__ ev4,
-                                                           const float* __restrict__ t, const long long* __restrict__ b,
-                                                           long long N, const int* __restrict__ start,
-                                                           int* __restrict__ cursor, float4* __restrict__ YV,
-                                                           float2* __restrict__ TI) {
+__global__ void __launch_bounds__(kThreads) k_fast_scatter_ordered(PlanConsts P, const float4* __restrict__ XVo,
+                                                                   const int4* __restrict__ TBo, long long N,
+                                                                   const int* __restrict__ start,
+                                                                   int* __restrict__ cursor, float4* __restrict__ YV,
+                                                                   float2* __restrict__ TI) {
+  const int lane = threadIdx.x & 31;
+  const unsigned below = (1u << lane) - 1u;
   const long long stride = (long long)gridDim.x * blockDim.x;
+  const long long first = blockIdx.x * (long long)blockDim.x + (threadIdx.x & ~31);
   for (int s = blockIdx.y; s < P.S; s += gridDim.y) {
-    for (long long j0 = blockIdx.x * (long long)blockDim.x + threadIdx.x; j0 < N; j0 += stride * kScatterILP) {
-      long long key[kScatterILP];
-      float4 rec[kScatterILP];
-      float tt[kScatterILP];
-#pragma unroll
-      for (int q = 0; q < kScatterILP; ++q) {
-        const long long j = j0 + q * stride;
-        key[q] = -1;
-        if (j < N) {
-          const float tj = t[j];
-          int s_lo, s_hi;
-          slice_range(P, tj, &s_lo, &s_hi);
-          if (s >= s_lo && s <= s_hi) {
-            const float4 e = ev4[j];
-            float yx, yy;
-            key[q] = source_key(P, e.x, e.y, e.z, e.w, tj, b[j], s, &yx, &yy);
-            rec[q] = make_float4(yx, yy, e.z, e.w);
-            tt[q] = tj;
-          }
+    for (long long i0 = first; i0 < N; i0 += stride) {  // warp-uniform loop
+      const long long i = i0 + lane;
+      int key = -1, id = 0;
+      float tj = 0.f;
+      float4 rec = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (i < N) {
+        const int4 tb = TBo[i];
+        tj = __int_as_float(tb.x);
+        id = tb.z;
+        int s_lo, s_hi;
+        slice_range(P, tj, &s_lo, &s_hi);
+        if (s >= s_lo && s <= s_hi) {
+          const float4 e = XVo[i];
+          float yx, yy;
+          key = (int)source_key(P, e.x, e.y, e.z, e.w, tj, tb.y, s, &yx, &yy);
+          rec = make_float4(yx, yy, e.z, e.w);
         }
       }
-      int pos[kScatterILP];
-#pragma unroll
-      for (int q = 0; q < kScatterILP; ++q) pos[q] = key[q] >= 0 ? atomicAdd(cursor + key[q], 1) : 0;
-#pragma unroll
-      for (int q = 0; q < kScatterILP; ++q) {
-        if (key[q] < 0) continue;
-        const int p = start[key[q]] + pos[q];
-        YV[p] = rec[q];
-        TI[p] = make_float2(tt[q], __int_as_float((int)(j0 + q * stride)));
+      const unsigned grp = __match_any_sync(0xffffffffu, key);
+      const int leader = __ffs(grp) - 1;
+      int base = 0;
+      if (key >= 0 && lane == leader) base = start[key] + atomicAdd(cursor + key, __popc(grp));
+      base = __shfl_sync(0xffffffffu, base, leader);
+      if (key >= 0) {
+        const int p = base + __popc(grp & below);
+        YV[p] = rec;
+        TI[p] = make_float2(tj, __int_as_float(id));
       }
     }
   }
@@ -473,11 +525,15 @@ struct ExactWs {
   float* gSb;
   int* slice_hist;
   float* SC;
+  int* ocount;   // events per mid-slice cell (B*GH*GW), then the order cursor
+  int* ostart;
+  float4* XVo;   // events in spatial order: (x, y, vx, vy)
+  int4* TBo;     // (t bits, b, original index, 0)
   int* scratch;
 };
 
 size_t ws_layout(long long N, long long M, long long ncell, long long S, long long B, long long n_check,
-                 ExactWs* w, void* base) {
+                 long long nkey, ExactWs* w, void* base) {
   const long long nent = N * S;
   size_t off = 0;
   char* p = (char*)align_ptr(base ? base : (void*)256);
@@ -499,6 +555,10 @@ size_t ws_layout(long long N, long long M, long long ncell, long long S, long lo
   x.gSb = (float*)take((size_t)M * 4);
   x.slice_hist = (int*)take((size_t)(B * n_check) * 4);
   x.SC = (float*)take((size_t)S * 4);
+  x.ocount = (int*)take((size_t)nkey * 4);
+  x.ostart = (int*)take((size_t)(nkey + 1) * 4);
+  x.XVo = (float4*)take((size_t)N * 16);
+  x.TBo = (int4*)take((size_t)N * 16);
   x.scratch = (int*)take(64);
   if (w) *w = x;
   return off + 256;
@@ -517,7 +577,7 @@ bool tau_covers(const atlb_plan_geom& g, double tau) {
 
 size_t exact_workspace_bytes(const atlb_exact_cfg& c, long long N, long long M, const atlb_plan_geom& g) {
   const long long ncell = c.B * (long long)g.S * g.GH * g.GW;
-  return ws_layout(N, M, ncell, g.S, c.B, c.n_check, nullptr, nullptr);
+  return ws_layout(N, M, ncell, g.S, c.B, c.n_check, c.B * g.GH * g.GW, nullptr, nullptr);
 }
 
 static MotionView motion_of(const atlb_exact_cfg& c) {
@@ -560,18 +620,27 @@ int exact_forward(const atlb_exact_cfg& c, const float* t, const long long* b, l
                   float* S_out, float* den_out, float* ls_out, cudaStream_t s) {
   const long long ncell = c.B * (long long)g.S * g.GH * g.GW;
   ExactWs w;
-  ws_layout(N, M, ncell, g.S, c.B, c.n_check, &w, ws);
+  ws_layout(N, M, ncell, g.S, c.B, c.n_check, c.B * g.GH * g.GW, &w, ws);
   const PlanConsts P = make_plan_consts(g, c.tau, c.B);
   // slice centres, entries and anchors
   launch(k_slice_centres, (unsigned)((g.S + 127) / 128), 128, 0, s, P, w.SC);
   cudaMemsetAsync(w.counts, 0, (size_t)ncell * 4, s);
   cudaMemsetAsync(w.acounts, 0, (size_t)ncell * 4, s);
-  if (N > 0) launch(k_fast_count, slice_grid(N, P.S), kThreads, 0, s, P, (const float4*)ev4, t, b, N, w.counts);
+  if (N > 0) {  // events in mid-slice cell order (see k_order_count)
+    const long long nkey = c.B * g.GH * g.GW;
+    cudaMemsetAsync(w.ocount, 0, (size_t)nkey * 4, s);
+    launch(k_order_count, grid_for(N), kThreads, 0, s, P, (const float4*)ev4, t, b, N, w.ocount);
+    exclusive_scan<int>(w.ocount, nkey, w.partials, w.ostart, s);
+    launch(k_order_scatter, grid_for(N), kThreads, 0, s, P, (const float4*)ev4, t, b, N, (const int*)w.ostart,
+           w.ocount, w.XVo, w.TBo);
+    launch(k_fast_count_ordered, slice_grid(N, P.S), kThreads, 0, s, P, (const float4*)w.XVo, (const int4*)w.TBo, N,
+           w.counts);
+  }
   if (M > 0) launch(k_fast_anchor_count, grid_for(M), kThreads, 0, s, P, (const float4*)anc4, anc_b, M, w.acounts);
   exclusive_scan<int>(w.counts, ncell, w.partials, w.start, s);
   if (N > 0)
-    launch(k_fast_scatter, slice_grid(N, P.S), kThreads, 0, s, P, (const float4*)ev4, t, b, N, (const int*)w.start,
-           w.counts, w.YV, w.TI);
+    launch(k_fast_scatter_ordered, slice_grid(N, P.S), kThreads, 0, s, P, (const float4*)w.XVo, (const int4*)w.TBo,
+           N, (const int*)w.start, w.counts, w.YV, w.TI);
   exclusive_scan<int>(w.acounts, ncell, w.partials, w.astart, s);
   if (M > 0)
     launch(k_fast_anchor_scatter, grid_for(M), kThreads, 0, s, P, (const float4*)anc4, anc_b, M,
@@ -636,7 +705,7 @@ int exact_backward(const atlb_exact_cfg& c, const float* grad_ls, const long lon
                    float* gtheta, cudaStream_t s) {
   const long long ncell = c.B * (long long)g.S * g.GH * g.GW;
   ExactWs w;
-  ws_layout(N, M, ncell, g.S, c.B, c.n_check, &w, ws);
+  ws_layout(N, M, ncell, g.S, c.B, c.n_check, c.B * g.GH * g.GW, &w, ws);
   const float eps = (float)(c.eps_frac / (double)(c.H * c.W));
   cudaMemsetAsync(gv, 0, (size_t)N * 2 * sizeof(float), s);
   const FastEntries E{w.YV, w.TI};
