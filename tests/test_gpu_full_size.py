@@ -39,6 +39,10 @@ def test_config2_loss_and_flow_gradient_vs_oracle(config2):
     g = m.grid.grad.cpu().numpy()
     scale = np.abs(ref["grad_theta"]).max()
     np.testing.assert_allclose(g, ref["grad_theta"], rtol=1e-3, atol=1e-4 * scale)
+    # per anchor: one pair accepted or rejected differently from the oracle's exact test would move that
+    # anchor's log score by >= exp(-cut^2/2) / S (about 3e-4 here), far above this tolerance
+    ls, _ = obj.log_scores(ev, m, noise=(anchors, u, z))
+    np.testing.assert_allclose(ls.detach().cpu().numpy(), ref["ls"], rtol=1e-5, atol=1e-5)
 
 
 def test_config2_fused_equals_stagewise(config2):

@@ -415,15 +415,24 @@ __global__ void __launch_bounds__(kThreads) k_fwd_overflow(FastEntries E, FastAn
 }
 
 // dL/dS in bucket order from the upstream dL/dls (torch's LogBackward then DivBackward).
-__global__ void __launch_bounds__(kThreads) k_exact_gs(const int* __restrict__ BI, long long M,
-                                                       const float* __restrict__ grad_ls, const float* __restrict__ S,
-                                                       const float* __restrict__ den, float eps,
-                                                       float* __restrict__ gSb) {
+// The backward's anchor records in bucket order: AB = (x, y, t - c_s, t) and GB = dL/dS / h^2, with
+// dL/dS = dL/dls / (eps + S / den) / den (the Log then Div backward of ls = log(eps + S / den)) (s = the anchor's slice, as in anchor_cell).
+__global__ void __launch_bounds__(kThreads) k_exact_gs_records(PlanConsts P, const float4* __restrict__ XT,
+                                                               const int* __restrict__ BI, long long M,
+                                                               const float* __restrict__ grad_ls,
+                                                               const float* __restrict__ S,
+                                                               const float* __restrict__ den, float eps, float invh2,
+                                                               const float* __restrict__ SC,
+                                                               float4* __restrict__ AB, float* __restrict__ GB) {
   const long long stride = (long long)gridDim.x * blockDim.x;
   for (long long p = blockIdx.x * (long long)blockDim.x + threadIdx.x; p < M; p += stride) {
     const int i = BI[p];
     const float q = div_rn(S[i], den[i]);
-    gSb[p] = div_rn(div_rn(grad_ls[i], add_rn(eps, q)), den[i]);
+    const float g = div_rn(div_rn(grad_ls[i], add_rn(eps, q)), den[i]);
+    const float4 a = XT[p];
+    const int sa = (int)clampf(floorf(div_rn(a.z, P.delta_f)), 0.f, (float)(P.S - 1));
+    AB[p] = make_float4(a.x, a.y, sub_rn(a.z, SC[sa]), a.z);
+    GB[p] = g * invh2;
   }
 }
 
@@ -522,9 +531,10 @@ struct ExactWs {
   int* astart;
   float4* XT;
   int* BI;
-  float* gSb;
   int* slice_hist;
   float* SC;
+  float4* AB;    // backward anchor records (x, y, t - c_s, t), bucket order
+  float* GB;     // dL/dS / h^2, bucket order
   int* ocount;   // events per mid-slice cell (B*GH*GW), then the order cursor
   int* ostart;
   float4* XVo;   // events in spatial order: (x, y, vx, vy)
@@ -552,9 +562,10 @@ size_t ws_layout(long long N, long long M, long long ncell, long long S, long lo
   x.astart = (int*)take((size_t)(ncell + 1) * 4);
   x.XT = (float4*)take((size_t)M * 16);
   x.BI = (int*)take((size_t)M * 4);
-  x.gSb = (float*)take((size_t)M * 4);
   x.slice_hist = (int*)take((size_t)(B * n_check) * 4);
   x.SC = (float*)take((size_t)S * 4);
+  x.AB = (float4*)take((size_t)M * 16);
+  x.GB = (float*)take((size_t)M * 4);
   x.ocount = (int*)take((size_t)nkey * 4);
   x.ostart = (int*)take((size_t)(nkey + 1) * 4);
   x.XVo = (float4*)take((size_t)N * 16);
@@ -709,29 +720,20 @@ int exact_backward(const atlb_exact_cfg& c, const float* grad_ls, const long lon
   const float eps = (float)(c.eps_frac / (double)(c.H * c.W));
   cudaMemsetAsync(gv, 0, (size_t)N * 2 * sizeof(float), s);
   const FastEntries E{w.YV, w.TI};
-  const FastAnchors A{w.XT, w.BI};
-  const CellGrid G{g.GW, g.GH, g.S, ncell};
   const PairConsts C = make_pair_consts(c.h, c.tau, c.cut);
   if (M > 0 && ncell > 0) {
-    launch(k_exact_gs, grid_for(M), kThreads, 0, s, (const int*)w.BI, M, grad_ls, S, den, eps, w.gSb);
-    static bool attr = false;
-    if (!attr) {
-      cudaFuncSetAttribute(k_pair_bwd_tiled<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           (int)sizeof(TileSmemBwd));
-      cudaFuncSetAttribute(k_pair_bwd_tiled<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           (int)sizeof(TileSmemBwd));
-      attr = true;
-    }
-    const dim3 grid((unsigned)((g.GW + kTileX - 1) / kTileX), (unsigned)((g.GH + kTileY - 1) / kTileY),
-                    (unsigned)g.S);
-    const TileGrid T{(int)g.GW, (int)g.GH, (int)g.S, (int)c.B};
+    const PlanConsts P = make_plan_consts(g, c.tau, c.B);
+    launch(k_exact_gs_records, grid_for(M), kThreads, 0, s, P, (const float4*)w.XT, (const int*)w.BI, M, grad_ls, S,
+           den, eps, C.invh2, (const float*)w.SC, w.AB, w.GB);
+    const int nrows = (int)(c.B * g.S * g.GH);
+    const dim3 grid((unsigned)((g.GW + 7) / 8), (unsigned)min(nrows, 65535));
     cudaEvent_t e0 = timing_begin(s);
     if (tau_covers(g, c.tau))
-      launch(k_pair_bwd_tiled<true>, grid, kTileThreads, sizeof(TileSmemBwd), s, E, A, (const int*)w.astart,
-             (const float*)w.gSb, (const int*)w.start, T, (const float*)w.SC, C, N, gv);
+      launch(k_pair_bwd_cells<true>, grid, 256, 0, s, E, (const float4*)w.AB, (const float*)w.GB,
+             (const int*)w.astart, (const int*)w.start, (int)g.GW, (int)g.GH, nrows, C, N, gv);
     else
-      launch(k_pair_bwd_tiled<false>, grid, kTileThreads, sizeof(TileSmemBwd), s, E, A, (const int*)w.astart,
-             (const float*)w.gSb, (const int*)w.start, T, (const float*)w.SC, C, N, gv);
+      launch(k_pair_bwd_cells<false>, grid, 256, 0, s, E, (const float4*)w.AB, (const float*)w.GB,
+             (const int*)w.astart, (const int*)w.start, (int)g.GW, (int)g.GH, nrows, C, N, gv);
     timing_end("k_pair_bwd", s, e0);
   }
   const MotionView Mv = motion_of(c);

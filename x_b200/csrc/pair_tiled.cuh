@@ -1,4 +1,4 @@
-// Shared-memory tiled pair kernels of the fused path (compact entry layout).
+// Pair kernels of the fused path (compact entry layout): shared-memory tiled forward, cell-per-warp backward.
 //
 // Grid: (tile column, tile row, slice); each CTA walks the batches of its slice.  A tile is TX x TY cells.
 //   forward : the entries of the (TX+2) x (TY+2) cells around the tile and the anchors of the tile are
@@ -7,8 +7,10 @@
 //             anchor cells: a cell's anchors in register groups of up to 4, the candidates of its 3x3
 //             neighbourhood streamed by the lanes.  A tile whose neighbourhood does not fit reads its
 //             candidates from global memory instead (same loop, global pointer).
-//   backward: the anchors (and their dL/dS) of the (TX+2) x (TY+2) cells are staged; each lane takes one
-//             source entry of the tile and sums its gradient over the staged anchors of its 3x3 cells.
+//   backward: not tiled.  One warp per source cell, one entry per lane; the anchors of the 3x3 cells are
+//             warp-uniform broadcast loads through L1 of per-anchor records prepared once per backward
+//             (measured faster than staging them: no barriers, no per-tile set-up, L1 reuse across the
+//             8 neighbouring cells of a CTA).
 // Index arithmetic is 32-bit and division-free (power-of-two tile width, one grid axis per coordinate):
 // per-thread integer divisions by runtime values cost more than the pair arithmetic they surround.
 #pragma once
@@ -25,7 +27,6 @@ constexpr int kTileY = 4;
 constexpr int kTileThreads = 512;
 constexpr int kStageCap = 3456;   // staged entries per CTA (forward): 3456 * 16 B = 54 KB (+ 8 B each for t)
 constexpr int kTileAncCap = 768;  // staged anchors per CTA (forward): 768 * 24 B = 18 KB
-constexpr int kAncCap = 1536;     // staged anchors per CTA (backward): 1536 * 24 B = 36 KB
 
 constexpr int kSR = kTileY + 2;  // staged rows
 constexpr int kSC = kTileX + 2;  // staged columns
@@ -77,16 +78,6 @@ struct TileSmemFwd {
   WorkQueue wq;
   float2 ti[kStageCap];  // entry times: staged only when tau does not cover the window (last member: the
                          // launch omits it from the dynamic shared memory otherwise)
-};
-
-struct TileSmemBwd {
-  float4 xa[kAncCap];  // (x, y, t - c_s, t - c_s)
-  float2 tg[kAncCap];  // (t, dL/dS / h^2)
-  int cell_off[kSR][kSC + 1];
-  int row_p0[kSR];
-  int row_base[kSR];
-  int total;
-  WorkQueue wq;
 };
 
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
@@ -397,154 +388,66 @@ __global__ void __launch_bounds__(kTileThreads) k_pair_fwd_tiled(FastEntries ent
 }
 
 // ---- backward ----------------------------------------------------------------------------------------
-// One chunk of (up to) 32 source entries [kb, min(kb + 32, k1)) of one cell, lane = entry, against the
-// anchors of the 3 neighbouring cell rows (warp-uniform ranges lo/hi): staged anchors come from shared
-// memory, otherwise from global memory.  STAGED is a template parameter so that the inner loop holds
-// only the path it takes.
-template <bool TAU_ALL, bool STAGED>
-__device__ __forceinline__ void bwd_chunk(const FastEntries& ent, const FastAnchors& anc,
-                                          const float* __restrict__ gSb, unsigned xa_s, unsigned tg_s,
-                                          const int* lo, const int* hi, int kb, int k1, float cs,
-                                          const PairConsts& C, long long N, float* __restrict__ gv, int lane) {
-  const int k = kb + lane;
-  const bool valid = k < k1;
-  float2 sy, sv;
-  float st;
-  int sid;
-  ent.load(valid ? k : kb, sy, sv, st, sid);
-  const f32x2 y = pk2(sy.x, sy.y), v = pk2(sv.x, sv.y);
-  float gx = 0.f, gy = 0.f;
+// One warp per source cell (grid: x = groups of 8 cells of a cell row, y = cell rows of all (batch, slice)
+// grids), lanes over the cell's entries in chunks of 32.  The anchors of the 3 neighbouring cell rows are
+// read as warp-uniform broadcast loads through L1 from records prepared once per backward:
+// AB = (x, y, t - c_s, t) and GB = dL/dS / h^2, in bucket order.
+template <bool TAU_ALL>
+__global__ void __launch_bounds__(256) k_pair_bwd_cells(FastEntries ent, const float4* __restrict__ AB,
+                                                        const float* __restrict__ GB, const int* __restrict__ astart,
+                                                        const int* __restrict__ cstart, int GW, int GH, int nrows,
+                                                        PairConsts C, long long N, float* __restrict__ gv) {
+  const int lane = threadIdx.x & 31;
+  const int cx = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (cx >= GW) return;
+  for (int row = blockIdx.y; row < nrows; row += gridDim.y) {  // row = (b * S + s) * GH + cy
+  const int cy = row % GH;
+  const int c = row * GW + cx;
+  const int k0 = cstart[c], k1 = cstart[c + 1];
+  if (k0 == k1) continue;
+  const int gbase = (row - cy) * GW;
+  const int xl = max(cx - 1, 0), xh = min(cx + 1, GW - 1) + 1;
+  int lo[3], hi[3];
 #pragma unroll
   for (int r = 0; r < 3; ++r) {
-    const int p1 = hi[r];
-    for (int p = lo[r]; p < p1; ++p) {
-      float4 a;
-      float2 tg;
-      if (STAGED) {
-        a = lds128(xa_s + 16u * (unsigned)p);
-        tg = lds64(tg_s + 8u * (unsigned)p);
-      } else {
-        const float4 qa = __ldg(anc.XT + p);
-        const float adt = sub_rn(qa.z, cs);
-        a = make_float4(qa.x, qa.y, adt, adt);
-        tg = make_float2(qa.z, __ldg(gSb + p) * C.invh2);
-      }
-      float2 rr;
-      const float d2 = residual2(pk2(a.x, a.y), pk2(a.z, a.w), y, v, &rr);
-      const float dt = sub_rn(tg.x, st);
-      bool ok = !(d2 > C.r2max);
-      if (!TAU_ALL) ok = ok && !(fabsf(dt) > C.tau);
-      const float f = ok ? tg.y * ex2_approx(-d2 * C.k2) * dt : 0.f;  // gS k dt / h^2
-      gx = fmaf(f, rr.x, gx);
-      gy = fmaf(f, rr.y, gy);
+    const int y = cy - 1 + r;
+    int l = 0, h = 0;
+    if (y >= 0 && y < GH) {
+      l = astart[gbase + y * GW + xl];
+      h = astart[gbase + y * GW + xh];
     }
+    lo[r] = l;
+    hi[r] = h;
   }
-  if (valid && (gx != 0.f || gy != 0.f) && sid >= 0 && sid < N) red_add_f2(gv + 2 * (long long)sid, gx, gy);
-}
-
-
-// Source entries of the tile; anchors of the (TX+2) x (TY+2) cells staged as (x, y, t - c_s) and
-// (t, dL/dS / h^2).  The self pair has dt = 0 and contributes nothing, so no leave-one-out test.
-template <bool TAU_ALL>
-__global__ void __launch_bounds__(kTileThreads) k_pair_bwd_tiled(FastEntries ent, FastAnchors anc,
-                                                                 const int* __restrict__ astart,
-                                                                 const float* __restrict__ gSb,
-                                                                 const int* __restrict__ cstart, TileGrid G,
-                                                                 const float* __restrict__ SC, PairConsts C,
-                                                                 long long N, float* __restrict__ gv) {
-  extern __shared__ __align__(16) unsigned char smem_raw[];
-  TileSmemBwd& sm = *reinterpret_cast<TileSmemBwd*>(smem_raw);
-  const TileGeo t = tile_geo(G);
-  const int GW = G.GW, GH = G.GH, s = (int)blockIdx.z;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
-  const float cs = __ldg(SC + s);
-  const int nsc = t.sx1 - t.sx0, ntx = t.tx1 - t.tx0, nty = t.ty1 - t.ty0;
-  const unsigned xa_s = smem_addr(sm.xa), tg_s = smem_addr(sm.tg);
-
-  for (int b = 0; b < G.B; ++b) {
-    const int gbase = (b * G.S + s) * GH * GW;
-    if (warp == 0)
-      block_offsets<kSC>(astart, gbase, GW, t.sy0, t.sy1, t.sx0, t.sx1, sm.cell_off, sm.row_p0, sm.row_base,
-                         &sm.total);
-    __syncthreads();
-    const bool staged = sm.total <= kAncCap;
-    if (staged) {
-      for (int r = 0; r < t.sy1 - t.sy0; ++r) {
-        const int p0 = sm.row_p0[r], b0 = sm.cell_off[r][0], n = sm.cell_off[r][nsc] - b0;
-        for (int i = threadIdx.x; i < n; i += blockDim.x) {
-          const float4 a = __ldg(anc.XT + p0 + i);
-          const float adt = sub_rn(a.z, cs);
-          sm.xa[b0 + i] = make_float4(a.x, a.y, adt, adt);
-          sm.tg[b0 + i] = make_float2(a.z, __ldg(gSb + p0 + i) * C.invh2);
-        }
-      }
-    }
-    __syncthreads();
-    // work items: (cell, chunk of 32 source entries), cost = sources x staged anchors of the 3x3 cells
-    if (warp == 0) {
-      int nch = 0, nanc = 0, k0 = 0, k1 = 0;
-      const int cxo = lane & (kTileX - 1), cyo = lane >> kTileXLog;
-      if (lane < kTileX * kTileY && cxo < ntx && cyo < nty) {
-        const int c = gbase + (t.ty0 + cyo) * GW + t.tx0 + cxo;
-        k0 = cstart[c];
-        k1 = cstart[c + 1];
-        nch = (k1 - k0 + 31) >> 5;
-        int lo[3], hi[3];
-        const int nr = neighbour_rows(t, gbase, GW, GH, t.tx0 + cxo, t.ty0 + cyo, staged, sm.cell_off, astart, lo, hi);
+  if (lo[0] == hi[0] && lo[1] == hi[1] && lo[2] == hi[2]) continue;
+  for (int kb = k0; kb < k1; kb += 32) {
+    const int k = kb + lane;
+    const bool valid = k < k1;
+    float2 sy, sv;
+    float st;
+    int sid;
+    ent.load(valid ? k : k0, sy, sv, st, sid);
+    const f32x2 y = pk2(sy.x, sy.y), v = pk2(sv.x, sv.y);
+    float gx = 0.f, gy = 0.f;
 #pragma unroll
-        for (int r = 0; r < 3; ++r) nanc += hi[r] - lo[r];
+    for (int r = 0; r < 3; ++r) {
+      const int p1 = hi[r];
+#pragma unroll 2
+      for (int p = lo[r]; p < p1; ++p) {
+        const float4 a = __ldg(AB + p);
+        const float ga = __ldg(GB + p);
+        float2 rr;
+        const float d2 = residual2(pk2(a.x, a.y), pk2(a.z, a.z), y, v, &rr);
+        const float dt = sub_rn(a.w, st);
+        bool ok = !(d2 > C.r2max);
+        if (!TAU_ALL) ok = ok && !(fabsf(dt) > C.tau);
+        const float f = ok ? ga * ex2_approx(-d2 * C.k2) * dt : 0.f;  // gS k dt / h^2
+        gx = fmaf(f, rr.x, gx);
+        gy = fmaf(f, rr.y, gy);
       }
-      if (nanc == 0) nch = 0;  // no anchor in reach: nothing to add
-      int incl = nch;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int u = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += u;
-      }
-      const int total_items = __shfl_sync(0xffffffffu, incl, 31);
-      for (int q = 0; q < nch; ++q) {
-        const int slot = incl - nch + q;
-        if (slot < kMaxItems) {
-          sm.wq.item[slot] = (lane << 16) | q;
-          sm.wq.cost[slot] = min(32, k1 - (k0 + 32 * q)) * nanc;
-        }
-      }
-      if (lane == 0) sm.wq.n = total_items;
     }
-    __syncthreads();
-    const int nitems = sm.wq.n;
-    if (nitems <= kMaxItems) sort_items(sm.wq);
-    __syncthreads();
-    for (int w = warp;; w += nwarps) {
-      int it;
-      if (nitems <= kMaxItems) {
-        it = next_item(sm.wq, lane);
-      } else {  // more chunks than the list holds: static walk over (cell, chunk)
-        it = -1;
-        int acc = 0;
-        for (int ci = 0; ci < kTileX * kTileY && it < 0; ++ci) {
-          const int cxo = ci & (kTileX - 1), cyo = ci >> kTileXLog;
-          if (cxo >= ntx || cyo >= nty) continue;
-          const int c = gbase + (t.ty0 + cyo) * GW + t.tx0 + cxo;
-          const int nch = (cstart[c + 1] - cstart[c] + 31) >> 5;
-          if (w < acc + nch) it = (ci << 16) | (w - acc);
-          acc += nch;
-        }
-      }
-      if (it < 0) break;
-      const int ci = it >> 16, q = it & 0xffff;
-      const int cxo = ci & (kTileX - 1), cyo = ci >> kTileXLog;
-      const int cx = t.tx0 + cxo, cy = t.ty0 + cyo;
-      const int c = gbase + cy * GW + cx;
-      const int k0 = cstart[c], k1 = cstart[c + 1];
-      int lo[3], hi[3];
-      neighbour_rows(t, gbase, GW, GH, cx, cy, staged, sm.cell_off, astart, lo, hi);
-      if (staged)
-        bwd_chunk<TAU_ALL, true>(ent, anc, gSb, xa_s, tg_s, lo, hi, k0 + 32 * q, k1, cs, C, N, gv, lane);
-      else
-        bwd_chunk<TAU_ALL, false>(ent, anc, gSb, xa_s, tg_s, lo, hi, k0 + 32 * q, k1, cs, C, N, gv, lane);
-    }
-    __syncthreads();  // the next batch reuses the shared buffers
+    if (valid && (gx != 0.f || gy != 0.f) && sid >= 0 && sid < N) red_add_f2(gv + 2 * (long long)sid, gx, gy);
+  }
   }
 }
 
