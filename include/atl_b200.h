@@ -38,7 +38,7 @@ enum {
 const char* atlb_last_error(void);
 /* ABI version of this header (bumped on incompatible changes). */
 int atlb_abi_version(void);
-#define ATLB_ABI_VERSION 2
+#define ATLB_ABI_VERSION 3
 /* Number of kernels this library has launched in the calling process (instrumentation; no reference
  * counterpart). */
 uint64_t atlb_kernel_launches(void);
@@ -60,11 +60,17 @@ int atlb_splat_bilinear_fwd(const float* pos, const float* w, const int64_t* bid
                             int64_t W, float* img, atlb_stream_t stream);
 int atlb_splat_bilinear_bwd(const float* gimg, const float* pos, const float* w, const int64_t* bidx, int64_t N,
                             int64_t B, int64_t H, int64_t W, float* gpos, float* gw, atlb_stream_t stream);
+/* Gaussian splat: events are bucketed by 32x32-pixel image tile in the workspace
+ * (atlb_splat_gauss_workspace_bytes), one shared-memory tile per CTA.  radius <= ATLB_SPLAT_GAUSS_MAX_RADIUS
+ * (the tile and its halo live in shared memory). */
+#define ATLB_SPLAT_GAUSS_MAX_RADIUS 96
+size_t atlb_splat_gauss_workspace_bytes(int64_t N, int64_t B, int64_t H, int64_t W);
 int atlb_splat_gauss_fwd(const float* pos, const float* w, const int64_t* bidx, int64_t N, int64_t B, int64_t H,
-                         int64_t W, double sigma, int64_t radius, float* img, atlb_stream_t stream);
+                         int64_t W, double sigma, int64_t radius, float* img, void* workspace, size_t workspace_bytes,
+                         atlb_stream_t stream);
 int atlb_splat_gauss_bwd(const float* gimg, const float* pos, const float* w, const int64_t* bidx, int64_t N,
                          int64_t B, int64_t H, int64_t W, double sigma, int64_t radius, float* gpos, float* gw,
-                         atlb_stream_t stream);
+                         void* workspace, size_t workspace_bytes, atlb_stream_t stream);
 int atlb_gather_bilinear_fwd(const float* img, const float* pos, const int64_t* bidx, int64_t N, int64_t B, int64_t H,
                              int64_t W, float* out, atlb_stream_t stream);
 int atlb_gather_bilinear_bwd(const float* gval, const float* img, const float* pos, const int64_t* bidx, int64_t N,

@@ -33,14 +33,14 @@ def test_binding_covers_header_exactly():
 
 def test_abi_version_and_counter():
     L = _lib.load_library()
-    assert L.atlb_abi_version() == 2
+    assert L.atlb_abi_version() == 3
     assert L.atlb_kernel_launches() >= 0
 
 
 def test_argument_validation_needs_no_device():
     """Invalid arguments are rejected before any CUDA call, with a message."""
     L = _lib.load_library()
-    st = L.atlb_splat_gauss_fwd(None, None, None, 10, 1, 4, 4, 1.0, 3, None, None)
+    st = L.atlb_splat_gauss_fwd(None, None, None, 10, 1, 4, 4, 1.0, 3, None, None, 0, None)
     assert st == _lib.ATLB_ERR_ARG
     assert b"NULL" in L.atlb_last_error()
     st = L.atlb_velocity(7, None, 1, 1, 1, 4, 4, None, None, 0, None, None)

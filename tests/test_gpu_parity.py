@@ -55,13 +55,18 @@ def test_ops_match_reference_goldens(ext):
     np.testing.assert_allclose(np_(ext.voxel_grid(pos, t, p, b, B, 5, H, W)), g["voxel"], rtol=RTOL, atol=1e-6)
 
 
-@pytest.mark.parametrize("n,B,H,W,sigma", [(20000, 3, 64, 80, 1.5), (5000, 1, 30, 40, 0.5), (0, 2, 8, 8, 1.0)])
+# sigma sweep of configuration 4 (R = 2, 3, 6, 12), a radius beyond the compiled window sizes (R = 15),
+# widths that are not multiples of 4 (scalar flush) and of 32 (partial tiles), window centres outside the image
+@pytest.mark.parametrize("n,B,H,W,sigma", [(20000, 3, 64, 80, 1.5), (5000, 1, 30, 40, 0.5), (0, 2, 8, 8, 1.0),
+                                           (30000, 2, 70, 101, 1.0), (20000, 1, 96, 128, 2.0),
+                                           (12000, 2, 64, 64, 4.0), (4000, 1, 50, 75, 5.0)])
 def test_splat_gather_vs_oracle(ext, n, B, H, W, sigma):
     rng = np.random.default_rng(n + B)
-    pos = np.stack([rng.uniform(-6, W + 6, n), rng.uniform(-6, H + 6, n)], 1).astype(np.float32)
-    w = rng.uniform(0.1, 1.1, n).astype(np.float32)
-    b = rng.integers(0, B, n).astype(np.int64)
     R = int(math.ceil(3 * sigma))
+    pos = np.stack([rng.uniform(-R - 3, W + R + 3, n), rng.uniform(-R - 3, H + R + 3, n)], 1).astype(np.float32)
+    w = rng.uniform(0.1, 1.1, n).astype(np.float32)
+    w[::97] = 0.0  # zero weights are skipped by the forward and still get gw in the backward
+    b = rng.integers(0, B, n).astype(np.int64)
     img = ext.splat_gauss_fwd(T(pos), T(w), T(b), B, H, W, sigma, R)
     np.testing.assert_allclose(np_(img), O.splat_gauss_fwd(pos, w, b, B, H, W, sigma, R), rtol=RTOL, atol=1e-5)
     gimg = rng.normal(size=(B, H, W)).astype(np.float32)

@@ -44,16 +44,20 @@ class _AtlB200Ext:
     def splat_gauss_fwd(self, pos, w, b, B, H, W, sigma, R):
         L.require_cuda("pos", pos, F32); L.require_cuda("w", w, F32); L.require_cuda("bidx", b, I64)
         img = _empty((B, H, W), pos)
+        nb = L.lib().atlb_splat_gauss_workspace_bytes(pos.shape[0], B, H, W)
+        ws = L.workspace(nb, pos.device)
         L.check(L.lib().atlb_splat_gauss_fwd(L.ptr(pos), L.ptr(w), L.ptr(b), pos.shape[0], B, H, W, float(sigma),
-                                              int(R), L.ptr(img), L.stream()), "splat_gauss_fwd")
+                                              int(R), L.ptr(img), L.ptr(ws), nb, L.stream()), "splat_gauss_fwd")
         return img
 
     def splat_gauss_bwd(self, g, pos, w, b, sigma, R):
         L.require_cuda("gimg", g, F32); L.require_cuda("pos", pos, F32)
         gp, gw = torch.empty_like(pos), torch.empty_like(w)
-        L.check(L.lib().atlb_splat_gauss_bwd(L.ptr(g), L.ptr(pos), L.ptr(w), L.ptr(b), pos.shape[0], g.shape[0],
-                                              g.shape[1], g.shape[2], float(sigma), int(R), L.ptr(gp), L.ptr(gw),
-                                              L.stream()),
+        B, H, W = g.shape
+        nb = L.lib().atlb_splat_gauss_workspace_bytes(pos.shape[0], B, H, W)
+        ws = L.workspace(nb, pos.device)
+        L.check(L.lib().atlb_splat_gauss_bwd(L.ptr(g), L.ptr(pos), L.ptr(w), L.ptr(b), pos.shape[0], B, H, W,
+                                              float(sigma), int(R), L.ptr(gp), L.ptr(gw), L.ptr(ws), nb, L.stream()),
                 "splat_gauss_bwd")
         return [gp, gw]
 

@@ -47,8 +47,9 @@ _SIGS = {
                                 _int]),
     "atlb_splat_bilinear_fwd": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _vp]),
     "atlb_splat_bilinear_bwd": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _vp, _vp]),
-    "atlb_splat_gauss_fwd": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _dbl, _i64, _vp, _vp]),
-    "atlb_splat_gauss_bwd": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _dbl, _i64, _vp, _vp, _vp]),
+    "atlb_splat_gauss_workspace_bytes": (_size, [_i64, _i64, _i64, _i64]),
+    "atlb_splat_gauss_fwd": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _dbl, _i64, _vp, _vp, _size, _vp]),
+    "atlb_splat_gauss_bwd": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _dbl, _i64, _vp, _vp, _vp, _size, _vp]),
     "atlb_gather_bilinear_fwd": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _vp]),
     "atlb_gather_bilinear_bwd": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _vp, _vp]),
     "atlb_voxel_grid": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _vp]),

@@ -51,10 +51,11 @@ int splat_bilinear_fwd(const float*, const float*, const long long*, long long, 
                        float*, cudaStream_t);
 int splat_bilinear_bwd(const float*, const float*, const float*, const long long*, long long, long long, long long,
                        long long, float*, float*, cudaStream_t);
+size_t splat_gauss_workspace_bytes(long long N, long long B, long long H, long long W);
 int splat_gauss_fwd(const float*, const float*, const long long*, long long, long long, long long, long long, double,
-                    long long, float*, cudaStream_t);
+                    long long, float*, void*, cudaStream_t);
 int splat_gauss_bwd(const float*, const float*, const float*, const long long*, long long, long long, long long,
-                    long long, double, long long, float*, float*, cudaStream_t);
+                    long long, double, long long, float*, float*, void*, cudaStream_t);
 int gather_fwd(const float*, const float*, const long long*, long long, long long, long long, long long, float*,
                cudaStream_t);
 int gather_bwd(const float*, const float*, const float*, const long long*, long long, long long, long long, long long,
@@ -138,21 +139,46 @@ int atlb_splat_bilinear_bwd(const float* gimg, const float* pos, const float* w,
   return splat_bilinear_bwd(gimg, pos, w, LL(bidx), N, B, H, W, gpos, gw, STREAM(stream));
 }
 
+size_t atlb_splat_gauss_workspace_bytes(int64_t N, int64_t B, int64_t H, int64_t W) {
+  return splat_gauss_workspace_bytes(N < 0 ? 0 : N, B < 0 ? 0 : B, H < 0 ? 0 : H, W < 0 ? 0 : W);
+}
+
+static int check_gauss(int64_t N, int64_t B, int64_t H, int64_t W, int64_t radius, void* ws, size_t ws_bytes,
+                       const char* fn) {
+  if (radius > ATLB_SPLAT_GAUSS_MAX_RADIUS) {
+    set_error("%s: radius %lld above the tiled splat's limit of %d", fn, (long long)radius,
+              ATLB_SPLAT_GAUSS_MAX_RADIUS);
+    return ATLB_ERR_ARG;
+  }
+  if (N > (1LL << 31) - 1 || H > (1LL << 30) || W > (1LL << 30) || B * ((H + 31) / 32) * ((W + 31) / 32) > (1LL << 31) - 2) {
+    set_error("%s: sizes exceed the int32 event / tile indices", fn);
+    return ATLB_ERR_OVERFLOW;
+  }
+  if (!ws || ws_bytes < splat_gauss_workspace_bytes(N, B, H, W)) {
+    set_error("%s: workspace %zu < %zu bytes", fn, ws_bytes, splat_gauss_workspace_bytes(N, B, H, W));
+    return ATLB_ERR_WORKSPACE;
+  }
+  return ATLB_OK;
+}
+
 int atlb_splat_gauss_fwd(const float* pos, const float* w, const int64_t* bidx, int64_t N, int64_t B, int64_t H,
-                         int64_t W, double sigma, int64_t radius, float* img, atlb_stream_t stream) {
+                         int64_t W, double sigma, int64_t radius, float* img, void* workspace, size_t workspace_bytes,
+                         atlb_stream_t stream) {
   clear();
   NONNEG(N); NONNEG(B); NONNEG(H); NONNEG(W); NONNEG(radius);
   NEED(pos, N); NEED(w, N); NEED(bidx, N); NEED(img, B * H * W);
-  return splat_gauss_fwd(pos, w, LL(bidx), N, B, H, W, sigma, radius, img, STREAM(stream));
+  if (int st = check_gauss(N, B, H, W, radius, workspace, workspace_bytes, __func__)) return st;
+  return splat_gauss_fwd(pos, w, LL(bidx), N, B, H, W, sigma, radius, img, workspace, STREAM(stream));
 }
 
 int atlb_splat_gauss_bwd(const float* gimg, const float* pos, const float* w, const int64_t* bidx, int64_t N,
                          int64_t B, int64_t H, int64_t W, double sigma, int64_t radius, float* gpos, float* gw,
-                         atlb_stream_t stream) {
+                         void* workspace, size_t workspace_bytes, atlb_stream_t stream) {
   clear();
   NONNEG(N); NONNEG(B); NONNEG(H); NONNEG(W); NONNEG(radius);
-  NEED(gimg, N); NEED(pos, N); NEED(w, N); NEED(bidx, N); NEED(gpos, N); NEED(gw, N);
-  return splat_gauss_bwd(gimg, pos, w, LL(bidx), N, B, H, W, sigma, radius, gpos, gw, STREAM(stream));
+  NEED(gimg, B * H * W); NEED(pos, N); NEED(w, N); NEED(bidx, N); NEED(gpos, N); NEED(gw, N);
+  if (int st = check_gauss(N, B, H, W, radius, workspace, workspace_bytes, __func__)) return st;
+  return splat_gauss_bwd(gimg, pos, w, LL(bidx), N, B, H, W, sigma, radius, gpos, gw, workspace, STREAM(stream));
 }
 
 int atlb_gather_bilinear_fwd(const float* img, const float* pos, const int64_t* bidx, int64_t N, int64_t B, int64_t H,

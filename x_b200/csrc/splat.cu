@@ -1,4 +1,5 @@
-// Splat / gather / voxel kernels of the sliced path (csrc/atl_cpu.cpp:17-172, 256-286).
+// Bilinear splat, gather and voxel kernels of the sliced path (csrc/atl_cpu.cpp:17-76, 134-172, 256-286); the
+// Gaussian splat is in gauss_tiled.cu.
 //
 // Each output keeps the reference's per-element rounding sequence.  Scatters go to L2 with
 // fire-and-forget red.global (no return value, no retry loop); gathers are one thread per event.
@@ -67,72 +68,6 @@ __global__ void __launch_bounds__(kThreads) k_splat_bilinear_bwd(const float* __
       sx = add_rn(sx, mul_rn(g, dcx));
       sy = add_rn(sy, mul_rn(g, dcy));
     });
-    const float wn = Wt[n];
-    GW[n] = sw;
-    GP[n] = make_float2(mul_rn(wn, sx), mul_rn(wn, sy));
-  }
-}
-
-struct GaussConsts {
-  float inv2s2, norm, s2;
-  long long R;
-};
-
-__global__ void __launch_bounds__(kThreads) k_splat_gauss_fwd(const float2* __restrict__ P,
-                                                              const float* __restrict__ Wt,
-                                                              const long long* __restrict__ Bi, long long N,
-                                                              long long B, long long H, long long W, GaussConsts K,
-                                                              float* __restrict__ I) {
-  const long long stride = (long long)gridDim.x * blockDim.x;
-  for (long long n = blockIdx.x * (long long)blockDim.x + threadIdx.x; n < N; n += stride) {
-    const float wn = mul_rn(Wt[n], K.norm);
-    if (wn == 0.f || Bi[n] < 0 || Bi[n] >= B) continue;
-    const float2 p = P[n];
-    if (!(fabsf(p.x) < 1e18f && fabsf(p.y) < 1e18f)) continue;  // no tap inside the image
-    const long long cx = lroundf(p.x), cy = lroundf(p.y);
-    float* base = I + Bi[n] * H * W;
-    const long long y0 = cy - K.R > 0 ? cy - K.R : 0, y1 = cy + K.R < H - 1 ? cy + K.R : H - 1;
-    const long long x0 = cx - K.R > 0 ? cx - K.R : 0, x1 = cx + K.R < W - 1 ? cx + K.R : W - 1;
-    for (long long yy = y0; yy <= y1; ++yy) {
-      const float dy = sub_rn((float)yy, p.y);
-      const float dy2 = mul_rn(dy, dy);
-      for (long long xx = x0; xx <= x1; ++xx) {
-        const float dx = sub_rn((float)xx, p.x);
-        const float e = expf(mul_rn(-add_rn(mul_rn(dx, dx), dy2), K.inv2s2));
-        red_add_f1(base + yy * W + xx, mul_rn(wn, e));
-      }
-    }
-  }
-}
-
-__global__ void __launch_bounds__(kThreads) k_splat_gauss_bwd(const float* __restrict__ G,
-                                                              const float2* __restrict__ P,
-                                                              const float* __restrict__ Wt,
-                                                              const long long* __restrict__ Bi, long long N,
-                                                              long long B, long long H, long long W, GaussConsts K,
-                                                              float2* __restrict__ GP, float* __restrict__ GW) {
-  const long long stride = (long long)gridDim.x * blockDim.x;
-  for (long long n = blockIdx.x * (long long)blockDim.x + threadIdx.x; n < N; n += stride) {
-    const float2 p = P[n];
-    const bool ok = Bi[n] >= 0 && Bi[n] < B && fabsf(p.x) < 1e18f && fabsf(p.y) < 1e18f;
-    const long long cx = ok ? lroundf(p.x) : 0, cy = ok ? lroundf(p.y) : 0;
-    const long long RR = ok ? K.R : -1;  // an empty tap window for skipped events
-    const float* base = G + (ok ? Bi[n] : 0) * H * W;
-    float sw = 0.f, sx = 0.f, sy = 0.f;
-    const long long y0 = cy - RR > 0 ? cy - RR : 0, y1 = cy + RR < H - 1 ? cy + RR : H - 1;
-    const long long x0 = cx - RR > 0 ? cx - RR : 0, x1 = cx + RR < W - 1 ? cx + RR : W - 1;
-    for (long long yy = y0; yy <= y1 && RR >= 0; ++yy) {
-      const float dy = sub_rn((float)yy, p.y);
-      const float dy2 = mul_rn(dy, dy);
-      for (long long xx = x0; xx <= x1; ++xx) {
-        const float dx = sub_rn((float)xx, p.x);
-        const float e = expf(mul_rn(-add_rn(mul_rn(dx, dx), dy2), K.inv2s2));
-        const float gk = mul_rn(mul_rn(K.norm, e), __ldg(base + yy * W + xx));
-        sw = add_rn(sw, gk);
-        sx = add_rn(sx, div_rn(mul_rn(gk, dx), K.s2));
-        sy = add_rn(sy, div_rn(mul_rn(gk, dy), K.s2));
-      }
-    }
     const float wn = Wt[n];
     GW[n] = sw;
     GP[n] = make_float2(mul_rn(wn, sx), mul_rn(wn, sy));
@@ -209,19 +144,6 @@ __global__ void __launch_bounds__(kThreads) k_voxel(const float2* __restrict__ P
   }
 }
 
-GaussConsts gauss_consts(double sigma, long long R) {
-  GaussConsts K;
-  const float s2 = (float)(sigma * sigma);
-  K.s2 = s2;
-  volatile float d = 2.f * s2;
-  K.inv2s2 = 1.f / d;
-  volatile float n = 2.f * (float)M_PI;
-  n = n * s2;
-  K.norm = 1.f / n;
-  K.R = R;
-  return K;
-}
-
 inline int grid_for(long long n) { return clamp_grid(blocks_for(n, kThreads)); }
 
 }  // namespace
@@ -238,22 +160,6 @@ int splat_bilinear_bwd(const float* g, const float* pos, const float* w, const l
   if (N > 0)
     launch(k_splat_bilinear_bwd, grid_for(N), kThreads, 0, s, g, (const float2*)pos, w, b, N, B, H, W, (float2*)gpos, gw);
   return launch_status("splat_bilinear_bwd");
-}
-
-int splat_gauss_fwd(const float* pos, const float* w, const long long* b, long long N, long long B, long long H,
-                    long long W, double sigma, long long R, float* img, cudaStream_t s) {
-  cudaMemsetAsync(img, 0, (size_t)(B * H * W) * sizeof(float), s);
-  if (N > 0)
-    launch(k_splat_gauss_fwd, grid_for(N), kThreads, 0, s, (const float2*)pos, w, b, N, B, H, W, gauss_consts(sigma, R), img);
-  return launch_status("splat_gauss_fwd");
-}
-
-int splat_gauss_bwd(const float* g, const float* pos, const float* w, const long long* b, long long N, long long B,
-                    long long H, long long W, double sigma, long long R, float* gpos, float* gw, cudaStream_t s) {
-  if (N > 0)
-    launch(k_splat_gauss_bwd, grid_for(N), kThreads, 0, s, g, (const float2*)pos, w, b, N, B, H, W, gauss_consts(sigma, R),
-                                                       (float2*)gpos, gw);
-  return launch_status("splat_gauss_bwd");
 }
 
 int gather_fwd(const float* img, const float* pos, const long long* b, long long N, long long B, long long H,
