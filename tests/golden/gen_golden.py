@@ -24,7 +24,7 @@ sys.path.insert(0, str(HERE.parents[1]))
 from oracle.refload import load_reference  # noqa: E402
 
 atl = load_reference()
-from atl.motion import Affine, DenseLinearFlow, Translation  # noqa: E402
+from atl.motion import Affine, DenseLinearFlow, PixelTrajectories, Translation  # noqa: E402
 from atl.objectives import ats as ATS  # noqa: E402
 from atl.ops import functional as F  # noqa: E402
 from atl.core.events import EventPacket  # noqa: E402
@@ -194,6 +194,33 @@ def gen_exact(kind, n, B, H, W, seed, n_anchors, h=1.0, tau=1.0, S=16, visibilit
          loss=out["loss"].detach(), grad_theta=m.theta.grad)
 
 
+def gen_sliced(name, kind, n, B, H, W, seed, S, sigma, K=3):
+    """AnchoredSliced (ats.py:108-183) on a seeded window: per-anchor log scores, loss and the gradient of
+    the loss w.r.t. the motion parameters (a PixelTrajectories coefficient grid, or theta / flow grid)."""
+    xy, t, b = synth_window(n, H, W, seed, B)
+    ev = EventPacket(xy, t, torch.ones(n), b, B, H, W)
+    g = torch.Generator().manual_seed(seed + 1)
+    if kind == "trajectories":
+        coeff = torch.nn.functional.avg_pool2d(torch.randn(B, 2 * K, H, W, generator=g), 9, 1, 4) * 12
+        coeff.requires_grad_(True)
+        m, param = PixelTrajectories(coeff, K, basis_kind="bezier", tile=4), coeff
+    elif kind == "affine_exact":
+        th = torch.cat([(torch.rand(B, 2, generator=g) - 0.5) * 20, (torch.rand(B, 4, generator=g) - 0.5) * 0.1], 1)
+        m = Affine(B, H, W, mode="exact", init=th)
+        param = m.theta
+    else:
+        grid = torch.nn.functional.avg_pool2d(torch.randn(B, 2, H, W, generator=g), 7, 1, 3) * 30
+        m = DenseLinearFlow(B, H, W, grid=(H, W), mode="linear", init=grid)
+        param = m.grid
+    init = param.detach().clone()
+    obj = ATS.AnchoredSliced(n_slices=S, sigma=sigma, seed=seed + 2)
+    ls, idx = obj.log_scores(ev, m)
+    loss = -ls.mean()
+    loss.backward()
+    save(name, kind=kind, xy=xy, t=t, b=b, B=B, H=H, W=W, S=S, sigma=sigma, K=K, seed=seed + 2, param=init,
+         ls=ls.detach(), idx=idx, loss=loss.detach(), grad=param.grad)
+
+
 if __name__ == "__main__":
     gen_ops()
     gen_plan("plan_tau1_s8", 600, 2, 20, 24, 3, 6.0, 1.0, 8, 1.5)
@@ -205,3 +232,6 @@ if __name__ == "__main__":
     gen_exact("translation", 3000, 1, 48, 64, 40, None)
     gen_exact("affine", 3000, 2, 48, 64, 50, 2000, tau=0.5, S=8)
     gen_exact("dense", 4000, 1, 48, 64, 60, None, h=1.0)
+    gen_sliced("sliced_trajectories", "trajectories", 3000, 2, 48, 64, 70, 4, 1.5)
+    gen_sliced("sliced_affine_exact", "affine_exact", 3000, 1, 48, 64, 80, 5, 1.0)
+    gen_sliced("sliced_dense", "dense", 3000, 1, 48, 64, 90, 4, 2.0)

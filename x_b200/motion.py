@@ -4,10 +4,12 @@
 w.r.t. ``theta`` / the flow grid) in libatlb200 kernels that round exactly like the reference's torch
 CPU ops, so the pair plan built from the velocities is bit-identical.  ``transport`` in
 ``mode="linear"`` is x + v(x) (t' - t); ``mode="exact"`` keeps the reference's closed-form matrix
-exponential (affine fields) or RK4 (dense fields) in torch ops on the device.
+exponential (affine fields) or RK4 (dense fields) in torch ops on the device.  ``PixelTrajectories``
+(atl/motion/trajectories.py) keeps its torch transport (fixed-point inversion on the tile coefficients).
 """
 from __future__ import annotations
 
+import math
 from typing import Optional
 
 import torch
@@ -209,6 +211,87 @@ def sample_grid(field: torch.Tensor, gpos: torch.Tensor, b: torch.Tensor) -> tor
         return f[base + yy * Wg + xx]
     return (at(y0, x0) * ((1 - ax) * (1 - ay))[:, None] + at(y0, x1) * (ax * (1 - ay))[:, None] +
             at(y1, x0) * ((1 - ax) * ay)[:, None] + at(y1, x1) * (ax * ay)[:, None])
+
+
+def basis(t: torch.Tensor, K: int, kind: str = "polynomial") -> torch.Tensor:
+    """(..., K) trajectory basis g_k(t) - g_k(0) (atl/motion/trajectories.py:26-37): t^k, or the degree-K
+    Bernstein polynomials B_{k,K}(t), k = 1..K (Bezier with the first control point pinned to the start)."""
+    t = t[..., None]
+    k = torch.arange(1, K + 1, device=t.device, dtype=t.dtype)
+    if kind == "polynomial":
+        return t ** k
+    if kind == "bezier":
+        logc = (math.lgamma(K + 1) - torch.lgamma(k + 1) - torch.lgamma(K - k + 1))
+        return torch.exp(logc) * t ** k * (1 - t) ** (K - k)
+    raise ValueError(kind)
+
+
+class PixelTrajectories(Motion):
+    """One continuous-time trajectory per ``tile`` x ``tile`` patch, coefficients from a (B, 2K, H, W) grid
+    (atl/motion/trajectories.py:40-120): q(p, t) = p + sum_k c_k(p) g_k(t), channels [y_1..y_K, x_1..x_K].
+    Transport inverts q(p, t) = x by fixed-point iteration, then evaluates q(p, t')."""
+
+    def __init__(self, coeff_grid: torch.Tensor, K: int, basis_kind: str = "polynomial", tile: int = 4,
+                 assign: str = "invert", n_fixed_point: int = 6):
+        super().__init__()
+        self.coeff_grid = coeff_grid
+        self.K, self.basis_kind, self.tile, self.assign, self.n_fp = K, basis_kind, tile, assign, n_fixed_point
+        B, C, H, W = coeff_grid.shape
+        assert C == 2 * K
+        self.B, self.H, self.W = B, H, W
+        s = tile // 2
+        self.tile_c = coeff_grid[:, :, s::tile, s::tile]
+        self.Hq, self.Wq = self.tile_c.shape[-2:]
+        self.offset = float(s)
+        self.linear_at_event = (K == 1 and basis_kind == "polynomial")
+
+    def _coeff_at(self, p, b):
+        g = (p - self.offset) / self.tile
+        c = sample_grid(self.tile_c, g, b)
+        cy, cx = c[:, :self.K], c[:, self.K:]
+        return torch.stack([cx, cy], -1)
+
+    def displacement(self, p, b, t):
+        g = basis(t, self.K, self.basis_kind)
+        return (self._coeff_at(p, b) * g[..., None]).sum(1)
+
+    def origin(self, xy, t, b):
+        p = xy
+        for _ in range(self.n_fp):
+            p = xy - self.displacement(p, b, t)
+        return p
+
+    def transport(self, xy, t, t_dst, b):
+        p = self.origin(xy, t, b)
+        return p + self.displacement(p, b, as_time(t_dst, t))
+
+    def velocity(self, xy, t, b):
+        if not self.linear_at_event:
+            raise NotImplementedError("per-event velocity only for the degree-1 polynomial prior")
+        p = self.origin(xy, t, b)
+        return self._coeff_at(p, b)[:, 0]
+
+    def tile_trajectories(self, times: torch.Tensor) -> torch.Tensor:
+        """Positions (B, n_t, n_tiles, 2) of every tile trajectory at the given times."""
+        B, Hq, Wq, K = self.B, self.Hq, self.Wq, self.K
+        dev = self.tile_c.device
+        ys = torch.arange(Hq, device=dev, dtype=torch.float32) * self.tile + self.offset
+        xs = torch.arange(Wq, device=dev, dtype=torch.float32) * self.tile + self.offset
+        gy, gx = torch.meshgrid(ys, xs, indexing="ij")
+        p = torch.stack([gx, gy], -1).reshape(1, 1, -1, 2)
+        c = self.tile_c.reshape(B, 2, K, Hq * Wq)
+        cxy = torch.stack([c[:, 1], c[:, 0]], -1)
+        g = basis(times, K, self.basis_kind)
+        return p + torch.einsum("tk,bknc->btnc", g, cxy)
+
+    def flow_field(self, B, H, W, t0=0.0, t1=1.0):
+        times = torch.tensor([t0, t1], device=self.tile_c.device, dtype=torch.float32)
+        tr = self.tile_trajectories(times)
+        f = (tr[:, 1] - tr[:, 0]).reshape(self.B, self.Hq, self.Wq, 2).permute(0, 3, 1, 2)
+        return torch.nn.functional.interpolate(f, size=(H, W), mode="bilinear", align_corners=False)
+
+    def regulariser_fields(self, B, H, W):
+        return self.tile_c
 
 
 MODELS = {"translation": Translation, "affine": Affine, "dense": DenseLinearFlow}
