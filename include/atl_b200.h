@@ -38,7 +38,7 @@ enum {
 const char* atlb_last_error(void);
 /* ABI version of this header (bumped on incompatible changes). */
 int atlb_abi_version(void);
-#define ATLB_ABI_VERSION 3
+#define ATLB_ABI_VERSION 4
 /* Number of kernels this library has launched in the calling process (instrumentation; no reference
  * counterpart). */
 uint64_t atlb_kernel_launches(void);
@@ -203,6 +203,10 @@ typedef struct {
   int64_t S;             /* n_slices */
   int32_t visibility;    /* exposure correction on (1) / off (0) */
   int64_t n_check;       /* slices of the exposure check (16 in the reference) */
+  int64_t src_begin, src_end; /* sources of the pair sums: events [src_begin, src_end); src_end <= 0: all.
+                              * With a sub-range, S_out holds the partial sums over those sources (sum
+                              * them across the ranges, then ls = log(eps + S / den)), and the backward
+                              * returns gv and gtheta of those sources only (sum gtheta across ranges). */
 } atlb_exact_cfg;
 
 int atlb_exact_prepare(const atlb_exact_cfg* cfg, const float* xy, const float* u, const float* t, const int64_t* b,

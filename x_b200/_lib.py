@@ -34,7 +34,7 @@ class ExactCfg(ctypes.Structure):
                 ("Wg", ctypes.c_int64), ("B", ctypes.c_int64), ("H", ctypes.c_int64), ("W", ctypes.c_int64),
                 ("h", ctypes.c_double), ("tau", ctypes.c_double), ("cut", ctypes.c_double),
                 ("eps_frac", ctypes.c_double), ("S", ctypes.c_int64), ("visibility", ctypes.c_int32),
-                ("n_check", ctypes.c_int64)]
+                ("n_check", ctypes.c_int64), ("src_begin", ctypes.c_int64), ("src_end", ctypes.c_int64)]
 
 
 # name -> (restype, argtypes)

@@ -399,6 +399,11 @@ static int check_exact_sizes(const atlb_exact_cfg* c, int64_t N, int64_t M, cons
     set_error("%s: N * n_slices = %lld entries exceed the int32 plan index", fn, (long long)(N * c->S));
     return ATLB_ERR_OVERFLOW;
   }
+  if (c->src_end > 0 && (c->src_begin < 0 || c->src_begin > c->src_end || c->src_end > N)) {
+    set_error("%s: source range [%lld, %lld) outside [0, %lld]", fn, (long long)c->src_begin, (long long)c->src_end,
+              (long long)N);
+    return ATLB_ERR_ARG;
+  }
   if (g && (g->S != c->S || g->GW < 1 || g->GH < 1 || (double)c->B * g->S * (double)g->GH * g->GW > 2.0e9)) {
     set_error("%s: invalid geometry", fn);
     return ATLB_ERR_OVERFLOW;

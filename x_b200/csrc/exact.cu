@@ -191,11 +191,12 @@ __global__ void __launch_bounds__(kThreads) k_order_count(PlanConsts P, const fl
     atomicAdd(ocount + order_key(P, ev4[j], t[j], (int)b[j]), 1);
 }
 
-// XVo[i] = (x, y, vx, vy) and TBo[i] = (t bits, b, original index, 0) of the i-th event in that order.
+// XVo[i] = (x, y, vx, vy) and TBo[i] = (t bits, b, original index, 0) of the i-th event in that order;
+// the arrays passed start at event id0.
 __global__ void __launch_bounds__(kThreads) k_order_scatter(PlanConsts P, const float4* __restrict__ ev4,
                                                             const float* __restrict__ t,
                                                             const long long* __restrict__ b, long long N,
-                                                            const int* __restrict__ ostart,
+                                                            long long id0, const int* __restrict__ ostart,
                                                             int* __restrict__ ocursor, float4* __restrict__ XVo,
                                                             int4* __restrict__ TBo) {
   const long long stride = (long long)gridDim.x * blockDim.x;
@@ -206,7 +207,7 @@ __global__ void __launch_bounds__(kThreads) k_order_scatter(PlanConsts P, const 
     const int key = order_key(P, e, tj, bj);
     const int pos = ostart[key] + atomicAdd(ocursor + key, 1);
     XVo[pos] = e;
-    TBo[pos] = make_int4(__float_as_int(tj), bj, (int)j, 0);
+    TBo[pos] = make_int4(__float_as_int(tj), bj, (int)(id0 + j), 0);
   }
 }
 
@@ -579,6 +580,12 @@ int warp_grid(long long nwarps) { return clamp_grid(blocks_for(nwarps * 32, kThr
 
 // Every pair passes |t_i - t_j| <= tau when tau covers the events' time range: fl(t_i - t_j) never exceeds
 // fl(t_hi - t_lo) (rounding is monotonic).  NaN bounds (unknown range) fail the test.
+// The events that are sources of the pair sums: [src_begin, src_end) of the configuration, all if src_end <= 0.
+void src_range(const atlb_exact_cfg& c, long long N, long long* j0, long long* j1) {
+  *j0 = c.src_end > 0 ? c.src_begin : 0;
+  *j1 = c.src_end > 0 ? c.src_end : N;
+}
+
 bool tau_covers(const atlb_plan_geom& g, double tau) {
   const float span = g.t_hi - g.t_lo;
   return span <= (float)tau;
@@ -588,7 +595,9 @@ bool tau_covers(const atlb_plan_geom& g, double tau) {
 
 size_t exact_workspace_bytes(const atlb_exact_cfg& c, long long N, long long M, const atlb_plan_geom& g) {
   const long long ncell = c.B * (long long)g.S * g.GH * g.GW;
-  return ws_layout(N, M, ncell, g.S, c.B, c.n_check, c.B * g.GH * g.GW, nullptr, nullptr);
+  long long j0, j1;
+  src_range(c, N, &j0, &j1);
+  return ws_layout(j1 - j0, M, ncell, g.S, c.B, c.n_check, c.B * g.GH * g.GW, nullptr, nullptr);
 }
 
 static MotionView motion_of(const atlb_exact_cfg& c) {
@@ -630,28 +639,34 @@ int exact_forward(const atlb_exact_cfg& c, const float* t, const long long* b, l
                   const float* ev4, const float* anc4, const long long* anc_b, const atlb_plan_geom& g, void* ws,
                   float* S_out, float* den_out, float* ls_out, cudaStream_t s) {
   const long long ncell = c.B * (long long)g.S * g.GH * g.GW;
+  long long j0, j1;
+  src_range(c, N, &j0, &j1);
+  const long long ns = j1 - j0;  // source events of this call
   ExactWs w;
-  ws_layout(N, M, ncell, g.S, c.B, c.n_check, c.B * g.GH * g.GW, &w, ws);
-  const PlanConsts P = make_plan_consts(g, c.tau, c.B);
+  ws_layout(ns, M, ncell, g.S, c.B, c.n_check, c.B * g.GH * g.GW, &w, ws);
+  PlanConsts P = make_plan_consts(g, c.tau, c.B);
+  P.src0 = j0;
+  P.src1 = j1;
   // slice centres, entries and anchors
   launch(k_slice_centres, (unsigned)((g.S + 127) / 128), 128, 0, s, P, w.SC);
   cudaMemsetAsync(w.counts, 0, (size_t)ncell * 4, s);
   cudaMemsetAsync(w.acounts, 0, (size_t)ncell * 4, s);
-  if (N > 0) {  // events in mid-slice cell order (see k_order_count)
+  if (ns > 0) {  // source events in mid-slice cell order (see k_order_count)
     const long long nkey = c.B * g.GH * g.GW;
+    const float4* ev = (const float4*)ev4 + j0;
     cudaMemsetAsync(w.ocount, 0, (size_t)nkey * 4, s);
-    launch(k_order_count, grid_for(N), kThreads, 0, s, P, (const float4*)ev4, t, b, N, w.ocount);
+    launch(k_order_count, grid_for(ns), kThreads, 0, s, P, ev, t + j0, b + j0, ns, w.ocount);
     exclusive_scan<int>(w.ocount, nkey, w.partials, w.ostart, s);
-    launch(k_order_scatter, grid_for(N), kThreads, 0, s, P, (const float4*)ev4, t, b, N, (const int*)w.ostart,
+    launch(k_order_scatter, grid_for(ns), kThreads, 0, s, P, ev, t + j0, b + j0, ns, j0, (const int*)w.ostart,
            w.ocount, w.XVo, w.TBo);
-    launch(k_fast_count_ordered, slice_grid(N, P.S), kThreads, 0, s, P, (const float4*)w.XVo, (const int4*)w.TBo, N,
-           w.counts);
+    launch(k_fast_count_ordered, slice_grid(ns, P.S), kThreads, 0, s, P, (const float4*)w.XVo, (const int4*)w.TBo,
+           ns, w.counts);
   }
   if (M > 0) launch(k_fast_anchor_count, grid_for(M), kThreads, 0, s, P, (const float4*)anc4, anc_b, M, w.acounts);
   exclusive_scan<int>(w.counts, ncell, w.partials, w.start, s);
-  if (N > 0)
-    launch(k_fast_scatter_ordered, slice_grid(N, P.S), kThreads, 0, s, P, (const float4*)w.XVo, (const int4*)w.TBo,
-           N, (const int*)w.start, w.counts, w.YV, w.TI);
+  if (ns > 0)
+    launch(k_fast_scatter_ordered, slice_grid(ns, P.S), kThreads, 0, s, P, (const float4*)w.XVo, (const int4*)w.TBo,
+           ns, (const int*)w.start, w.counts, w.YV, w.TI);
   exclusive_scan<int>(w.acounts, ncell, w.partials, w.astart, s);
   if (M > 0)
     launch(k_fast_anchor_scatter, grid_for(M), kThreads, 0, s, P, (const float4*)anc4, anc_b, M,
@@ -715,8 +730,11 @@ int exact_backward(const atlb_exact_cfg& c, const float* grad_ls, const long lon
                    const float* ev4, const atlb_plan_geom& g, void* ws, const float* S, const float* den, float* gv,
                    float* gtheta, cudaStream_t s) {
   const long long ncell = c.B * (long long)g.S * g.GH * g.GW;
+  long long j0, j1;
+  src_range(c, N, &j0, &j1);
+  const long long ns = j1 - j0;
   ExactWs w;
-  ws_layout(N, M, ncell, g.S, c.B, c.n_check, c.B * g.GH * g.GW, &w, ws);
+  ws_layout(ns, M, ncell, g.S, c.B, c.n_check, c.B * g.GH * g.GW, &w, ws);
   const float eps = (float)(c.eps_frac / (double)(c.H * c.W));
   cudaMemsetAsync(gv, 0, (size_t)N * 2 * sizeof(float), s);
   const FastEntries E{w.YV, w.TI};
@@ -740,11 +758,13 @@ int exact_backward(const atlb_exact_cfg& c, const float* grad_ls, const long lon
   const size_t nth = c.kind == ATLB_MOTION_DENSE ? (size_t)(c.Bt * 2 * c.Hg * c.Wg)
                                                  : (size_t)(c.Bt * (c.kind == ATLB_MOTION_TRANSLATION ? 2 : 6));
   cudaMemsetAsync(gtheta, 0, nth * sizeof(float), s);
-  if (N > 0) {
+  if (ns > 0) {  // the motion gradient of this call's source events
+    const float2* g2 = (const float2*)gv + j0;
+    const float4* e4 = (const float4*)ev4 + j0;
     if (c.kind == ATLB_MOTION_DENSE)
-      launch(k_exact_vbwd_dense, grid_for(N), kThreads, 0, s, Mv, (const float2*)gv, (const float4*)ev4, b, N, gtheta);
+      launch(k_exact_vbwd_dense, grid_for(ns), kThreads, 0, s, Mv, g2, e4, b + j0, ns, gtheta);
     else
-      launch(k_exact_vbwd_param, grid_for(N), kThreads, 0, s, Mv, (const float2*)gv, (const float4*)ev4, b, N, gtheta);
+      launch(k_exact_vbwd_param, grid_for(ns), kThreads, 0, s, Mv, g2, e4, b + j0, ns, gtheta);
   }
   return launch_status("exact_backward");
 }

@@ -198,6 +198,7 @@ __device__ __forceinline__ int neighbour_rows(const TileGeo& t, int gbase, int G
 __device__ __forceinline__ float self_term(const PlanConsts& P, const PairConsts& C, const float4* __restrict__ ev4,
                                            int a, float xi, float yi, float ti, float dti, int b, int s, int cx,
                                            int cy) {
+  if (a < P.src0 || a >= P.src1) return 0.f;  // the anchor's own event is not among this call's sources
   int s_lo, s_hi;
   slice_range(P, ti, &s_lo, &s_hi);
   if (s < s_lo || s > s_hi || b < 0 || b >= P.B) return 0.f;

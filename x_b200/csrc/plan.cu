@@ -203,6 +203,8 @@ PlanConsts make_plan_consts(const atlb_plan_geom& g, double tau, long long B) {
   P.GH = g.GH;
   P.S = g.S;
   P.B = B;
+  P.src0 = 0;
+  P.src1 = LLONG_MAX;
   return P;
 }
 

@@ -12,6 +12,7 @@ struct PlanConsts {
   long long GW, GH;
   int S;
   long long B;
+  long long src0, src1;  // events that are sources of the pair sums (fused path), [src0, src1)
 };
 
 // torch's row norm of an (N,2) float32 tensor (vectorised last-dim reduction): sqrt(fma(y, y, x*x)).
