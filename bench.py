@@ -45,6 +45,9 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--events", type=int, default=N_EVENTS)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", default="config2", choices=["config2", "config5"],
+                    help="config2: one 1M-event window per GPU (the headline); config5: one 64M-event window "
+                         "on 1280x720 shared by all GPUs (sources split across ranks, NCCL all-reduce)")
     ap.add_argument("--cpu-worker", default=None, help=argparse.SUPPRESS)
     return ap.parse_args()
 
@@ -383,6 +386,101 @@ def ours_arm(args):
     print(json.dumps(line))
 
 
+# ------------------------------------------------------------------------------------------------ config 5
+def config5_arm(args):
+    """One window of --events (default 64M) events on 1280x720 (times over 200 ms, dense flow as in
+    configuration 2), sources split across the ranks (x_b200.distributed): strong scaling."""
+    import torch
+    import torch.distributed as dist
+    from x_b200 import _lib, synth
+    from x_b200.distributed import ShardedAnchoredExact
+    from x_b200.events import EventPacket
+    from x_b200.motion import DenseLinearFlow
+
+    H5, W5 = 720, 1280
+    n = args.events if args.events != N_EVENTS else 64_000_000
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    ev_cpu = synth.textured_window(n, H5, W5, duration=0.2, seed=5000)   # the same window on every rank
+    flow = synth.lowpass_flow(1, H5, W5, sigma=32.0, vmax=20.0, seed=5001)
+    ev = ev_cpu.to(dev)
+    m = DenseLinearFlow(1, H5, W5, grid=(H5, W5), mode="linear", init=flow).to(dev)
+    obj = ShardedAnchoredExact(h=1.0, tau=1.0, n_anchors=None, n_slices=16, seed=5002, visibility=True)
+    noise = obj.draw(ev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def step():
+        m.grid.grad = None
+        ls, _ = obj.log_scores(ev, m, noise=noise)
+        loss = -ls.mean()
+        loss.backward()
+        return loss
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    L = _lib.load_library()
+    L.atlb_timing_enable(1)
+    for k in ("k_pair_fwd", "k_pair_bwd"):
+        _lib.timing_read(k, reset=True)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    barrier()
+    torch.cuda.synchronize()
+    launches0 = L.atlb_kernel_launches()
+    with ClockSampler(local) as clk:
+        clk.mark()
+        for i in range(args.steps):
+            flush.zero_()
+            starts[i].record()
+            step()
+            ends[i].record()
+        torch.cuda.synchronize()
+        clk.mark(end=True)
+        barrier()
+    launches = L.atlb_kernel_launches() - launches0
+    ktime = {k: _lib.timing_read(k, reset=True) for k in ("k_pair_fwd", "k_pair_bwd")}
+    L.atlb_timing_enable(0)
+    clocks = clk.summary()
+    total = torch.tensor([sum(a.elapsed_time(b) for a, b in zip(starts, ends))], device=dev)
+    if world > 1:
+        dist.all_reduce(total, op=dist.ReduceOp.MAX)
+        dist.destroy_process_group()
+    ms_step = float(total) / args.steps
+    if rank != 0:
+        return
+    dom = max(ktime, key=lambda k: ktime[k][0])
+    dom_ms = ktime[dom][0] / max(ktime[dom][1], 1)
+    ns = n // world
+    alg = {"k_pair_fwd": ns * 16 * 16 + n * 36, "k_pair_bwd": ns * 16 * 24 + n * 20 + ns * 8}[dom]  # 16 slices, tau = 1
+    peak, peak_kind = measured_peak()
+    achieved = alg / (dom_ms / 1000) / 1e9
+    print(json.dumps({
+        "metric": METRIC, "value": n / (ms_step / 1000), "unit": "events/s", "n_gpus": world, "steps": args.steps,
+        "warmup": max(args.warmup, 3), "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"config5a: one {n}-event window on 1280x720, AnchoredExact(h=1, tau=1, all anchors, "
+                               "16 slices, visibility) + DenseLinearFlow(2x720x1280), sources split across ranks",
+                   "events_per_window": n, "windows": 1, "l2": "flushed (256 MB write) before every step",
+                   "parallelism": f"source shards x{world}, NCCL all-reduce of S (M floats) and of the flow grad"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "traffic": None, "kernel": dom, "avg_launch_ms": dom_ms, "algorithmic_bytes": alg,
+                     "peak_source": peak_kind},
+        "kernels_ms_per_step": {k: v[0] / max(v[1], 1) for k, v in ktime.items()},
+        "gpu_launches": int(launches), "clocks": clocks,
+    }))
+
+
 def main():
     args = parse()
     if args.cpu_worker:
@@ -390,6 +488,8 @@ def main():
         return
     if args.impl == "reference":
         reference_arm(args)
+    elif args.workload == "config5":
+        config5_arm(args)
     else:
         ours_arm(args)
 

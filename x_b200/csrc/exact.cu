@@ -374,46 +374,6 @@ struct FusedOut {
   }
 };
 
-// Bucket index -> original anchor index, for the untiled kernel of pair_kernels.cuh.
-struct BucketOut {
-  FusedOut o;
-  const int* idx;
-  __device__ __forceinline__ void operator()(int p, double v) const { o(idx[p], v); }
-};
-
-// Cells of tiles that held more anchors than the tiled kernel stages: one warp per such cell, candidates
-// from global memory (the untiled forward of pair_kernels.cuh, restricted to those cells).
-__global__ void __launch_bounds__(kThreads) k_fwd_overflow(FastEntries E, FastAnchors A, const int* __restrict__ astart,
-                                                           const int* __restrict__ cstart, TileGrid T, CellGrid G,
-                                                           const float* __restrict__ SC, PairConsts C, BucketOut out,
-                                                           const int* __restrict__ overflow) {
-  if (*overflow == 0) return;
-  const int lane = threadIdx.x & 31;
-  const long long nwarps = ((long long)gridDim.x * blockDim.x) >> 5;
-  for (long long c = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5; c < G.ncell; c += nwarps) {
-    const int a0 = astart[c], a1 = astart[c + 1];
-    if (a0 == a1) continue;
-    long long cx, cy, g;
-    cell_coords<int>(c, G, &cx, &cy, &g);
-    // the cell's tile and its anchor count (as the tiled kernel saw it)
-    const int tx0 = (int)(cx >> kTileXLog) << kTileXLog, ty0 = (int)(cy / kTileY) * kTileY;
-    const int tx1 = min(tx0 + kTileX, T.GW), ty1 = min(ty0 + kTileY, T.GH);
-    const long long gbase = g * G.GH * G.GW;
-    int na = 0;
-    for (int y = ty0; y < ty1; ++y) na += astart[gbase + (long long)y * G.GW + tx1] - astart[gbase + (long long)y * G.GW + tx0];
-    if (na <= kTileAncCap) continue;
-    const float cs = __ldg(SC + g % G.S);
-    const long long xlo = cx > 0 ? cx - 1 : 0, xhi = cx + 1 < G.GW ? cx + 1 : G.GW - 1;
-    const long long ylo = cy > 0 ? cy - 1 : 0, yhi = cy + 1 < G.GH ? cy + 1 : G.GH - 1;
-    for (int base = a0; base < a1; base += 4) {
-      const int n = min(4, a1 - base);
-      if (n == 4) fwd_group<4>(E, A, base, cstart, gbase, G.GW, ylo, yhi, xlo, xhi, cs, C, out, lane);
-      else if (n == 3) fwd_group<3>(E, A, base, cstart, gbase, G.GW, ylo, yhi, xlo, xhi, cs, C, out, lane);
-      else if (n == 2) fwd_group<2>(E, A, base, cstart, gbase, G.GW, ylo, yhi, xlo, xhi, cs, C, out, lane);
-      else fwd_group<1>(E, A, base, cstart, gbase, G.GW, ylo, yhi, xlo, xhi, cs, C, out, lane);
-    }
-  }
-}
 
 // dL/dS in bucket order from the upstream dL/dls (torch's LogBackward then DivBackward).
 // The backward's anchor records in bucket order: AB = (x, y, t - c_s, t) and GB = dL/dS / h^2, with
@@ -719,9 +679,14 @@ int exact_forward(const atlb_exact_cfg& c, const float* t, const long long* b, l
       launch(k_pair_fwd_tiled<false, FusedOut>, grid, kTileThreads, smem_all, s, E, A,
              (const int*)w.astart, (const int*)w.start, T, (const float*)w.SC, C, P, (const float4*)ev4, out,
              w.scratch);
+    // cells of tiles with more anchors than the tiled kernel stages (dense windows)
+    if (tau_covers(g, c.tau))
+      launch(k_pair_fwd_overflow<true, FusedOut>, warp_grid(ncell), 256, 0, s, E, A, (const int*)w.astart,
+             (const int*)w.start, T, (const float*)w.SC, C, P, (const float4*)ev4, out, (const int*)w.scratch);
+    else
+      launch(k_pair_fwd_overflow<false, FusedOut>, warp_grid(ncell), 256, 0, s, E, A, (const int*)w.astart,
+             (const int*)w.start, T, (const float*)w.SC, C, P, (const float4*)ev4, out, (const int*)w.scratch);
     timing_end("k_pair_fwd", s, e0);
-    launch(k_fwd_overflow, warp_grid(ncell), kThreads, 0, s, E, A, (const int*)w.astart, (const int*)w.start, T, G,
-           (const float*)w.SC, C, BucketOut{out, w.BI}, (const int*)w.scratch);
   }
   return launch_status("exact_forward");
 }

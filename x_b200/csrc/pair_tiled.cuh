@@ -388,6 +388,108 @@ __global__ void __launch_bounds__(kTileThreads) k_pair_fwd_tiled(FastEntries ent
   }
 }
 
+// ---- forward, untiled (cells the tiled kernel leaves: tiles with more anchors than it stages) -----------
+// One warp per anchor cell: its anchors in register groups of up to 8, the candidates of the 3 neighbouring
+// cell rows streamed from global memory (L1) by the lanes; the same arithmetic as the tiled kernel.
+template <int NA, bool TAU_ALL, class Out>
+__device__ __forceinline__ void fwd_group_cells(const FastEntries& ent, const FastAnchors& anc, int p, const int* lo,
+                                                const int* hi, float cs, const PairConsts& C, const PlanConsts& P,
+                                                const float4* __restrict__ ev4, int b, int s, int cx, int cy,
+                                                Out& out, int lane) {
+  f32x2 axy[NA], adt2[NA];
+  float at[NA], acc[NA];
+  float self_k = 0.f;
+  if (lane < NA) {
+    const float4 a = __ldg(anc.XT + p + lane);
+    self_k = self_term(P, C, ev4, __float_as_int(a.w), a.x, a.y, a.z, sub_rn(a.z, cs), b, s, cx, cy);
+  }
+#pragma unroll
+  for (int q = 0; q < NA; ++q) {
+    const float4 a = __ldg(anc.XT + p + q);
+    const float adt = sub_rn(a.z, cs);
+    axy[q] = pk2(a.x, a.y);
+    adt2[q] = pk2(adt, adt);
+    at[q] = a.z;
+    acc[q] = 0.f;
+  }
+#pragma unroll
+  for (int r = 0; r < 3; ++r) {
+    const int k1 = hi[r];
+    for (int k = lo[r] + lane; k < k1; k += 32) {
+      const float4 e = __ldg(ent.YV + k);
+      const float st = TAU_ALL ? 0.f : __ldg(ent.TI + k).x;
+      const f32x2 y = pk2(e.x, e.y), v = pk2(e.z, e.w);
+#pragma unroll
+      for (int q = 0; q < NA; ++q) {
+        float2 rr;
+        const float d2 = residual2(axy[q], adt2[q], y, v, &rr);
+        bool ok = !(d2 > C.r2max);
+        if (!TAU_ALL) ok = ok && !(fabsf(sub_rn(at[q], st)) > C.tau);
+        const float kv = ex2_approx(-d2 * C.k2);
+        acc[q] += ok ? kv : 0.f;
+      }
+    }
+  }
+#pragma unroll
+  for (int q = 0; q < NA; ++q) {
+    const float sum = warp_sum(acc[q]);
+    const float self_q = __shfl_sync(0xffffffffu, self_k, q);
+    if (lane == 0) out(__ldg(anc.idx + p + q), (double)(sum - self_q));
+  }
+}
+
+// Anchor cells of the tiles with more than kTileAncCap anchors (the tiled kernel set *overflow).
+template <bool TAU_ALL, class Out>
+__global__ void __launch_bounds__(256) k_pair_fwd_overflow(FastEntries ent, FastAnchors anc,
+                                                           const int* __restrict__ astart,
+                                                           const int* __restrict__ cstart, TileGrid G,
+                                                           const float* __restrict__ SC, PairConsts C, PlanConsts P,
+                                                           const float4* __restrict__ ev4, Out out,
+                                                           const int* __restrict__ overflow) {
+  if (*overflow == 0) return;
+  const int lane = threadIdx.x & 31;
+  const long long ncell = (long long)G.B * G.S * G.GH * G.GW;
+  const long long nwarps = ((long long)gridDim.x * blockDim.x) >> 5;
+  for (long long c = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5; c < ncell; c += nwarps) {
+    const int a0 = astart[c], a1 = astart[c + 1];
+    if (a0 == a1) continue;
+    const int GW = G.GW, GH = G.GH;
+    const int row = (int)(c / GW), cx = (int)(c - (long long)row * GW);
+    const int g = row / GH, cy = row - g * GH;
+    const int b = g / G.S, s = g - b * G.S;
+    const int gbase = g * GH * GW;
+    // the cell's tile and its anchor count, as the tiled kernel saw it
+    const int tx0 = (cx >> kTileXLog) << kTileXLog, ty0 = (cy / kTileY) * kTileY;
+    const int tx1 = min(tx0 + kTileX, GW), ty1 = min(ty0 + kTileY, GH);
+    int na = 0;
+    for (int y = ty0; y < ty1; ++y) na += astart[gbase + y * GW + tx1] - astart[gbase + y * GW + tx0];
+    if (na <= kTileAncCap) continue;
+    const int xl = max(cx - 1, 0), xh = min(cx + 1, GW - 1) + 1;
+    int lo[3], hi[3];
+#pragma unroll
+    for (int r = 0; r < 3; ++r) {
+      const int y = cy - 1 + r;
+      int l = 0, h = 0;
+      if (y >= 0 && y < GH) {
+        l = cstart[gbase + y * GW + xl];
+        h = cstart[gbase + y * GW + xh];
+      }
+      lo[r] = l;
+      hi[r] = h;
+    }
+    const float cs = __ldg(SC + s);
+    for (int p = a0; p < a1; p += 8) {
+      switch (min(8, a1 - p)) {
+#define ATLB_OVF(n) \
+  case n: fwd_group_cells<n, TAU_ALL>(ent, anc, p, lo, hi, cs, C, P, ev4, b, s, cx, cy, out, lane); break;
+        ATLB_OVF(8) ATLB_OVF(7) ATLB_OVF(6) ATLB_OVF(5) ATLB_OVF(4) ATLB_OVF(3) ATLB_OVF(2)
+#undef ATLB_OVF
+        default: fwd_group_cells<1, TAU_ALL>(ent, anc, p, lo, hi, cs, C, P, ev4, b, s, cx, cy, out, lane); break;
+      }
+    }
+  }
+}
+
 // ---- backward ----------------------------------------------------------------------------------------
 // One warp per source cell (grid: x = groups of 8 cells of a cell row, y = cell rows of all (batch, slice)
 // grids), lanes over the cell's entries in chunks of 32.  The anchors of the 3 neighbouring cell rows are
