@@ -215,7 +215,7 @@ __global__ void __launch_bounds__(kThreads) k_order_scatter(PlanConsts P, const 
 // (the cell count is checked against the int32 range by the caller).
 __global__ void __launch_bounds__(kThreads) k_fast_count_ordered(PlanConsts P, const float4* __restrict__ XVo,
                                                                  const int4* __restrict__ TBo, long long N,
-                                                                 int* __restrict__ counts) {
+                                                                 int* __restrict__ counts, int* __restrict__ KEY) {
   const int lane = threadIdx.x & 31;
   const long long stride = (long long)gridDim.x * blockDim.x;
   const long long first = blockIdx.x * (long long)blockDim.x + (threadIdx.x & ~31);
@@ -233,6 +233,7 @@ __global__ void __launch_bounds__(kThreads) k_fast_count_ordered(PlanConsts P, c
           float yx, yy;
           key = (int)source_key(P, e.x, e.y, e.z, e.w, tj, tb.y, s, &yx, &yy);
         }
+        KEY[(long long)s * N + i] = key;
       }
       const unsigned grp = __match_any_sync(0xffffffffu, key);
       if (key >= 0 && lane == __ffs(grp) - 1) atomicAdd(counts + key, __popc(grp));
@@ -242,6 +243,7 @@ __global__ void __launch_bounds__(kThreads) k_fast_count_ordered(PlanConsts P, c
 
 __global__ void __launch_bounds__(kThreads) k_fast_scatter_ordered(PlanConsts P, const float4* __restrict__ XVo,
                                                                    const int4* __restrict__ TBo, long long N,
+                                                                   const int* __restrict__ KEY,
                                                                    const int* __restrict__ start,
                                                                    int* __restrict__ cursor, float4* __restrict__ YV,
                                                                    float2* __restrict__ TI) {
@@ -252,31 +254,21 @@ __global__ void __launch_bounds__(kThreads) k_fast_scatter_ordered(PlanConsts P,
   for (int s = blockIdx.y; s < P.S; s += gridDim.y) {
     for (long long i0 = first; i0 < N; i0 += stride) {  // warp-uniform loop
       const long long i = i0 + lane;
-      int key = -1, id = 0;
-      float tj = 0.f;
-      float4 rec = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (i < N) {
-        const int4 tb = TBo[i];
-        tj = __int_as_float(tb.x);
-        id = tb.z;
-        int s_lo, s_hi;
-        slice_range(P, tj, &s_lo, &s_hi);
-        if (s >= s_lo && s <= s_hi) {
-          const float4 e = XVo[i];
-          float yx, yy;
-          key = (int)source_key(P, e.x, e.y, e.z, e.w, tj, tb.y, s, &yx, &yy);
-          rec = make_float4(yx, yy, e.z, e.w);
-        }
-      }
+      const int key = i < N ? KEY[(long long)s * N + i] : -1;  // the count pass's keys
       const unsigned grp = __match_any_sync(0xffffffffu, key);
       const int leader = __ffs(grp) - 1;
       int base = 0;
       if (key >= 0 && lane == leader) base = start[key] + atomicAdd(cursor + key, __popc(grp));
       base = __shfl_sync(0xffffffffu, base, leader);
       if (key >= 0) {
+        const int4 tb = TBo[i];
+        const float tj = __int_as_float(tb.x);
+        const float4 e = XVo[i];
+        float yx, yy;
+        transported(P, e.x, e.y, e.z, e.w, tj, s, &yx, &yy);
         const int p = base + __popc(grp & below);
-        YV[p] = rec;
-        TI[p] = make_float2(tj, __int_as_float(id));
+        YV[p] = make_float4(yx, yy, e.z, e.w);
+        TI[p] = make_float2(tj, __int_as_float(tb.z));
       }
     }
   }
@@ -336,11 +328,24 @@ struct NormConsts {
   int n_check, visibility;
 };
 
+// bstart[k] = first event of batch k (events sorted by b, b in [0, B)), bstart[B] = N.
+__global__ void __launch_bounds__(kThreads) k_batch_bounds(const long long* __restrict__ b, long long N, long long B,
+                                                           long long* __restrict__ bstart) {
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long j = blockIdx.x * (long long)blockDim.x + threadIdx.x; j <= N; j += stride) {
+    const long long lo = j == 0 ? 0 : b[j - 1] + 1, hi = j == N ? B : b[j];
+    for (long long k = lo; k <= hi && k <= B; ++k) bstart[k] = j;
+  }
+}
+
+// Normaliser den = Wn * vis * 2 pi h^2.  bstart != nullptr: tau exceeds the events' time span (with margin)
+// and tau + span < 4, so the window of every anchor is its whole batch and the count is n_b - 1 (the
+// reference's float64 key search gives the same, functional.py:210-217).
 __global__ void __launch_bounds__(kThreads) k_exact_norm(MotionView Mv, NormConsts K, const float4* __restrict__ anc4,
                                                          const long long* __restrict__ anc_b, long long M,
                                                          const float* __restrict__ t, const long long* __restrict__ b,
-                                                         long long N, const int* __restrict__ counts,
-                                                         float* __restrict__ den) {
+                                                         long long N, const long long* __restrict__ bstart,
+                                                         const int* __restrict__ counts, float* __restrict__ den) {
   const long long stride = (long long)gridDim.x * blockDim.x;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < M; i += stride) {
     const float4 a = anc4[i];
@@ -350,8 +355,13 @@ __global__ void __launch_bounds__(kThreads) k_exact_norm(MotionView Mv, NormCons
       den[i] = __int_as_float(0x7fc00000);
       continue;
     }
-    const double ki = ev_key(t, b, ai);
-    const long long c = key_search(t, b, N, ki + K.tau, true) - key_search(t, b, N, ki - K.tau, false) - 1;
+    long long c;
+    if (bstart) {
+      c = bstart[ba + 1] - bstart[ba] - 1;
+    } else {
+      const double ki = ev_key(t, b, ai);
+      c = key_search(t, b, N, ki + K.tau, true) - key_search(t, b, N, ki - K.tau, false) - 1;
+    }
     float wn = (float)(c > 0 ? c : 0);
     wn = wn < 1.f ? 1.f : wn;  // .clamp(min=1)
     if (K.visibility)
@@ -494,6 +504,8 @@ struct ExactWs {
   int* BI;
   int* slice_hist;
   float* SC;
+  long long* bstart;  // first event of each batch (B + 1)
+  int* KEY;      // cell key of each (slice, source event) of the count pass, -1 = no entry
   float4* AB;    // backward anchor records (x, y, t - c_s, t), bucket order
   float* GB;     // dL/dS / h^2, bucket order
   int* ocount;   // events per mid-slice cell (B*GH*GW), then the order cursor
@@ -525,6 +537,8 @@ size_t ws_layout(long long N, long long M, long long ncell, long long S, long lo
   x.BI = (int*)take((size_t)M * 4);
   x.slice_hist = (int*)take((size_t)(B * n_check) * 4);
   x.SC = (float*)take((size_t)S * 4);
+  x.bstart = (long long*)take((size_t)(B + 1) * 8);
+  x.KEY = (int*)take((size_t)nent * 4);
   x.AB = (float4*)take((size_t)M * 16);
   x.GB = (float*)take((size_t)M * 4);
   x.ocount = (int*)take((size_t)nkey * 4);
@@ -620,13 +634,13 @@ int exact_forward(const atlb_exact_cfg& c, const float* t, const long long* b, l
     launch(k_order_scatter, grid_for(ns), kThreads, 0, s, P, ev, t + j0, b + j0, ns, j0, (const int*)w.ostart,
            w.ocount, w.XVo, w.TBo);
     launch(k_fast_count_ordered, slice_grid(ns, P.S), kThreads, 0, s, P, (const float4*)w.XVo, (const int4*)w.TBo,
-           ns, w.counts);
+           ns, w.counts, w.KEY);
   }
   if (M > 0) launch(k_fast_anchor_count, grid_for(M), kThreads, 0, s, P, (const float4*)anc4, anc_b, M, w.acounts);
   exclusive_scan<int>(w.counts, ncell, w.partials, w.start, s);
   if (ns > 0)
     launch(k_fast_scatter_ordered, slice_grid(ns, P.S), kThreads, 0, s, P, (const float4*)w.XVo, (const int4*)w.TBo,
-           ns, (const int*)w.start, w.counts, w.YV, w.TI);
+           ns, (const int*)w.KEY, (const int*)w.start, w.counts, w.YV, w.TI);
   exclusive_scan<int>(w.acounts, ncell, w.partials, w.astart, s);
   if (M > 0)
     launch(k_fast_anchor_scatter, grid_for(M), kThreads, 0, s, P, (const float4*)anc4, anc_b, M,
@@ -646,9 +660,12 @@ int exact_forward(const atlb_exact_cfg& c, const float* t, const long long* b, l
   if (c.visibility && N > 0)
     launch(k_slice_hist, clamp_grid(blocks_for(N, kThreads * 16)), kThreads, 0, s, t, b, N, c.B, (int)c.n_check,
            w.slice_hist);
+  const double span = (double)g.t_hi - (double)g.t_lo;  // NaN (unknown) fails both tests
+  const bool whole_batch = c.tau >= span + 1e-6 && c.tau + span < 4.0 - 1e-6;
+  if (whole_batch) launch(k_batch_bounds, grid_for(N + 1), kThreads, 0, s, b, N, c.B, w.bstart);
   if (M > 0)
     launch(k_exact_norm, grid_for(M), kThreads, 0, s, Mv, K, (const float4*)anc4, anc_b, M, t, b, N,
-           (const int*)w.slice_hist, den_out);
+           whole_batch ? (const long long*)w.bstart : nullptr, (const int*)w.slice_hist, den_out);
   // pair sums + log scores
   const FastEntries E{w.YV, w.TI};
   const FastAnchors A{w.XT, w.BI};

@@ -34,12 +34,19 @@ __device__ __forceinline__ float slice_centre(const PlanConsts& P, int s) {
   return mul_rn(add_rn((float)s, 0.5f), P.delta_f);
 }
 
-// functional.py:158-163: transported position y = x + v (c_s - t) and its cell key (-1 = dropped).
+// functional.py:158: transported position y = x + v (c_s - t) at the centre of slice s.
+__device__ __forceinline__ void transported(const PlanConsts& P, float xj, float yj, float vx, float vy, float tj,
+                                            int s, float* yx, float* yy) {
+  const float dtc = sub_rn(slice_centre(P, s), tj);
+  *yx = add_rn(xj, mul_rn(vx, dtc));
+  *yy = add_rn(yj, mul_rn(vy, dtc));
+}
+
+// functional.py:158-163: transported position and its cell key (-1 = dropped).
 __device__ __forceinline__ long long source_key(const PlanConsts& P, float xj, float yj, float vx, float vy, float tj,
                                                 long long bj, int s, float* yx_out, float* yy_out) {
-  const float dtc = sub_rn(slice_centre(P, s), tj);
-  const float yx = add_rn(xj, mul_rn(vx, dtc));
-  const float yy = add_rn(yj, mul_rn(vy, dtc));
+  float yx, yy;
+  transported(P, xj, yj, vx, vy, tj, s, &yx, &yy);
   *yx_out = yx;
   *yy_out = yy;
   const float qx = floorf(div_rn(sub_rn(yx, P.ox_f), P.cell_f));
