@@ -45,9 +45,11 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--events", type=int, default=N_EVENTS)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="config2", choices=["config2", "config5"],
+    ap.add_argument("--windows", type=int, default=8, help="--workload splat: windows of --events events")
+    ap.add_argument("--workload", default="config2", choices=["config2", "config5", "splat"],
                     help="config2: one 1M-event window per GPU (the headline); config5: one 64M-event window "
-                         "on 1280x720 shared by all GPUs (sources split across ranks, NCCL all-reduce)")
+                         "on 1280x720 shared by all GPUs (sources split across ranks, NCCL all-reduce); splat: the "
+                         "Gaussian splat forward + backward of one slice of configuration 3 (sigma 1.5, 8 x 2M)")
     ap.add_argument("--cpu-worker", default=None, help=argparse.SUPPRESS)
     return ap.parse_args()
 
@@ -481,6 +483,63 @@ def config5_arm(args):
     }))
 
 
+# ------------------------------------------------------------------------------------------------ splat
+def splat_arm(args):
+    """The sliced path's Gaussian splat (configuration 3: --windows windows of --events events on 640x480,
+    sigma = 1.5, R = 5, weight 1), forward + backward of one slice on one GPU: taps/s."""
+    import torch
+    from x_b200 import _lib, get_ext, synth
+    n = args.events if args.events != N_EVENTS else 2_000_000
+    B, sigma = args.windows, 1.5
+    R = int(math.ceil(3 * sigma))
+    ev = synth.textured_window(n, H, W, duration=0.1, seed=3000, batch=B)
+    g = torch.Generator().manual_seed(3001)
+    pos = (ev.xy + (torch.rand(ev.xy.shape, generator=g) - 0.5)).cuda()
+    w = torch.ones(pos.shape[0], device="cuda")
+    b = ev.b.cuda()
+    gimg = torch.randn(B, H, W, generator=g).cuda()
+    ext = get_ext()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+
+    def step():
+        img = ext.splat_gauss_fwd(pos, w, b, B, H, W, sigma, R)
+        gp, gw = ext.splat_gauss_bwd(gimg, pos, w, b, sigma, R)
+        return img, gp, gw
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    L = _lib.load_library()
+    L.atlb_timing_enable(1)
+    for k in ("k_gsplat_fwd", "k_gsplat_bwd"):
+        _lib.timing_read(k, reset=True)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    launches0 = L.atlb_kernel_launches()
+    with ClockSampler(0) as clk:
+        clk.mark()
+        for i in range(args.steps):
+            flush.zero_()
+            starts[i].record()
+            step()
+            ends[i].record()
+        torch.cuda.synchronize()
+        clk.mark(end=True)
+    launches = L.atlb_kernel_launches() - launches0
+    kt = {k: _lib.timing_read(k, reset=True) for k in ("k_gsplat_fwd", "k_gsplat_bwd")}
+    L.atlb_timing_enable(0)
+    ms = sum(a.elapsed_time(e) for a, e in zip(starts, ends)) / args.steps
+    taps = pos.shape[0] * (2 * R + 1) ** 2
+    print(json.dumps({
+        "metric": "Gaussian splat fwd+bwd taps/s (configuration 3, one slice)", "value": taps / (ms / 1000),
+        "unit": "taps/s", "n_gpus": 1, "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"splat: {B} windows x {n} events, 640x480, sigma {sigma}, R {R}", "taps": taps},
+        "kernels_ms_per_step": {k: v[0] / max(v[1], 1) for k, v in kt.items()},
+        "gpu_launches": int(launches), "clocks": clk.summary(),
+    }))
+
+
 def main():
     args = parse()
     if args.cpu_worker:
@@ -490,6 +549,8 @@ def main():
         reference_arm(args)
     elif args.workload == "config5":
         config5_arm(args)
+    elif args.workload == "splat":
+        splat_arm(args)
     else:
         ours_arm(args)
 
