@@ -319,24 +319,45 @@ def ours_arm(args):
     ms_step = total_ms / args.steps
     value = world * args.events / (ms_step / 1000)
 
-    # ---- end to end: pinned host inputs -> device, step, loss read back
+    # ---- end to end: every step's inputs copied from pinned host memory, its loss read back.  The copies
+    # go through a second stream into two device buffers, so step i+1's inputs load while step i computes;
+    # the timed region is the whole job, from the first copy to the last loss read.
     pin = {k: v.pin_memory() for k, v in (("xy", ev_cpu.xy), ("t", ev_cpu.t), ("b", ev_cpu.b),
                                           ("u", u.cpu()), ("z", z.cpu()), ("anchors", anchors.cpu()))}
     h2d = sum(v.numel() * v.element_size() for v in pin.values())
-    e_starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    e_ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    bufs = [{k: torch.empty(v.shape, dtype=v.dtype, device=dev) for k, v in pin.items()} for _ in range(2)]
+    cstream = torch.cuda.Stream(device=dev)
+    copied = [torch.cuda.Event() for _ in range(2)]
+    freed = [torch.cuda.Event() for _ in range(2)]
+
+    def issue_copy(slot):
+        with torch.cuda.stream(cstream):
+            cstream.wait_event(freed[slot])  # the step that last read this buffer is done
+            for k, v in pin.items():
+                bufs[slot][k].copy_(v, non_blocking=True)
+            copied[slot].record(cstream)
+
+    for e in freed:
+        e.record()
     barrier()
     torch.cuda.synchronize()
+    e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e_start.record()
+    cstream.wait_event(e_start)
+    issue_copy(0)
     for i in range(args.steps):
-        flush.zero_()
-        e_starts[i].record()
-        d = {k: v.to(dev, non_blocking=True) for k, v in pin.items()}
+        slot = i % 2
+        torch.cuda.current_stream().wait_event(copied[slot])
+        if i + 1 < args.steps:
+            issue_copy(1 - slot)
+        d = bufs[slot]
         e2 = EventPacket(d["xy"], d["t"], ev.p, d["b"], 1, H, W)
         loss = step(e2, (d["anchors"], d["u"], d["z"]))
+        freed[slot].record()
         float(loss)
-        e_ends[i].record()
+    e_end.record()
     torch.cuda.synchronize()
-    e2e_ms = sum(s.elapsed_time(e) for s, e in zip(e_starts, e_ends)) / args.steps
+    e2e_ms = e_start.elapsed_time(e_end) / args.steps
     t = torch.tensor([e2e_ms], device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -379,7 +400,8 @@ def ours_arm(args):
                      "peak_source": peak_kind, "traffic_source": PROFILE_SUMMARY.name if traffic else None},
         "kernels_ms_per_step": {k: v[0] / max(v[1], 1) for k, v in ktime.items()},
         "e2e": {"value": world * args.events / (e2e_ms / 1000), "unit": "events/s", "ms_per_step": e2e_ms,
-                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4},
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4,
+                "timing": "whole job, first H2D to last loss read; H2D of step i+1 overlaps step i (two buffers)"},
         "gpu_launches": int(launches),
         "clocks": clocks,
     }
