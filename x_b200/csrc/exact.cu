@@ -14,6 +14,8 @@
 // cells are the reference's cells.
 #include <cstddef>
 
+#include <mutex>
+
 #include "common.cuh"
 #include "motion_math.cuh"
 #include "pair_kernels.cuh"
@@ -552,6 +554,19 @@ size_t ws_layout(long long N, long long M, long long ncell, long long S, long lo
 
 int warp_grid(long long nwarps) { return clamp_grid(blocks_for(nwarps * 32, kThreads)); }
 
+// True on the first call for the current device (per flag set): kernel attributes are per device.
+std::mutex g_attr_mu;
+unsigned long long g_fwd_attr = 0;
+bool first_use_on_device(unsigned long long& done) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return true;
+  std::lock_guard<std::mutex> lk(g_attr_mu);
+  const unsigned long long m = 1ULL << dev;
+  if (done & m) return false;
+  done |= m;
+  return true;
+}
+
 // Every pair passes |t_i - t_j| <= tau when tau covers the events' time range: fl(t_i - t_j) never exceeds
 // fl(t_hi - t_lo) (rounding is monotonic).  NaN bounds (unknown range) fail the test.
 // The events that are sources of the pair sums: [src_begin, src_end) of the configuration, all if src_end <= 0.
@@ -675,13 +690,11 @@ int exact_forward(const atlb_exact_cfg& c, const float* t, const long long* b, l
   if (M > 0 && ncell > 0) {
     // the entry times (last member) are only staged when tau does not cover the window
     const size_t smem_all = sizeof(TileSmemFwd), smem_no_t = offsetof(TileSmemFwd, ti);
-    static bool attr = false;
-    if (!attr) {
+    if (first_use_on_device(g_fwd_attr)) {  // the opt-in above 48 KB is a per-device attribute
       cudaFuncSetAttribute(k_pair_fwd_tiled<true, FusedOut>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            (int)smem_no_t);
       cudaFuncSetAttribute(k_pair_fwd_tiled<false, FusedOut>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            (int)smem_all);
-      attr = true;
     }
     const dim3 grid((unsigned)((g.GW + kTileX - 1) / kTileX), (unsigned)((g.GH + kTileY - 1) / kTileY),
                     (unsigned)g.S);
