@@ -46,7 +46,7 @@ def parse():
     ap.add_argument("--events", type=int, default=N_EVENTS)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--windows", type=int, default=8, help="--workload splat: windows of --events events")
-    ap.add_argument("--workload", default="config2", choices=["config2", "config5", "splat"],
+    ap.add_argument("--workload", default="config2", choices=["config2", "config3", "config5", "splat"],
                     help="config2: one 1M-event window per GPU (the headline); config5: one 64M-event window "
                          "on 1280x720 shared by all GPUs (sources split across ranks, NCCL all-reduce); splat: the "
                          "Gaussian splat forward + backward of one slice of configuration 3 (sigma 1.5, 8 x 2M)")
@@ -562,6 +562,64 @@ def splat_arm(args):
     }))
 
 
+# ------------------------------------------------------------------------------------------------ config 3
+def config3_arm(args):
+    """Configuration 3: AnchoredSliced(n_slices=10, sigma=1.5) + Bezier PixelTrajectories (K = 10 control
+    displacements on the 160x120 tile grid, random smooth, |disp| <= 15 px) over --windows windows of --events
+    events on 640x480, forward + backward to the coefficient grid, one GPU."""
+    import torch
+    from x_b200 import _lib, synth
+    from x_b200.motion import PixelTrajectories
+    from x_b200.objectives import AnchoredSliced
+    n = args.events if args.events != N_EVENTS else 2_000_000
+    B, K = args.windows, 10
+    ev = synth.textured_window(n, H, W, duration=0.1, seed=3100, batch=B).to("cuda")
+    g = torch.Generator().manual_seed(3101)
+    raw = torch.nn.functional.avg_pool2d(torch.randn(B, 2 * K, H, W, generator=g), 17, 1, 8)
+    coeff = (raw / raw.abs().amax() * 15.0 / K).cuda().requires_grad_(True)  # sum_k |c_k| g_k <= 15 px
+    m = PixelTrajectories(coeff, K, basis_kind="bezier", tile=4)
+    obj = AnchoredSliced(n_slices=10, sigma=1.5, seed=3102)
+
+    def step():
+        coeff.grad = None
+        ls, _ = obj.log_scores(ev, m)
+        loss = -ls.mean()
+        loss.backward()
+        return loss
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    L = _lib.load_library()
+    L.atlb_timing_enable(1)
+    names = ("k_gsplat_fwd", "k_gsplat_bwd")
+    for k in names:
+        _lib.timing_read(k, reset=True)
+    s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches0 = L.atlb_kernel_launches()
+    with ClockSampler(0) as clk:
+        clk.mark()
+        s_ev.record()
+        for _ in range(args.steps):
+            step()
+        e_ev.record()
+        torch.cuda.synchronize()
+        clk.mark(end=True)
+    launches = L.atlb_kernel_launches() - launches0
+    kt = {k: _lib.timing_read(k, reset=True) for k in names}
+    L.atlb_timing_enable(0)
+    ms = s_ev.elapsed_time(e_ev) / args.steps
+    print(json.dumps({
+        "metric": "anchored-score (sliced) fwd+bwd events/s, configuration 3", "value": B * n / (ms / 1000),
+        "unit": "events/s", "n_gpus": 1, "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"config3: AnchoredSliced(10 slices, sigma 1.5) + PixelTrajectories(K=10 Bezier, tile 4) "
+                               f"on {B} x {n} events, 640x480", "events": B * n},
+        "kernels_ms_per_step": {k: v[0] / args.steps for k, v in kt.items()},
+        "gpu_launches": int(launches), "clocks": clk.summary(),
+    }))
+
+
 def main():
     args = parse()
     if args.cpu_worker:
@@ -573,6 +631,8 @@ def main():
         config5_arm(args)
     elif args.workload == "splat":
         splat_arm(args)
+    elif args.workload == "config3":
+        config3_arm(args)
     else:
         ours_arm(args)
 

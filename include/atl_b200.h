@@ -38,7 +38,7 @@ enum {
 const char* atlb_last_error(void);
 /* ABI version of this header (bumped on incompatible changes). */
 int atlb_abi_version(void);
-#define ATLB_ABI_VERSION 4
+#define ATLB_ABI_VERSION 5
 /* Number of kernels this library has launched in the calling process (instrumentation; no reference
  * counterpart). */
 uint64_t atlb_kernel_launches(void);
@@ -181,6 +181,26 @@ int atlb_visible_fraction(int kind, const float* theta, int64_t B, int64_t Hg, i
                           const float* xa, const float* ta, const int64_t* ba, int64_t M, const float* t,
                           const int64_t* b, int64_t N, double tau, int64_t n_check, float* out, void* scratch,
                           atlb_stream_t stream);
+
+/* ----------------------------------------------------------------------------------------------
+ * Continuous-time pixel trajectories (atl/motion/trajectories.py:40-90), the motion of the sliced
+ * path: transport of events x at times t to t_dst and its backward to the tile coefficients.
+ *   coeff  (B, Hq, Wq, 2K) channels-last tile coefficients, channels [y_1..y_K, x_1..x_K]
+ *   basis  0: g_k(t) = t^k;  1: Bezier, g_k(t) = bezier_c[k] t^k (1 - t)^(K - k)  (bezier_c: K floats,
+ *          exp(lgamma(K+1) - lgamma(k+1) - lgamma(K-k+1)) as the reference computes them in fp32)
+ *   the coefficients at p are the bilinear (border-clamped) sample at (p - offset) / tile; the origin is
+ *   the fixed point of p = x - d(p, t) after n_fp iterations; t_dst (N) per event, or NULL for t_dst_s.
+ * K <= 16 and n_fp <= 16.  Events with b outside [0, B) get NaN.  The backward ADDS dL/dcoeff (same
+ * layout) for gy = dL/dout into gcoeff.
+ * ---------------------------------------------------------------------------------------------- */
+int atlb_traj_transport(const float* coeff, int64_t B, int64_t Hq, int64_t Wq, int64_t K, int basis,
+                        const float* bezier_c, double offset, double tile, int64_t n_fp, const float* xy,
+                        const float* t, const float* t_dst, double t_dst_s, const int64_t* b, int64_t N, float* out,
+                        atlb_stream_t stream);
+int atlb_traj_transport_bwd(const float* gy, const float* coeff, int64_t B, int64_t Hq, int64_t Wq, int64_t K,
+                            int basis, const float* bezier_c, double offset, double tile, int64_t n_fp,
+                            const float* xy, const float* t, const float* t_dst, double t_dst_s, const int64_t* b,
+                            int64_t N, float* gcoeff, atlb_stream_t stream);
 
 /* ----------------------------------------------------------------------------------------------
  * Fused anchored score: AnchoredExact.log_scores (atl/objectives/ats.py:75-96) for the motion kinds

@@ -1,0 +1,41 @@
+"""PixelTrajectories transport on the device (atlb_traj_transport / _bwd) against the torch restatement of
+atl/motion/trajectories.py:40-90 (the same module with the kernels bypassed): positions and the gradient
+w.r.t. the coefficient grid, Bezier and polynomial bases, scalar and per-event target times, border
+clamping of the coefficient samples."""
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _torch_transport(m, xy, t, t_dst, b):
+    from x_b200.motion import as_time
+    p = m.origin(xy, t, b)
+    return p + m.displacement(p, b, as_time(t_dst, t))
+
+
+@pytest.mark.parametrize("K,basis,per_event", [(10, "bezier", False), (3, "polynomial", True), (1, "polynomial", False),
+                                                (4, "bezier", True)])
+def test_traj_transport_matches_torch(K, basis, per_event):
+    from x_b200.motion import PixelTrajectories
+    g = torch.Generator().manual_seed(K * 7 + per_event)
+    B, H, W, n = 2, 48, 64, 20000
+    coeff = (torch.nn.functional.avg_pool2d(torch.randn(B, 2 * K, H, W, generator=g), 9, 1, 4) * 10).cuda()
+    xy = torch.stack([torch.rand(n, generator=g) * (W + 16) - 8, torch.rand(n, generator=g) * (H + 16) - 8], 1).cuda()
+    t = torch.rand(n, generator=g).cuda()
+    b = torch.randint(0, B, (n,), generator=g).cuda()
+    t_dst = torch.rand(n, generator=g).cuda() if per_event else 0.375
+    w = torch.randn(n, 2, generator=g).cuda()
+    c1 = coeff.clone().requires_grad_(True)
+    m1 = PixelTrajectories(c1, K, basis_kind=basis, tile=4)
+    assert m1._device_transport(xy, t)
+    y1 = m1.transport(xy, t, t_dst, b)
+    (y1 * w).sum().backward()
+    c2 = coeff.clone().requires_grad_(True)
+    m2 = PixelTrajectories(c2, K, basis_kind=basis, tile=4)
+    y2 = _torch_transport(m2, xy, t, t_dst, b)
+    (y2 * w).sum().backward()
+    np.testing.assert_allclose(y1.detach().cpu().numpy(), y2.detach().cpu().numpy(), rtol=0, atol=2e-4)
+    g1, g2 = c1.grad.cpu().numpy(), c2.grad.cpu().numpy()
+    np.testing.assert_allclose(g1, g2, rtol=1e-3, atol=1e-4 * np.abs(g2).max())

@@ -6,6 +6,7 @@
 #include "common.cuh"
 #include "motion_math.cuh"
 #include "plan_math.cuh"
+#include "traj.cuh"
 
 namespace atlb {
 
@@ -70,6 +71,11 @@ int window_counts(const float*, const long long*, long long, const long long*, l
                   cudaStream_t);
 int window_counts_keys(const double*, long long, const float*, const long long*, const long long*, long long, double,
                        float*, cudaStream_t);
+
+int traj_transport(const TrajView&, const float*, const float*, const float*, float, const long long*, long long,
+                   float*, cudaStream_t);
+int traj_transport_bwd(const TrajView&, const float*, const float*, const float*, const float*, float,
+                       const long long*, long long, float*, cudaStream_t);
 
 size_t exact_workspace_bytes(const atlb_exact_cfg&, long long, long long, const atlb_plan_geom&);
 int exact_prepare(const atlb_exact_cfg&, const float*, const float*, const float*, const long long*, long long,
@@ -466,3 +472,49 @@ int atlb_exact_backward(const atlb_exact_cfg* cfg, const float* grad_ls, const i
 }
 
 }  // extern "C"
+
+static int make_traj(const float* coeff, int64_t B, int64_t Hq, int64_t Wq, int64_t K, int basis, const float* bc,
+                     double offset, double tile, int64_t n_fp, TrajView* V, const char* fn) {
+  if (!coeff || B < 1 || Hq < 1 || Wq < 1 || K < 1 || K > kTrajKMax || n_fp < 0 || n_fp > kTrajKMax ||
+      !(tile > 0) || (basis != 0 && basis != 1) || (basis == 1 && !bc) || B * Hq * Wq * 2 * K > (1LL << 40)) {
+    set_error("%s: invalid trajectory grid (B %lld, %lld x %lld, K %lld, basis %d, n_fp %lld, tile %g)", fn,
+              (long long)B, (long long)Hq, (long long)Wq, (long long)K, basis, (long long)n_fp, tile);
+    return ATLB_ERR_ARG;
+  }
+  V->C = coeff;
+  V->B = (int)B;
+  V->Hq = (int)Hq;
+  V->Wq = (int)Wq;
+  V->K = (int)K;
+  V->n_fp = (int)n_fp;
+  V->basis = basis;
+  V->offset = (float)offset;
+  V->tile = (float)tile;
+  for (int k = 0; k < kTrajKMax; ++k) V->bc[k] = (basis == 1 && k < K) ? bc[k] : 0.f;
+  return ATLB_OK;
+}
+
+int atlb_traj_transport(const float* coeff, int64_t B, int64_t Hq, int64_t Wq, int64_t K, int basis,
+                        const float* bezier_c, double offset, double tile, int64_t n_fp, const float* xy,
+                        const float* t, const float* t_dst, double t_dst_s, const int64_t* b, int64_t N, float* out,
+                        atlb_stream_t stream) {
+  clear();
+  NONNEG(N);
+  NEED(xy, N); NEED(t, N); NEED(b, N); NEED(out, N);
+  TrajView V;
+  if (int st = make_traj(coeff, B, Hq, Wq, K, basis, bezier_c, offset, tile, n_fp, &V, __func__)) return st;
+  return traj_transport(V, xy, t, t_dst, (float)t_dst_s, LL(b), N, out, STREAM(stream));
+}
+
+int atlb_traj_transport_bwd(const float* gy, const float* coeff, int64_t B, int64_t Hq, int64_t Wq, int64_t K,
+                            int basis, const float* bezier_c, double offset, double tile, int64_t n_fp,
+                            const float* xy, const float* t, const float* t_dst, double t_dst_s, const int64_t* b,
+                            int64_t N, float* gcoeff, atlb_stream_t stream) {
+  clear();
+  NONNEG(N);
+  NEED(gy, N); NEED(xy, N); NEED(t, N); NEED(b, N);
+  if (!gcoeff) { set_error("%s: gcoeff is NULL", __func__); return ATLB_ERR_ARG; }
+  TrajView V;
+  if (int st = make_traj(coeff, B, Hq, Wq, K, basis, bezier_c, offset, tile, n_fp, &V, __func__)) return st;
+  return traj_transport_bwd(V, gy, xy, t, t_dst, (float)t_dst_s, LL(b), N, gcoeff, STREAM(stream));
+}

@@ -226,6 +226,42 @@ def basis(t: torch.Tensor, K: int, kind: str = "polynomial") -> torch.Tensor:
     raise ValueError(kind)
 
 
+class _TrajTransport(torch.autograd.Function):
+    """PixelTrajectories.transport on the device (atlb_traj_transport): differentiable w.r.t. the tile
+    coefficients; the event positions and times are data (no gradient)."""
+
+    @staticmethod
+    def forward(ctx, tile_c, xy, t, t_dst, b, model):
+        C = tile_c.detach().float().permute(0, 2, 3, 1).contiguous()
+        xyc, tc, bc = xy.detach().float().contiguous(), t.detach().float().contiguous(), b.contiguous().long()
+        if torch.is_tensor(t_dst) and t_dst.dim() > 0:
+            tdc, tds = t_dst.detach().float().contiguous(), 0.0
+        else:
+            tdc, tds = None, float(t_dst)
+        out = torch.empty_like(xyc)
+        B, Hq, Wq, C2 = C.shape
+        L.check(L.lib().atlb_traj_transport(L.ptr(C), B, Hq, Wq, C2 // 2, model._basis_id, L.ptr(model._bc),
+                                            model.offset, float(model.tile), model.n_fp, L.ptr(xyc), L.ptr(tc),
+                                            L.ptr(tdc), tds, L.ptr(bc), xyc.shape[0], L.ptr(out), L.stream()),
+                "traj_transport")
+        ctx.save_for_backward(C, xyc, tc, bc, *(() if tdc is None else (tdc,)))
+        ctx.tds, ctx.model = tds, model
+        return out
+
+    @staticmethod
+    def backward(ctx, gy):
+        C, xyc, tc, bc, *rest = ctx.saved_tensors
+        tdc = rest[0] if rest else None
+        m = ctx.model
+        gC = torch.zeros_like(C)
+        B, Hq, Wq, C2 = C.shape
+        L.check(L.lib().atlb_traj_transport_bwd(L.ptr(gy.contiguous().float()), L.ptr(C), B, Hq, Wq, C2 // 2,
+                                                m._basis_id, L.ptr(m._bc), m.offset, float(m.tile), m.n_fp,
+                                                L.ptr(xyc), L.ptr(tc), L.ptr(tdc), ctx.tds, L.ptr(bc), xyc.shape[0],
+                                                L.ptr(gC), L.stream()), "traj_transport_bwd")
+        return gC.permute(0, 3, 1, 2), None, None, None, None, None
+
+
 class PixelTrajectories(Motion):
     """One continuous-time trajectory per ``tile`` x ``tile`` patch, coefficients from a (B, 2K, H, W) grid
     (atl/motion/trajectories.py:40-120): q(p, t) = p + sum_k c_k(p) g_k(t), channels [y_1..y_K, x_1..x_K].
@@ -244,6 +280,10 @@ class PixelTrajectories(Motion):
         self.Hq, self.Wq = self.tile_c.shape[-2:]
         self.offset = float(s)
         self.linear_at_event = (K == 1 and basis_kind == "polynomial")
+        # Bezier binomial factors as the reference evaluates them (fp32 torch on the host), for the kernels
+        k = torch.arange(1, K + 1, dtype=torch.float32)
+        self._bc = torch.exp(math.lgamma(K + 1) - torch.lgamma(k + 1) - torch.lgamma(K - k + 1)).contiguous()
+        self._basis_id = {"polynomial": 0, "bezier": 1}.get(basis_kind, -1)
 
     def _coeff_at(self, p, b):
         g = (p - self.offset) / self.tile
@@ -262,8 +302,15 @@ class PixelTrajectories(Motion):
         return p
 
     def transport(self, xy, t, t_dst, b):
+        if self._device_transport(xy, t):
+            return _TrajTransport.apply(self.tile_c, xy, t, t_dst, b, self)
         p = self.origin(xy, t, b)
         return p + self.displacement(p, b, as_time(t_dst, t))
+
+    def _device_transport(self, xy, t) -> bool:
+        """The kernels cover the invert assignment, K <= 16 and n_fp <= 16, for positions without gradient."""
+        return (self.tile_c.is_cuda and xy.is_cuda and self.assign == "invert" and self._basis_id >= 0
+                and self.K <= 16 and self.n_fp <= 16 and not xy.requires_grad and not t.requires_grad)
 
     def velocity(self, xy, t, b):
         if not self.linear_at_event:
