@@ -6,10 +6,15 @@
 //   transport(x, t -> t'):  p_0 = x,  p_{i+1} = x - d(p_i, t)  (n_fp times),  y = p_n + d(p_n, t')
 //
 // The coefficients are read channels-last (B, Hq, Wq, 2K) with channels [y_1..y_K, x_1..x_K], so one tap of
-// a sample is 2K consecutive floats.  The backward recomputes the iterates and runs reverse mode through
-// them: dL/dp_i = -J_d(p_i)^T dL/dp_{i+1}, and every sample scatters w_tap * g_k(t) * dL/dp into the four
-// taps of its coefficient cell (red.global).  The rounding sequence follows the reference's torch ops
-// (p - offset, / tile, clamp, floor, weights, products summed in tap order, then over k).
+// a sample is 2K consecutive floats (16-byte vector loads when 2K is a multiple of 4).  The kernels are
+// instantiated per K (1..16) so that the per-event basis and channel sums live in registers.  Sums follow
+// the reference's order (taps in order, then over k); the basis powers are products (t^k by repeated
+// multiplication instead of pow), so values differ from the reference's in the last bits.
+// The backward recomputes the iterates and runs reverse mode through them: dL/dp_i = -J_d(p_i)^T dL/dp_{i+1}.
+// The coefficient gradient w_tap * g_k(t) * dL/dp of the samples of one coefficient cell is accumulated per
+// tap (the iterates of one event rarely leave their cell) and leaves with vector reds when the cell changes.
+#include <type_traits>
+
 #include "common.cuh"
 #include "traj.cuh"
 
@@ -19,10 +24,18 @@ namespace {
 constexpr int kTThreads = 256;
 
 // g_k(t) - g_k(0), k = 1..K (trajectories.py:26-37): t^k, or (c_k t^k) (1 - t)^(K - k).
-__device__ __forceinline__ void traj_basis(const TrajView& V, float t, float* g) {
-  for (int k = 0; k < V.K; ++k) {
-    const float tk = powf(t, (float)(k + 1));
-    g[k] = V.basis == 0 ? tk : mul_rn(mul_rn(V.bc[k], tk), powf(sub_rn(1.f, t), (float)(V.K - k - 1)));
+template <int K>
+__device__ __forceinline__ void traj_basis(const TrajView& V, float t, float (&g)[K]) {
+  float om[K];  // (1 - t)^j, j = 0..K-1
+  const float u = sub_rn(1.f, t);
+  om[0] = 1.f;
+#pragma unroll
+  for (int j = 1; j < K; ++j) om[j] = om[j - 1] * u;
+  float tk = t;
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    g[k] = V.basis == 0 ? tk : (V.bc[k] * tk) * om[K - 1 - k];
+    tk *= t;
   }
 }
 
@@ -57,22 +70,47 @@ __device__ __forceinline__ Taps traj_taps(const TrajView& V, int b, float px, fl
   return T;
 }
 
-// displacement d(p, t) = sum_k (cx_k, cy_k) g_k with c the bilinear sample at p
-__device__ __forceinline__ float2 traj_disp(const TrajView& V, const Taps& T, const float* g) {
-  float dx = 0.f, dy = 0.f;
-  for (int k = 0; k < V.K; ++k) {
-    float cy = 0.f, cx = 0.f;
+// The 2K channels of one tap into registers.
+template <int K>
+__device__ __forceinline__ void load_tap(const float* __restrict__ p, float (&f)[2 * K]) {
+  if constexpr ((2 * K) % 4 == 0) {
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      cy = add_rn(cy, mul_rn(__ldg(V.C + T.base[q] + k), T.w[q]));
-      cx = add_rn(cx, mul_rn(__ldg(V.C + T.base[q] + V.K + k), T.w[q]));
+    for (int c = 0; c < 2 * K; c += 4) {
+      const float4 v = __ldg(reinterpret_cast<const float4*>(p + c));
+      f[c] = v.x; f[c + 1] = v.y; f[c + 2] = v.z; f[c + 3] = v.w;
     }
-    dx = add_rn(dx, mul_rn(cx, g[k]));
-    dy = add_rn(dy, mul_rn(cy, g[k]));
+  } else {
+#pragma unroll
+    for (int c = 0; c < 2 * K; c += 2) {
+      const float2 v = __ldg(reinterpret_cast<const float2*>(p + c));
+      f[c] = v.x; f[c + 1] = v.y;
+    }
+  }
+}
+
+// displacement d(p, t) = sum_k (cx_k, cy_k) g_k with c the bilinear sample at p (taps summed in order)
+template <int K>
+__device__ __forceinline__ float2 traj_disp(const TrajView& V, const Taps& T, const float (&g)[K]) {
+  float c[2 * K];
+#pragma unroll
+  for (int ch = 0; ch < 2 * K; ++ch) c[ch] = 0.f;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    float f[2 * K];
+    load_tap<K>(V.C + T.base[q], f);
+#pragma unroll
+    for (int ch = 0; ch < 2 * K; ++ch) c[ch] = add_rn(c[ch], mul_rn(f[ch], T.w[q]));
+  }
+  float dx = 0.f, dy = 0.f;
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    dx = add_rn(dx, mul_rn(c[K + k], g[k]));
+    dy = add_rn(dy, mul_rn(c[k], g[k]));
   }
   return make_float2(dx, dy);
 }
 
+template <int K>
 __global__ void __launch_bounds__(kTThreads) k_traj_fwd(TrajView V, const float2* __restrict__ xy,
                                                         const float* __restrict__ t, const float* __restrict__ tdst,
                                                         float tdst_s, const long long* __restrict__ b, long long N,
@@ -85,51 +123,101 @@ __global__ void __launch_bounds__(kTThreads) k_traj_fwd(TrajView V, const float2
       continue;
     }
     const int bb = (int)b[n];
-    float g[kTrajKMax];
-    traj_basis(V, t[n], g);
+    float g[K];
+    traj_basis<K>(V, t[n], g);
     float px = x.x, py = x.y;
     for (int i = 0; i < V.n_fp; ++i) {
-      const float2 d = traj_disp(V, traj_taps(V, bb, px, py), g);
+      const float2 d = traj_disp<K>(V, traj_taps(V, bb, px, py), g);
       px = sub_rn(x.x, d.x);
       py = sub_rn(x.y, d.y);
     }
-    traj_basis(V, tdst ? tdst[n] : tdst_s, g);
-    const float2 d = traj_disp(V, traj_taps(V, bb, px, py), g);
+    traj_basis<K>(V, tdst ? tdst[n] : tdst_s, g);
+    const float2 d = traj_disp<K>(V, traj_taps(V, bb, px, py), g);
     out[n] = make_float2(add_rn(px, d.x), add_rn(py, d.y));
   }
 }
 
-// Reverse step through one sample of d at p (basis g, incoming dL/dd = (ux, uy)): scatters the coefficient
-// gradient and returns J_d(p)^T (ux, uy).
-__device__ __forceinline__ float2 traj_disp_bwd(const TrajView& V, const Taps& T, const float* g, float ux, float uy,
-                                                float* __restrict__ gC) {
-  // d(sample)/d(ax), d(sample)/d(ay) per channel, from the weights' derivatives
+// J_d(p)^T (ux, uy) for one sample of d at p with basis g (the transposed bilinear Jacobian; the clamp passes
+// gradient inside its range, floor none).
+template <int K>
+__device__ __forceinline__ float2 traj_jt(const TrajView& V, const Taps& T, const float (&g)[K], float ux,
+                                          float uy) {
+  float f[4][2 * K];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) load_tap<K>(V.C + T.base[q], f[q]);
   float jxx = 0.f, jxy = 0.f, jyx = 0.f, jyy = 0.f;  // J = [[d dx/d px, d dx/d py], [d dy/d px, d dy/d py]]
   const float oax = 1.f - T.ax, oay = 1.f - T.ay;
-  for (int k = 0; k < V.K; ++k) {
-    float f[4][2];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      f[q][0] = __ldg(V.C + T.base[q] + V.K + k);  // x channel
-      f[q][1] = __ldg(V.C + T.base[q] + k);        // y channel
-    }
-#pragma unroll
-    for (int c = 0; c < 2; ++c) {
-      const float dax = (f[1][c] - f[0][c]) * oay + (f[3][c] - f[2][c]) * T.ay;
-      const float day = (f[2][c] - f[0][c]) * oax + (f[3][c] - f[1][c]) * T.ax;
-      if (c == 0) { jxx += g[k] * dax; jxy += g[k] * day; } else { jyx += g[k] * dax; jyy += g[k] * day; }
-    }
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const float wg = T.w[q] * g[k];
-      if (uy != 0.f) red_add_f1(gC + T.base[q] + k, wg * uy);
-      if (ux != 0.f) red_add_f1(gC + T.base[q] + V.K + k, wg * ux);
-    }
+  for (int k = 0; k < K; ++k) {
+    const int X = K + k;
+    jxx += g[k] * ((f[1][X] - f[0][X]) * oay + (f[3][X] - f[2][X]) * T.ay);
+    jxy += g[k] * ((f[2][X] - f[0][X]) * oax + (f[3][X] - f[1][X]) * T.ax);
+    jyx += g[k] * ((f[1][k] - f[0][k]) * oay + (f[3][k] - f[2][k]) * T.ay);
+    jyy += g[k] * ((f[2][k] - f[0][k]) * oax + (f[3][k] - f[1][k]) * T.ax);
   }
   const float sx = T.gx_in ? 1.f / V.tile : 0.f, sy = T.gy_in ? 1.f / V.tile : 0.f;
   return make_float2((jxx * ux + jyx * uy) * sx, (jxy * ux + jyy * uy) * sy);
 }
 
+// Coefficient gradient of the samples that fall in one coefficient cell.  For samples with basis g the
+// gradient of (tap q, channel k) is g_k * sum_i w_q(p_i) u_i, so per cell only the per-tap sums
+// a_q = sum_i w_q u_i (basis of the origin iterations) and f_q (basis of the final sample) are kept; they are
+// flushed as g_k a_q + gd_k f_q into the 2K channels of each tap (vector reds) when the cell changes.
+struct CellAcc {
+  long long base[4];
+  float a[4][2], f[4][2];  // [tap][x, y]
+  bool live;
+};
+
+template <int K>
+__device__ __forceinline__ void acc_flush(CellAcc& A, const float (&g)[K], const float (&gd)[K],
+                                          float* __restrict__ gC) {
+  if (!A.live) return;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    float v[2 * K];
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      v[k] = g[k] * A.a[q][1] + gd[k] * A.f[q][1];
+      v[K + k] = g[k] * A.a[q][0] + gd[k] * A.f[q][0];
+    }
+    float* dst = gC + A.base[q];
+    if constexpr ((2 * K) % 4 == 0) {
+#pragma unroll
+      for (int c = 0; c < 2 * K; c += 4) red_add_f4(dst + c, v[c], v[c + 1], v[c + 2], v[c + 3]);
+    } else {
+#pragma unroll
+      for (int c = 0; c < 2 * K; c += 2) red_add_f2(dst + c, v[c], v[c + 1]);
+    }
+  }
+  A.live = false;
+}
+
+template <int K>
+__device__ __forceinline__ void acc_add(CellAcc& A, const Taps& T, bool final_basis, float ux, float uy,
+                                        const float (&g)[K], const float (&gd)[K], float* __restrict__ gC) {
+  if (A.live && A.base[0] != T.base[0]) acc_flush<K>(A, g, gd, gC);
+  if (!A.live) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      A.base[q] = T.base[q];
+      A.a[q][0] = A.a[q][1] = A.f[q][0] = A.f[q][1] = 0.f;
+    }
+    A.live = true;
+  }
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    if (final_basis) {
+      A.f[q][0] += T.w[q] * ux;
+      A.f[q][1] += T.w[q] * uy;
+    } else {
+      A.a[q][0] += T.w[q] * ux;
+      A.a[q][1] += T.w[q] * uy;
+    }
+  }
+}
+
+template <int K>
 __global__ void __launch_bounds__(kTThreads) k_traj_bwd(TrajView V, const float2* __restrict__ gy,
                                                         const float2* __restrict__ xy, const float* __restrict__ t,
                                                         const float* __restrict__ tdst, float tdst_s,
@@ -141,45 +229,76 @@ __global__ void __launch_bounds__(kTThreads) k_traj_bwd(TrajView V, const float2
     if ((u.x == 0.f && u.y == 0.f) || b[n] < 0 || b[n] >= V.B) continue;
     const float2 x = xy[n];
     const int bb = (int)b[n];
-    float g[kTrajKMax], gd[kTrajKMax];
-    traj_basis(V, t[n], g);
-    traj_basis(V, tdst ? tdst[n] : tdst_s, gd);
-    float P[kTrajKMax + 1][2];  // iterates p_0 .. p_n (n_fp <= kTrajKMax)
+    float g[K], gd[K];
+    traj_basis<K>(V, t[n], g);
+    traj_basis<K>(V, tdst ? tdst[n] : tdst_s, gd);
+    float P[kTrajKMax + 1][2];  // iterates p_0 .. p_n (n_fp <= kTrajKMax), as the forward computes them
     P[0][0] = x.x;
     P[0][1] = x.y;
     for (int i = 0; i < V.n_fp; ++i) {
-      const float2 d = traj_disp(V, traj_taps(V, bb, P[i][0], P[i][1]), g);
+      const float2 d = traj_disp<K>(V, traj_taps(V, bb, P[i][0], P[i][1]), g);
       P[i + 1][0] = sub_rn(x.x, d.x);
       P[i + 1][1] = sub_rn(x.y, d.y);
     }
+    CellAcc A;
+    A.live = false;
     // y = p_n + d(p_n, t')
-    const float2 jt = traj_disp_bwd(V, traj_taps(V, bb, P[V.n_fp][0], P[V.n_fp][1]), gd, u.x, u.y, gC);
+    Taps T = traj_taps(V, bb, P[V.n_fp][0], P[V.n_fp][1]);
+    acc_add<K>(A, T, true, u.x, u.y, g, gd, gC);
+    const float2 jt = traj_jt<K>(V, T, gd, u.x, u.y);
     float gpx = u.x + jt.x, gpy = u.y + jt.y;
     // p_{i+1} = x - d(p_i, t)
     for (int i = V.n_fp - 1; i >= 0; --i) {
-      const float2 j = traj_disp_bwd(V, traj_taps(V, bb, P[i][0], P[i][1]), g, -gpx, -gpy, gC);
+      T = traj_taps(V, bb, P[i][0], P[i][1]);
+      acc_add<K>(A, T, false, -gpx, -gpy, g, gd, gC);
+      const float2 j = traj_jt<K>(V, T, g, -gpx, -gpy);
       gpx = j.x;
       gpy = j.y;
     }
+    acc_flush<K>(A, g, gd, gC);
   }
 }
 
 inline int tgrid(long long n) { return clamp_grid(blocks_for(n, kTThreads)); }
 
+template <typename F>
+void dispatch_k(int K, F&& f) {
+  switch (K) {
+#define ATLB_K(k) \
+  case k: f(std::integral_constant<int, k>{}); break;
+    ATLB_K(1) ATLB_K(2) ATLB_K(3) ATLB_K(4) ATLB_K(5) ATLB_K(6) ATLB_K(7) ATLB_K(8)
+    ATLB_K(9) ATLB_K(10) ATLB_K(11) ATLB_K(12) ATLB_K(13) ATLB_K(14) ATLB_K(15) ATLB_K(16)
+#undef ATLB_K
+    default: break;
+  }
+}
+
 }  // namespace
 
 int traj_transport(const TrajView& V, const float* xy, const float* t, const float* tdst, float tdst_s,
                    const long long* b, long long N, float* out, cudaStream_t s) {
-  if (N > 0)
-    launch(k_traj_fwd, tgrid(N), kTThreads, 0, s, V, (const float2*)xy, t, tdst, tdst_s, b, N, (float2*)out);
+  if (N > 0) {
+    cudaEvent_t e0 = timing_begin(s);
+    dispatch_k(V.K, [&](auto kc) {
+      constexpr int K = decltype(kc)::value;
+      launch(k_traj_fwd<K>, tgrid(N), kTThreads, 0, s, V, (const float2*)xy, t, tdst, tdst_s, b, N, (float2*)out);
+    });
+    timing_end("k_traj_fwd", s, e0);
+  }
   return launch_status("traj_transport");
 }
 
 int traj_transport_bwd(const TrajView& V, const float* gy, const float* xy, const float* t, const float* tdst,
                        float tdst_s, const long long* b, long long N, float* gC, cudaStream_t s) {
-  if (N > 0)
-    launch(k_traj_bwd, tgrid(N), kTThreads, 0, s, V, (const float2*)gy, (const float2*)xy, t, tdst, tdst_s, b, N,
-           gC);
+  if (N > 0) {
+    cudaEvent_t e0 = timing_begin(s);
+    dispatch_k(V.K, [&](auto kc) {
+      constexpr int K = decltype(kc)::value;
+      launch(k_traj_bwd<K>, tgrid(N), kTThreads, 0, s, V, (const float2*)gy, (const float2*)xy, t, tdst, tdst_s, b,
+             N, gC);
+    });
+    timing_end("k_traj_bwd", s, e0);
+  }
   return launch_status("traj_transport_bwd");
 }
 
