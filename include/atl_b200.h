@@ -197,6 +197,14 @@ int atlb_traj_transport(const float* coeff, int64_t B, int64_t Hq, int64_t Wq, i
                         const float* bezier_c, double offset, double tile, int64_t n_fp, const float* xy,
                         const float* t, const float* t_dst, double t_dst_s, const int64_t* b, int64_t N, float* out,
                         atlb_stream_t stream);
+/* Exposure correction (atl/objectives/ats.py:31-50) of M anchors (xa, ta, ba) under these trajectories:
+ * counts (B, n_check) per-batch event counts of the n_check time slices, centres (n_check) the slice
+ * centres (device arrays), sensor W x H; out (M).  The trajectory's origin is solved once per anchor. */
+int atlb_traj_visible_fraction(const float* coeff, int64_t B, int64_t Hq, int64_t Wq, int64_t K, int basis,
+                               const float* bezier_c, double offset, double tile, int64_t n_fp, const float* xa,
+                               const float* ta, const int64_t* ba, int64_t M, const float* counts,
+                               const float* centres, int64_t n_check, double tau, int64_t H, int64_t W, float* out,
+                               atlb_stream_t stream);
 int atlb_traj_transport_bwd(const float* gy, const float* coeff, int64_t B, int64_t Hq, int64_t Wq, int64_t K,
                             int basis, const float* bezier_c, double offset, double tile, int64_t n_fp,
                             const float* xy, const float* t, const float* t_dst, double t_dst_s, const int64_t* b,

@@ -39,3 +39,25 @@ def test_traj_transport_matches_torch(K, basis, per_event):
     np.testing.assert_allclose(y1.detach().cpu().numpy(), y2.detach().cpu().numpy(), rtol=0, atol=2e-4)
     g1, g2 = c1.grad.cpu().numpy(), c2.grad.cpu().numpy()
     np.testing.assert_allclose(g1, g2, rtol=1e-3, atol=1e-4 * np.abs(g2).max())
+
+
+def test_traj_visible_fraction_matches_torch():
+    """The fused exposure correction (origin solved once per anchor) against the torch loop of
+    atl/objectives/ats.py:31-50 over the same trajectories.  The inside test on positions that differ in the
+    last bits can flip for an anchor exactly on the image border, so a tiny share may differ."""
+    from x_b200 import synth
+    from x_b200.motion import PixelTrajectories
+    from x_b200.objectives import visible_fraction
+    g = torch.Generator().manual_seed(99)
+    B, H, W, K = 2, 48, 64, 10
+    ev = synth.textured_window(20000, H, W, duration=0.1, seed=98, batch=B).to("cuda")
+    coeff = (torch.nn.functional.avg_pool2d(torch.randn(B, 2 * K, H, W, generator=g), 9, 1, 4) * 4).cuda()
+    m1 = PixelTrajectories(coeff, K, basis_kind="bezier", tile=4)
+    m2 = PixelTrajectories(coeff, K, basis_kind="bezier", tile=4)
+    m2._device_transport = lambda xy, t: False  # the torch transport
+    xa = ev.xy + torch.randn(ev.xy.shape, generator=g).cuda()
+    for tau in (1.0, 0.3):
+        v1 = visible_fraction(m1, xa, ev.t, ev.b, ev, tau).cpu().numpy()
+        v2 = visible_fraction(m2, xa, ev.t, ev.b, ev, tau).cpu().numpy()
+        close = np.isclose(v1, v2, rtol=1e-6, atol=1e-7)
+        assert close.mean() > 0.999

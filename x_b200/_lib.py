@@ -74,6 +74,8 @@ _SIGS = {
                                    _vp, _i64, _vp, _vp]),
     "atlb_traj_transport_bwd": (_int, [_vp, _vp, _i64, _i64, _i64, _i64, _int, _vp, _dbl, _dbl, _i64, _vp, _vp, _vp,
                                        _dbl, _vp, _i64, _vp, _vp]),
+    "atlb_traj_visible_fraction": (_int, [_vp, _i64, _i64, _i64, _i64, _int, _vp, _dbl, _dbl, _i64, _vp, _vp, _vp,
+                                          _i64, _vp, _vp, _i64, _dbl, _i64, _i64, _vp, _vp]),
     "atlb_exact_prepare": (_int, [ctypes.POINTER(ExactCfg), _vp, _vp, _vp, _vp, _i64, _vp, _vp, _i64, _vp, _vp, _vp,
                                   _vp, ctypes.POINTER(PlanGeom), _vp]),
     "atlb_exact_workspace_bytes": (_size, [ctypes.POINTER(ExactCfg), _i64, _i64, ctypes.POINTER(PlanGeom)]),

@@ -76,6 +76,8 @@ int traj_transport(const TrajView&, const float*, const float*, const float*, fl
                    float*, cudaStream_t);
 int traj_transport_bwd(const TrajView&, const float*, const float*, const float*, const float*, float,
                        const long long*, long long, float*, cudaStream_t);
+int traj_visible_fraction(const TrajView&, const float*, const float*, const long long*, long long, const float*,
+                          const float*, int, float, float, float, float*, cudaStream_t);
 
 size_t exact_workspace_bytes(const atlb_exact_cfg&, long long, long long, const atlb_plan_geom&);
 int exact_prepare(const atlb_exact_cfg&, const float*, const float*, const float*, const long long*, long long,
@@ -517,4 +519,23 @@ int atlb_traj_transport_bwd(const float* gy, const float* coeff, int64_t B, int6
   TrajView V;
   if (int st = make_traj(coeff, B, Hq, Wq, K, basis, bezier_c, offset, tile, n_fp, &V, __func__)) return st;
   return traj_transport_bwd(V, gy, xy, t, t_dst, (float)t_dst_s, LL(b), N, gcoeff, STREAM(stream));
+}
+
+int atlb_traj_visible_fraction(const float* coeff, int64_t B, int64_t Hq, int64_t Wq, int64_t K, int basis,
+                               const float* bezier_c, double offset, double tile, int64_t n_fp, const float* xa,
+                               const float* ta, const int64_t* ba, int64_t M, const float* counts,
+                               const float* centres, int64_t n_check, double tau, int64_t H, int64_t W, float* out,
+                               atlb_stream_t stream) {
+  clear();
+  NONNEG(M); NONNEG(H); NONNEG(W);
+  NEED(xa, M); NEED(ta, M); NEED(ba, M); NEED(out, M);
+  if (n_check < 1 || n_check > 4096 || !counts || !centres) {
+    set_error("%s: n_check = %lld, counts / centres %s", __func__, (long long)n_check,
+              (!counts || !centres) ? "NULL" : "set");
+    return ATLB_ERR_ARG;
+  }
+  TrajView V;
+  if (int st = make_traj(coeff, B, Hq, Wq, K, basis, bezier_c, offset, tile, n_fp, &V, __func__)) return st;
+  return traj_visible_fraction(V, xa, ta, LL(ba), M, counts, centres, (int)n_check, (float)tau, (float)(W - 1),
+                               (float)(H - 1), out, STREAM(stream));
 }

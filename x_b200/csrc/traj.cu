@@ -259,6 +259,51 @@ __global__ void __launch_bounds__(kTThreads) k_traj_bwd(TrajView V, const float2
   }
 }
 
+// Exposure correction (atl/objectives/ats.py:31-50) under the trajectories: for each anchor, the share of
+// its window's events recorded while the anchor's trajectory was inside the image, over n_check slice
+// centres.  The origin of the anchor's trajectory is solved once and reused for every centre (the
+// reference transports the anchor to each centre separately; the origin does not depend on the centre).
+template <int K>
+__global__ void __launch_bounds__(kTThreads) k_traj_vis(TrajView V, const float2* __restrict__ xa,
+                                                        const float* __restrict__ ta, const long long* __restrict__ ba,
+                                                        long long M, const float* __restrict__ counts,
+                                                        const float* __restrict__ centres, int n_check, float tau,
+                                                        float wmax, float hmax, float* __restrict__ out) {
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < M; i += stride) {
+    const float2 x = xa[i];
+    if (ba[i] < 0 || ba[i] >= V.B) {
+      out[i] = __int_as_float(0x7fc00000);
+      continue;
+    }
+    const int bb = (int)ba[i];
+    const float t = ta[i];
+    float g[K];
+    traj_basis<K>(V, t, g);
+    float px = x.x, py = x.y;
+    for (int it = 0; it < V.n_fp; ++it) {
+      const float2 d = traj_disp<K>(V, traj_taps(V, bb, px, py), g);
+      px = sub_rn(x.x, d.x);
+      py = sub_rn(x.y, d.y);
+    }
+    const Taps T = traj_taps(V, bb, px, py);
+    float vis = 0.f, tot = 0.f;
+    for (int k = 0; k < n_check; ++k) {
+      const float c = __ldg(centres + k);
+      const float near = fabsf(sub_rn(t, c)) <= tau ? 1.f : 0.f;
+      traj_basis<K>(V, c, g);
+      const float2 d = traj_disp<K>(V, T, g);
+      const float yx = add_rn(px, d.x), yy = add_rn(py, d.y);
+      const float inside = (yx >= 0.f && yx <= wmax && yy >= 0.f && yy <= hmax) ? 1.f : 0.f;
+      const float w = mul_rn(__ldg(counts + (long long)bb * n_check + k), near);
+      vis = add_rn(vis, mul_rn(w, inside));
+      tot = add_rn(tot, w);
+    }
+    const float r = div_rn(vis, tot < 1.f ? 1.f : tot);
+    out[i] = r < 1e-3f ? 1e-3f : r;
+  }
+}
+
 inline int tgrid(long long n) { return clamp_grid(blocks_for(n, kTThreads)); }
 
 template <typename F>
@@ -300,6 +345,18 @@ int traj_transport_bwd(const TrajView& V, const float* gy, const float* xy, cons
     timing_end("k_traj_bwd", s, e0);
   }
   return launch_status("traj_transport_bwd");
+}
+
+int traj_visible_fraction(const TrajView& V, const float* xa, const float* ta, const long long* ba, long long M,
+                          const float* counts, const float* centres, int n_check, float tau, float wmax, float hmax,
+                          float* out, cudaStream_t s) {
+  if (M > 0)
+    dispatch_k(V.K, [&](auto kc) {
+      constexpr int K = decltype(kc)::value;
+      launch(k_traj_vis<K>, tgrid(M), kTThreads, 0, s, V, (const float2*)xa, ta, ba, M, counts, centres, n_check, tau,
+             wmax, hmax, out);
+    });
+  return launch_status("traj_visible_fraction");
 }
 
 }  // namespace atlb

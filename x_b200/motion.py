@@ -318,6 +318,21 @@ class PixelTrajectories(Motion):
         p = self.origin(xy, t, b)
         return self._coeff_at(p, b)[:, 0]
 
+    @torch.no_grad()
+    def visible_fraction(self, xa, ta, ba, counts, centres, tau, H, W):
+        """The exposure correction of the anchors (atl/objectives/ats.py:31-50) in one kernel
+        (atlb_traj_visible_fraction): counts (B, n_check) slice counts, centres (n_check) slice centres."""
+        C = self.tile_c.detach().float().permute(0, 2, 3, 1).contiguous()
+        xac, tac, bac = xa.detach().float().contiguous(), ta.detach().float().contiguous(), ba.contiguous().long()
+        out = torch.empty(tac.shape[0], dtype=torch.float32, device=xa.device)
+        B, Hq, Wq, C2 = C.shape
+        L.check(L.lib().atlb_traj_visible_fraction(L.ptr(C), B, Hq, Wq, C2 // 2, self._basis_id, L.ptr(self._bc),
+                                                   self.offset, float(self.tile), self.n_fp, L.ptr(xac), L.ptr(tac),
+                                                   L.ptr(bac), tac.shape[0], L.ptr(counts.float()), L.ptr(centres),
+                                                   centres.shape[0], float(tau), H, W, L.ptr(out), L.stream()),
+                "traj_visible_fraction")
+        return out.to(ta.dtype)
+
     def tile_trajectories(self, times: torch.Tensor) -> torch.Tensor:
         """Positions (B, n_t, n_tiles, 2) of every tile trajectory at the given times."""
         B, Hq, Wq, K = self.B, self.Hq, self.Wq, self.K

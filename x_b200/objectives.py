@@ -31,9 +31,19 @@ def _fused_kind(motion) -> int:
 
 
 @torch.no_grad()
-def visible_fraction(motion, xa, ta, ba, ev: EventPacket, tau: float, n_check: int = 16) -> torch.Tensor:
+def slice_counts(ev: EventPacket, n_check: int = 16) -> torch.Tensor:
+    """Per-batch event counts in ``n_check`` equal time slices (ats.py:40-42), as exact integer counts
+    (a bincount, not an accumulating scatter of ones), float32 (B, n_check)."""
+    sl = torch.clamp((ev.t * n_check).long(), 0, n_check - 1)
+    return torch.bincount(ev.b * n_check + sl, minlength=ev.batch_size * n_check).view(
+        ev.batch_size, n_check).to(torch.float32)
+
+
+def visible_fraction(motion, xa, ta, ba, ev: EventPacket, tau: float, n_check: int = 16,
+                     counts: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Exposure correction (atl/objectives/ats.py:31-50): fraction of the anchor's source mass recorded
-    while its scene point was inside the image, checked at ``n_check`` slice centres."""
+    while its scene point was inside the image, checked at ``n_check`` slice centres.  ``counts``: the
+    window's :func:`slice_counts`, when the caller evaluates several anchor sets of one window."""
     kind = _fused_kind(motion)
     if kind >= 0 and xa.is_cuda:
         th = motion.theta.detach().float().contiguous()
@@ -49,13 +59,17 @@ def visible_fraction(motion, xa, ta, ba, ev: EventPacket, tau: float, n_check: i
         return out.to(ta.dtype)
     # other motion models: the same computation with the motion's own transport (torch ops on the device)
     edges = torch.linspace(0, 1, n_check + 1, device=ev.device)
-    centres = 0.5 * (edges[:-1] + edges[1:])
-    sl = torch.clamp((ev.t * n_check).long(), 0, n_check - 1)
-    counts = torch.zeros(ev.batch_size, n_check, device=ev.device)
-    counts.index_put_((ev.b, sl), torch.ones_like(ev.t), accumulate=True)
+    if getattr(motion, "_device_transport", None) is not None and motion._device_transport(xa, ta):
+        if counts is None:
+            counts = slice_counts(ev, n_check)
+        cen = (0.5 * (edges[:-1] + edges[1:])).contiguous()
+        return motion.visible_fraction(xa, ta, ba, counts.contiguous(), cen, float(tau), ev.height, ev.width)
+    centres = (0.5 * (edges[:-1] + edges[1:])).tolist()  # the fp32 centres, read back once
+    if counts is None:
+        counts = slice_counts(ev, n_check)
     vis = torch.zeros_like(ta); tot = torch.zeros_like(ta)
     for k in range(n_check):
-        c = float(centres[k])
+        c = centres[k]
         near = ((ta - c).abs() <= tau).to(ta.dtype)
         y = motion.transport(xa, ta, c, ba)
         inside = ((y[:, 0] >= 0) & (y[:, 0] <= ev.width - 1) & (y[:, 1] >= 0) & (y[:, 1] <= ev.height - 1)).to(ta.dtype)
@@ -231,6 +245,7 @@ class AnchoredSliced(Objective):
             xs = xs + (torch.rand(xs.shape, generator=self.gen).to(xs) - 0.5)
         xsm = xs + self.sigma * torch.randn(xs.shape, generator=self.gen).to(xs) if self.smooth_anchors else xs
         out, idx_all = [], []
+        counts = slice_counts(ev) if self.visibility else None  # the same for every slice
         for s in slices:
             c = (s + 0.5) * delta
             src = (ev.t - c).abs() <= self.tau + delta / 2
@@ -260,7 +275,8 @@ class AnchoredSliced(Objective):
                 own = src[ai].to(val.dtype) * _self_term(a, self.sigma, ev.height, ev.width)
             nsrc = torch.bincount(ev.b[si], minlength=ev.batch_size).to(val.dtype)[ev.b[ai]] - src[ai].to(val.dtype)
             if self.visibility:
-                nsrc = nsrc * visible_fraction(motion, xsm[ai].detach(), ev.t[ai], ev.b[ai], ev, self.tau)
+                nsrc = nsrc * visible_fraction(motion, xsm[ai].detach(), ev.t[ai], ev.b[ai], ev, self.tau,
+                                               counts=counts)
             rho = (val - own).clamp(min=0) / nsrc.clamp(min=1)
             out.append(torch.log(eps + rho) + ld)
             idx_all.append(ai)
