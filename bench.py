@@ -579,10 +579,11 @@ def config3_arm(args):
     coeff = (raw / raw.abs().amax() * 15.0 / K).cuda().requires_grad_(True)  # sum_k |c_k| g_k <= 15 px
     m = PixelTrajectories(coeff, K, basis_kind="bezier", tile=4)
     obj = AnchoredSliced(n_slices=10, sigma=1.5, seed=3102)
+    noise = obj.draw(ev)  # the reference's CPU-generator draws, once (as for configuration 2)
 
     def step():
         coeff.grad = None
-        ls, _ = obj.log_scores(ev, m)
+        ls, _ = obj.log_scores(ev, m, noise=noise)
         loss = -ls.mean()
         loss.backward()
         return loss

@@ -38,7 +38,7 @@ enum {
 const char* atlb_last_error(void);
 /* ABI version of this header (bumped on incompatible changes). */
 int atlb_abi_version(void);
-#define ATLB_ABI_VERSION 5
+#define ATLB_ABI_VERSION 6
 /* Number of kernels this library has launched in the calling process (instrumentation; no reference
  * counterpart). */
 uint64_t atlb_kernel_launches(void);
@@ -193,7 +193,10 @@ int atlb_visible_fraction(int kind, const float* theta, int64_t B, int64_t Hg, i
  * K <= 16 and n_fp <= 16.  Events with b outside [0, B) get NaN.  The backward ADDS dL/dcoeff (same
  * layout) for gy = dL/dout into gcoeff.
  * ---------------------------------------------------------------------------------------------- */
-int atlb_traj_transport(const float* coeff, int64_t B, int64_t Hq, int64_t Wq, int64_t K, int basis,
+/* mode 0: out = transport(xy, t -> t_dst); 1: out = the origin p (the fixed point; t_dst unused);
+ * 2: xy holds origins, out = p + d(p, t_dst) (t unused).  Modes 1 then 2 reproduce mode 0 exactly, so a
+ * caller moving the same events to several times solves each origin once. */
+int atlb_traj_transport(int mode, const float* coeff, int64_t B, int64_t Hq, int64_t Wq, int64_t K, int basis,
                         const float* bezier_c, double offset, double tile, int64_t n_fp, const float* xy,
                         const float* t, const float* t_dst, double t_dst_s, const int64_t* b, int64_t N, float* out,
                         atlb_stream_t stream);
@@ -205,10 +208,12 @@ int atlb_traj_visible_fraction(const float* coeff, int64_t B, int64_t Hq, int64_
                                const float* ta, const int64_t* ba, int64_t M, const float* counts,
                                const float* centres, int64_t n_check, double tau, int64_t H, int64_t W, float* out,
                                atlb_stream_t stream);
-int atlb_traj_transport_bwd(const float* gy, const float* coeff, int64_t B, int64_t Hq, int64_t Wq, int64_t K,
-                            int basis, const float* bezier_c, double offset, double tile, int64_t n_fp,
+/* Backward of the same mode for gy = dL/dout: adds dL/dcoeff into gcoeff; mode 2 also writes gp (N,2) =
+ * dL/d(its input origins). */
+int atlb_traj_transport_bwd(int mode, const float* gy, const float* coeff, int64_t B, int64_t Hq, int64_t Wq,
+                            int64_t K, int basis, const float* bezier_c, double offset, double tile, int64_t n_fp,
                             const float* xy, const float* t, const float* t_dst, double t_dst_s, const int64_t* b,
-                            int64_t N, float* gcoeff, atlb_stream_t stream);
+                            int64_t N, float* gcoeff, float* gp, atlb_stream_t stream);
 
 /* ----------------------------------------------------------------------------------------------
  * Fused anchored score: AnchoredExact.log_scores (atl/objectives/ats.py:75-96) for the motion kinds

@@ -70,10 +70,10 @@ _SIGS = {
     "atlb_velocity_bwd": (_int, [_int, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _vp, _i64, _vp, _vp]),
     "atlb_visible_fraction": (_int, [_int, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _i64, _vp, _vp, _i64,
                                      _dbl, _i64, _vp, _vp, _vp]),
-    "atlb_traj_transport": (_int, [_vp, _i64, _i64, _i64, _i64, _int, _vp, _dbl, _dbl, _i64, _vp, _vp, _vp, _dbl,
-                                   _vp, _i64, _vp, _vp]),
-    "atlb_traj_transport_bwd": (_int, [_vp, _vp, _i64, _i64, _i64, _i64, _int, _vp, _dbl, _dbl, _i64, _vp, _vp, _vp,
-                                       _dbl, _vp, _i64, _vp, _vp]),
+    "atlb_traj_transport": (_int, [_int, _vp, _i64, _i64, _i64, _i64, _int, _vp, _dbl, _dbl, _i64, _vp, _vp, _vp,
+                                   _dbl, _vp, _i64, _vp, _vp]),
+    "atlb_traj_transport_bwd": (_int, [_int, _vp, _vp, _i64, _i64, _i64, _i64, _int, _vp, _dbl, _dbl, _i64, _vp, _vp,
+                                       _vp, _dbl, _vp, _i64, _vp, _vp, _vp]),
     "atlb_traj_visible_fraction": (_int, [_vp, _i64, _i64, _i64, _i64, _int, _vp, _dbl, _dbl, _i64, _vp, _vp, _vp,
                                           _i64, _vp, _vp, _i64, _dbl, _i64, _i64, _vp, _vp]),
     "atlb_exact_prepare": (_int, [ctypes.POINTER(ExactCfg), _vp, _vp, _vp, _vp, _i64, _vp, _vp, _i64, _vp, _vp, _vp,

@@ -72,10 +72,10 @@ int window_counts(const float*, const long long*, long long, const long long*, l
 int window_counts_keys(const double*, long long, const float*, const long long*, const long long*, long long, double,
                        float*, cudaStream_t);
 
-int traj_transport(const TrajView&, const float*, const float*, const float*, float, const long long*, long long,
-                   float*, cudaStream_t);
-int traj_transport_bwd(const TrajView&, const float*, const float*, const float*, const float*, float,
-                       const long long*, long long, float*, cudaStream_t);
+int traj_transport(const TrajView&, int, const float*, const float*, const float*, float, const long long*,
+                   long long, float*, cudaStream_t);
+int traj_transport_bwd(const TrajView&, int, const float*, const float*, const float*, const float*, float,
+                       const long long*, long long, float*, float*, cudaStream_t);
 int traj_visible_fraction(const TrajView&, const float*, const float*, const long long*, long long, const float*,
                           const float*, int, float, float, float, float*, cudaStream_t);
 
@@ -496,29 +496,32 @@ static int make_traj(const float* coeff, int64_t B, int64_t Hq, int64_t Wq, int6
   return ATLB_OK;
 }
 
-int atlb_traj_transport(const float* coeff, int64_t B, int64_t Hq, int64_t Wq, int64_t K, int basis,
+int atlb_traj_transport(int mode, const float* coeff, int64_t B, int64_t Hq, int64_t Wq, int64_t K, int basis,
                         const float* bezier_c, double offset, double tile, int64_t n_fp, const float* xy,
                         const float* t, const float* t_dst, double t_dst_s, const int64_t* b, int64_t N, float* out,
                         atlb_stream_t stream) {
   clear();
   NONNEG(N);
   NEED(xy, N); NEED(t, N); NEED(b, N); NEED(out, N);
+  if (mode < 0 || mode > 2) { set_error("%s: mode %d", __func__, mode); return ATLB_ERR_ARG; }
   TrajView V;
   if (int st = make_traj(coeff, B, Hq, Wq, K, basis, bezier_c, offset, tile, n_fp, &V, __func__)) return st;
-  return traj_transport(V, xy, t, t_dst, (float)t_dst_s, LL(b), N, out, STREAM(stream));
+  return traj_transport(V, mode, xy, t, t_dst, (float)t_dst_s, LL(b), N, out, STREAM(stream));
 }
 
-int atlb_traj_transport_bwd(const float* gy, const float* coeff, int64_t B, int64_t Hq, int64_t Wq, int64_t K,
-                            int basis, const float* bezier_c, double offset, double tile, int64_t n_fp,
+int atlb_traj_transport_bwd(int mode, const float* gy, const float* coeff, int64_t B, int64_t Hq, int64_t Wq,
+                            int64_t K, int basis, const float* bezier_c, double offset, double tile, int64_t n_fp,
                             const float* xy, const float* t, const float* t_dst, double t_dst_s, const int64_t* b,
-                            int64_t N, float* gcoeff, atlb_stream_t stream) {
+                            int64_t N, float* gcoeff, float* gp, atlb_stream_t stream) {
   clear();
   NONNEG(N);
   NEED(gy, N); NEED(xy, N); NEED(t, N); NEED(b, N);
+  if (mode < 0 || mode > 2) { set_error("%s: mode %d", __func__, mode); return ATLB_ERR_ARG; }
+  if (mode == 2) NEED(gp, N);
   if (!gcoeff) { set_error("%s: gcoeff is NULL", __func__); return ATLB_ERR_ARG; }
   TrajView V;
   if (int st = make_traj(coeff, B, Hq, Wq, K, basis, bezier_c, offset, tile, n_fp, &V, __func__)) return st;
-  return traj_transport_bwd(V, gy, xy, t, t_dst, (float)t_dst_s, LL(b), N, gcoeff, STREAM(stream));
+  return traj_transport_bwd(V, mode, gy, xy, t, t_dst, (float)t_dst_s, LL(b), N, gcoeff, gp, STREAM(stream));
 }
 
 int atlb_traj_visible_fraction(const float* coeff, int64_t B, int64_t Hq, int64_t Wq, int64_t K, int basis,

@@ -110,8 +110,10 @@ __device__ __forceinline__ float2 traj_disp(const TrajView& V, const Taps& T, co
   return make_float2(dx, dy);
 }
 
+// mode 0: x -> transport(x, t -> t');  1: x -> origin p (the fixed point, t' unused);  2: p -> p + d(p, t')
+// (the input is an origin; t unused).  Modes 1 then 2 give exactly the values of mode 0.
 template <int K>
-__global__ void __launch_bounds__(kTThreads) k_traj_fwd(TrajView V, const float2* __restrict__ xy,
+__global__ void __launch_bounds__(kTThreads) k_traj_fwd(TrajView V, int mode, const float2* __restrict__ xy,
                                                         const float* __restrict__ t, const float* __restrict__ tdst,
                                                         float tdst_s, const long long* __restrict__ b, long long N,
                                                         float2* __restrict__ out) {
@@ -124,12 +126,18 @@ __global__ void __launch_bounds__(kTThreads) k_traj_fwd(TrajView V, const float2
     }
     const int bb = (int)b[n];
     float g[K];
-    traj_basis<K>(V, t[n], g);
     float px = x.x, py = x.y;
-    for (int i = 0; i < V.n_fp; ++i) {
-      const float2 d = traj_disp<K>(V, traj_taps(V, bb, px, py), g);
-      px = sub_rn(x.x, d.x);
-      py = sub_rn(x.y, d.y);
+    if (mode != 2) {
+      traj_basis<K>(V, t[n], g);
+      for (int i = 0; i < V.n_fp; ++i) {
+        const float2 d = traj_disp<K>(V, traj_taps(V, bb, px, py), g);
+        px = sub_rn(x.x, d.x);
+        py = sub_rn(x.y, d.y);
+      }
+    }
+    if (mode == 1) {
+      out[n] = make_float2(px, py);
+      continue;
     }
     traj_basis<K>(V, tdst ? tdst[n] : tdst_s, g);
     const float2 d = traj_disp<K>(V, traj_taps(V, bb, px, py), g);
@@ -217,45 +225,61 @@ __device__ __forceinline__ void acc_add(CellAcc& A, const Taps& T, bool final_ba
   }
 }
 
+// Backward of k_traj_fwd's modes for u = dL/d(output): mode 0 and 1 scatter the coefficient gradient (mode 1:
+// u is dL/dp of the origin); mode 2 also writes gp = dL/dp of its input origin.
 template <int K>
-__global__ void __launch_bounds__(kTThreads) k_traj_bwd(TrajView V, const float2* __restrict__ gy,
+__global__ void __launch_bounds__(kTThreads) k_traj_bwd(TrajView V, int mode, const float2* __restrict__ gy,
                                                         const float2* __restrict__ xy, const float* __restrict__ t,
                                                         const float* __restrict__ tdst, float tdst_s,
                                                         const long long* __restrict__ b, long long N,
-                                                        float* __restrict__ gC) {
+                                                        float* __restrict__ gC, float2* __restrict__ gp_out) {
   const long long stride = (long long)gridDim.x * blockDim.x;
   for (long long n = blockIdx.x * (long long)blockDim.x + threadIdx.x; n < N; n += stride) {
     const float2 u = gy[n];
-    if ((u.x == 0.f && u.y == 0.f) || b[n] < 0 || b[n] >= V.B) continue;
+    if ((u.x == 0.f && u.y == 0.f) || b[n] < 0 || b[n] >= V.B) {
+      if (mode == 2) gp_out[n] = make_float2(0.f, 0.f);
+      continue;
+    }
     const float2 x = xy[n];
     const int bb = (int)b[n];
     float g[K], gd[K];
-    traj_basis<K>(V, t[n], g);
-    traj_basis<K>(V, tdst ? tdst[n] : tdst_s, gd);
+    const int nfp = mode == 2 ? 0 : V.n_fp;
+    if (mode != 2) traj_basis<K>(V, t[n], g);
+    if (mode != 1) traj_basis<K>(V, tdst ? tdst[n] : tdst_s, gd);
+    if (mode == 2)
+#pragma unroll
+      for (int k = 0; k < K; ++k) g[k] = 0.f;
+    if (mode == 1)
+#pragma unroll
+      for (int k = 0; k < K; ++k) gd[k] = 0.f;
     float P[kTrajKMax + 1][2];  // iterates p_0 .. p_n (n_fp <= kTrajKMax), as the forward computes them
     P[0][0] = x.x;
     P[0][1] = x.y;
-    for (int i = 0; i < V.n_fp; ++i) {
+    for (int i = 0; i < nfp; ++i) {
       const float2 d = traj_disp<K>(V, traj_taps(V, bb, P[i][0], P[i][1]), g);
       P[i + 1][0] = sub_rn(x.x, d.x);
       P[i + 1][1] = sub_rn(x.y, d.y);
     }
     CellAcc A;
     A.live = false;
-    // y = p_n + d(p_n, t')
-    Taps T = traj_taps(V, bb, P[V.n_fp][0], P[V.n_fp][1]);
-    acc_add<K>(A, T, true, u.x, u.y, g, gd, gC);
-    const float2 jt = traj_jt<K>(V, T, gd, u.x, u.y);
-    float gpx = u.x + jt.x, gpy = u.y + jt.y;
+    float gpx = u.x, gpy = u.y;
+    if (mode != 1) {  // y = p_n + d(p_n, t')
+      const Taps T = traj_taps(V, bb, P[nfp][0], P[nfp][1]);
+      acc_add<K>(A, T, true, u.x, u.y, g, gd, gC);
+      const float2 jt = traj_jt<K>(V, T, gd, u.x, u.y);
+      gpx = u.x + jt.x;
+      gpy = u.y + jt.y;
+    }
     // p_{i+1} = x - d(p_i, t)
-    for (int i = V.n_fp - 1; i >= 0; --i) {
-      T = traj_taps(V, bb, P[i][0], P[i][1]);
+    for (int i = nfp - 1; i >= 0; --i) {
+      const Taps T = traj_taps(V, bb, P[i][0], P[i][1]);
       acc_add<K>(A, T, false, -gpx, -gpy, g, gd, gC);
       const float2 j = traj_jt<K>(V, T, g, -gpx, -gpy);
       gpx = j.x;
       gpy = j.y;
     }
     acc_flush<K>(A, g, gd, gC);
+    if (mode == 2) gp_out[n] = make_float2(gpx, gpy);
   }
 }
 
@@ -320,27 +344,29 @@ void dispatch_k(int K, F&& f) {
 
 }  // namespace
 
-int traj_transport(const TrajView& V, const float* xy, const float* t, const float* tdst, float tdst_s,
+int traj_transport(const TrajView& V, int mode, const float* xy, const float* t, const float* tdst, float tdst_s,
                    const long long* b, long long N, float* out, cudaStream_t s) {
   if (N > 0) {
     cudaEvent_t e0 = timing_begin(s);
     dispatch_k(V.K, [&](auto kc) {
       constexpr int K = decltype(kc)::value;
-      launch(k_traj_fwd<K>, tgrid(N), kTThreads, 0, s, V, (const float2*)xy, t, tdst, tdst_s, b, N, (float2*)out);
+      launch(k_traj_fwd<K>, tgrid(N), kTThreads, 0, s, V, mode, (const float2*)xy, t, tdst, tdst_s, b, N,
+             (float2*)out);
     });
     timing_end("k_traj_fwd", s, e0);
   }
   return launch_status("traj_transport");
 }
 
-int traj_transport_bwd(const TrajView& V, const float* gy, const float* xy, const float* t, const float* tdst,
-                       float tdst_s, const long long* b, long long N, float* gC, cudaStream_t s) {
+int traj_transport_bwd(const TrajView& V, int mode, const float* gy, const float* xy, const float* t,
+                       const float* tdst, float tdst_s, const long long* b, long long N, float* gC, float* gp,
+                       cudaStream_t s) {
   if (N > 0) {
     cudaEvent_t e0 = timing_begin(s);
     dispatch_k(V.K, [&](auto kc) {
       constexpr int K = decltype(kc)::value;
-      launch(k_traj_bwd<K>, tgrid(N), kTThreads, 0, s, V, (const float2*)gy, (const float2*)xy, t, tdst, tdst_s, b,
-             N, gC);
+      launch(k_traj_bwd<K>, tgrid(N), kTThreads, 0, s, V, mode, (const float2*)gy, (const float2*)xy, t, tdst, tdst_s,
+             b, N, gC, (float2*)gp);
     });
     timing_end("k_traj_bwd", s, e0);
   }

@@ -227,11 +227,12 @@ def basis(t: torch.Tensor, K: int, kind: str = "polynomial") -> torch.Tensor:
 
 
 class _TrajTransport(torch.autograd.Function):
-    """PixelTrajectories.transport on the device (atlb_traj_transport): differentiable w.r.t. the tile
-    coefficients; the event positions and times are data (no gradient)."""
+    """PixelTrajectories transport on the device (atlb_traj_transport), differentiable w.r.t. the tile
+    coefficients.  mode 0: xy -> transport to t_dst; 1: xy -> trajectory origin; 2: xy are origins ->
+    position at t_dst (also differentiable w.r.t. those origins).  Event positions and times are data."""
 
     @staticmethod
-    def forward(ctx, tile_c, xy, t, t_dst, b, model):
+    def forward(ctx, tile_c, xy, t, t_dst, b, model, mode):
         C = tile_c.detach().float().permute(0, 2, 3, 1).contiguous()
         xyc, tc, bc = xy.detach().float().contiguous(), t.detach().float().contiguous(), b.contiguous().long()
         if torch.is_tensor(t_dst) and t_dst.dim() > 0:
@@ -240,26 +241,27 @@ class _TrajTransport(torch.autograd.Function):
             tdc, tds = None, float(t_dst)
         out = torch.empty_like(xyc)
         B, Hq, Wq, C2 = C.shape
-        L.check(L.lib().atlb_traj_transport(L.ptr(C), B, Hq, Wq, C2 // 2, model._basis_id, L.ptr(model._bc),
+        L.check(L.lib().atlb_traj_transport(mode, L.ptr(C), B, Hq, Wq, C2 // 2, model._basis_id, L.ptr(model._bc),
                                             model.offset, float(model.tile), model.n_fp, L.ptr(xyc), L.ptr(tc),
                                             L.ptr(tdc), tds, L.ptr(bc), xyc.shape[0], L.ptr(out), L.stream()),
                 "traj_transport")
         ctx.save_for_backward(C, xyc, tc, bc, *(() if tdc is None else (tdc,)))
-        ctx.tds, ctx.model = tds, model
+        ctx.tds, ctx.model, ctx.mode = tds, model, mode
         return out
 
     @staticmethod
     def backward(ctx, gy):
         C, xyc, tc, bc, *rest = ctx.saved_tensors
         tdc = rest[0] if rest else None
-        m = ctx.model
+        m, mode = ctx.model, ctx.mode
         gC = torch.zeros_like(C)
+        gp = torch.empty_like(xyc) if mode == 2 else None
         B, Hq, Wq, C2 = C.shape
-        L.check(L.lib().atlb_traj_transport_bwd(L.ptr(gy.contiguous().float()), L.ptr(C), B, Hq, Wq, C2 // 2,
+        L.check(L.lib().atlb_traj_transport_bwd(mode, L.ptr(gy.contiguous().float()), L.ptr(C), B, Hq, Wq, C2 // 2,
                                                 m._basis_id, L.ptr(m._bc), m.offset, float(m.tile), m.n_fp,
                                                 L.ptr(xyc), L.ptr(tc), L.ptr(tdc), ctx.tds, L.ptr(bc), xyc.shape[0],
-                                                L.ptr(gC), L.stream()), "traj_transport_bwd")
-        return gC.permute(0, 3, 1, 2), None, None, None, None, None
+                                                L.ptr(gC), L.ptr(gp), L.stream()), "traj_transport_bwd")
+        return gC.permute(0, 3, 1, 2), gp, None, None, None, None, None
 
 
 class PixelTrajectories(Motion):
@@ -303,9 +305,19 @@ class PixelTrajectories(Motion):
 
     def transport(self, xy, t, t_dst, b):
         if self._device_transport(xy, t):
-            return _TrajTransport.apply(self.tile_c, xy, t, t_dst, b, self)
+            return _TrajTransport.apply(self.tile_c, xy, t, t_dst, b, self, 0)
         p = self.origin(xy, t, b)
         return p + self.displacement(p, b, as_time(t_dst, t))
+
+    def origin_on_device(self, xy, t, b):
+        """The trajectory origins of events (xy, t) (the fixed point of :meth:`origin`), on the device."""
+        return _TrajTransport.apply(self.tile_c, xy, t, 0.0, b, self, 1)
+
+    def from_origin(self, p, t, t_dst, b):
+        """Positions at t_dst of the trajectories starting at origins p: with p = :meth:`origin_on_device`,
+        exactly :meth:`transport`; differentiable w.r.t. p (a caller moving the same events to several
+        times solves each origin once)."""
+        return _TrajTransport.apply(self.tile_c, p, t, t_dst, b, self, 2)
 
     def _device_transport(self, xy, t) -> bool:
         """The kernels cover the invert assignment, K <= 16 and n_fp <= 16, for positions without gradient."""

@@ -231,21 +231,38 @@ class AnchoredSliced(Objective):
         self.nap, self.logdet = n_anchors_per_slice, logdet
         self.gen = torch.Generator().manual_seed(seed) if seed is not None else None
 
-    def log_scores(self, ev: EventPacket, motion, anchor_mask: Optional[torch.Tensor] = None,
-                   source_mask: Optional[torch.Tensor] = None):
-        S, dev = self.S, ev.device
-        delta = 1.0 / S
-        sl = torch.clamp(torch.floor(ev.t / delta), 0, S - 1).long()
+    def draw(self, ev: EventPacket):
+        """The objective's random draws in the reference's order (ats.py:127-135): the slice subset (when
+        slices_per_step < n_slices), dequantisation jitter u ~ U[0,1)^2 and anchor smoothing noise
+        z ~ N(0, I) per event.  Returns (slices, u, z), u / z on the events' device (None when off)."""
+        S = self.S
         slices = list(range(S))
         if self.sps is not None and self.sps < S:
             slices = torch.randperm(S, generator=self.gen)[: self.sps].tolist()
+        u = torch.rand(ev.xy.shape, generator=self.gen).to(ev.xy) if self.dequantize else None
+        z = torch.randn(ev.xy.shape, generator=self.gen).to(ev.xy) if self.smooth_anchors else None
+        return slices, u, z
+
+    def log_scores(self, ev: EventPacket, motion, anchor_mask: Optional[torch.Tensor] = None,
+                   source_mask: Optional[torch.Tensor] = None, noise=None):
+        """Per-anchor log scores and anchor indices (ats.py:122-174).  ``noise`` = :meth:`draw`'s
+        (slices, u, z) replaces the generator draws."""
+        S, dev = self.S, ev.device
+        delta = 1.0 / S
+        sl = torch.clamp(torch.floor(ev.t / delta), 0, S - 1).long()
+        slices, u, z = self.draw(ev) if noise is None else noise
         eps = self.eps_frac / (ev.height * ev.width)
         xs = ev.xy
         if self.dequantize:
-            xs = xs + (torch.rand(xs.shape, generator=self.gen).to(xs) - 0.5)
-        xsm = xs + self.sigma * torch.randn(xs.shape, generator=self.gen).to(xs) if self.smooth_anchors else xs
+            xs = xs + (u - 0.5)
+        xsm = xs + self.sigma * z if self.smooth_anchors else xs
         out, idx_all = [], []
         counts = slice_counts(ev) if self.visibility else None  # the same for every slice
+        bounds = _batch_bounds(ev)  # None unless the events are sorted by batch
+        # trajectories: every source's origin is solved once for all slices (it does not depend on the slice)
+        p_src = None
+        if source_mask is None and hasattr(motion, "from_origin") and motion._device_transport(xs, ev.t):
+            p_src = motion.origin_on_device(xs, ev.t, ev.b)
         for s in slices:
             c = (s + 0.5) * delta
             src = (ev.t - c).abs() <= self.tau + delta / 2
@@ -260,8 +277,13 @@ class AnchoredSliced(Objective):
             if self.nap is not None and ai.numel() > self.nap:
                 ai = ai[torch.randperm(ai.numel(), generator=self.gen)[: self.nap].to(dev)]
             si = torch.nonzero(src).squeeze(1)
-            y = motion.transport(xs[si], ev.t[si], c, ev.b[si])
-            img = splat(y, torch.ones_like(ev.t[si]), ev.b[si], ev.batch_size, ev.height, ev.width,
+            all_src = si.numel() == ev.n  # every event is a source: no gathers
+            xs_s, t_s, b_s = (xs, ev.t, ev.b) if all_src else (xs[si], ev.t[si], ev.b[si])
+            if p_src is not None:
+                y = motion.from_origin(p_src if all_src else p_src[si], t_s, c, b_s)
+            else:
+                y = motion.transport(xs_s, t_s, c, b_s)
+            img = splat(y, torch.ones_like(t_s), b_s, ev.batch_size, ev.height, ev.width,
                         kernel="gauss", sigma=self.sigma)
             if self.logdet:
                 a, ld = motion.transport_logdet(xsm[ai], ev.t[ai], c, ev.b[ai])
@@ -273,7 +295,12 @@ class AnchoredSliced(Objective):
                 own = src[ai].to(val.dtype) * _cross_term(a, y_own, self.sigma, ev.height, ev.width)
             else:
                 own = src[ai].to(val.dtype) * _self_term(a, self.sigma, ev.height, ev.width)
-            nsrc = torch.bincount(ev.b[si], minlength=ev.batch_size).to(val.dtype)[ev.b[ai]] - src[ai].to(val.dtype)
+            if bounds is not None:  # per-batch source counts from a prefix sum at the batch bounds (exact)
+                cs = torch.nn.functional.pad(torch.cumsum(src, 0), (1, 0))
+                per_b = cs[bounds[1:]] - cs[bounds[:-1]]
+            else:
+                per_b = torch.bincount(b_s, minlength=ev.batch_size)
+            nsrc = per_b.to(val.dtype)[ev.b[ai]] - src[ai].to(val.dtype)
             if self.visibility:
                 nsrc = nsrc * visible_fraction(motion, xsm[ai].detach(), ev.t[ai], ev.b[ai], ev, self.tau,
                                                counts=counts)
@@ -288,8 +315,8 @@ class AnchoredSliced(Objective):
     def set_bandwidth(self, h: float):
         self.sigma = float(h)
 
-    def __call__(self, ev, motion):
-        ls, _ = self.log_scores(ev, motion)
+    def __call__(self, ev, motion, noise=None):
+        ls, _ = self.log_scores(ev, motion, noise=noise)
         s = ls.mean() if ls.numel() else ev.t.new_zeros(())
         return {"loss": -s, "score": s.detach()}
 
@@ -309,6 +336,15 @@ def _cross_term(a: torch.Tensor, y: torch.Tensor, sigma: float, H: int, W: int) 
             d2 = (px - y[:, 0]) ** 2 + (py - y[:, 1]) ** 2
             s = s + wx * wy * ok.to(a.dtype) * norm * torch.exp(-d2 / (2 * sigma * sigma))
     return s
+
+
+def _batch_bounds(ev: EventPacket) -> Optional[torch.Tensor]:
+    """First event of each batch and the end (B + 1) for batch-sorted events (the EventPacket invariant),
+    else None."""
+    b = ev.b
+    if b.numel() > 1 and not bool((b[1:] >= b[:-1]).all()):
+        return None
+    return torch.searchsorted(b, torch.arange(ev.batch_size + 1, device=b.device, dtype=b.dtype))
 
 
 def _self_term(y: torch.Tensor, sigma: float, H: int, W: int) -> torch.Tensor:
