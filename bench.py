@@ -46,6 +46,9 @@ def parse():
     ap.add_argument("--events", type=int, default=N_EVENTS)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--windows", type=int, default=8, help="--workload splat: windows of --events events")
+    ap.add_argument("--dropin", action="store_true",
+                    help="config2 through the stage-by-stage drop-in ops (device plan + ats_pair_fwd/bwd extension "
+                         "calls, as atl's objective makes them) instead of the fused pipeline")
     ap.add_argument("--workload", default="config2", choices=["config2", "config3", "config5", "splat"],
                     help="config2: one 1M-event window per GPU (the headline); config5: one 64M-event window "
                          "on 1280x720 shared by all GPUs (sources split across ranks, NCCL all-reduce); splat: the "
@@ -273,7 +276,8 @@ def ours_arm(args):
     ev_cpu, flow_cpu = window_data(rank, args.events)
     ev = ev_cpu.to(dev)
     m = DenseLinearFlow(1, H, W, grid=(H, W), mode="linear", init=flow_cpu).to(dev)
-    obj = AnchoredExact(h=1.0, tau=1.0, n_anchors=None, n_slices=16, seed=7 + rank, visibility=True)
+    obj = AnchoredExact(h=1.0, tau=1.0, n_anchors=None, n_slices=16, seed=7 + rank, visibility=True,
+                        fused=not args.dropin)
     anchors, u, z = obj.draw(ev)
     noise = (anchors, u, z)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)  # > 126 MB L2
@@ -381,18 +385,21 @@ def ours_arm(args):
         Ns, M = plan.src_y.shape[0], plan.anc_x.shape[0]
         del plan
     alg = {"k_pair_fwd": Ns * 16 + M * (16 + 16 + 4), "k_pair_bwd": Ns * 24 + M * 20 + args.events * 8}
+    if args.dropin:  # the reference's plan layout: (y, v, t, int64 id) 28 B per entry, anchors bucketed 28 B
+        alg = {"k_pair_fwd": Ns * 28 + M * 32, "k_pair_bwd": Ns * 28 + M * 32 + args.events * 8}
     alg_bytes = alg[dom]
     avg_ms = dom_ms / max(dom_n, 1)
     peak, peak_kind = measured_peak()
     achieved = alg_bytes / (avg_ms / 1000) / 1e9
-    traffic = profiled_traffic(dom)
+    traffic = None if args.dropin else profiled_traffic(dom)
     cores = os.cpu_count()
     cpu = None if (args.no_cpu_baseline or world > 1) else cpu_baseline(ev_cpu, flow_cpu, args.events)
     line = {
         "metric": METRIC, "value": value, "unit": "events/s", "n_gpus": world, "steps": args.steps,
         "warmup": max(args.warmup, 3), "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "events_per_window": args.events, "windows_per_gpu": 1,
+        "config": {"workload": WORKLOAD + (" [stage-by-stage drop-in ops]" if args.dropin else ""),
+                   "events_per_window": args.events, "windows_per_gpu": 1,
                    "anchors_per_window": M, "plan_entries": Ns, "l2": "flushed (256 MB write) before every step",
                    "parallelism": f"replicas x{world}"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
