@@ -5,15 +5,16 @@
 //   prepare   one pass over the events: dequantised position xs = xy + (u - 1/2), velocity v(xs),
 //             packed (xs, v) record, vmax and (b, t)-order checks; one pass over the anchors:
 //             xa = xs[a] + h z and the anchors' bounding box                       [1 host read]
-//   forward   slice-major count + scan + scatter of the (source, slice) entries into a compact
-//             24-byte layout, anchors bucketed by cell, per-anchor normaliser W_i * vis_i * 2 pi h^2
+//   forward   count + scan + scatter of the (source, slice) entries into a compact 24-byte layout (the
+//             events walked in mid-slice cell order, warp-aggregated cursors; optionally a range of the
+//             events as sources, for one window split over GPUs), anchors bucketed by cell, per-anchor
+//             normaliser W_i * vis_i * 2 pi h^2
 //             (window count + exposure correction fused), pair sums with the log score written
 //             directly (log(eps + S / den)).
 //   backward  dL/dS from the upstream dL/dls, source-centric pair gradient, velocity-field gradient.
 // Every step keeps the reference's rounding, so scores match it to float accuracy and the plan's
 // cells are the reference's cells.
 #include <cstddef>
-
 #include <mutex>
 
 #include "common.cuh"
@@ -684,7 +685,6 @@ int exact_forward(const atlb_exact_cfg& c, const float* t, const long long* b, l
   // pair sums + log scores
   const FastEntries E{w.YV, w.TI};
   const FastAnchors A{w.XT, w.BI};
-  const CellGrid G{g.GW, g.GH, g.S, ncell};
   const PairConsts C = make_pair_consts(c.h, c.tau, c.cut);
   const float eps = (float)(c.eps_frac / (double)(c.H * c.W));
   if (M > 0 && ncell > 0) {

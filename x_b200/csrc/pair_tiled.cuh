@@ -6,7 +6,8 @@
 //             the anchors' leave-one-out terms are evaluated while staging.  Warps then walk the tile's
 //             anchor cells: a cell's anchors in register groups of up to 4, the candidates of its 3x3
 //             neighbourhood streamed by the lanes.  A tile whose neighbourhood does not fit reads its
-//             candidates from global memory instead (same loop, global pointer).
+//             candidates from global memory instead (same loop, global pointer); a tile with more anchors
+//             than it stages is left to k_pair_fwd_overflow (warp per anchor cell, groups of up to 8).
 //   backward: not tiled.  One warp per source cell, one entry per lane; the anchors of the 3x3 cells are
 //             warp-uniform broadcast loads through L1 of per-anchor records prepared once per backward
 //             (measured faster than staging them: no barriers, no per-tile set-up, L1 reuse across the
