@@ -41,13 +41,13 @@ int plan_fill(const float*, const float*, const float*, const long long*, long l
 size_t pair_workspace_bytes(long long M, long long ncell);
 int pair_fwd(const float*, const float*, const float*, const long long*, const long long*, const float*, const float*,
              const long long*, const long long*, const float*, long long, long long, long long, long long, long long,
-             double, double, double, float*, void*, cudaStream_t);
+             long long, double, double, double, float*, void*, cudaStream_t);
 int pair_bwd(const float*, const float*, const float*, const float*, const long long*, const long long*, const float*,
-             const float*, const long long*, const long long*, const float*, long long, long long, long long,
+             const float*, const long long*, const long long*, const float*, long long, long long, long long, long long,
              long long, long long, double, double, double, long long, float*, void*, cudaStream_t);
 int pair_fwd_noalloc(const float*, const float*, const float*, const long long*, const long long*, const float*,
                      const float*, const long long*, const long long*, const float*, long long, long long, long long,
-                     long long, long long, double, double, double, float*, cudaStream_t);
+                     long long, long long, long long, double, double, double, float*, cudaStream_t);
 int splat_bilinear_fwd(const float*, const float*, const long long*, long long, long long, long long, long long,
                        float*, cudaStream_t);
 int splat_bilinear_bwd(const float*, const float*, const float*, const long long*, long long, long long, long long,
@@ -306,8 +306,8 @@ int atlb_ats_pair_fwd(const float* src_y, const float* src_v, const float* src_t
   if (int st = check_pair(cell_start, slice_c, Ns, M, ncell, S, GH, GW, workspace, workspace_bytes, __func__)) return st;
   NEED(src_y, Ns); NEED(src_v, Ns); NEED(src_t, Ns); NEED(src_id, Ns);
   NEED(anc_x, M); NEED(anc_t, M); NEED(anc_cell, M); NEED(anc_id, M); NEED(out, M);
-  return pair_fwd(src_y, src_v, src_t, LL(src_id), LL(cell_start), anc_x, anc_t, LL(anc_cell), LL(anc_id), slice_c, M,
-                  ncell, S, GH, GW, h, tau, cut, out, workspace, STREAM(stream));
+  return pair_fwd(src_y, src_v, src_t, LL(src_id), LL(cell_start), anc_x, anc_t, LL(anc_cell), LL(anc_id), slice_c, Ns,
+                  M, ncell, S, GH, GW, h, tau, cut, out, workspace, STREAM(stream));
 }
 
 int atlb_ats_pair_fwd_noalloc(const float* src_y, const float* src_v, const float* src_t, const int64_t* src_id,
@@ -322,7 +322,7 @@ int atlb_ats_pair_fwd_noalloc(const float* src_y, const float* src_v, const floa
   NEED(src_y, Ns); NEED(src_v, Ns); NEED(src_t, Ns); NEED(src_id, Ns);
   NEED(anc_x, M); NEED(anc_t, M); NEED(anc_cell, M); NEED(anc_id, M); NEED(out, M);
   return pair_fwd_noalloc(src_y, src_v, src_t, LL(src_id), LL(cell_start), anc_x, anc_t, LL(anc_cell), LL(anc_id),
-                          slice_c, M, ncell, S, GH, GW, h, tau, cut, out, STREAM(stream));
+                          slice_c, Ns, M, ncell, S, GH, GW, h, tau, cut, out, STREAM(stream));
 }
 
 int atlb_ats_pair_bwd(const float* gS, const float* src_y, const float* src_v, const float* src_t,
@@ -336,7 +336,7 @@ int atlb_ats_pair_bwd(const float* gS, const float* src_y, const float* src_v, c
   NEED(gS, M); NEED(src_y, Ns); NEED(src_v, Ns); NEED(src_t, Ns); NEED(src_id, Ns);
   NEED(anc_x, M); NEED(anc_t, M); NEED(anc_cell, M); NEED(anc_id, M); NEED(gv, N);
   return pair_bwd(gS, src_y, src_v, src_t, LL(src_id), LL(cell_start), anc_x, anc_t, LL(anc_cell), LL(anc_id), slice_c,
-                  M, ncell, S, GH, GW, h, tau, cut, N, gv, workspace, STREAM(stream));
+                  Ns, M, ncell, S, GH, GW, h, tau, cut, N, gv, workspace, STREAM(stream));
 }
 
 int atlb_window_counts(const float* t, const int64_t* b, int64_t N, const int64_t* idx, int64_t M, double tau,

@@ -10,6 +10,7 @@
 #include <climits>
 #include <cstring>
 #include <atomic>
+#include <mutex>
 #include <utility>
 
 #include "atl_b200.h"
@@ -85,6 +86,19 @@ inline void launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
 // Opt-in event timing of a launch (timing.cu); both are no-ops unless atlb_timing_enable(1).
 cudaEvent_t timing_begin(cudaStream_t s);
 void timing_end(const char* name, cudaStream_t s, cudaEvent_t e0);
+
+// True on the first call for the current device per flag set (one bit per device): kernel attributes, such
+// as the opt-in to more than 48 KB of dynamic shared memory, are per device.
+inline std::mutex g_attr_mu;
+inline bool first_use_on_device(unsigned long long& done) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return true;
+  std::lock_guard<std::mutex> lk(g_attr_mu);
+  const unsigned long long m = 1ULL << dev;
+  if (done & m) return false;
+  done |= m;
+  return true;
+}
 
 // Host-side status plumbing (capi.cu owns the thread-local message).
 void set_error(const char* fmt, ...);

@@ -555,18 +555,7 @@ size_t ws_layout(long long N, long long M, long long ncell, long long S, long lo
 
 int warp_grid(long long nwarps) { return clamp_grid(blocks_for(nwarps * 32, kThreads)); }
 
-// True on the first call for the current device (per flag set): kernel attributes are per device.
-std::mutex g_attr_mu;
-unsigned long long g_fwd_attr = 0;
-bool first_use_on_device(unsigned long long& done) {
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return true;
-  std::lock_guard<std::mutex> lk(g_attr_mu);
-  const unsigned long long m = 1ULL << dev;
-  if (done & m) return false;
-  done |= m;
-  return true;
-}
+unsigned long long g_fwd_attr = 0;  // devices on which the tiled forward's shared-memory opt-in is set
 
 // Every pair passes |t_i - t_j| <= tau when tau covers the events' time range: fl(t_i - t_j) never exceeds
 // fl(t_hi - t_lo) (rounding is monotonic).  NaN bounds (unknown range) fail the test.
@@ -691,9 +680,9 @@ int exact_forward(const atlb_exact_cfg& c, const float* t, const long long* b, l
     // the entry times (last member) are only staged when tau does not cover the window
     const size_t smem_all = sizeof(TileSmemFwd), smem_no_t = offsetof(TileSmemFwd, ti);
     if (first_use_on_device(g_fwd_attr)) {  // the opt-in above 48 KB is a per-device attribute
-      cudaFuncSetAttribute(k_pair_fwd_tiled<true, FusedOut>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+      cudaFuncSetAttribute(k_pair_fwd_tiled<true, false, FastEntries, int, FusedOut>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            (int)smem_no_t);
-      cudaFuncSetAttribute(k_pair_fwd_tiled<false, FusedOut>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+      cudaFuncSetAttribute(k_pair_fwd_tiled<false, false, FastEntries, int, FusedOut>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            (int)smem_all);
     }
     const dim3 grid((unsigned)((g.GW + kTileX - 1) / kTileX), (unsigned)((g.GH + kTileY - 1) / kTileY),
@@ -703,18 +692,20 @@ int exact_forward(const atlb_exact_cfg& c, const float* t, const long long* b, l
     cudaMemsetAsync(w.scratch, 0, sizeof(int), s);
     cudaEvent_t e0 = timing_begin(s);
     if (tau_covers(g, c.tau))
-      launch(k_pair_fwd_tiled<true, FusedOut>, grid, kTileThreads, smem_no_t, s, E, A, (const int*)w.astart,
+      launch(k_pair_fwd_tiled<true, false, FastEntries, int, FusedOut>, grid, kTileThreads, smem_no_t, s, E, A, (const int*)w.astart,
              (const int*)w.start, T, (const float*)w.SC, C, P, (const float4*)ev4, out, w.scratch);
     else
-      launch(k_pair_fwd_tiled<false, FusedOut>, grid, kTileThreads, smem_all, s, E, A,
+      launch(k_pair_fwd_tiled<false, false, FastEntries, int, FusedOut>, grid, kTileThreads, smem_all, s, E, A,
              (const int*)w.astart, (const int*)w.start, T, (const float*)w.SC, C, P, (const float4*)ev4, out,
              w.scratch);
     // cells of tiles with more anchors than the tiled kernel stages (dense windows)
     if (tau_covers(g, c.tau))
-      launch(k_pair_fwd_overflow<true, FusedOut>, warp_grid(ncell), 256, 0, s, E, A, (const int*)w.astart,
+      launch(k_pair_fwd_overflow<true, false, FastEntries, int, FusedOut>, warp_grid(ncell), 256, 0, s, E, A,
+             nullptr, (const int*)w.astart,
              (const int*)w.start, T, (const float*)w.SC, C, P, (const float4*)ev4, out, (const int*)w.scratch);
     else
-      launch(k_pair_fwd_overflow<false, FusedOut>, warp_grid(ncell), 256, 0, s, E, A, (const int*)w.astart,
+      launch(k_pair_fwd_overflow<false, false, FastEntries, int, FusedOut>, warp_grid(ncell), 256, 0, s, E, A,
+             nullptr, (const int*)w.astart,
              (const int*)w.start, T, (const float*)w.SC, C, P, (const float4*)ev4, out, (const int*)w.scratch);
     timing_end("k_pair_fwd", s, e0);
   }
@@ -742,10 +733,12 @@ int exact_backward(const atlb_exact_cfg& c, const float* grad_ls, const long lon
     const dim3 grid((unsigned)((g.GW + 7) / 8), (unsigned)min(nrows, 65535));
     cudaEvent_t e0 = timing_begin(s);
     if (tau_covers(g, c.tau))
-      launch(k_pair_bwd_cells<true>, grid, 256, 0, s, E, (const float4*)w.AB, (const float*)w.GB,
+      launch(k_pair_bwd_cells<true, false, FastEntries, int>, grid, 256, 0, s, E, (const float4*)w.AB,
+             (const float*)w.GB, nullptr,
              (const int*)w.astart, (const int*)w.start, (int)g.GW, (int)g.GH, nrows, C, N, gv);
     else
-      launch(k_pair_bwd_cells<false>, grid, 256, 0, s, E, (const float4*)w.AB, (const float*)w.GB,
+      launch(k_pair_bwd_cells<false, false, FastEntries, int>, grid, 256, 0, s, E, (const float4*)w.AB,
+             (const float*)w.GB, nullptr,
              (const int*)w.astart, (const int*)w.start, (int)g.GW, (int)g.GH, nrows, C, N, gv);
     timing_end("k_pair_bwd", s, e0);
   }

@@ -1,22 +1,28 @@
 // Anchored pair sums over the reference plan layout: the B200 replacement of ats_pair_fwd /
 // ats_pair_bwd (csrc/atl_cpu.cpp:176-253).
 //
-// Reference: one thread per anchor walks its 3x3 cells; the backward scatters 2 global float
-// atomics per pair.  Here:
-//   * anchors are first bucketed by cell (counting sort, same key as the sources), so one WARP owns
-//     one anchor cell: its anchors sit in registers and the 32 lanes stream the candidate sources of
-//     the 3 neighbouring cell rows (each row is one contiguous CSR range), coalesced;
-//   * the backward is source-centric over the same bucketing: one warp owns one source cell, each
-//     lane one source, and the anchors of the 3x3 neighbourhood are broadcast -- the gradient of a
-//     source entry is summed in registers and leaves with ONE vector red.global per entry instead of
-//     two atomics per pair.
-// The pair test (|dt| <= tau, d^2 <= (cut h)^2, leave-one-out by id) is evaluated with the exact
-// rounding sequence of the reference, so the set of contributing pairs is identical.
+// Reference: one thread per anchor walks its 3x3 cells; the backward scatters 2 global float atomics per
+// pair.  Here the anchors are first bucketed by cell (counting sort, same key as the sources) into 16-byte
+// records, and the plan's entries are read where the caller holds them (SoA, int64 ids and CSR offsets):
+//   * forward: the shared-memory tiled kernel of the fused path (pair_tiled.cuh).  Per tile of 8 x 4 cells
+//     the entries of the surrounding cells are staged with cp.async and assembled there into (y, v) and
+//     (t, id) records.  Leave-one-out compares the entry's id with the anchor's, per pair, on the low 32
+//     bits; when some id does not fit in 32 bits (the count pass flags it) every cell takes the untiled
+//     kernel instead, which compares all 64;
+//   * backward: one warp per source cell, one entry per lane, the anchors of the 3x3 neighbourhood read as
+//     warp-uniform broadcast records: the gradient of an entry is summed in registers and leaves with ONE
+//     vector red.global instead of two atomics per pair.
+// The acceptance test (|dt| <= tau, d^2 <= (cut h)^2, leave-one-out by id) follows the reference's exact
+// rounding sequence, so the set of contributing pairs is identical; the kernel value (ex2) and the order of
+// summation differ from the reference in the last bits.  Grids the tiled kernels cannot index (2^31 entries
+// or more, a cell count that is not a whole number of S x GH x GW grids, more than 65535 slices) take the
+// per-cell-warp kernels of pair_kernels.cuh.
 #include <mutex>
 
 #include "common.cuh"
 #include "pair_kernels.cuh"
 #include "pair_math.cuh"
+#include "pair_tiled.cuh"
 #include "plan_math.cuh"
 #include "scan.cuh"
 
@@ -24,7 +30,6 @@ namespace atlb {
 namespace {
 
 constexpr int kThreads = 256;
-constexpr int kAnchorChunk = 8;
 
 __device__ __forceinline__ long long anchor_key(const long long* AC, long long i, long long S, long long GH,
                                                 long long GW, long long ncell) {
@@ -34,16 +39,30 @@ __device__ __forceinline__ long long anchor_key(const long long* AC, long long i
   return key < ncell ? key : -1;
 }
 
-__global__ void __launch_bounds__(kThreads) k_anchor_count(const long long* __restrict__ AC, long long M, long long S,
-                                                           long long GH, long long GW, long long ncell,
-                                                           int* __restrict__ counts) {
+__device__ __forceinline__ bool wide_id(long long id) { return ((unsigned long long)id >> 32) != 0; }
+
+// Anchors per cell.  With `flags`, also raises kOverflowAll when an anchor id (AID) or an entry id (SID) is
+// negative or not below 2^32, the range in which the tiled forward's 32-bit comparison is exact.
+__global__ void __launch_bounds__(kThreads) k_anchor_count(const long long* __restrict__ AC,
+                                                           const long long* __restrict__ AID, long long M,
+                                                           const long long* __restrict__ SID, long long Ns,
+                                                           long long S, long long GH, long long GW, long long ncell,
+                                                           int* __restrict__ counts, int* __restrict__ flags) {
   const long long stride = (long long)gridDim.x * blockDim.x;
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < M; i += stride) {
-    const long long key = anchor_key(AC, i, S, GH, GW, ncell);
-    if (key >= 0) atomicAdd(counts + key, 1);
+  const long long n = M > Ns ? M : Ns;
+  bool wide = false;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += stride) {
+    if (i < M) {
+      const long long key = anchor_key(AC, i, S, GH, GW, ncell);
+      if (key >= 0) atomicAdd(counts + key, 1);
+      if (flags) wide |= wide_id(AID[i]);
+    }
+    if (flags && i < Ns) wide |= wide_id(SID[i]);
   }
+  if (wide) atomicOr(flags, kOverflowAll);
 }
 
+// Generic kernels' anchor buckets: SoA copies.
 __global__ void __launch_bounds__(kThreads) k_anchor_scatter(const long long* __restrict__ AC,
                                                              const float2* __restrict__ AX,
                                                              const float* __restrict__ AT,
@@ -69,10 +88,64 @@ __global__ void __launch_bounds__(kThreads) k_anchor_scatter(const long long* __
   }
 }
 
+// Tiled forward's anchor records: XT = (x, y, t, low 32 bits of the id), BI = original index.
+__global__ void __launch_bounds__(kThreads) k_anchor_records_fwd(const long long* __restrict__ AC,
+                                                                 const float2* __restrict__ AX,
+                                                                 const float* __restrict__ AT,
+                                                                 const long long* __restrict__ AID, long long M,
+                                                                 long long S, long long GH, long long GW,
+                                                                 long long ncell, const int* __restrict__ start,
+                                                                 int* __restrict__ cursor, float4* __restrict__ XT,
+                                                                 int* __restrict__ BI, float* __restrict__ out) {
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < M; i += stride) {
+    const long long key = anchor_key(AC, i, S, GH, GW, ncell);
+    if (key < 0) {
+      out[i] = __int_as_float(0x7fc00000);  // a cell outside the grid, as the generic path
+      continue;
+    }
+    const int p = start[key] + atomicAdd(cursor + key, 1);
+    const float2 x = AX[i];
+    XT[p] = make_float4(x.x, x.y, AT[i], __int_as_float((int)AID[i]));
+    BI[p] = (int)i;
+  }
+}
+
+// Cell-per-warp backward's anchor records: AB = (x, y, t - c_s, t), GB = dL/dS / h^2, GID = id.
+__global__ void __launch_bounds__(kThreads) k_anchor_records_bwd(const long long* __restrict__ AC,
+                                                                 const float2* __restrict__ AX,
+                                                                 const float* __restrict__ AT,
+                                                                 const long long* __restrict__ AID,
+                                                                 const float* __restrict__ gS,
+                                                                 const float* __restrict__ SC, long long M,
+                                                                 long long S, long long GH, long long GW,
+                                                                 long long ncell, float invh2,
+                                                                 const int* __restrict__ start,
+                                                                 int* __restrict__ cursor, float4* __restrict__ AB,
+                                                                 float* __restrict__ GB, long long* __restrict__ GID) {
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < M; i += stride) {
+    const long long key = anchor_key(AC, i, S, GH, GW, ncell);
+    if (key < 0) continue;
+    const int p = start[key] + atomicAdd(cursor + key, 1);
+    const float2 x = AX[i];
+    const float t = AT[i];
+    AB[p] = make_float4(x.x, x.y, sub_rn(t, __ldg(SC + AC[3 * i] % S)), t);
+    GB[p] = gS[i] * invh2;
+    GID[p] = AID[i];
+  }
+}
+
 struct RefOut {
   float* out;
   const int* idx;
   __device__ __forceinline__ void operator()(int p, double v) const { out[idx[p]] = (float)v; }
+};
+
+// Output of the tiled forward: it passes the original anchor index.
+struct DirectOut {
+  float* out;
+  __device__ __forceinline__ void operator()(int i, double v) const { out[i] = (float)v; }
 };
 
 __global__ void __launch_bounds__(kThreads) k_gather_bucketed(const float* __restrict__ g, const int* __restrict__ idx,
@@ -83,13 +156,15 @@ __global__ void __launch_bounds__(kThreads) k_gather_bucketed(const float* __res
 
 }  // namespace
 
+// Per anchor: a 16-byte record (tiled kernels; the generic kernels keep x and t there), the id, the original
+// index and dL/dS in bucket order.  Per cell: a count / cursor and a CSR offset.  Two ints after the counts
+// hold the forward's overflow word.
 size_t pair_workspace_bytes(long long M, long long ncell) {
   size_t n = 0;
-  n += align_up((size_t)ncell * sizeof(int));              // counts / cursor
+  n += align_up((size_t)(ncell + 2) * sizeof(int));        // counts / cursor, overflow word
   n += align_up((size_t)(ncell + 1) * sizeof(int));        // start
   n += align_up(scan_partials_bytes(ncell));               // scan partials
-  n += align_up((size_t)M * sizeof(float2));               // xy
-  n += align_up((size_t)M * sizeof(float));                // t
+  n += align_up((size_t)M * sizeof(float4));               // records (generic: xy, then t)
   n += align_up((size_t)M * sizeof(long long));            // id
   n += align_up((size_t)M * sizeof(int));                  // idx
   n += align_up((size_t)M * sizeof(float));                // gS in bucket order
@@ -99,9 +174,11 @@ size_t pair_workspace_bytes(long long M, long long ncell) {
 namespace {
 struct PairWs {
   int* counts;
+  int* flags;
   int* start;
   long long* partials;
-  float2* xy;
+  float4* rec;
+  float2* xy;  // generic kernels: inside rec
   float* t;
   long long* id;
   int* idx;
@@ -110,11 +187,13 @@ struct PairWs {
 PairWs carve(void* ws, long long M, long long ncell) {
   char* p = (char*)align_ptr(ws);
   PairWs w;
-  w.counts = (int*)p; p += align_up((size_t)ncell * sizeof(int));
+  w.counts = (int*)p; p += align_up((size_t)(ncell + 2) * sizeof(int));
+  w.flags = w.counts + ncell;
   w.start = (int*)p; p += align_up((size_t)(ncell + 1) * sizeof(int));
   w.partials = (long long*)p; p += align_up(scan_partials_bytes(ncell));
-  w.xy = (float2*)p; p += align_up((size_t)M * sizeof(float2));
-  w.t = (float*)p; p += align_up((size_t)M * sizeof(float));
+  w.rec = (float4*)p; p += align_up((size_t)M * sizeof(float4));
+  w.xy = (float2*)w.rec;
+  w.t = (float*)(w.xy + M);
   w.id = (long long*)p; p += align_up((size_t)M * sizeof(long long));
   w.idx = (int*)p; p += align_up((size_t)M * sizeof(int));
   w.gb = (float*)p;
@@ -122,51 +201,112 @@ PairWs carve(void* ws, long long M, long long ncell) {
 }
 
 RefAnchors bucket_anchors(const PairWs& w, const long long* AC, const float* AX, const float* AT,
-                             const long long* AID, long long M, long long S, long long GH, long long GW,
-                             long long ncell, float* out_invalid, cudaStream_t s) {
+                          const long long* AID, long long M, long long S, long long GH, long long GW,
+                          long long ncell, float* out_invalid, cudaStream_t s) {
   cudaMemsetAsync(w.counts, 0, (size_t)ncell * sizeof(int), s);
   if (M > 0)
-    launch(k_anchor_count, clamp_grid(blocks_for(M, kThreads)), kThreads, 0, s, AC, M, S, GH, GW, ncell, w.counts);
+    launch(k_anchor_count, clamp_grid(blocks_for(M, kThreads)), kThreads, 0, s, AC, AID, M, (const long long*)nullptr,
+           0LL, S, GH, GW, ncell, w.counts, (int*)nullptr);
   exclusive_scan<int>(w.counts, ncell, w.partials, w.start, s);
   if (M > 0)
-    launch(k_anchor_scatter, clamp_grid(blocks_for(M, kThreads)), kThreads, 0, s, 
-        AC, (const float2*)AX, AT, AID, M, S, GH, GW, ncell, w.start, w.counts, w.xy, w.t, w.id, w.idx, out_invalid);
+    launch(k_anchor_scatter, clamp_grid(blocks_for(M, kThreads)), kThreads, 0, s, AC, (const float2*)AX, AT, AID, M,
+           S, GH, GW, ncell, w.start, w.counts, w.xy, w.t, w.id, w.idx, out_invalid);
   RefAnchors A;
   A.xy = w.xy; A.t = w.t; A.id = w.id; A.idx = w.idx;
   return A;
 }
 
 int warp_grid(long long nwarps) { return clamp_grid(blocks_for(nwarps * 32, kThreads)); }
+
+// The tiled kernels' grid when the plan fits their 32-bit indexing: ncell = B x S x GH x GW.
+bool tiled_grid(long long Ns, long long ncell, long long S, long long GH, long long GW, TileGrid* T) {
+  if (Ns >= INT_MAX || GH <= 0 || GW <= 0 || S < 1 || S > 65535) return false;
+  const long long per = S * GH * GW;
+  if (ncell % per != 0 || (GH + kTileY - 1) / kTileY > 65535) return false;
+  *T = TileGrid{(int)GW, (int)GH, (int)S, (int)(ncell / per)};
+  return true;
+}
+
+unsigned long long g_ref_fwd_attr = 0;  // devices on which the tiled forward's shared-memory opt-in is set
+
+// Forward into `out` with the buckets in `ws`; `timed`: report the pair kernels to atlb_timing_*.
+int pair_fwd_ws(const float* SY, const float* SV, const float* ST, const long long* SID, const long long* CS,
+                const float* AX, const float* AT, const long long* AC, const long long* AID, const float* SC,
+                long long Ns, long long M, long long ncell, long long S, long long GH, long long GW, double h,
+                double tau, double cut, float* out, void* ws, bool timed, cudaStream_t s) {
+  const PairWs w = carve(ws, M, ncell);
+  const RefEntries E{(const float2*)SY, (const float2*)SV, ST, SID};
+  const PairConsts C = make_pair_consts(h, tau, cut);
+  TileGrid T;
+  if (M > 0 && ncell > 0 && tiled_grid(Ns, ncell, S, GH, GW, &T)) {
+    using Tiled = void (*)(RefEntries, FastAnchors, const int*, const long long*, TileGrid, const float*, PairConsts,
+                           PlanConsts, const float4*, DirectOut, int*);
+    const Tiled tiled = k_pair_fwd_tiled<false, true, RefEntries, long long, DirectOut>;
+    if (first_use_on_device(g_ref_fwd_attr))  // the opt-in above 48 KB is a per-device attribute
+      cudaFuncSetAttribute(tiled, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(TileSmemFwd));
+    cudaMemsetAsync(w.counts, 0, (size_t)(ncell + 2) * sizeof(int), s);  // counts and the overflow word
+    launch(k_anchor_count, clamp_grid(blocks_for(M > Ns ? M : Ns, kThreads)), kThreads, 0, s, AC, AID, M, SID, Ns, S,
+           GH, GW, ncell, w.counts, w.flags);
+    exclusive_scan<int>(w.counts, ncell, w.partials, w.start, s);
+    launch(k_anchor_records_fwd, clamp_grid(blocks_for(M, kThreads)), kThreads, 0, s, AC, (const float2*)AX, AT, AID,
+           M, S, GH, GW, ncell, (const int*)w.start, w.counts, w.rec, w.idx, out);
+    const FastAnchors A{w.rec, w.idx};
+    const PlanConsts P{};
+    const dim3 grid((unsigned)((GW + kTileX - 1) / kTileX), (unsigned)((GH + kTileY - 1) / kTileY), (unsigned)S);
+    cudaEvent_t e0 = timed ? timing_begin(s) : nullptr;
+    launch(tiled, grid, kTileThreads, sizeof(TileSmemFwd), s, E, A, (const int*)w.start, CS, T, SC, C, P,
+           (const float4*)nullptr, DirectOut{out}, w.flags);
+    launch(k_pair_fwd_overflow<false, true, RefEntries, long long, DirectOut>, warp_grid(ncell), 256, 0, s, E, A, AID,
+           (const int*)w.start, CS, T, SC, C, P, (const float4*)nullptr, DirectOut{out}, (const int*)w.flags);
+    if (timed) timing_end("k_pair_fwd", s, e0);
+    return ATLB_OK;
+  }
+  const RefAnchors A = bucket_anchors(w, AC, AX, AT, AID, M, S, GH, GW, ncell, out, s);
+  const CellGrid G{GW, GH, S, ncell};
+  if (M > 0 && ncell > 0) {
+    cudaEvent_t e0 = timed ? timing_begin(s) : nullptr;
+    launch(k_pair_fwd_t<RefEntries, RefAnchors, long long, RefOut>, warp_grid(ncell), kThreads, 0, s, E, A,
+           (const int*)w.start, CS, G, SC, C, RefOut{out, w.idx});
+    if (timed) timing_end("k_pair_fwd", s, e0);
+  }
+  return ATLB_OK;
+}
 }  // namespace
 
 int pair_fwd(const float* SY, const float* SV, const float* ST, const long long* SID, const long long* CS,
-             const float* AX, const float* AT, const long long* AC, const long long* AID, const float* SC, long long M,
-             long long ncell, long long S, long long GH, long long GW, double h, double tau, double cut, float* out,
-             void* ws, cudaStream_t s) {
-  const PairWs w = carve(ws, M, ncell);
-  const RefAnchors A = bucket_anchors(w, AC, AX, AT, AID, M, S, GH, GW, ncell, out, s);
-  const RefEntries E{(const float2*)SY, (const float2*)SV, ST, SID};
-  const CellGrid G{GW, GH, S, ncell};
-  const PairConsts C = make_pair_consts(h, tau, cut);
-  if (M > 0 && ncell > 0) {
-    cudaEvent_t e0 = timing_begin(s);
-    launch(k_pair_fwd_t<RefEntries, RefAnchors, long long, RefOut>, warp_grid(ncell), kThreads, 0, s, E, A,
-           (const int*)w.start, CS, G, SC, C, RefOut{out, w.idx});
-    timing_end("k_pair_fwd", s, e0);
-  }
+             const float* AX, const float* AT, const long long* AC, const long long* AID, const float* SC, long long Ns,
+             long long M, long long ncell, long long S, long long GH, long long GW, double h, double tau, double cut,
+             float* out, void* ws, cudaStream_t s) {
+  pair_fwd_ws(SY, SV, ST, SID, CS, AX, AT, AC, AID, SC, Ns, M, ncell, S, GH, GW, h, tau, cut, out, ws, true, s);
   return launch_status("ats_pair_fwd");
 }
 
 int pair_bwd(const float* gS, const float* SY, const float* SV, const float* ST, const long long* SID,
              const long long* CS, const float* AX, const float* AT, const long long* AC, const long long* AID,
-             const float* SC, long long M, long long ncell, long long S, long long GH, long long GW, double h,
-             double tau, double cut, long long N, float* gv, void* ws, cudaStream_t s) {
+             const float* SC, long long Ns, long long M, long long ncell, long long S, long long GH, long long GW,
+             double h, double tau, double cut, long long N, float* gv, void* ws, cudaStream_t s) {
   const PairWs w = carve(ws, M, ncell);
   cudaMemsetAsync(gv, 0, (size_t)N * 2 * sizeof(float), s);
-  const RefAnchors A = bucket_anchors(w, AC, AX, AT, AID, M, S, GH, GW, ncell, nullptr, s);
   const RefEntries E{(const float2*)SY, (const float2*)SV, ST, SID};
-  const CellGrid G{GW, GH, S, ncell};
   const PairConsts C = make_pair_consts(h, tau, cut);
+  TileGrid T;
+  if (M > 0 && ncell > 0 && tiled_grid(Ns, ncell, S, GH, GW, &T)) {
+    cudaMemsetAsync(w.counts, 0, (size_t)ncell * sizeof(int), s);
+    launch(k_anchor_count, clamp_grid(blocks_for(M, kThreads)), kThreads, 0, s, AC, AID, M, (const long long*)nullptr,
+           0LL, S, GH, GW, ncell, w.counts, (int*)nullptr);
+    exclusive_scan<int>(w.counts, ncell, w.partials, w.start, s);
+    launch(k_anchor_records_bwd, clamp_grid(blocks_for(M, kThreads)), kThreads, 0, s, AC, (const float2*)AX, AT, AID,
+           gS, SC, M, S, GH, GW, ncell, C.invh2, (const int*)w.start, w.counts, w.rec, w.gb, w.id);
+    const int nrows = (int)(ncell / GW);
+    const dim3 grid((unsigned)((GW + 7) / 8), (unsigned)(nrows < 65535 ? nrows : 65535));
+    cudaEvent_t e0 = timing_begin(s);
+    launch(k_pair_bwd_cells<false, true, RefEntries, long long>, grid, 256, 0, s, E, (const float4*)w.rec,
+           (const float*)w.gb, (const long long*)w.id, (const int*)w.start, CS, (int)GW, (int)GH, nrows, C, N, gv);
+    timing_end("k_pair_bwd", s, e0);
+    return launch_status("ats_pair_bwd");
+  }
+  const RefAnchors A = bucket_anchors(w, AC, AX, AT, AID, M, S, GH, GW, ncell, nullptr, s);
+  const CellGrid G{GW, GH, S, ncell};
   if (M > 0 && ncell > 0) {
     launch(k_gather_bucketed, clamp_grid(blocks_for(M, kThreads)), kThreads, 0, s, gS, (const int*)w.idx, M, w.gb);
     cudaEvent_t e0 = timing_begin(s);
@@ -221,15 +361,15 @@ int pair_scratch_address(void** out) {
 }
 }  // namespace
 
-// Same kernels and result as pair_fwd; the workspace is g_pair_scratch.  The per-cell counters are
-// zeroed on the stream by every call (bucket_anchors), and every other byte used is written before it
-// is read, so what an earlier call left in the array does not matter.  Calls whose work overlaps on the
-// GPU (two streams, or two host threads) share the array and race.  Not timed by atlb_timing_*, whose
-// events would be created here.
+// Same kernels and result as pair_fwd; the workspace is g_pair_scratch.  The per-cell counters and the
+// overflow word are zeroed on the stream by every call, and every other byte used is written before it is
+// read, so what an earlier call left in the array does not matter.  Calls whose work overlaps on the GPU
+// (two streams, or two host threads) share the array and race.  Not timed by atlb_timing_*, whose events
+// would be created here.
 int pair_fwd_noalloc(const float* SY, const float* SV, const float* ST, const long long* SID, const long long* CS,
                      const float* AX, const float* AT, const long long* AC, const long long* AID, const float* SC,
-                     long long M, long long ncell, long long S, long long GH, long long GW, double h, double tau,
-                     double cut, float* out, cudaStream_t s) {
+                     long long Ns, long long M, long long ncell, long long S, long long GH, long long GW, double h,
+                     double tau, double cut, float* out, cudaStream_t s) {
   const size_t need = pair_workspace_bytes(M, ncell);
   if (need > kNoAllocScratchBytes) {
     set_error("atlb_ats_pair_fwd_noalloc: %lld anchors over %lld cells need %zu scratch bytes, above the fixed %zu",
@@ -238,14 +378,7 @@ int pair_fwd_noalloc(const float* SY, const float* SV, const float* ST, const lo
   }
   void* ws = nullptr;
   if (int st = pair_scratch_address(&ws)) return st;
-  const PairWs w = carve(ws, M, ncell);
-  const RefAnchors A = bucket_anchors(w, AC, AX, AT, AID, M, S, GH, GW, ncell, out, s);
-  const RefEntries E{(const float2*)SY, (const float2*)SV, ST, SID};
-  const CellGrid G{GW, GH, S, ncell};
-  const PairConsts C = make_pair_consts(h, tau, cut);
-  if (M > 0 && ncell > 0)
-    launch(k_pair_fwd_t<RefEntries, RefAnchors, long long, RefOut>, warp_grid(ncell), kThreads, 0, s, E, A,
-           (const int*)w.start, CS, G, SC, C, RefOut{out, w.idx});
+  pair_fwd_ws(SY, SV, ST, SID, CS, AX, AT, AC, AID, SC, Ns, M, ncell, S, GH, GW, h, tau, cut, out, ws, false, s);
   return launch_status("ats_pair_fwd_noalloc");
 }
 

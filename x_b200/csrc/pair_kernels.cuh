@@ -33,6 +33,13 @@ struct RefEntries {
     t = __ldg(ST + k);
     id = __ldg(SID + k);
   }
+  __device__ __forceinline__ float4 yv(long long k) const {
+    const float2 y = __ldg(SY + k), v = __ldg(SV + k);
+    return make_float4(y.x, y.y, v.x, v.y);
+  }
+  __device__ __forceinline__ float t(long long k) const { return __ldg(ST + k); }
+  __device__ __forceinline__ int id(long long k) const { return (int)__ldg(SID + k); }
+  __device__ __forceinline__ long long id64(long long k) const { return __ldg(SID + k); }
 };
 
 // Compact layout of the fused path: (y.x, y.y, v.x, v.y) + (t, id bits), 24 bytes per entry.
@@ -48,6 +55,9 @@ struct FastEntries {
     t = b.x;
     id = __float_as_int(b.y);
   }
+  __device__ __forceinline__ float4 yv(long long k) const { return __ldg(YV + k); }
+  __device__ __forceinline__ float t(long long k) const { return __ldg(TI + k).x; }
+  __device__ __forceinline__ int id(long long k) const { return __float_as_int(__ldg(TI + k).y); }
 };
 
 // ---- anchor accessors (bucketed by cell) -------------------------------------------------------------

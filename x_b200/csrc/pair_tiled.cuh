@@ -134,16 +134,16 @@ __device__ __forceinline__ TileGeo tile_geo(const TileGrid& G) {
 // Buffer offsets of a block of cells (rows [y0, y1), columns [x0, x1)) from a CSR array: off[r][c] = slot of
 // cell (y0 + r, x0 + c) (c = x1 - x0 gives the row end), row0[r] = CSR index of the row's first cell,
 // rbase[r] = the row's first slot.  Executed by one full warp; *total = the block's entries.
-template <int NC>
-__device__ __forceinline__ void block_offsets(const int* __restrict__ csr, int gbase, int GW, int y0, int y1, int x0,
+template <int NC, typename CS>
+__device__ __forceinline__ void block_offsets(const CS* __restrict__ csr, int gbase, int GW, int y0, int y1, int x0,
                                               int x1, int (*off)[NC + 1], int* row0, int* rbase, int* total) {
   const int lane = threadIdx.x & 31;
   const int nr = y1 - y0, nc = x1 - x0;
   int len = 0, k0 = 0;
   if (lane < nr) {
     const int row = gbase + (y0 + lane) * GW;
-    k0 = csr[row + x0];
-    len = csr[row + x1] - k0;
+    k0 = (int)csr[row + x0];
+    len = (int)csr[row + x1] - k0;
   }
   int incl = len;
 #pragma unroll
@@ -160,7 +160,7 @@ __device__ __forceinline__ void block_offsets(const int* __restrict__ csr, int g
   __syncwarp();
   for (int r = 0; r < nr; ++r) {
     const int row = gbase + (y0 + r) * GW;
-    for (int c = lane; c <= nc; c += 32) off[r][c] = csr[row + x0 + c] - row0[r] + rbase[r];
+    for (int c = lane; c <= nc; c += 32) off[r][c] = (int)csr[row + x0 + c] - row0[r] + rbase[r];
   }
   __syncwarp();
 }
@@ -170,8 +170,9 @@ __device__ __forceinline__ void block_offsets(const int* __restrict__ csr, int g
 // The CSR ranges of the 3 cell rows (cy-1 .. cy+1, each spanning cells cx-1 .. cx+1 clipped to the grid)
 // around cell (cx, cy); a row outside the grid gets an empty range.  Always 3 rows, so that callers
 // unroll their row loops and lo/hi stay in registers.
+template <typename CS>
 __device__ __forceinline__ int neighbour_rows(const TileGeo& t, int gbase, int GW, int GH, int cx, int cy, bool staged,
-                                              const int (*off)[kSC + 1], const int* __restrict__ csr, int* lo,
+                                              const int (*off)[kSC + 1], const CS* __restrict__ csr, int* lo,
                                               int* hi) {
   const int xl = max(cx - 1, 0), xh = min(cx + 1, GW - 1) + 1;
 #pragma unroll
@@ -184,14 +185,29 @@ __device__ __forceinline__ int neighbour_rows(const TileGeo& t, int gbase, int G
         h = off[y - t.sy0][xh - t.sx0];
       } else {
         const int row = gbase + y * GW;
-        l = csr[row + xl];
-        h = csr[row + xh];
+        l = (int)csr[row + xl];
+        h = (int)csr[row + xh];
       }
     }
     lo[r] = l;
     hi[r] = h;
   }
   return 3;
+}
+
+// Stage plan entry k into shared memory as (y, v) and, if asked, (t, id bits).  Compact layout: two copies;
+// the reference's layout: four (its int64 id contributes its low word; ids are below 2^31).
+__device__ __forceinline__ void stage_entry(const FastEntries& e, float4* dyv, float2* dti, int k, bool with_ti) {
+  cp_async16(dyv, e.YV + k);
+  if (with_ti) cp_async8(dti, e.TI + k);
+}
+__device__ __forceinline__ void stage_entry(const RefEntries& e, float4* dyv, float2* dti, int k, bool with_ti) {
+  cp_async8(&dyv->x, e.SY + k);
+  cp_async8(&dyv->z, e.SV + k);
+  if (with_ti) {
+    cp_async4(&dti->x, e.ST + k);
+    cp_async4(&dti->y, e.SID + k);  // little-endian: the low 32 bits
+  }
 }
 
 // Leave-one-out: anchor a's own event appears among the candidates iff its entry of slice s exists and its
@@ -218,17 +234,20 @@ __device__ __forceinline__ float self_term(const PlanConsts& P, const PairConsts
 }
 
 // ---- forward -----------------------------------------------------------------------------------------
-template <int NA, bool TAU_ALL, bool STAGED, class Out>
-__device__ __forceinline__ void fwd_group_tile(const TileSmemFwd& sm, int p, const float4* __restrict__ yv,
-                                               const float2* __restrict__ ti, const int* lo, const int* hi, int nrows,
-                                               float cs, const PairConsts& C, const PlanConsts& P,
+// LOO_ID: leave-one-out by comparing event ids per pair (the reference's plan layout, where an anchor's own
+// entry cannot be located); otherwise the anchor's own pair is recomputed and subtracted (self_term).
+template <int NA, bool TAU_ALL, bool LOO_ID, bool STAGED, class E, class Out>
+__device__ __forceinline__ void fwd_group_tile(const TileSmemFwd& sm, int p, const E& ent, const int* lo,
+                                               const int* hi, float cs, const PairConsts& C, const PlanConsts& P,
                                                const float4* __restrict__ ev4, int b, int s, int cx, int cy, Out& out,
                                                int lane) {
+  constexpr bool kTI = !TAU_ALL || LOO_ID;  // entry times / ids needed
   f32x2 axy[NA], adt2[NA];
   float at[NA], acc[NA];
+  int aid[NA];
   // lane q < NA evaluates anchor q's leave-one-out term; its latency overlaps the candidate loop
   float self_k = 0.f;
-  if (lane < NA) {
+  if (!LOO_ID && lane < NA) {
     const float4 a = sm.anc[p + lane];
     self_k = self_term(P, C, ev4, __float_as_int(a.w), a.x, a.y, a.z, sub_rn(a.z, cs), b, s, cx, cy);
   }
@@ -239,21 +258,30 @@ __device__ __forceinline__ void fwd_group_tile(const TileSmemFwd& sm, int p, con
     axy[q] = pk2(a.x, a.y);
     adt2[q] = pk2(adt, adt);
     at[q] = a.z;
+    aid[q] = __float_as_int(a.w);
     acc[q] = 0.f;
   }
-  const unsigned yv_s = STAGED ? smem_addr(yv) : 0u, ti_s = STAGED ? smem_addr(ti) : 0u;
+  const unsigned yv_s = STAGED ? smem_addr(sm.yv) : 0u, ti_s = STAGED ? smem_addr(sm.ti) : 0u;
 #pragma unroll
   for (int r = 0; r < 3; ++r) {
     const int k1 = hi[r];
     for (int k = lo[r] + lane; k < k1; k += 32) {
       float4 e;
       float st = 0.f;
+      int eid = 0;
       if (STAGED) {
         e = lds128(yv_s + 16u * (unsigned)k);
-        if (!TAU_ALL) st = lds64(ti_s + 8u * (unsigned)k).x;
+        if (kTI) {
+          const float2 q = lds64(ti_s + 8u * (unsigned)k);
+          st = q.x;
+          eid = __float_as_int(q.y);
+        }
       } else {
-        e = __ldg(yv + k);
-        if (!TAU_ALL) st = __ldg(ti + k).x;
+        e = ent.yv(k);
+        if (kTI) {
+          st = ent.t(k);
+          eid = ent.id(k);
+        }
       }
       const f32x2 y = pk2(e.x, e.y), v = pk2(e.z, e.w);
 #pragma unroll
@@ -262,6 +290,7 @@ __device__ __forceinline__ void fwd_group_tile(const TileSmemFwd& sm, int p, con
         const float d2 = residual2(axy[q], adt2[q], y, v, &rr);
         bool ok = !(d2 > C.r2max);
         if (!TAU_ALL) ok = ok && !(fabsf(sub_rn(at[q], st)) > C.tau);
+        if (LOO_ID) ok = ok && eid != aid[q];
         const float kv = ex2_approx(-d2 * C.k2);
         acc[q] += ok ? kv : 0.f;
       }
@@ -270,22 +299,27 @@ __device__ __forceinline__ void fwd_group_tile(const TileSmemFwd& sm, int p, con
 #pragma unroll
   for (int q = 0; q < NA; ++q) {
     const float sum = warp_sum(acc[q]);
-    const float self_q = __shfl_sync(0xffffffffu, self_k, q);
+    const float self_q = LOO_ID ? 0.f : __shfl_sync(0xffffffffu, self_k, q);
     if (lane == 0) out(sm.aidx[p + q], (double)(sum - self_q));
   }
 }
 
+// Bits of the overflow word shared by the tiled and untiled forward kernels.
+constexpr int kOverflowTiles = 1;  // some tile has more anchors than the tiled kernel stages
+constexpr int kOverflowAll = 2;    // set by the caller before the launch: the untiled kernel takes every cell
+
 // out(i, S_i) with i the original anchor index.  A tile with more than kTileAncCap anchors sets *overflow
 // and leaves its anchors to the caller's untiled pass.
-template <bool TAU_ALL, class Out>
-__global__ void __launch_bounds__(kTileThreads) k_pair_fwd_tiled(FastEntries ent, FastAnchors anc,
+template <bool TAU_ALL, bool LOO_ID, class E, typename CS, class Out>
+__global__ void __launch_bounds__(kTileThreads) k_pair_fwd_tiled(E ent, FastAnchors anc,
                                                                  const int* __restrict__ astart,
-                                                                 const int* __restrict__ cstart, TileGrid G,
+                                                                 const CS* __restrict__ cstart, TileGrid G,
                                                                  const float* __restrict__ SC, PairConsts C,
                                                                  PlanConsts P, const float4* __restrict__ ev4,
                                                                  Out out, int* __restrict__ overflow) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   TileSmemFwd& sm = *reinterpret_cast<TileSmemFwd*>(smem_raw);
+  if (LOO_ID && (*overflow & kOverflowAll)) return;  // ids beyond 32 bits: every cell goes to the untiled kernel
   const TileGeo t = tile_geo(G);
   const int GW = G.GW, GH = G.GH, s = (int)blockIdx.z;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
@@ -304,7 +338,7 @@ __global__ void __launch_bounds__(kTileThreads) k_pair_fwd_tiled(FastEntries ent
     const int na = sm.atotal;
     const bool staged = sm.total <= kStageCap;
     if (na == 0 || na > kTileAncCap) {  // CTA-uniform
-      if (na > kTileAncCap && threadIdx.x == 0) atomicOr(overflow, 1);
+      if (na > kTileAncCap && threadIdx.x == 0) atomicOr(overflow, kOverflowTiles);
       __syncthreads();
       continue;
     }
@@ -319,10 +353,8 @@ __global__ void __launch_bounds__(kTileThreads) k_pair_fwd_tiled(FastEntries ent
     if (staged) {
       for (int r = 0; r < t.sy1 - t.sy0; ++r) {
         const int k0 = sm.row_k0[r], b0 = sm.cell_off[r][0], n = sm.cell_off[r][nsc] - b0;
-        for (int i = threadIdx.x; i < n; i += blockDim.x) {
-          cp_async16(&sm.yv[b0 + i], ent.YV + k0 + i);
-          if (!TAU_ALL) cp_async8(&sm.ti[b0 + i], ent.TI + k0 + i);
-        }
+        for (int i = threadIdx.x; i < n; i += blockDim.x)
+          stage_entry(ent, &sm.yv[b0 + i], &sm.ti[b0 + i], k0 + i, !TAU_ALL || LOO_ID);
       }
     }
     // work items: (cell, group of <= 4 anchors), cost = anchors x candidates
@@ -366,21 +398,21 @@ __global__ void __launch_bounds__(kTileThreads) k_pair_fwd_tiled(FastEntries ent
       const int nrows = neighbour_rows(t, gbase, GW, GH, t.tx0 + cxo, t.ty0 + cyo, staged, sm.cell_off, cstart, lo, hi);
       const int na_g = min(4, p1 - p);
       const int cx = t.tx0 + cxo, cy = t.ty0 + cyo;
-#define ATLB_GROUP(n, st, yvp, tip) \
-  fwd_group_tile<n, TAU_ALL, st>(sm, p, yvp, tip, lo, hi, nrows, cs, C, P, ev4, b, s, cx, cy, out, lane)
+#define ATLB_GROUP(n, st) \
+  fwd_group_tile<n, TAU_ALL, LOO_ID, st>(sm, p, ent, lo, hi, cs, C, P, ev4, b, s, cx, cy, out, lane)
       if (staged) {
         switch (na_g) {
-          case 4: ATLB_GROUP(4, true, sm.yv, sm.ti); break;
-          case 3: ATLB_GROUP(3, true, sm.yv, sm.ti); break;
-          case 2: ATLB_GROUP(2, true, sm.yv, sm.ti); break;
-          default: ATLB_GROUP(1, true, sm.yv, sm.ti); break;
+          case 4: ATLB_GROUP(4, true); break;
+          case 3: ATLB_GROUP(3, true); break;
+          case 2: ATLB_GROUP(2, true); break;
+          default: ATLB_GROUP(1, true); break;
         }
       } else {
         switch (na_g) {
-          case 4: ATLB_GROUP(4, false, ent.YV, ent.TI); break;
-          case 3: ATLB_GROUP(3, false, ent.YV, ent.TI); break;
-          case 2: ATLB_GROUP(2, false, ent.YV, ent.TI); break;
-          default: ATLB_GROUP(1, false, ent.YV, ent.TI); break;
+          case 4: ATLB_GROUP(4, false); break;
+          case 3: ATLB_GROUP(3, false); break;
+          case 2: ATLB_GROUP(2, false); break;
+          default: ATLB_GROUP(1, false); break;
         }
       }
 #undef ATLB_GROUP
@@ -391,16 +423,19 @@ __global__ void __launch_bounds__(kTileThreads) k_pair_fwd_tiled(FastEntries ent
 
 // ---- forward, untiled (cells the tiled kernel leaves: tiles with more anchors than it stages) -----------
 // One warp per anchor cell: its anchors in register groups of up to 8, the candidates of the 3 neighbouring
-// cell rows streamed from global memory (L1) by the lanes; the same arithmetic as the tiled kernel.
-template <int NA, bool TAU_ALL, class Out>
-__device__ __forceinline__ void fwd_group_cells(const FastEntries& ent, const FastAnchors& anc, int p, const int* lo,
+// cell rows streamed from global memory (L1) by the lanes; the same arithmetic as the tiled kernel.  With
+// LOO_ID the ids are compared at full width: AID holds the anchors' ids by original index.
+template <int NA, bool TAU_ALL, bool LOO_ID, class E, class Out>
+__device__ __forceinline__ void fwd_group_cells(const E& ent, const FastAnchors& anc,
+                                                const long long* __restrict__ AID, int p, const int* lo,
                                                 const int* hi, float cs, const PairConsts& C, const PlanConsts& P,
                                                 const float4* __restrict__ ev4, int b, int s, int cx, int cy,
                                                 Out& out, int lane) {
   f32x2 axy[NA], adt2[NA];
   float at[NA], acc[NA];
+  long long aid[NA];
   float self_k = 0.f;
-  if (lane < NA) {
+  if (!LOO_ID && lane < NA) {
     const float4 a = __ldg(anc.XT + p + lane);
     self_k = self_term(P, C, ev4, __float_as_int(a.w), a.x, a.y, a.z, sub_rn(a.z, cs), b, s, cx, cy);
   }
@@ -411,14 +446,17 @@ __device__ __forceinline__ void fwd_group_cells(const FastEntries& ent, const Fa
     axy[q] = pk2(a.x, a.y);
     adt2[q] = pk2(adt, adt);
     at[q] = a.z;
+    aid[q] = LOO_ID ? __ldg(AID + __ldg(anc.idx + p + q)) : 0;
     acc[q] = 0.f;
   }
 #pragma unroll
   for (int r = 0; r < 3; ++r) {
     const int k1 = hi[r];
     for (int k = lo[r] + lane; k < k1; k += 32) {
-      const float4 e = __ldg(ent.YV + k);
-      const float st = TAU_ALL ? 0.f : __ldg(ent.TI + k).x;
+      const float4 e = ent.yv(k);
+      const float st = TAU_ALL ? 0.f : ent.t(k);
+      long long eid = 0;
+      if constexpr (LOO_ID) eid = ent.id64(k);
       const f32x2 y = pk2(e.x, e.y), v = pk2(e.z, e.w);
 #pragma unroll
       for (int q = 0; q < NA; ++q) {
@@ -426,6 +464,7 @@ __device__ __forceinline__ void fwd_group_cells(const FastEntries& ent, const Fa
         const float d2 = residual2(axy[q], adt2[q], y, v, &rr);
         bool ok = !(d2 > C.r2max);
         if (!TAU_ALL) ok = ok && !(fabsf(sub_rn(at[q], st)) > C.tau);
+        if (LOO_ID) ok = ok && eid != aid[q];
         const float kv = ex2_approx(-d2 * C.k2);
         acc[q] += ok ? kv : 0.f;
       }
@@ -434,20 +473,23 @@ __device__ __forceinline__ void fwd_group_cells(const FastEntries& ent, const Fa
 #pragma unroll
   for (int q = 0; q < NA; ++q) {
     const float sum = warp_sum(acc[q]);
-    const float self_q = __shfl_sync(0xffffffffu, self_k, q);
+    const float self_q = LOO_ID ? 0.f : __shfl_sync(0xffffffffu, self_k, q);
     if (lane == 0) out(__ldg(anc.idx + p + q), (double)(sum - self_q));
   }
 }
 
-// Anchor cells of the tiles with more than kTileAncCap anchors (the tiled kernel set *overflow).
-template <bool TAU_ALL, class Out>
-__global__ void __launch_bounds__(256) k_pair_fwd_overflow(FastEntries ent, FastAnchors anc,
+// Anchor cells of the tiles with more than kTileAncCap anchors (the tiled kernel set kOverflowTiles), or of
+// every tile when the caller set kOverflowAll.
+template <bool TAU_ALL, bool LOO_ID, class E, typename CS, class Out>
+__global__ void __launch_bounds__(256) k_pair_fwd_overflow(E ent, FastAnchors anc, const long long* __restrict__ AID,
                                                            const int* __restrict__ astart,
-                                                           const int* __restrict__ cstart, TileGrid G,
+                                                           const CS* __restrict__ cstart, TileGrid G,
                                                            const float* __restrict__ SC, PairConsts C, PlanConsts P,
                                                            const float4* __restrict__ ev4, Out out,
                                                            const int* __restrict__ overflow) {
-  if (*overflow == 0) return;
+  const int flags = *overflow;
+  if (flags == 0) return;
+  const bool all = LOO_ID && (flags & kOverflowAll);
   const int lane = threadIdx.x & 31;
   const long long ncell = (long long)G.B * G.S * G.GH * G.GW;
   const long long nwarps = ((long long)gridDim.x * blockDim.x) >> 5;
@@ -459,12 +501,13 @@ __global__ void __launch_bounds__(256) k_pair_fwd_overflow(FastEntries ent, Fast
     const int g = row / GH, cy = row - g * GH;
     const int b = g / G.S, s = g - b * G.S;
     const int gbase = g * GH * GW;
-    // the cell's tile and its anchor count, as the tiled kernel saw it
-    const int tx0 = (cx >> kTileXLog) << kTileXLog, ty0 = (cy / kTileY) * kTileY;
-    const int tx1 = min(tx0 + kTileX, GW), ty1 = min(ty0 + kTileY, GH);
-    int na = 0;
-    for (int y = ty0; y < ty1; ++y) na += astart[gbase + y * GW + tx1] - astart[gbase + y * GW + tx0];
-    if (na <= kTileAncCap) continue;
+    if (!all) {  // the cell's tile and its anchor count, as the tiled kernel saw it
+      const int tx0 = (cx >> kTileXLog) << kTileXLog, ty0 = (cy / kTileY) * kTileY;
+      const int tx1 = min(tx0 + kTileX, GW), ty1 = min(ty0 + kTileY, GH);
+      int na = 0;
+      for (int y = ty0; y < ty1; ++y) na += astart[gbase + y * GW + tx1] - astart[gbase + y * GW + tx0];
+      if (na <= kTileAncCap) continue;
+    }
     const int xl = max(cx - 1, 0), xh = min(cx + 1, GW - 1) + 1;
     int lo[3], hi[3];
 #pragma unroll
@@ -472,8 +515,8 @@ __global__ void __launch_bounds__(256) k_pair_fwd_overflow(FastEntries ent, Fast
       const int y = cy - 1 + r;
       int l = 0, h = 0;
       if (y >= 0 && y < GH) {
-        l = cstart[gbase + y * GW + xl];
-        h = cstart[gbase + y * GW + xh];
+        l = (int)cstart[gbase + y * GW + xl];
+        h = (int)cstart[gbase + y * GW + xh];
       }
       lo[r] = l;
       hi[r] = h;
@@ -481,11 +524,15 @@ __global__ void __launch_bounds__(256) k_pair_fwd_overflow(FastEntries ent, Fast
     const float cs = __ldg(SC + s);
     for (int p = a0; p < a1; p += 8) {
       switch (min(8, a1 - p)) {
-#define ATLB_OVF(n) \
-  case n: fwd_group_cells<n, TAU_ALL>(ent, anc, p, lo, hi, cs, C, P, ev4, b, s, cx, cy, out, lane); break;
+#define ATLB_OVF(n)                                                                                     \
+  case n:                                                                                               \
+    fwd_group_cells<n, TAU_ALL, LOO_ID>(ent, anc, AID, p, lo, hi, cs, C, P, ev4, b, s, cx, cy, out, lane); \
+    break;
         ATLB_OVF(8) ATLB_OVF(7) ATLB_OVF(6) ATLB_OVF(5) ATLB_OVF(4) ATLB_OVF(3) ATLB_OVF(2)
 #undef ATLB_OVF
-        default: fwd_group_cells<1, TAU_ALL>(ent, anc, p, lo, hi, cs, C, P, ev4, b, s, cx, cy, out, lane); break;
+        default:
+          fwd_group_cells<1, TAU_ALL, LOO_ID>(ent, anc, AID, p, lo, hi, cs, C, P, ev4, b, s, cx, cy, out, lane);
+          break;
       }
     }
   }
@@ -495,19 +542,23 @@ __global__ void __launch_bounds__(256) k_pair_fwd_overflow(FastEntries ent, Fast
 // One warp per source cell (grid: x = groups of 8 cells of a cell row, y = cell rows of all (batch, slice)
 // grids), lanes over the cell's entries in chunks of 32.  The anchors of the 3 neighbouring cell rows are
 // read as warp-uniform broadcast loads through L1 from records prepared once per backward:
-// AB = (x, y, t - c_s, t) and GB = dL/dS / h^2, in bucket order.
-template <bool TAU_ALL>
-__global__ void __launch_bounds__(256) k_pair_bwd_cells(FastEntries ent, const float4* __restrict__ AB,
-                                                        const float* __restrict__ GB, const int* __restrict__ astart,
-                                                        const int* __restrict__ cstart, int GW, int GH, int nrows,
-                                                        PairConsts C, long long N, float* __restrict__ gv) {
+// AB = (x, y, t - c_s, t) and GB = dL/dS / h^2, in bucket order.  Leave-one-out: the anchor's own pair has
+// dt = 0 and adds nothing in the fused layout; with LOO_ID the pair is excluded by comparing the entry's id
+// with the anchor's (GID, bucket order), as the reference does.
+template <bool TAU_ALL, bool LOO_ID, class E, typename CS>
+__global__ void __launch_bounds__(256) k_pair_bwd_cells(E ent, const float4* __restrict__ AB,
+                                                        const float* __restrict__ GB,
+                                                        const long long* __restrict__ GID,
+                                                        const int* __restrict__ astart, const CS* __restrict__ cstart,
+                                                        int GW, int GH, int nrows, PairConsts C, long long N,
+                                                        float* __restrict__ gv) {
   const int lane = threadIdx.x & 31;
   const int cx = blockIdx.x * 8 + (threadIdx.x >> 5);
   if (cx >= GW) return;
   for (int row = blockIdx.y; row < nrows; row += gridDim.y) {  // row = (b * S + s) * GH + cy
   const int cy = row % GH;
   const int c = row * GW + cx;
-  const int k0 = cstart[c], k1 = cstart[c + 1];
+  const int k0 = (int)cstart[c], k1 = (int)cstart[c + 1];
   if (k0 == k1) continue;
   const int gbase = (row - cy) * GW;
   const int xl = max(cx - 1, 0), xh = min(cx + 1, GW - 1) + 1;
@@ -529,7 +580,7 @@ __global__ void __launch_bounds__(256) k_pair_bwd_cells(FastEntries ent, const f
     const bool valid = k < k1;
     float2 sy, sv;
     float st;
-    int sid;
+    typename E::Id sid;
     ent.load(valid ? k : k0, sy, sv, st, sid);
     const f32x2 y = pk2(sy.x, sy.y), v = pk2(sv.x, sv.y);
     float gx = 0.f, gy = 0.f;
@@ -545,12 +596,14 @@ __global__ void __launch_bounds__(256) k_pair_bwd_cells(FastEntries ent, const f
         const float dt = sub_rn(a.w, st);
         bool ok = !(d2 > C.r2max);
         if (!TAU_ALL) ok = ok && !(fabsf(dt) > C.tau);
+        if (LOO_ID) ok = ok && (long long)sid != __ldg(GID + p);
         const float f = ok ? ga * ex2_approx(-d2 * C.k2) * dt : 0.f;  // gS k dt / h^2
         gx = fmaf(f, rr.x, gx);
         gy = fmaf(f, rr.y, gy);
       }
     }
-    if (valid && (gx != 0.f || gy != 0.f) && sid >= 0 && sid < N) red_add_f2(gv + 2 * (long long)sid, gx, gy);
+    if (valid && (gx != 0.f || gy != 0.f) && sid >= 0 && (long long)sid < N)
+      red_add_f2(gv + 2 * (long long)sid, gx, gy);
   }
   }
 }
