@@ -294,18 +294,29 @@ __global__ void __launch_bounds__(kThreads) k_fast_anchor_count(PlanConsts P, co
   }
 }
 
-__global__ void __launch_bounds__(kThreads) k_fast_anchor_scatter(PlanConsts P, const float4* __restrict__ anc4,
+// Anchor records in cell order: XT = (x, y, t, the anchor's own pair value) and BI = original index.  The own
+// pair (leave-one-out) is evaluated here once per anchor, with every lane busy, rather than in the pair kernel.
+__global__ void __launch_bounds__(kThreads) k_fast_anchor_scatter(PlanConsts P, PairConsts C,
+                                                                  const float4* __restrict__ anc4,
                                                                   const long long* __restrict__ anc_b, long long M,
+                                                                  const float4* __restrict__ ev4,
+                                                                  const float* __restrict__ SC,
                                                                   const int* __restrict__ start,
                                                                   int* __restrict__ cursor, float4* __restrict__ XT,
                                                                   int* __restrict__ BI) {
   const long long stride = (long long)gridDim.x * blockDim.x;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < M; i += stride) {
     const float4 a = anc4[i];
-    const long long key = fast_anchor_key(P, a, anc_b[i]);
-    if (key < 0) continue;
+    const long long ba = anc_b[i];
+    if (__float_as_int(a.w) < 0 || ba < 0 || ba >= P.B) continue;  // as fast_anchor_key
+    long long g, cx, cy;
+    anchor_cell(P, a.x, a.y, a.z, ba, &g, &cx, &cy);
+    const long long key = (g * P.GH + cy) * P.GW + cx;
     const int p = start[key] + atomicAdd(cursor + key, 1);
-    XT[p] = a;
+    const int s = (int)(g - ba * P.S);
+    const float self = self_term(P, C, ev4, __float_as_int(a.w), a.x, a.y, a.z, sub_rn(a.z, SC[s]), (int)ba, s,
+                                 (int)cx, (int)cy);
+    XT[p] = make_float4(a.x, a.y, a.z, self);
     BI[p] = (int)i;
   }
 }
@@ -648,8 +659,9 @@ int exact_forward(const atlb_exact_cfg& c, const float* t, const long long* b, l
            ns, (const int*)w.KEY, (const int*)w.start, w.counts, w.YV, w.TI);
   exclusive_scan<int>(w.acounts, ncell, w.partials, w.astart, s);
   if (M > 0)
-    launch(k_fast_anchor_scatter, grid_for(M), kThreads, 0, s, P, (const float4*)anc4, anc_b, M,
-           (const int*)w.astart, w.acounts, w.XT, w.BI);
+    launch(k_fast_anchor_scatter, grid_for(M), kThreads, 0, s, P, make_pair_consts(c.h, c.tau, c.cut),
+           (const float4*)anc4, anc_b, M, (const float4*)ev4, (const float*)w.SC, (const int*)w.astart, w.acounts,
+           w.XT, w.BI);
   // normaliser
   const MotionView Mv = motion_of(c);
   NormConsts K;
@@ -691,22 +703,22 @@ int exact_forward(const atlb_exact_cfg& c, const float* t, const long long* b, l
     const FusedOut out{S_out, ls_out, den_out, eps};
     cudaMemsetAsync(w.scratch, 0, sizeof(int), s);
     cudaEvent_t e0 = timing_begin(s);
+    const int* as = (const int*)w.astart;
+    const int* cs = (const int*)w.start;
+    const float* sc = (const float*)w.SC;
     if (tau_covers(g, c.tau))
-      launch(k_pair_fwd_tiled<true, false, FastEntries, int, FusedOut>, grid, kTileThreads, smem_no_t, s, E, A, (const int*)w.astart,
-             (const int*)w.start, T, (const float*)w.SC, C, P, (const float4*)ev4, out, w.scratch);
+      launch(k_pair_fwd_tiled<true, false, FastEntries, int, FusedOut>, grid, kTileThreads, smem_no_t, s, E, A, as, cs,
+             T, sc, C, out, w.scratch);
     else
-      launch(k_pair_fwd_tiled<false, false, FastEntries, int, FusedOut>, grid, kTileThreads, smem_all, s, E, A,
-             (const int*)w.astart, (const int*)w.start, T, (const float*)w.SC, C, P, (const float4*)ev4, out,
-             w.scratch);
+      launch(k_pair_fwd_tiled<false, false, FastEntries, int, FusedOut>, grid, kTileThreads, smem_all, s, E, A, as, cs,
+             T, sc, C, out, w.scratch);
     // cells of tiles with more anchors than the tiled kernel stages (dense windows)
     if (tau_covers(g, c.tau))
-      launch(k_pair_fwd_overflow<true, false, FastEntries, int, FusedOut>, warp_grid(ncell), 256, 0, s, E, A,
-             nullptr, (const int*)w.astart,
-             (const int*)w.start, T, (const float*)w.SC, C, P, (const float4*)ev4, out, (const int*)w.scratch);
+      launch(k_pair_fwd_overflow<true, false, FastEntries, int, FusedOut>, warp_grid(ncell), 256, 0, s, E, A, nullptr,
+             as, cs, T, sc, C, out, (const int*)w.scratch);
     else
-      launch(k_pair_fwd_overflow<false, false, FastEntries, int, FusedOut>, warp_grid(ncell), 256, 0, s, E, A,
-             nullptr, (const int*)w.astart,
-             (const int*)w.start, T, (const float*)w.SC, C, P, (const float4*)ev4, out, (const int*)w.scratch);
+      launch(k_pair_fwd_overflow<false, false, FastEntries, int, FusedOut>, warp_grid(ncell), 256, 0, s, E, A, nullptr,
+             as, cs, T, sc, C, out, (const int*)w.scratch);
     timing_end("k_pair_fwd", s, e0);
   }
   return launch_status("exact_forward");

@@ -240,7 +240,7 @@ int pair_fwd_ws(const float* SY, const float* SV, const float* ST, const long lo
   TileGrid T;
   if (M > 0 && ncell > 0 && tiled_grid(Ns, ncell, S, GH, GW, &T)) {
     using Tiled = void (*)(RefEntries, FastAnchors, const int*, const long long*, TileGrid, const float*, PairConsts,
-                           PlanConsts, const float4*, DirectOut, int*);
+                           DirectOut, int*);
     const Tiled tiled = k_pair_fwd_tiled<false, true, RefEntries, long long, DirectOut>;
     if (first_use_on_device(g_ref_fwd_attr))  // the opt-in above 48 KB is a per-device attribute
       cudaFuncSetAttribute(tiled, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(TileSmemFwd));
@@ -251,13 +251,12 @@ int pair_fwd_ws(const float* SY, const float* SV, const float* ST, const long lo
     launch(k_anchor_records_fwd, clamp_grid(blocks_for(M, kThreads)), kThreads, 0, s, AC, (const float2*)AX, AT, AID,
            M, S, GH, GW, ncell, (const int*)w.start, w.counts, w.rec, w.idx, out);
     const FastAnchors A{w.rec, w.idx};
-    const PlanConsts P{};
     const dim3 grid((unsigned)((GW + kTileX - 1) / kTileX), (unsigned)((GH + kTileY - 1) / kTileY), (unsigned)S);
     cudaEvent_t e0 = timed ? timing_begin(s) : nullptr;
-    launch(tiled, grid, kTileThreads, sizeof(TileSmemFwd), s, E, A, (const int*)w.start, CS, T, SC, C, P,
-           (const float4*)nullptr, DirectOut{out}, w.flags);
+    launch(tiled, grid, kTileThreads, sizeof(TileSmemFwd), s, E, A, (const int*)w.start, CS, T, SC, C, DirectOut{out},
+           w.flags);
     launch(k_pair_fwd_overflow<false, true, RefEntries, long long, DirectOut>, warp_grid(ncell), 256, 0, s, E, A, AID,
-           (const int*)w.start, CS, T, SC, C, P, (const float4*)nullptr, DirectOut{out}, (const int*)w.flags);
+           (const int*)w.start, CS, T, SC, C, DirectOut{out}, (const int*)w.flags);
     if (timed) timing_end("k_pair_fwd", s, e0);
     return ATLB_OK;
   }

@@ -210,6 +210,34 @@ __device__ __forceinline__ void stage_entry(const RefEntries& e, float4* dyv, fl
   }
 }
 
+// Warp sums of NA (<= 8) values at once, by a transposing butterfly: each exchange step halves the values a lane
+// holds, so NA sums cost about as many shuffles as two.  On return lane q * (32 / NP) holds the total of v[q]
+// (NP = NA rounded up to a power of two); the other lanes hold partial sums.
+template <int NA>
+constexpr int sum_lane_stride() {
+  return 32 / (NA <= 1 ? 1 : NA <= 2 ? 2 : NA <= 4 ? 4 : 8);
+}
+template <int NA>
+__device__ __forceinline__ float warp_sum_many(const float (&v)[NA], int lane) {
+  constexpr int NP = 32 / sum_lane_stride<NA>();
+  float w[NP];
+#pragma unroll
+  for (int i = 0; i < NP; ++i) w[i] = i < NA ? v[i] : 0.f;
+#pragma unroll
+  for (int cnt = NP, off = 16; cnt > 1; cnt >>= 1, off >>= 1) {
+    const bool upper = (lane & off) != 0;
+#pragma unroll
+    for (int i = 0; i < cnt / 2; ++i) {
+      const float send = upper ? w[i] : w[i + cnt / 2];
+      const float keep = upper ? w[i + cnt / 2] : w[i];
+      w[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+    }
+  }
+#pragma unroll
+  for (int off = 16 / NP; off > 0; off >>= 1) w[0] += __shfl_xor_sync(0xffffffffu, w[0], off);
+  return w[0];
+}
+
 // Leave-one-out: anchor a's own event appears among the candidates iff its entry of slice s exists and its
 // cell lies in the anchor's 3x3 cells; returns that entry's (bit-identical) kernel value, else 0.
 __device__ __forceinline__ float self_term(const PlanConsts& P, const PairConsts& C, const float4* __restrict__ ev4,
@@ -234,23 +262,17 @@ __device__ __forceinline__ float self_term(const PlanConsts& P, const PairConsts
 }
 
 // ---- forward -----------------------------------------------------------------------------------------
-// LOO_ID: leave-one-out by comparing event ids per pair (the reference's plan layout, where an anchor's own
-// entry cannot be located); otherwise the anchor's own pair is recomputed and subtracted (self_term).
+// Anchor records (x, y, t, w).  Fused layout: w = the anchor's own pair value, self_term() evaluated once per
+// anchor when the records are built, subtracted from the sum.  LOO_ID (the reference's plan layout, where an
+// anchor's own entry cannot be located): w = the low 32 bits of the anchor's id, and pairs are excluded by
+// comparing ids.
 template <int NA, bool TAU_ALL, bool LOO_ID, bool STAGED, class E, class Out>
 __device__ __forceinline__ void fwd_group_tile(const TileSmemFwd& sm, int p, const E& ent, const int* lo,
-                                               const int* hi, float cs, const PairConsts& C, const PlanConsts& P,
-                                               const float4* __restrict__ ev4, int b, int s, int cx, int cy, Out& out,
-                                               int lane) {
+                                               const int* hi, float cs, const PairConsts& C, Out& out, int lane) {
   constexpr bool kTI = !TAU_ALL || LOO_ID;  // entry times / ids needed
   f32x2 axy[NA], adt2[NA];
   float at[NA], acc[NA];
   int aid[NA];
-  // lane q < NA evaluates anchor q's leave-one-out term; its latency overlaps the candidate loop
-  float self_k = 0.f;
-  if (!LOO_ID && lane < NA) {
-    const float4 a = sm.anc[p + lane];
-    self_k = self_term(P, C, ev4, __float_as_int(a.w), a.x, a.y, a.z, sub_rn(a.z, cs), b, s, cx, cy);
-  }
 #pragma unroll
   for (int q = 0; q < NA; ++q) {
     const float4 a = sm.anc[p + q];
@@ -296,12 +318,10 @@ __device__ __forceinline__ void fwd_group_tile(const TileSmemFwd& sm, int p, con
       }
     }
   }
-#pragma unroll
-  for (int q = 0; q < NA; ++q) {
-    const float sum = warp_sum(acc[q]);
-    const float self_q = LOO_ID ? 0.f : __shfl_sync(0xffffffffu, self_k, q);
-    if (lane == 0) out(sm.aidx[p + q], (double)(sum - self_q));
-  }
+  const float sum = warp_sum_many<NA>(acc, lane);
+  constexpr int kStride = sum_lane_stride<NA>();
+  const int q = lane / kStride;
+  if (lane % kStride == 0 && q < NA) out(sm.aidx[p + q], (double)(LOO_ID ? sum : sum - sm.anc[p + q].w));
 }
 
 // Bits of the overflow word shared by the tiled and untiled forward kernels.
@@ -314,9 +334,8 @@ template <bool TAU_ALL, bool LOO_ID, class E, typename CS, class Out>
 __global__ void __launch_bounds__(kTileThreads) k_pair_fwd_tiled(E ent, FastAnchors anc,
                                                                  const int* __restrict__ astart,
                                                                  const CS* __restrict__ cstart, TileGrid G,
-                                                                 const float* __restrict__ SC, PairConsts C,
-                                                                 PlanConsts P, const float4* __restrict__ ev4,
-                                                                 Out out, int* __restrict__ overflow) {
+                                                                 const float* __restrict__ SC, PairConsts C, Out out,
+                                                                 int* __restrict__ overflow) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   TileSmemFwd& sm = *reinterpret_cast<TileSmemFwd*>(smem_raw);
   if (LOO_ID && (*overflow & kOverflowAll)) return;  // ids beyond 32 bits: every cell goes to the untiled kernel
@@ -398,8 +417,7 @@ __global__ void __launch_bounds__(kTileThreads) k_pair_fwd_tiled(E ent, FastAnch
       const int nrows = neighbour_rows(t, gbase, GW, GH, t.tx0 + cxo, t.ty0 + cyo, staged, sm.cell_off, cstart, lo, hi);
       const int na_g = min(4, p1 - p);
       const int cx = t.tx0 + cxo, cy = t.ty0 + cyo;
-#define ATLB_GROUP(n, st) \
-  fwd_group_tile<n, TAU_ALL, LOO_ID, st>(sm, p, ent, lo, hi, cs, C, P, ev4, b, s, cx, cy, out, lane)
+#define ATLB_GROUP(n, st) fwd_group_tile<n, TAU_ALL, LOO_ID, st>(sm, p, ent, lo, hi, cs, C, out, lane)
       if (staged) {
         switch (na_g) {
           case 4: ATLB_GROUP(4, true); break;
@@ -428,17 +446,10 @@ __global__ void __launch_bounds__(kTileThreads) k_pair_fwd_tiled(E ent, FastAnch
 template <int NA, bool TAU_ALL, bool LOO_ID, class E, class Out>
 __device__ __forceinline__ void fwd_group_cells(const E& ent, const FastAnchors& anc,
                                                 const long long* __restrict__ AID, int p, const int* lo,
-                                                const int* hi, float cs, const PairConsts& C, const PlanConsts& P,
-                                                const float4* __restrict__ ev4, int b, int s, int cx, int cy,
-                                                Out& out, int lane) {
+                                                const int* hi, float cs, const PairConsts& C, Out& out, int lane) {
   f32x2 axy[NA], adt2[NA];
   float at[NA], acc[NA];
   long long aid[NA];
-  float self_k = 0.f;
-  if (!LOO_ID && lane < NA) {
-    const float4 a = __ldg(anc.XT + p + lane);
-    self_k = self_term(P, C, ev4, __float_as_int(a.w), a.x, a.y, a.z, sub_rn(a.z, cs), b, s, cx, cy);
-  }
 #pragma unroll
   for (int q = 0; q < NA; ++q) {
     const float4 a = __ldg(anc.XT + p + q);
@@ -470,12 +481,11 @@ __device__ __forceinline__ void fwd_group_cells(const E& ent, const FastAnchors&
       }
     }
   }
-#pragma unroll
-  for (int q = 0; q < NA; ++q) {
-    const float sum = warp_sum(acc[q]);
-    const float self_q = LOO_ID ? 0.f : __shfl_sync(0xffffffffu, self_k, q);
-    if (lane == 0) out(__ldg(anc.idx + p + q), (double)(sum - self_q));
-  }
+  const float sum = warp_sum_many<NA>(acc, lane);
+  constexpr int kStride = sum_lane_stride<NA>();
+  const int q = lane / kStride;
+  if (lane % kStride == 0 && q < NA)
+    out(__ldg(anc.idx + p + q), (double)(LOO_ID ? sum : sum - __ldg(&anc.XT[p + q].w)));
 }
 
 // Anchor cells of the tiles with more than kTileAncCap anchors (the tiled kernel set kOverflowTiles), or of
@@ -484,8 +494,7 @@ template <bool TAU_ALL, bool LOO_ID, class E, typename CS, class Out>
 __global__ void __launch_bounds__(256) k_pair_fwd_overflow(E ent, FastAnchors anc, const long long* __restrict__ AID,
                                                            const int* __restrict__ astart,
                                                            const CS* __restrict__ cstart, TileGrid G,
-                                                           const float* __restrict__ SC, PairConsts C, PlanConsts P,
-                                                           const float4* __restrict__ ev4, Out out,
+                                                           const float* __restrict__ SC, PairConsts C, Out out,
                                                            const int* __restrict__ overflow) {
   const int flags = *overflow;
   if (flags == 0) return;
@@ -524,15 +533,11 @@ __global__ void __launch_bounds__(256) k_pair_fwd_overflow(E ent, FastAnchors an
     const float cs = __ldg(SC + s);
     for (int p = a0; p < a1; p += 8) {
       switch (min(8, a1 - p)) {
-#define ATLB_OVF(n)                                                                                     \
-  case n:                                                                                               \
-    fwd_group_cells<n, TAU_ALL, LOO_ID>(ent, anc, AID, p, lo, hi, cs, C, P, ev4, b, s, cx, cy, out, lane); \
-    break;
+#define ATLB_OVF(n) \
+  case n: fwd_group_cells<n, TAU_ALL, LOO_ID>(ent, anc, AID, p, lo, hi, cs, C, out, lane); break;
         ATLB_OVF(8) ATLB_OVF(7) ATLB_OVF(6) ATLB_OVF(5) ATLB_OVF(4) ATLB_OVF(3) ATLB_OVF(2)
 #undef ATLB_OVF
-        default:
-          fwd_group_cells<1, TAU_ALL, LOO_ID>(ent, anc, AID, p, lo, hi, cs, C, P, ev4, b, s, cx, cy, out, lane);
-          break;
+        default: fwd_group_cells<1, TAU_ALL, LOO_ID>(ent, anc, AID, p, lo, hi, cs, C, out, lane); break;
       }
     }
   }
