@@ -230,6 +230,41 @@ class ClockSampler:
 PROFILE_SUMMARY = ROOT / "profiles" / "pair_kernels.config2_1M.md"
 
 
+def candidate_pairs(plan) -> int:
+    """Anchor-candidate pairs the pair kernels evaluate: for every anchor, the plan entries of the 3x3 cells
+    around its cell (clipped to the grid).  Every candidate runs the acceptance test and one exp2."""
+    import torch
+    cnt = plan.cell_start[1:] - plan.cell_start[:-1]
+    g = cnt.view(-1, plan.GH, plan.GW).to(torch.float64)
+    pad = torch.nn.functional.pad(g, (1, 1, 1, 1))
+    nb = sum(pad[:, 1 + dy:1 + dy + plan.GH, 1 + dx:1 + dx + plan.GW] for dy in (-1, 0, 1) for dx in (-1, 0, 1))
+    ac = plan.anc_cell
+    return int(nb[ac[:, 0], ac[:, 2], ac[:, 1]].sum().item())
+
+
+# FP32 lane operations per candidate pair, counted from the arithmetic the kernels must do for the reference's
+# exactly rounded test: r = x_i - (y_j + v_j dt_i) (2 mul, 2 add, 2 sub), d^2 = rx^2 + ry^2 (2 mul, 1 add),
+# the d^2 test, the exponent scale and the accumulation (forward: 12); the backward adds dt = t_i - t_j,
+# gS k, (.) dt and the two gradient multiply-adds (16).  One exp2 per candidate in both.
+FP32_OPS_PER_CANDIDATE = {"k_pair_fwd": 12, "k_pair_bwd": 16}
+
+
+def compute_roofline(kernel, candidates, entries, alg_bytes, avg_ms, rates):
+    """T_roof = max(bytes / HBM, fp32 / FP32 rate, exp2 / SFU rate, reductions / red rate) for one pair kernel,
+    with the rates measured on this GPU; frac = T_roof / the kernel's CUDA-event time."""
+    hbm, _ = measured_peak()
+    fp32_rate = max(rates["fp32_lane_ops"], rates["fp32x2_lane_ops"])
+    terms = {"hbm": alg_bytes / (hbm * 1e9), "fp32": candidates * FP32_OPS_PER_CANDIDATE[kernel] / fp32_rate,
+             "sfu": candidates / rates["ex2"]}
+    if kernel == "k_pair_bwd":
+        terms["red"] = entries / rates["red_v4"]  # one red.global.add.v2.f32 per plan entry at most
+    bound = max(terms, key=terms.get)
+    t_roof = terms[bound]
+    return {"bound": bound, "t_roof_ms": t_roof * 1e3, "t_measured_ms": avg_ms, "frac": t_roof / (avg_ms * 1e-3),
+            "terms_ms": {k: v * 1e3 for k, v in terms.items()}, "candidates": candidates,
+            "fp32_lane_ops_per_candidate": FP32_OPS_PER_CANDIDATE[kernel], "exp2_per_candidate": 1}
+
+
 def profiled_traffic(kernel):
     """DRAM bytes (read + write) per launch of ``kernel`` from the committed ncu summary of this workload
     (a line ``traffic <kernel> <bytes>``), or None."""
@@ -371,9 +406,9 @@ def ours_arm(args):
     if rank != 0:
         return
     # ---- roofline of the dominant kernel.  Algorithmic bytes of the fused path's compact layout:
-    # forward (tau covering the window): per plan entry its (y, v) float4; per anchor its (x, y, t, id)
-    # float4, its event's (x, v) float4 for the self term and S out.  Backward: per plan entry (y, v) +
-    # (t, id) = 24 B; per anchor (x, y, t, id) + dL/dS = 20 B; per event its (gx, gy) out.
+    # forward (tau covering the window): per plan entry its (y, v) float4; per anchor its (x, y, t, self)
+    # record and original index, den in, S and ls out.  Backward: per plan entry (y, v) + (t, id) = 24 B;
+    # per anchor (x, y, t - c_s, t) + dL/dS = 20 B; per event its (gx, gy) out.
     dom = max(ktime, key=lambda k: ktime[k][0])
     dom_ms, dom_n = ktime[dom]
     with torch.no_grad():
@@ -383,10 +418,14 @@ def ours_arm(args):
         v = m.velocity(xs, ev.t, ev.b)
         plan = F.build_pair_plan(xs, ev.t, v, ev.b, 1, H, W, anchors, 1.0, 1.0, 3.0, 16, anchor_xy=xa)
         Ns, M = plan.src_y.shape[0], plan.anc_x.shape[0]
+        cand = candidate_pairs(plan)
         del plan
-    alg = {"k_pair_fwd": Ns * 16 + M * (16 + 16 + 4), "k_pair_bwd": Ns * 24 + M * 20 + args.events * 8}
+    alg = {"k_pair_fwd": Ns * 16 + M * (16 + 4 + 4 + 8), "k_pair_bwd": Ns * 24 + M * 20 + args.events * 8}
     if args.dropin:  # the reference's plan layout: (y, v, t, int64 id) 28 B per entry, anchors bucketed 28 B
         alg = {"k_pair_fwd": Ns * 28 + M * 32, "k_pair_bwd": Ns * 28 + M * 32 + args.events * 8}
+    rates = _lib.unit_rates(dev)
+    compute = {k: compute_roofline(k, cand, Ns, alg[k], ktime[k][0] / max(ktime[k][1], 1), rates)
+               for k in ("k_pair_fwd", "k_pair_bwd")}
     alg_bytes = alg[dom]
     avg_ms = dom_ms / max(dom_n, 1)
     peak, peak_kind = measured_peak()
@@ -405,6 +444,8 @@ def ours_arm(args):
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "traffic": traffic, "kernel": dom, "avg_launch_ms": avg_ms, "algorithmic_bytes": alg_bytes,
                      "peak_source": peak_kind, "traffic_source": PROFILE_SUMMARY.name if traffic else None},
+        "roofline_compute": compute,
+        "unit_rates": {**{k: v for k, v in rates.items()}, "source": "atlb_measure_unit_rates on this GPU, after the timed region"},
         "kernels_ms_per_step": {k: v[0] / max(v[1], 1) for k, v in ktime.items()},
         "e2e": {"value": world * args.events / (e2e_ms / 1000), "unit": "events/s", "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4,

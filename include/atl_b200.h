@@ -38,7 +38,7 @@ enum {
 const char* atlb_last_error(void);
 /* ABI version of this header (bumped on incompatible changes). */
 int atlb_abi_version(void);
-#define ATLB_ABI_VERSION 6
+#define ATLB_ABI_VERSION 7
 /* Number of kernels this library has launched in the calling process (instrumentation; no reference
  * counterpart). */
 uint64_t atlb_kernel_launches(void);
@@ -48,6 +48,23 @@ uint64_t atlb_kernel_launches(void);
  * for `name` (reset != 0 forgets them). */
 int atlb_timing_enable(int on);
 int atlb_timing_read(const char* name, double* total_ms, int64_t* count, int reset);
+
+/* Execution-unit rates of the current device (instrumentation; no reference counterpart): the
+ * denominators of the compute roofline of the pair and splat kernels.  Each figure is whole-device
+ * operations per second, from a CUDA-event-timed kernel that runs independent chains of that one
+ * operation on every SM, after an identical warm-up launch.  Blocking: returns when the measurement
+ * kernels (about 10 ms) have finished on `stream`.  scratch: atlb_unit_rates_scratch_bytes() bytes of
+ * device memory, overwritten. */
+typedef struct {
+  double fp32_lane_ops;   /* fma.rn.f32: lane operations per second */
+  double fp32x2_lane_ops; /* fma.rn.f32x2: lane operations per second (two per instruction and lane) */
+  double ex2;             /* ex2.approx.ftz.f32 per second */
+  double red_f32;         /* red.global.add.f32 at scattered words of an L2-resident 32 MB buffer */
+  double red_v4;          /* red.global.add.v4.f32 at scattered 16-byte quads of the same buffer */
+  double smem_atomic;     /* atomicAdd on scattered shared-memory floats */
+} atlb_unit_rates;
+size_t atlb_unit_rates_scratch_bytes(void);
+int atlb_measure_unit_rates(atlb_unit_rates* out, void* scratch, size_t scratch_bytes, atlb_stream_t stream);
 
 /* ----------------------------------------------------------------------------------------------
  * Splat / gather / voxel.  Replace the reference's bound kernels

@@ -37,6 +37,11 @@ class ExactCfg(ctypes.Structure):
                 ("n_check", ctypes.c_int64), ("src_begin", ctypes.c_int64), ("src_end", ctypes.c_int64)]
 
 
+class UnitRates(ctypes.Structure):
+    _fields_ = [("fp32_lane_ops", ctypes.c_double), ("fp32x2_lane_ops", ctypes.c_double), ("ex2", ctypes.c_double),
+                ("red_f32", ctypes.c_double), ("red_v4", ctypes.c_double), ("smem_atomic", ctypes.c_double)]
+
+
 # name -> (restype, argtypes)
 _SIGS = {
     "atlb_last_error": (ctypes.c_char_p, []),
@@ -45,6 +50,8 @@ _SIGS = {
     "atlb_timing_enable": (_int, [_int]),
     "atlb_timing_read": (_int, [ctypes.c_char_p, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_int64),
                                 _int]),
+    "atlb_unit_rates_scratch_bytes": (_size, []),
+    "atlb_measure_unit_rates": (_int, [ctypes.POINTER(UnitRates), _vp, _size, _vp]),
     "atlb_splat_bilinear_fwd": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _vp]),
     "atlb_splat_bilinear_bwd": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _vp, _vp]),
     "atlb_splat_gauss_workspace_bytes": (_size, [_i64, _i64, _i64, _i64]),
@@ -143,6 +150,19 @@ def require_cuda(name: str, t: torch.Tensor, dtype=None):
 
 def workspace(nbytes: int, device) -> torch.Tensor:
     return torch.empty(max(int(nbytes), 1), dtype=torch.uint8, device=device)
+
+
+def unit_rates(device=None) -> dict:
+    """Execution-unit rates of the current (or given) CUDA device, operations per second (atlb_measure_unit_rates):
+    fp32_lane_ops, fp32x2_lane_ops, ex2, red_f32, red_v4, smem_atomic.  Blocks for about 10 ms."""
+    L = lib()
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    with torch.cuda.device(dev):
+        nb = L.atlb_unit_rates_scratch_bytes()
+        scratch = workspace(nb, dev)
+        r = UnitRates()
+        check(L.atlb_measure_unit_rates(ctypes.byref(r), ptr(scratch), nb, stream()), "measure_unit_rates")
+    return {name: float(getattr(r, name)) for name, _ in UnitRates._fields_}
 
 
 def timing_read(name: str, reset: bool = True):

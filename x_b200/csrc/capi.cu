@@ -39,6 +39,8 @@ int plan_fill(const float*, const float*, const float*, const long long*, long l
               const atlb_plan_geom*, const long long*, const float*, long long, const long long*, void*, float*,
               float*, float*, long long*, float*, float*, long long*, long long*, float*, cudaStream_t);
 size_t pair_workspace_bytes(long long M, long long ncell);
+size_t unit_rates_scratch_bytes();
+int measure_unit_rates(atlb_unit_rates*, void*, cudaStream_t);
 int pair_fwd(const float*, const float*, const float*, const long long*, const long long*, const float*, const float*,
              const long long*, const long long*, const float*, long long, long long, long long, long long, long long,
              long long, double, double, double, float*, void*, cudaStream_t);
@@ -130,6 +132,18 @@ extern "C" {
 const char* atlb_last_error(void) { return g_err; }
 int atlb_abi_version(void) { return ATLB_ABI_VERSION; }
 uint64_t atlb_kernel_launches(void) { return g_launches.load(std::memory_order_relaxed); }
+
+size_t atlb_unit_rates_scratch_bytes(void) { return unit_rates_scratch_bytes(); }
+
+int atlb_measure_unit_rates(atlb_unit_rates* out, void* scratch, size_t scratch_bytes, atlb_stream_t stream) {
+  clear();
+  if (!out) { set_error("atlb_measure_unit_rates: NULL out"); return ATLB_ERR_ARG; }
+  if (!scratch || scratch_bytes < unit_rates_scratch_bytes()) {
+    set_error("atlb_measure_unit_rates: scratch %zu < %zu bytes", scratch_bytes, unit_rates_scratch_bytes());
+    return ATLB_ERR_WORKSPACE;
+  }
+  return measure_unit_rates(out, scratch, STREAM(stream));
+}
 
 int atlb_splat_bilinear_fwd(const float* pos, const float* w, const int64_t* bidx, int64_t N, int64_t B, int64_t H,
                             int64_t W, float* img, atlb_stream_t stream) {

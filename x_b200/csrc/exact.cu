@@ -215,35 +215,43 @@ __global__ void __launch_bounds__(kThreads) k_order_scatter(PlanConsts P, const 
 }
 
 // Plan entry counts over the ordered events; one atomic per distinct cell of a warp.  Keys fit in int
-// (the cell count is checked against the int32 range by the caller).
+// (the cell count is checked against the int32 range by the caller).  One event per lane, its slices in an
+// inner loop: the event is read and its slice range computed once, not once per slice.
 __global__ void __launch_bounds__(kThreads) k_fast_count_ordered(PlanConsts P, const float4* __restrict__ XVo,
                                                                  const int4* __restrict__ TBo, long long N,
                                                                  int* __restrict__ counts, int* __restrict__ KEY) {
   const int lane = threadIdx.x & 31;
   const long long stride = (long long)gridDim.x * blockDim.x;
   const long long first = blockIdx.x * (long long)blockDim.x + (threadIdx.x & ~31);
-  for (int s = blockIdx.y; s < P.S; s += gridDim.y) {
-    for (long long i0 = first; i0 < N; i0 += stride) {  // warp-uniform loop
-      const long long i = i0 + lane;
+  for (long long i0 = first; i0 < N; i0 += stride) {  // warp-uniform loop
+    const long long i = i0 + lane;
+    const bool live = i < N;
+    int s_lo = 1, s_hi = 0;  // empty range for lanes past the end
+    float4 e = make_float4(0.f, 0.f, 0.f, 0.f);
+    float tj = 0.f;
+    long long bj = 0;
+    if (live) {
+      const int4 tb = TBo[i];
+      tj = __int_as_float(tb.x);
+      bj = tb.y;
+      slice_range(P, tj, &s_lo, &s_hi);
+      e = XVo[i];
+    }
+    for (int s = 0; s < P.S; ++s) {
       int key = -1;
-      if (i < N) {
-        const int4 tb = TBo[i];
-        const float tj = __int_as_float(tb.x);
-        int s_lo, s_hi;
-        slice_range(P, tj, &s_lo, &s_hi);
-        if (s >= s_lo && s <= s_hi) {
-          const float4 e = XVo[i];
-          float yx, yy;
-          key = (int)source_key(P, e.x, e.y, e.z, e.w, tj, tb.y, s, &yx, &yy);
-        }
-        KEY[(long long)s * N + i] = key;
+      if (s >= s_lo && s <= s_hi) {
+        float yx, yy;
+        key = (int)source_key(P, e.x, e.y, e.z, e.w, tj, bj, s, &yx, &yy);
       }
+      if (live) KEY[(long long)s * N + i] = key;
       const unsigned grp = __match_any_sync(0xffffffffu, key);
       if (key >= 0 && lane == __ffs(grp) - 1) atomicAdd(counts + key, __popc(grp));
     }
   }
 }
 
+// Entries of the ordered events: the count pass's keys, one cursor atomic per distinct cell of a warp, and
+// the lanes of a cell writing consecutive slots.  One event per lane, its slices in an inner loop.
 __global__ void __launch_bounds__(kThreads) k_fast_scatter_ordered(PlanConsts P, const float4* __restrict__ XVo,
                                                                    const int4* __restrict__ TBo, long long N,
                                                                    const int* __restrict__ KEY,
@@ -254,24 +262,31 @@ __global__ void __launch_bounds__(kThreads) k_fast_scatter_ordered(PlanConsts P,
   const unsigned below = (1u << lane) - 1u;
   const long long stride = (long long)gridDim.x * blockDim.x;
   const long long first = blockIdx.x * (long long)blockDim.x + (threadIdx.x & ~31);
-  for (int s = blockIdx.y; s < P.S; s += gridDim.y) {
-    for (long long i0 = first; i0 < N; i0 += stride) {  // warp-uniform loop
-      const long long i = i0 + lane;
-      const int key = i < N ? KEY[(long long)s * N + i] : -1;  // the count pass's keys
+  for (long long i0 = first; i0 < N; i0 += stride) {  // warp-uniform loop
+    const long long i = i0 + lane;
+    const bool live = i < N;
+    float4 e = make_float4(0.f, 0.f, 0.f, 0.f);
+    float tj = 0.f;
+    int id = 0;
+    if (live) {
+      const int4 tb = TBo[i];
+      tj = __int_as_float(tb.x);
+      id = tb.z;
+      e = XVo[i];
+    }
+    for (int s = 0; s < P.S; ++s) {
+      const int key = live ? KEY[(long long)s * N + i] : -1;  // the count pass's keys
       const unsigned grp = __match_any_sync(0xffffffffu, key);
       const int leader = __ffs(grp) - 1;
       int base = 0;
       if (key >= 0 && lane == leader) base = start[key] + atomicAdd(cursor + key, __popc(grp));
       base = __shfl_sync(0xffffffffu, base, leader);
       if (key >= 0) {
-        const int4 tb = TBo[i];
-        const float tj = __int_as_float(tb.x);
-        const float4 e = XVo[i];
         float yx, yy;
         transported(P, e.x, e.y, e.z, e.w, tj, s, &yx, &yy);
         const int p = base + __popc(grp & below);
         YV[p] = make_float4(yx, yy, e.z, e.w);
-        TI[p] = make_float2(tj, __int_as_float(tb.z));
+        TI[p] = make_float2(tj, __int_as_float(id));
       }
     }
   }
@@ -340,7 +355,34 @@ struct NormConsts {
   double tau;
   float tau_f, pi_f, h2_f, wmax, hmax;
   int n_check, visibility;
+  long long B;  // rows of the slice histogram
 };
+
+// Exposure-check tables staged per CTA: the check-slice centres and the per-batch slice counts as floats.
+constexpr int kNormMaxCheck = 64;
+constexpr int kNormMaxCounts = 2048;
+
+// visible_fraction_one with the centres and float counts read from tables: the same operations in the same
+// order, without recomputing each centre (an IEEE division and the linspace formula) and converting each
+// count per anchor.
+__device__ __forceinline__ float visible_fraction_tab(float2 v, float xa, float ya, float ta, const float* cen,
+                                                      const float* cnt_b, int n_check, float tau, float wmax,
+                                                      float hmax) {
+  float vis = 0.f, tot = 0.f;
+#pragma unroll 16
+  for (int k = 0; k < n_check; ++k) {
+    const float c = cen[k];
+    const float near = fabsf(sub_rn(ta, c)) <= tau ? 1.f : 0.f;
+    const float dt = sub_rn(c, ta);
+    const float yx = add_rn(xa, mul_rn(v.x, dt)), yy = add_rn(ya, mul_rn(v.y, dt));
+    const float inside = (yx >= 0.f && yx <= wmax && yy >= 0.f && yy <= hmax) ? 1.f : 0.f;
+    const float w = mul_rn(cnt_b[k], near);
+    vis = add_rn(vis, mul_rn(w, inside));
+    tot = add_rn(tot, w);
+  }
+  const float r = div_rn(vis, tot < 1.f ? 1.f : tot);
+  return r < 1e-3f ? 1e-3f : r;
+}
 
 // bstart[k] = first event of batch k (events sorted by b, b in [0, B)), bstart[B] = N.
 __global__ void __launch_bounds__(kThreads) k_batch_bounds(const long long* __restrict__ b, long long N, long long B,
@@ -360,12 +402,21 @@ __global__ void __launch_bounds__(kThreads) k_exact_norm(MotionView Mv, NormCons
                                                          const float* __restrict__ t, const long long* __restrict__ b,
                                                          long long N, const long long* __restrict__ bstart,
                                                          const int* __restrict__ counts, float* __restrict__ den) {
+  __shared__ float cen[kNormMaxCheck];
+  __shared__ float cntf[kNormMaxCounts];
+  const int nc = K.n_check;
+  const bool tab = K.visibility && nc <= kNormMaxCheck && K.B * nc <= kNormMaxCounts;  // CTA-uniform
+  if (tab) {
+    for (int k = threadIdx.x; k < nc; k += blockDim.x) cen[k] = check_centre(k, nc);
+    for (int k = threadIdx.x; k < (int)(K.B * nc); k += blockDim.x) cntf[k] = (float)counts[k];
+  }
+  __syncthreads();
   const long long stride = (long long)gridDim.x * blockDim.x;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < M; i += stride) {
     const float4 a = anc4[i];
     const int ai = __float_as_int(a.w);
     const long long ba = anc_b[i];
-    if (ai < 0 || ba < 0 || ba >= Mv.B) {
+    if (ai < 0 || ba < 0 || ba >= Mv.B || ba >= K.B) {
       den[i] = __int_as_float(0x7fc00000);
       continue;
     }
@@ -378,7 +429,10 @@ __global__ void __launch_bounds__(kThreads) k_exact_norm(MotionView Mv, NormCons
     }
     float wn = (float)(c > 0 ? c : 0);
     wn = wn < 1.f ? 1.f : wn;  // .clamp(min=1)
-    if (K.visibility)
+    if (tab)
+      wn = mul_rn(wn, visible_fraction_tab(motion_field(Mv, a.x, a.y, ba), a.x, a.y, a.z, cen, cntf + ba * nc, nc,
+                                           K.tau_f, K.wmax, K.hmax));
+    else if (K.visibility)
       wn = mul_rn(wn, visible_fraction_one(Mv, a.x, a.y, a.z, ba, counts + ba * K.n_check, K.n_check, K.tau_f,
                                            K.wmax, K.hmax));
     den[i] = mul_rn(mul_rn(mul_rn(wn, 2.f), K.pi_f), K.h2_f);  // Wn * 2 * math.pi * h ** 2
@@ -568,6 +622,38 @@ int warp_grid(long long nwarps) { return clamp_grid(blocks_for(nwarps * 32, kThr
 
 unsigned long long g_fwd_attr = 0;  // devices on which the tiled forward's shared-memory opt-in is set
 
+// A second stream of the calling host thread on the current device, with the events that fork work onto it
+// from the caller's stream and join it back (null if it cannot be created: the caller's stream is used).
+// Per thread, so that concurrent callers never record into each other's events.  Under stream capture the
+// fork / join pair brings the second stream into the caller's graph.
+struct SideStream {
+  cudaStream_t s = nullptr;
+  cudaEvent_t fork = nullptr, join = nullptr;
+};
+SideStream* side_stream() {
+  thread_local SideStream per_dev[64];
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  SideStream& x = per_dev[dev];
+  if (!x.s) {
+    cudaStream_t st = nullptr;
+    cudaEvent_t f = nullptr, j = nullptr;
+    if (cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaEventCreateWithFlags(&f, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&j, cudaEventDisableTiming) != cudaSuccess) {
+      if (j) cudaEventDestroy(j);
+      if (f) cudaEventDestroy(f);
+      if (st) cudaStreamDestroy(st);
+      cudaGetLastError();  // not sticky: clear it, the caller's stream does the work instead
+      return nullptr;
+    }
+    x.s = st;
+    x.fork = f;
+    x.join = j;
+  }
+  return &x;
+}
+
 // Every pair passes |t_i - t_j| <= tau when tau covers the events' time range: fl(t_i - t_j) never exceeds
 // fl(t_hi - t_lo) (rounding is monotonic).  NaN bounds (unknown range) fail the test.
 // The events that are sources of the pair sums: [src_begin, src_end) of the configuration, all if src_end <= 0.
@@ -637,6 +723,35 @@ int exact_forward(const atlb_exact_cfg& c, const float* t, const long long* b, l
   PlanConsts P = make_plan_consts(g, c.tau, c.B);
   P.src0 = j0;
   P.src1 = j1;
+  // normaliser (window counts, exposure correction): depends on the prepared events and anchors only, so it
+  // runs on a second stream beside the plan build below
+  SideStream* side = side_stream();
+  const cudaStream_t norm_s = side ? side->s : s;
+  if (side) {
+    cudaEventRecord(side->fork, s);
+    cudaStreamWaitEvent(side->s, side->fork, 0);
+  }
+  const MotionView Mv = motion_of(c);
+  NormConsts K;
+  K.tau = c.tau;
+  K.tau_f = (float)c.tau;
+  K.pi_f = (float)M_PI;
+  K.h2_f = (float)(c.h * c.h);
+  K.wmax = (float)(c.W - 1);
+  K.hmax = (float)(c.H - 1);
+  K.n_check = (int)c.n_check;
+  K.visibility = c.visibility;
+  K.B = c.B;
+  cudaMemsetAsync(w.slice_hist, 0, (size_t)(c.B * c.n_check) * 4, norm_s);
+  if (c.visibility && N > 0)
+    launch(k_slice_hist, clamp_grid(blocks_for(N, kThreads * 16)), kThreads, 0, norm_s, t, b, N, c.B, (int)c.n_check,
+           w.slice_hist);
+  const double span = (double)g.t_hi - (double)g.t_lo;  // NaN (unknown) fails both tests
+  const bool whole_batch = c.tau >= span + 1e-6 && c.tau + span < 4.0 - 1e-6;
+  if (whole_batch) launch(k_batch_bounds, grid_for(N + 1), kThreads, 0, norm_s, b, N, c.B, w.bstart);
+  if (M > 0)
+    launch(k_exact_norm, grid_for(M), kThreads, 0, norm_s, Mv, K, (const float4*)anc4, anc_b, M, t, b, N,
+           whole_batch ? (const long long*)w.bstart : nullptr, (const int*)w.slice_hist, den_out);
   // slice centres, entries and anchors
   launch(k_slice_centres, (unsigned)((g.S + 127) / 128), 128, 0, s, P, w.SC);
   cudaMemsetAsync(w.counts, 0, (size_t)ncell * 4, s);
@@ -649,40 +764,23 @@ int exact_forward(const atlb_exact_cfg& c, const float* t, const long long* b, l
     exclusive_scan<int>(w.ocount, nkey, w.partials, w.ostart, s);
     launch(k_order_scatter, grid_for(ns), kThreads, 0, s, P, ev, t + j0, b + j0, ns, j0, (const int*)w.ostart,
            w.ocount, w.XVo, w.TBo);
-    launch(k_fast_count_ordered, slice_grid(ns, P.S), kThreads, 0, s, P, (const float4*)w.XVo, (const int4*)w.TBo,
+    launch(k_fast_count_ordered, grid_for(ns), kThreads, 0, s, P, (const float4*)w.XVo, (const int4*)w.TBo,
            ns, w.counts, w.KEY);
   }
   if (M > 0) launch(k_fast_anchor_count, grid_for(M), kThreads, 0, s, P, (const float4*)anc4, anc_b, M, w.acounts);
   exclusive_scan<int>(w.counts, ncell, w.partials, w.start, s);
   if (ns > 0)
-    launch(k_fast_scatter_ordered, slice_grid(ns, P.S), kThreads, 0, s, P, (const float4*)w.XVo, (const int4*)w.TBo,
+    launch(k_fast_scatter_ordered, grid_for(ns), kThreads, 0, s, P, (const float4*)w.XVo, (const int4*)w.TBo,
            ns, (const int*)w.KEY, (const int*)w.start, w.counts, w.YV, w.TI);
   exclusive_scan<int>(w.acounts, ncell, w.partials, w.astart, s);
   if (M > 0)
     launch(k_fast_anchor_scatter, grid_for(M), kThreads, 0, s, P, make_pair_consts(c.h, c.tau, c.cut),
            (const float4*)anc4, anc_b, M, (const float4*)ev4, (const float*)w.SC, (const int*)w.astart, w.acounts,
            w.XT, w.BI);
-  // normaliser
-  const MotionView Mv = motion_of(c);
-  NormConsts K;
-  K.tau = c.tau;
-  K.tau_f = (float)c.tau;
-  K.pi_f = (float)M_PI;
-  K.h2_f = (float)(c.h * c.h);
-  K.wmax = (float)(c.W - 1);
-  K.hmax = (float)(c.H - 1);
-  K.n_check = (int)c.n_check;
-  K.visibility = c.visibility;
-  cudaMemsetAsync(w.slice_hist, 0, (size_t)(c.B * c.n_check) * 4, s);
-  if (c.visibility && N > 0)
-    launch(k_slice_hist, clamp_grid(blocks_for(N, kThreads * 16)), kThreads, 0, s, t, b, N, c.B, (int)c.n_check,
-           w.slice_hist);
-  const double span = (double)g.t_hi - (double)g.t_lo;  // NaN (unknown) fails both tests
-  const bool whole_batch = c.tau >= span + 1e-6 && c.tau + span < 4.0 - 1e-6;
-  if (whole_batch) launch(k_batch_bounds, grid_for(N + 1), kThreads, 0, s, b, N, c.B, w.bstart);
-  if (M > 0)
-    launch(k_exact_norm, grid_for(M), kThreads, 0, s, Mv, K, (const float4*)anc4, anc_b, M, t, b, N,
-           whole_batch ? (const long long*)w.bstart : nullptr, (const int*)w.slice_hist, den_out);
+  if (side) {  // the pair kernels below read den
+    cudaEventRecord(side->join, norm_s);
+    cudaStreamWaitEvent(s, side->join, 0);
+  }
   // pair sums + log scores
   const FastEntries E{w.YV, w.TI};
   const FastAnchors A{w.XT, w.BI};

@@ -199,6 +199,8 @@ PlanConsts make_plan_consts(const atlb_plan_geom& g, double tau, long long B) {
   P.ox_f = (float)g.ox;
   P.oy_f = (float)g.oy;
   P.cell_f = (float)g.cell;
+  volatile float one = 1.f;  // an fp32 division on the host: RN(1 / cell_f)
+  P.rcell_f = one / P.cell_f;
   P.GW = g.GW;
   P.GH = g.GH;
   P.S = g.S;

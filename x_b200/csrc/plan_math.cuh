@@ -9,6 +9,7 @@ namespace atlb {
 struct PlanConsts {
   float tau_f, hd_f, delta_f;  // tau, delta/2, delta = 1/S (rounded to fp32)
   float ox_f, oy_f, cell_f;    // grid origin and cell size (rounded to fp32)
+  float rcell_f;               // RN(1 / cell_f), the fp32 division
   long long GW, GH;
   int S;
   long long B;
@@ -42,6 +43,20 @@ __device__ __forceinline__ void transported(const PlanConsts& P, float xj, float
   *yy = add_rn(yj, mul_rn(vy, dtc));
 }
 
+// floorf(div_rn(a, c)) for c > 0, given rc = RN(1 / c), without the division in all but rare cases.
+// q = RN(a * rc) differs from a / c by at most (2^-23 + 2^-48) |a / c| (the rounding of rc, then of the
+// product), and RN(a / c) differs from a / c by at most 2^-24 |a / c|; so |q - RN(a / c)| < 1.6 * 2^-23 |q|.
+// When q's distance to the nearest integer exceeds 2^-21 |q| (more than twice that), no integer lies between
+// the two and floor(q) = floor(RN(a / c)); otherwise (and for NaN / infinite q) the quotient is computed.
+__device__ __forceinline__ float floor_div(float a, float c, float rc) {
+  const float q = __fmul_rn(a, rc);
+  const float f = floorf(q);
+  const float fr = __fsub_rn(q, f);              // exact: q - floor(q) for |q| < 2^23
+  const float d = __fmul_rn(fabsf(q), 0x1p-21f);
+  if (fr > d && fr < __fsub_rn(1.f, d)) return f;  // false for NaN and infinities
+  return floorf(div_rn(a, c));
+}
+
 // functional.py:158-163: transported position and its cell key (-1 = dropped).
 __device__ __forceinline__ long long source_key(const PlanConsts& P, float xj, float yj, float vx, float vy, float tj,
                                                 long long bj, int s, float* yx_out, float* yy_out) {
@@ -49,8 +64,8 @@ __device__ __forceinline__ long long source_key(const PlanConsts& P, float xj, f
   transported(P, xj, yj, vx, vy, tj, s, &yx, &yy);
   *yx_out = yx;
   *yy_out = yy;
-  const float qx = floorf(div_rn(sub_rn(yx, P.ox_f), P.cell_f));
-  const float qy = floorf(div_rn(sub_rn(yy, P.oy_f), P.cell_f));
+  const float qx = floor_div(sub_rn(yx, P.ox_f), P.cell_f, P.rcell_f);
+  const float qy = floor_div(sub_rn(yy, P.oy_f), P.cell_f, P.rcell_f);
   // in-range tests on the integral float (NaN fails them, as the reference's int64 cast then does)
   if (!(qx >= 0.f && qx < (float)P.GW && qy >= 0.f && qy < (float)P.GH)) return -1;
   if (bj < 0 || bj >= P.B) return -1;  // batch index outside [0, B): no cell (the reference's key would overflow)
