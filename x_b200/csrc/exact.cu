@@ -454,7 +454,7 @@ struct FusedOut {
 
 
 // dL/dS in bucket order from the upstream dL/dls (torch's LogBackward then DivBackward).
-// The backward's anchor records in bucket order: AB = (x, y, t - c_s, t) and GB = dL/dS / h^2, with
+// The backward's anchor records in bucket order: AB = (x, y, t - c_s, t - c_s) and GT = (dL/dS / h^2, t), with
 // dL/dS = dL/dls / (eps + S / den) / den (the Log then Div backward of ls = log(eps + S / den)) (s = the anchor's slice, as in anchor_cell).
 __global__ void __launch_bounds__(kThreads) k_exact_gs_records(PlanConsts P, const float4* __restrict__ XT,
                                                                const int* __restrict__ BI, long long M,
@@ -462,7 +462,7 @@ __global__ void __launch_bounds__(kThreads) k_exact_gs_records(PlanConsts P, con
                                                                const float* __restrict__ S,
                                                                const float* __restrict__ den, float eps, float invh2,
                                                                const float* __restrict__ SC,
-                                                               float4* __restrict__ AB, float* __restrict__ GB) {
+                                                               float4* __restrict__ AB, float2* __restrict__ GT) {
   const long long stride = (long long)gridDim.x * blockDim.x;
   for (long long p = blockIdx.x * (long long)blockDim.x + threadIdx.x; p < M; p += stride) {
     const int i = BI[p];
@@ -470,8 +470,9 @@ __global__ void __launch_bounds__(kThreads) k_exact_gs_records(PlanConsts P, con
     const float g = div_rn(div_rn(grad_ls[i], add_rn(eps, q)), den[i]);
     const float4 a = XT[p];
     const int sa = (int)clampf(floorf(div_rn(a.z, P.delta_f)), 0.f, (float)(P.S - 1));
-    AB[p] = make_float4(a.x, a.y, sub_rn(a.z, SC[sa]), a.z);
-    GB[p] = g * invh2;
+    const float dts = sub_rn(a.z, SC[sa]);
+    AB[p] = make_float4(a.x, a.y, dts, dts);
+    GT[p] = make_float2(g * invh2, a.z);
   }
 }
 
@@ -575,7 +576,7 @@ struct ExactWs {
   long long* bstart;  // first event of each batch (B + 1)
   int* KEY;      // cell key of each (slice, source event) of the count pass, -1 = no entry
   float4* AB;    // backward anchor records (x, y, t - c_s, t), bucket order
-  float* GB;     // dL/dS / h^2, bucket order
+  float2* GT;    // (dL/dS / h^2, t), bucket order
   int* ocount;   // events per mid-slice cell (B*GH*GW), then the order cursor
   int* ostart;
   float4* XVo;   // events in spatial order: (x, y, vx, vy)
@@ -608,7 +609,7 @@ size_t ws_layout(long long N, long long M, long long ncell, long long S, long lo
   x.bstart = (long long*)take((size_t)(B + 1) * 8);
   x.KEY = (int*)take((size_t)nent * 4);
   x.AB = (float4*)take((size_t)M * 16);
-  x.GB = (float*)take((size_t)M * 4);
+  x.GT = (float2*)take((size_t)M * 8);
   x.ocount = (int*)take((size_t)nkey * 4);
   x.ostart = (int*)take((size_t)(nkey + 1) * 4);
   x.XVo = (float4*)take((size_t)N * 16);
@@ -746,8 +747,13 @@ int exact_forward(const atlb_exact_cfg& c, const float* t, const long long* b, l
   if (c.visibility && N > 0)
     launch(k_slice_hist, clamp_grid(blocks_for(N, kThreads * 16)), kThreads, 0, norm_s, t, b, N, c.B, (int)c.n_check,
            w.slice_hist);
-  const double span = (double)g.t_hi - (double)g.t_lo;  // NaN (unknown) fails both tests
-  const bool whole_batch = c.tau >= span + 1e-6 && c.tau + span < 4.0 - 1e-6;
+  // Window counts are batch size - 1 when every event of a batch lies within tau of every other and no other
+  // batch does: span <= tau (then key_i - tau <= key_j <= key_i + tau holds for the float64 keys b*4 + t of one
+  // batch, which are exact, after the monotone rounding of key_i +- tau) and tau + span < 4 with a margin
+  // (keys of the neighbouring batch stay outside).  span is exact: two floats subtracted in double.  NaN
+  // (unknown range) fails both tests.
+  const double span = (double)g.t_hi - (double)g.t_lo;
+  const bool whole_batch = c.tau >= span && c.tau + span < 4.0 - 1e-6;
   if (whole_batch) launch(k_batch_bounds, grid_for(N + 1), kThreads, 0, norm_s, b, N, c.B, w.bstart);
   if (M > 0)
     launch(k_exact_norm, grid_for(M), kThreads, 0, norm_s, Mv, K, (const float4*)anc4, anc_b, M, t, b, N,
@@ -838,17 +844,17 @@ int exact_backward(const atlb_exact_cfg& c, const float* grad_ls, const long lon
   if (M > 0 && ncell > 0) {
     const PlanConsts P = make_plan_consts(g, c.tau, c.B);
     launch(k_exact_gs_records, grid_for(M), kThreads, 0, s, P, (const float4*)w.XT, (const int*)w.BI, M, grad_ls, S,
-           den, eps, C.invh2, (const float*)w.SC, w.AB, w.GB);
+           den, eps, C.invh2, (const float*)w.SC, w.AB, w.GT);
     const int nrows = (int)(c.B * g.S * g.GH);
     const dim3 grid((unsigned)((g.GW + 7) / 8), (unsigned)min(nrows, 65535));
     cudaEvent_t e0 = timing_begin(s);
     if (tau_covers(g, c.tau))
       launch(k_pair_bwd_cells<true, false, FastEntries, int>, grid, 256, 0, s, E, (const float4*)w.AB,
-             (const float*)w.GB, nullptr,
+             (const float2*)w.GT, nullptr,
              (const int*)w.astart, (const int*)w.start, (int)g.GW, (int)g.GH, nrows, C, N, gv);
     else
       launch(k_pair_bwd_cells<false, false, FastEntries, int>, grid, 256, 0, s, E, (const float4*)w.AB,
-             (const float*)w.GB, nullptr,
+             (const float2*)w.GT, nullptr,
              (const int*)w.astart, (const int*)w.start, (int)g.GW, (int)g.GH, nrows, C, N, gv);
     timing_end("k_pair_bwd", s, e0);
   }

@@ -111,7 +111,7 @@ __global__ void __launch_bounds__(kThreads) k_anchor_records_fwd(const long long
   }
 }
 
-// Cell-per-warp backward's anchor records: AB = (x, y, t - c_s, t), GB = dL/dS / h^2, GID = id.
+// Cell-per-warp backward's anchor records: AB = (x, y, t - c_s, t - c_s), GT = (dL/dS / h^2, t), GID = id.
 __global__ void __launch_bounds__(kThreads) k_anchor_records_bwd(const long long* __restrict__ AC,
                                                                  const float2* __restrict__ AX,
                                                                  const float* __restrict__ AT,
@@ -122,7 +122,7 @@ __global__ void __launch_bounds__(kThreads) k_anchor_records_bwd(const long long
                                                                  long long ncell, float invh2,
                                                                  const int* __restrict__ start,
                                                                  int* __restrict__ cursor, float4* __restrict__ AB,
-                                                                 float* __restrict__ GB, long long* __restrict__ GID) {
+                                                                 float2* __restrict__ GT, long long* __restrict__ GID) {
   const long long stride = (long long)gridDim.x * blockDim.x;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < M; i += stride) {
     const long long key = anchor_key(AC, i, S, GH, GW, ncell);
@@ -130,8 +130,9 @@ __global__ void __launch_bounds__(kThreads) k_anchor_records_bwd(const long long
     const int p = start[key] + atomicAdd(cursor + key, 1);
     const float2 x = AX[i];
     const float t = AT[i];
-    AB[p] = make_float4(x.x, x.y, sub_rn(t, __ldg(SC + AC[3 * i] % S)), t);
-    GB[p] = gS[i] * invh2;
+    const float dts = sub_rn(t, __ldg(SC + AC[3 * i] % S));
+    AB[p] = make_float4(x.x, x.y, dts, dts);
+    GT[p] = make_float2(gS[i] * invh2, t);
     GID[p] = AID[i];
   }
 }
@@ -156,9 +157,10 @@ __global__ void __launch_bounds__(kThreads) k_gather_bucketed(const float* __res
 
 }  // namespace
 
-// Per anchor: a 16-byte record (tiled kernels; the generic kernels keep x and t there), the id, the original
-// index and dL/dS in bucket order.  Per cell: a count / cursor and a CSR offset.  Two ints after the counts
-// hold the forward's overflow word.
+// Per anchor: a 16-byte record (tiled kernels; the generic kernels keep x and t there), the id, and 8 bytes
+// that hold the original index and dL/dS (generic kernels, tiled forward) or the tiled backward's
+// (dL/dS / h^2, t).  Per cell: a count / cursor and a CSR offset.  Two ints after the counts hold the
+// forward's overflow word.
 size_t pair_workspace_bytes(long long M, long long ncell) {
   size_t n = 0;
   n += align_up((size_t)(ncell + 2) * sizeof(int));        // counts / cursor, overflow word
@@ -166,8 +168,7 @@ size_t pair_workspace_bytes(long long M, long long ncell) {
   n += align_up(scan_partials_bytes(ncell));               // scan partials
   n += align_up((size_t)M * sizeof(float4));               // records (generic: xy, then t)
   n += align_up((size_t)M * sizeof(long long));            // id
-  n += align_up((size_t)M * sizeof(int));                  // idx
-  n += align_up((size_t)M * sizeof(float));                // gS in bucket order
+  n += align_up((size_t)M * 2 * sizeof(float));            // idx + gS in bucket order, or (gS / h^2, t)
   return n + 256;
 }
 
@@ -182,7 +183,8 @@ struct PairWs {
   float* t;
   long long* id;
   int* idx;
-  float* gb;
+  float* gb;   // follows idx
+  float2* gt;  // the tiled backward's (gS / h^2, t): the idx and gb bytes
 };
 PairWs carve(void* ws, long long M, long long ncell) {
   char* p = (char*)align_ptr(ws);
@@ -195,8 +197,9 @@ PairWs carve(void* ws, long long M, long long ncell) {
   w.xy = (float2*)w.rec;
   w.t = (float*)(w.xy + M);
   w.id = (long long*)p; p += align_up((size_t)M * sizeof(long long));
-  w.idx = (int*)p; p += align_up((size_t)M * sizeof(int));
-  w.gb = (float*)p;
+  w.idx = (int*)p;
+  w.gb = (float*)(w.idx + M);
+  w.gt = (float2*)p;
   return w;
 }
 
@@ -295,12 +298,12 @@ int pair_bwd(const float* gS, const float* SY, const float* SV, const float* ST,
            0LL, S, GH, GW, ncell, w.counts, (int*)nullptr);
     exclusive_scan<int>(w.counts, ncell, w.partials, w.start, s);
     launch(k_anchor_records_bwd, clamp_grid(blocks_for(M, kThreads)), kThreads, 0, s, AC, (const float2*)AX, AT, AID,
-           gS, SC, M, S, GH, GW, ncell, C.invh2, (const int*)w.start, w.counts, w.rec, w.gb, w.id);
+           gS, SC, M, S, GH, GW, ncell, C.invh2, (const int*)w.start, w.counts, w.rec, w.gt, w.id);
     const int nrows = (int)(ncell / GW);
     const dim3 grid((unsigned)((GW + 7) / 8), (unsigned)(nrows < 65535 ? nrows : 65535));
     cudaEvent_t e0 = timing_begin(s);
     launch(k_pair_bwd_cells<false, true, RefEntries, long long>, grid, 256, 0, s, E, (const float4*)w.rec,
-           (const float*)w.gb, (const long long*)w.id, (const int*)w.start, CS, (int)GW, (int)GH, nrows, C, N, gv);
+           (const float2*)w.gt, (const long long*)w.id, (const int*)w.start, CS, (int)GW, (int)GH, nrows, C, N, gv);
     timing_end("k_pair_bwd", s, e0);
     return launch_status("ats_pair_bwd");
   }

@@ -8,8 +8,9 @@
 //             neighbourhood streamed by the lanes.  A tile whose neighbourhood does not fit reads its
 //             candidates from global memory instead (same loop, global pointer); a tile with more anchors
 //             than it stages is left to k_pair_fwd_overflow (warp per anchor cell, groups of up to 8).
-//   backward: not tiled.  One warp per source cell, one entry per lane; the anchors of the 3x3 cells are
-//             warp-uniform broadcast loads through L1 of per-anchor records prepared once per backward
+//   backward: not tiled.  One warp per source cell, one entry per lane (a cell's last chunk of at most 16
+//             entries spreads each entry over several lanes); the anchors of the 3x3 cells are broadcast
+//             loads through L1 of per-anchor records prepared once per backward
 //             (measured faster than staging them: no barriers, no per-tile set-up, L1 reuse across the
 //             8 neighbouring cells of a CTA).
 // Index arithmetic is 32-bit and division-free (power-of-two tile width, one grid axis per coordinate):
@@ -544,15 +545,46 @@ __global__ void __launch_bounds__(256) k_pair_fwd_overflow(E ent, FastAnchors an
 }
 
 // ---- backward ----------------------------------------------------------------------------------------
+// Gradient of one entry (y, v, t, id) over the anchors of 3 cell rows [lo[r], hi[r]), anchors p = lo[r] + g,
+// lo[r] + g + G, ... (STRIDED) or every anchor (g = 0, G = 1: a warp-uniform loop).
+template <bool TAU_ALL, bool LOO_ID, bool STRIDED, typename Id>
+__device__ __forceinline__ float2 bwd_entry(const float4* __restrict__ AB, const float2* __restrict__ GT,
+                                            const long long* __restrict__ GID, const int* lo, const int* hi,
+                                            f32x2 y, f32x2 v, float st, Id sid, int g, int G, const PairConsts& C) {
+  float gx = 0.f, gy = 0.f;
+#pragma unroll
+  for (int r = 0; r < 3; ++r) {
+    const int p1 = hi[r];
+#pragma unroll 2
+    for (int p = lo[r] + (STRIDED ? g : 0); p < p1; p += (STRIDED ? G : 1)) {
+      const float4 a = __ldg(AB + p);   // (x, y, t - c_s, t - c_s): both pairs are packed operands as loaded
+      const float2 gt = __ldg(GT + p);  // (dL/dS / h^2, t)
+      const float ga = gt.x;
+      float2 rr;
+      const float d2 = residual2(pk2(a.x, a.y), pk2(a.z, a.w), y, v, &rr);
+      const float dt = sub_rn(gt.y, st);
+      bool ok = !(d2 > C.r2max);
+      if (!TAU_ALL) ok = ok && !(fabsf(dt) > C.tau);
+      if (LOO_ID) ok = ok && (long long)sid != __ldg(GID + p);
+      const float f = ok ? ga * ex2_approx(-d2 * C.k2) * dt : 0.f;  // gS k dt / h^2
+      gx = fmaf(f, rr.x, gx);
+      gy = fmaf(f, rr.y, gy);
+    }
+  }
+  return make_float2(gx, gy);
+}
+
 // One warp per source cell (grid: x = groups of 8 cells of a cell row, y = cell rows of all (batch, slice)
-// grids), lanes over the cell's entries in chunks of 32.  The anchors of the 3 neighbouring cell rows are
-// read as warp-uniform broadcast loads through L1 from records prepared once per backward:
-// AB = (x, y, t - c_s, t) and GB = dL/dS / h^2, in bucket order.  Leave-one-out: the anchor's own pair has
-// dt = 0 and adds nothing in the fused layout; with LOO_ID the pair is excluded by comparing the entry's id
-// with the anchor's (GID, bucket order), as the reference does.
+// grids), lanes over the cell's entries in chunks of 32.  The anchors of the 3 neighbouring cell rows are read
+// as warp-uniform broadcast loads through L1 from records prepared once per backward:
+// AB = (x, y, t - c_s, t - c_s) and GT = (dL/dS / h^2, t), in bucket order.  A last chunk of m <= 16 entries would leave most lanes idle: there
+// each entry gets G = floor(32 / m) lanes, lane g of them taking every G-th anchor of each row, and the G
+// partial gradients are summed by shuffles.  Leave-one-out: the anchor's own pair has dt = 0 and adds
+// nothing in the fused layout; with LOO_ID the pair is excluded by comparing the entry's id with the
+// anchor's (GID, bucket order), as the reference does.
 template <bool TAU_ALL, bool LOO_ID, class E, typename CS>
-__global__ void __launch_bounds__(256) k_pair_bwd_cells(E ent, const float4* __restrict__ AB,
-                                                        const float* __restrict__ GB,
+__global__ void __launch_bounds__(256, 6) k_pair_bwd_cells(E ent, const float4* __restrict__ AB,
+                                                        const float2* __restrict__ GT,
                                                         const long long* __restrict__ GID,
                                                         const int* __restrict__ astart, const CS* __restrict__ cstart,
                                                         int GW, int GH, int nrows, PairConsts C, long long N,
@@ -561,55 +593,61 @@ __global__ void __launch_bounds__(256) k_pair_bwd_cells(E ent, const float4* __r
   const int cx = blockIdx.x * 8 + (threadIdx.x >> 5);
   if (cx >= GW) return;
   for (int row = blockIdx.y; row < nrows; row += gridDim.y) {  // row = (b * S + s) * GH + cy
-  const int cy = row % GH;
-  const int c = row * GW + cx;
-  const int k0 = (int)cstart[c], k1 = (int)cstart[c + 1];
-  if (k0 == k1) continue;
-  const int gbase = (row - cy) * GW;
-  const int xl = max(cx - 1, 0), xh = min(cx + 1, GW - 1) + 1;
-  int lo[3], hi[3];
-#pragma unroll
-  for (int r = 0; r < 3; ++r) {
-    const int y = cy - 1 + r;
-    int l = 0, h = 0;
-    if (y >= 0 && y < GH) {
-      l = astart[gbase + y * GW + xl];
-      h = astart[gbase + y * GW + xh];
-    }
-    lo[r] = l;
-    hi[r] = h;
-  }
-  if (lo[0] == hi[0] && lo[1] == hi[1] && lo[2] == hi[2]) continue;
-  for (int kb = k0; kb < k1; kb += 32) {
-    const int k = kb + lane;
-    const bool valid = k < k1;
-    float2 sy, sv;
-    float st;
-    typename E::Id sid;
-    ent.load(valid ? k : k0, sy, sv, st, sid);
-    const f32x2 y = pk2(sy.x, sy.y), v = pk2(sv.x, sv.y);
-    float gx = 0.f, gy = 0.f;
+    const int cy = row % GH;
+    const int c = row * GW + cx;
+    const int k0 = (int)cstart[c], k1 = (int)cstart[c + 1];
+    if (k0 == k1) continue;
+    const int gbase = (row - cy) * GW;
+    const int xl = max(cx - 1, 0), xh = min(cx + 1, GW - 1) + 1;
+    int lo[3], hi[3];
 #pragma unroll
     for (int r = 0; r < 3; ++r) {
-      const int p1 = hi[r];
-#pragma unroll 2
-      for (int p = lo[r]; p < p1; ++p) {
-        const float4 a = __ldg(AB + p);
-        const float ga = __ldg(GB + p);
-        float2 rr;
-        const float d2 = residual2(pk2(a.x, a.y), pk2(a.z, a.z), y, v, &rr);
-        const float dt = sub_rn(a.w, st);
-        bool ok = !(d2 > C.r2max);
-        if (!TAU_ALL) ok = ok && !(fabsf(dt) > C.tau);
-        if (LOO_ID) ok = ok && (long long)sid != __ldg(GID + p);
-        const float f = ok ? ga * ex2_approx(-d2 * C.k2) * dt : 0.f;  // gS k dt / h^2
-        gx = fmaf(f, rr.x, gx);
-        gy = fmaf(f, rr.y, gy);
+      const int y = cy - 1 + r;
+      int l = 0, h = 0;
+      if (y >= 0 && y < GH) {
+        l = astart[gbase + y * GW + xl];
+        h = astart[gbase + y * GW + xh];
+      }
+      lo[r] = l;
+      hi[r] = h;
+    }
+    if (lo[0] == hi[0] && lo[1] == hi[1] && lo[2] == hi[2]) continue;
+    for (int kb = k0; kb < k1; kb += 32) {
+      const int m = min(32, k1 - kb);
+      float2 sy, sv;
+      float st;
+      typename E::Id sid;
+      if (m > 16) {  // warp-uniform: one entry per lane, every lane walks every anchor
+        const bool valid = lane < m;
+        ent.load(kb + (valid ? lane : 0), sy, sv, st, sid);
+        const float2 gr = bwd_entry<TAU_ALL, LOO_ID, false>(AB, GT, GID, lo, hi, pk2(sy.x, sy.y), pk2(sv.x, sv.y),
+                                                            st, sid, 0, 1, C);
+        if (valid && (gr.x != 0.f || gr.y != 0.f) && sid >= 0 && (long long)sid < N)
+          red_add_f2(gv + 2 * (long long)sid, gr.x, gr.y);
+      } else {
+        // G lanes per entry: entry e = lane / G, part g = lane % G.  The float quotients are exact after
+        // truncation: 32.5 / m and (lane + 0.5) / G lie at least 1/64 from an integer.
+        const int G = (int)__fdividef(32.5f, (float)m);
+        const int e = (int)__fdividef((float)lane + 0.5f, (float)G);
+        const int g = lane - e * G;
+        const bool valid = e < m;
+        ent.load(kb + (valid ? e : 0), sy, sv, st, sid);
+        int hv[3];
+#pragma unroll
+        for (int r = 0; r < 3; ++r) hv[r] = valid ? hi[r] : lo[r];
+        float2 gr = bwd_entry<TAU_ALL, LOO_ID, true>(AB, GT, GID, lo, hv, pk2(sy.x, sy.y), pk2(sv.x, sv.y), st, sid,
+                                                     g, G, C);
+        for (int d = 1; d < G; d <<= 1) {  // tree sum of each entry's G partials into its lane g = 0
+          const float ox = __shfl_down_sync(0xffffffffu, gr.x, d), oy = __shfl_down_sync(0xffffffffu, gr.y, d);
+          if ((g & (2 * d - 1)) == 0 && g + d < G) {
+            gr.x += ox;
+            gr.y += oy;
+          }
+        }
+        if (valid && g == 0 && (gr.x != 0.f || gr.y != 0.f) && sid >= 0 && (long long)sid < N)
+          red_add_f2(gv + 2 * (long long)sid, gr.x, gr.y);
       }
     }
-    if (valid && (gx != 0.f || gy != 0.f) && sid >= 0 && (long long)sid < N)
-      red_add_f2(gv + 2 * (long long)sid, gx, gy);
-  }
   }
 }
 
