@@ -98,8 +98,14 @@ __device__ __forceinline__ f32x2 sub2(f32x2 a, f32x2 b) {
 
 // r = x_i - (y_j + v_j * dti) for both components, each op rounded as the reference's scalar code
 // (atl_cpu.cpp:192-193); returns d^2 = rx*rx + ry*ry (atl_cpu.cpp:194) and r in *r.
+// The products v_j * dti are scalar __fmul_rn: the code generator contracts a packed mul.rn.f32x2 followed
+// by add.rn.f32x2 into one fused multiply-add (measured: y + v dt rounded once; an explicit packed fma with a
+// -0 addend is folded the same way), which would change the acceptance of pairs at the cut; __fmul_rn is
+// never contracted.  The squares may stay packed: their sum is __fadd_rn, which is never merged into an FMA.
 __device__ __forceinline__ float residual2(f32x2 xi, f32x2 dti2, f32x2 y, f32x2 v, float2* r) {
-  const f32x2 rr = sub2(xi, add2(y, mul2(v, dti2)));
+  const float2 vv = upk2(v), dd = upk2(dti2);
+  const f32x2 vd = pk2(__fmul_rn(vv.x, dd.x), __fmul_rn(vv.y, dd.y));
+  const f32x2 rr = sub2(xi, add2(y, vd));
   *r = upk2(rr);
   const float2 sq = upk2(mul2(rr, rr));
   return add_rn(sq.x, sq.y);
