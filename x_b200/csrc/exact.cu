@@ -274,19 +274,34 @@ __global__ void __launch_bounds__(kThreads) k_fast_scatter_ordered(PlanConsts P,
       id = tb.z;
       e = XVo[i];
     }
-    for (int s = 0; s < P.S; ++s) {
-      const int key = live ? KEY[(long long)s * N + i] : -1;  // the count pass's keys
-      const unsigned grp = __match_any_sync(0xffffffffu, key);
-      const int leader = __ffs(grp) - 1;
-      int base = 0;
-      if (key >= 0 && lane == leader) base = start[key] + atomicAdd(cursor + key, __popc(grp));
-      base = __shfl_sync(0xffffffffu, base, leader);
-      if (key >= 0) {
-        float yx, yy;
-        transported(P, e.x, e.y, e.z, e.w, tj, s, &yx, &yy);
-        const int p = base + __popc(grp & below);
-        YV[p] = make_float4(yx, yy, e.z, e.w);
-        TI[p] = make_float2(tj, __int_as_float(id));
+    // slices in batches of kSB: the batch's cursor atomics are issued back to back before any result is
+    // used, so a warp waits for one round trip to L2 per batch rather than per slice
+    constexpr int kSB = 8;
+    for (int s0 = 0; s0 < P.S; s0 += kSB) {
+      int key[kSB], base[kSB];
+      unsigned grp[kSB];
+#pragma unroll
+      for (int u = 0; u < kSB; ++u)
+        key[u] = live && s0 + u < P.S ? KEY[(long long)(s0 + u) * N + i] : -1;  // the count pass's keys
+#pragma unroll
+      for (int u = 0; u < kSB; ++u) {
+        grp[u] = __match_any_sync(0xffffffffu, key[u]);
+        base[u] = 0;
+        if (key[u] >= 0 && lane == __ffs(grp[u]) - 1) base[u] = atomicAdd(cursor + key[u], __popc(grp[u]));
+      }
+#pragma unroll
+      for (int u = 0; u < kSB; ++u) {
+        const int leader = __ffs(grp[u]) - 1;
+        int b = 0;
+        if (key[u] >= 0 && lane == leader) b = start[key[u]] + base[u];
+        b = __shfl_sync(0xffffffffu, b, leader);
+        if (key[u] >= 0) {
+          float yx, yy;
+          transported(P, e.x, e.y, e.z, e.w, tj, s0 + u, &yx, &yy);
+          const int p = b + __popc(grp[u] & below);
+          YV[p] = make_float4(yx, yy, e.z, e.w);
+          TI[p] = make_float2(tj, __int_as_float(id));
+        }
       }
     }
   }

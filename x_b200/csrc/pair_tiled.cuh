@@ -9,10 +9,10 @@
 //             candidates from global memory instead (same loop, global pointer); a tile with more anchors
 //             than it stages is left to k_pair_fwd_overflow (warp per anchor cell, groups of up to 8).
 //   backward: not tiled.  One warp per source cell, one entry per lane (a cell's last chunk of at most 16
-//             entries spreads each entry over several lanes); the anchors of the 3x3 cells are broadcast
-//             loads through L1 of per-anchor records prepared once per backward
-//             (measured faster than staging them: no barriers, no per-tile set-up, L1 reuse across the
-//             8 neighbouring cells of a CTA).
+//             entries spreads each entry over several lanes); the warp copies the anchor records of the
+//             3x3 cells (prepared once per backward) into its own shared-memory list and the lanes walk it
+//             (per warp: no CTA barriers, no per-tile set-up; a flat, unrolled walk with immediate offsets
+//             instead of three row loops over global addresses).
 // Index arithmetic is 32-bit and division-free (power-of-two tile width, one grid axis per coordinate):
 // per-thread integer divisions by runtime values cost more than the pair arithmetic they surround.
 #pragma once
@@ -545,53 +545,58 @@ __global__ void __launch_bounds__(256) k_pair_fwd_overflow(E ent, FastAnchors an
 }
 
 // ---- backward ----------------------------------------------------------------------------------------
-// Gradient of one entry (y, v, t, id) over the anchors of 3 cell rows [lo[r], hi[r]), anchors p = lo[r] + g,
-// lo[r] + g + G, ... (STRIDED) or every anchor (g = 0, G = 1: a warp-uniform loop).
+constexpr int kBwdWarps = 8;   // warps (source cells) per CTA
+constexpr int kBwdAnc = 128;   // anchor records a warp stages at a time
+
+// Gradient of one entry (y, v, t, id) over the staged anchors i = g, g + G, ... < na (g = 0, G = 1: every
+// anchor, a warp-uniform loop).
 template <bool TAU_ALL, bool LOO_ID, bool STRIDED, typename Id>
-__device__ __forceinline__ float2 bwd_entry(const float4* __restrict__ AB, const float2* __restrict__ GT,
-                                            const long long* __restrict__ GID, const int* lo, const int* hi,
+__device__ __forceinline__ float2 bwd_entry(const float4* ab, const float2* gt, const long long* gid, int na,
                                             f32x2 y, f32x2 v, float st, Id sid, int g, int G, const PairConsts& C) {
   float gx = 0.f, gy = 0.f;
-#pragma unroll
-  for (int r = 0; r < 3; ++r) {
-    const int p1 = hi[r];
-#pragma unroll 2
-    for (int p = lo[r] + (STRIDED ? g : 0); p < p1; p += (STRIDED ? G : 1)) {
-      const float4 a = __ldg(AB + p);   // (x, y, t - c_s, t - c_s): both pairs are packed operands as loaded
-      const float2 gt = __ldg(GT + p);  // (dL/dS / h^2, t)
-      const float ga = gt.x;
-      float2 rr;
-      const float d2 = residual2(pk2(a.x, a.y), pk2(a.z, a.w), y, v, &rr);
-      const float dt = sub_rn(gt.y, st);
-      bool ok = !(d2 > C.r2max);
-      if (!TAU_ALL) ok = ok && !(fabsf(dt) > C.tau);
-      if (LOO_ID) ok = ok && (long long)sid != __ldg(GID + p);
-      const float f = ok ? ga * ex2_approx(-d2 * C.k2) * dt : 0.f;  // gS k dt / h^2
-      gx = fmaf(f, rr.x, gx);
-      gy = fmaf(f, rr.y, gy);
-    }
+#pragma unroll 4
+  for (int i = STRIDED ? g : 0; i < na; i += STRIDED ? G : 1) {
+    const float4 a = ab[i];   // (x, y, t - c_s, t - c_s): both pairs are packed operands as loaded
+    const float2 q = gt[i];   // (dL/dS / h^2, t)
+    float2 rr;
+    const float d2 = residual2(pk2(a.x, a.y), pk2(a.z, a.w), y, v, &rr);
+    const float dt = sub_rn(q.y, st);
+    bool ok = !(d2 > C.r2max);
+    if (!TAU_ALL) ok = ok && !(fabsf(dt) > C.tau);
+    if (LOO_ID) ok = ok && (long long)sid != gid[i];
+    const float f = ok ? q.x * ex2_approx(-d2 * C.k2) * dt : 0.f;  // gS k dt / h^2
+    gx = fmaf(f, rr.x, gx);
+    gy = fmaf(f, rr.y, gy);
   }
   return make_float2(gx, gy);
 }
 
 // One warp per source cell (grid: x = groups of 8 cells of a cell row, y = cell rows of all (batch, slice)
-// grids), lanes over the cell's entries in chunks of 32.  The anchors of the 3 neighbouring cell rows are read
-// as warp-uniform broadcast loads through L1 from records prepared once per backward:
-// AB = (x, y, t - c_s, t - c_s) and GT = (dL/dS / h^2, t), in bucket order.  A last chunk of m <= 16 entries would leave most lanes idle: there
-// each entry gets G = floor(32 / m) lanes, lane g of them taking every G-th anchor of each row, and the G
-// partial gradients are summed by shuffles.  Leave-one-out: the anchor's own pair has dt = 0 and adds
-// nothing in the fused layout; with LOO_ID the pair is excluded by comparing the entry's id with the
-// anchor's (GID, bucket order), as the reference does.
+// grids).  The anchor records of the 3 neighbouring cell rows, AB = (x, y, t - c_s, t - c_s) and
+// GT = (dL/dS / h^2, t) in bucket order (prepared once per backward), are copied by the warp into its own
+// shared-memory arrays, up to kBwdAnc at a time, as one flat list; the lanes then walk that list with
+// broadcast shared loads, one entry of the cell per lane, in chunks of 32 entries.  A last chunk of m <= 16
+// entries would leave most lanes idle: there each entry gets G = floor(32 / m) lanes, lane g of them taking
+// every G-th anchor, and the G partial gradients are summed by shuffles.  Leave-one-out: the anchor's own
+// pair has dt = 0 and adds nothing in the fused layout; with LOO_ID the pair is excluded by comparing the
+// entry's id with the anchor's (GID, bucket order), as the reference does.
 template <bool TAU_ALL, bool LOO_ID, class E, typename CS>
-__global__ void __launch_bounds__(256, 6) k_pair_bwd_cells(E ent, const float4* __restrict__ AB,
-                                                        const float2* __restrict__ GT,
-                                                        const long long* __restrict__ GID,
-                                                        const int* __restrict__ astart, const CS* __restrict__ cstart,
-                                                        int GW, int GH, int nrows, PairConsts C, long long N,
-                                                        float* __restrict__ gv) {
-  const int lane = threadIdx.x & 31;
-  const int cx = blockIdx.x * 8 + (threadIdx.x >> 5);
-  if (cx >= GW) return;
+__global__ void __launch_bounds__(kBwdWarps * 32, LOO_ID ? 5 : 6) k_pair_bwd_cells(E ent, const float4* __restrict__ AB,
+                                                                    const float2* __restrict__ GT,
+                                                                    const long long* __restrict__ GID,
+                                                                    const int* __restrict__ astart,
+                                                                    const CS* __restrict__ cstart, int GW, int GH,
+                                                                    int nrows, PairConsts C, long long N,
+                                                                    float* __restrict__ gv) {
+  __shared__ float4 s_ab[kBwdWarps][kBwdAnc];
+  __shared__ float2 s_gt[kBwdWarps][kBwdAnc];
+  __shared__ long long s_id[LOO_ID ? kBwdWarps : 1][LOO_ID ? kBwdAnc : 1];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int cx = blockIdx.x * kBwdWarps + w;
+  if (cx >= GW) return;  // warp-uniform; no CTA-wide barrier follows
+  float4* ab = s_ab[w];
+  float2* gt = s_gt[w];
+  long long* gid = s_id[LOO_ID ? w : 0];
   for (int row = blockIdx.y; row < nrows; row += gridDim.y) {  // row = (b * S + s) * GH + cy
     const int cy = row % GH;
     const int c = row * GW + cx;
@@ -599,7 +604,7 @@ __global__ void __launch_bounds__(256, 6) k_pair_bwd_cells(E ent, const float4* 
     if (k0 == k1) continue;
     const int gbase = (row - cy) * GW;
     const int xl = max(cx - 1, 0), xh = min(cx + 1, GW - 1) + 1;
-    int lo[3], hi[3];
+    int lo[3], len[3];
 #pragma unroll
     for (int r = 0; r < 3; ++r) {
       const int y = cy - 1 + r;
@@ -609,43 +614,52 @@ __global__ void __launch_bounds__(256, 6) k_pair_bwd_cells(E ent, const float4* 
         h = astart[gbase + y * GW + xh];
       }
       lo[r] = l;
-      hi[r] = h;
+      len[r] = h - l;
     }
-    if (lo[0] == hi[0] && lo[1] == hi[1] && lo[2] == hi[2]) continue;
-    for (int kb = k0; kb < k1; kb += 32) {
-      const int m = min(32, k1 - kb);
-      float2 sy, sv;
-      float st;
-      typename E::Id sid;
-      if (m > 16) {  // warp-uniform: one entry per lane, every lane walks every anchor
-        const bool valid = lane < m;
-        ent.load(kb + (valid ? lane : 0), sy, sv, st, sid);
-        const float2 gr = bwd_entry<TAU_ALL, LOO_ID, false>(AB, GT, GID, lo, hi, pk2(sy.x, sy.y), pk2(sv.x, sv.y),
-                                                            st, sid, 0, 1, C);
-        if (valid && (gr.x != 0.f || gr.y != 0.f) && sid >= 0 && (long long)sid < N)
-          red_add_f2(gv + 2 * (long long)sid, gr.x, gr.y);
-      } else {
-        // G lanes per entry: entry e = lane / G, part g = lane % G.  The float quotients are exact after
-        // truncation: 32.5 / m and (lane + 0.5) / G lie at least 1/64 from an integer.
-        const int G = (int)__fdividef(32.5f, (float)m);
-        const int e = (int)__fdividef((float)lane + 0.5f, (float)G);
-        const int g = lane - e * G;
-        const bool valid = e < m;
-        ent.load(kb + (valid ? e : 0), sy, sv, st, sid);
-        int hv[3];
-#pragma unroll
-        for (int r = 0; r < 3; ++r) hv[r] = valid ? hi[r] : lo[r];
-        float2 gr = bwd_entry<TAU_ALL, LOO_ID, true>(AB, GT, GID, lo, hv, pk2(sy.x, sy.y), pk2(sv.x, sv.y), st, sid,
-                                                     g, G, C);
-        for (int d = 1; d < G; d <<= 1) {  // tree sum of each entry's G partials into its lane g = 0
-          const float ox = __shfl_down_sync(0xffffffffu, gr.x, d), oy = __shfl_down_sync(0xffffffffu, gr.y, d);
-          if ((g & (2 * d - 1)) == 0 && g + d < G) {
-            gr.x += ox;
-            gr.y += oy;
+    const int A = len[0] + len[1] + len[2];
+    for (int a0 = 0; a0 < A; a0 += kBwdAnc) {
+      const int na = min(kBwdAnc, A - a0);
+      __syncwarp();  // the previous batch of records is no longer read
+      for (int i = lane; i < na; i += 32) {
+        const int f = a0 + i;  // flat index over the 3 rows
+        const int p = f < len[0] ? lo[0] + f : (f < len[0] + len[1] ? lo[1] + (f - len[0]) : lo[2] + (f - len[0] - len[1]));
+        ab[i] = __ldg(AB + p);
+        gt[i] = __ldg(GT + p);
+        if (LOO_ID) gid[i] = __ldg(GID + p);
+      }
+      __syncwarp();
+      for (int kb = k0; kb < k1; kb += 32) {
+        const int m = min(32, k1 - kb);
+        float2 sy, sv;
+        float st;
+        typename E::Id sid;
+        if (m > 16) {  // warp-uniform: one entry per lane, every lane walks every anchor
+          const bool valid = lane < m;
+          ent.load(kb + (valid ? lane : 0), sy, sv, st, sid);
+          const float2 gr = bwd_entry<TAU_ALL, LOO_ID, false>(ab, gt, gid, na, pk2(sy.x, sy.y), pk2(sv.x, sv.y), st,
+                                                              sid, 0, 1, C);
+          if (valid && (gr.x != 0.f || gr.y != 0.f) && sid >= 0 && (long long)sid < N)
+            red_add_f2(gv + 2 * (long long)sid, gr.x, gr.y);
+        } else {
+          // G lanes per entry: entry e = lane / G, part g = lane % G.  The float quotients are exact after
+          // truncation: 32.5 / m and (lane + 0.5) / G lie at least 1/64 from an integer.
+          const int G = (int)__fdividef(32.5f, (float)m);
+          const int e = (int)__fdividef((float)lane + 0.5f, (float)G);
+          const int g = lane - e * G;
+          const bool valid = e < m;
+          ent.load(kb + (valid ? e : 0), sy, sv, st, sid);
+          float2 gr = bwd_entry<TAU_ALL, LOO_ID, true>(ab, gt, gid, valid ? na : 0, pk2(sy.x, sy.y), pk2(sv.x, sv.y),
+                                                       st, sid, g, G, C);
+          for (int d = 1; d < G; d <<= 1) {  // tree sum of each entry's G partials into its lane g = 0
+            const float ox = __shfl_down_sync(0xffffffffu, gr.x, d), oy = __shfl_down_sync(0xffffffffu, gr.y, d);
+            if ((g & (2 * d - 1)) == 0 && g + d < G) {
+              gr.x += ox;
+              gr.y += oy;
+            }
           }
+          if (valid && g == 0 && (gr.x != 0.f || gr.y != 0.f) && sid >= 0 && (long long)sid < N)
+            red_add_f2(gv + 2 * (long long)sid, gr.x, gr.y);
         }
-        if (valid && g == 0 && (gr.x != 0.f || gr.y != 0.f) && sid >= 0 && (long long)sid < N)
-          red_add_f2(gv + 2 * (long long)sid, gr.x, gr.y);
       }
     }
   }
