@@ -1,9 +1,11 @@
-// Pair kernels of the fused path (compact entry layout): shared-memory tiled forward, cell-per-warp backward.
+// Pair kernels: shared-memory tiled forward, cell-per-warp backward.  Templated on the entry layout: the
+// fused path's compact records (FastEntries) or the reference's plan arrays (RefEntries, drop-in ops).
 //
 // Grid: (tile column, tile row, slice); each CTA walks the batches of its slice.  A tile is TX x TY cells.
 //   forward : the entries of the (TX+2) x (TY+2) cells around the tile and the anchors of the tile are
 //             staged in shared memory with cp.async (every row of cells is one contiguous CSR range);
-//             the anchors' leave-one-out terms are evaluated while staging.  Warps then walk the tile's
+//             each anchor record carries its leave-one-out term (fused layout) or its id (drop-in
+//             layout, compared per pair).  Warps then walk the tile's
 //             anchor cells: a cell's anchors in register groups of up to 4, the candidates of its 3x3
 //             neighbourhood streamed by the lanes.  A tile whose neighbourhood does not fit reads its
 //             candidates from global memory instead (same loop, global pointer); a tile with more anchors
