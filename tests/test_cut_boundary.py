@@ -95,3 +95,31 @@ def test_pair_kernels_exact_at_the_cut(n_slots, batches):
     gv = ext.ats_pair_bwd(T(gS), *args, 1, 1, 1, 1.0, 1.0, 3.0, 2 * K).cpu().numpy()
     gvo = O.pair_bwd(p, gS, 1.0, 1.0, 3.0, 2 * K)
     np.testing.assert_allclose(gv, gvo, rtol=1e-4, atol=1e-6 * np.abs(gvo).max())
+
+
+@pytest.mark.gpu
+def test_pair_fwd_with_ids_beyond_32_bits():
+    """Ids outside [0, 2^32) (the reference compares int64 ids): the count pass flags them and every cell
+    takes the untiled kernel, which compares all 64 bits.  Source ids that share their low 32 bits with an
+    anchor's id must still count; the anchor's own source (same 64-bit id) must not."""
+    import torch
+    from oracle import oracle as O
+    from x_b200 import get_ext
+    ext = get_ext()
+    c = craft(400, seed=11)
+    p = plan_of(c, 2)
+    K = c["x"].shape[0]
+    base = np.int64(1) << np.int64(33)
+    # each anchor's own crafted source keeps the anchor's id (excluded); the others alias in the low 32 bits
+    p["anc_id"] = base + np.arange(K, dtype=np.int64)
+    order = p["src_id"] - K
+    p["src_id"] = np.where(order % 2 == 0, base + order, (np.int64(1) << np.int64(34)) + order).astype(np.int64)
+    T = lambda a: torch.as_tensor(np.ascontiguousarray(a)).cuda()
+    args = [T(p[k]) for k in ("src_y", "src_v", "src_t", "src_id", "cell_start", "anc_x", "anc_t", "anc_cell",
+                              "anc_id", "slice_c")]
+    S = ext.ats_pair_fwd(*args, 1, 1, 1, 1.0, 1.0, 3.0).cpu().numpy()
+    So, _ = O.pair_fwd(p, 1.0, 1.0, 3.0)
+    np.testing.assert_allclose(S, So, rtol=2e-6, atol=1e-7)
+    even = (np.arange(K) % 2 == 0)
+    assert np.all(So[even] == 0.0)          # own source (same id) excluded
+    assert np.any(So[~even] > 0.0)          # low-32-bit aliases counted
