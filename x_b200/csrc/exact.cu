@@ -454,18 +454,20 @@ __global__ void __launch_bounds__(kThreads) k_exact_norm(MotionView Mv, NormCons
   }
 }
 
-// Writes S_i and the log score log(eps + S_i / den_i) of original anchor i.
+// Writes S_i of original anchor i (the pair kernels' output).
 struct FusedOut {
   float* S;
-  float* ls;
-  const float* den;
-  float eps;
-  __device__ __forceinline__ void operator()(int i, double v) const {
-    const float s = (float)v;
-    S[i] = s;
-    ls[i] = logf(add_rn(eps, div_rn(s, den[i])));  // log(eps + S / den)
-  }
+  __device__ __forceinline__ void operator()(int i, double v) const { S[i] = (float)v; }
 };
+
+// The log score ls_i = log(eps + S_i / den_i) (ats.py:95), one thread per anchor after the pair sums: the
+// division and the logarithm cost a full warp instruction stream per anchor group inside the pair kernel.
+__global__ void __launch_bounds__(kThreads) k_exact_ls(const float* __restrict__ S, const float* __restrict__ den,
+                                                       float eps, long long M, float* __restrict__ ls) {
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < M; i += stride)
+    ls[i] = logf(add_rn(eps, div_rn(S[i], den[i])));  // log(eps + S / den)
+}
 
 
 // dL/dS in bucket order from the upstream dL/dls (torch's LogBackward then DivBackward).
@@ -534,12 +536,22 @@ __global__ void __launch_bounds__(kThreads) k_exact_vbwd_dense(MotionView Mv, co
     DenseTaps T;
     dense_taps(Mv, e.x, e.y, &T);
     float* G = ggrid + b[j] * 2 * plane;
-    const long long idx[4] = {T.y0 * Mv.Wg + T.x0, T.y0 * Mv.Wg + T.x1, T.y1 * Mv.Wg + T.x0, T.y1 * Mv.Wg + T.x1};
+    // per channel and tap row, the taps (x0, x1) are adjacent floats: one red.v2 when they form an 8-byte
+    // aligned pair, else one red per non-zero tap
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      if (T.w[q] == 0.f) continue;
-      red_add_f1(G + idx[q], g.x * T.w[q]);
-      red_add_f1(G + plane + idx[q], g.y * T.w[q]);
+    for (int c = 0; c < 2; ++c) {
+      const float gc = c ? g.y : g.x;
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        float* row = G + c * plane + (r ? T.y1 : T.y0) * Mv.Wg;
+        const float w0 = T.w[2 * r], w1 = T.w[2 * r + 1];
+        if (T.x1 == T.x0 + 1 && ((reinterpret_cast<uintptr_t>(row + T.x0) & 7) == 0)) {
+          red_add_f2(row + T.x0, gc * w0, gc * w1);
+        } else {
+          if (w0 != 0.f) red_add_f1(row + T.x0, gc * w0);
+          if (w1 != 0.f) red_add_f1(row + T.x1, gc * w1);
+        }
+      }
     }
   }
 }
@@ -819,7 +831,7 @@ int exact_forward(const atlb_exact_cfg& c, const float* t, const long long* b, l
     const dim3 grid((unsigned)((g.GW + kTileX - 1) / kTileX), (unsigned)((g.GH + kTileY - 1) / kTileY),
                     (unsigned)g.S);
     const TileGrid T{(int)g.GW, (int)g.GH, (int)g.S, (int)c.B};
-    const FusedOut out{S_out, ls_out, den_out, eps};
+    const FusedOut out{S_out};
     cudaMemsetAsync(w.scratch, 0, sizeof(int), s);
     cudaEvent_t e0 = timing_begin(s);
     const int* as = (const int*)w.astart;
@@ -839,6 +851,7 @@ int exact_forward(const atlb_exact_cfg& c, const float* t, const long long* b, l
       launch(k_pair_fwd_overflow<false, false, FastEntries, int, FusedOut>, warp_grid(ncell), 256, 0, s, E, A, nullptr,
              as, cs, T, sc, C, out, (const int*)w.scratch);
     timing_end("k_pair_fwd", s, e0);
+    launch(k_exact_ls, grid_for(M), kThreads, 0, s, (const float*)S_out, (const float*)den_out, eps, M, ls_out);
   }
   return launch_status("exact_forward");
 }
