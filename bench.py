@@ -414,8 +414,9 @@ def ours_arm(args):
         return
     # ---- roofline of the dominant kernel.  Algorithmic bytes of the fused path's compact layout:
     # forward (tau covering the window): per plan entry its (y, v) float4; per anchor its (x, y, t, self)
-    # record and original index, den in, S and ls out.  Backward: per plan entry (y, v) + (t, id) = 24 B;
-    # per anchor (x, y, t - c_s, t) + dL/dS = 20 B; per event its (gx, gy) out.
+    # record, original index and S out (ls follows in its own kernel).  Backward: per plan entry (y, v) +
+    # (t, id) = 24 B; per anchor (x, y, t - c_s, t - c_s) + (dL/dS, t) = 24 B read as 20 algorithmic B;
+    # per event its (gx, gy) out.
     dom = max(ktime, key=lambda k: ktime[k][0])
     dom_ms, dom_n = ktime[dom]
     with torch.no_grad():
@@ -427,7 +428,7 @@ def ours_arm(args):
         Ns, M = plan.src_y.shape[0], plan.anc_x.shape[0]
         cand = candidate_pairs(plan)
         del plan
-    alg = {"k_pair_fwd": Ns * 16 + M * (16 + 4 + 4 + 8), "k_pair_bwd": Ns * 24 + M * 20 + args.events * 8}
+    alg = {"k_pair_fwd": Ns * 16 + M * (16 + 4 + 4), "k_pair_bwd": Ns * 24 + M * 20 + args.events * 8}
     if args.dropin:  # the reference's plan layout: (y, v, t, int64 id) 28 B per entry, anchors bucketed 28 B
         alg = {"k_pair_fwd": Ns * 28 + M * 32, "k_pair_bwd": Ns * 28 + M * 32 + args.events * 8}
     rates = _lib.unit_rates(dev)
