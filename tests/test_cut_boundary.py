@@ -123,3 +123,30 @@ def test_pair_fwd_with_ids_beyond_32_bits():
     even = (np.arange(K) % 2 == 0)
     assert np.all(So[even] == 0.0)          # own source (same id) excluded
     assert np.any(So[~even] > 0.0)          # low-32-bit aliases counted
+
+
+@pytest.mark.gpu
+def test_pair_ops_fallback_grid():
+    """A cell count that is not a whole number of S x GH x GW grids cannot be indexed by the tiled kernels:
+    the drop-in ops take the per-cell-warp kernels, with the same results as the oracle."""
+    import torch
+    from oracle import oracle as O
+    from x_b200 import get_ext
+    ext = get_ext()
+    c = craft(300, seed=13)
+    p = plan_of(c, 3)   # 3 one-cell grids ...
+    p["S"] = 2          # ... declared as slices of 2: ncell = 3 is not a multiple of S * GH * GW = 2
+    T = lambda a: torch.as_tensor(np.ascontiguousarray(a)).cuda()
+    args = [T(p[k]) for k in ("src_y", "src_v", "src_t", "src_id", "cell_start", "anc_x", "anc_t", "anc_cell",
+                              "anc_id", "slice_c")]
+    args[-1] = T(np.array([0.5, 0.5], f32))  # one centre per declared slice
+    p["slice_c"] = np.array([0.5, 0.5], f32)
+    S = ext.ats_pair_fwd(*args, 2, 1, 1, 1.0, 1.0, 3.0).cpu().numpy()
+    So, hits = O.pair_fwd(p, 1.0, 1.0, 3.0)
+    assert hits == int(c["accept"].sum())
+    np.testing.assert_allclose(S, So, rtol=2e-6, atol=1e-7)
+    K = c["x"].shape[0]
+    gS = np.linspace(0.5, 1.5, K).astype(f32)
+    gv = ext.ats_pair_bwd(T(gS), *args, 2, 1, 1, 1.0, 1.0, 3.0, 2 * K).cpu().numpy()
+    gvo = O.pair_bwd(p, gS, 1.0, 1.0, 3.0, 2 * K)
+    np.testing.assert_allclose(gv, gvo, rtol=1e-4, atol=1e-6 * np.abs(gvo).max())
