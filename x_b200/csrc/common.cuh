@@ -26,9 +26,6 @@ __device__ __forceinline__ float mul_rn(float a, float b) { return __fmul_rn(a, 
 __device__ __forceinline__ float div_rn(float a, float b) { return __fdiv_rn(a, b); }
 __device__ __forceinline__ float clampf(float v, float lo, float hi) { return v < lo ? lo : (v > hi ? hi : v); }
 
-// Same as C's (int64_t)floorf(q) for in-range q; out-of-range values only ever feed range checks.
-__device__ __forceinline__ long long floor_to_ll(float q) { return (long long)floorf(q); }
-
 // Ordered-int encoding of floats for atomicMin / atomicMax over signed values.
 __device__ __forceinline__ int float_to_ordered(float f) {
   int i = __float_as_int(f);

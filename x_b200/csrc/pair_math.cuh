@@ -50,19 +50,6 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
-// Branch-free pair evaluation for the fused kernels: the same acceptance test as pair_test (exact
-// rounding of r and d^2), the kernel value selected to 0 for rejected pairs.
-__device__ __forceinline__ float pair_eval(const PairConsts& C, float xi, float yi, float ti, float dti, float2 sy,
-                                           float2 sv, float st, bool same, float* rx, float* ry, float* dt) {
-  *dt = sub_rn(ti, st);
-  *rx = sub_rn(xi, add_rn(sy.x, mul_rn(sv.x, dti)));
-  *ry = sub_rn(yi, add_rn(sy.y, mul_rn(sv.y, dti)));
-  const float d2 = add_rn(mul_rn(*rx, *rx), mul_rn(*ry, *ry));
-  const bool ok = !(fabsf(*dt) > C.tau) && !(d2 > C.r2max) && !same;
-  const float e = ex2_approx(-d2 * C.k2);
-  return ok ? e : 0.f;
-}
-
 // f = gS_i * k * dt / h^2, in the reference's order (atl_cpu.cpp:244).
 __device__ __forceinline__ float pair_grad_factor(const PairConsts& C, float gi, float kern, float dt) {
   return mul_rn(mul_rn(mul_rn(gi, kern), dt), C.invh2);
