@@ -54,6 +54,8 @@ def parse():
                          "on 1280x720 shared by all GPUs (sources split across ranks, NCCL all-reduce); splat: the "
                          "Gaussian splat forward + backward of one slice of configuration 3 (sigma 1.5, 8 x 2M)")
     ap.add_argument("--cpu-worker", default=None, help=argparse.SUPPRESS)
+    ap.add_argument("--record-traffic", nargs=2, metavar=("CSV", "COMMAND"), default=None,
+                    help="write the per-launch DRAM traffic of the pair kernels from an ncu raw CSV export")
     return ap.parse_args()
 
 
@@ -98,6 +100,52 @@ def run_reference_steps(xy, t, p, b, flow, steps, warmup, budget_s=None):
     return times
 
 
+def run_port_steps(xy, t, b, flow, steps, warmup, budget_s=None):
+    """The C restatement of the reference's path (oracle/atl_oracle.c, OpenMP) on the same window and the same
+    per-step work as the reference's objective: the host draws of the dequantisation and smoothing noise (the
+    objective's CPU generator), the pair plan, pair sums, window counts, exposure correction, score and the
+    backward to the flow grid.  Returns per-step seconds."""
+    import numpy as np
+    import torch
+    from oracle import oracle as O
+    torch.set_num_threads(os.cpu_count() or 1)
+    xy_n, t_n, b_n, flow_n = xy.numpy(), t.numpy(), b.numpy(), flow.numpy()
+    n = t_n.shape[0]
+    anchors = np.arange(n, dtype=np.int64)
+    gen = torch.Generator().manual_seed(7)
+
+    def step():
+        u = torch.rand((n, 2), generator=gen).numpy()
+        z = torch.randn((n, 2), generator=gen).numpy()
+        xs = (xy_n + (u - np.float32(0.5))).astype(np.float32)
+        xa = (xs + z).astype(np.float32)
+        return O.anchored_exact("dense", flow_n, xs, t_n, b_n, 1, H, W, anchors, xa)["loss"]
+
+    for _ in range(warmup):
+        step()
+    times = []
+    t_start = time.perf_counter()
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        step()
+        times.append(time.perf_counter() - t0)
+        if budget_s is not None and time.perf_counter() - t_start > budget_s:
+            break
+    return times
+
+
+def reference_or_port(xy, t, p, b, flow, steps, warmup, budget_s):
+    """Times the reference's own CPU path (kind "reference"); where its package or its compiled extension is
+    not present on this host, the C restatement of the same path (kind "port").  Returns (times, kind, note)."""
+    try:
+        from oracle.refload import load_reference
+        load_reference()
+    except ImportError as e:
+        note = f"reference not importable here ({str(e)[:120]}); timed the C port of its CPU path"
+        return run_port_steps(xy, t, b, flow, steps, warmup, budget_s), "port", note
+    return run_reference_steps(xy, t, p, b, flow, steps, warmup, budget_s), "reference", ""
+
+
 def reference_arm(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -105,50 +153,63 @@ def reference_arm(args):
     try:
         ev, flow = window_data(0, args.events)
         budget = 150.0
-        times = run_reference_steps(ev.xy, ev.t, ev.p, ev.b, flow, args.steps, min(args.warmup, 1), budget_s=budget)
-    except Exception as e:  # the reference could not run here
+        times, kind, note = reference_or_port(ev.xy, ev.t, ev.p, ev.b, flow, args.steps, min(args.warmup, 1), budget)
+    except Exception as e:  # neither the reference nor its C port could run here
         print(json.dumps({"impl": "reference", "unavailable": f"{type(e).__name__}: {e}"[:300]}))
         return
     ms = 1000 * statistics.mean(times)
     value = args.events / (ms / 1000)
     cores = os.cpu_count() or 1
-    sample = (f"full workload per step ({args.events} events, all anchors); {len(times)} timed steps"
-              + (" (capped by a 150 s budget)" if len(times) < args.steps else "") + f", {min(args.warmup, 1)} warm-up")
+    what = ("reference AnchoredExact + its OpenMP kernels" if kind == "reference"
+            else "C port of the reference's CPU path (OpenMP)")
+    sample = (f"full workload per step ({args.events} events, all anchors, host noise draws included; {what}); "
+              f"{len(times)} timed steps" + (" (capped by a 150 s budget)" if len(times) < args.steps else "")
+              + f", {min(args.warmup, 1)} warm-up" + (f"; {note}" if note else ""))
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": value, "unit": "events/s", "n_gpus": args.gpus,
         "steps": len(times), "warmup": min(args.warmup, 1), "ms_per_step": ms, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": WORKLOAD, "events_per_window": args.events, "device": "cpu"},
-        "cpu_baseline": {"value": value, "unit": "events/s", "cores": cores, "kind": "reference", "sample": sample},
+        "cpu_baseline": {"value": value, "unit": "events/s", "cores": cores, "kind": kind, "sample": sample},
         "e2e": {"value": value, "unit": "events/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }))
 
 
 def cpu_worker(path):
-    """Subprocess body of the cpu_baseline leg: time the reference on the saved window."""
+    """Subprocess body of the cpu_baseline leg: time the reference (or its C port) on the saved window."""
     import torch
     d = torch.load(path)
-    times = run_reference_steps(d["xy"], d["t"], d["p"], d["b"], d["flow"], steps=3, warmup=1, budget_s=25.0)
-    print(json.dumps({"times": times}))
+    times, kind, note = reference_or_port(d["xy"], d["t"], d["p"], d["b"], d["flow"], steps=3, warmup=1,
+                                          budget_s=25.0)
+    print(json.dumps({"times": times, "kind": kind, "note": note}))
 
 
 def cpu_baseline(ev, flow, n):
-    """The reference's CPU path timed on this host (bounded: 1 warm-up + up to 3 steps, <= ~25 s)."""
+    """The reference's CPU path timed on this host (bounded: 1 warm-up + up to 3 steps, <= ~25 s), in a child
+    process without the GPU.  A failure reports the child's own error output."""
     import torch
+    cores = os.cpu_count()
     try:
         with tempfile.TemporaryDirectory() as td:
             path = os.path.join(td, "win.pt")
             torch.save({"xy": ev.xy.cpu(), "t": ev.t.cpu(), "p": ev.p.cpu(), "b": ev.b.cpu(), "flow": flow.cpu()}, path)
-            env = dict(os.environ, OMP_NUM_THREADS=str(os.cpu_count() or 1), CUDA_VISIBLE_DEVICES="")
+            env = dict(os.environ, OMP_NUM_THREADS=str(cores or 1), CUDA_VISIBLE_DEVICES="")
             r = subprocess.run([sys.executable, __file__, "--cpu-worker", path], capture_output=True, text=True,
                                env=env, timeout=600)
-            times = json.loads(r.stdout.strip().splitlines()[-1])["times"]
     except Exception as e:
-        return {"value": None, "unit": "events/s", "cores": os.cpu_count(), "kind": "reference",
+        return {"value": None, "unit": "events/s", "cores": cores, "kind": "reference",
                 "sample": f"unavailable: {type(e).__name__}: {str(e)[:200]}"}
-    return {"value": n / statistics.mean(times), "unit": "events/s", "cores": os.cpu_count(), "kind": "reference",
-            "sample": f"the same 1M-event window, full fwd+bwd, {len(times)} timed steps after 1 warm-up "
-                      f"(reference AnchoredExact + its OpenMP kernels, {os.cpu_count()} threads)"}
+    lines = [ln for ln in r.stdout.strip().splitlines() if ln.startswith("{")]
+    if r.returncode != 0 or not lines:
+        return {"value": None, "unit": "events/s", "cores": cores, "kind": "reference",
+                "sample": f"unavailable: child exited {r.returncode}: {r.stderr.strip()[-300:]}"}
+    d = json.loads(lines[-1])
+    times, kind = d["times"], d["kind"]
+    what = ("reference AnchoredExact + its OpenMP kernels" if kind == "reference"
+            else "C port of the reference's CPU path")
+    return {"value": n / statistics.mean(times), "unit": "events/s", "cores": cores, "kind": kind,
+            "sample": f"the same 1M-event window, full fwd+bwd with the host noise draws, {len(times)} timed steps "
+                      f"after 1 warm-up ({what}, {cores} threads)" + (f"; {d['note']}" if d.get("note") else "")}
 
 
 # ------------------------------------------------------------------------------------------------ clocks
@@ -227,7 +288,7 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------------------------------------------ ours
-PROFILE_SUMMARY = ROOT / "profiles" / "pair_kernels.config2_1M.md"
+PROFILE_TRAFFIC = ROOT / "profiles" / "traffic.config2_1M.json"
 
 
 def candidate_pairs(plan) -> int:
@@ -266,17 +327,42 @@ def compute_roofline(kernel, candidates, entries, alg_bytes, avg_ms, rates):
 
 
 def profiled_traffic(kernel):
-    """DRAM bytes (read + write) per launch of ``kernel`` from the committed ncu summary of this workload
-    (a line ``traffic <kernel> <bytes>``), or None."""
-    import re
+    """DRAM bytes (read + write) per launch of ``kernel`` from the ncu capture of this workload recorded in
+    PROFILE_TRAFFIC (written by ``--record-traffic``), or None."""
     try:
-        for line in open(PROFILE_SUMMARY):
-            m_ = re.match(r"\s*[-*]?\s*traffic\s+(\w+)\s+(\d+)", line)
-            if m_ and m_.group(1) == kernel:
-                return int(m_.group(2))
-    except OSError:
-        pass
-    return None
+        d = json.load(open(PROFILE_TRAFFIC))
+        return int(d["kernels"][kernel]["dram_bytes_per_launch"])
+    except (OSError, KeyError, ValueError, TypeError):
+        return None
+
+
+def record_traffic(csv_path, command):
+    """Writes PROFILE_TRAFFIC from an ncu raw-page CSV export (``ncu -i <report> --page raw --csv``): per kernel
+    (matched by the pair-kernel names the bench times), the mean of dram__bytes_read.sum + dram__bytes_write.sum
+    over the captured launches."""
+    import csv
+    names = {"k_pair_fwd": "k_pair_fwd", "k_pair_bwd": "k_pair_bwd"}
+    rows = list(csv.reader(open(csv_path)))
+    head = rows[0]
+    col = {h: i for i, h in enumerate(head)}
+    units = rows[1] if len(rows) > 1 and not rows[1][col["Kernel Name"]].strip() else None
+    scale = {"byte": 1, "Kbyte": 1e3, "Mbyte": 1e6, "Gbyte": 1e9, "KB": 1e3, "MB": 1e6, "GB": 1e9}
+    acc = {}
+    for r in rows[2 if units else 1:]:
+        kname = r[col["Kernel Name"]]
+        key = next((k for k, pat in names.items() if pat in kname), None)
+        if key is None:
+            continue
+        tot = 0.0
+        for m_ in ("dram__bytes_read.sum", "dram__bytes_write.sum"):
+            v = float(r[col[m_]].replace(",", ""))
+            tot += v * (scale.get(units[col[m_]], 1) if units else 1)
+        acc.setdefault(key, []).append(tot)
+    out = {"source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, mean over the captured launches",
+           "command": command,
+           "kernels": {k: {"dram_bytes_per_launch": int(sum(v) / len(v)), "launches": len(v)} for k, v in acc.items()}}
+    PROFILE_TRAFFIC.write_text(json.dumps(out, indent=1) + "\n")
+    print(json.dumps(out))
 
 
 def measured_peak():
@@ -397,7 +483,7 @@ def ours_arm(args):
             e2 = EventPacket(d["xy"], d["t"], ev.p, d["b"], 1, H, W)
             loss = step(e2, (torch.arange(args.events, device=dev), d["u"], d["z"]))
             freed[slot].record()
-            float(loss)
+            float(loss.detach())
         e_end.record()
         torch.cuda.synchronize()
         return e_start.elapsed_time(e_end)
@@ -451,7 +537,7 @@ def ours_arm(args):
                    "parallelism": f"replicas x{world}"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "traffic": traffic, "kernel": dom, "avg_launch_ms": avg_ms, "algorithmic_bytes": alg_bytes,
-                     "peak_source": peak_kind, "traffic_source": PROFILE_SUMMARY.name if traffic else None},
+                     "peak_source": peak_kind, "traffic_source": PROFILE_TRAFFIC.name if traffic else None},
         "roofline_compute": compute,
         "unit_rates": {**{k: v for k, v in rates.items()}, "source": "atlb_measure_unit_rates on this GPU, after the timed region"},
         "kernels_ms_per_step": {k: v[0] / max(v[1], 1) for k, v in ktime.items()},
@@ -682,6 +768,9 @@ def main():
     args = parse()
     if args.cpu_worker:
         cpu_worker(args.cpu_worker)
+        return
+    if args.record_traffic:
+        record_traffic(*args.record_traffic)
         return
     if args.impl == "reference":
         reference_arm(args)

@@ -146,16 +146,19 @@ int atlb_ats_pair_fwd(const float* src_y, const float* src_v, const float* src_t
                       int64_t GH, int64_t GW, double h, double tau, double cut, float* out, void* workspace,
                       size_t workspace_bytes, atlb_stream_t stream);
 /* atlb_ats_pair_fwd without a workspace argument: the same sums, for callers that cannot allocate
- * device memory when they need them (code running inside someone else's stream capture, hosts that give
- * the library a fixed memory budget, FFI layers without a device allocator).  No counterpart in the
- * reference: it is an addition of this library.  The anchor buckets live in one file-scope device
+ * device memory when they need them -- hosts that give the library a fixed device-memory budget (a
+ * custom allocator, an embedded runtime), loops that forbid cudaMalloc after start-up because it can
+ * synchronise the device, and FFI layers that have no device allocator of their own.  No counterpart in
+ * the reference: it is an addition of this library.  The anchor buckets live in one file-scope device
  * array of ATLB_PAIR_NOALLOC_SCRATCH_BYTES, which every device that loads the library holds until the
- * process exits; the call allocates nothing.  Sizes with atlb_pair_workspace_bytes(M, ncell) above
- * that limit fail with ATLB_ERR_WORKSPACE before any device work.  The first call on a device looks up
- * the array's device address (cudaGetSymbolAddress, with that device current), so make that first
- * call before any stream capture.  All calls share the array: calls whose work overlaps on the GPU
- * (other streams or host threads) race; calls ordered on one stream do not.  Not covered by
- * atlb_timing_*. */
+ * process exits; the call allocates nothing.  A call needs atlb_pair_workspace_bytes(M, ncell) - 256
+ * bytes of it (the array is 256-byte aligned, so the workspace's alignment slack is not needed); larger
+ * sizes fail with ATLB_ERR_WORKSPACE before any device work.  The first call on a device looks up the
+ * array's device address (cudaGetSymbolAddress, with that device current) and keeps it for the process,
+ * so make that first call before any stream capture; the kept address belongs to the device's primary
+ * context and does not survive cudaDeviceReset or a switch to another context on that device.  All
+ * calls share the array: calls whose work overlaps on the GPU (other streams or host threads) race;
+ * calls ordered on one stream do not.  Not covered by atlb_timing_*. */
 #define ATLB_PAIR_NOALLOC_SCRATCH_BYTES ((size_t)16 << 20)
 int atlb_ats_pair_fwd_noalloc(const float* src_y, const float* src_v, const float* src_t, const int64_t* src_id,
                               const int64_t* cell_start, const float* anc_x, const float* anc_t,

@@ -260,6 +260,37 @@ ORACLE_API void oracle_pair_bwd(const float* G, const float* SY, const float* SV
   }
 }
 
+/* The same gradient as oracle_pair_bwd with every contribution f*r (rounded as the reference rounds it)
+ * summed in double: the accurate value that fp32 results of any summation order are compared against.
+ * Also returns, per event component, the sum of |contribution| (gabs) and the number of contributions
+ * (cnt): the ingredients of the fp32 summation bound |err| <= (cnt - 1) u sum|x| + per-term rounding. */
+ORACLE_API void oracle_pair_bwd_f64(const float* G, const float* SY, const float* SV, const float* ST,
+                                    const int64_t* SID, const int64_t* CS, const float* AX, const float* AT,
+                                    const int64_t* AC, const int64_t* AID, const float* SC, int64_t M, int64_t S,
+                                    int64_t GH, int64_t GW, double h, double tau, double cut, int64_t N, double* gv,
+                                    double* gabs, int64_t* cnt) {
+  const pair_args A = make_pair_args(SY, SV, ST, SID, CS, AX, AT, AC, AID, SC, S, GH, GW, h, tau, cut);
+  const float invh2 = 1.f / (float)(h * h);
+  memset(gv, 0, sizeof(double) * (size_t)(2 * N));
+  memset(gabs, 0, sizeof(double) * (size_t)(2 * N));
+  memset(cnt, 0, sizeof(int64_t) * (size_t)N);
+  for (int64_t i = 0; i < M; ++i) {
+    const float gi = G[i];
+    if (gi == 0.f) continue;
+    FOR_EACH_PAIR(A, i, {
+      const float f = gi * kern * dt * invh2;
+      const int64_t j = A.SID[k];
+      const float cx = f * rx;
+      const float cy = f * ry;
+      gv[2 * j] += (double)cx;
+      gv[2 * j + 1] += (double)cy;
+      gabs[2 * j] += fabs((double)cx);
+      gabs[2 * j + 1] += fabs((double)cy);
+      cnt[j] += 1;
+    });
+  }
+}
+
 /* ------------------------------------------------------------------------------------------------
  * Splat / gather / voxel.  csrc/atl_cpu.cpp:17-33 (bilinear_corners), :38-131, :134-172, :256-286.
  * ---------------------------------------------------------------------------------------------- */

@@ -57,6 +57,9 @@ def lib():
                                              ctypes.POINTER(ctypes.c_int64)]
         L.oracle_pair_bwd.restype = None
         L.oracle_pair_bwd.argtypes = [_f32p] + pair + [_i64, _i64, _i64, _i64, _dbl, _dbl, _dbl, _i64, _f32p]
+        L.oracle_pair_bwd_f64.restype = None
+        L.oracle_pair_bwd_f64.argtypes = [_f32p] + pair + [_i64, _i64, _i64, _i64, _dbl, _dbl, _dbl, _i64, _f64p, _f64p,
+                                                          _i64p]
         L.oracle_splat_bilinear_fwd.argtypes = [_f32p, _f32p, _i64p, _i64, _i64, _i64, _i64, _f32p]
         L.oracle_splat_bilinear_bwd.argtypes = [_f32p, _f32p, _f32p, _i64p, _i64, _i64, _i64, _f32p, _f32p]
         L.oracle_splat_gauss_fwd.argtypes = [_f32p, _f32p, _i64p, _i64, _i64, _i64, _i64, _dbl, _i64, _f32p]
@@ -144,6 +147,17 @@ def pair_bwd(p, g, h, tau, cut, N):
     L.oracle_pair_bwd(_f(g), *_pair_arrays(p), M, p["S"], p["GH"], p["GW"], float(h), float(tau), float(cut), N,
                       gv)
     return gv
+
+
+def pair_bwd_f64(p, g, h, tau, cut, N):
+    """The pair gradient with double accumulation (the accurate value), plus per component the sum of the
+    contributions' magnitudes and per event their count: (gv (N,2) f64, gabs (N,2) f64, cnt (N,) i64)."""
+    L = lib()
+    M = p["anc_t"].shape[0]
+    gv, gabs, cnt = np.zeros((N, 2)), np.zeros((N, 2)), np.zeros(N, np.int64)
+    L.oracle_pair_bwd_f64(_f(g), *_pair_arrays(p), M, p["S"], p["GH"], p["GW"], float(h), float(tau), float(cut), N,
+                          gv, gabs, cnt)
+    return gv, gabs, cnt
 
 
 def ats_pair_sums(x, t, v, b, B, H, W, anchors, h, tau, cut=3.0, n_slices=16, anchor_xy=None):
@@ -263,11 +277,13 @@ def visible_fraction(kind, theta, xa, ta, ba, t, b, B, H, W, tau, n_check=16):
 
 # ------------------------------------------------------------------------------------------------- objective
 def anchored_exact(kind, theta, xs, t, b, B, H, W, anchors, xa, h=1.0, tau=1.0, eps_frac=1e-2, n_slices=16,
-                   cut=3.0, visibility=True, with_grad=True):
+                   cut=3.0, visibility=True, with_grad=True, exact_grad=False):
     """AnchoredExact.log_scores + loss + gradient (atl/objectives/ats.py:75-105) on pre-drawn inputs:
     ``xs`` are the dequantised positions, ``xa`` the (smoothed) anchor positions.
 
-    Returns dict(ls (M,), loss, S (M,), Wn (M,), vis (M,), grad_v (N,2), grad_theta, hits)."""
+    Returns dict(ls (M,), loss, S (M,), Wn (M,), vis (M,), grad_v (N,2), grad_theta, hits); with
+    ``exact_grad`` also the double-accumulated gradients (grad_v64, grad_theta64) and the fp32 error-bound
+    ingredients (grad_v_abs, grad_v_cnt, grad_theta_abs, grad_theta_terms)."""
     xs, t, b, anchors, xa = _f(xs).reshape(-1, 2), _f(t), _l(b), _l(anchors), _f(xa).reshape(-1, 2)
     N, M = t.shape[0], anchors.shape[0]
     v = velocity(kind, theta, xs, b, H, W)
@@ -289,7 +305,52 @@ def anchored_exact(kind, theta, xs, t, b, B, H, W, anchors, xa, h=1.0, tau=1.0, 
         gv = pair_bwd(p, gS, h, tau, cut, N)
         out["grad_v"] = gv
         out["grad_theta"] = velocity_backward(kind, theta, xs, b, H, W, gv)
+        if exact_grad:
+            gv64, gabs, cnt = pair_bwd_f64(p, gS, h, tau, cut, N)
+            out["grad_v64"], out["grad_v_abs"], out["grad_v_cnt"] = gv64, gabs, cnt
+            out["grad_theta64"] = velocity_backward(kind, theta, xs, b, H, W, gv64)
+            out["grad_theta_abs"], out["grad_theta_terms"] = velocity_backward_bound(kind, theta, xs, b, H, W, gabs,
+                                                                                      cnt)
     return out
+
+
+def velocity_backward_bound(kind, theta, xy, b, H, W, gabs, cnt):
+    """Ingredients of the fp32 error bound of d(sum gv . v)/d theta when every gv_j is itself an fp32 sum of
+    cnt_j terms with magnitude sum gabs_j: returns (A, n) per theta element, A = sum_j |w_j| gabs_j (w_j the
+    element's weight of event j) and n = max_j cnt_j + (events reaching the element), the term count of the
+    two-level sum."""
+    theta = np.asarray(theta)
+    xy, gabs, b = np.asarray(xy, np.float64).reshape(-1, 2), np.asarray(gabs, np.float64).reshape(-1, 2), _l(b)
+    A = np.zeros(theta.shape, np.float64)
+    m = np.zeros(theta.shape, np.float64)
+    one = np.ones(b.shape[0])
+    if kind == "translation":
+        np.add.at(A, b, gabs)
+        np.add.at(m[:, 0], b, one); m[:, 1] = m[:, 0]
+    elif kind == "affine":
+        c = np.array([np.float32((W - 1) / 2.0), np.float32((H - 1) / 2.0)], np.float64)
+        d = np.abs((xy.astype(np.float32) - c.astype(np.float32)).astype(np.float64))
+        np.add.at(A[:, 0], b, gabs[:, 0]); np.add.at(A[:, 1], b, gabs[:, 1])
+        np.add.at(A[:, 2], b, gabs[:, 0] * d[:, 0]); np.add.at(A[:, 3], b, gabs[:, 0] * d[:, 1])
+        np.add.at(A[:, 4], b, gabs[:, 1] * d[:, 0]); np.add.at(A[:, 5], b, gabs[:, 1] * d[:, 1])
+        for k in range(6):
+            np.add.at(m[:, k], b, one)
+    else:
+        Bn, C, Hg, Wg = theta.shape
+        x32 = xy.astype(np.float32)
+        gx = (x32[:, 0] / np.float32(max(W - 1, 1))).astype(np.float32) * np.float32(Wg - 1)
+        gy = (x32[:, 1] / np.float32(max(H - 1, 1))).astype(np.float32) * np.float32(Hg - 1)
+        gx = np.clip(gx.astype(np.float32), 0, Wg - 1); gy = np.clip(gy.astype(np.float32), 0, Hg - 1)
+        x0 = np.minimum(np.floor(gx), max(Wg - 2, 0)); y0 = np.minimum(np.floor(gy), max(Hg - 2, 0))
+        ax, ay = (gx - x0).astype(np.float64), (gy - y0).astype(np.float64)
+        x0, y0 = x0.astype(np.int64), y0.astype(np.int64)
+        x1, y1 = np.minimum(x0 + 1, Wg - 1), np.minimum(y0 + 1, Hg - 1)
+        for yy, xx, w in ((y0, x0, (1 - ax) * (1 - ay)), (y0, x1, ax * (1 - ay)), (y1, x0, (1 - ax) * ay),
+                          (y1, x1, ax * ay)):
+            for c in range(C):
+                np.add.at(A[:, c], (b, yy, xx), w * gabs[:, c])
+                np.add.at(m[:, c], (b, yy, xx), one)
+    return A, m + float(np.max(cnt, initial=0))
 
 
 def threads() -> int:

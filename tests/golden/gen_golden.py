@@ -221,6 +221,45 @@ def gen_sliced(name, kind, n, B, H, W, seed, S, sigma, K=3):
          ls=ls.detach(), idx=idx, loss=loss.detach(), grad=param.grad)
 
 
+def gen_traj(name, K, basis_kind, per_event, seed, B=2, H=48, W=64, n=3000, scale=10.0):
+    """PixelTrajectories.transport (atl/motion/trajectories.py:62-81) of seeded events: the transported
+    positions and the gradient of sum(y * w) w.r.t. the coefficient grid, with positions spilling past the
+    border (clamped coefficient samples) and scalar or per-event target times."""
+    g = torch.Generator().manual_seed(seed)
+    coeff = torch.nn.functional.avg_pool2d(torch.randn(B, 2 * K, H, W, generator=g), 9, 1, 4) * scale
+    xy = torch.stack([torch.rand(n, generator=g) * (W + 16) - 8, torch.rand(n, generator=g) * (H + 16) - 8], 1)
+    t = torch.rand(n, generator=g)
+    b = torch.randint(0, B, (n,), generator=g)
+    t_dst = torch.rand(n, generator=g) if per_event else torch.tensor(0.375)
+    w = torch.randn(n, 2, generator=g)
+    c = coeff.clone().requires_grad_(True)
+    m = PixelTrajectories(c, K, basis_kind=basis_kind, tile=4)
+    y = m.transport(xy, t, t_dst if per_event else 0.375, b)
+    (y * w).sum().backward()
+    save(name, K=K, basis=basis_kind, per_event=per_event, coeff=coeff, xy=xy, t=t, b=b, t_dst=t_dst, w=w,
+         y=y.detach(), grad=c.grad)
+
+
+def gen_exact_traj(name, n, B, H, W, seed, n_anchors=None, h=1.0):
+    """AnchoredExact with PixelTrajectories(K=1, "polynomial") -- the trainer's loss call
+    (atl/train/trainer.py:167; exact-path eligible by atl/motion/trajectories.py:54) -- on a seeded batch of
+    windows: per-anchor log scores, loss, and the gradient w.r.t. the coefficient grid."""
+    xy, t, b = synth_window(n, H, W, seed, B)
+    ev = EventPacket(xy, t, torch.ones(n), b, B, H, W)
+    g = torch.Generator().manual_seed(seed + 1)
+    coeff = torch.nn.functional.avg_pool2d(torch.randn(B, 2, H, W, generator=g), 9, 1, 4) * 40
+    init = coeff.clone()
+    coeff.requires_grad_(True)
+    m = PixelTrajectories(coeff, 1, basis_kind="polynomial", tile=4)
+    assert m.linear_at_event
+    obj = ATS.AnchoredExact(h=h, tau=1.0, n_anchors=n_anchors, n_slices=16, seed=seed + 2, visibility=True)
+    ls, anchors = obj.log_scores(ev, m)
+    loss = -ls.mean()
+    loss.backward()
+    save(name, xy=xy, t=t, b=b, B=B, H=H, W=W, h=h, seed=seed + 2, coeff=init, anchors=anchors, ls=ls.detach(),
+         loss=loss.detach(), grad=coeff.grad)
+
+
 if __name__ == "__main__":
     gen_ops()
     gen_plan("plan_tau1_s8", 600, 2, 20, 24, 3, 6.0, 1.0, 8, 1.5)
@@ -235,3 +274,8 @@ if __name__ == "__main__":
     gen_sliced("sliced_trajectories", "trajectories", 3000, 2, 48, 64, 70, 4, 1.5)
     gen_sliced("sliced_affine_exact", "affine_exact", 3000, 1, 48, 64, 80, 5, 1.0)
     gen_sliced("sliced_dense", "dense", 3000, 1, 48, 64, 90, 4, 2.0)
+    gen_traj("traj_k10_bezier", 10, "bezier", False, 101)
+    gen_traj("traj_k3_poly_pe", 3, "polynomial", True, 102)
+    gen_traj("traj_k1_poly", 1, "polynomial", False, 103)
+    gen_traj("traj_k4_bezier_pe", 4, "bezier", True, 104)
+    gen_exact_traj("exact_traj_k1", 4000, 4, 48, 64, 110)

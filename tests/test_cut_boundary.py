@@ -10,6 +10,8 @@ boundary pair.  The CPU test pins the oracle to the exact sequence; the GPU test
 import numpy as np
 import pytest
 
+from tests.parity import assert_grad_parity
+
 f32 = np.float32
 
 
@@ -93,8 +95,8 @@ def test_pair_kernels_exact_at_the_cut(n_slots, batches):
     K = c["x"].shape[0]
     gS = np.linspace(0.5, 1.5, K).astype(f32)
     gv = ext.ats_pair_bwd(T(gS), *args, 1, 1, 1, 1.0, 1.0, 3.0, 2 * K).cpu().numpy()
-    gvo = O.pair_bwd(p, gS, 1.0, 1.0, 3.0, 2 * K)
-    np.testing.assert_allclose(gv, gvo, rtol=1e-4, atol=1e-6 * np.abs(gvo).max())
+    gvo, gabs, cnt = O.pair_bwd_f64(p, gS, 1.0, 1.0, 3.0, 2 * K)
+    assert_grad_parity(gv, gvo, A=gabs, n=cnt[:, None], what="pair gradient at the cut")
 
 
 @pytest.mark.gpu
@@ -148,5 +150,5 @@ def test_pair_ops_fallback_grid():
     K = c["x"].shape[0]
     gS = np.linspace(0.5, 1.5, K).astype(f32)
     gv = ext.ats_pair_bwd(T(gS), *args, 2, 1, 1, 1.0, 1.0, 3.0, 2 * K).cpu().numpy()
-    gvo = O.pair_bwd(p, gS, 1.0, 1.0, 3.0, 2 * K)
-    np.testing.assert_allclose(gv, gvo, rtol=1e-4, atol=1e-6 * np.abs(gvo).max())
+    gvo, gabs, cnt = O.pair_bwd_f64(p, gS, 1.0, 1.0, 3.0, 2 * K)
+    assert_grad_parity(gv, gvo, A=gabs, n=cnt[:, None], what="pair gradient at the cut")

@@ -9,6 +9,7 @@ import torch
 
 from oracle import oracle as O
 from tests.goldens import load, plan_of, sort_within_cells
+from tests.parity import assert_grad_parity, grad_errors
 
 pytestmark = pytest.mark.gpu
 
@@ -72,8 +73,10 @@ def test_splat_gather_vs_oracle(ext, n, B, H, W, sigma):
     gimg = rng.normal(size=(B, H, W)).astype(np.float32)
     gp, gw = ext.splat_gauss_bwd(T(gimg), T(pos), T(w), T(b), sigma, R)
     ogp, ogw = O.splat_gauss_bwd(gimg, pos, w, b, sigma, R)
-    np.testing.assert_allclose(np_(gp), ogp, rtol=1e-4, atol=1e-5)
-    np.testing.assert_allclose(np_(gw), ogw, rtol=1e-4, atol=1e-5)
+    if n:
+        for got, ref, what in ((np_(gp), ogp, "d pos"), (np_(gw), ogw, "d w")):
+            e = assert_grad_parity(got, ref, what=f"Gaussian splat {what}")
+            assert e["max_over_max"] <= 1e-5, e
     val = ext.gather_bilinear_fwd(T(gimg), T(pos), T(b))
     np.testing.assert_array_equal(np_(val), O.gather_fwd(gimg, pos, b))
 
@@ -117,8 +120,11 @@ def test_pair_fwd_bwd_vs_reference(ext, name):
     h, tau = float(g["h"]), float(g["tau"])
     S = ext.ats_pair_fwd(*args, pl["S"], pl["GH"], pl["GW"], h, tau, 3.0)
     np.testing.assert_allclose(np_(S), g["pair_S"], rtol=RTOL, atol=1e-6)
-    gv = ext.ats_pair_bwd(T(g["gS"]), *args, pl["S"], pl["GH"], pl["GW"], h, tau, 3.0, g["pos"].shape[0])
-    np.testing.assert_allclose(np_(gv), g["pair_gv"], rtol=1e-4, atol=1e-5 * np.abs(g["pair_gv"]).max())
+    n = g["pos"].shape[0]
+    gv = np_(ext.ats_pair_bwd(T(g["gS"]), *args, pl["S"], pl["GH"], pl["GW"], h, tau, 3.0, n))
+    assert_grad_parity(gv, g["pair_gv"], what="pair gradient vs the reference")
+    gv64, gabs, cnt = O.pair_bwd_f64(pl, g["gS"], h, tau, 3.0, n)
+    assert_grad_parity(gv, gv64, A=gabs, n=cnt[:, None], what="pair gradient vs the double-accumulated oracle")
 
 
 def test_ats_pair_sums_autograd_matches_bruteforce_reference():
@@ -131,7 +137,7 @@ def test_ats_pair_sums_autograd_matches_bruteforce_reference():
                             T(g["anchors"]), float(g["h"]), float(g["tau"]), 3.0, int(g["S"]))
         np.testing.assert_allclose(np_(s), g["brute_S"], rtol=1e-4, atol=1e-4)
         (s * T(g["gS"])).sum().backward()
-        np.testing.assert_allclose(np_(v.grad), g["pair_gv"], rtol=1e-3, atol=1e-4)
+        assert_grad_parity(np_(v.grad), g["pair_gv"], what=f"ats_pair_sums autograd ({name})")
 
 
 @pytest.mark.parametrize("n,tau,S,vs", [(60000, 1.0, 16, 20.0), (40000, 0.1, 8, 5.0), (30000, 0.3, 24, 40.0)])
@@ -161,8 +167,8 @@ def test_plan_and_pairs_vs_oracle_larger(ext, n, tau, S, vs):
     gS = rng.normal(size=anchors.size).astype(np.float32)
     gv = ext.ats_pair_bwd(T(gS), p.src_y, p.src_v, p.src_t, p.src_id, p.cell_start, p.anc_x, p.anc_t, p.anc_cell,
                           p.anc_id, p.slice_c, p.S, p.GH, p.GW, 1.0, tau, 3.0, n)
-    ogv = O.pair_bwd(ref, gS, 1.0, tau, 3.0, n)
-    np.testing.assert_allclose(np_(gv), ogv, rtol=1e-4, atol=1e-5 * np.abs(ogv).max())
+    gv64, gabs, cnt = O.pair_bwd_f64(ref, gS, 1.0, tau, 3.0, n)
+    assert_grad_parity(np_(gv), gv64, A=gabs, n=cnt[:, None], what="pair gradient vs the double-accumulated oracle")
 
 
 def test_plan_edge_cases():
@@ -222,8 +228,9 @@ def test_velocity_backward_vs_oracle(kind):
          "dense": lambda: Mo.DenseLinearFlow(B, H, W, grid=(H, W), init=th)}[kind]().to(DEV)
     gv = np.random.default_rng(1).normal(size=g["xy"].shape).astype(np.float32)
     (m.velocity(T(g["xy"]), T(g["t"]), T(g["b"])) * T(gv)).sum().backward()
-    ref = O.velocity_backward(kind, g[f"{kind}_theta"], g["xy"], g["b"], H, W, gv)
-    np.testing.assert_allclose(np_(m.theta.grad), ref, rtol=1e-4, atol=1e-4 * np.abs(ref).max())
+    ref = O.velocity_backward(kind, g[f"{kind}_theta"], g["xy"], g["b"], H, W, gv)  # double accumulation
+    e = assert_grad_parity(np_(m.theta.grad), ref, what=f"{kind} velocity backward")
+    assert e["max_over_max"] <= 1e-5, e
 
 
 # ------------------------------------------------------------------------------------------- objective
@@ -254,8 +261,16 @@ def test_anchored_exact_objective_vs_reference(kind, fused):
     loss = -ls.mean()
     loss.backward()
     assert math.isclose(float(loss.detach()), float(g["loss"]), rel_tol=RTOL)
-    ref = g["grad_theta"]
-    np.testing.assert_allclose(np_(m.theta.grad), ref, rtol=1e-3, atol=1e-4 * np.abs(ref).max())
+    gr = np_(m.theta.grad)
+    assert_grad_parity(gr, g["grad_theta"], what=f"{kind} motion gradient vs the reference")
+    # and against the oracle's double-accumulated gradient on the same draws, element by element
+    h = np.float32(g["h"])
+    xs = (g["xy"] + (np_(u) - np.float32(0.5))).astype(np.float32)
+    xa = (xs[np_(anchors)] + h * np_(z)).astype(np.float32)
+    ref = O.anchored_exact(kind, g["theta"], xs, g["t"], g["b"], B, H, W, np_(anchors), xa, h=float(g["h"]),
+                           tau=float(g["tau"]), n_slices=int(g["S"]), visibility=bool(g["visibility"]), exact_grad=True)
+    assert_grad_parity(gr, ref["grad_theta64"], A=ref["grad_theta_abs"], n=ref["grad_theta_terms"],
+                       what=f"{kind} motion gradient vs the double-accumulated oracle")
 
 
 def test_fused_matches_stagewise_unsorted_fallback():
@@ -301,6 +316,7 @@ def test_fused_dense_clusters_vs_oracle(n, box):
     (-ls.mean()).backward()
     xs = (xy + (np_(u) - np.float32(0.5))).astype(np.float32)
     xa = (xs[np_(anchors)] + np_(z)).astype(np.float32)
-    ref = O.anchored_exact("translation", th, xs, t, b, 1, H, W, np_(anchors), xa)
+    ref = O.anchored_exact("translation", th, xs, t, b, 1, H, W, np_(anchors), xa, exact_grad=True)
     np.testing.assert_allclose(np_(ls), ref["ls"], rtol=RTOL, atol=RTOL)
-    np.testing.assert_allclose(np_(m.theta.grad), ref["grad_theta"], rtol=1e-3, atol=1e-4 * np.abs(ref["grad_theta"]).max())
+    assert_grad_parity(np_(m.theta.grad), ref["grad_theta64"], A=ref["grad_theta_abs"], n=ref["grad_theta_terms"],
+                       what="dense-cluster translation gradient")

@@ -1,12 +1,67 @@
-"""PixelTrajectories transport on the device (atlb_traj_transport / _bwd) against the torch restatement of
-atl/motion/trajectories.py:40-90 (the same module with the kernels bypassed): positions and the gradient
+"""PixelTrajectories transport on the device (atlb_traj_transport / _bwd): against the reference's own
+transport outputs (tests/golden/traj_*.npz, written by the reference's atl/motion/trajectories.py), and
+against the torch restatement of the same module with the kernels bypassed.  Positions and the gradient
 w.r.t. the coefficient grid, Bezier and polynomial bases, scalar and per-event target times, border
-clamping of the coefficient samples."""
+clamping of the coefficient samples.  Also the trainer's loss (configuration 5b): AnchoredExact with
+PixelTrajectories(K=1, polynomial) against the reference's outputs."""
+import math
+
 import numpy as np
 import pytest
 import torch
 
+from tests.goldens import load
+from tests.parity import assert_grad_parity
+
 pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("name", ["traj_k10_bezier", "traj_k3_poly_pe", "traj_k1_poly", "traj_k4_bezier_pe"])
+def test_traj_transport_vs_reference(name):
+    """Positions within 1e-5 relative of the reference's (the fixed-point iterates round in another order),
+    the coefficient gradient within 1e-5 norm-wise."""
+    from x_b200.motion import PixelTrajectories
+    g = load(name)
+    dev = "cuda"
+    T = lambda a: torch.as_tensor(np.asarray(a)).to(dev).contiguous()  # noqa: E731
+    K = int(g["K"])
+    c = T(g["coeff"]).requires_grad_(True)
+    m = PixelTrajectories(c, K, basis_kind=str(g["basis"]), tile=4)
+    xy, t, b = T(g["xy"]), T(g["t"]), T(g["b"])
+    assert m._device_transport(xy, t)
+    t_dst = T(g["t_dst"]) if bool(g["per_event"]) else float(g["t_dst"])
+    y = m.transport(xy, t, t_dst, b)
+    (y * T(g["w"])).sum().backward()
+    np.testing.assert_allclose(y.detach().cpu().numpy(), g["y"], rtol=1e-5, atol=1e-5)
+    e = assert_grad_parity(c.grad.cpu().numpy(), g["grad"], what=f"{name} coefficient gradient")
+    assert e["max_over_max"] <= 1e-5, e
+
+
+def test_anchored_exact_pixel_trajectories_k1_vs_reference():
+    """Configuration 5b's loss, the trainer's call (atl/train/trainer.py:167): AnchoredExact over a batch of
+    windows with PixelTrajectories(K=1, "polynomial") motion (linear at the event), against the reference's
+    per-anchor scores, loss and coefficient gradient on identical seeded inputs."""
+    from x_b200.events import EventPacket
+    from x_b200.motion import PixelTrajectories
+    from x_b200.objectives import AnchoredExact
+    g = load("exact_traj_k1")
+    dev = "cuda"
+    T = lambda a: torch.as_tensor(np.asarray(a)).to(dev).contiguous()  # noqa: E731
+    B, H, W = int(g["B"]), int(g["H"]), int(g["W"])
+    c = T(g["coeff"]).requires_grad_(True)
+    m = PixelTrajectories(c, 1, basis_kind="polynomial", tile=4)
+    assert m.linear_at_event
+    n = g["t"].shape[0]
+    ev = EventPacket(T(g["xy"]), T(g["t"]), torch.ones(n, device=dev), T(g["b"]), B, H, W)
+    obj = AnchoredExact(h=float(g["h"]), tau=1.0, n_anchors=None, n_slices=16, seed=int(g["seed"]), visibility=True)
+    ls, anchors = obj.log_scores(ev, m)
+    np.testing.assert_array_equal(anchors.cpu().numpy(), g["anchors"])
+    np.testing.assert_allclose(ls.detach().cpu().numpy(), g["ls"], rtol=1e-5, atol=1e-5)
+    loss = -ls.mean()
+    loss.backward()
+    assert math.isclose(float(loss.detach()), float(g["loss"]), rel_tol=1e-5)
+    e = assert_grad_parity(c.grad.cpu().numpy(), g["grad"], what="PixelTrajectories(K=1) coefficient gradient")
+    assert e["max_over_max"] <= 1e-5, e
 
 
 def _torch_transport(m, xy, t, t_dst, b):
@@ -36,9 +91,10 @@ def test_traj_transport_matches_torch(K, basis, per_event):
     m2 = PixelTrajectories(c2, K, basis_kind=basis, tile=4)
     y2 = _torch_transport(m2, xy, t, t_dst, b)
     (y2 * w).sum().backward()
-    np.testing.assert_allclose(y1.detach().cpu().numpy(), y2.detach().cpu().numpy(), rtol=0, atol=2e-4)
+    np.testing.assert_allclose(y1.detach().cpu().numpy(), y2.detach().cpu().numpy(), rtol=1e-5, atol=1e-5)
     g1, g2 = c1.grad.cpu().numpy(), c2.grad.cpu().numpy()
-    np.testing.assert_allclose(g1, g2, rtol=1e-3, atol=1e-4 * np.abs(g2).max())
+    e = assert_grad_parity(g1, g2, what="coefficient gradient vs the torch transport")
+    assert e["max_over_max"] <= 1e-5, e
 
 
 def test_traj_visible_fraction_matches_torch():
@@ -86,4 +142,5 @@ def test_traj_origin_then_from_origin_equals_transport():
     for a, c in zip(ys1, ys2):
         assert torch.equal(a, c)
     g1, g2 = c1.grad.cpu().numpy(), c2.grad.cpu().numpy()
-    np.testing.assert_allclose(g2, g1, rtol=1e-4, atol=1e-5 * np.abs(g1).max())
+    e = assert_grad_parity(g2, g1, what="coefficient gradient through origins")
+    assert e["max_over_max"] <= 1e-5, e

@@ -96,4 +96,8 @@ def test_anchored_exact_objective_matches_reference(kind):
     np.testing.assert_array_equal(r["vis"], g["vis"])
     np.testing.assert_allclose(r["ls"], g["ls"], rtol=1e-6, atol=1e-6)
     assert math.isclose(r["loss"], float(g["loss"]), rel_tol=1e-6)
-    np.testing.assert_allclose(r["grad_theta"], g["grad_theta"], rtol=1e-4, atol=1e-7 * np.abs(g["grad_theta"]).max())
+    # the reference's fp32 gradient against the oracle's: both are fp32 sums in different orders (the
+    # reference's omp atomics), so norm-wise within the north star's 1e-5
+    d = r["grad_theta"].astype(np.float64) - g["grad_theta"]
+    assert np.linalg.norm(d) <= 1e-5 * np.linalg.norm(g["grad_theta"].astype(np.float64))
+    assert np.abs(d).max() <= 1e-5 * np.abs(g["grad_theta"]).max()

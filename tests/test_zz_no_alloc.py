@@ -84,36 +84,69 @@ def test_no_alloc_matches_workspace_entry_point_on_two_calls():
         np.testing.assert_allclose(o.cpu().numpy(), r.cpu().numpy(), rtol=RTOL, atol=1e-6)
 
 
+LIMIT = 16 << 20  # ATLB_PAIR_NOALLOC_SCRATCH_BYTES
+
+
+def _largest_fitting_m(ncell):
+    """The largest anchor count whose workspace, less its 256 bytes of alignment slack, fits the fixed array
+    (from the library's own sizing query, so that the boundary tested is the one the entry point checks)."""
+    lib = _lib().load_library()
+    lo, hi = 0, LIMIT
+    while lo < hi:  # largest M with bytes(M) - 256 <= LIMIT
+        mid = (lo + hi + 1) // 2
+        if lib.atlb_pair_workspace_bytes(mid, ncell) - 256 <= LIMIT:
+            lo = mid
+        else:
+            hi = mid - 1
+    return lo
+
+
 @pytest.mark.gpu
-def test_no_alloc_rejects_sizes_beyond_its_array():
+def test_no_alloc_at_its_size_limit():
+    """The largest anchor count that fits the array runs and matches the workspace entry point; one anchor
+    more is rejected before any device work, and the array stays usable afterwards."""
     L = _lib()
-    p = _plan(13, 5000, 1, 40, 56, 0.2, 8, 5.0)
-    Ns, M, ncell = _sizes(p)
-    big_m = (16 << 20) // 28 + 1  # 28 bytes of anchor buckets per anchor
-    ax = torch.zeros(big_m, 2, dtype=torch.float32, device="cuda")
-    at = torch.zeros(big_m, dtype=torch.float32, device="cuda")
-    ac = torch.zeros(big_m, 3, dtype=torch.int64, device="cuda")
-    aid = torch.zeros(big_m, dtype=torch.int64, device="cuda")
-    out = torch.empty(big_m, dtype=torch.float32, device="cuda")
+    # 1.5M events, a third of them anchors: more anchors than the array holds for this grid
+    p = _plan(13, 1_500_000, 1, 480, 640, 1.0, 16, 20.0)
+    Ns, M_all, ncell = _sizes(p)
+    m_max = _largest_fitting_m(ncell)
+    assert 0 < m_max < M_all
     a = _args(p)
-    a[5], a[6], a[7], a[8] = L.ptr(ax), L.ptr(at), L.ptr(ac), L.ptr(aid)
-    st = L.lib().atlb_ats_pair_fwd_noalloc(*a, Ns, big_m, ncell, p.S, p.GH, p.GW, 1.0, 0.2, 3.0, L.ptr(out),
+    cut = {k: getattr(p, k)[: m_max + 1].contiguous() for k in ("anc_x", "anc_t", "anc_cell", "anc_id")}
+    a[5], a[6], a[7], a[8] = (L.ptr(cut[k]) for k in ("anc_x", "anc_t", "anc_cell", "anc_id"))
+    out = torch.full((m_max + 1,), float("nan"), dtype=torch.float32, device="cuda")
+    st = L.lib().atlb_ats_pair_fwd_noalloc(*a, Ns, m_max + 1, ncell, p.S, p.GH, p.GW, 1.0, 1.0, 3.0, L.ptr(out),
                                            L.stream())
     assert st == L.ATLB_ERR_WORKSPACE
     assert b"scratch bytes" in L.lib().atlb_last_error()
-    # the array is still usable afterwards
-    r = _with_workspace(p, 0.2)
-    o = _no_alloc(p, 0.2, torch.full_like(r, float("nan")))
+    L.check(L.lib().atlb_ats_pair_fwd_noalloc(*a, Ns, m_max, ncell, p.S, p.GH, p.GW, 1.0, 1.0, 3.0, L.ptr(out),
+                                              L.stream()), "ats_pair_fwd_noalloc at the limit")
+    ref = torch.empty(m_max, dtype=torch.float32, device="cuda")
+    nb = L.lib().atlb_pair_workspace_bytes(m_max, ncell)
+    ws = L.workspace(nb, "cuda")
+    L.check(L.lib().atlb_ats_pair_fwd(*a, Ns, m_max, ncell, p.S, p.GH, p.GW, 1.0, 1.0, 3.0, L.ptr(ref), L.ptr(ws), nb,
+                                      L.stream()), "ats_pair_fwd")
+    torch.cuda.synchronize()
+    assert torch.isfinite(out[:m_max]).all()
+    np.testing.assert_allclose(out[:m_max].cpu().numpy(), ref.cpu().numpy(), rtol=RTOL, atol=1e-6)
+    assert torch.isnan(out[m_max])  # the rejected call wrote nothing
+    # a small call after the rejected one still matches
+    q = _plan(14, 5000, 1, 40, 56, 0.2, 8, 5.0)
+    r = _with_workspace(q, 0.2)
+    o = _no_alloc(q, 0.2, torch.full_like(r, float("nan")))
     np.testing.assert_allclose(o.cpu().numpy(), r.cpu().numpy(), rtol=RTOL, atol=1e-6)
 
 
 def test_no_alloc_rejects_oversize_without_a_device():
-    """The size check comes before any device work, so it answers on a host without a GPU."""
+    """The size check comes before any device work, so it answers on a host without a GPU: one anchor beyond
+    the largest count that fits is rejected, and so are invalid sizes."""
     L = _lib()
     lib = L.load_library()
     fake = ctypes.c_void_p(256)  # never dereferenced: the call fails before any device access
-    big_m = (16 << 20) // 28 + 1
-    st = lib.atlb_ats_pair_fwd_noalloc(*([fake] * 10), 0, big_m, 1, 1, 1, 1, 1.0, 0.2, 3.0, fake, None)
+    ncell = 1
+    big_m = _largest_fitting_m(ncell) + 1
+    assert lib.atlb_pair_workspace_bytes(big_m, ncell) - 256 > LIMIT
+    st = lib.atlb_ats_pair_fwd_noalloc(*([fake] * 10), 0, big_m, ncell, 1, 1, 1, 1.0, 0.2, 3.0, fake, None)
     assert st == L.ATLB_ERR_WORKSPACE
     assert b"scratch bytes" in lib.atlb_last_error()
     st = lib.atlb_ats_pair_fwd_noalloc(*([fake] * 10), -1, 1, 1, 1, 1, 1, 1.0, 0.2, 3.0, fake, None)

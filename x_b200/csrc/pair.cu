@@ -320,14 +320,15 @@ int pair_bwd(const float* gS, const float* SY, const float* SV, const float* ST,
 }
 
 // ---- allocation-free forward ---------------------------------------------------------------------
-// Some callers cannot call cudaMalloc at the point where they need the pair sums: code running while
-// a stream is being captured into a CUDA graph by someone else, hosts that hand the library a fixed
-// device-memory budget (a custom allocator, an embedded runtime, a real-time loop that forbids
-// allocation after start-up), or FFI layers with no device allocator of their own.  For them the
-// forward's anchor buckets live in this file-scope device array instead of a caller workspace.  Every
-// device that loads the library holds these bytes until the process exits.  In host code the array's
-// name is a stand-in for the symbol, not a device address: its address on the current device comes
-// from cudaGetSymbolAddress, looked up once per device on that device's first call.
+// Some callers cannot call cudaMalloc at the point where they need the pair sums: hosts that hand the
+// library a fixed device-memory budget (a custom allocator, an embedded runtime), loops that forbid
+// cudaMalloc after start-up because it can synchronise the device, and FFI layers with no device
+// allocator of their own.  For them the forward's anchor buckets live in this file-scope device array
+// instead of a caller workspace.  Every device that loads the library holds these bytes until the
+// process exits.  In host code the array's name is a stand-in for the symbol, not a device address: its
+// address on the current device comes from cudaGetSymbolAddress, looked up once per device on that
+// device's first call and kept for the process (the primary context's module; cudaDeviceReset or another
+// context on the device would invalidate it).
 constexpr size_t kNoAllocScratchBytes = ATLB_PAIR_NOALLOC_SCRATCH_BYTES;
 static __device__ __align__(256) unsigned char g_pair_scratch[kNoAllocScratchBytes];
 
@@ -372,7 +373,8 @@ int pair_fwd_noalloc(const float* SY, const float* SV, const float* ST, const lo
                      const float* AX, const float* AT, const long long* AC, const long long* AID, const float* SC,
                      long long Ns, long long M, long long ncell, long long S, long long GH, long long GW, double h,
                      double tau, double cut, float* out, cudaStream_t s) {
-  const size_t need = pair_workspace_bytes(M, ncell);
+  // the workspace size less its 256 bytes of alignment slack: the array itself is 256-byte aligned
+  const size_t need = pair_workspace_bytes(M, ncell) - 256;
   if (need > kNoAllocScratchBytes) {
     set_error("atlb_ats_pair_fwd_noalloc: %lld anchors over %lld cells need %zu scratch bytes, above the fixed %zu",
               M, ncell, need, kNoAllocScratchBytes);
