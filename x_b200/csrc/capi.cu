@@ -426,7 +426,8 @@ static int check_exact_sizes(const atlb_exact_cfg* c, int64_t N, int64_t M, cons
               (long long)N);
     return ATLB_ERR_ARG;
   }
-  if (g && (g->S != c->S || g->GW < 1 || g->GH < 1 || (double)c->B * g->S * (double)g->GH * g->GW > 2.0e9)) {
+  // the fused plan indexes its sub-cells (kFine x kFine per plan cell) with 32-bit integers
+  if (g && (g->S != c->S || g->GW < 1 || g->GH < 1 || (double)c->B * g->S * (double)g->GH * g->GW * 9.0 > 2.0e9)) {
     set_error("%s: invalid geometry", fn);
     return ATLB_ERR_OVERFLOW;
   }

@@ -14,12 +14,15 @@
 //   backward  dL/dS from the upstream dL/dls, source-centric pair gradient, velocity-field gradient.
 // Every step keeps the reference's rounding, so scores match it to float accuracy and the plan's
 // cells are the reference's cells.
+#include <algorithm>
+#include <cmath>
 #include <cstddef>
 #include <mutex>
 
 #include "common.cuh"
 #include "motion_math.cuh"
 #include "pair_kernels.cuh"
+#include "pair_fine.cuh"
 #include "pair_tiled.cuh"
 #include "plan_math.cuh"
 #include "scan.cuh"
@@ -239,10 +242,7 @@ __global__ void __launch_bounds__(kThreads) k_fast_count_ordered(PlanConsts P, c
     }
     for (int s = 0; s < P.S; ++s) {
       int key = -1;
-      if (s >= s_lo && s <= s_hi) {
-        float yx, yy;
-        key = (int)source_key(P, e.x, e.y, e.z, e.w, tj, bj, s, &yx, &yy);
-      }
+      if (s >= s_lo && s <= s_hi) key = source_fine_key(P, e.x, e.y, e.z, e.w, tj, bj, s);
       if (live) KEY[(long long)s * N + i] = key;
       const unsigned grp = __match_any_sync(0xffffffffu, key);
       if (key >= 0 && lane == __ffs(grp) - 1) atomicAdd(counts + key, __popc(grp));
@@ -307,11 +307,19 @@ __global__ void __launch_bounds__(kThreads) k_fast_scatter_ordered(PlanConsts P,
   }
 }
 
-__device__ __forceinline__ long long fast_anchor_key(const PlanConsts& P, float4 a, long long ba) {
+// Sub-cell key of an anchor (its plan cell as anchor_cell computes it, then the sub-cell inside), -1 if it has
+// no cell.  *g, *fy, *fx: its plane and sub-cell; *cx, *cy: its plan cell.
+__device__ __forceinline__ long long fast_anchor_key(const PlanConsts& P, float4 a, long long ba, int* g, int* fy,
+                                                     int* fx, int* cx, int* cy) {
   if (__float_as_int(a.w) < 0 || ba < 0 || ba >= P.B) return -1;
-  long long g, cx, cy;
-  anchor_cell(P, a.x, a.y, a.z, ba, &g, &cx, &cy);
-  return (g * P.GH + cy) * P.GW + cx;
+  long long gg, qx, qy;
+  anchor_cell(P, a.x, a.y, a.z, ba, &gg, &qx, &qy);
+  *g = (int)gg;
+  *cx = (int)qx;
+  *cy = (int)qy;
+  *fx = fine_index(a.x, P.ox_f, P.rfine_f, (int)qx);
+  *fy = fine_index(a.y, P.oy_f, P.rfine_f, (int)qy);
+  return (gg * P.GHf + *fy) * P.GWf + *fx;
 }
 
 __global__ void __launch_bounds__(kThreads) k_fast_anchor_count(PlanConsts P, const float4* __restrict__ anc4,
@@ -319,13 +327,15 @@ __global__ void __launch_bounds__(kThreads) k_fast_anchor_count(PlanConsts P, co
                                                                 int* __restrict__ counts) {
   const long long stride = (long long)gridDim.x * blockDim.x;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < M; i += stride) {
-    const long long key = fast_anchor_key(P, anc4[i], anc_b[i]);
+    int g, fy, fx, cx, cy;
+    const long long key = fast_anchor_key(P, anc4[i], anc_b[i], &g, &fy, &fx, &cx, &cy);
     if (key >= 0) atomicAdd(counts + key, 1);
   }
 }
 
-// Anchor records in cell order: XT = (x, y, t, the anchor's own pair value) and BI = original index.  The own
-// pair (leave-one-out) is evaluated here once per anchor, with every lane busy, rather than in the pair kernel.
+// Anchor records in sub-cell order: XT = (x, y, t, the anchor's own pair value) and XK = (original index, plane,
+// sub-cell row, sub-cell column).  The own pair (leave-one-out) is evaluated here once per anchor, with every
+// lane busy, rather than in the pair kernel.
 __global__ void __launch_bounds__(kThreads) k_fast_anchor_scatter(PlanConsts P, PairConsts C,
                                                                   const float4* __restrict__ anc4,
                                                                   const long long* __restrict__ anc_b, long long M,
@@ -333,21 +343,19 @@ __global__ void __launch_bounds__(kThreads) k_fast_anchor_scatter(PlanConsts P, 
                                                                   const float* __restrict__ SC,
                                                                   const int* __restrict__ start,
                                                                   int* __restrict__ cursor, float4* __restrict__ XT,
-                                                                  int* __restrict__ BI) {
+                                                                  int4* __restrict__ XK) {
   const long long stride = (long long)gridDim.x * blockDim.x;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < M; i += stride) {
     const float4 a = anc4[i];
     const long long ba = anc_b[i];
-    if (__float_as_int(a.w) < 0 || ba < 0 || ba >= P.B) continue;  // as fast_anchor_key
-    long long g, cx, cy;
-    anchor_cell(P, a.x, a.y, a.z, ba, &g, &cx, &cy);
-    const long long key = (g * P.GH + cy) * P.GW + cx;
+    int g, fy, fx, cx, cy;
+    const long long key = fast_anchor_key(P, a, ba, &g, &fy, &fx, &cx, &cy);
+    if (key < 0) continue;
     const int p = start[key] + atomicAdd(cursor + key, 1);
     const int s = (int)(g - ba * P.S);
-    const float self = self_term(P, C, ev4, __float_as_int(a.w), a.x, a.y, a.z, sub_rn(a.z, SC[s]), (int)ba, s,
-                                 (int)cx, (int)cy);
+    const float self = self_term(P, C, ev4, __float_as_int(a.w), a.x, a.y, a.z, sub_rn(a.z, SC[s]), (int)ba, s, cx, cy);
     XT[p] = make_float4(a.x, a.y, a.z, self);
-    BI[p] = (int)i;
+    XK[p] = make_int4((int)i, g, fy, fx);
   }
 }
 
@@ -454,11 +462,6 @@ __global__ void __launch_bounds__(kThreads) k_exact_norm(MotionView Mv, NormCons
   }
 }
 
-// Writes S_i of original anchor i (the pair kernels' output).
-struct FusedOut {
-  float* S;
-  __device__ __forceinline__ void operator()(int i, double v) const { S[i] = (float)v; }
-};
 
 // The log score ls_i = log(eps + S_i / den_i) (ats.py:95), one thread per anchor after the pair sums: the
 // division and the logarithm cost a full warp instruction stream per anchor group inside the pair kernel.
@@ -474,7 +477,7 @@ __global__ void __launch_bounds__(kThreads) k_exact_ls(const float* __restrict__
 // The backward's anchor records in bucket order: AB = (x, y, t - c_s, t - c_s) and GT = (dL/dS / h^2, t), with
 // dL/dS = dL/dls / (eps + S / den) / den (the Log then Div backward of ls = log(eps + S / den)) (s = the anchor's slice, as in anchor_cell).
 __global__ void __launch_bounds__(kThreads) k_exact_gs_records(PlanConsts P, const float4* __restrict__ XT,
-                                                               const int* __restrict__ BI, long long M,
+                                                               const int4* __restrict__ XK, long long M,
                                                                const float* __restrict__ grad_ls,
                                                                const float* __restrict__ S,
                                                                const float* __restrict__ den, float eps, float invh2,
@@ -482,7 +485,7 @@ __global__ void __launch_bounds__(kThreads) k_exact_gs_records(PlanConsts P, con
                                                                float4* __restrict__ AB, float2* __restrict__ GT) {
   const long long stride = (long long)gridDim.x * blockDim.x;
   for (long long p = blockIdx.x * (long long)blockDim.x + threadIdx.x; p < M; p += stride) {
-    const int i = BI[p];
+    const int i = XK[p].x;
     const float q = div_rn(S[i], den[i]);
     const float g = div_rn(div_rn(grad_ls[i], add_rn(eps, q)), den[i]);
     const float4 a = XT[p];
@@ -517,9 +520,11 @@ __global__ void __launch_bounds__(kThreads) k_slice_hist(const float* __restrict
       if (hist[i]) atomicAdd(counts + i, hist[i]);
 }
 
-__global__ void k_slice_centres(PlanConsts P, float* sc) {
-  const int s = blockIdx.x * blockDim.x + threadIdx.x;
-  if (s < P.S) sc[s] = slice_centre(P, s);
+// sc[s] = centre of slice s (S values), then scg[g] = centre of the slice of plane g = b S + s (B S values)
+__global__ void k_slice_centres(PlanConsts P, float* sc, float* scg) {
+  const long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+  if (i < P.S) sc[i] = slice_centre(P, (int)i);
+  if (i < P.B * P.S) scg[i] = slice_centre(P, (int)(i % P.S));
 }
 
 // velocity-field gradient at the dequantised positions stored in ev4 (x, y in the first two lanes)
@@ -597,9 +602,10 @@ struct ExactWs {
   int* acounts;
   int* astart;
   float4* XT;
-  int* BI;
+  int4* XK;      // (original index, plane, sub-cell row, sub-cell column) of the bucketed anchors
   int* slice_hist;
   float* SC;
+  float* SCg;    // slice centre of every plane (B S)
   long long* bstart;  // first event of each batch (B + 1)
   int* KEY;      // cell key of each (slice, source event) of the count pass, -1 = no entry
   float4* AB;    // backward anchor records (x, y, t - c_s, t), bucket order
@@ -630,9 +636,10 @@ size_t ws_layout(long long N, long long M, long long ncell, long long S, long lo
   x.acounts = (int*)take((size_t)ncell * 4);
   x.astart = (int*)take((size_t)(ncell + 1) * 4);
   x.XT = (float4*)take((size_t)M * 16);
-  x.BI = (int*)take((size_t)M * 4);
+  x.XK = (int4*)take((size_t)M * 16);
   x.slice_hist = (int*)take((size_t)(B * n_check) * 4);
   x.SC = (float*)take((size_t)S * 4);
+  x.SCg = (float*)take((size_t)(B * S) * 4);
   x.bstart = (long long*)take((size_t)(B + 1) * 8);
   x.KEY = (int*)take((size_t)nent * 4);
   x.AB = (float4*)take((size_t)M * 16);
@@ -648,7 +655,6 @@ size_t ws_layout(long long N, long long M, long long ncell, long long S, long lo
 
 int warp_grid(long long nwarps) { return clamp_grid(blocks_for(nwarps * 32, kThreads)); }
 
-unsigned long long g_fwd_attr = 0;  // devices on which the tiled forward's shared-memory opt-in is set
 
 // A second stream of the calling host thread on the current device, with the events that fork work onto it
 // from the caller's stream and join it back (null if it cannot be created: the caller's stream is used).
@@ -697,8 +703,40 @@ bool tau_covers(const atlb_plan_geom& g, double tau) {
 
 }  // namespace
 
+// Sub-cells of the fused plan: every plan cell split kFine x kFine.
+static long long fine_cells(const atlb_exact_cfg& c, const atlb_plan_geom& g) {
+  return c.B * (long long)g.S * (g.GH * kFine) * (g.GW * kFine);
+}
+
+// Window constants of the pair kernels (pair_fine.cuh).  The margin covers the rounding of the positions, of
+// the sub-cell bounds and of the window arithmetic: 0.01 px plus 16 ulp of the largest coordinate of the grid.
+static FineConsts fine_consts(const atlb_exact_cfg& c, const atlb_plan_geom& g, const PlanConsts& P) {
+  FineConsts F;
+  F.ox = P.ox_f;
+  F.oy = P.oy_f;
+  F.f = (float)(g.cell / kFine);
+  F.rf = P.rfine_f;
+  const double r2 = (double)make_pair_consts(c.h, c.tau, c.cut).r2max;
+  F.rcut = (float)(std::sqrt(r2) * (1.0 + 1e-6));
+  F.vmax = (float)((double)g.vmax * (1.0 + 1e-6));
+  const double maxc = std::max(std::max(std::fabs(g.ox), std::fabs(g.oy)),
+                               std::max(std::fabs(g.ox + g.GW * g.cell), std::fabs(g.oy + g.GH * g.cell)));
+  F.margin = (float)(0.01 + 16.0 * maxc * std::ldexp(1.0, -23));
+  // max |t_a - c_s| over anchors (events): half a slice inside [0, 1], more for times outside it
+  const double delta = 1.0 / (double)g.S;
+  double dtmax = delta / 2;
+  if (g.t_lo == g.t_lo) dtmax = std::max(dtmax, delta / 2 - (double)g.t_lo);
+  if (g.t_hi == g.t_hi) dtmax = std::max(dtmax, (double)g.t_hi - (1.0 - delta / 2));
+  F.rho_max = (float)(((double)F.rcut + (double)F.vmax * dtmax * (1.0 + 1e-6) + F.margin) * (1.0 + 1e-6));
+  F.GWf = (int)(g.GW * kFine);
+  F.GHf = (int)(g.GH * kFine);
+  const bool finite_t = g.t_lo == g.t_lo && g.t_hi == g.t_hi;
+  F.clip = (std::isfinite(F.rho_max) && finite_t) ? 1 : 0;
+  return F;
+}
+
 size_t exact_workspace_bytes(const atlb_exact_cfg& c, long long N, long long M, const atlb_plan_geom& g) {
-  const long long ncell = c.B * (long long)g.S * g.GH * g.GW;
+  const long long ncell = fine_cells(c, g);
   long long j0, j1;
   src_range(c, N, &j0, &j1);
   return ws_layout(j1 - j0, M, ncell, g.S, c.B, c.n_check, c.B * g.GH * g.GW, nullptr, nullptr);
@@ -742,7 +780,7 @@ int exact_prepare(const atlb_exact_cfg& c, const float* xy, const float* u, cons
 int exact_forward(const atlb_exact_cfg& c, const float* t, const long long* b, long long N, long long M,
                   const float* ev4, const float* anc4, const long long* anc_b, const atlb_plan_geom& g, void* ws,
                   float* S_out, float* den_out, float* ls_out, cudaStream_t s) {
-  const long long ncell = c.B * (long long)g.S * g.GH * g.GW;
+  const long long ncell = fine_cells(c, g);
   long long j0, j1;
   src_range(c, N, &j0, &j1);
   const long long ns = j1 - j0;  // source events of this call
@@ -786,7 +824,7 @@ int exact_forward(const atlb_exact_cfg& c, const float* t, const long long* b, l
     launch(k_exact_norm, grid_for(M), kThreads, 0, norm_s, Mv, K, (const float4*)anc4, anc_b, M, t, b, N,
            whole_batch ? (const long long*)w.bstart : nullptr, (const int*)w.slice_hist, den_out);
   // slice centres, entries and anchors
-  launch(k_slice_centres, (unsigned)((g.S + 127) / 128), 128, 0, s, P, w.SC);
+  launch(k_slice_centres, (unsigned)((c.B * g.S + 127) / 128), 128, 0, s, P, w.SC, w.SCg);
   cudaMemsetAsync(w.counts, 0, (size_t)ncell * 4, s);
   cudaMemsetAsync(w.acounts, 0, (size_t)ncell * 4, s);
   if (ns > 0) {  // source events in mid-slice cell order (see k_order_count)
@@ -809,47 +847,29 @@ int exact_forward(const atlb_exact_cfg& c, const float* t, const long long* b, l
   if (M > 0)
     launch(k_fast_anchor_scatter, grid_for(M), kThreads, 0, s, P, make_pair_consts(c.h, c.tau, c.cut),
            (const float4*)anc4, anc_b, M, (const float4*)ev4, (const float*)w.SC, (const int*)w.astart, w.acounts,
-           w.XT, w.BI);
+           w.XT, w.XK);
   if (side) {  // the pair kernels below read den
     cudaEventRecord(side->join, norm_s);
     cudaStreamWaitEvent(s, side->join, 0);
   }
   // pair sums + log scores
   const FastEntries E{w.YV, w.TI};
-  const FastAnchors A{w.XT, w.BI};
   const PairConsts C = make_pair_consts(c.h, c.tau, c.cut);
   const float eps = (float)(c.eps_frac / (double)(c.H * c.W));
   if (M > 0 && ncell > 0) {
-    // the entry times (last member) are only staged when tau does not cover the window
-    const size_t smem_all = sizeof(TileSmemFwd), smem_no_t = offsetof(TileSmemFwd, ti);
-    if (first_use_on_device(g_fwd_attr)) {  // the opt-in above 48 KB is a per-device attribute
-      cudaFuncSetAttribute(k_pair_fwd_tiled<true, false, FastEntries, int, FusedOut>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           (int)smem_no_t);
-      cudaFuncSetAttribute(k_pair_fwd_tiled<false, false, FastEntries, int, FusedOut>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           (int)smem_all);
-    }
-    const dim3 grid((unsigned)((g.GW + kTileX - 1) / kTileX), (unsigned)((g.GH + kTileY - 1) / kTileY),
-                    (unsigned)g.S);
-    const TileGrid T{(int)g.GW, (int)g.GH, (int)g.S, (int)c.B};
-    const FusedOut out{S_out};
-    cudaMemsetAsync(w.scratch, 0, sizeof(int), s);
+    const FineConsts F = fine_consts(c, g, P);
+    const dim3 grid((unsigned)((F.GWf + kFwdTileX - 1) / kFwdTileX), (unsigned)((F.GHf + kFwdTileY - 1) / kFwdTileY),
+                    (unsigned)(c.B * g.S));
     cudaEvent_t e0 = timing_begin(s);
-    const int* as = (const int*)w.astart;
-    const int* cs = (const int*)w.start;
-    const float* sc = (const float*)w.SC;
-    if (tau_covers(g, c.tau))
-      launch(k_pair_fwd_tiled<true, false, FastEntries, int, FusedOut>, grid, kTileThreads, smem_no_t, s, E, A, as, cs,
-             T, sc, C, out, w.scratch);
+    const int n_ent = (int)(ns * (long long)g.S);  // an upper bound of the entries; only read through cstart
+    if (ns == 0)  // no sources, no pairs: every sum is 0 (and so is every own pair value)
+      cudaMemsetAsync(S_out, 0, (size_t)M * sizeof(float), s);
+    else if (tau_covers(g, c.tau))
+      launch(k_pair_fwd_fine<true>, grid, kFwdWarps * 32, 0, s, E, (const float4*)w.XT, (const int4*)w.XK,
+             (const int*)w.astart, (const int*)w.start, F, (const float*)w.SCg, C, n_ent, S_out);
     else
-      launch(k_pair_fwd_tiled<false, false, FastEntries, int, FusedOut>, grid, kTileThreads, smem_all, s, E, A, as, cs,
-             T, sc, C, out, w.scratch);
-    // cells of tiles with more anchors than the tiled kernel stages (dense windows)
-    if (tau_covers(g, c.tau))
-      launch(k_pair_fwd_overflow<true, false, FastEntries, int, FusedOut>, warp_grid(ncell), 256, 0, s, E, A, nullptr,
-             as, cs, T, sc, C, out, (const int*)w.scratch);
-    else
-      launch(k_pair_fwd_overflow<false, false, FastEntries, int, FusedOut>, warp_grid(ncell), 256, 0, s, E, A, nullptr,
-             as, cs, T, sc, C, out, (const int*)w.scratch);
+      launch(k_pair_fwd_fine<false>, grid, kFwdWarps * 32, 0, s, E, (const float4*)w.XT, (const int4*)w.XK,
+             (const int*)w.astart, (const int*)w.start, F, (const float*)w.SCg, C, n_ent, S_out);
     timing_end("k_pair_fwd", s, e0);
     launch(k_exact_ls, grid_for(M), kThreads, 0, s, (const float*)S_out, (const float*)den_out, eps, M, ls_out);
   }
@@ -859,7 +879,7 @@ int exact_forward(const atlb_exact_cfg& c, const float* t, const long long* b, l
 int exact_backward(const atlb_exact_cfg& c, const float* grad_ls, const long long* b, long long N, long long M,
                    const float* ev4, const atlb_plan_geom& g, void* ws, const float* S, const float* den, float* gv,
                    float* gtheta, cudaStream_t s) {
-  const long long ncell = c.B * (long long)g.S * g.GH * g.GW;
+  const long long ncell = fine_cells(c, g);
   long long j0, j1;
   src_range(c, N, &j0, &j1);
   const long long ns = j1 - j0;
@@ -871,19 +891,18 @@ int exact_backward(const atlb_exact_cfg& c, const float* grad_ls, const long lon
   const PairConsts C = make_pair_consts(c.h, c.tau, c.cut);
   if (M > 0 && ncell > 0) {
     const PlanConsts P = make_plan_consts(g, c.tau, c.B);
-    launch(k_exact_gs_records, grid_for(M), kThreads, 0, s, P, (const float4*)w.XT, (const int*)w.BI, M, grad_ls, S,
+    launch(k_exact_gs_records, grid_for(M), kThreads, 0, s, P, (const float4*)w.XT, (const int4*)w.XK, M, grad_ls, S,
            den, eps, C.invh2, (const float*)w.SC, w.AB, w.GT);
-    const int nrows = (int)(c.B * g.S * g.GH);
-    const dim3 grid((unsigned)((g.GW + 7) / 8), (unsigned)min(nrows, 65535));
+    const FineConsts F = fine_consts(c, g, P);
+    const int nrows = (int)(c.B * g.S * g.GH);  // plan cell rows of all planes
+    const dim3 grid((unsigned)((g.GW + kBwdWarps - 1) / kBwdWarps), (unsigned)min(nrows, 65535));
     cudaEvent_t e0 = timing_begin(s);
     if (tau_covers(g, c.tau))
-      launch(k_pair_bwd_cells<true, false, FastEntries, int>, grid, 256, 0, s, E, (const float4*)w.AB,
-             (const float2*)w.GT, nullptr,
-             (const int*)w.astart, (const int*)w.start, (int)g.GW, (int)g.GH, nrows, C, N, gv);
+      launch(k_pair_bwd_fine<true>, grid, kBwdWarps * 32, 0, s, E, (const float4*)w.AB, (const float2*)w.GT,
+             (const int*)w.astart, (const int*)w.start, F, (int)g.GW, nrows, C, N, gv);
     else
-      launch(k_pair_bwd_cells<false, false, FastEntries, int>, grid, 256, 0, s, E, (const float4*)w.AB,
-             (const float2*)w.GT, nullptr,
-             (const int*)w.astart, (const int*)w.start, (int)g.GW, (int)g.GH, nrows, C, N, gv);
+      launch(k_pair_bwd_fine<false>, grid, kBwdWarps * 32, 0, s, E, (const float4*)w.AB, (const float2*)w.GT,
+             (const int*)w.astart, (const int*)w.start, F, (int)g.GW, nrows, C, N, gv);
     timing_end("k_pair_bwd", s, e0);
   }
   const MotionView Mv = motion_of(c);

@@ -1,0 +1,360 @@
+// Pair kernels of the fused path over a fine plan: every cell of the reference's plan grid (size c >=
+// cut h + vmax delta / 2) is split into kFine x kFine sub-cells of size f = c / kFine, and entries and
+// anchors are bucketed by sub-cell, row-major within each (batch, slice) plane.  A sub-cell index is
+// clamped into the point's EXACT reference cell, so the reference's candidate set -- the entries of the
+// 3x3 cells around the anchor's cell -- is a union of sub-cell ranges: the pairs these kernels test are a
+// subset of the reference's candidates, and every pair the reference's test can accept is in that subset.
+//
+// Which candidates are tested: a pair (i, j) can pass |r| <= cut h only if |x_i - y_j| <= cut h +
+// |v_j| |t_i - c_s| <= rho_i = cut h + vmax |t_i - c_s| (+ a margin for rounding).  So
+//   forward : 8 lanes per anchor; they walk, row by row, the sub-cells of its 3x3 cells that meet the
+//             disc of radius rho_i around the anchor (180 entries per anchor at configuration 2 against 397
+//             for the whole 3x3 cells); the sum is a shuffle reduction.  No shared-memory staging or
+//             barriers: the entries of neighbouring anchors stay in L1, because a CTA takes the anchors of
+//             one tile of sub-cells.
+//   backward: source-centric, one warp per plan cell (its kFine sub-cell rows are kFine entry ranges); the
+//             anchors of its 3x3 cells that lie within rho_max of the cell (a rounded rectangle) are copied
+//             into the warp's shared-memory list and the lanes, one entry each (or several lanes per entry
+//             for a short last chunk), walk it with broadcast loads; one red.v2 per entry.
+// Windows are computed with a margin that covers the rounding of positions, of the sub-cell bounds and of
+// the window arithmetic.  When an anchor is not finite (the reference's test accepts NaN residuals), the
+// window is the whole 3x3 cells, as in the reference (FineConsts.clip = 0 for the whole call).
+#pragma once
+#include "common.cuh"
+#include "pair_kernels.cuh"
+#include "pair_math.cuh"
+#include "pair_tiled.cuh"
+#include "plan_math.cuh"
+
+namespace atlb {
+
+constexpr int kFwdTileX = 16;   // forward: a CTA takes the anchors of a 16 x 8 tile of sub-cells
+constexpr int kFwdTileY = 8;
+constexpr int kFwdWarps = 4;
+constexpr int kMaxWinRows = 3 * kFine;  // sub-cell rows of a 3x3 neighbourhood
+
+struct FineConsts {
+  float ox, oy;    // grid origin (fp32)
+  float f, rf;     // sub-cell size and its reciprocal (fp32)
+  float rcut;      // cut * h, rounded up
+  float vmax;      // bound of the sources' |v|, rounded up
+  float margin;    // rounding slack of the windows (px)
+  float rho_max;   // bound of every anchor's radius: rcut + vmax * max|t_a - c_s| + margin
+  int GWf, GHf;    // sub-cells per row / sub-cell rows per (batch, slice) plane
+  int clip;        // 0: every window is the whole 3x3 cells (a non-finite anchor is present)
+};
+
+// ---- forward -------------------------------------------------------------------------------------------
+// Anchor records in bucket order: XT = (x, y, t, own pair value), XK = (original index, plane g, sub-cell
+// row, sub-cell column).  SCg[g] = centre of the slice of plane g.  Each group of kFwdLanes = 8 lanes takes
+// one anchor: its lanes compute the window rows (entry ranges of the sub-cell rows that meet the disc, two
+// rows per lane), then the group walks each row as four 8-wide chunks with predicated loads (rows hold ~28
+// entries at configuration 2) and a loop for longer rows; the 8 partial sums are reduced by shuffles.
+
+// One candidate: the kernel value of entry k if the pair passes the reference's test, else 0.
+template <bool TAU_ALL>
+__device__ __forceinline__ float fwd_candidate(const FastEntries& E, int k, f32x2 axy, f32x2 adt2, float at,
+                                               const PairConsts& C) {
+  const float4 e = E.yv(k);
+  float2 rr;
+  const float d2 = residual2(axy, adt2, pk2(e.x, e.y), pk2(e.z, e.w), &rr);
+  bool ok = !(d2 > C.r2max);
+  if (!TAU_ALL) ok = ok && !(fabsf(sub_rn(at, E.t(k))) > C.tau);
+  const float kv = ex2_approx(-d2 * C.k2);
+  return ok ? kv : 0.f;
+}
+// The same without a branch: k is clamped to a valid entry (kmax = Ns - 1 >= 0) and the value masked by on.
+template <bool TAU_ALL>
+__device__ __forceinline__ float fwd_candidate_masked(const FastEntries& E, int k, bool on, int kmax, f32x2 axy,
+                                                      f32x2 adt2, float at, const PairConsts& C) {
+  const int kk = min(k, kmax);
+  const float4 e = E.yv(kk);
+  float2 rr;
+  const float d2 = residual2(axy, adt2, pk2(e.x, e.y), pk2(e.z, e.w), &rr);
+  bool ok = on && !(d2 > C.r2max);
+  if (!TAU_ALL) ok = ok && !(fabsf(sub_rn(at, E.t(kk))) > C.tau);
+  const float kv = ex2_approx(-d2 * C.k2);
+  return ok ? kv : 0.f;
+}
+
+constexpr int kFwdLanes = 8;  // lanes per anchor (measured against 16 and 32 at configuration 2: fastest)
+constexpr int kFwdPerWarp = 32 / kFwdLanes;
+
+// Grid: (sub-cell tiles along x, tiles along y, planes g = b * S + s).  Ns >= 1 (the caller skips empty plans).
+template <bool TAU_ALL>
+__global__ void __launch_bounds__(kFwdWarps * 32, 12) k_pair_fwd_fine(FastEntries E, const float4* __restrict__ XT,
+                                                                  const int4* __restrict__ XK,
+                                                                  const int* __restrict__ astart,
+                                                                  const int* __restrict__ cstart, FineConsts F,
+                                                                  const float* __restrict__ SCg, PairConsts C,
+                                                                  int Ns, float* __restrict__ S_out) {
+  __shared__ int seg_lo[kFwdTileY], seg_pre[kFwdTileY + 1];
+  const int g = (int)blockIdx.z;
+  const int fx0 = (int)blockIdx.x * kFwdTileX, fy0 = (int)blockIdx.y * kFwdTileY;
+  const int nx = min(kFwdTileX, F.GWf - fx0), ny = min(kFwdTileY, F.GHf - fy0);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int grp = lane / kFwdLanes, lg = lane % kFwdLanes;
+  const int kmax = Ns - 1;
+  if (warp == 0) {  // the tile's anchors: one contiguous bucket range per sub-cell row
+    int lo = 0, len = 0;
+    if (lane < ny) {
+      const int base = (g * F.GHf + fy0 + lane) * F.GWf + fx0;
+      lo = __ldg(astart + base);
+      len = __ldg(astart + base + nx) - lo;
+    }
+    int incl = len;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int u = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += u;
+    }
+    if (lane < kFwdTileY) {
+      seg_lo[lane] = lo;
+      seg_pre[lane + 1] = incl;
+    }
+    if (lane == 0) seg_pre[0] = 0;
+  }
+  __syncthreads();
+  const int na = seg_pre[ny];
+  const float cs = __ldg(SCg + g);
+  const int plane_row = g * F.GHf;
+  for (int q0 = kFwdPerWarp * warp; q0 < na; q0 += kFwdPerWarp * kFwdWarps) {  // warp-uniform
+    const int q = q0 + grp;
+    const bool live = q < na;
+    float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+    int4 kq = make_int4(0, 0, 0, 0);
+    if (live) {
+      int r = 0;
+      while (q >= seg_pre[r + 1]) ++r;
+      const int p = seg_lo[r] + (q - seg_pre[r]);
+      a = __ldg(XT + p);
+      kq = __ldg(XK + p);
+    }
+    const float dta = sub_rn(a.z, cs);
+    const int fy = kq.z, fx = kq.w;
+    const int cy = fy / kFine, cx = fx / kFine;
+    int ry0 = max((cy - 1) * kFine, 0), ry1 = min((cy + 2) * kFine - 1, F.GHf - 1);
+    const int c0n = max((cx - 1) * kFine, 0), c1n = min((cx + 2) * kFine - 1, F.GWf - 1);
+    const bool geo = F.clip && fabsf(a.x) < 1e30f && fabsf(a.y) < 1e30f && fabsf(dta) < 1e30f;
+    const float rho = F.rcut + F.vmax * fabsf(dta) + F.margin;
+    if (geo) {
+      ry0 = max(ry0, fy + (int)floorf(((a.y - rho) - F.oy) * F.rf - (float)fy));
+      ry1 = min(ry1, fy + (int)floorf(((a.y + rho) - F.oy) * F.rf - (float)fy));
+    }
+    const int nrows = live ? ry1 - ry0 + 1 : 0;  // <= kMaxWinRows
+    // the entry range of window row ry0 + j, j = lg and (8-lane groups) lg + 8
+    int lo[2] = {0, 0}, hi[2] = {0, 0};
+#pragma unroll
+    for (int u = 0; u < (kFwdLanes < kMaxWinRows ? 2 : 1); ++u) {
+      const int j = lg + u * kFwdLanes;
+      if (j < nrows) {
+        const int r = ry0 + j;
+        int c0 = c0n, c1 = c1n;
+        if (geo) {
+          const float blo = F.oy + (float)r * F.f, bhi = blo + F.f;
+          const float dy = fmaxf(fmaxf(blo - a.y, a.y - bhi), 0.f);
+          const float w = __fsqrt_rn(fmaxf(rho * rho - dy * dy, 0.f));
+          c0 = max(c0, fx + (int)floorf(((a.x - w) - F.ox) * F.rf - (float)fx));
+          c1 = min(c1, fx + (int)floorf(((a.x + w) - F.ox) * F.rf - (float)fx));
+          if (rho * rho < dy * dy) c1 = c0 - 1;
+        }
+        if (c0 <= c1) {
+          const int base = (plane_row + r) * F.GWf;
+          lo[u] = __ldg(cstart + base + c0);
+          hi[u] = __ldg(cstart + base + c1 + 1);
+        }
+      }
+    }
+    int rmax = nrows;
+#pragma unroll
+    for (int o = kFwdLanes; o < 32; o <<= 1) rmax = max(rmax, __shfl_xor_sync(0xffffffffu, rmax, o));
+    const f32x2 axy = pk2(a.x, a.y), adt2 = pk2(dta, dta);
+    float acc = 0.f;
+    for (int r = 0; r < rmax; ++r) {  // warp-uniform
+      const int src = grp * kFwdLanes + (r % kFwdLanes);
+      int l = __shfl_sync(0xffffffffu, lo[0], src), h = __shfl_sync(0xffffffffu, hi[0], src);
+      if (kFwdLanes < kMaxWinRows) {
+        const int l2 = __shfl_sync(0xffffffffu, lo[1], src), h2 = __shfl_sync(0xffffffffu, hi[1], src);
+        if (r >= kFwdLanes) { l = l2; h = h2; }
+      }
+      constexpr int kChunks = 32 / kFwdLanes;  // predicated chunks of kFwdLanes entries, then a loop for longer rows
+      int k = l + lg;
+#pragma unroll
+      for (int c = 0; c < kChunks; ++c, k += kFwdLanes)
+        acc += fwd_candidate_masked<TAU_ALL>(E, k, k < h, kmax, axy, adt2, a.z, C);
+      for (; k < h; k += kFwdLanes) acc += fwd_candidate<TAU_ALL>(E, k, axy, adt2, a.z, C);
+    }
+#pragma unroll
+    for (int o = kFwdLanes / 2; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (live && lg == 0) S_out[kq.x] = acc - a.w;  // leave-one-out: the own pair value, when it was counted
+  }
+}
+
+// ---- backward ------------------------------------------------------------------------------------------
+// One warp per plan cell (kFine x kFine sub-cells: kFine entry ranges, one per sub-cell row).  The cell's
+// anchor list is the anchors of its 3x3 cells that lie within rho_max of the cell (a rounded rectangle),
+// copied into the warp's shared memory and padded to a multiple of 4 with far-away records that no test
+// accepts, so the lanes -- one entry each, or several per entry for a short last chunk -- walk it 4 at a time
+// without bounds checks.  Grid: x = groups of kBwdWarps cells of a cell row, y = cell rows of all planes
+// (grid-stride).  AB = (x, y, t - c_s, t - c_s), GT = (dL/dS / h^2, t) in anchor bucket order.
+constexpr int kBwdList = 128;  // anchor records a warp holds at a time
+
+// Gradient of one entry over the anchors i = g, g + G, ... of the padded list (na a multiple of 4 when G = 1).
+template <bool TAU_ALL, bool STRIDED>
+__device__ __forceinline__ float2 bwd_entry_fine(const float4* ab, const float2* gt, int na, f32x2 y, f32x2 v,
+                                                 float st, int g, int G, float r2max, float k2, float tau) {
+  float gx = 0.f, gy = 0.f;
+  auto one = [&](int i) {
+    const float4 a = ab[i];  // (x, y, t - c_s, t - c_s)
+    const float2 q = gt[i];  // (dL/dS / h^2, t)
+    float2 rr;
+    const float d2 = residual2(pk2(a.x, a.y), pk2(a.z, a.w), y, v, &rr);
+    const float dt = sub_rn(q.y, st);
+    bool ok = !(d2 > r2max);
+    if (!TAU_ALL) ok = ok && !(fabsf(dt) > tau);
+    const float f = ok ? q.x * ex2_approx(-d2 * k2) * dt : 0.f;  // gS k dt / h^2
+    gx = fmaf(f, rr.x, gx);
+    gy = fmaf(f, rr.y, gy);
+  };
+  if (STRIDED) {
+    for (int i = g; i < na; i += G) one(i);
+  } else {
+    for (int i = 0; i < na; i += 4) {
+      one(i);
+      one(i + 1);
+      one(i + 2);
+      one(i + 3);
+    }
+  }
+  return make_float2(gx, gy);
+}
+
+template <bool TAU_ALL>
+__global__ void __launch_bounds__(kBwdWarps * 32, 6) k_pair_bwd_fine(FastEntries E, const float4* __restrict__ AB,
+                                                                     const float2* __restrict__ GT,
+                                                                     const int* __restrict__ astart,
+                                                                     const int* __restrict__ cstart, FineConsts F,
+                                                                     int GW, int nrows, PairConsts C, long long N,
+                                                                     float* __restrict__ gv) {
+  __shared__ float4 s_ab[kBwdWarps][kBwdList];
+  __shared__ float2 s_gt[kBwdWarps][kBwdList];
+  __shared__ int s_row[kBwdWarps][2][kMaxWinRows];  // per window row: first flat index, first bucket position
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int cx = blockIdx.x * kBwdWarps + w;
+  if (cx >= GW) return;  // warp-uniform; no CTA-wide barrier follows
+  float4* ab = s_ab[w];
+  float2* gt = s_gt[w];
+  int* rex = s_row[w][0];
+  int* rlo = s_row[w][1];
+  const float r2max = C.r2max, k2 = C.k2, tau = C.tau;
+  const int GHc = F.GHf / kFine;
+  const int fxs = cx * kFine;
+  for (int crow = blockIdx.y; crow < nrows; crow += gridDim.y) {  // crow = g * GH + cy
+    const int cy = crow % GHc;
+    const int prow = (crow - cy) * kFine;  // the plane's first sub-cell row
+    const int fys = cy * kFine;             // the cell's first sub-cell row
+    // the cell's entries: kFine ranges (its sub-cell rows), flattened
+    int elo = 0, elen = 0;
+    if (lane < kFine) {
+      const int base = (prow + fys + lane) * F.GWf + fxs;
+      elo = __ldg(cstart + base);
+      elen = __ldg(cstart + base + kFine) - elo;
+    }
+    const int e1 = __shfl_sync(0xffffffffu, elen, 0), e2 = e1 + __shfl_sync(0xffffffffu, elen, 1);
+    const int en = e2 + __shfl_sync(0xffffffffu, elen, 2);
+    if (en == 0) continue;
+    const int el0 = __shfl_sync(0xffffffffu, elo, 0), el1 = __shfl_sync(0xffffffffu, elo, 1),
+              el2 = __shfl_sync(0xffffffffu, elo, 2);
+    // anchor rows of the 3x3 cells within rho_max of the cell's band
+    const int ry0 = max(fys - kFine, 0), ry1 = min(fys + 2 * kFine - 1, F.GHf - 1);
+    const int c0n = max(fxs - kFine, 0), c1n = min(fxs + 2 * kFine - 1, F.GWf - 1);
+    const int nr = ry1 - ry0 + 1;  // <= kMaxWinRows
+    int lo = 0, len = 0;
+    if (lane < nr) {
+      const int r = ry0 + lane;
+      int c0 = c0n, c1 = c1n;
+      if (F.clip) {
+        const int gap_cells = max(max(fys - r - 1, r - (fys + kFine - 1) - 1), 0);
+        const float dy = (float)gap_cells * F.f - F.margin;  // band-to-band distance, rounded down
+        const float w2 = F.rho_max * F.rho_max - (dy > 0.f ? dy * dy : 0.f);
+        if (w2 < 0.f) {
+          c1 = c0 - 1;
+        } else {
+          const int ew = (int)floorf(__fsqrt_rn(w2) * F.rf) + 1;
+          c0 = max(c0, fxs - ew);
+          c1 = min(c1, fxs + kFine - 1 + ew);
+        }
+      }
+      if (c0 <= c1) {
+        const int base = (prow + r) * F.GWf;
+        lo = __ldg(astart + base + c0);
+        len = __ldg(astart + base + c1 + 1) - lo;
+      }
+    }
+    int incl = len;  // flat index over the rows
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int u = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += u;
+    }
+    const int A = __shfl_sync(0xffffffffu, incl, 31);
+    __syncwarp();  // the previous cell's tables and records are no longer read
+    if (lane < kMaxWinRows) {
+      rex[lane] = lane < nr ? incl - len : A;  // rows past nr: A, never selected
+      rlo[lane] = lo;
+    }
+    __syncwarp();
+    for (int a0 = 0; a0 < A; a0 += kBwdList) {
+      const int na = min(kBwdList, A - a0);
+      const int na4 = (na + 3) & ~3;
+      if (a0 > 0) __syncwarp();  // the previous batch of records is no longer read
+      for (int i = lane; i < na4; i += 32) {
+        if (i < na) {
+          const int f = a0 + i;
+          int rsel = 0;  // the row holding flat index f: the last row whose first flat index is <= f
+#pragma unroll
+          for (int q = 1; q < kMaxWinRows; ++q) rsel += f >= rex[q] ? 1 : 0;
+          const int p = rlo[rsel] + (f - rex[rsel]);
+          ab[i] = __ldg(AB + p);
+          gt[i] = __ldg(GT + p);
+        } else {  // padding: a residual of ~1e30 fails the test, and 0 * 1e30 adds nothing
+          ab[i] = make_float4(1e30f, 1e30f, 0.f, 0.f);
+          gt[i] = make_float2(0.f, 0.f);
+        }
+      }
+      __syncwarp();
+      for (int kb = 0; kb < en; kb += 32) {
+        const int m = min(32, en - kb);
+        const bool big = m > 16;  // warp-uniform: one entry per lane; else G lanes per entry
+        const int G = big ? 1 : (int)__fdividef(32.5f, (float)m);
+        const int e = big ? lane : (int)__fdividef((float)lane + 0.5f, (float)G);
+        const int gsub = lane - e * G;
+        const bool valid = e < m;
+        const int fe = kb + (valid ? e : 0);  // flat entry index -> its sub-cell row's range
+        const int k = fe < e1 ? el0 + fe : (fe < e2 ? el1 + (fe - e1) : el2 + (fe - e2));
+        float2 sy, sv;
+        float st;
+        int sid;
+        E.load(k, sy, sv, st, sid);
+        float2 gr;
+        if (big) {
+          gr = bwd_entry_fine<TAU_ALL, false>(ab, gt, na4, pk2(sy.x, sy.y), pk2(sv.x, sv.y), st, 0, 1, r2max, k2, tau);
+        } else {
+          gr = bwd_entry_fine<TAU_ALL, true>(ab, gt, valid ? na : 0, pk2(sy.x, sy.y), pk2(sv.x, sv.y), st, gsub, G,
+                                             r2max, k2, tau);
+          for (int d = 1; d < G; d <<= 1) {
+            const float ox = __shfl_down_sync(0xffffffffu, gr.x, d), oy = __shfl_down_sync(0xffffffffu, gr.y, d);
+            if ((gsub & (2 * d - 1)) == 0 && gsub + d < G) {
+              gr.x += ox;
+              gr.y += oy;
+            }
+          }
+        }
+        if (valid && gsub == 0 && (gr.x != 0.f || gr.y != 0.f) && sid >= 0 && (long long)sid < N)
+          red_add_f2(gv + 2 * (long long)sid, gr.x, gr.y);
+      }
+    }
+  }
+}
+
+}  // namespace atlb

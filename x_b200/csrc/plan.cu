@@ -207,6 +207,9 @@ PlanConsts make_plan_consts(const atlb_plan_geom& g, double tau, long long B) {
   P.B = B;
   P.src0 = 0;
   P.src1 = LLONG_MAX;
+  P.rfine_f = (float)((double)kFine / g.cell);
+  P.GWf = g.GW * kFine;
+  P.GHf = g.GH * kFine;
   return P;
 }
 

@@ -14,7 +14,21 @@ struct PlanConsts {
   int S;
   long long B;
   long long src0, src1;  // events that are sources of the pair sums (fused path), [src0, src1)
+  float rfine_f;         // fused path: kFine / cell, the reciprocal of the sub-cell size
+  long long GWf, GHf;    // fused path: sub-cells per row / sub-cell rows of a plane (GW, GH times kFine)
 };
+
+// The fused path splits every plan cell into kFine x kFine sub-cells (pair_fine.cuh).
+constexpr int kFine = 3;
+
+// Sub-cell index along one axis of a point at coordinate p (grid origin o, rf = kFine / cell) whose plan cell
+// index is q (exact): floor((p - o) rf) clamped into [q kFine, q kFine + kFine - 1].  Only the pair windows
+// depend on it, and they carry a margin for its rounding; the clamp keeps the plan cells exact.
+__device__ __forceinline__ int fine_index(float p, float o, float rf, int q) {
+  const float u = (p - o) * rf;
+  const int lo = q * kFine;
+  return u == u ? (int)fmaxf(fminf(floorf(u), (float)(lo + kFine - 1)), (float)lo) : lo;
+}
 
 // torch's row norm of an (N,2) float32 tensor (vectorised last-dim reduction): sqrt(fma(y, y, x*x)).
 __device__ __forceinline__ float row_norm(float x, float y) {
@@ -71,6 +85,20 @@ __device__ __forceinline__ long long source_key(const PlanConsts& P, float xj, f
   if (bj < 0 || bj >= P.B) return -1;  // batch index outside [0, B): no cell (the reference's key would overflow)
   const long long cx = (long long)qx, cy = (long long)qy;
   return ((bj * P.S + s) * P.GH + cy) * P.GW + cx;
+}
+
+// The sub-cell key of the fused path, ((b S + s) GHf + fy) GWf + fx, of a source at slice s (-1 = dropped,
+// exactly when source_key drops it): the plan cell as source_key computes it, then the sub-cell inside it.
+__device__ __forceinline__ int source_fine_key(const PlanConsts& P, float xj, float yj, float vx, float vy, float tj,
+                                               long long bj, int s) {
+  float yx, yy;
+  transported(P, xj, yj, vx, vy, tj, s, &yx, &yy);
+  const float qx = floor_div(sub_rn(yx, P.ox_f), P.cell_f, P.rcell_f);
+  const float qy = floor_div(sub_rn(yy, P.oy_f), P.cell_f, P.rcell_f);
+  if (!(qx >= 0.f && qx < (float)P.GW && qy >= 0.f && qy < (float)P.GH)) return -1;
+  if (bj < 0 || bj >= P.B) return -1;
+  const int fx = fine_index(yx, P.ox_f, P.rfine_f, (int)qx), fy = fine_index(yy, P.oy_f, P.rfine_f, (int)qy);
+  return (int)((((long long)bj * P.S + s) * P.GHf + fy) * P.GWf + fx);
 }
 
 // functional.py:170-175: anchor grid g = b*S + clamp(floor(t/delta), 0, S-1) and clamped cell.
