@@ -172,20 +172,20 @@ __global__ void __launch_bounds__(kThreads) k_exact_anchors(const float4* __rest
 
 // ---- compact plan -------------------------------------------------------------------------------------
 // ---- spatial order of the events for the plan passes ------------------------------------------------
-// The count and scatter passes walk the events in the order of their cell at the middle slice, i.e. of
+// The count and scatter passes walk the events in the order of their sub-cell at the middle slice, i.e. of
 // where each event sits at mid-window under its own motion.  Under a smooth motion field, events that
-// share that cell stay within a few cells of one another at every slice, so the 32 lanes of a warp fall
-// into a handful of cells: one cursor atomic per distinct cell (warp-aggregated with match.any), and the
-// lanes of one cell write consecutive slots.  The order only decides where inside a cell an entry lands;
-// the cell keys themselves come from source_key, unchanged.
+// share that sub-cell stay within a few sub-cells of one another at every slice, so the 32 lanes of a warp
+// fall into a handful of sub-cells: one cursor atomic per distinct sub-cell (warp-aggregated with
+// match.any), and the lanes of one sub-cell write consecutive slots.  The order only decides where inside a
+// sub-cell an entry lands; the keys themselves come from source_fine_key, unchanged.
 __device__ __forceinline__ int order_key(const PlanConsts& P, float4 e, float t, int b) {
   const float dtc = slice_centre(P, P.S / 2) - t;
-  const float qx = floorf((e.x + e.z * dtc - P.ox_f) / P.cell_f);
-  const float qy = floorf((e.y + e.w * dtc - P.oy_f) / P.cell_f);
-  const int cx = (int)fminf(fmaxf(qx, 0.f), (float)(P.GW - 1));  // NaN -> 0
-  const int cy = (int)fminf(fmaxf(qy, 0.f), (float)(P.GH - 1));
+  const float qx = floorf((e.x + e.z * dtc - P.ox_f) * P.rfine_f);
+  const float qy = floorf((e.y + e.w * dtc - P.oy_f) * P.rfine_f);
+  const int cx = (int)fminf(fmaxf(qx, 0.f), (float)(P.GWf - 1));  // NaN -> 0
+  const int cy = (int)fminf(fmaxf(qy, 0.f), (float)(P.GHf - 1));
   const int bb = (b >= 0 && b < P.B) ? b : 0;
-  return (bb * (int)P.GH + cy) * (int)P.GW + cx;
+  return (bb * (int)P.GHf + cy) * (int)P.GWf + cx;
 }
 
 __global__ void __launch_bounds__(kThreads) k_order_count(PlanConsts P, const float4* __restrict__ ev4,
@@ -739,7 +739,7 @@ size_t exact_workspace_bytes(const atlb_exact_cfg& c, long long N, long long M, 
   const long long ncell = fine_cells(c, g);
   long long j0, j1;
   src_range(c, N, &j0, &j1);
-  return ws_layout(j1 - j0, M, ncell, g.S, c.B, c.n_check, c.B * g.GH * g.GW, nullptr, nullptr);
+  return ws_layout(j1 - j0, M, ncell, g.S, c.B, c.n_check, c.B * g.GH * g.GW * kFine * kFine, nullptr, nullptr);
 }
 
 static MotionView motion_of(const atlb_exact_cfg& c) {
@@ -785,7 +785,7 @@ int exact_forward(const atlb_exact_cfg& c, const float* t, const long long* b, l
   src_range(c, N, &j0, &j1);
   const long long ns = j1 - j0;  // source events of this call
   ExactWs w;
-  ws_layout(ns, M, ncell, g.S, c.B, c.n_check, c.B * g.GH * g.GW, &w, ws);
+  ws_layout(ns, M, ncell, g.S, c.B, c.n_check, c.B * g.GH * g.GW * kFine * kFine, &w, ws);
   PlanConsts P = make_plan_consts(g, c.tau, c.B);
   P.src0 = j0;
   P.src1 = j1;
@@ -828,7 +828,7 @@ int exact_forward(const atlb_exact_cfg& c, const float* t, const long long* b, l
   cudaMemsetAsync(w.counts, 0, (size_t)ncell * 4, s);
   cudaMemsetAsync(w.acounts, 0, (size_t)ncell * 4, s);
   if (ns > 0) {  // source events in mid-slice cell order (see k_order_count)
-    const long long nkey = c.B * g.GH * g.GW;
+    const long long nkey = c.B * g.GH * g.GW * kFine * kFine;  // mid-slice sub-cells
     const float4* ev = (const float4*)ev4 + j0;
     cudaMemsetAsync(w.ocount, 0, (size_t)nkey * 4, s);
     launch(k_order_count, grid_for(ns), kThreads, 0, s, P, ev, t + j0, b + j0, ns, w.ocount);
@@ -884,7 +884,7 @@ int exact_backward(const atlb_exact_cfg& c, const float* grad_ls, const long lon
   src_range(c, N, &j0, &j1);
   const long long ns = j1 - j0;
   ExactWs w;
-  ws_layout(ns, M, ncell, g.S, c.B, c.n_check, c.B * g.GH * g.GW, &w, ws);
+  ws_layout(ns, M, ncell, g.S, c.B, c.n_check, c.B * g.GH * g.GW * kFine * kFine, &w, ws);
   const float eps = (float)(c.eps_frac / (double)(c.H * c.W));
   cudaMemsetAsync(gv, 0, (size_t)N * 2 * sizeof(float), s);
   const FastEntries E{w.YV, w.TI};

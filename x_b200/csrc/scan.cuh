@@ -44,16 +44,26 @@ __device__ __forceinline__ long long block_exclusive_scan(long long v, long long
   return out;
 }
 
+// The kScanItems counts of thread t of chunk c are counts[c * kScanChunk + t * kScanItems + q]: one 16-byte
+// load when the chunk's counts are 16-byte aligned (every chunk of a 16-byte aligned array).
+__device__ __forceinline__ void load_items(const int* __restrict__ counts, long long n, long long base, int (&v)[kScanItems]) {
+  static_assert(kScanItems == 4, "vector load of 4 ints");
+  if (base + kScanItems <= n && ((reinterpret_cast<uintptr_t>(counts) & 15) == 0)) {
+    const int4 q = __ldg(reinterpret_cast<const int4*>(counts + base));
+    v[0] = q.x; v[1] = q.y; v[2] = q.z; v[3] = q.w;
+  } else {
+#pragma unroll
+    for (int q = 0; q < kScanItems; ++q) v[q] = base + q < n ? counts[base + q] : 0;
+  }
+}
+
 __global__ void __launch_bounds__(kScanThreads) k_scan_partials(const int* __restrict__ counts, long long n,
                                                                 long long* __restrict__ partials) {
   __shared__ long long sw[33];
-  const long long base = blockIdx.x * kScanChunk;
-  long long s = 0;
-#pragma unroll
-  for (int q = 0; q < kScanItems; ++q) {
-    const long long i = base + (long long)q * kScanThreads + threadIdx.x;
-    if (i < n) s += counts[i];
-  }
+  const long long base = blockIdx.x * kScanChunk + (long long)threadIdx.x * kScanItems;
+  int v[kScanItems];
+  load_items(counts, n, base, v);
+  const long long s = (long long)v[0] + v[1] + v[2] + v[3];
   long long tot;
   block_exclusive_scan(s, sw, &tot);
   if (threadIdx.x == 0) partials[blockIdx.x] = tot;
@@ -80,23 +90,25 @@ __global__ void __launch_bounds__(kScanThreads) k_scan_final(int* __restrict__ c
                                                              OutT* __restrict__ offsets) {
   __shared__ long long sw[33];
   const long long base = blockIdx.x * kScanChunk + (long long)threadIdx.x * kScanItems;
-  long long v[kScanItems];
-  long long s = 0;
-#pragma unroll
-  for (int q = 0; q < kScanItems; ++q) {
-    const long long i = base + q;
-    v[q] = i < n ? counts[i] : 0;
-    s += v[q];
-  }
+  int v[kScanItems];
+  load_items(counts, n, base, v);
+  const long long s = (long long)v[0] + v[1] + v[2] + v[3];
   long long ex = block_exclusive_scan(s, sw, nullptr) + partials[blockIdx.x];
+  if (sizeof(OutT) == 4 && base + kScanItems <= n && ((reinterpret_cast<uintptr_t>(offsets) & 15) == 0) &&
+      ((reinterpret_cast<uintptr_t>(counts) & 15) == 0)) {
+    const int o0 = (int)ex, o1 = o0 + v[0], o2 = o1 + v[1], o3 = o2 + v[2];
+    *reinterpret_cast<int4*>(offsets + base) = make_int4(o0, o1, o2, o3);
+    *reinterpret_cast<int4*>(counts + base) = make_int4(0, 0, 0, 0);
+  } else {
 #pragma unroll
-  for (int q = 0; q < kScanItems; ++q) {
-    const long long i = base + q;
-    if (i < n) {
-      offsets[i] = (OutT)ex;
-      counts[i] = 0;
+    for (int q = 0; q < kScanItems; ++q) {
+      const long long i = base + q;
+      if (i < n) {
+        offsets[i] = (OutT)ex;
+        counts[i] = 0;
+      }
+      ex += v[q];
     }
-    ex += v[q];
   }
   if (blockIdx.x == 0 && threadIdx.x == 0) offsets[n] = (OutT)partials[gridDim.x];
 }
