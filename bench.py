@@ -449,52 +449,81 @@ def ours_arm(args):
     # the timed region is the whole job, from the first copy to the last loss read.
     # The anchors are all events (n_anchors=None): the objective builds that index on the device
     # (objectives._pick_anchors), so it is made there each step rather than copied.
-    pin = {k: v.pin_memory() for k, v in (("xy", ev_cpu.xy), ("t", ev_cpu.t), ("b", ev_cpu.b),
-                                          ("u", u.cpu()), ("z", z.cpu()))}
-    h2d = sum(v.numel() * v.element_size() for v in pin.values())
-    bufs = [{k: torch.empty(v.shape, dtype=v.dtype, device=dev) for k, v in pin.items()} for _ in range(2)]
-    cstream = torch.cuda.Stream(device=dev)
-    copied = [torch.cuda.Event() for _ in range(2)]
-    freed = [torch.cuda.Event() for _ in range(2)]
+    # Two pipelines: (a) the reference's noise, drawn on the host with the objective's CPU generator and
+    # copied with the events (the draws themselves are timed separately: host_rng_ms); (b) device_rng, the
+    # opt-in device draws inside the fused pipeline, so only the events are copied.
+    obj_dev = AnchoredExact(h=1.0, tau=1.0, n_anchors=None, n_slices=16, seed=7 + rank, visibility=True,
+                            fused=not args.dropin, device_rng=True)
 
-    def issue_copy(slot):
-        with torch.cuda.stream(cstream):
-            cstream.wait_event(freed[slot])  # the step that last read this buffer is done
-            for k, v in pin.items():
-                bufs[slot][k].copy_(v, non_blocking=True)
-            copied[slot].record(cstream)
+    def e2e_pipeline(with_noise: bool):
+        keys = (("xy", ev_cpu.xy), ("t", ev_cpu.t), ("b", ev_cpu.b)) + ((("u", u.cpu()), ("z", z.cpu()))
+                                                                       if with_noise else ())
+        pin = {k: v.pin_memory() for k, v in keys}
+        h2d = sum(v.numel() * v.element_size() for v in pin.values())
+        bufs = [{k: torch.empty(v.shape, dtype=v.dtype, device=dev) for k, v in pin.items()} for _ in range(2)]
+        cstream = torch.cuda.Stream(device=dev)
+        copied = [torch.cuda.Event() for _ in range(2)]
+        freed = [torch.cuda.Event() for _ in range(2)]
 
-    def run_e2e(nsteps):
-        """nsteps end-to-end steps; returns their device time in ms (events around the whole job)."""
-        for e in freed:
-            e.record()
-        barrier()
-        torch.cuda.synchronize()
-        e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e_start.record()
-        cstream.wait_event(e_start)
-        issue_copy(0)
-        for i in range(nsteps):
-            slot = i % 2
-            torch.cuda.current_stream().wait_event(copied[slot])
-            if i + 1 < nsteps:
-                issue_copy(1 - slot)
-            d = bufs[slot]
+        def issue_copy(slot):
+            with torch.cuda.stream(cstream):
+                cstream.wait_event(freed[slot])  # the step that last read this buffer is done
+                for k, v in pin.items():
+                    bufs[slot][k].copy_(v, non_blocking=True)
+                copied[slot].record(cstream)
+
+        def one_step(d):
             e2 = EventPacket(d["xy"], d["t"], ev.p, d["b"], 1, H, W)
-            loss = step(e2, (torch.arange(args.events, device=dev), d["u"], d["z"]))
-            freed[slot].record()
-            float(loss.detach())
-        e_end.record()
-        torch.cuda.synchronize()
-        return e_start.elapsed_time(e_end)
+            if with_noise:
+                return step(e2, (torch.arange(args.events, device=dev), d["u"], d["z"]))
+            m.grid.grad = None
+            out = obj_dev(e2, m)
+            out["loss"].backward()
+            return out["loss"]
 
-    run_e2e(max(args.warmup, 3))  # untimed: the pipeline's first use of its buffers
-    e2e_ms = run_e2e(args.steps) / args.steps
-    t = torch.tensor([e2e_ms], device=dev)
+        def run(nsteps):
+            """nsteps end-to-end steps; returns their device time in ms (events around the whole job)."""
+            for e in freed:
+                e.record()
+            barrier()
+            torch.cuda.synchronize()
+            e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e_start.record()
+            cstream.wait_event(e_start)
+            issue_copy(0)
+            for i in range(nsteps):
+                slot = i % 2
+                torch.cuda.current_stream().wait_event(copied[slot])
+                if i + 1 < nsteps:
+                    issue_copy(1 - slot)
+                loss = one_step(bufs[slot])
+                freed[slot].record()
+                float(loss.detach())
+            e_end.record()
+            torch.cuda.synchronize()
+            return e_start.elapsed_time(e_end)
+
+        run(max(args.warmup, 3))  # untimed: the pipeline's first use of its buffers
+        ms = run(args.steps) / args.steps
+        t_ = torch.tensor([ms], device=dev)
+        if world > 1:
+            dist.all_reduce(t_, op=dist.ReduceOp.MAX)
+        return float(t_), h2d
+
+    e2e_ms, h2d = e2e_pipeline(True)
+    e2e_dev_ms, h2d_dev = e2e_pipeline(False)
+    # the reference's per-step host draws (ats.py:84-88): uniforms for every event, normals for every anchor,
+    # from one CPU generator (single-threaded by construction: one sequential stream)
+    gen = torch.Generator().manual_seed(7)
+    for _ in range(2):
+        torch.rand((args.events, 2), generator=gen); torch.randn((args.events, 2), generator=gen)
+    t0 = time.perf_counter()
+    nrep = 5
+    for _ in range(nrep):
+        torch.rand((args.events, 2), generator=gen); torch.randn((args.events, 2), generator=gen)
+    host_rng_ms = 1000 * (time.perf_counter() - t0) / nrep
     if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
         dist.destroy_process_group()
-    e2e_ms = float(t)
 
     if rank != 0:
         return
@@ -544,7 +573,16 @@ def ours_arm(args):
         "e2e": {"value": world * args.events / (e2e_ms / 1000), "unit": "events/s", "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4,
                 "timing": "whole job, first H2D to last loss read, after untimed warm-up steps of the same "
-                          "pipeline; H2D of step i+1 overlaps step i (two buffers)"},
+                          "pipeline; H2D of step i+1 overlaps step i (two buffers); the step's noise (the "
+                          "reference's host draws) is copied with the events, its drawing is host_rng_ms",
+                "host_rng_ms": host_rng_ms,
+                "host_rng": "the reference's per-step draws on the host (torch CPU generator: (N,2) uniforms + "
+                            "(M,2) normals), not in value: a caller that draws them serially per step adds them"},
+        "e2e_device_rng": {"value": world * args.events / (e2e_dev_ms / 1000), "unit": "events/s",
+                           "ms_per_step": e2e_dev_ms, "h2d_bytes_per_step": h2d_dev, "d2h_bytes_per_step": 4,
+                           "timing": "as e2e, with AnchoredExact(device_rng=True): the noise is drawn on the device "
+                                     "inside the fused pipeline (opt-in; another stream than the reference's), so "
+                                     "only the events are copied"},
         "gpu_launches": int(launches),
         "clocks": clocks,
     }

@@ -38,7 +38,7 @@ enum {
 const char* atlb_last_error(void);
 /* ABI version of this header (bumped on incompatible changes). */
 int atlb_abi_version(void);
-#define ATLB_ABI_VERSION 7
+#define ATLB_ABI_VERSION 8
 /* Number of kernels this library has launched in the calling process (instrumentation; no reference
  * counterpart). */
 uint64_t atlb_kernel_launches(void);
@@ -260,6 +260,10 @@ typedef struct {
                               * With a sub-range, S_out holds the partial sums over those sources (sum
                               * them across the ranges, then ls = log(eps + S / den)), and the backward
                               * returns gv and gtheta of those sources only (sum gtheta across ranges). */
+  int32_t rng;           /* bit 0 (u) / bit 1 (z): atlb_exact_prepare draws that noise on the device when it
+                          * is given as NULL (atlb_rng_uniform2 / atlb_rng_normal2 of rng_seed, call
+                          * rng_call) instead of leaving it out; 0: NULL means "none", as in the reference */
+  uint64_t rng_seed, rng_call;
 } atlb_exact_cfg;
 
 int atlb_exact_prepare(const atlb_exact_cfg* cfg, const float* xy, const float* u, const float* t, const int64_t* b,
@@ -273,6 +277,16 @@ int atlb_exact_forward(const atlb_exact_cfg* cfg, const float* t, const int64_t*
 int atlb_exact_backward(const atlb_exact_cfg* cfg, const float* grad_ls, const int64_t* b, int64_t N, int64_t M,
                         const float* ev4, const atlb_plan_geom* geom, void* workspace, size_t workspace_bytes,
                         const float* S, const float* den, float* gv, float* gtheta, atlb_stream_t stream);
+
+/* ----------------------------------------------------------------------------------------------
+ * Opt-in device draws of the objective's noise.  No counterpart in the reference, which draws the
+ * dequantisation jitter u ~ U[0,1)^2 (atl/objectives/ats.py:84-85, 133-134) and the anchor smoothing
+ * noise z ~ N(0, I) (ats.py:87-88, 135) on the host with torch's CPU generator; these streams differ
+ * from torch's, so callers use them only when they ask for device draws.  Philox4x32-10 (Salmon et
+ * al., SC'11) with counter (i, stream, call, call >> 32) and key seed: out (n,2) float32.
+ * ---------------------------------------------------------------------------------------------- */
+int atlb_rng_uniform2(uint64_t seed, uint64_t call, int64_t n, float* out, atlb_stream_t stream);
+int atlb_rng_normal2(uint64_t seed, uint64_t call, int64_t n, float* out, atlb_stream_t stream);
 
 #ifdef __cplusplus
 }

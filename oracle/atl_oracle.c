@@ -549,3 +549,46 @@ ORACLE_API void oracle_visible_fraction(int kind, const float* theta, int64_t Hg
   }
   free(counts); free(centres); free(edges);
 }
+
+/* ------------------------------------------------------------------------------------------------
+ * Opt-in device draws (no counterpart in the reference, which draws with torch's CPU generator):
+ * Philox4x32-10 as published by Salmon, Moraes, Dror and Shaw (SC'11), restated in plain C, and the
+ * library's stream layout: item i of call c uses counter (i, (i >> 32) << 1 | stream, c, c >> 32) and
+ * key (seed, seed >> 32); stream 0 = two uniforms (w >> 8) 2^-24, stream 1 = two Box-Muller normals
+ * (computed here in double: the GPU's fp32 log / sincospi differ by a few ulp).
+ * ---------------------------------------------------------------------------------------------- */
+ORACLE_API void oracle_philox4x32_10(const uint32_t* ctr, const uint32_t* key, uint32_t* out) {
+  uint32_t c0 = ctr[0], c1 = ctr[1], c2 = ctr[2], c3 = ctr[3], k0 = key[0], k1 = key[1];
+  for (int r = 0; r < 10; ++r) {
+    const uint64_t p0 = (uint64_t)0xD2511F53u * c0, p1 = (uint64_t)0xCD9E8D57u * c2;
+    const uint32_t hi0 = (uint32_t)(p0 >> 32), lo0 = (uint32_t)p0, hi1 = (uint32_t)(p1 >> 32), lo1 = (uint32_t)p1;
+    c0 = hi1 ^ c1 ^ k0;
+    c1 = lo1;
+    c2 = hi0 ^ c3 ^ k1;
+    c3 = lo0;
+    k0 += 0x9E3779B9u;
+    k1 += 0xBB67AE85u;
+  }
+  out[0] = c0; out[1] = c1; out[2] = c2; out[3] = c3;
+}
+
+ORACLE_API void oracle_rng_draw2(int normal, uint64_t seed, uint64_t call, int64_t n, double* out) {
+  const uint32_t key[2] = {(uint32_t)seed, (uint32_t)(seed >> 32)};
+  for (int64_t i = 0; i < n; ++i) {
+    const uint64_t iu = (uint64_t)i;
+    const uint32_t ctr[4] = {(uint32_t)iu, ((uint32_t)(iu >> 32) << 1) | (uint32_t)(normal ? 1 : 0), (uint32_t)call,
+                             (uint32_t)(call >> 32)};
+    uint32_t o[4];
+    oracle_philox4x32_10(ctr, key, o);
+    if (!normal) {
+      out[2 * i] = (double)(o[0] >> 8) * 0x1p-24;
+      out[2 * i + 1] = (double)(o[1] >> 8) * 0x1p-24;
+    } else {
+      const double u1 = (double)((o[0] >> 8) + 1u) * 0x1p-24, u2 = (double)(o[1] >> 8) * 0x1p-24;
+      const double r = sqrt(-2.0 * log(u1));
+      out[2 * i] = r * cos(2.0 * M_PI * u2);
+      out[2 * i + 1] = r * sin(2.0 * M_PI * u2);
+    }
+  }
+}
+

@@ -60,6 +60,11 @@ def lib():
         L.oracle_pair_bwd_f64.restype = None
         L.oracle_pair_bwd_f64.argtypes = [_f32p] + pair + [_i64, _i64, _i64, _i64, _dbl, _dbl, _dbl, _i64, _f64p, _f64p,
                                                           _i64p]
+        _u32p = np.ctypeslib.ndpointer(dtype=np.uint32, flags="C_CONTIGUOUS")
+        L.oracle_philox4x32_10.restype = None
+        L.oracle_philox4x32_10.argtypes = [_u32p, _u32p, _u32p]
+        L.oracle_rng_draw2.restype = None
+        L.oracle_rng_draw2.argtypes = [ctypes.c_int, ctypes.c_uint64, ctypes.c_uint64, _i64, _f64p]
         L.oracle_splat_bilinear_fwd.argtypes = [_f32p, _f32p, _i64p, _i64, _i64, _i64, _i64, _f32p]
         L.oracle_splat_bilinear_bwd.argtypes = [_f32p, _f32p, _f32p, _i64p, _i64, _i64, _i64, _f32p, _f32p]
         L.oracle_splat_gauss_fwd.argtypes = [_f32p, _f32p, _i64p, _i64, _i64, _i64, _i64, _dbl, _i64, _f32p]
@@ -356,3 +361,19 @@ def velocity_backward_bound(kind, theta, xy, b, H, W, gabs, cnt):
 def threads() -> int:
     """Threads the OpenMP parts of the oracle use (pair forward only)."""
     return int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
+
+
+# ------------------------------------------------------------------------------------------------- device draws
+def philox4x32_10(ctr, key):
+    """Philox4x32-10 (Salmon et al., SC'11) of a 4-word counter and a 2-word key."""
+    out = np.zeros(4, np.uint32)
+    lib().oracle_philox4x32_10(np.asarray(ctr, np.uint32), np.asarray(key, np.uint32), out)
+    return out
+
+
+def rng_draw2(normal, seed, call, n):
+    """The library's device draws (atlb_rng_uniform2 / _normal2) in double: (n, 2)."""
+    out = np.zeros((n, 2), np.float64)
+    lib().oracle_rng_draw2(1 if normal else 0, int(seed), int(call), int(n), out)
+    return out
+

@@ -34,7 +34,8 @@ class ExactCfg(ctypes.Structure):
                 ("Wg", ctypes.c_int64), ("B", ctypes.c_int64), ("H", ctypes.c_int64), ("W", ctypes.c_int64),
                 ("h", ctypes.c_double), ("tau", ctypes.c_double), ("cut", ctypes.c_double),
                 ("eps_frac", ctypes.c_double), ("S", ctypes.c_int64), ("visibility", ctypes.c_int32),
-                ("n_check", ctypes.c_int64), ("src_begin", ctypes.c_int64), ("src_end", ctypes.c_int64)]
+                ("n_check", ctypes.c_int64), ("src_begin", ctypes.c_int64), ("src_end", ctypes.c_int64),
+                ("rng", ctypes.c_int32), ("rng_seed", ctypes.c_uint64), ("rng_call", ctypes.c_uint64)]
 
 
 class UnitRates(ctypes.Structure):
@@ -46,6 +47,8 @@ class UnitRates(ctypes.Structure):
 _SIGS = {
     "atlb_last_error": (ctypes.c_char_p, []),
     "atlb_abi_version": (_int, []),
+    "atlb_rng_uniform2": (_int, [ctypes.c_uint64, ctypes.c_uint64, _i64, _vp, _vp]),
+    "atlb_rng_normal2": (_int, [ctypes.c_uint64, ctypes.c_uint64, _i64, _vp, _vp]),
     "atlb_kernel_launches": (ctypes.c_uint64, []),
     "atlb_timing_enable": (_int, [_int]),
     "atlb_timing_read": (_int, [ctypes.c_char_p, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_int64),

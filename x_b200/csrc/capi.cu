@@ -47,6 +47,8 @@ int pair_fwd(const float*, const float*, const float*, const long long*, const l
 int pair_bwd(const float*, const float*, const float*, const float*, const long long*, const long long*, const float*,
              const float*, const long long*, const long long*, const float*, long long, long long, long long, long long,
              long long, long long, double, double, double, long long, float*, void*, cudaStream_t);
+int rng_draw2(bool normal, unsigned long long seed, unsigned long long call, long long n, float* out,
+              cudaStream_t s);
 int pair_fwd_noalloc(const float*, const float*, const float*, const long long*, const long long*, const float*,
                      const float*, const long long*, const long long*, const float*, long long, long long, long long,
                      long long, long long, long long, double, double, double, float*, cudaStream_t);
@@ -131,6 +133,20 @@ extern "C" {
 
 const char* atlb_last_error(void) { return g_err; }
 int atlb_abi_version(void) { return ATLB_ABI_VERSION; }
+
+int atlb_rng_uniform2(uint64_t seed, uint64_t call, int64_t n, float* out, atlb_stream_t stream) {
+  clear();
+  if (n < 0) { set_error("%s: negative size", __func__); return ATLB_ERR_ARG; }
+  NEED(out, n);
+  return rng_draw2(false, seed, call, n, out, STREAM(stream));
+}
+
+int atlb_rng_normal2(uint64_t seed, uint64_t call, int64_t n, float* out, atlb_stream_t stream) {
+  clear();
+  if (n < 0) { set_error("%s: negative size", __func__); return ATLB_ERR_ARG; }
+  NEED(out, n);
+  return rng_draw2(true, seed, call, n, out, STREAM(stream));
+}
 uint64_t atlb_kernel_launches(void) { return g_launches.load(std::memory_order_relaxed); }
 
 size_t atlb_unit_rates_scratch_bytes(void) { return unit_rates_scratch_bytes(); }

@@ -25,6 +25,7 @@
 #include "pair_fine.cuh"
 #include "pair_tiled.cuh"
 #include "plan_math.cuh"
+#include "rng.cuh"
 #include "scan.cuh"
 
 namespace atlb {
@@ -51,10 +52,11 @@ __global__ void k_exact_init(int* r) {
   }
 }
 
+// rng: u == NULL and rng set -> the dequantisation jitter is drawn on the device (stream 0 of rng.cuh)
 __global__ void __launch_bounds__(kThreads) k_exact_events(MotionView Mv, const float2* __restrict__ xy,
                                                            const float2* __restrict__ u, const float* __restrict__ t,
                                                            const long long* __restrict__ b, long long N, long long B,
-                                                           float4* __restrict__ ev4, int* r) {
+                                                           bool rng, RngKey K, float4* __restrict__ ev4, int* r) {
   float vm = 0.f;
   int unsorted = 0, badb = 0, tmn = 0x7fffffff, tmx = (int)0x80000000;
   const long long stride = (long long)gridDim.x * blockDim.x;
@@ -63,8 +65,8 @@ __global__ void __launch_bounds__(kThreads) k_exact_events(MotionView Mv, const 
     tmn = min(tmn, ot);
     tmx = max(tmx, ot);
     float2 p = xy[j];
-    if (u) {  // ats.py:84-85: xs = xy + (u - 0.5)
-      const float2 q = u[j];
+    if (u || rng) {  // ats.py:84-85: xs = xy + (u - 0.5)
+      const float2 q = u ? u[j] : rng_uniform2(K, (unsigned long long)j);
       p = make_float2(add_rn(p.x, sub_rn(q.x, 0.5f)), add_rn(p.y, sub_rn(q.y, 0.5f)));
     }
     const long long bj = b[j];
@@ -119,7 +121,8 @@ __global__ void __launch_bounds__(kThreads) k_exact_anchors(const float4* __rest
                                                             const float* __restrict__ t,
                                                             const long long* __restrict__ b, long long N,
                                                             const long long* __restrict__ anchors,
-                                                            const float2* __restrict__ z, float h_f, long long M,
+                                                            const float2* __restrict__ z, bool rng, RngKey K,
+                                                            float h_f, long long M,
                                                             float4* __restrict__ anc4, long long* __restrict__ anc_b,
                                                             int* r) {
   int mnx = 0x7fffffff, mny = 0x7fffffff, mxx = (int)0x80000000, mxy = (int)0x80000000, bad = 0;
@@ -134,8 +137,8 @@ __global__ void __launch_bounds__(kThreads) k_exact_anchors(const float4* __rest
     }
     const float4 e = ev4[a];
     float xa = e.x, ya = e.y;
-    if (z) {  // ats.py:87-88: xa = xs[a] + h * z
-      const float2 q = z[i];
+    if (z || rng) {  // ats.py:87-88: xa = xs[a] + h * z (z drawn on the device: stream 1 of rng.cuh)
+      const float2 q = z ? z[i] : rng_normal2(K, (unsigned long long)i);
       xa = add_rn(xa, mul_rn(h_f, q.x));
       ya = add_rn(ya, mul_rn(h_f, q.y));
     }
@@ -752,12 +755,14 @@ int exact_prepare(const atlb_exact_cfg& c, const float* xy, const float* u, cons
   int* r = (int*)scratch;
   launch(k_exact_init, 1, 32, 0, s, r);
   const MotionView Mv = motion_of(c);
+  const bool rng_u = (c.rng & 1) != 0, rng_z = (c.rng & 2) != 0;
+  const RngKey K = make_rng_key(c.rng_seed, c.rng_call);
   if (N > 0)
-    launch(k_exact_events, grid_for(N), kThreads, 0, s, Mv, (const float2*)xy, (const float2*)u, t, b, N, c.B,
-           (float4*)ev4, r);
+    launch(k_exact_events, grid_for(N), kThreads, 0, s, Mv, (const float2*)xy, (const float2*)u, t, b, N, c.B, rng_u,
+           K, (float4*)ev4, r);
   if (M > 0)
     launch(k_exact_anchors, grid_for(M), kThreads, 0, s, (const float4*)ev4, t, b, N, anchors, (const float2*)z,
-           (float)c.h, M, (float4*)anc4, anc_b, r);
+           rng_z, K, (float)c.h, M, (float4*)anc4, anc_b, r);
   int host[10];
   if (cudaMemcpyAsync(host, r, sizeof(host), cudaMemcpyDeviceToHost, s) != cudaSuccess)
     return launch_status("exact_prepare copy");

@@ -18,6 +18,7 @@ from typing import Optional
 import torch
 
 from . import _lib as L
+from . import rng as R
 from .events import EventPacket
 from .functional import ats_pair_sums, gather, splat, window_counts
 from .motion import VectorFieldMotion
@@ -84,13 +85,15 @@ class _FusedExact(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, theta, xy, t, b, anchors, u, z, spec):
-        kind, B, H, W, h, tau, cut, eps_frac, S, visibility, n_check = spec
+        kind, B, H, W, h, tau, cut, eps_frac, S, visibility, n_check, rng_bits, rng_seed, rng_call = spec
         lib = L.lib()
         dev = xy.device
         th = theta.detach().float().contiguous()
         Hg, Wg = (th.shape[-2], th.shape[-1]) if kind == L.MOTION_DENSE else (1, 1)
         cfg = L.ExactCfg(kind, th.data_ptr(), th.shape[0], Hg, Wg, B, H, W, float(h), float(tau), float(cut),
                          float(eps_frac), int(S), int(bool(visibility)), int(n_check))
+        # noise drawn on the device inside the prepare kernels (device_rng objectives): bit 0 u, bit 1 z
+        cfg.rng, cfg.rng_seed, cfg.rng_call = int(rng_bits), int(rng_seed) & (2**64 - 1), int(rng_call)
         xyc, tc, bc = xy.detach().float().contiguous(), t.detach().float().contiguous(), b.contiguous().long()
         N = tc.shape[0]
         anc = None if anchors is None else anchors.contiguous().long()
@@ -155,9 +158,12 @@ class AnchoredExact(Objective):
 
     def __init__(self, h: float = 1.0, tau: float = 1.0, eps_frac: float = 1e-2, n_anchors: Optional[int] = 20000,
                  n_slices: int = 16, cut: float = 3.0, seed: Optional[int] = None, smooth_anchors: bool = True,
-                 dequantize: bool = True, visibility: bool = True, anchor_margin: float = 0.0, fused: bool = True):
+                 dequantize: bool = True, visibility: bool = True, anchor_margin: float = 0.0, fused: bool = True,
+                 device_rng: bool = False):
         self.visibility, self.anchor_margin = visibility, anchor_margin
         self.fused = fused  # one libatlb200 pipeline for the motion fields it implements
+        # opt-in: u and z from the device generator (x_b200.rng) instead of the host generator's stream
+        self.device_draws = R.DeviceDraws(seed) if device_rng else None
         self.h, self.tau, self.eps_frac, self.n_anchors, self.n_slices, self.cut = h, tau, eps_frac, n_anchors, n_slices, cut
         self.smooth_anchors, self.dequantize = smooth_anchors, dequantize
         self.gen = torch.Generator().manual_seed(seed) if seed is not None else None
@@ -166,24 +172,41 @@ class AnchoredExact(Objective):
         """The objective's random draws (ats.py:79-88), in the reference's order: anchors, dequantisation
         jitter u ~ U[0,1)^2 per event, smoothing noise z ~ N(0, I) per anchor.  Returns (anchors, u, z)
         with u / z on the events' device (None when the option is off)."""
+        anchors = self._anchors(ev, anchors)
+        if self.device_draws is not None:  # opt-in device draws: the same numbers the fused path draws inline
+            call = self.device_draws.next_call()
+            u = R.uniform2(self.device_draws.seed, call, ev.n, ev.device) if self.dequantize else None
+            z = R.normal2(self.device_draws.seed, call, anchors.numel(), ev.device) if self.smooth_anchors else None
+            return anchors, u, z
+        u = torch.rand(ev.xy.shape, generator=self.gen).to(ev.xy) if self.dequantize else None
+        z = torch.randn((anchors.numel(), 2), generator=self.gen).to(ev.xy) if self.smooth_anchors else None
+        return anchors, u, z
+
+    def _anchors(self, ev: EventPacket, anchors: Optional[torch.Tensor]) -> torch.Tensor:
         if anchors is None:
             anchors = _pick_anchors(ev, self.n_anchors, self.gen)
             if self.anchor_margin > 0:
                 anchors = anchors[ev.inside(ev.xy[anchors], margin=-self.anchor_margin)]
-        u = torch.rand(ev.xy.shape, generator=self.gen).to(ev.xy) if self.dequantize else None
-        z = torch.randn((anchors.numel(), 2), generator=self.gen).to(ev.xy) if self.smooth_anchors else None
-        return anchors, u, z
+        return anchors
 
     def log_scores(self, ev: EventPacket, motion, anchors: Optional[torch.Tensor] = None, noise=None):
         """Per-anchor log predictive densities and the anchor indices (ats.py:75-96).  ``noise`` =
         (anchors, u, z) as returned by :meth:`draw` replaces the generator draws."""
         if not getattr(motion, "linear_at_event", False):
             raise ValueError("AnchoredExact needs a motion that is linear at the event; use AnchoredSliced")
-        anchors, u, z = self.draw(ev, anchors) if noise is None else noise
         kind = _fused_kind(motion)
-        if self.fused and kind >= 0 and ev.xy.is_cuda:
+        fused = self.fused and kind >= 0 and ev.xy.is_cuda
+        rng_bits, rng_seed, rng_call = 0, 0, 0
+        if noise is None and fused and self.device_draws is not None:
+            # device draws inside the fused pipeline's prepare kernels: no noise buffers
+            anchors, u, z = self._anchors(ev, anchors), None, None
+            rng_bits = (1 if self.dequantize else 0) | (2 if self.smooth_anchors else 0)
+            rng_seed, rng_call = self.device_draws.seed, self.device_draws.next_call()
+        else:
+            anchors, u, z = self.draw(ev, anchors) if noise is None else noise
+        if fused:
             spec = (kind, ev.batch_size, ev.height, ev.width, self.h, self.tau, self.cut, self.eps_frac,
-                    self.n_slices, self.visibility, 16)
+                    self.n_slices, self.visibility, 16, rng_bits, rng_seed, rng_call)
             try:
                 ls = _FusedExact.apply(motion.theta, ev.xy, ev.t, ev.b, anchors, u if self.dequantize else None,
                                        z if self.smooth_anchors else None, spec)
@@ -192,6 +215,9 @@ class AnchoredExact(Objective):
                 if "not sorted" not in str(e):
                     raise
                 # unsorted events: the stage-by-stage path below sorts the window keys like the reference
+                if rng_bits:  # the same draws, materialised
+                    u = R.uniform2(rng_seed, rng_call, ev.n, ev.device) if self.dequantize else None
+                    z = R.normal2(rng_seed, rng_call, anchors.numel(), ev.device) if self.smooth_anchors else None
         xs = ev.xy
         if self.dequantize:
             xs = xs + (u - 0.5)
@@ -225,9 +251,10 @@ class AnchoredSliced(Objective):
     def __init__(self, n_slices: int = 10, slices_per_step: Optional[int] = None, sigma: float = 1.0,
                  tau: float = 1.0, eps_frac: float = 1e-2, n_anchors_per_slice: Optional[int] = None,
                  logdet: bool = True, seed: Optional[int] = None, smooth_anchors: bool = True,
-                 dequantize: bool = True, visibility: bool = True):
+                 dequantize: bool = True, visibility: bool = True, device_rng: bool = False):
         self.smooth_anchors, self.dequantize, self.visibility = smooth_anchors, dequantize, visibility
         self.S, self.sps, self.sigma, self.tau, self.eps_frac = n_slices, slices_per_step, sigma, tau, eps_frac
+        self.device_draws = R.DeviceDraws(seed) if device_rng else None  # opt-in: see AnchoredExact
         self.nap, self.logdet = n_anchors_per_slice, logdet
         self.gen = torch.Generator().manual_seed(seed) if seed is not None else None
 
@@ -239,6 +266,11 @@ class AnchoredSliced(Objective):
         slices = list(range(S))
         if self.sps is not None and self.sps < S:
             slices = torch.randperm(S, generator=self.gen)[: self.sps].tolist()
+        if self.device_draws is not None:
+            call = self.device_draws.next_call()
+            u = R.uniform2(self.device_draws.seed, call, ev.n, ev.device) if self.dequantize else None
+            z = R.normal2(self.device_draws.seed, call, ev.n, ev.device) if self.smooth_anchors else None
+            return slices, u, z
         u = torch.rand(ev.xy.shape, generator=self.gen).to(ev.xy) if self.dequantize else None
         z = torch.randn(ev.xy.shape, generator=self.gen).to(ev.xy) if self.smooth_anchors else None
         return slices, u, z
