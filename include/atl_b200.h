@@ -38,7 +38,7 @@ enum {
 const char* atlb_last_error(void);
 /* ABI version of this header (bumped on incompatible changes). */
 int atlb_abi_version(void);
-#define ATLB_ABI_VERSION 8
+#define ATLB_ABI_VERSION 10
 /* Number of kernels this library has launched in the calling process (instrumentation; no reference
  * counterpart). */
 uint64_t atlb_kernel_launches(void);
@@ -72,11 +72,17 @@ int atlb_measure_unit_rates(atlb_unit_rates* out, void* scratch, size_t scratch_
  *   splat_gauss_fwd/bwd     csrc/atl_cpu.cpp:79-131  (decl. csrc/atl_ops.h:23-26)
  *   gather_bilinear_fwd/bwd csrc/atl_cpu.cpp:134-172 (decl. csrc/atl_ops.h:28-29)
  *   voxel_grid              csrc/atl_cpu.cpp:256-286 (decl. csrc/atl_ops.h:48-49)
+ * and the separable blur of atl/ops/functional.py:99-110 (torch conv2d in the reference).
+ * The bilinear splat, the gather and the voxel grid bucket their points by 32x32-pixel image tile in the
+ * workspace (atlb_tile_ops_workspace_bytes) and work on shared-memory tiles; per point, corners are taken
+ * in the reference's order and rounding (the gather and both backward passes are bit-identical to it).
  * ---------------------------------------------------------------------------------------------- */
+size_t atlb_tile_ops_workspace_bytes(int64_t N, int64_t B, int64_t H, int64_t W);
 int atlb_splat_bilinear_fwd(const float* pos, const float* w, const int64_t* bidx, int64_t N, int64_t B, int64_t H,
-                            int64_t W, float* img, atlb_stream_t stream);
+                            int64_t W, float* img, void* workspace, size_t workspace_bytes, atlb_stream_t stream);
 int atlb_splat_bilinear_bwd(const float* gimg, const float* pos, const float* w, const int64_t* bidx, int64_t N,
-                            int64_t B, int64_t H, int64_t W, float* gpos, float* gw, atlb_stream_t stream);
+                            int64_t B, int64_t H, int64_t W, float* gpos, float* gw, void* workspace,
+                            size_t workspace_bytes, atlb_stream_t stream);
 /* Gaussian splat: events are bucketed by 32x32-pixel image tile in the workspace
  * (atlb_splat_gauss_workspace_bytes), one shared-memory tile per CTA.  radius <= ATLB_SPLAT_GAUSS_MAX_RADIUS
  * (the tile and its halo live in shared memory). */
@@ -89,11 +95,17 @@ int atlb_splat_gauss_bwd(const float* gimg, const float* pos, const float* w, co
                          int64_t B, int64_t H, int64_t W, double sigma, int64_t radius, float* gpos, float* gw,
                          void* workspace, size_t workspace_bytes, atlb_stream_t stream);
 int atlb_gather_bilinear_fwd(const float* img, const float* pos, const int64_t* bidx, int64_t N, int64_t B, int64_t H,
-                             int64_t W, float* out, atlb_stream_t stream);
+                             int64_t W, float* out, void* workspace, size_t workspace_bytes, atlb_stream_t stream);
 int atlb_gather_bilinear_bwd(const float* gval, const float* img, const float* pos, const int64_t* bidx, int64_t N,
-                             int64_t B, int64_t H, int64_t W, float* gimg, float* gpos, atlb_stream_t stream);
+                             int64_t B, int64_t H, int64_t W, float* gimg, float* gpos, void* workspace,
+                             size_t workspace_bytes, atlb_stream_t stream);
 int atlb_voxel_grid(const float* pos, const float* t, const float* p, const int64_t* bidx, int64_t N, int64_t B,
-                    int64_t C, int64_t H, int64_t W, float* vox, atlb_stream_t stream);
+                    int64_t C, int64_t H, int64_t W, float* vox, void* workspace, size_t workspace_bytes,
+                    atlb_stream_t stream);
+/* Separable Gaussian blur with zero padding of P planes of H x W: the normalised kernel of radius
+ * max(ceil(3 sigma), 1) <= 32 along rows, then along columns.  The blur is its own adjoint (symmetric kernel,
+ * zero padding), so the same call gives the backward.  out must not alias img. */
+int atlb_blur(const float* img, int64_t P, int64_t H, int64_t W, double sigma, float* out, atlb_stream_t stream);
 
 /* ----------------------------------------------------------------------------------------------
  * Pair plan: the device replacement of build_pair_plan (atl/ops/functional.py:132-178), in three
@@ -277,6 +289,19 @@ int atlb_exact_forward(const atlb_exact_cfg* cfg, const float* t, const int64_t*
 int atlb_exact_backward(const atlb_exact_cfg* cfg, const float* grad_ls, const int64_t* b, int64_t N, int64_t M,
                         const float* ev4, const atlb_plan_geom* geom, void* workspace, size_t workspace_bytes,
                         const float* S, const float* den, float* gv, float* gtheta, atlb_stream_t stream);
+
+/* ----------------------------------------------------------------------------------------------
+ * Exact transport of the affine velocity fields (Translation, Affine), VectorFieldMotion.transport with
+ * mode="exact" (atl/motion/parametric.py:60-71): y = c + E[:2,:2] (x - c) + E[:2,2] with
+ * E = exp(dt [[A, t], [0, 0]]), dt = t_dst - t (t_dst per event, or the scalar t_dst_s when NULL),
+ * c = ((W - 1) / 2, (H - 1) / 2).  kind: ATLB_MOTION_TRANSLATION or ATLB_MOTION_AFFINE.
+ * The backward overwrites gtheta (B, 2|6) with dL/dtheta and, when gxy is not NULL, writes dL/dxy.
+ * ---------------------------------------------------------------------------------------------- */
+int atlb_flow_exact(int kind, const float* theta, int64_t B, int64_t H, int64_t W, const float* xy, const float* t,
+                    const float* t_dst, double t_dst_s, const int64_t* b, int64_t N, float* out, atlb_stream_t stream);
+int atlb_flow_exact_bwd(int kind, const float* gy, const float* theta, int64_t B, int64_t H, int64_t W,
+                        const float* xy, const float* t, const float* t_dst, double t_dst_s, const int64_t* b,
+                        int64_t N, float* gtheta, float* gxy, atlb_stream_t stream);
 
 /* ----------------------------------------------------------------------------------------------
  * Opt-in device draws of the objective's noise.  No counterpart in the reference, which draws the

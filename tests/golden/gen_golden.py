@@ -221,6 +221,21 @@ def gen_sliced(name, kind, n, B, H, W, seed, S, sigma, K=3):
          ls=ls.detach(), idx=idx, loss=loss.detach(), grad=param.grad)
 
 
+class _MatrixExpF64:
+    """Within the block, torch.linalg.matrix_exp (the reference's exact affine transport,
+    atl/motion/parametric.py:64-70) is evaluated in float64 and returned in the input's dtype: the
+    reference's math with an accurate exponential (its fp32 call is off by up to ~1e-4 px on these inputs)."""
+
+    def __enter__(self):
+        self.orig = torch.linalg.matrix_exp
+        orig = self.orig
+        torch.linalg.matrix_exp = lambda Z: orig(Z.double()).to(Z.dtype)
+        return self
+
+    def __exit__(self, *exc):
+        torch.linalg.matrix_exp = self.orig
+
+
 def gen_traj(name, K, basis_kind, per_event, seed, B=2, H=48, W=64, n=3000, scale=10.0):
     """PixelTrajectories.transport (atl/motion/trajectories.py:62-81) of seeded events: the transported
     positions and the gradient of sum(y * w) w.r.t. the coefficient grid, with positions spilling past the
@@ -279,3 +294,6 @@ if __name__ == "__main__":
     gen_traj("traj_k1_poly", 1, "polynomial", False, 103)
     gen_traj("traj_k4_bezier_pe", 4, "bezier", True, 104)
     gen_exact_traj("exact_traj_k1", 4000, 4, 48, 64, 110)
+    with _MatrixExpF64():
+        gen_sliced("sliced_affine_exact_f64exp", "affine_exact", 3000, 1, 48, 64, 80, 5, 1.0)
+

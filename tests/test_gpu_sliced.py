@@ -25,7 +25,12 @@ def np_(t):
     return t.detach().cpu().numpy()
 
 
-@pytest.mark.parametrize("name", ["sliced_trajectories", "sliced_affine_exact", "sliced_dense"])
+# sliced_affine_exact_f64exp: the reference's objective with torch.linalg.matrix_exp evaluated in float64
+# (tests/golden/gen_golden.py); sliced_affine_exact: as the reference runs, with its fp32 matrix_exp, whose
+# own error (up to ~1e-4 px here) moves the reference's scores by up to 2.4e-4 and its gradient by 1.9e-4
+# norm-wise (measured between the two goldens, both made by the reference)
+@pytest.mark.parametrize("name", ["sliced_trajectories", "sliced_affine_exact_f64exp", "sliced_affine_exact",
+                                  "sliced_dense"])
 def test_anchored_sliced_vs_reference(name):
     from x_b200 import motion as Mo
     from x_b200.events import EventPacket
@@ -48,11 +53,20 @@ def test_anchored_sliced_vs_reference(name):
     ls, idx = obj.log_scores(ev, m)
     np.testing.assert_array_equal(np_(idx), g["idx"])
     # splat sums in another order and with separable exponentials: scores within 1e-5
-    np.testing.assert_allclose(np_(ls), g["ls"], rtol=1e-5, atol=2e-5)
+    fp32_exp = name == "sliced_affine_exact"
+    if fp32_exp:
+        # the device flow is within 2e-6 px of float64; the reference's fp32 matrix_exp error enters the
+        # finite-difference log-determinant (ats.py:154-157, delta = 0.5) of a few anchors in 1e3
+        off = ~np.isclose(np_(ls), g["ls"], rtol=1e-5, atol=2e-5)
+        assert off.mean() <= 1e-3, off.sum()
+        np.testing.assert_allclose(np_(ls), g["ls"], rtol=1e-4, atol=1e-4)
+    else:
+        np.testing.assert_allclose(np_(ls), g["ls"], rtol=1e-5, atol=2e-5)
     loss = -ls.mean()
     loss.backward()
-    assert math.isclose(float(loss.detach()), float(g["loss"]), rel_tol=1e-5)
+    assert math.isclose(float(loss.detach()), float(g["loss"]), rel_tol=1e-5)  # the mean hides single anchors
     # the reference's gradient is an fp32 sum in another order: norm-wise within 1e-5, and no element off by
     # more than 1e-5 of the largest
-    e = assert_grad_parity(np_(param.grad), g["grad"], what=f"{name} parameter gradient")
-    assert e["max_over_max"] <= 1e-5, e
+    tol = 3e-4 if fp32_exp else 1e-5
+    e = assert_grad_parity(np_(param.grad), g["grad"], rtol=tol, what=f"{name} parameter gradient")
+    assert e["max_over_max"] <= tol, e

@@ -29,15 +29,20 @@ class _AtlB200Ext:
     def splat_bilinear_fwd(self, pos, w, b, B, H, W):
         L.require_cuda("pos", pos, F32); L.require_cuda("w", w, F32); L.require_cuda("bidx", b, I64)
         img = _empty((B, H, W), pos)
+        nb = L.lib().atlb_tile_ops_workspace_bytes(pos.shape[0], B, H, W)
+        ws = L.workspace(nb, pos.device)
         L.check(L.lib().atlb_splat_bilinear_fwd(L.ptr(pos), L.ptr(w), L.ptr(b), pos.shape[0], B, H, W, L.ptr(img),
-                                                 L.stream()), "splat_bilinear_fwd")
+                                                 L.ptr(ws), nb, L.stream()), "splat_bilinear_fwd")
         return img
 
     def splat_bilinear_bwd(self, g, pos, w, b):
         L.require_cuda("gimg", g, F32); L.require_cuda("pos", pos, F32)
         gp, gw = torch.empty_like(pos), torch.empty_like(w)
-        L.check(L.lib().atlb_splat_bilinear_bwd(L.ptr(g), L.ptr(pos), L.ptr(w), L.ptr(b), pos.shape[0], g.shape[0],
-                                                 g.shape[1], g.shape[2], L.ptr(gp), L.ptr(gw), L.stream()),
+        B, H, W = g.shape
+        nb = L.lib().atlb_tile_ops_workspace_bytes(pos.shape[0], B, H, W)
+        ws = L.workspace(nb, pos.device)
+        L.check(L.lib().atlb_splat_bilinear_bwd(L.ptr(g), L.ptr(pos), L.ptr(w), L.ptr(b), pos.shape[0], B, H, W,
+                                                 L.ptr(gp), L.ptr(gw), L.ptr(ws), nb, L.stream()),
                 "splat_bilinear_bwd")
         return [gp, gw]
 
@@ -65,16 +70,21 @@ class _AtlB200Ext:
         L.require_cuda("img", img, F32); L.require_cuda("pos", pos, F32); L.require_cuda("bidx", b, I64)
         out = _empty((pos.shape[0],), pos)
         B, H, W = img.shape
+        nb = L.lib().atlb_tile_ops_workspace_bytes(pos.shape[0], B, H, W)
+        ws = L.workspace(nb, pos.device)
         L.check(L.lib().atlb_gather_bilinear_fwd(L.ptr(img), L.ptr(pos), L.ptr(b), pos.shape[0], B, H, W, L.ptr(out),
-                                                  L.stream()), "gather_bilinear_fwd")
+                                                  L.ptr(ws), nb, L.stream()), "gather_bilinear_fwd")
         return out
 
     def gather_bilinear_bwd(self, g, img, pos, b):
         L.require_cuda("gval", g, F32); L.require_cuda("img", img, F32)
         gi, gp = torch.empty_like(img), torch.empty_like(pos)
         B, H, W = img.shape
+        nb = L.lib().atlb_tile_ops_workspace_bytes(pos.shape[0], B, H, W)
+        ws = L.workspace(nb, pos.device)
         L.check(L.lib().atlb_gather_bilinear_bwd(L.ptr(g), L.ptr(img), L.ptr(pos), L.ptr(b), pos.shape[0], B, H, W,
-                                                  L.ptr(gi), L.ptr(gp), L.stream()), "gather_bilinear_bwd")
+                                                  L.ptr(gi), L.ptr(gp), L.ptr(ws), nb, L.stream()),
+                "gather_bilinear_bwd")
         return [gi, gp]
 
     def voxel_grid(self, pos, t, p, b, B, C, H, W):
@@ -82,9 +92,20 @@ class _AtlB200Ext:
             L.require_cuda(n, x, F32)
         L.require_cuda("bidx", b, I64)
         vox = _empty((B, C, H, W), pos)
+        nb = L.lib().atlb_tile_ops_workspace_bytes(pos.shape[0], B, H, W)
+        ws = L.workspace(nb, pos.device)
         L.check(L.lib().atlb_voxel_grid(L.ptr(pos), L.ptr(t), L.ptr(p), L.ptr(b), pos.shape[0], B, C, H, W,
-                                         L.ptr(vox), L.stream()), "voxel_grid")
+                                         L.ptr(vox), L.ptr(ws), nb, L.stream()), "voxel_grid")
         return vox
+
+    def blur(self, img, sigma):
+        """Separable Gaussian blur of (P, H, W) planes (atl/ops/functional.py:99-110), zero padding."""
+        L.require_cuda("img", img, F32)
+        x = img.contiguous()
+        out = torch.empty_like(x)
+        P = x.numel() // (x.shape[-1] * x.shape[-2]) if x.numel() else 0
+        L.check(L.lib().atlb_blur(L.ptr(x), P, x.shape[-2], x.shape[-1], float(sigma), L.ptr(out), L.stream()), "blur")
+        return out
 
     # ---------------------------------------------------------------------------- anchored pairs
     @staticmethod

@@ -47,6 +47,10 @@ class UnitRates(ctypes.Structure):
 _SIGS = {
     "atlb_last_error": (ctypes.c_char_p, []),
     "atlb_abi_version": (_int, []),
+    "atlb_tile_ops_workspace_bytes": (_size, [_i64, _i64, _i64, _i64]),
+    "atlb_blur": (_int, [_vp, _i64, _i64, _i64, _dbl, _vp, _vp]),
+    "atlb_flow_exact": (_int, [_int, _vp, _i64, _i64, _i64, _vp, _vp, _vp, _dbl, _vp, _i64, _vp, _vp]),
+    "atlb_flow_exact_bwd": (_int, [_int, _vp, _vp, _i64, _i64, _i64, _vp, _vp, _vp, _dbl, _vp, _i64, _vp, _vp, _vp]),
     "atlb_rng_uniform2": (_int, [ctypes.c_uint64, ctypes.c_uint64, _i64, _vp, _vp]),
     "atlb_rng_normal2": (_int, [ctypes.c_uint64, ctypes.c_uint64, _i64, _vp, _vp]),
     "atlb_kernel_launches": (ctypes.c_uint64, []),
@@ -55,14 +59,14 @@ _SIGS = {
                                 _int]),
     "atlb_unit_rates_scratch_bytes": (_size, []),
     "atlb_measure_unit_rates": (_int, [ctypes.POINTER(UnitRates), _vp, _size, _vp]),
-    "atlb_splat_bilinear_fwd": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _vp]),
-    "atlb_splat_bilinear_bwd": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _vp, _vp]),
+    "atlb_splat_bilinear_fwd": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _vp, _size, _vp]),
+    "atlb_splat_bilinear_bwd": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _size, _vp]),
     "atlb_splat_gauss_workspace_bytes": (_size, [_i64, _i64, _i64, _i64]),
     "atlb_splat_gauss_fwd": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _dbl, _i64, _vp, _vp, _size, _vp]),
     "atlb_splat_gauss_bwd": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _dbl, _i64, _vp, _vp, _vp, _size, _vp]),
-    "atlb_gather_bilinear_fwd": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _vp]),
-    "atlb_gather_bilinear_bwd": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _vp, _vp]),
-    "atlb_voxel_grid": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _vp]),
+    "atlb_gather_bilinear_fwd": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _vp, _size, _vp]),
+    "atlb_gather_bilinear_bwd": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _size, _vp]),
+    "atlb_voxel_grid": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _vp, _size, _vp]),
     "atlb_plan_geometry": (_int, [_vp, _vp, _i64, _vp, _vp, _i64, _i64, _i64, _dbl, _dbl, _i64, _vp,
                                   ctypes.POINTER(PlanGeom), _vp]),
     "atlb_plan_workspace_bytes": (_size, [_i64]),

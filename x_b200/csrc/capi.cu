@@ -47,26 +47,33 @@ int pair_fwd(const float*, const float*, const float*, const long long*, const l
 int pair_bwd(const float*, const float*, const float*, const float*, const long long*, const long long*, const float*,
              const float*, const long long*, const long long*, const float*, long long, long long, long long, long long,
              long long, long long, double, double, double, long long, float*, void*, cudaStream_t);
+int flow_exact(int kind, const float* theta, long long B, long long H, long long W, const float* xy, const float* t,
+               const float* t_dst, double t_dst_s, const long long* b, long long N, float* out, cudaStream_t s);
+int flow_exact_bwd(int kind, const float* gy, const float* theta, long long B, long long H, long long W,
+                   const float* xy, const float* t, const float* t_dst, double t_dst_s, const long long* b, long long N,
+                   float* gtheta, float* gxy, cudaStream_t s);
 int rng_draw2(bool normal, unsigned long long seed, unsigned long long call, long long n, float* out,
               cudaStream_t s);
 int pair_fwd_noalloc(const float*, const float*, const float*, const long long*, const long long*, const float*,
                      const float*, const long long*, const long long*, const float*, long long, long long, long long,
                      long long, long long, long long, double, double, double, float*, cudaStream_t);
+size_t tile_ops_workspace_bytes(long long N, long long B, long long H, long long W);
 int splat_bilinear_fwd(const float*, const float*, const long long*, long long, long long, long long, long long,
-                       float*, cudaStream_t);
+                       float*, void*, cudaStream_t);
 int splat_bilinear_bwd(const float*, const float*, const float*, const long long*, long long, long long, long long,
-                       long long, float*, float*, cudaStream_t);
+                       long long, float*, float*, void*, cudaStream_t);
+int blur(const float*, long long, long long, long long, double, float*, cudaStream_t);
 size_t splat_gauss_workspace_bytes(long long N, long long B, long long H, long long W);
 int splat_gauss_fwd(const float*, const float*, const long long*, long long, long long, long long, long long, double,
                     long long, float*, void*, cudaStream_t);
 int splat_gauss_bwd(const float*, const float*, const float*, const long long*, long long, long long, long long,
                     long long, double, long long, float*, float*, void*, cudaStream_t);
-int gather_fwd(const float*, const float*, const long long*, long long, long long, long long, long long, float*,
+int gather_fwd(const float*, const float*, const long long*, long long, long long, long long, long long, float*, void*,
                cudaStream_t);
 int gather_bwd(const float*, const float*, const float*, const long long*, long long, long long, long long, long long,
-               float*, float*, cudaStream_t);
+               float*, float*, void*, cudaStream_t);
 int voxel_grid(const float*, const float*, const float*, const long long*, long long, long long, long long, long long,
-               long long, float*, cudaStream_t);
+               long long, float*, void*, cudaStream_t);
 int velocity(const MotionView&, const float*, const long long*, long long, float*, cudaStream_t);
 int velocity_bwd(const MotionView&, const float*, const float*, const long long*, long long, float*, cudaStream_t);
 int visible_fraction(const MotionView&, const float*, const float*, const long long*, long long, const float*,
@@ -134,6 +141,33 @@ extern "C" {
 const char* atlb_last_error(void) { return g_err; }
 int atlb_abi_version(void) { return ATLB_ABI_VERSION; }
 
+static int check_flow(int kind, const float* theta, int64_t B, int64_t H, int64_t W, int64_t N, const char* fn) {
+  if (kind != ATLB_MOTION_TRANSLATION && kind != ATLB_MOTION_AFFINE) {
+    set_error("%s: kind %d has no closed-form flow (translation or affine only)", fn, kind);
+    return ATLB_ERR_ARG;
+  }
+  if (N < 0 || B < 1 || H < 1 || W < 1 || !theta) { set_error("%s: invalid sizes", fn); return ATLB_ERR_ARG; }
+  return ATLB_OK;
+}
+
+int atlb_flow_exact(int kind, const float* theta, int64_t B, int64_t H, int64_t W, const float* xy, const float* t,
+                    const float* t_dst, double t_dst_s, const int64_t* b, int64_t N, float* out, atlb_stream_t stream) {
+  clear();
+  if (int st = check_flow(kind, theta, B, H, W, N, __func__)) return st;
+  NEED(xy, N); NEED(t, N); NEED(b, N); NEED(out, N);
+  return flow_exact(kind, theta, B, H, W, xy, t, t_dst, t_dst_s, LL(b), N, out, STREAM(stream));
+}
+
+int atlb_flow_exact_bwd(int kind, const float* gy, const float* theta, int64_t B, int64_t H, int64_t W,
+                        const float* xy, const float* t, const float* t_dst, double t_dst_s, const int64_t* b,
+                        int64_t N, float* gtheta, float* gxy, atlb_stream_t stream) {
+  clear();
+  if (int st = check_flow(kind, theta, B, H, W, N, __func__)) return st;
+  NEED(gy, N); NEED(xy, N); NEED(t, N); NEED(b, N);
+  if (!gtheta) { set_error("%s: gtheta NULL", __func__); return ATLB_ERR_ARG; }
+  return flow_exact_bwd(kind, gy, theta, B, H, W, xy, t, t_dst, t_dst_s, LL(b), N, gtheta, gxy, STREAM(stream));
+}
+
 int atlb_rng_uniform2(uint64_t seed, uint64_t call, int64_t n, float* out, atlb_stream_t stream) {
   clear();
   if (n < 0) { set_error("%s: negative size", __func__); return ATLB_ERR_ARG; }
@@ -161,20 +195,49 @@ int atlb_measure_unit_rates(atlb_unit_rates* out, void* scratch, size_t scratch_
   return measure_unit_rates(out, scratch, STREAM(stream));
 }
 
+size_t atlb_tile_ops_workspace_bytes(int64_t N, int64_t B, int64_t H, int64_t W) {
+  return tile_ops_workspace_bytes(N < 0 ? 0 : N, B < 0 ? 0 : B, H < 0 ? 0 : H, W < 0 ? 0 : W);
+}
+
+// Sizes the tiled bilinear ops index with 32-bit integers, and their workspace.
+static int check_tiles(int64_t N, int64_t B, int64_t H, int64_t W, void* ws, size_t ws_bytes, const char* fn) {
+  if (N > (1LL << 31) - 1 || H > (1LL << 30) || W > (1LL << 30) || B * ((H + 31) / 32) * ((W + 31) / 32) > (1LL << 31) - 2) {
+    set_error("%s: sizes exceed the int32 point / tile indices", fn);
+    return ATLB_ERR_OVERFLOW;
+  }
+  if (!ws || ws_bytes < tile_ops_workspace_bytes(N, B, H, W)) {
+    set_error("%s: workspace %zu < %zu bytes", fn, ws_bytes, tile_ops_workspace_bytes(N, B, H, W));
+    return ATLB_ERR_WORKSPACE;
+  }
+  return ATLB_OK;
+}
+
 int atlb_splat_bilinear_fwd(const float* pos, const float* w, const int64_t* bidx, int64_t N, int64_t B, int64_t H,
-                            int64_t W, float* img, atlb_stream_t stream) {
+                            int64_t W, float* img, void* workspace, size_t workspace_bytes, atlb_stream_t stream) {
   clear();
   NONNEG(N); NONNEG(B); NONNEG(H); NONNEG(W);
   NEED(pos, N); NEED(w, N); NEED(bidx, N); NEED(img, B * H * W);
-  return splat_bilinear_fwd(pos, w, LL(bidx), N, B, H, W, img, STREAM(stream));
+  if (int st = check_tiles(N, B, H, W, workspace, workspace_bytes, __func__)) return st;
+  return splat_bilinear_fwd(pos, w, LL(bidx), N, B, H, W, img, workspace, STREAM(stream));
 }
 
 int atlb_splat_bilinear_bwd(const float* gimg, const float* pos, const float* w, const int64_t* bidx, int64_t N,
-                            int64_t B, int64_t H, int64_t W, float* gpos, float* gw, atlb_stream_t stream) {
+                            int64_t B, int64_t H, int64_t W, float* gpos, float* gw, void* workspace,
+                            size_t workspace_bytes, atlb_stream_t stream) {
   clear();
   NONNEG(N); NONNEG(B); NONNEG(H); NONNEG(W);
-  NEED(gimg, N); NEED(pos, N); NEED(w, N); NEED(bidx, N); NEED(gpos, N); NEED(gw, N);
-  return splat_bilinear_bwd(gimg, pos, w, LL(bidx), N, B, H, W, gpos, gw, STREAM(stream));
+  NEED(gimg, B * H * W); NEED(pos, N); NEED(w, N); NEED(bidx, N); NEED(gpos, N); NEED(gw, N);
+  if (int st = check_tiles(N, B, H, W, workspace, workspace_bytes, __func__)) return st;
+  return splat_bilinear_bwd(gimg, pos, w, LL(bidx), N, B, H, W, gpos, gw, workspace, STREAM(stream));
+}
+
+int atlb_blur(const float* img, int64_t P, int64_t H, int64_t W, double sigma, float* out, atlb_stream_t stream) {
+  clear();
+  NONNEG(P); NONNEG(H); NONNEG(W);
+  NEED(img, P * H * W); NEED(out, P * H * W);
+  if (!(sigma > 0)) { set_error("%s: sigma must be positive", __func__); return ATLB_ERR_ARG; }
+  if (img == out) { set_error("%s: out must not alias img", __func__); return ATLB_ERR_ARG; }
+  return blur(img, P, H, W, sigma, out, STREAM(stream));
 }
 
 size_t atlb_splat_gauss_workspace_bytes(int64_t N, int64_t B, int64_t H, int64_t W) {
@@ -220,27 +283,32 @@ int atlb_splat_gauss_bwd(const float* gimg, const float* pos, const float* w, co
 }
 
 int atlb_gather_bilinear_fwd(const float* img, const float* pos, const int64_t* bidx, int64_t N, int64_t B, int64_t H,
-                             int64_t W, float* out, atlb_stream_t stream) {
+                             int64_t W, float* out, void* workspace, size_t workspace_bytes, atlb_stream_t stream) {
   clear();
   NONNEG(N); NONNEG(B); NONNEG(H); NONNEG(W);
-  NEED(img, N); NEED(pos, N); NEED(bidx, N); NEED(out, N);
-  return gather_fwd(img, pos, LL(bidx), N, B, H, W, out, STREAM(stream));
+  NEED(img, B * H * W); NEED(pos, N); NEED(bidx, N); NEED(out, N);
+  if (int st = check_tiles(N, B, H, W, workspace, workspace_bytes, __func__)) return st;
+  return gather_fwd(img, pos, LL(bidx), N, B, H, W, out, workspace, STREAM(stream));
 }
 
 int atlb_gather_bilinear_bwd(const float* gval, const float* img, const float* pos, const int64_t* bidx, int64_t N,
-                             int64_t B, int64_t H, int64_t W, float* gimg, float* gpos, atlb_stream_t stream) {
+                             int64_t B, int64_t H, int64_t W, float* gimg, float* gpos, void* workspace,
+                             size_t workspace_bytes, atlb_stream_t stream) {
   clear();
   NONNEG(N); NONNEG(B); NONNEG(H); NONNEG(W);
-  NEED(gval, N); NEED(img, N); NEED(pos, N); NEED(bidx, N); NEED(gimg, B * H * W); NEED(gpos, N);
-  return gather_bwd(gval, img, pos, LL(bidx), N, B, H, W, gimg, gpos, STREAM(stream));
+  NEED(gval, N); NEED(img, B * H * W); NEED(pos, N); NEED(bidx, N); NEED(gimg, B * H * W); NEED(gpos, N);
+  if (int st = check_tiles(N, B, H, W, workspace, workspace_bytes, __func__)) return st;
+  return gather_bwd(gval, img, pos, LL(bidx), N, B, H, W, gimg, gpos, workspace, STREAM(stream));
 }
 
 int atlb_voxel_grid(const float* pos, const float* t, const float* p, const int64_t* bidx, int64_t N, int64_t B,
-                    int64_t C, int64_t H, int64_t W, float* vox, atlb_stream_t stream) {
+                    int64_t C, int64_t H, int64_t W, float* vox, void* workspace, size_t workspace_bytes,
+                    atlb_stream_t stream) {
   clear();
   NONNEG(N); NONNEG(B); NONNEG(C); NONNEG(H); NONNEG(W);
   NEED(pos, N); NEED(t, N); NEED(p, N); NEED(bidx, N); NEED(vox, B * C * H * W);
-  return voxel_grid(pos, t, p, LL(bidx), N, B, C, H, W, vox, STREAM(stream));
+  if (int st = check_tiles(N, B, H, W, workspace, workspace_bytes, __func__)) return st;
+  return voxel_grid(pos, t, p, LL(bidx), N, B, C, H, W, vox, workspace, STREAM(stream));
 }
 
 int atlb_plan_geometry(const float* x, const float* v, int64_t N, const int64_t* anchors, const float* anchor_xy,

@@ -11,6 +11,7 @@ import ctypes
 import math
 from dataclasses import dataclass
 
+import numpy as np
 import torch
 
 from . import _lib as L
@@ -93,26 +94,36 @@ def gather(img: torch.Tensor, pos: torch.Tensor, b: torch.Tensor) -> torch.Tenso
 
 
 # ------------------------------------------------------------------------------------------- blur
-def gaussian_kernel1d(sigma: float, device, dtype=torch.float32):
-    """Normalised 1-D Gaussian kernel of radius ceil(3 sigma) (functional.py:91-96)."""
+def gaussian_kernel1d(sigma: float, device, dtype=torch.float32) -> torch.Tensor:
+    """The normalised 1-D Gaussian kernel of radius max(ceil(3 sigma), 1) that :func:`blur` applies
+    (atl/ops/functional.py:89-96): fp32 exp(-i^2 / (2 sigma^2)) for i = -r..r, divided by their sum."""
     r = max(int(math.ceil(3 * sigma)), 1)
-    x = torch.arange(-r, r + 1, device=device, dtype=dtype)
-    k = torch.exp(-x * x / (2 * sigma * sigma))
-    return k / k.sum()
+    i = np.arange(-r, r + 1, dtype=np.float32)
+    k = np.exp(-(i * i) / np.float32(2 * sigma * sigma), dtype=np.float32)
+    return torch.as_tensor(k / k.sum(dtype=np.float32), device=device).to(dtype)
+
+
+class _Blur(torch.autograd.Function):
+    """Separable Gaussian blur on the device (atlb_blur).  The zero-padded convolution with a symmetric kernel
+    is self-adjoint, so the backward is the same blur of the incoming gradient."""
+
+    @staticmethod
+    def forward(ctx, img, sigma):
+        ctx.sigma = sigma
+        return get_ext().blur(_f32(img), sigma)
+
+    @staticmethod
+    def backward(ctx, g):
+        return get_ext().blur(_f32(g), ctx.sigma), None
 
 
 def blur(img: torch.Tensor, sigma: float) -> torch.Tensor:
-    """Separable Gaussian blur, zero padding (functional.py:99-110; baseline IWEs, not the anchored path)."""
+    """Separable Gaussian blur of a (B, H, W) or (B, C, H, W) image, zero padding, normalised kernel of radius
+    max(ceil(3 sigma), 1) (atl/ops/functional.py:99-110; baseline IWEs, not the anchored path)."""
     if sigma <= 0:
         return img
-    squeeze = img.dim() == 3
-    x = img[:, None] if squeeze else img
-    C = x.shape[1]
-    k = gaussian_kernel1d(sigma, img.device, img.dtype)
-    r = (k.numel() - 1) // 2
-    x = torch.nn.functional.conv2d(x, k.view(1, 1, 1, -1).expand(C, 1, 1, -1), padding=(0, r), groups=C)
-    x = torch.nn.functional.conv2d(x, k.view(1, 1, -1, 1).expand(C, 1, -1, 1), padding=(r, 0), groups=C)
-    return x[:, 0] if squeeze else x
+    _need_cuda(img, "blur")
+    return _Blur.apply(img, float(sigma)).to(img.dtype)
 
 
 # ------------------------------------------------------------------------------------------- anchored pairs

@@ -76,6 +76,37 @@ class _VelocityFn(torch.autograd.Function):
         return g.to(dtype), None, None, None, None, None
 
 
+class _FlowExactFn(torch.autograd.Function):
+    """Exact flow of an affine field on the device (atlb_flow_exact / _bwd), differentiable w.r.t. theta and the
+    positions."""
+
+    @staticmethod
+    def forward(ctx, theta, xy, t, t_dst, b, kind, H, W):
+        th = theta.detach().float().contiguous()
+        xyc, tc, bl = xy.detach().float().contiguous(), t.detach().float().contiguous(), b.contiguous().long()
+        if torch.is_tensor(t_dst) and t_dst.dim() > 0:
+            td, tds = t_dst.detach().float().contiguous().expand_as(tc).contiguous(), 0.0
+        else:
+            td, tds = None, float(t_dst)
+        out = torch.empty_like(xyc)
+        L.check(L.lib().atlb_flow_exact(kind, L.ptr(th), th.shape[0], H, W, L.ptr(xyc), L.ptr(tc), L.ptr(td), tds,
+                                        L.ptr(bl), tc.shape[0], L.ptr(out), L.stream()), "flow_exact")
+        ctx.save_for_backward(th, xyc, tc, bl, td if td is not None else tc.new_empty(0))
+        ctx.meta = (kind, H, W, tds, td is not None, theta.dtype, xy.dtype)
+        return out.to(xy.dtype)
+
+    @staticmethod
+    def backward(ctx, gy):
+        th, xyc, tc, bl, td = ctx.saved_tensors
+        kind, H, W, tds, per_event, tdt, xdt = ctx.meta
+        gth = torch.empty_like(th)
+        gxy = torch.empty_like(xyc) if ctx.needs_input_grad[1] else None
+        L.check(L.lib().atlb_flow_exact_bwd(kind, L.ptr(gy.contiguous().float()), L.ptr(th), th.shape[0], H, W,
+                                            L.ptr(xyc), L.ptr(tc), L.ptr(td if per_event else None), tds, L.ptr(bl),
+                                            tc.shape[0], L.ptr(gth), L.ptr(gxy), L.stream()), "flow_exact_bwd")
+        return gth.to(tdt), (None if gxy is None else gxy.to(xdt)), None, None, None, None, None, None
+
+
 class VectorFieldMotion(Motion):
     """Autonomous velocity field v(x; theta) (parametric.py:84-145)."""
     n_params: int = 0
@@ -103,29 +134,28 @@ class VectorFieldMotion(Motion):
         return None
 
     def transport(self, xy, t, t_dst, b):
-        """parametric.py:114-139: linear warp, closed-form affine flow, or RK4."""
-        dt = as_time(t_dst, t) - t
+        """Where the scene point of event (xy, t) is at t_dst (atl/motion/parametric.py:53-78).  mode="linear": the
+        warp x + v(x) (t_dst - t).  mode="exact": the flow of the field -- in closed form on the device for the
+        affine fields (the augmented matrix exponential, atlb_flow_exact), by classic fourth-order Runge-Kutta
+        stages of the field otherwise (rk4_steps steps)."""
         if self.mode == "linear":
+            dt = as_time(t_dst, t) - t
             return xy + self.field(xy, b) * dt[:, None]
-        parts = self.affine_parts(b)
-        if parts is not None:
-            A, tr = parts
-            c = self.c.to(xy)
-            n = A.shape[0]
-            Z = torch.zeros(n, 3, 3, device=xy.device, dtype=xy.dtype)
-            Z[:, :2, :2] = A
-            Z[:, :2, 2] = tr
-            E = torch.linalg.matrix_exp(Z * dt[:, None, None])
-            return c + torch.bmm(E[:, :2, :2], (xy - c)[..., None])[..., 0] + E[:, :2, 2]
-        n = self.rk4_steps
-        h = dt / n
-        x = xy
-        for _ in range(n):
-            k1 = self._field_any(x, b)
-            k2 = self._field_any(x + 0.5 * h[:, None] * k1, b)
-            k3 = self._field_any(x + 0.5 * h[:, None] * k2, b)
-            k4 = self._field_any(x + h[:, None] * k3, b)
-            x = x + h[:, None] * (k1 + 2 * k2 + 2 * k3 + k4) / 6
+        if self.kind in (L.MOTION_TRANSLATION, L.MOTION_AFFINE) and xy.is_cuda:
+            return _FlowExactFn.apply(self.theta, xy, t, t_dst, b, self.kind, self.H, self.W)
+        return self._runge_kutta(xy, as_time(t_dst, t) - t, b)
+
+    def _runge_kutta(self, x, dt, b):
+        """rk4_steps classic RK4 steps of dx/ds = v(x) over dt (per event): stage slopes at the start, twice at the
+        midpoint and at the end, combined with weights 1/6, 1/3, 1/3, 1/6."""
+        step = (dt / self.rk4_steps)[:, None]
+        half = 0.5 * step
+        for _ in range(self.rk4_steps):
+            s1 = self._field_any(x, b)
+            s2 = self._field_any(x + half * s1, b)
+            s3 = self._field_any(x + half * s2, b)
+            s4 = self._field_any(x + step * s3, b)
+            x = x + step * (s1 + 2 * s2 + 2 * s3 + s4) / 6
         return x
 
     def _field_any(self, xy, b):
