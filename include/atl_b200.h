@@ -38,7 +38,7 @@ enum {
 const char* atlb_last_error(void);
 /* ABI version of this header (bumped on incompatible changes). */
 int atlb_abi_version(void);
-#define ATLB_ABI_VERSION 10
+#define ATLB_ABI_VERSION 11
 /* Number of kernels this library has launched in the calling process (instrumentation; no reference
  * counterpart). */
 uint64_t atlb_kernel_launches(void);
@@ -246,6 +246,25 @@ int atlb_traj_transport_bwd(int mode, const float* gy, const float* coeff, int64
                             int64_t K, int basis, const float* bezier_c, double offset, double tile, int64_t n_fp,
                             const float* xy, const float* t, const float* t_dst, double t_dst_s, const int64_t* b,
                             int64_t N, float* gcoeff, float* gp, atlb_stream_t stream);
+
+/* ----------------------------------------------------------------------------------------------
+ * AnchoredSliced per-anchor score (atl/objectives/ats.py:154-169; the leave-one-out terms of
+ * ats.py:186-200 and atl/objectives/cmax.py:125-137), all anchors of all slices in one call.
+ * pos (N, P, 2): per anchor P transported positions at its slice centre; slot ia = the smoothed anchor
+ * position a, slot io = the unsmoothed (source) position (io < 0: self term at a), slots ip..ip+3 = the
+ * transports of x +- delta e_x, x +- delta e_y (ip < 0: no log-determinant).  val (N) density gathered at a,
+ * cnt (N) sources of the anchor's slice and batch minus src, vis (N) exposure correction (NULL: none),
+ * src (N) 1 / 0 = the anchor is / is not a source of its slice.  Image W x H, Gaussian sigma, eps.
+ *   ls = log(eps + max(val - src loo, 0) / max(cnt vis, 1)) + log(max(|det J|, 1e-12))
+ * The backward writes gval (N) = dL/dval and gpos (N, P, 2) = dL/dpos for gls = dL/dls.
+ * ---------------------------------------------------------------------------------------------- */
+int atlb_sliced_score(int64_t N, int P, int ia, int io, int ip, const float* pos, const float* val, const float* cnt,
+                      const float* vis, const float* src, double sigma, double delta, double eps, int64_t H,
+                      int64_t W, float* ls, atlb_stream_t stream);
+int atlb_sliced_score_bwd(int64_t N, int P, int ia, int io, int ip, const float* gls, const float* pos,
+                          const float* val, const float* cnt, const float* vis, const float* src, double sigma,
+                          double delta, double eps, int64_t H, int64_t W, float* gval, float* gpos,
+                          atlb_stream_t stream);
 
 /* ----------------------------------------------------------------------------------------------
  * Fused anchored score: AnchoredExact.log_scores (atl/objectives/ats.py:75-96) for the motion kinds

@@ -194,9 +194,12 @@ def gen_exact(kind, n, B, H, W, seed, n_anchors, h=1.0, tau=1.0, S=16, visibilit
          loss=out["loss"].detach(), grad_theta=m.theta.grad)
 
 
-def gen_sliced(name, kind, n, B, H, W, seed, S, sigma, K=3):
+def gen_sliced(name, kind, n, B, H, W, seed, S, sigma, K=3, masks=False, **obj_kw):
     """AnchoredSliced (ats.py:108-183) on a seeded window: per-anchor log scores, loss and the gradient of
-    the loss w.r.t. the motion parameters (a PixelTrajectories coefficient grid, or theta / flow grid)."""
+    the loss w.r.t. the motion parameters (a PixelTrajectories coefficient grid, or theta / flow grid).
+    ``obj_kw``: further constructor options (slices_per_step, n_anchors_per_slice, tau, smooth_anchors,
+    dequantize, logdet, visibility); ``masks``: seeded held-out anchor / source masks (the split of
+    heldout_score, ats.py:204-213)."""
     xy, t, b = synth_window(n, H, W, seed, B)
     ev = EventPacket(xy, t, torch.ones(n), b, B, H, W)
     g = torch.Generator().manual_seed(seed + 1)
@@ -204,21 +207,23 @@ def gen_sliced(name, kind, n, B, H, W, seed, S, sigma, K=3):
         coeff = torch.nn.functional.avg_pool2d(torch.randn(B, 2 * K, H, W, generator=g), 9, 1, 4) * 12
         coeff.requires_grad_(True)
         m, param = PixelTrajectories(coeff, K, basis_kind="bezier", tile=4), coeff
-    elif kind == "affine_exact":
+    elif kind in ("affine_exact", "affine_linear"):
         th = torch.cat([(torch.rand(B, 2, generator=g) - 0.5) * 20, (torch.rand(B, 4, generator=g) - 0.5) * 0.1], 1)
-        m = Affine(B, H, W, mode="exact", init=th)
+        m = Affine(B, H, W, mode="exact" if kind == "affine_exact" else "linear", init=th)
         param = m.theta
     else:
         grid = torch.nn.functional.avg_pool2d(torch.randn(B, 2, H, W, generator=g), 7, 1, 3) * 30
         m = DenseLinearFlow(B, H, W, grid=(H, W), mode="linear", init=grid)
         param = m.grid
     init = param.detach().clone()
-    obj = ATS.AnchoredSliced(n_slices=S, sigma=sigma, seed=seed + 2)
-    ls, idx = obj.log_scores(ev, m)
+    obj = ATS.AnchoredSliced(n_slices=S, sigma=sigma, seed=seed + 2, **obj_kw)
+    held = torch.rand(n, generator=torch.Generator().manual_seed(seed + 3)) < 0.3 if masks else None
+    ls, idx = obj.log_scores(ev, m, anchor_mask=held, source_mask=None if held is None else ~held)
     loss = -ls.mean()
     loss.backward()
+    extra = {"held": held} if masks else {}
     save(name, kind=kind, xy=xy, t=t, b=b, B=B, H=H, W=W, S=S, sigma=sigma, K=K, seed=seed + 2, param=init,
-         ls=ls.detach(), idx=idx, loss=loss.detach(), grad=param.grad)
+         ls=ls.detach(), idx=idx, loss=loss.detach(), grad=param.grad, obj_kw=repr(obj_kw), **extra)
 
 
 class _MatrixExpF64:
@@ -289,6 +294,11 @@ if __name__ == "__main__":
     gen_sliced("sliced_trajectories", "trajectories", 3000, 2, 48, 64, 70, 4, 1.5)
     gen_sliced("sliced_affine_exact", "affine_exact", 3000, 1, 48, 64, 80, 5, 1.0)
     gen_sliced("sliced_dense", "dense", 3000, 1, 48, 64, 90, 4, 2.0)
+    gen_sliced("sliced_traj_subsets", "trajectories", 3000, 2, 48, 64, 71, 6, 1.5, slices_per_step=4,
+               n_anchors_per_slice=150, tau=0.3)
+    gen_sliced("sliced_affine_plain", "affine_linear", 3000, 1, 48, 64, 81, 5, 1.0, smooth_anchors=False,
+               logdet=False, dequantize=False, visibility=False)
+    gen_sliced("sliced_dense_heldout", "dense", 3000, 2, 48, 64, 91, 4, 1.0, masks=True, tau=0.5)
     gen_traj("traj_k10_bezier", 10, "bezier", False, 101)
     gen_traj("traj_k3_poly_pe", 3, "polynomial", True, 102)
     gen_traj("traj_k1_poly", 1, "polynomial", False, 103)

@@ -3,6 +3,7 @@ against the reference's own outputs on identical seeded inputs (tests/golden/sli
 continuous-time Bezier PixelTrajectories of configuration 3, the exact (matrix-exponential) Affine flow
 and a linear dense flow.  Both sides draw the dequantisation / smoothing noise from the same seeded CPU
 generator, so the per-anchor scores compare one to one."""
+import ast
 import math
 
 import numpy as np
@@ -29,8 +30,12 @@ def np_(t):
 # (tests/golden/gen_golden.py); sliced_affine_exact: as the reference runs, with its fp32 matrix_exp, whose
 # own error (up to ~1e-4 px here) moves the reference's scores by up to 2.4e-4 and its gradient by 1.9e-4
 # norm-wise (measured between the two goldens, both made by the reference)
+# sliced_traj_subsets: slices_per_step, n_anchors_per_slice and tau < 1 (sources a subset of the window);
+# sliced_affine_plain: no smoothing (self term), no log-determinant, no jitter, no exposure correction;
+# sliced_dense_heldout: the held-out split of heldout_score (anchor and source masks, ats.py:204-213)
 @pytest.mark.parametrize("name", ["sliced_trajectories", "sliced_affine_exact_f64exp", "sliced_affine_exact",
-                                  "sliced_dense"])
+                                  "sliced_dense", "sliced_traj_subsets", "sliced_affine_plain",
+                                  "sliced_dense_heldout"])
 def test_anchored_sliced_vs_reference(name):
     from x_b200 import motion as Mo
     from x_b200.events import EventPacket
@@ -41,16 +46,18 @@ def test_anchored_sliced_vs_reference(name):
     if kind == "trajectories":
         param = T(g["param"]).requires_grad_(True)
         m = Mo.PixelTrajectories(param, int(g["K"]), basis_kind="bezier", tile=4)
-    elif kind == "affine_exact":
-        m = Mo.Affine(B, H, W, mode="exact", init=T(g["param"])).to(DEV)
+    elif kind in ("affine_exact", "affine_linear"):
+        m = Mo.Affine(B, H, W, mode="exact" if kind == "affine_exact" else "linear", init=T(g["param"])).to(DEV)
         param = m.theta
     else:
         m = Mo.DenseLinearFlow(B, H, W, grid=(H, W), mode="linear", init=T(g["param"])).to(DEV)
         param = m.grid
     n = g["t"].shape[0]
     ev = EventPacket(T(g["xy"]), T(g["t"]), torch.ones(n, device=DEV), T(g["b"]), B, H, W)
-    obj = AnchoredSliced(n_slices=int(g["S"]), sigma=float(g["sigma"]), seed=int(g["seed"]))
-    ls, idx = obj.log_scores(ev, m)
+    kw = ast.literal_eval(str(g["obj_kw"])) if "obj_kw" in g else {}
+    obj = AnchoredSliced(n_slices=int(g["S"]), sigma=float(g["sigma"]), seed=int(g["seed"]), **kw)
+    held = T(g["held"]) if "held" in g else None
+    ls, idx = obj.log_scores(ev, m, anchor_mask=held, source_mask=None if held is None else ~held)
     np.testing.assert_array_equal(np_(idx), g["idx"])
     # splat sums in another order and with separable exponentials: scores within 1e-5
     fp32_exp = name == "sliced_affine_exact"

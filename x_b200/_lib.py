@@ -49,6 +49,10 @@ _SIGS = {
     "atlb_abi_version": (_int, []),
     "atlb_tile_ops_workspace_bytes": (_size, [_i64, _i64, _i64, _i64]),
     "atlb_blur": (_int, [_vp, _i64, _i64, _i64, _dbl, _vp, _vp]),
+    "atlb_sliced_score": (_int, [_i64, _int, _int, _int, _int, _vp, _vp, _vp, _vp, _vp, _dbl, _dbl, _dbl, _i64, _i64,
+                                 _vp, _vp]),
+    "atlb_sliced_score_bwd": (_int, [_i64, _int, _int, _int, _int, _vp, _vp, _vp, _vp, _vp, _vp, _dbl, _dbl, _dbl,
+                                     _i64, _i64, _vp, _vp, _vp]),
     "atlb_flow_exact": (_int, [_int, _vp, _i64, _i64, _i64, _vp, _vp, _vp, _dbl, _vp, _i64, _vp, _vp]),
     "atlb_flow_exact_bwd": (_int, [_int, _vp, _vp, _i64, _i64, _i64, _vp, _vp, _vp, _dbl, _vp, _i64, _vp, _vp, _vp]),
     "atlb_rng_uniform2": (_int, [ctypes.c_uint64, ctypes.c_uint64, _i64, _vp, _vp]),

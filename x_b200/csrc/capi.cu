@@ -63,6 +63,11 @@ int splat_bilinear_fwd(const float*, const float*, const long long*, long long, 
 int splat_bilinear_bwd(const float*, const float*, const float*, const long long*, long long, long long, long long,
                        long long, float*, float*, void*, cudaStream_t);
 int blur(const float*, long long, long long, long long, double, float*, cudaStream_t);
+int sliced_score(long long, int, int, int, int, const float*, const float*, const float*, const float*, const float*,
+                 double, double, double, long long, long long, float*, cudaStream_t);
+int sliced_score_bwd(long long, int, int, int, int, const float*, const float*, const float*, const float*,
+                     const float*, const float*, double, double, double, long long, long long, float*, float*,
+                     cudaStream_t);
 size_t splat_gauss_workspace_bytes(long long N, long long B, long long H, long long W);
 int splat_gauss_fwd(const float*, const float*, const long long*, long long, long long, long long, long long, double,
                     long long, float*, void*, cudaStream_t);
@@ -640,4 +645,37 @@ int atlb_traj_visible_fraction(const float* coeff, int64_t B, int64_t Hq, int64_
   if (int st = make_traj(coeff, B, Hq, Wq, K, basis, bezier_c, offset, tile, n_fp, &V, __func__)) return st;
   return traj_visible_fraction(V, xa, ta, LL(ba), M, counts, centres, (int)n_check, (float)tau, (float)(W - 1),
                                (float)(H - 1), out, STREAM(stream));
+}
+
+static int check_score(int64_t N, int P, int ia, int io, int ip, double sigma, double delta, int64_t H, int64_t W,
+                       const char* fn) {
+  const bool slot_ok = P >= 1 && P <= 16 && ia >= 0 && ia < P && io < P && (ip < 0 || ip + 4 <= P);
+  if (!slot_ok || !(sigma > 0) || !(delta > 0) || H < 1 || W < 1 || N > (1LL << 40)) {
+    set_error("%s: P %d, slots a %d own %d probes %d, sigma %g, delta %g, image %lld x %lld", fn, P, ia, io, ip,
+              sigma, delta, (long long)W, (long long)H);
+    return ATLB_ERR_ARG;
+  }
+  return ATLB_OK;
+}
+
+int atlb_sliced_score(int64_t N, int P, int ia, int io, int ip, const float* pos, const float* val, const float* cnt,
+                      const float* vis, const float* src, double sigma, double delta, double eps, int64_t H,
+                      int64_t W, float* ls, atlb_stream_t stream) {
+  clear();
+  NONNEG(N);
+  if (int st = check_score(N, P, ia, io, ip, sigma, delta, H, W, __func__)) return st;
+  NEED(pos, N); NEED(val, N); NEED(cnt, N); NEED(src, N); NEED(ls, N);
+  return sliced_score(N, P, ia, io, ip, pos, val, cnt, vis, src, sigma, delta, eps, H, W, ls, STREAM(stream));
+}
+
+int atlb_sliced_score_bwd(int64_t N, int P, int ia, int io, int ip, const float* gls, const float* pos,
+                          const float* val, const float* cnt, const float* vis, const float* src, double sigma,
+                          double delta, double eps, int64_t H, int64_t W, float* gval, float* gpos,
+                          atlb_stream_t stream) {
+  clear();
+  NONNEG(N);
+  if (int st = check_score(N, P, ia, io, ip, sigma, delta, H, W, __func__)) return st;
+  NEED(gls, N); NEED(pos, N); NEED(val, N); NEED(cnt, N); NEED(src, N); NEED(gval, N); NEED(gpos, N);
+  return sliced_score_bwd(N, P, ia, io, ip, gls, pos, val, cnt, vis, src, sigma, delta, eps, H, W, gval, gpos,
+                          STREAM(stream));
 }

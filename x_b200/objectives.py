@@ -242,6 +242,40 @@ class AnchoredExact(Objective):
         return {"loss": -s, "score": s.detach()}
 
 
+class _SlicedScore(torch.autograd.Function):
+    """AnchoredSliced's per-anchor score from the transported anchor records (atlb_sliced_score / _bwd):
+    ls = log(eps + max(val - src loo(a, own), 0) / max(cnt vis, 1)) + log|det J| (ats.py:154-169),
+    differentiable w.r.t. the records ``pos`` (N, P, 2) and the gathered density ``val``."""
+
+    @staticmethod
+    def forward(ctx, pos, val, cnt, vis, src, slots, sigma, delta, eps, H, W):
+        P, ia, io, ip = slots
+        posc, valc = pos.detach().float().contiguous(), val.detach().float().contiguous()
+        cntc, srcc = cnt.float().contiguous(), src.float().contiguous()
+        visc = None if vis is None else vis.float().contiguous()
+        n = valc.shape[0]
+        ls = torch.empty(n, dtype=torch.float32, device=valc.device)
+        L.check(L.lib().atlb_sliced_score(n, P, ia, io, ip, L.ptr(posc), L.ptr(valc), L.ptr(cntc), L.ptr(visc),
+                                          L.ptr(srcc), float(sigma), float(delta), float(eps), H, W, L.ptr(ls),
+                                          L.stream()), "sliced_score")
+        ctx.save_for_backward(posc, valc, cntc, srcc, *(() if visc is None else (visc,)))
+        ctx.meta = (slots, float(sigma), float(delta), float(eps), H, W, pos.dtype, val.dtype)
+        return ls.to(val.dtype)
+
+    @staticmethod
+    def backward(ctx, gls):
+        posc, valc, cntc, srcc, *rest = ctx.saved_tensors
+        visc = rest[0] if rest else None
+        (P, ia, io, ip), sigma, delta, eps, H, W, pdt, vdt = ctx.meta
+        n = valc.shape[0]
+        gval = torch.empty_like(valc)
+        gpos = torch.empty_like(posc)
+        L.check(L.lib().atlb_sliced_score_bwd(n, P, ia, io, ip, L.ptr(gls.contiguous().float()), L.ptr(posc),
+                                              L.ptr(valc), L.ptr(cntc), L.ptr(visc), L.ptr(srcc), sigma, delta, eps,
+                                              H, W, L.ptr(gval), L.ptr(gpos), L.stream()), "sliced_score_bwd")
+        return gpos.to(pdt), gval.to(vdt), None, None, None, None, None, None, None, None, None
+
+
 class AnchoredSliced(Objective):
     """Anchored transport score for any motion model (ats.py:108-183): Gaussian splats at slice centres,
     anchors moved by the small step t_i -> c_s with the exact finite-difference log|det|."""
@@ -278,71 +312,112 @@ class AnchoredSliced(Objective):
     def log_scores(self, ev: EventPacket, motion, anchor_mask: Optional[torch.Tensor] = None,
                    source_mask: Optional[torch.Tensor] = None, noise=None):
         """Per-anchor log scores and anchor indices (ats.py:122-174).  ``noise`` = :meth:`draw`'s
-        (slices, u, z) replaces the generator draws."""
-        S, dev = self.S, ev.device
+        (slices, u, z) replaces the generator draws.
+
+        All slices are evaluated at once: one transport of every (source, slice) pair into a stack of
+        len(slices) x B density images (one splat), one transport of every anchor's record (its position,
+        the four log-determinant probes and its unsmoothed source copy) to its own slice centre, one gather
+        and the fused per-anchor score kernel (atlb_sliced_score).  Anchors come out in the reference's
+        order: slice by slice in ``slices`` order, ascending event index inside a slice (or the slice's
+        random subset when n_anchors_per_slice is set, drawn as the reference draws it)."""
+        S, dev, B = self.S, ev.device, ev.batch_size
         delta = 1.0 / S
-        sl = torch.clamp(torch.floor(ev.t / delta), 0, S - 1).long()
         slices, u, z = self.draw(ev) if noise is None else noise
         eps = self.eps_frac / (ev.height * ev.width)
         xs = ev.xy
         if self.dequantize:
             xs = xs + (u - 0.5)
         xsm = xs + self.sigma * z if self.smooth_anchors else xs
-        out, idx_all = [], []
-        counts = slice_counts(ev) if self.visibility else None  # the same for every slice
-        bounds = _batch_bounds(ev)  # None unless the events are sorted by batch
-        # trajectories: every source's origin is solved once for all slices (it does not depend on the slice)
-        p_src = None
-        if source_mask is None and hasattr(motion, "from_origin") and motion._device_transport(xs, ev.t):
-            p_src = motion.origin_on_device(xs, ev.t, ev.b)
-        for s in slices:
-            c = (s + 0.5) * delta
-            src = (ev.t - c).abs() <= self.tau + delta / 2
-            if source_mask is not None:
-                src = src & source_mask
-            anc = sl == s
-            if anchor_mask is not None:
-                anc = anc & anchor_mask
-            ai = torch.nonzero(anc).squeeze(1)
+        Sp = len(slices)
+        # slice of each event, floor(t / delta) divided (not multiplied by a reciprocal) as the CPU reference
+        sl = torch.clamp(torch.floor(ev.t / torch.tensor(delta, dtype=ev.t.dtype, device=dev)), 0, S - 1).long()
+        rank_of = torch.full((S,), Sp, dtype=torch.long)
+        rank_of[torch.tensor(slices, dtype=torch.long)] = torch.arange(Sp)
+        rank = rank_of.to(dev)[sl]  # position of the event's slice in `slices` (Sp: not evaluated)
+        if anchor_mask is not None:
+            rank = torch.where(anchor_mask, rank, torch.full_like(rank, Sp))
+        centres = torch.tensor([(s + 0.5) * delta for s in slices], dtype=ev.t.dtype).to(dev)
+        src = (ev.t[None, :] - centres[:, None]).abs() <= torch.tensor(self.tau + delta / 2, dtype=ev.t.dtype,
+                                                                       device=dev)
+        if source_mask is not None:
+            src = src & source_mask[None, :]
+        # the one read-back of the step: anchors per slice and the number of (source, slice) pairs
+        stats = torch.cat([torch.bincount(rank, minlength=Sp + 1)[:Sp], src.sum().view(1)]).tolist()
+        n_anc, n_pairs = stats[:Sp], stats[Sp]
+        rank_sorted, order = torch.sort(rank, stable=True)
+        pieces, ranks, off = [], [], 0
+        for k in range(Sp):
+            ai = order[off:off + n_anc[k]]
+            off += n_anc[k]
             if ai.numel() == 0:
                 continue
             if self.nap is not None and ai.numel() > self.nap:
                 ai = ai[torch.randperm(ai.numel(), generator=self.gen)[: self.nap].to(dev)]
-            si = torch.nonzero(src).squeeze(1)
-            all_src = si.numel() == ev.n  # every event is a source: no gathers
-            xs_s, t_s, b_s = (xs, ev.t, ev.b) if all_src else (xs[si], ev.t[si], ev.b[si])
-            if p_src is not None:
-                y = motion.from_origin(p_src if all_src else p_src[si], t_s, c, b_s)
-            else:
-                y = motion.transport(xs_s, t_s, c, b_s)
-            img = splat(y, torch.ones_like(t_s), b_s, ev.batch_size, ev.height, ev.width,
-                        kernel="gauss", sigma=self.sigma)
-            if self.logdet:
-                a, ld = motion.transport_logdet(xsm[ai], ev.t[ai], c, ev.b[ai])
-            else:
-                a, ld = motion.transport(xsm[ai], ev.t[ai], c, ev.b[ai]), 0.0
-            val = gather(img, a, ev.b[ai])
-            if self.smooth_anchors:
-                y_own = motion.transport(xs[ai], ev.t[ai], c, ev.b[ai])
-                own = src[ai].to(val.dtype) * _cross_term(a, y_own, self.sigma, ev.height, ev.width)
-            else:
-                own = src[ai].to(val.dtype) * _self_term(a, self.sigma, ev.height, ev.width)
-            if bounds is not None:  # per-batch source counts from a prefix sum at the batch bounds (exact)
-                cs = torch.nn.functional.pad(torch.cumsum(src, 0), (1, 0))
-                per_b = cs[bounds[1:]] - cs[bounds[:-1]]
-            else:
-                per_b = torch.bincount(b_s, minlength=ev.batch_size)
-            nsrc = per_b.to(val.dtype)[ev.b[ai]] - src[ai].to(val.dtype)
-            if self.visibility:
-                nsrc = nsrc * visible_fraction(motion, xsm[ai].detach(), ev.t[ai], ev.b[ai], ev, self.tau,
-                                               counts=counts)
-            rho = (val - own).clamp(min=0) / nsrc.clamp(min=1)
-            out.append(torch.log(eps + rho) + ld)
-            idx_all.append(ai)
-        if not out:
-            z = ev.t.new_zeros(0)
-            return z, z.long()
-        return torch.cat(out), torch.cat(idx_all)
+            pieces.append(ai)
+            ranks.append(k)
+        if not pieces:
+            z0 = ev.t.new_zeros(0)
+            return z0, z0.long()
+        if self.nap is None:
+            ai = order[:off]
+            ka = rank_sorted[:off]
+        else:
+            ai = torch.cat(pieces)
+            ka = torch.cat([torch.full((p.numel(),), k, dtype=torch.long, device=dev) for p, k in zip(pieces, ranks)])
+
+        # sources of every slice, transported to its centre and splatted into image k * B + b
+        if n_pairs == Sp * ev.n:
+            ks = torch.arange(Sp, device=dev).repeat_interleave(ev.n)
+            js = torch.arange(ev.n, device=dev).repeat(Sp)
+        else:
+            flat = torch.nonzero(src.reshape(-1)).squeeze(1)
+            ks, js = flat // ev.n, flat % ev.n
+        y = self._sources_at_centres(motion, xs, ev, js, centres[ks])
+        img = splat(y, torch.ones_like(y[:, 0]), ks * B + ev.b[js], Sp * B, ev.height, ev.width,
+                    kernel="gauss", sigma=self.sigma)
+
+        # anchor records at their slice centres: [x +- d e_x, x +- d e_y,] a [, unsmoothed copy]
+        xa, ta, ba, ca = xsm[ai], ev.t[ai], ev.b[ai], centres[ka]
+        recs = []
+        if self.logdet:
+            d = 0.5  # Motion.transport_logdet's default step (atl/motion/base.py:43)
+            ex, ey = xa.new_tensor([d, 0.0]), xa.new_tensor([0.0, d])
+            recs += [xa + ex, xa - ex, xa + ey, xa - ey]
+        ia = len(recs)
+        recs.append(xa)
+        io = -1
+        if self.smooth_anchors:
+            io = len(recs)
+            recs.append(xs[ai])
+        P = len(recs)
+        rec = torch.stack(recs, 1).reshape(-1, 2)
+        pos = motion.transport(rec, ta.repeat_interleave(P), ca.repeat_interleave(P),
+                               ba.repeat_interleave(P)).reshape(-1, P, 2)
+        img_a = ka * B + ba
+        val = gather(img, pos[:, ia], img_a)
+        src_a = src[ka, ai].to(val.dtype)
+        per_kb = torch.bincount(ks * B + ev.b[js], minlength=Sp * B).to(val.dtype)
+        cnt = per_kb[img_a] - src_a
+        vis = None
+        if self.visibility:
+            vis = visible_fraction(motion, xa.detach(), ta, ba, ev, self.tau, counts=slice_counts(ev))
+        ls = _SlicedScore.apply(pos, val, cnt, vis, src_a, (P, ia, io, 0 if self.logdet else -1), self.sigma,
+                                0.5, eps, ev.height, ev.width)
+        return ls, ai
+
+    @staticmethod
+    def _sources_at_centres(motion, xs, ev: EventPacket, js, cen):
+        """Positions at the centres ``cen`` of the sources ``js`` (one entry per (source, slice) pair):
+        trajectories solve each event's origin once and move it to every centre; linear vector fields
+        evaluate each velocity once (x + v (c - t), the reference's warp); other models transport each pair."""
+        t, b = ev.t, ev.b
+        if hasattr(motion, "from_origin") and motion._device_transport(xs, t):
+            p = motion.origin_on_device(xs, t, b)
+            return motion.from_origin(p[js], t[js], cen, b[js])
+        if _fused_kind(motion) >= 0:
+            v = motion.velocity(xs, t, b)
+            return xs[js] + v[js] * (cen - t[js])[:, None]
+        return motion.transport(xs[js], t[js], cen, b[js])
 
     def set_bandwidth(self, h: float):
         self.sigma = float(h)
@@ -351,47 +426,6 @@ class AnchoredSliced(Objective):
         ls, _ = self.log_scores(ev, motion, noise=noise)
         s = ls.mean() if ls.numel() else ev.t.new_zeros(())
         return {"loss": -s, "score": s.detach()}
-
-
-def _cross_term(a: torch.Tensor, y: torch.Tensor, sigma: float, H: int, W: int) -> torch.Tensor:
-    """Bilinear look-up at ``a`` of the truncated Gaussian splat centred at ``y`` (ats.py:186-200)."""
-    R = int(math.ceil(3 * sigma))
-    cy0, cx0 = torch.round(y[:, 1]), torch.round(y[:, 0])
-    x0, y0 = torch.floor(a[:, 0]), torch.floor(a[:, 1])
-    ax, ay = a[:, 0] - x0, a[:, 1] - y0
-    s = torch.zeros_like(ax)
-    norm = 1.0 / (2 * math.pi * sigma * sigma)
-    for dy, wy in ((0, 1 - ay), (1, ay)):
-        for dx, wx in ((0, 1 - ax), (1, ax)):
-            px, py = x0 + dx, y0 + dy
-            ok = ((px >= 0) & (px < W) & (py >= 0) & (py < H) & ((px - cx0).abs() <= R) & ((py - cy0).abs() <= R))
-            d2 = (px - y[:, 0]) ** 2 + (py - y[:, 1]) ** 2
-            s = s + wx * wy * ok.to(a.dtype) * norm * torch.exp(-d2 / (2 * sigma * sigma))
-    return s
-
-
-def _batch_bounds(ev: EventPacket) -> Optional[torch.Tensor]:
-    """First event of each batch and the end (B + 1) for batch-sorted events (the EventPacket invariant),
-    else None."""
-    b = ev.b
-    if b.numel() > 1 and not bool((b[1:] >= b[:-1]).all()):
-        return None
-    return torch.searchsorted(b, torch.arange(ev.batch_size + 1, device=b.device, dtype=b.dtype))
-
-
-def _self_term(y: torch.Tensor, sigma: float, H: int, W: int) -> torch.Tensor:
-    """Own Gaussian splat seen by the bilinear look-up at its own position (atl/objectives/cmax.py:125-137)."""
-    x0, y0 = torch.floor(y[:, 0]), torch.floor(y[:, 1])
-    ax, ay = y[:, 0] - x0, y[:, 1] - y0
-    s = torch.zeros_like(ax)
-    norm = 1.0 / (2 * math.pi * sigma * sigma)
-    for dy, wy in ((0, 1 - ay), (1, ay)):
-        for dx, wx in ((0, 1 - ax), (1, ax)):
-            cx, cy = x0 + dx, y0 + dy
-            inside = ((cx >= 0) & (cx < W) & (cy >= 0) & (cy < H)).to(y.dtype)
-            d2 = (cx - y[:, 0]) ** 2 + (cy - y[:, 1]) ** 2
-            s = s + wx * wy * inside * norm * torch.exp(-d2 / (2 * sigma * sigma))
-    return s
 
 
 def build(name: str, **kw) -> Objective:
