@@ -774,7 +774,8 @@ def config3_arm(args):
     torch.cuda.synchronize()
     L = _lib.load_library()
     L.atlb_timing_enable(1)
-    names = ("k_gsplat_fwd", "k_gsplat_bwd", "k_traj_fwd", "k_traj_bwd")
+    names = ("k_gsplat_fwd", "k_gsplat_bwd", "k_traj_fwd", "k_traj_bwd", "k_traj_records_fwd", "k_traj_records_bwd",
+             "k_traj_targets_fwd", "k_traj_targets_bwd", "k_traj_vis")
     for k in names:
         _lib.timing_read(k, reset=True)
     s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)

@@ -94,6 +94,12 @@ int atlb_splat_gauss_fwd(const float* pos, const float* w, const int64_t* bidx, 
 int atlb_splat_gauss_bwd(const float* gimg, const float* pos, const float* w, const int64_t* bidx, int64_t N,
                          int64_t B, int64_t H, int64_t W, double sigma, int64_t radius, float* gpos, float* gw,
                          void* workspace, size_t workspace_bytes, atlb_stream_t stream);
+/* Backward w.r.t. the positions only (gpos (N,2)), over the buckets that the preceding atlb_splat_gauss_fwd
+ * of the same (pos, w, bidx, B, H, W, R) left in `workspace`, which the caller keeps unchanged in between:
+ * the forward's bucketing is reused instead of redone.  Events the forward skipped (zero weight) get 0. */
+int atlb_splat_gauss_bwd_pos(const float* gimg, const float* w, int64_t N, int64_t B, int64_t H, int64_t W,
+                             double sigma, int64_t R, float* gpos, void* workspace, size_t workspace_bytes,
+                             atlb_stream_t stream);
 int atlb_gather_bilinear_fwd(const float* img, const float* pos, const int64_t* bidx, int64_t N, int64_t B, int64_t H,
                              int64_t W, float* out, void* workspace, size_t workspace_bytes, atlb_stream_t stream);
 int atlb_gather_bilinear_bwd(const float* gval, const float* img, const float* pos, const int64_t* bidx, int64_t N,
@@ -246,6 +252,31 @@ int atlb_traj_transport_bwd(int mode, const float* gy, const float* coeff, int64
                             int64_t K, int basis, const float* bezier_c, double offset, double tile, int64_t n_fp,
                             const float* xy, const float* t, const float* t_dst, double t_dst_s, const int64_t* b,
                             int64_t N, float* gcoeff, float* gp, atlb_stream_t stream);
+/* Records: xy (N, R, 2) holds R positions per event, all at the event's time t; each is moved to the event's
+ * target time (t_dst (N), or t_dst_s when t_dst is NULL) exactly as mode 0 moves it: out (N, R, 2).  The
+ * transports of an anchor and of its finite-difference probes (atl/motion/base.py:43-50) in one call.
+ * iterates (optional, NULL: none) receives the fixed-point iterates, (n_fp, N, R, 2).  The backward ADDS
+ * dL/dcoeff for gy (N, R, 2) into gcoeff; given the forward's iterates it reads them instead of solving
+ * the fixed points again. */
+int atlb_traj_records(const float* coeff, int64_t B, int64_t Hq, int64_t Wq, int64_t K, int basis,
+                      const float* bezier_c, double offset, double tile, int64_t n_fp, const float* xy, int64_t R,
+                      const float* t, const float* t_dst, double t_dst_s, const int64_t* b, int64_t N, float* out,
+                      float* iterates, atlb_stream_t stream);
+int atlb_traj_records_bwd(const float* gy, const float* coeff, int64_t B, int64_t Hq, int64_t Wq, int64_t K,
+                          int basis, const float* bezier_c, double offset, double tile, int64_t n_fp, const float* xy,
+                          int64_t R, const float* t, const float* t_dst, double t_dst_s, const int64_t* b, int64_t N,
+                          const float* iterates, float* gcoeff, atlb_stream_t stream);
+/* Targets: every event (xy (N,2), t) moved to each of T target times (targets, a device array, T <= 64):
+ * out (T, N, 2), entry (j, n) exactly as mode 0 moves event n to targets[j] (the transports of every source
+ * to every slice centre, atl/objectives/ats.py:141-147, with one origin solve per event).  The backward ADDS
+ * dL/dcoeff for gy (T, N, 2) into gcoeff. */
+int atlb_traj_targets(const float* coeff, int64_t B, int64_t Hq, int64_t Wq, int64_t K, int basis,
+                      const float* bezier_c, double offset, double tile, int64_t n_fp, const float* xy, const float* t,
+                      const int64_t* b, int64_t N, const float* targets, int64_t T, float* out, atlb_stream_t stream);
+int atlb_traj_targets_bwd(const float* gy, const float* coeff, int64_t B, int64_t Hq, int64_t Wq, int64_t K,
+                          int basis, const float* bezier_c, double offset, double tile, int64_t n_fp, const float* xy,
+                          const float* t, const int64_t* b, int64_t N, const float* targets, int64_t T, float* gcoeff,
+                          atlb_stream_t stream);
 
 /* ----------------------------------------------------------------------------------------------
  * AnchoredSliced per-anchor score (atl/objectives/ats.py:154-169; the leave-one-out terms of
@@ -258,6 +289,12 @@ int atlb_traj_transport_bwd(int mode, const float* gy, const float* coeff, int64
  *   ls = log(eps + max(val - src loo, 0) / max(cnt vis, 1)) + log(max(|det J|, 1e-12))
  * The backward writes gval (N) = dL/dval and gpos (N, P, 2) = dL/dpos for gls = dL/dls.
  * ---------------------------------------------------------------------------------------------- */
+/* Key counts: out (R, nbins) int64, out[r][k] = #{n < N : key[n] == k and (mask == NULL or
+ * mask[r * N + n] != 0)}; keys outside [0, nbins) are not counted; nbins * R <= 2^24.  The histograms of
+ * AnchoredSliced: anchors per slice, sources per slice and batch (R = slices, mask = source masks),
+ * events per exposure-check slice (ats.py:39-41). */
+int atlb_count_keys(const int64_t* key, int64_t N, int64_t nbins, const float* mask, int64_t R, int64_t* out,
+                    atlb_stream_t stream);
 int atlb_sliced_score(int64_t N, int P, int ia, int io, int ip, const float* pos, const float* val, const float* cnt,
                       const float* vis, const float* src, double sigma, double delta, double eps, int64_t H,
                       int64_t W, float* ls, atlb_stream_t stream);

@@ -77,3 +77,43 @@ def test_anchored_sliced_vs_reference(name):
     tol = 3e-4 if fp32_exp else 1e-5
     e = assert_grad_parity(np_(param.grad), g["grad"], rtol=tol, what=f"{name} parameter gradient")
     assert e["max_over_max"] <= tol, e
+
+
+def test_count_keys_matches_bincount():
+    """atlb_count_keys against torch.bincount: sorted and shuffled keys, keys outside [0, nbins), mask rows."""
+    from x_b200.objectives import count_keys
+    g = torch.Generator().manual_seed(21)
+    n, nbins, R = 300_000, 37, 5
+    key = torch.sort(torch.randint(-3, nbins + 3, (n,), generator=g)).values
+    mask = (torch.rand(R, n, generator=g) < 0.6).float()
+    for k in (key, key[torch.randperm(n, generator=g)]):
+        kc, mc = k.to(DEV), mask.to(DEV)
+        ok = (k >= 0) & (k < nbins)
+        ref = torch.bincount(k[ok], minlength=nbins)
+        assert torch.equal(count_keys(kc, nbins).cpu(), ref)
+        got = count_keys(kc, nbins, mc).cpu()
+        for r in range(R):
+            assert torch.equal(got[r], torch.bincount(k[ok], weights=mask[r][ok], minlength=nbins).long())
+    assert count_keys(torch.zeros(0, dtype=torch.long, device=DEV), 4).sum() == 0
+
+
+def test_splat_slices_matches_splat():
+    """The stacked splat of T point sets equals T separate splats, and its position gradient (reusing the
+    forward's buckets) equals theirs; zero weights add nothing and get zero gradient."""
+    from x_b200.functional import splat, splat_slices
+    g = torch.Generator().manual_seed(22)
+    T_, n, B, H, W, sigma = 3, 20000, 2, 40, 72, 1.5
+    pos = torch.stack([torch.rand(T_, n, generator=g) * (W + 10) - 5, torch.rand(T_, n, generator=g) * (H + 10) - 5],
+                      2).to(DEV)
+    w = (torch.rand(T_, n, generator=g) < 0.7).float().to(DEV)
+    b = torch.sort(torch.randint(0, B, (n,), generator=g)).values.to(DEV)
+    gimg = torch.randn(T_ * B, H, W, generator=g).to(DEV)
+    p1 = pos.clone().requires_grad_(True)
+    img1 = splat_slices(p1, w, b, B, H, W, sigma)
+    (img1 * gimg).sum().backward()
+    p2 = pos.clone().requires_grad_(True)
+    img2 = torch.cat([splat(p2[j], w[j], b, B, H, W, kernel="gauss", sigma=sigma) for j in range(T_)])
+    (img2 * gimg).sum().backward()
+    torch.testing.assert_close(img1, img2, rtol=1e-6, atol=1e-7)  # tile flushes add in any order
+    assert torch.equal(p1.grad, p2.grad)
+    assert bool((p1.grad[w == 0] == 0).all())

@@ -144,3 +144,43 @@ def test_traj_origin_then_from_origin_equals_transport():
     g1, g2 = c1.grad.cpu().numpy(), c2.grad.cpu().numpy()
     e = assert_grad_parity(g2, g1, what="coefficient gradient through origins")
     assert e["max_over_max"] <= 1e-5, e
+
+
+@pytest.mark.parametrize("K,basis", [(10, "bezier"), (3, "polynomial"), (1, "polynomial")])
+def test_traj_records_and_targets_equal_transport(K, basis):
+    """The batched transports of AnchoredSliced: records (R positions per event, one target time per event)
+    and targets (every event to each of T shared times) reproduce the per-position transport bit for bit,
+    and their coefficient gradients equal the per-position ones up to summation order.  Positions include
+    ones past the image border (clamped coefficient samples)."""
+    from x_b200.motion import PixelTrajectories
+    g = torch.Generator().manual_seed(6 + K)
+    B, H, W, n, R = 2, 48, 64, 8000, 6
+    coeff = (torch.nn.functional.avg_pool2d(torch.randn(B, 2 * K, H, W, generator=g), 9, 1, 4) * 8).cuda()
+    xy = torch.stack([torch.rand(n, R, generator=g) * (W + 8) - 4, torch.rand(n, R, generator=g) * (H + 8) - 4],
+                     2).cuda()
+    t = torch.rand(n, generator=g).cuda()
+    td = torch.rand(n, generator=g).cuda()
+    b = torch.randint(0, B, (n,), generator=g).cuda()
+    targets = torch.tensor([0.05, 0.15, 0.35, 0.55, 0.75, 0.95]).cuda()
+    wr = torch.randn(n, R, 2, generator=g).cuda()
+    wt = torch.randn(targets.numel(), n, 2, generator=g).cuda()
+
+    def run(batched):
+        c = coeff.clone().requires_grad_(True)
+        m = PixelTrajectories(c, K, basis_kind=basis, tile=4)
+        if batched:
+            yr = m.transport_records(xy, t, td, b)
+            yt = m.transport_targets(xy[:, 0].contiguous(), t, targets, b)
+        else:
+            yr = m.transport(xy.reshape(-1, 2), t.repeat_interleave(R), td.repeat_interleave(R),
+                             b.repeat_interleave(R)).view(n, R, 2)
+            yt = torch.stack([m.transport(xy[:, 0].contiguous(), t, float(c_), b) for c_ in targets.tolist()])
+        ((yr * wr).sum() + (yt * wt).sum()).backward()
+        return yr.detach(), yt.detach(), c.grad.cpu().numpy()
+
+    yr1, yt1, g1 = run(False)
+    yr2, yt2, g2 = run(True)
+    assert torch.equal(yr1, yr2)
+    assert torch.equal(yt1, yt2)
+    e = assert_grad_parity(g2, g1, what=f"records / targets coefficient gradient (K={K})")
+    assert e["max_over_max"] <= 1e-5, e

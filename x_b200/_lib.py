@@ -49,6 +49,7 @@ _SIGS = {
     "atlb_abi_version": (_int, []),
     "atlb_tile_ops_workspace_bytes": (_size, [_i64, _i64, _i64, _i64]),
     "atlb_blur": (_int, [_vp, _i64, _i64, _i64, _dbl, _vp, _vp]),
+    "atlb_count_keys": (_int, [_vp, _i64, _i64, _vp, _i64, _vp, _vp]),
     "atlb_sliced_score": (_int, [_i64, _int, _int, _int, _int, _vp, _vp, _vp, _vp, _vp, _dbl, _dbl, _dbl, _i64, _i64,
                                  _vp, _vp]),
     "atlb_sliced_score_bwd": (_int, [_i64, _int, _int, _int, _int, _vp, _vp, _vp, _vp, _vp, _vp, _dbl, _dbl, _dbl,
@@ -68,6 +69,7 @@ _SIGS = {
     "atlb_splat_gauss_workspace_bytes": (_size, [_i64, _i64, _i64, _i64]),
     "atlb_splat_gauss_fwd": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _dbl, _i64, _vp, _vp, _size, _vp]),
     "atlb_splat_gauss_bwd": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _dbl, _i64, _vp, _vp, _vp, _size, _vp]),
+    "atlb_splat_gauss_bwd_pos": (_int, [_vp, _vp, _i64, _i64, _i64, _i64, _dbl, _i64, _vp, _vp, _size, _vp]),
     "atlb_gather_bilinear_fwd": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _vp, _size, _vp]),
     "atlb_gather_bilinear_bwd": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _size, _vp]),
     "atlb_voxel_grid": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _vp, _size, _vp]),
@@ -92,6 +94,14 @@ _SIGS = {
                                    _dbl, _vp, _i64, _vp, _vp]),
     "atlb_traj_transport_bwd": (_int, [_int, _vp, _vp, _i64, _i64, _i64, _i64, _int, _vp, _dbl, _dbl, _i64, _vp, _vp,
                                        _vp, _dbl, _vp, _i64, _vp, _vp, _vp]),
+    "atlb_traj_records": (_int, [_vp, _i64, _i64, _i64, _i64, _int, _vp, _dbl, _dbl, _i64, _vp, _i64, _vp, _vp, _dbl,
+                                 _vp, _i64, _vp, _vp, _vp]),
+    "atlb_traj_records_bwd": (_int, [_vp, _vp, _i64, _i64, _i64, _i64, _int, _vp, _dbl, _dbl, _i64, _vp, _i64, _vp,
+                                     _vp, _dbl, _vp, _i64, _vp, _vp, _vp]),
+    "atlb_traj_targets": (_int, [_vp, _i64, _i64, _i64, _i64, _int, _vp, _dbl, _dbl, _i64, _vp, _vp, _vp, _i64, _vp,
+                                 _i64, _vp, _vp]),
+    "atlb_traj_targets_bwd": (_int, [_vp, _vp, _i64, _i64, _i64, _i64, _int, _vp, _dbl, _dbl, _i64, _vp, _vp, _vp,
+                                     _i64, _vp, _i64, _vp, _vp]),
     "atlb_traj_visible_fraction": (_int, [_vp, _i64, _i64, _i64, _i64, _int, _vp, _dbl, _dbl, _i64, _vp, _vp, _vp,
                                           _i64, _vp, _vp, _i64, _dbl, _i64, _i64, _vp, _vp]),
     "atlb_exact_prepare": (_int, [ctypes.POINTER(ExactCfg), _vp, _vp, _vp, _vp, _i64, _vp, _vp, _i64, _vp, _vp, _vp,

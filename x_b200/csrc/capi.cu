@@ -63,6 +63,7 @@ int splat_bilinear_fwd(const float*, const float*, const long long*, long long, 
 int splat_bilinear_bwd(const float*, const float*, const float*, const long long*, long long, long long, long long,
                        long long, float*, float*, void*, cudaStream_t);
 int blur(const float*, long long, long long, long long, double, float*, cudaStream_t);
+int count_keys(const long long*, long long, long long, const float*, long long, long long*, cudaStream_t);
 int sliced_score(long long, int, int, int, int, const float*, const float*, const float*, const float*, const float*,
                  double, double, double, long long, long long, float*, cudaStream_t);
 int sliced_score_bwd(long long, int, int, int, int, const float*, const float*, const float*, const float*,
@@ -73,6 +74,8 @@ int splat_gauss_fwd(const float*, const float*, const long long*, long long, lon
                     long long, float*, void*, cudaStream_t);
 int splat_gauss_bwd(const float*, const float*, const float*, const long long*, long long, long long, long long,
                     long long, double, long long, float*, float*, void*, cudaStream_t);
+int splat_gauss_bwd_pos(const float*, const float*, long long, long long, long long, long long, double, long long,
+                        float*, void*, cudaStream_t);
 int gather_fwd(const float*, const float*, const long long*, long long, long long, long long, long long, float*, void*,
                cudaStream_t);
 int gather_bwd(const float*, const float*, const float*, const long long*, long long, long long, long long, long long,
@@ -92,6 +95,15 @@ int traj_transport(const TrajView&, int, const float*, const float*, const float
                    long long, float*, cudaStream_t);
 int traj_transport_bwd(const TrajView&, int, const float*, const float*, const float*, const float*, float,
                        const long long*, long long, float*, float*, cudaStream_t);
+int traj_records(const TrajView&, int, const float*, const float*, const float*, float, const long long*, long long,
+                 float*, float*, cudaStream_t);
+int traj_records_bwd(const TrajView&, int, const float*, const float*, const float*, const float*, float,
+                     const long long*, long long, const float*, float*, cudaStream_t);
+int traj_targets(const TrajView&, const float*, const float*, const long long*, long long, const float*, int, float*,
+                 cudaStream_t);
+int traj_targets_bwd(const TrajView&, const float*, const float*, const float*, const long long*, long long,
+                     const float*, int, float*, cudaStream_t);
+int traj_targets_max();
 int traj_visible_fraction(const TrajView&, const float*, const float*, const long long*, long long, const float*,
                           const float*, int, float, float, float, float*, cudaStream_t);
 
@@ -285,6 +297,16 @@ int atlb_splat_gauss_bwd(const float* gimg, const float* pos, const float* w, co
   NEED(gimg, B * H * W); NEED(pos, N); NEED(w, N); NEED(bidx, N); NEED(gpos, N); NEED(gw, N);
   if (int st = check_gauss(N, B, H, W, radius, workspace, workspace_bytes, __func__)) return st;
   return splat_gauss_bwd(gimg, pos, w, LL(bidx), N, B, H, W, sigma, radius, gpos, gw, workspace, STREAM(stream));
+}
+
+int atlb_splat_gauss_bwd_pos(const float* gimg, const float* w, int64_t N, int64_t B, int64_t H, int64_t W,
+                             double sigma, int64_t R, float* gpos, void* workspace, size_t workspace_bytes,
+                             atlb_stream_t stream) {
+  clear();
+  NONNEG(N); NONNEG(B); NONNEG(H); NONNEG(W); NONNEG(R);
+  NEED(gimg, B * H * W); NEED(w, N); NEED(gpos, N);
+  if (int st = check_gauss(N, B, H, W, R, workspace, workspace_bytes, __func__)) return st;
+  return splat_gauss_bwd_pos(gimg, w, N, B, H, W, sigma, R, gpos, workspace, STREAM(stream));
 }
 
 int atlb_gather_bilinear_fwd(const float* img, const float* pos, const int64_t* bidx, int64_t N, int64_t B, int64_t H,
@@ -678,4 +700,77 @@ int atlb_sliced_score_bwd(int64_t N, int P, int ia, int io, int ip, const float*
   NEED(gls, N); NEED(pos, N); NEED(val, N); NEED(cnt, N); NEED(src, N); NEED(gval, N); NEED(gpos, N);
   return sliced_score_bwd(N, P, ia, io, ip, gls, pos, val, cnt, vis, src, sigma, delta, eps, H, W, gval, gpos,
                           STREAM(stream));
+}
+
+int atlb_traj_records(const float* coeff, int64_t B, int64_t Hq, int64_t Wq, int64_t K, int basis,
+                      const float* bezier_c, double offset, double tile, int64_t n_fp, const float* xy, int64_t R,
+                      const float* t, const float* t_dst, double t_dst_s, const int64_t* b, int64_t N, float* out,
+                      float* iterates, atlb_stream_t stream) {
+  clear();
+  NONNEG(N);
+  if (R < 1 || R > 64) { set_error("%s: R = %lld records per event", __func__, (long long)R); return ATLB_ERR_ARG; }
+  NEED(xy, N * R); NEED(t, N); NEED(b, N); NEED(out, N * R);
+  TrajView V;
+  if (int st = make_traj(coeff, B, Hq, Wq, K, basis, bezier_c, offset, tile, n_fp, &V, __func__)) return st;
+  return traj_records(V, (int)R, xy, t, t_dst, (float)t_dst_s, LL(b), N, out, iterates, STREAM(stream));
+}
+
+int atlb_traj_records_bwd(const float* gy, const float* coeff, int64_t B, int64_t Hq, int64_t Wq, int64_t K,
+                          int basis, const float* bezier_c, double offset, double tile, int64_t n_fp, const float* xy,
+                          int64_t R, const float* t, const float* t_dst, double t_dst_s, const int64_t* b, int64_t N,
+                          const float* iterates, float* gcoeff, atlb_stream_t stream) {
+  clear();
+  NONNEG(N);
+  if (R < 1 || R > 64) { set_error("%s: R = %lld records per event", __func__, (long long)R); return ATLB_ERR_ARG; }
+  NEED(gy, N * R); NEED(xy, N * R); NEED(t, N); NEED(b, N);
+  if (!gcoeff) { set_error("%s: gcoeff is NULL", __func__); return ATLB_ERR_ARG; }
+  TrajView V;
+  if (int st = make_traj(coeff, B, Hq, Wq, K, basis, bezier_c, offset, tile, n_fp, &V, __func__)) return st;
+  return traj_records_bwd(V, (int)R, gy, xy, t, t_dst, (float)t_dst_s, LL(b), N, iterates, gcoeff, STREAM(stream));
+}
+
+int atlb_traj_targets(const float* coeff, int64_t B, int64_t Hq, int64_t Wq, int64_t K, int basis,
+                      const float* bezier_c, double offset, double tile, int64_t n_fp, const float* xy, const float* t,
+                      const int64_t* b, int64_t N, const float* targets, int64_t T, float* out, atlb_stream_t stream) {
+  clear();
+  NONNEG(N);
+  if (T < 1 || T > traj_targets_max() || !targets) {
+    set_error("%s: T = %lld targets (1..%d), targets %s", __func__, (long long)T, traj_targets_max(),
+              targets ? "set" : "NULL");
+    return ATLB_ERR_ARG;
+  }
+  NEED(xy, N); NEED(t, N); NEED(b, N); NEED(out, N * T);
+  TrajView V;
+  if (int st = make_traj(coeff, B, Hq, Wq, K, basis, bezier_c, offset, tile, n_fp, &V, __func__)) return st;
+  return traj_targets(V, xy, t, LL(b), N, targets, (int)T, out, STREAM(stream));
+}
+
+int atlb_traj_targets_bwd(const float* gy, const float* coeff, int64_t B, int64_t Hq, int64_t Wq, int64_t K,
+                          int basis, const float* bezier_c, double offset, double tile, int64_t n_fp, const float* xy,
+                          const float* t, const int64_t* b, int64_t N, const float* targets, int64_t T, float* gcoeff,
+                          atlb_stream_t stream) {
+  clear();
+  NONNEG(N);
+  if (T < 1 || T > traj_targets_max() || !targets) {
+    set_error("%s: T = %lld targets (1..%d), targets %s", __func__, (long long)T, traj_targets_max(),
+              targets ? "set" : "NULL");
+    return ATLB_ERR_ARG;
+  }
+  NEED(gy, N * T); NEED(xy, N); NEED(t, N); NEED(b, N);
+  if (!gcoeff) { set_error("%s: gcoeff is NULL", __func__); return ATLB_ERR_ARG; }
+  TrajView V;
+  if (int st = make_traj(coeff, B, Hq, Wq, K, basis, bezier_c, offset, tile, n_fp, &V, __func__)) return st;
+  return traj_targets_bwd(V, gy, xy, t, LL(b), N, targets, (int)T, gcoeff, STREAM(stream));
+}
+
+int atlb_count_keys(const int64_t* key, int64_t N, int64_t nbins, const float* mask, int64_t R, int64_t* out,
+                    atlb_stream_t stream) {
+  clear();
+  NONNEG(N);
+  if (nbins < 1 || R < 1 || nbins * R > (1LL << 24)) {
+    set_error("%s: nbins %lld x R %lld", __func__, (long long)nbins, (long long)R);
+    return ATLB_ERR_ARG;
+  }
+  NEED(key, N); NEED(out, nbins * R);
+  return count_keys(LL(key), N, nbins, mask, R, LLW(out), STREAM(stream));
 }

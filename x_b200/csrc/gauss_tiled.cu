@@ -392,7 +392,7 @@ __device__ __forceinline__ void splat_event_bwd(const float* __restrict__ tile, 
     }
   }
   sw = mul_rn(K.norm, sw);
-  GW[n] = sw;
+  if (GW) GW[n] = sw;
   GP[n] = make_float2(mul_rn(w, div_rn(mul_rn(K.norm, sx), K.s2)), mul_rn(w, div_rn(mul_rn(K.norm, sy), K.s2)));
 }
 
@@ -424,7 +424,7 @@ __global__ void __launch_bounds__(kGThreads) k_gsplat_bwd_init(const float* __re
   const long long stride = (long long)gridDim.x * blockDim.x;
   for (long long n = blockIdx.x * (long long)blockDim.x + threadIdx.x; n < N; n += stride) {
     const float z = mul_rn(Wt[n], 0.f);
-    GW[n] = 0.f;
+    if (GW) GW[n] = 0.f;
     GP[n] = make_float2(z, z);
   }
 }
@@ -550,6 +550,30 @@ int splat_gauss_bwd(const float* g, const float* pos, const float* w, const long
     timing_end("k_gsplat_bwd", s, e0);
   }
   return launch_status("splat_gauss_bwd");
+}
+
+// Backward w.r.t. the positions only, over the buckets that the preceding splat_gauss_fwd of the same
+// (pos, w, b) left in ws: the forward's bucketing is reused, not redone.  Events the forward skipped (zero
+// weight) get gpos = w * 0.
+int splat_gauss_bwd_pos(const float* g, const float* w, long long N, long long B, long long H, long long W,
+                        double sigma, long long R, float* gpos, void* ws, cudaStream_t s) {
+  const GTiles T = make_tiles(B, H, W, R);
+  const GaussConsts K = gauss_consts(sigma);
+  const GaussWs gw = carve_gauss(ws, N, T.ntiles);
+  if (N > 0) launch(k_gsplat_bwd_init, ggrid(N), kGThreads, 0, s, w, N, (float*)nullptr, (float2*)gpos);
+  if (N > 0 && T.ntiles > 0) {
+    const size_t smem = tile_smem((int)R);
+    const int grid = (int)(T.ntiles < 148LL * 16 ? T.ntiles : 148LL * 16);
+    cudaEvent_t e0 = timing_begin(s);
+    dispatch_radius((int)R, [&](auto rc) {
+      constexpr int RT = decltype(rc)::value;
+      allow_smem(k_gsplat_bwd_tiles<RT>, smem);
+      launch(k_gsplat_bwd_tiles<RT>, grid, kGThreads, smem, s, T, K, (const float4*)gw.EV, (const int*)gw.start, g,
+             (float*)nullptr, (float2*)gpos);
+    });
+    timing_end("k_gsplat_bwd", s, e0);
+  }
+  return launch_status("splat_gauss_bwd_pos");
 }
 
 }  // namespace atlb

@@ -158,6 +158,44 @@ __global__ void __launch_bounds__(kThreads) k_score_bwd(ScoreConsts K, long long
   }
 }
 
+// Counts of small keys: out[r][k] = #{n : key[n] == k, mask == NULL or mask[r * N + n] != 0} for R mask rows.
+// The histograms of AnchoredSliced (anchors per slice, sources per slice and batch, events per check slice):
+// keys of sorted events repeat along a warp, so each warp adds one count per distinct key (__match_any_sync)
+// to shared counters, flushed once per block.
+constexpr int kCountSmem = 8192;
+
+__global__ void __launch_bounds__(kThreads) k_count_keys(const long long* __restrict__ key, long long N, int nbins,
+                                                         const float* __restrict__ mask, int R,
+                                                         unsigned long long* __restrict__ out) {
+  __shared__ unsigned int hist[kCountSmem];
+  const int total = nbins * R;
+  const bool sm = total <= kCountSmem;
+  if (sm)
+    for (int i = threadIdx.x; i < total; i += blockDim.x) hist[i] = 0;
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long n0 = blockIdx.x * (long long)blockDim.x; n0 < N; n0 += stride) {  // warp-uniform
+    const long long n = n0 + threadIdx.x;
+    long long k = n < N ? key[n] : -1;
+    if (k >= nbins) k = -1;
+    const unsigned grp = __match_any_sync(0xffffffffu, k);
+    const bool leader = lane == __ffs(grp) - 1;
+    for (int r = 0; r < R; ++r) {
+      const bool m = k >= 0 && (mask == nullptr || mask[(long long)r * N + n] != 0.f);
+      const unsigned c = __popc(__ballot_sync(0xffffffffu, m) & grp);
+      if (leader && k >= 0 && c) {
+        if (sm) atomicAdd(hist + r * nbins + k, c);
+        else atomicAdd(out + (long long)r * nbins + k, (unsigned long long)c);
+      }
+    }
+  }
+  __syncthreads();
+  if (sm)
+    for (int i = threadIdx.x; i < total; i += blockDim.x)
+      if (hist[i]) atomicAdd(out + i, (unsigned long long)hist[i]);
+}
+
 ScoreConsts score_consts(int P, int ia, int io, int ip, double sigma, double delta, double eps, long long H,
                          long long W) {
   ScoreConsts K;
@@ -195,6 +233,15 @@ int sliced_score_bwd(long long N, int P, int ia, int io, int ip, const float* gl
     launch(k_score_bwd, clamp_grid(blocks_for(N, kThreads)), kThreads, 0, s, K, N, gls, (const float2*)pos, val, cnt,
            vis, src, gval, (float2*)gpos);
   return launch_status("sliced_score_bwd");
+}
+
+int count_keys(const long long* key, long long N, long long nbins, const float* mask, long long R, long long* out,
+               cudaStream_t s) {
+  cudaMemsetAsync(out, 0, (size_t)(nbins * R) * sizeof(long long), s);
+  if (N > 0 && nbins > 0)
+    launch(k_count_keys, clamp_grid(blocks_for(N, kThreads)), kThreads, 0, s, key, N, (int)nbins, mask, (int)R,
+           (unsigned long long*)out);
+  return launch_status("count_keys");
 }
 
 }  // namespace atlb

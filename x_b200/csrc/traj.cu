@@ -328,6 +328,318 @@ __global__ void __launch_bounds__(kTThreads) k_traj_vis(TrajView V, const float2
   }
 }
 
+// Records: R positions per event (xy (N, R, 2), all at the event's time t) moved to one target time each
+// (t_dst per event or t_dst_s): out (N, R, 2), each record exactly as mode 0 moves it.  One thread per record,
+// so the records of an event sit in neighbouring lanes and their coefficient taps (close together, usually
+// in one cell) are served by the same load instructions.  The backward merges the final per-tap gradient
+// sums of neighbouring lanes of one event and one coefficient cell (segmented shuffle reduction) before a
+// single lane flushes them.
+template <int K>
+__global__ void __launch_bounds__(kTThreads) k_traj_records_fwd(TrajView V, int R, const float2* __restrict__ xy,
+                                                                const float* __restrict__ t,
+                                                                const float* __restrict__ tdst, float tdst_s,
+                                                                const long long* __restrict__ b, long long N,
+                                                                float2* __restrict__ out, float2* __restrict__ iters) {
+  const long long NR = N * R;
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < NR; i += stride) {
+    const long long n = i / R;
+    if (b[n] < 0 || b[n] >= V.B) {
+      out[i] = make_float2(__int_as_float(0x7fc00000), __int_as_float(0x7fc00000));
+      continue;
+    }
+    const int bb = (int)b[n];
+    float g[K];
+    traj_basis<K>(V, t[n], g);
+    const float2 x = xy[i];
+    float px = x.x, py = x.y;
+    for (int it = 0; it < V.n_fp; ++it) {
+      const float2 d = traj_disp<K>(V, traj_taps(V, bb, px, py), g);
+      px = sub_rn(x.x, d.x);
+      py = sub_rn(x.y, d.y);
+      if (iters) iters[(long long)it * NR + i] = make_float2(px, py);  // iterate-major: coalesced
+    }
+    traj_basis<K>(V, tdst ? tdst[n] : tdst_s, g);
+    const float2 d = traj_disp<K>(V, traj_taps(V, bb, px, py), g);
+    out[i] = make_float2(add_rn(px, d.x), add_rn(py, d.y));
+  }
+}
+
+template <int K>
+__global__ void __launch_bounds__(kTThreads) k_traj_records_bwd(TrajView V, int R, const float2* __restrict__ gy,
+                                                                const float2* __restrict__ xy,
+                                                                const float* __restrict__ t,
+                                                                const float* __restrict__ tdst, float tdst_s,
+                                                                const long long* __restrict__ b, long long N,
+                                                                const float2* __restrict__ iters,
+                                                                float* __restrict__ gC) {
+  const long long NR = N * R;
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  const int lane = threadIdx.x & 31;
+  // warp-uniform loop: every lane reaches the merge below on every pass
+  for (long long i0 = blockIdx.x * (long long)blockDim.x; i0 < NR; i0 += stride) {
+    const long long i = i0 + threadIdx.x;
+    const long long n = i < NR ? i / R : -1;
+    float g[K], gd[K];
+    CellAcc A;
+    A.live = false;
+    const float2 u = n >= 0 ? gy[i] : make_float2(0.f, 0.f);
+    if (n >= 0 && (u.x != 0.f || u.y != 0.f) && b[n] >= 0 && b[n] < V.B) {
+      const int bb = (int)b[n];
+      traj_basis<K>(V, t[n], g);
+      traj_basis<K>(V, tdst ? tdst[n] : tdst_s, gd);
+      const float2 x = xy[i];
+      float P[kTrajKMax + 1][2];
+      P[0][0] = x.x;
+      P[0][1] = x.y;
+      for (int it = 0; it < V.n_fp; ++it) {
+        if (iters) {  // the forward's iterates
+          const float2 q = iters[(long long)it * NR + i];
+          P[it + 1][0] = q.x;
+          P[it + 1][1] = q.y;
+          continue;
+        }
+        const float2 d = traj_disp<K>(V, traj_taps(V, bb, P[it][0], P[it][1]), g);
+        P[it + 1][0] = sub_rn(x.x, d.x);
+        P[it + 1][1] = sub_rn(x.y, d.y);
+      }
+      const Taps T = traj_taps(V, bb, P[V.n_fp][0], P[V.n_fp][1]);
+      acc_add<K>(A, T, true, u.x, u.y, g, gd, gC);
+      const float2 jt = traj_jt<K>(V, T, gd, u.x, u.y);
+      float gpx = u.x + jt.x, gpy = u.y + jt.y;
+      for (int it = V.n_fp - 1; it >= 0; --it) {
+        const Taps Ti = traj_taps(V, bb, P[it][0], P[it][1]);
+        acc_add<K>(A, Ti, false, -gpx, -gpy, g, gd, gC);
+        const float2 j = traj_jt<K>(V, Ti, g, -gpx, -gpy);
+        gpx = j.x;
+        gpy = j.y;
+      }
+    }
+    // runs of neighbouring lanes with the same event and the same open cell add up their per-tap sums
+    const long long key_n = A.live ? n : -1 - lane;
+    const long long key_c = A.live ? A.base[0] : -1;
+    const long long prev_n = __shfl_up_sync(0xffffffffu, key_n, 1), prev_c = __shfl_up_sync(0xffffffffu, key_c, 1);
+    const bool head = lane == 0 || prev_n != key_n || prev_c != key_c;
+    const unsigned heads = __ballot_sync(0xffffffffu, head);
+    const int run = __popc(heads & (0xffffffffu >> (31 - lane)));
+    for (int off = 1; off < R && off < 32; off <<= 1) {
+      const int orun = __shfl_down_sync(0xffffffffu, run, off);
+      const bool take = lane + off < 32 && orun == run;
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          const float oa = __shfl_down_sync(0xffffffffu, A.a[q][c], off);
+          const float of = __shfl_down_sync(0xffffffffu, A.f[q][c], off);
+          if (take) {
+            A.a[q][c] += oa;
+            A.f[q][c] += of;
+          }
+        }
+    }
+    if (head && A.live) acc_flush<K>(A, g, gd, gC);
+  }
+}
+
+// Targets: every event moved to each of T shared target times (targets, T <= kTrajTargetsMax): the origin
+// is solved once, the coefficients are sampled once at it, and each target costs one basis dot product.
+// out (T, N, 2), each entry exactly as mode 0 computes it.  Backward: with u_j = dL/dout[j] and
+// U_k = sum_j g_k(c_j) u_j, the coefficient gradient of the final samples is w_q U_k and dL/dp is
+// sum_j u_j + J^T(U), one Jacobian evaluation for all targets; then reverse mode through the iterations.
+constexpr int kTrajTargetsMax = 64;
+
+template <int K>
+__device__ __forceinline__ void load_target_bases(const TrajView& V, const float* __restrict__ targets, int T,
+                                                  float* s_gd) {
+  for (int j = threadIdx.x; j < T; j += blockDim.x) {
+    float gd[K];
+    traj_basis<K>(V, targets[j], gd);
+#pragma unroll
+    for (int k = 0; k < K; ++k) s_gd[j * K + k] = gd[k];
+  }
+  __syncthreads();
+}
+
+template <int K>
+__global__ void __launch_bounds__(kTThreads) k_traj_targets_fwd(TrajView V, const float2* __restrict__ xy,
+                                                                const float* __restrict__ t,
+                                                                const long long* __restrict__ b, long long N,
+                                                                const float* __restrict__ targets, int T,
+                                                                float2* __restrict__ out) {
+  __shared__ float s_gd[kTrajTargetsMax * K];
+  load_target_bases<K>(V, targets, T, s_gd);
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long n = blockIdx.x * (long long)blockDim.x + threadIdx.x; n < N; n += stride) {
+    if (b[n] < 0 || b[n] >= V.B) {
+      for (int j = 0; j < T; ++j) out[j * N + n] = make_float2(__int_as_float(0x7fc00000), __int_as_float(0x7fc00000));
+      continue;
+    }
+    const int bb = (int)b[n];
+    const float2 x = xy[n];
+    float g[K];
+    traj_basis<K>(V, t[n], g);
+    float px = x.x, py = x.y;
+    for (int i = 0; i < V.n_fp; ++i) {
+      const float2 d = traj_disp<K>(V, traj_taps(V, bb, px, py), g);
+      px = sub_rn(x.x, d.x);
+      py = sub_rn(x.y, d.y);
+    }
+    // the coefficient sample at the origin (taps summed in order, as traj_disp sums them)
+    const Taps Tp = traj_taps(V, bb, px, py);
+    float c[2 * K];
+#pragma unroll
+    for (int ch = 0; ch < 2 * K; ++ch) c[ch] = 0.f;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      float f[2 * K];
+      load_tap<K>(V.C + Tp.base[q], f);
+#pragma unroll
+      for (int ch = 0; ch < 2 * K; ++ch) c[ch] = add_rn(c[ch], mul_rn(f[ch], Tp.w[q]));
+    }
+    for (int j = 0; j < T; ++j) {
+      const float* gd = s_gd + j * K;
+      float dx = 0.f, dy = 0.f;
+#pragma unroll
+      for (int k = 0; k < K; ++k) {
+        dx = add_rn(dx, mul_rn(c[K + k], gd[k]));
+        dy = add_rn(dy, mul_rn(c[k], gd[k]));
+      }
+      out[j * N + n] = make_float2(add_rn(px, dx), add_rn(py, dy));
+    }
+  }
+}
+
+template <int K>
+__global__ void __launch_bounds__(kTThreads) k_traj_targets_bwd(TrajView V, const float2* __restrict__ gy,
+                                                                const float2* __restrict__ xy,
+                                                                const float* __restrict__ t,
+                                                                const long long* __restrict__ b, long long N,
+                                                                const float* __restrict__ targets, int T,
+                                                                float* __restrict__ gC) {
+  __shared__ float s_gd[kTrajTargetsMax * K];
+  load_target_bases<K>(V, targets, T, s_gd);
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long n = blockIdx.x * (long long)blockDim.x + threadIdx.x; n < N; n += stride) {
+    if (b[n] < 0 || b[n] >= V.B) continue;
+    float Ux[K], Uy[K];
+#pragma unroll
+    for (int k = 0; k < K; ++k) Ux[k] = Uy[k] = 0.f;
+    float sux = 0.f, suy = 0.f;
+    for (int j = 0; j < T; ++j) {
+      const float2 u = gy[j * N + n];
+      const float* gd = s_gd + j * K;
+      sux += u.x;
+      suy += u.y;
+#pragma unroll
+      for (int k = 0; k < K; ++k) {
+        Ux[k] += gd[k] * u.x;
+        Uy[k] += gd[k] * u.y;
+      }
+    }
+    if (sux == 0.f && suy == 0.f) {
+      bool any = false;
+#pragma unroll
+      for (int k = 0; k < K; ++k) any |= (Ux[k] != 0.f) | (Uy[k] != 0.f);
+      if (!any) continue;
+    }
+    const int bb = (int)b[n];
+    const float2 x = xy[n];
+    float g[K];
+    traj_basis<K>(V, t[n], g);
+    float P[kTrajKMax + 1][2];
+    P[0][0] = x.x;
+    P[0][1] = x.y;
+    for (int i = 0; i < V.n_fp; ++i) {
+      const float2 d = traj_disp<K>(V, traj_taps(V, bb, P[i][0], P[i][1]), g);
+      P[i + 1][0] = sub_rn(x.x, d.x);
+      P[i + 1][1] = sub_rn(x.y, d.y);
+    }
+    const Taps Tp = traj_taps(V, bb, P[V.n_fp][0], P[V.n_fp][1]);
+    // final samples: coefficient gradient w_q U_k, and dL/dp = sum_j u_j + J^T(U)
+    float jx = 0.f, jy = 0.f;
+    {
+      float f[4][2 * K];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) load_tap<K>(V.C + Tp.base[q], f[q]);
+      const float oax = 1.f - Tp.ax, oay = 1.f - Tp.ay;
+#pragma unroll
+      for (int k = 0; k < K; ++k) {
+        const int X = K + k;
+        jx += Ux[k] * ((f[1][X] - f[0][X]) * oay + (f[3][X] - f[2][X]) * Tp.ay) +
+              Uy[k] * ((f[1][k] - f[0][k]) * oay + (f[3][k] - f[2][k]) * Tp.ay);
+        jy += Ux[k] * ((f[2][X] - f[0][X]) * oax + (f[3][X] - f[1][X]) * Tp.ax) +
+              Uy[k] * ((f[2][k] - f[0][k]) * oax + (f[3][k] - f[1][k]) * Tp.ax);
+      }
+    }
+    float gpx = sux + (Tp.gx_in ? jx / V.tile : 0.f), gpy = suy + (Tp.gy_in ? jy / V.tile : 0.f);
+    // the fixed-point part accumulates per tap (basis g); the final samples' w_q U_k joins the flush of the
+    // origin's cell (the cell of the last iterate, where the reverse pass starts)
+    CellAcc A;
+    A.live = false;
+    bool final_pending = true;
+    auto flush = [&]() {
+      if (!A.live) return;
+      const bool fin = final_pending && A.base[0] == Tp.base[0];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float v[2 * K];
+#pragma unroll
+        for (int k = 0; k < K; ++k) {
+          v[k] = g[k] * A.a[q][1] + (fin ? Tp.w[q] * Uy[k] : 0.f);
+          v[K + k] = g[k] * A.a[q][0] + (fin ? Tp.w[q] * Ux[k] : 0.f);
+        }
+        float* dst = gC + A.base[q];
+        if constexpr ((2 * K) % 4 == 0) {
+#pragma unroll
+          for (int c = 0; c < 2 * K; c += 4) red_add_f4(dst + c, v[c], v[c + 1], v[c + 2], v[c + 3]);
+        } else {
+#pragma unroll
+          for (int c = 0; c < 2 * K; c += 2) red_add_f2(dst + c, v[c], v[c + 1]);
+        }
+      }
+      if (fin) final_pending = false;
+      A.live = false;
+    };
+    // open the accumulator on the origin's cell so that the final samples always find it
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      A.base[q] = Tp.base[q];
+      A.a[q][0] = A.a[q][1] = 0.f;
+    }
+    A.live = true;
+    for (int i = V.n_fp - 1; i >= 0; --i) {
+      const Taps Ti = traj_taps(V, bb, P[i][0], P[i][1]);
+      if (A.live && A.base[0] != Ti.base[0]) flush();
+      if (!A.live) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          A.base[q] = Ti.base[q];
+          A.a[q][0] = A.a[q][1] = 0.f;
+        }
+        A.live = true;
+      }
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        A.a[q][0] -= Ti.w[q] * gpx;
+        A.a[q][1] -= Ti.w[q] * gpy;
+      }
+      const float2 j = traj_jt<K>(V, Ti, g, -gpx, -gpy);
+      gpx = j.x;
+      gpy = j.y;
+    }
+    flush();
+    if (final_pending) {  // the iterations left the origin's cell: the final samples flush on their own
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        A.base[q] = Tp.base[q];
+        A.a[q][0] = A.a[q][1] = 0.f;
+      }
+      A.live = true;
+      flush();
+    }
+  }
+}
+
 inline int tgrid(long long n) { return clamp_grid(blocks_for(n, kTThreads)); }
 
 template <typename F>
@@ -373,15 +685,76 @@ int traj_transport_bwd(const TrajView& V, int mode, const float* gy, const float
   return launch_status("traj_transport_bwd");
 }
 
+int traj_records(const TrajView& V, int R, const float* xy, const float* t, const float* tdst, float tdst_s,
+                 const long long* b, long long N, float* out, float* iters, cudaStream_t s) {
+  if (N > 0) {
+    cudaEvent_t e0 = timing_begin(s);
+    dispatch_k(V.K, [&](auto kc) {
+      constexpr int K = decltype(kc)::value;
+      launch(k_traj_records_fwd<K>, tgrid(N * R), kTThreads, 0, s, V, R, (const float2*)xy, t, tdst, tdst_s, b, N,
+             (float2*)out, (float2*)iters);
+    });
+    timing_end("k_traj_records_fwd", s, e0);
+  }
+  return launch_status("traj_records");
+}
+
+int traj_records_bwd(const TrajView& V, int R, const float* gy, const float* xy, const float* t, const float* tdst,
+                     float tdst_s, const long long* b, long long N, const float* iters, float* gC, cudaStream_t s) {
+  if (N > 0) {
+    cudaEvent_t e0 = timing_begin(s);
+    dispatch_k(V.K, [&](auto kc) {
+      constexpr int K = decltype(kc)::value;
+      launch(k_traj_records_bwd<K>, tgrid(N * R), kTThreads, 0, s, V, R, (const float2*)gy, (const float2*)xy, t,
+             tdst, tdst_s, b, N, (const float2*)iters, gC);
+    });
+    timing_end("k_traj_records_bwd", s, e0);
+  }
+  return launch_status("traj_records_bwd");
+}
+
+int traj_targets(const TrajView& V, const float* xy, const float* t, const long long* b, long long N,
+                 const float* targets, int T, float* out, cudaStream_t s) {
+  if (N > 0) {
+    cudaEvent_t e0 = timing_begin(s);
+    dispatch_k(V.K, [&](auto kc) {
+      constexpr int K = decltype(kc)::value;
+      launch(k_traj_targets_fwd<K>, tgrid(N), kTThreads, 0, s, V, (const float2*)xy, t, b, N, targets, T,
+             (float2*)out);
+    });
+    timing_end("k_traj_targets_fwd", s, e0);
+  }
+  return launch_status("traj_targets");
+}
+
+int traj_targets_bwd(const TrajView& V, const float* gy, const float* xy, const float* t, const long long* b,
+                     long long N, const float* targets, int T, float* gC, cudaStream_t s) {
+  if (N > 0) {
+    cudaEvent_t e0 = timing_begin(s);
+    dispatch_k(V.K, [&](auto kc) {
+      constexpr int K = decltype(kc)::value;
+      launch(k_traj_targets_bwd<K>, tgrid(N), kTThreads, 0, s, V, (const float2*)gy, (const float2*)xy, t, b, N,
+             targets, T, gC);
+    });
+    timing_end("k_traj_targets_bwd", s, e0);
+  }
+  return launch_status("traj_targets_bwd");
+}
+
+int traj_targets_max() { return kTrajTargetsMax; }
+
 int traj_visible_fraction(const TrajView& V, const float* xa, const float* ta, const long long* ba, long long M,
                           const float* counts, const float* centres, int n_check, float tau, float wmax, float hmax,
                           float* out, cudaStream_t s) {
-  if (M > 0)
+  if (M > 0) {
+    cudaEvent_t e0 = timing_begin(s);
     dispatch_k(V.K, [&](auto kc) {
       constexpr int K = decltype(kc)::value;
       launch(k_traj_vis<K>, tgrid(M), kTThreads, 0, s, V, (const float2*)xa, ta, ba, M, counts, centres, n_check, tau,
              wmax, hmax, out);
     });
+    timing_end("k_traj_vis", s, e0);
+  }
   return launch_status("traj_visible_fraction");
 }
 

@@ -71,6 +71,54 @@ def splat(pos: torch.Tensor, w: torch.Tensor, b: torch.Tensor, B: int, H: int, W
     raise ValueError(kernel)
 
 
+class _SplatSlices(torch.autograd.Function):
+    """Gaussian splats of T point sets sharing one batch index into a (T * B, H, W) stack: set j goes to
+    images j * B .. j * B + B - 1 (one atlb_splat_gauss_fwd per set).  Differentiable w.r.t. the positions
+    only (the weights are masks): the backward reuses each set's forward buckets (atlb_splat_gauss_bwd_pos)."""
+
+    @staticmethod
+    def forward(ctx, pos, w, b, B, H, W, sigma, radius):
+        pos, w, b = _f32(pos), _f32(w), b.contiguous().long()
+        T, N = pos.shape[0], pos.shape[1]
+        img = torch.empty(T * B, H, W, dtype=torch.float32, device=pos.device)
+        nb = L.lib().atlb_splat_gauss_workspace_bytes(N, B, H, W)
+        # one workspace per set, kept for the backward: its buckets are reused there (weights are constants)
+        keep = ctx.needs_input_grad[0]
+        wss = [L.workspace(nb, pos.device) for _ in range(T if keep else 1)]
+        for j in range(T):
+            ws = wss[j if keep else 0]
+            L.check(L.lib().atlb_splat_gauss_fwd(L.ptr(pos[j]), L.ptr(w[j]), L.ptr(b), N, B, H, W, float(sigma),
+                                                  int(radius), L.ptr(img[j * B:(j + 1) * B]), L.ptr(ws), nb,
+                                                  L.stream()), "splat_slices")
+        ctx.save_for_backward(w)
+        ctx.wss = wss if keep else None
+        ctx.meta = (T, N, B, H, W, float(sigma), int(radius), nb)
+        return img
+
+    @staticmethod
+    def backward(ctx, g):
+        (w,) = ctx.saved_tensors
+        T, N, B, H, W, sigma, radius, nb = ctx.meta
+        g = g.contiguous().float()
+        gp = torch.empty(T, N, 2, dtype=torch.float32, device=g.device)
+        for j in range(T):
+            L.check(L.lib().atlb_splat_gauss_bwd_pos(L.ptr(g[j * B:(j + 1) * B]), L.ptr(w[j]), N, B, H, W, sigma,
+                                                      radius, L.ptr(gp[j]), L.ptr(ctx.wss[j]), nb, L.stream()),
+                    "splat_slices_bwd")
+        ctx.wss = None
+        return gp, None, None, None, None, None, None, None
+
+
+def splat_slices(pos: torch.Tensor, w: torch.Tensor, b: torch.Tensor, B: int, H: int, W: int, sigma: float,
+                 radius: int | None = None) -> torch.Tensor:
+    """Gaussian splat of T point sets (pos (T, N, 2), weights w (T, N), batch index b (N) shared) into a
+    (T * B, H, W) image stack: ``splat(pos[j], w[j], b, B, H, W, "gauss", sigma)`` for each j, stacked.
+    Gradient w.r.t. ``pos`` only."""
+    _need_cuda(pos, "splat_slices")
+    radius = int(math.ceil(3 * sigma)) if radius is None else radius
+    return _SplatSlices.apply(pos, w, b, B, H, W, float(sigma), int(radius))
+
+
 # ------------------------------------------------------------------------------------------- gather
 class _Gather(torch.autograd.Function):
     """atl/ops/functional.py:69-80."""

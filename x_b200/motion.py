@@ -294,6 +294,79 @@ class _TrajTransport(torch.autograd.Function):
         return gC.permute(0, 3, 1, 2), gp, None, None, None, None, None
 
 
+def _traj_args(model):
+    """(coefficients channels-last, the leading C-ABI arguments) of a PixelTrajectories model."""
+    C = model.tile_c.detach().float().permute(0, 2, 3, 1).contiguous()
+    B, Hq, Wq, C2 = C.shape
+    return C, (L.ptr(C), B, Hq, Wq, C2 // 2, model._basis_id, L.ptr(model._bc), model.offset, float(model.tile),
+               model.n_fp)
+
+
+class _TrajRecords(torch.autograd.Function):
+    """R positions per event (xy (N, R, 2), at the event's time) moved to one target time per event
+    (atlb_traj_records), differentiable w.r.t. the tile coefficients; each record as mode 0 moves it."""
+
+    @staticmethod
+    def forward(ctx, tile_c, xy, t, t_dst, b, model):
+        C, head = _traj_args(model)
+        xyc, tc, bc = xy.detach().float().contiguous(), t.detach().float().contiguous(), b.contiguous().long()
+        if torch.is_tensor(t_dst) and t_dst.dim() > 0:
+            tdc, tds = t_dst.detach().float().contiguous(), 0.0
+        else:
+            tdc, tds = None, float(t_dst)
+        N, R = xyc.shape[0], xyc.shape[1]
+        out = torch.empty_like(xyc)
+        # the fixed-point iterates are kept for the backward when it will run (n_fp x 8 bytes per record)
+        its = torch.empty(model.n_fp, N, R, 2, dtype=torch.float32, device=xyc.device) \
+            if ctx.needs_input_grad[0] and model.n_fp > 0 else None
+        L.check(L.lib().atlb_traj_records(*head, L.ptr(xyc), R, L.ptr(tc), L.ptr(tdc), tds, L.ptr(bc), N, L.ptr(out),
+                                          L.ptr(its), L.stream()), "traj_records")
+        ctx.save_for_backward(C, xyc, tc, bc, *(() if tdc is None else (tdc,)))
+        ctx.tds, ctx.model, ctx.its = tds, model, its
+        return out
+
+    @staticmethod
+    def backward(ctx, gy):
+        C, xyc, tc, bc, *rest = ctx.saved_tensors
+        tdc = rest[0] if rest else None
+        _, head = _traj_args(ctx.model)
+        gC = torch.zeros_like(C)
+        N, R = xyc.shape[0], xyc.shape[1]
+        L.check(L.lib().atlb_traj_records_bwd(L.ptr(gy.contiguous().float()), *head, L.ptr(xyc), R, L.ptr(tc),
+                                              L.ptr(tdc), ctx.tds, L.ptr(bc), N, L.ptr(ctx.its), L.ptr(gC),
+                                              L.stream()), "traj_records_bwd")
+        ctx.its = None
+        return gC.permute(0, 3, 1, 2), None, None, None, None, None
+
+
+class _TrajTargets(torch.autograd.Function):
+    """Every event moved to each of T target times (atlb_traj_targets): (T, N, 2), differentiable w.r.t. the
+    tile coefficients; entry (j, n) as mode 0 moves event n to targets[j]."""
+
+    @staticmethod
+    def forward(ctx, tile_c, xy, t, targets, b, model):
+        C, head = _traj_args(model)
+        xyc, tc, bc = xy.detach().float().contiguous(), t.detach().float().contiguous(), b.contiguous().long()
+        tg = targets.detach().float().contiguous()
+        N, T = xyc.shape[0], tg.shape[0]
+        out = torch.empty(T, N, 2, dtype=torch.float32, device=xyc.device)
+        L.check(L.lib().atlb_traj_targets(*head, L.ptr(xyc), L.ptr(tc), L.ptr(bc), N, L.ptr(tg), T, L.ptr(out),
+                                          L.stream()), "traj_targets")
+        ctx.save_for_backward(C, xyc, tc, bc, tg)
+        ctx.model = model
+        return out
+
+    @staticmethod
+    def backward(ctx, gy):
+        C, xyc, tc, bc, tg = ctx.saved_tensors
+        _, head = _traj_args(ctx.model)
+        gC = torch.zeros_like(C)
+        L.check(L.lib().atlb_traj_targets_bwd(L.ptr(gy.contiguous().float()), *head, L.ptr(xyc), L.ptr(tc),
+                                              L.ptr(bc), xyc.shape[0], L.ptr(tg), tg.shape[0], L.ptr(gC), L.stream()),
+                "traj_targets_bwd")
+        return gC.permute(0, 3, 1, 2), None, None, None, None, None
+
+
 class PixelTrajectories(Motion):
     """One continuous-time trajectory per ``tile`` x ``tile`` patch, coefficients from a (B, 2K, H, W) grid
     (atl/motion/trajectories.py:40-120): q(p, t) = p + sum_k c_k(p) g_k(t), channels [y_1..y_K, x_1..x_K].
@@ -348,6 +421,16 @@ class PixelTrajectories(Motion):
         exactly :meth:`transport`; differentiable w.r.t. p (a caller moving the same events to several
         times solves each origin once)."""
         return _TrajTransport.apply(self.tile_c, p, t, t_dst, b, self, 2)
+
+    def transport_records(self, xy, t, t_dst, b):
+        """xy (N, R, 2): R positions per event at its time t, each moved to t_dst (scalar or per event) as
+        :meth:`transport` moves it, in one kernel (the anchor and its log-determinant probes)."""
+        return _TrajRecords.apply(self.tile_c, xy, t, t_dst, b, self)
+
+    def transport_targets(self, xy, t, targets, b):
+        """(T, N, 2): every event moved to each of the T times ``targets`` as :meth:`transport` moves it; one
+        origin solve per event (the sources at every slice centre)."""
+        return _TrajTargets.apply(self.tile_c, xy, t, targets, b, self)
 
     def _device_transport(self, xy, t) -> bool:
         """The kernels cover the invert assignment, K <= 16 and n_fp <= 16, for positions without gradient."""

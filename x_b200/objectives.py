@@ -20,7 +20,7 @@ import torch
 from . import _lib as L
 from . import rng as R
 from .events import EventPacket
-from .functional import ats_pair_sums, gather, splat, window_counts
+from .functional import ats_pair_sums, gather, splat, splat_slices, window_counts
 from .motion import VectorFieldMotion
 
 
@@ -32,12 +32,27 @@ def _fused_kind(motion) -> int:
 
 
 @torch.no_grad()
+def count_keys(key: torch.Tensor, nbins: int, mask: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Exact counts of the keys in [0, nbins) (atlb_count_keys), int64: (nbins,) without ``mask``, else
+    (R, nbins) counting, for each row r of the (R, N) ``mask``, the keys where mask[r] != 0."""
+    if not key.is_cuda:
+        raise RuntimeError("x_b200.count_keys: expected CUDA tensors (there is no CPU path)")
+    kc = key.contiguous().long()
+    mc = None if mask is None else mask.reshape(-1, kc.shape[0]).float().contiguous()
+    R = 1 if mc is None else mc.shape[0]
+    out = torch.empty(R, nbins, dtype=torch.int64, device=key.device)
+    L.check(L.lib().atlb_count_keys(L.ptr(kc), kc.shape[0], nbins, L.ptr(mc), R, L.ptr(out), L.stream()),
+            "count_keys")
+    return out[0] if mc is None else out
+
+
+@torch.no_grad()
 def slice_counts(ev: EventPacket, n_check: int = 16) -> torch.Tensor:
     """Per-batch event counts in ``n_check`` equal time slices (ats.py:40-42), as exact integer counts
-    (a bincount, not an accumulating scatter of ones), float32 (B, n_check)."""
+    (not an accumulating scatter of ones), float32 (B, n_check)."""
     sl = torch.clamp((ev.t * n_check).long(), 0, n_check - 1)
-    return torch.bincount(ev.b * n_check + sl, minlength=ev.batch_size * n_check).view(
-        ev.batch_size, n_check).to(torch.float32)
+    key = torch.where((ev.b >= 0) & (ev.b < ev.batch_size), ev.b * n_check + sl, -1)
+    return count_keys(key, ev.batch_size * n_check).view(ev.batch_size, n_check).to(torch.float32)
 
 
 def visible_fraction(motion, xa, ta, ba, ev: EventPacket, tau: float, n_check: int = 16,
@@ -314,10 +329,10 @@ class AnchoredSliced(Objective):
         """Per-anchor log scores and anchor indices (ats.py:122-174).  ``noise`` = :meth:`draw`'s
         (slices, u, z) replaces the generator draws.
 
-        All slices are evaluated at once: one transport of every (source, slice) pair into a stack of
-        len(slices) x B density images (one splat), one transport of every anchor's record (its position,
-        the four log-determinant probes and its unsmoothed source copy) to its own slice centre, one gather
-        and the fused per-anchor score kernel (atlb_sliced_score).  Anchors come out in the reference's
+        All slices are evaluated at once: every event moved to every evaluated slice centre and splatted,
+        weighted by its source mask, into a stack of len(slices) x B density images; every anchor's record
+        (its position, the four log-determinant probes and its unsmoothed source copy) moved to its own
+        slice centre; one gather and the fused per-anchor score kernel (atlb_sliced_score).  Anchors come out in the reference's
         order: slice by slice in ``slices`` order, ascending event index inside a slice (or the slice's
         random subset when n_anchors_per_slice is set, drawn as the reference draws it)."""
         S, dev, B = self.S, ev.device, ev.batch_size
@@ -341,9 +356,7 @@ class AnchoredSliced(Objective):
                                                                        device=dev)
         if source_mask is not None:
             src = src & source_mask[None, :]
-        # the one read-back of the step: anchors per slice and the number of (source, slice) pairs
-        stats = torch.cat([torch.bincount(rank, minlength=Sp + 1)[:Sp], src.sum().view(1)]).tolist()
-        n_anc, n_pairs = stats[:Sp], stats[Sp]
+        n_anc = count_keys(rank, Sp).tolist()  # the one read-back of the step
         rank_sorted, order = torch.sort(rank, stable=True)
         pieces, ranks, off = [], [], 0
         for k in range(Sp):
@@ -365,16 +378,12 @@ class AnchoredSliced(Objective):
             ai = torch.cat(pieces)
             ka = torch.cat([torch.full((p.numel(),), k, dtype=torch.long, device=dev) for p, k in zip(pieces, ranks)])
 
-        # sources of every slice, transported to its centre and splatted into image k * B + b
-        if n_pairs == Sp * ev.n:
-            ks = torch.arange(Sp, device=dev).repeat_interleave(ev.n)
-            js = torch.arange(ev.n, device=dev).repeat(Sp)
-        else:
-            flat = torch.nonzero(src.reshape(-1)).squeeze(1)
-            ks, js = flat // ev.n, flat % ev.n
-        y = self._sources_at_centres(motion, xs, ev, js, centres[ks])
-        img = splat(y, torch.ones_like(y[:, 0]), ks * B + ev.b[js], Sp * B, ev.height, ev.width,
-                    kernel="gauss", sigma=self.sigma)
+        # every event at every evaluated slice centre (Sp, N, 2), splatted with the slice's source mask as
+        # weights (zero weights add nothing) into images k * B + b
+        Y = self._events_at_centres(motion, xs, ev, centres)
+        wsrc = src.to(xs.dtype)
+        img = splat_slices(Y, wsrc, ev.b, B, ev.height, ev.width, self.sigma)
+        per_kb = count_keys(ev.b, B, wsrc).to(xs.dtype)  # sources per (slice, batch)
 
         # anchor records at their slice centres: [x +- d e_x, x +- d e_y,] a [, unsmoothed copy]
         xa, ta, ba, ca = xsm[ai], ev.t[ai], ev.b[ai], centres[ka]
@@ -390,14 +399,16 @@ class AnchoredSliced(Objective):
             io = len(recs)
             recs.append(xs[ai])
         P = len(recs)
-        rec = torch.stack(recs, 1).reshape(-1, 2)
-        pos = motion.transport(rec, ta.repeat_interleave(P), ca.repeat_interleave(P),
-                               ba.repeat_interleave(P)).reshape(-1, P, 2)
+        rec = torch.stack(recs, 1)
+        if hasattr(motion, "transport_records") and motion._device_transport(xa, ta):
+            pos = motion.transport_records(rec, ta, ca, ba)
+        else:
+            pos = motion.transport(rec.reshape(-1, 2), ta.repeat_interleave(P), ca.repeat_interleave(P),
+                                   ba.repeat_interleave(P)).reshape(-1, P, 2)
         img_a = ka * B + ba
         val = gather(img, pos[:, ia], img_a)
         src_a = src[ka, ai].to(val.dtype)
-        per_kb = torch.bincount(ks * B + ev.b[js], minlength=Sp * B).to(val.dtype)
-        cnt = per_kb[img_a] - src_a
+        cnt = per_kb[ka, ba] - src_a
         vis = None
         if self.visibility:
             vis = visible_fraction(motion, xa.detach(), ta, ba, ev, self.tau, counts=slice_counts(ev))
@@ -406,18 +417,18 @@ class AnchoredSliced(Objective):
         return ls, ai
 
     @staticmethod
-    def _sources_at_centres(motion, xs, ev: EventPacket, js, cen):
-        """Positions at the centres ``cen`` of the sources ``js`` (one entry per (source, slice) pair):
-        trajectories solve each event's origin once and move it to every centre; linear vector fields
-        evaluate each velocity once (x + v (c - t), the reference's warp); other models transport each pair."""
-        t, b = ev.t, ev.b
-        if hasattr(motion, "from_origin") and motion._device_transport(xs, t):
-            p = motion.origin_on_device(xs, t, b)
-            return motion.from_origin(p[js], t[js], cen, b[js])
+    def _events_at_centres(motion, xs, ev: EventPacket, centres):
+        """(Sp, N, 2): every event at every centre.  Trajectories: one kernel, one origin solve per event;
+        linear vector fields: each velocity once, x + v (c - t) (the reference's warp); other models: their
+        transport of every (event, centre) pair."""
+        t, b, n, Sp = ev.t, ev.b, ev.n, centres.shape[0]
+        if hasattr(motion, "transport_targets") and motion._device_transport(xs, t):
+            return motion.transport_targets(xs, t, centres, b)
         if _fused_kind(motion) >= 0:
             v = motion.velocity(xs, t, b)
-            return xs[js] + v[js] * (cen - t[js])[:, None]
-        return motion.transport(xs[js], t[js], cen, b[js])
+            return xs[None] + v[None] * (centres[:, None] - t[None])[..., None]
+        return motion.transport(xs.repeat(Sp, 1), t.repeat(Sp), centres.repeat_interleave(n),
+                                b.repeat(Sp)).view(Sp, n, 2)
 
     def set_bandwidth(self, h: float):
         self.sigma = float(h)
