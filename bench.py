@@ -53,6 +53,9 @@ def parse():
                     help="config2: one 1M-event window per GPU (the headline); config5: one 64M-event window "
                          "on 1280x720 shared by all GPUs (sources split across ranks, NCCL all-reduce); splat: the "
                          "Gaussian splat forward + backward of one slice of configuration 3 (sigma 1.5, 8 x 2M)")
+    ap.add_argument("--no-strong", action="store_true",
+                    help="leave out the strong-scaling legs of the default line (configuration 5a and 3 sharded "
+                         "over the --gpus ranks)")
     ap.add_argument("--cpu-worker", default=None, help=argparse.SUPPRESS)
     ap.add_argument("--record-traffic", nargs=2, metavar=("CSV", "COMMAND"), default=None,
                     help="write the per-launch DRAM traffic of the pair kernels from an ncu raw CSV export")
@@ -522,6 +525,7 @@ def ours_arm(args):
     for _ in range(nrep):
         torch.rand((args.events, 2), generator=gen); torch.randn((args.events, 2), generator=gen)
     host_rng_ms = 1000 * (time.perf_counter() - t0) / nrep
+    strong = None if args.no_strong else strong_scaling(world, dev)
     if world > 1:
         dist.destroy_process_group()
 
@@ -586,9 +590,91 @@ def ours_arm(args):
         "gpu_launches": int(launches),
         "clocks": clocks,
     }
+    if strong is not None:
+        line["strong_scaling"] = strong
     if cpu is not None:
         line["cpu_baseline"] = cpu
     print(json.dumps(line))
+
+
+# ------------------------------------------------------------------------------------------------ strong scaling
+def _timed_steps(step, steps, warmup, world, dev):
+    """Device ms per step (CUDA events around each step, summed; max over ranks), after untimed warm-up."""
+    import torch
+    import torch.distributed as dist
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    for i in range(steps):
+        starts[i].record()
+        step()
+        ends[i].record()
+    torch.cuda.synchronize()
+    tot = torch.tensor([sum(a.elapsed_time(b) for a, b in zip(starts, ends))], device=dev)
+    if world > 1:
+        dist.all_reduce(tot, op=dist.ReduceOp.MAX)
+    return float(tot) / steps
+
+
+def strong_scaling(world: int, dev, steps: int = 3, warmup: int = 3) -> dict:
+    """The two sharded workloads at this run's number of GPUs (total work fixed as N grows):
+    configuration 5a, one 64M-event window on 1280x720 under AnchoredExact + DenseLinearFlow, sources split
+    across the ranks (NCCL all-reduce of the M partial sums and of the flow gradient); and configuration 3,
+    AnchoredSliced + Bezier PixelTrajectories on 8 x 2M events, events split across the ranks (NCCL
+    all-reduce of the slices x 8 x 480 x 640 density stack, its gradient, the counts and the coefficient
+    gradient).  The windows are drawn on the device (seeded, identical on every rank)."""
+    import torch
+    from x_b200 import synth
+    from x_b200.distributed import ShardedAnchoredExact, ShardedAnchoredSliced
+    from x_b200.motion import DenseLinearFlow, PixelTrajectories
+    out = {}
+    # configuration 5a
+    n5, H5, W5 = 64_000_000, 720, 1280
+    ev = synth.textured_window(n5, H5, W5, duration=0.2, seed=5000, device=dev, draw_on_device=True)
+    flow = synth.lowpass_flow(1, H5, W5, sigma=32.0, vmax=20.0, seed=5001).to(dev)
+    m = DenseLinearFlow(1, H5, W5, grid=(H5, W5), mode="linear", init=flow).to(dev)
+    obj = ShardedAnchoredExact(h=1.0, tau=1.0, n_anchors=None, n_slices=16, seed=5002, visibility=True)
+    noise = obj.draw(ev)
+
+    def step5():
+        m.grid.grad = None
+        ls, _ = obj.log_scores(ev, m, noise=noise)
+        (-ls.mean()).backward()
+
+    ms = _timed_steps(step5, steps, warmup, world, dev)
+    out["config5a"] = {"value": n5 / (ms / 1000), "unit": "events/s", "ms_per_step": ms, "n_gpus": world,
+                       "steps": steps, "warmup": warmup, "events": n5,
+                       "workload": "one 64M-event window, 1280x720, AnchoredExact(h=1, tau=1, all anchors, 16 slices, "
+                                   "visibility) + DenseLinearFlow, fwd+bwd; sources split across the ranks"}
+    del ev, m, obj, noise, flow
+    torch.cuda.empty_cache()
+    # configuration 3
+    B3, n3, K = 8, 2_000_000, 10
+    ev = synth.textured_window(n3, H, W, duration=0.1, seed=3100, batch=B3, device=dev, draw_on_device=True)
+    g = torch.Generator(device=dev).manual_seed(3101)
+    raw = torch.nn.functional.avg_pool2d(torch.randn(B3, 2 * K, H, W, generator=g, device=dev), 17, 1, 8)
+    coeff = (raw / raw.abs().amax() * 15.0 / K).requires_grad_(True)
+    mt = PixelTrajectories(coeff, K, basis_kind="bezier", tile=4)
+    obj3 = ShardedAnchoredSliced(n_slices=10, sigma=1.5, seed=3102)
+    noise3 = obj3.draw(ev)
+
+    def step3():
+        coeff.grad = None
+        obj3(ev, mt, noise=noise3)["loss"].backward()
+        obj3.reduce_gradients([coeff])
+
+    ms = _timed_steps(step3, steps, warmup, world, dev)
+    out["config3"] = {"value": B3 * n3 / (ms / 1000), "unit": "events/s", "ms_per_step": ms, "n_gpus": world,
+                      "steps": steps, "warmup": warmup, "events": B3 * n3,
+                      "workload": "AnchoredSliced(10 slices, sigma 1.5) + PixelTrajectories(K=10 Bezier, tile 4), "
+                                  "8 x 2M events on 640x480, fwd+bwd; events split across the ranks"}
+    del ev, mt, obj3, noise3, coeff
+    torch.cuda.empty_cache()
+    return out
 
 
 # ------------------------------------------------------------------------------------------------ config 5

@@ -78,3 +78,55 @@ def test_partial_pair_sums_allreduce_to_full_sums_gloo():
         p.join(timeout=300)
     assert all(p.exitcode == 0 for p in procs)
     assert q.get(timeout=10) < 1e-6
+
+
+def _rank_sliced(rank, world, port, q):
+    """The sliced path's decomposition over gloo: each rank splats its share of the points (the C oracle's
+    Gaussian splat), the partial density stacks are summed by the differentiable all-reduce, and each
+    rank's loss reads the full stack; the summed position gradients equal the single-process ones."""
+    import torch.distributed as dist
+    from oracle import oracle as O
+    from x_b200.distributed import allreduce_sum_autograd
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    try:
+        rng = np.random.default_rng(11)
+        n, B, H, W, sigma, R = 4000, 2, 24, 40, 1.5, 5
+        pos = np.stack([rng.uniform(-3, W + 3, n), rng.uniform(-3, H + 3, n)], 1).astype(np.float32)
+        w = rng.uniform(0.5, 1.5, n).astype(np.float32)
+        b = np.sort(rng.integers(0, B, n)).astype(np.int64)
+        gimg = [rng.normal(size=(B, H, W)).astype(np.float32) for _ in range(world)]  # each rank's dL/dimg
+        j0, j1 = shard_range(n, rank, world)
+        part = torch.as_tensor(np.asarray(O.splat_gauss_fwd(pos[j0:j1], w[j0:j1], b[j0:j1], B, H, W, sigma, R),
+                                          np.float32)).requires_grad_(True)
+        img = allreduce_sum_autograd(part)
+        (img * torch.as_tensor(gimg[rank])).sum().backward()
+        # what the rank's splat backward receives: the sum over the ranks of dL/dimg
+        g_total = np.sum(gimg, 0)
+        full = np.asarray(O.splat_gauss_fwd(pos, w, b, B, H, W, sigma, R), np.float32)
+        gp_rank, _ = O.splat_gauss_bwd(part.grad.numpy(), pos[j0:j1], w[j0:j1], b[j0:j1], sigma, R)
+        gp_full, _ = O.splat_gauss_bwd(g_total, pos, w, b, sigma, R)
+        gp_all = allreduce_sum(torch.zeros(n, 2).index_copy_(0, torch.arange(j0, j1),
+                                                             torch.as_tensor(np.asarray(gp_rank, np.float32))))
+        if rank == 0:
+            q.put((float(np.abs(img.detach().numpy() - full).max() / np.abs(full).max()),
+                   float(np.abs(part.grad.numpy() - g_total).max()),
+                   float(np.abs(gp_all.numpy() - np.asarray(gp_full, np.float32)).max() /
+                         np.abs(np.asarray(gp_full)).max())))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_sliced_density_allreduce_decomposition_gloo():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_rank_sliced, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+    assert all(p.exitcode == 0 for p in procs)
+    e_img, e_g, e_gp = q.get(timeout=10)
+    assert e_img < 1e-6 and e_g < 1e-5 and e_gp < 1e-6

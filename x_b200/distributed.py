@@ -1,4 +1,12 @@
-"""One large event window over several GPUs (one process per GPU, torch.distributed over NCCL).
+"""Large event windows over several GPUs (one process per GPU, torch.distributed over NCCL).
+
+AnchoredSliced (``ShardedAnchoredSliced``): the events are split across the ranks.  Each rank moves its
+share of the events to every slice centre and splats it into a partial density stack (slices x B x H x W);
+the partial stacks and the per-(slice, batch) source counts are summed with an all-reduce; each rank then
+gathers and scores the anchors among its own events against the full density.  The backward all-reduces
+dL/d(density) the same way, so each rank's splat backward sees every rank's anchors.
+
+AnchoredExact (``ShardedAnchoredExact``):
 
 The anchored score of a single window of N events (configuration 5: 64M events) is split by SOURCES.
 Every rank prepares all N events and all M anchors, but builds the pair plan of its own contiguous share
@@ -25,7 +33,7 @@ import torch
 
 from . import _lib as L
 from .events import EventPacket
-from .objectives import AnchoredExact, _fused_kind
+from .objectives import AnchoredExact, AnchoredSliced, _fused_kind, slice_counts
 
 
 def shard_range(n: int, rank: int, world: int) -> tuple[int, int]:
@@ -136,3 +144,74 @@ class ShardedAnchoredExact(AnchoredExact):
         ls = _ShardedExact.apply(motion.theta, ev.xy, ev.t, ev.b, anchors, u if self.dequantize else None,
                                  z if self.smooth_anchors else None, spec, src, self.group)
         return ls, anchors
+
+
+class _AllReduceSum(torch.autograd.Function):
+    """y = the sum over the ranks of x; the gradient of each rank's x is the sum over the ranks of dL/dy
+    (every rank's loss reads the same y)."""
+
+    @staticmethod
+    def forward(ctx, x, group):
+        ctx.group = group
+        return allreduce_sum(x.detach().clone(), group)
+
+    @staticmethod
+    def backward(ctx, g):
+        return allreduce_sum(g.contiguous().clone(), ctx.group), None
+
+
+def allreduce_sum_autograd(x: torch.Tensor, group=None) -> torch.Tensor:
+    """Differentiable all-reduce (sum) over ``group``: see :class:`_AllReduceSum`."""
+    return _AllReduceSum.apply(x, group)
+
+
+class ShardedAnchoredSliced(AnchoredSliced):
+    """AnchoredSliced over windows whose events are split across the ranks of ``group`` (the north star's
+    multi-GPU design for the splat path: local splat, NCCL all-reduce of the density, local gather and score).
+
+    Every rank passes the same events, motion and noise.  Rank r takes the contiguous share
+    ``shard_range(ev.n, r, world)`` of the events as its sources and anchor candidates.  ``log_scores``
+    returns the scores of the rank's own anchors (ordered by slice, then event index) and their global
+    event indices; :meth:`__call__` returns this rank's part of the loss, -sum(ls_r) / M (M = anchors of
+    all ranks), whose sum over the ranks is the loss -mean(ls).  After ``backward``,
+    :meth:`reduce_gradients` sums the parameter gradients over the ranks (each rank's gradient holds its
+    own sources and anchors).  n_anchors_per_slice (a random subset of each slice over the whole window) is
+    not supported here."""
+
+    def __init__(self, *args, group=None, rank: Optional[int] = None, world: Optional[int] = None, **kw):
+        super().__init__(*args, **kw)
+        if self.nap is not None:
+            raise ValueError("ShardedAnchoredSliced: n_anchors_per_slice draws over the whole window; not sharded")
+        import torch.distributed as dist
+        live = dist.is_available() and dist.is_initialized()
+        self.group = group
+        self.rank = rank if rank is not None else (dist.get_rank(group) if live else 0)
+        self.world = world if world is not None else (dist.get_world_size(group) if live else 1)
+
+    def log_scores(self, ev: EventPacket, motion, anchor_mask=None, source_mask=None, noise=None):
+        e0, e1 = shard_range(ev.n, self.rank, self.world)
+        st = self._setup(ev, noise, anchor_mask, source_mask, e0, e1)
+        img_r, per_kb_r = self._density(st, motion)
+        img = allreduce_sum_autograd(img_r, self.group)
+        per_kb = allreduce_sum(per_kb_r, self.group)  # integer-valued: exact in fp32 below 2^24 per bin
+        counts = allreduce_sum(slice_counts(ev, t=st["t"], b=st["b"]), self.group) if self.visibility else None
+        picked = self._pick(st)
+        if picked is None:  # no anchors here: an empty result that still reads the density, so that the
+            z0 = img.reshape(-1)[:0]  # backward all-reduce runs on this rank as on the others
+            return z0, torch.zeros(0, dtype=torch.long, device=ev.device)
+        ai, ka = picked
+        return self._scores(st, motion, img, per_kb, counts, ai, ka), ai + e0
+
+    def __call__(self, ev, motion, noise=None):
+        ls, _ = self.log_scores(ev, motion, noise=noise)
+        m = allreduce_sum(torch.tensor([float(ls.numel())], device=ls.device), self.group)
+        part = -ls.sum() / m.clamp(min=1)[0]
+        total = allreduce_sum(part.detach().clone(), self.group)
+        return {"loss": part, "score": -total}
+
+    def reduce_gradients(self, tensors) -> None:
+        """Sum the ``.grad`` of each tensor over the ranks (after backward)."""
+        for p in tensors:
+            if p.grad is not None:
+                allreduce_sum(p.grad, self.group)
+

@@ -47,14 +47,19 @@ def count_keys(key: torch.Tensor, nbins: int, mask: Optional[torch.Tensor] = Non
 
 
 @torch.no_grad()
-def slice_counts(ev: EventPacket, n_check: int = 16) -> torch.Tensor:
+def slice_counts(ev: EventPacket, n_check: int = 16, t: Optional[torch.Tensor] = None,
+                 b: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Per-batch event counts in ``n_check`` equal time slices (ats.py:40-42), as exact integer counts
-    (not an accumulating scatter of ones), float32 (B, n_check)."""
-    sl = torch.clamp((ev.t * n_check).long(), 0, n_check - 1)
-    key = torch.where((ev.b >= 0) & (ev.b < ev.batch_size), ev.b * n_check + sl, -1)
+    (not an accumulating scatter of ones), float32 (B, n_check); of the events (t, b) when given (a share of
+    the window's events), else of all of ``ev``'s."""
+    t = ev.t if t is None else t
+    b = ev.b if b is None else b
+    sl = torch.clamp((t * n_check).long(), 0, n_check - 1)
+    key = torch.where((b >= 0) & (b < ev.batch_size), b * n_check + sl, -1)
     return count_keys(key, ev.batch_size * n_check).view(ev.batch_size, n_check).to(torch.float32)
 
 
+@torch.no_grad()
 def visible_fraction(motion, xa, ta, ba, ev: EventPacket, tau: float, n_check: int = 16,
                      counts: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Exposure correction (atl/objectives/ats.py:31-50): fraction of the anchor's source mass recorded
@@ -73,24 +78,21 @@ def visible_fraction(motion, xa, ta, ba, ev: EventPacket, tau: float, n_check: i
                                               float(tau), int(n_check), L.ptr(out), L.ptr(scratch), L.stream()),
                 "visible_fraction")
         return out.to(ta.dtype)
-    # other motion models: the same computation with the motion's own transport (torch ops on the device)
+    # other motion models: the anchors moved to all check centres in one call of the motion's own transport
     edges = torch.linspace(0, 1, n_check + 1, device=ev.device)
-    if getattr(motion, "_device_transport", None) is not None and motion._device_transport(xa, ta):
-        if counts is None:
-            counts = slice_counts(ev, n_check)
-        cen = (0.5 * (edges[:-1] + edges[1:])).contiguous()
-        return motion.visible_fraction(xa, ta, ba, counts.contiguous(), cen, float(tau), ev.height, ev.width)
-    centres = (0.5 * (edges[:-1] + edges[1:])).tolist()  # the fp32 centres, read back once
+    cen = (0.5 * (edges[:-1] + edges[1:])).contiguous()  # the fp32 centres
     if counts is None:
         counts = slice_counts(ev, n_check)
-    vis = torch.zeros_like(ta); tot = torch.zeros_like(ta)
-    for k in range(n_check):
-        c = centres[k]
-        near = ((ta - c).abs() <= tau).to(ta.dtype)
-        y = motion.transport(xa, ta, c, ba)
-        inside = ((y[:, 0] >= 0) & (y[:, 0] <= ev.width - 1) & (y[:, 1] >= 0) & (y[:, 1] <= ev.height - 1)).to(ta.dtype)
-        w = counts[ba, k] * near
-        vis += w * inside; tot += w
+    if getattr(motion, "_device_transport", None) is not None and motion._device_transport(xa, ta):
+        return motion.visible_fraction(xa, ta, ba, counts.contiguous(), cen, float(tau), ev.height, ev.width)
+    M = ta.shape[0]
+    y = motion.transport(xa.repeat(n_check, 1), ta.repeat(n_check), cen.repeat_interleave(M),
+                         ba.repeat(n_check)).view(n_check, M, 2)
+    inside = (y[..., 0] >= 0) & (y[..., 0] <= ev.width - 1) & (y[..., 1] >= 0) & (y[..., 1] <= ev.height - 1)
+    near = (ta[None, :] - cen[:, None]).abs() <= tau
+    w = counts[ba].t() * near.to(ta.dtype)  # (n_check, M) integer-valued weights: every sum below is exact
+    vis = (w * inside.to(ta.dtype)).sum(0)
+    tot = w.sum(0)
     return (vis / tot.clamp(min=1)).clamp(min=1e-3)
 
 
@@ -332,30 +334,49 @@ class AnchoredSliced(Objective):
         All slices are evaluated at once: every event moved to every evaluated slice centre and splatted,
         weighted by its source mask, into a stack of len(slices) x B density images; every anchor's record
         (its position, the four log-determinant probes and its unsmoothed source copy) moved to its own
-        slice centre; one gather and the fused per-anchor score kernel (atlb_sliced_score).  Anchors come out in the reference's
-        order: slice by slice in ``slices`` order, ascending event index inside a slice (or the slice's
-        random subset when n_anchors_per_slice is set, drawn as the reference draws it)."""
-        S, dev, B = self.S, ev.device, ev.batch_size
+        slice centre; one gather and the fused per-anchor score kernel (atlb_sliced_score).  Anchors come
+        out in the reference's order: slice by slice in ``slices`` order, ascending event index inside a
+        slice (or the slice's random subset when n_anchors_per_slice is set, drawn as the reference draws
+        it)."""
+        st = self._setup(ev, noise, anchor_mask, source_mask, 0, ev.n)
+        picked = self._pick(st)
+        if picked is None:
+            z0 = ev.t.new_zeros(0)
+            return z0, z0.long()
+        ai, ka = picked
+        img, per_kb = self._density(st, motion)
+        counts = slice_counts(ev) if self.visibility else None
+        return self._scores(st, motion, img, per_kb, counts, ai, ka), ai
+
+    # -- stages (also used by x_b200.distributed.ShardedAnchoredSliced over a share of the events) --------
+    def _setup(self, ev: EventPacket, noise, anchor_mask, source_mask, e0: int, e1: int) -> dict:
+        """Draws, jittered positions, slice ranks, centres and source masks of the events [e0, e1)."""
+        S, dev = self.S, ev.device
         delta = 1.0 / S
         slices, u, z = self.draw(ev) if noise is None else noise
-        eps = self.eps_frac / (ev.height * ev.width)
-        xs = ev.xy
-        if self.dequantize:
-            xs = xs + (u - 0.5)
-        xsm = xs + self.sigma * z if self.smooth_anchors else xs
+        part = (e0, e1) != (0, ev.n)
+        cut = (lambda x: x[e0:e1]) if part else (lambda x: x)  # noqa: E731
+        xy, t, b = cut(ev.xy), cut(ev.t), cut(ev.b)
+        xs = xy + (cut(u) - 0.5) if self.dequantize else xy
+        xsm = xs + self.sigma * cut(z) if self.smooth_anchors else xs
         Sp = len(slices)
         # slice of each event, floor(t / delta) divided (not multiplied by a reciprocal) as the CPU reference
-        sl = torch.clamp(torch.floor(ev.t / torch.tensor(delta, dtype=ev.t.dtype, device=dev)), 0, S - 1).long()
+        sl = torch.clamp(torch.floor(t / torch.tensor(delta, dtype=t.dtype, device=dev)), 0, S - 1).long()
         rank_of = torch.full((S,), Sp, dtype=torch.long)
         rank_of[torch.tensor(slices, dtype=torch.long)] = torch.arange(Sp)
         rank = rank_of.to(dev)[sl]  # position of the event's slice in `slices` (Sp: not evaluated)
         if anchor_mask is not None:
-            rank = torch.where(anchor_mask, rank, torch.full_like(rank, Sp))
-        centres = torch.tensor([(s + 0.5) * delta for s in slices], dtype=ev.t.dtype).to(dev)
-        src = (ev.t[None, :] - centres[:, None]).abs() <= torch.tensor(self.tau + delta / 2, dtype=ev.t.dtype,
-                                                                       device=dev)
+            rank = torch.where(cut(anchor_mask), rank, torch.full_like(rank, Sp))
+        centres = torch.tensor([(s + 0.5) * delta for s in slices], dtype=t.dtype).to(dev)
+        src = (t[None, :] - centres[:, None]).abs() <= torch.tensor(self.tau + delta / 2, dtype=t.dtype, device=dev)
         if source_mask is not None:
-            src = src & source_mask[None, :]
+            src = src & cut(source_mask)[None, :]
+        return dict(ev=ev, xy=xy, t=t, b=b, xs=xs, xsm=xsm, Sp=Sp, rank=rank, centres=centres, src=src,
+                    eps=self.eps_frac / (ev.height * ev.width))
+
+    def _pick(self, st: dict):
+        """Anchors (indices into the setup's events) and their slice ranks, in the reference's order."""
+        Sp, rank, dev = st["Sp"], st["rank"], st["t"].device
         n_anc = count_keys(rank, Sp).tolist()  # the one read-back of the step
         rank_sorted, order = torch.sort(rank, stable=True)
         pieces, ranks, off = [], [], 0
@@ -369,24 +390,27 @@ class AnchoredSliced(Objective):
             pieces.append(ai)
             ranks.append(k)
         if not pieces:
-            z0 = ev.t.new_zeros(0)
-            return z0, z0.long()
+            return None
         if self.nap is None:
-            ai = order[:off]
-            ka = rank_sorted[:off]
-        else:
-            ai = torch.cat(pieces)
-            ka = torch.cat([torch.full((p.numel(),), k, dtype=torch.long, device=dev) for p, k in zip(pieces, ranks)])
+            return order[:off], rank_sorted[:off]
+        ka = torch.cat([torch.full((p.numel(),), k, dtype=torch.long, device=dev) for p, k in zip(pieces, ranks)])
+        return torch.cat(pieces), ka
 
-        # every event at every evaluated slice centre (Sp, N, 2), splatted with the slice's source mask as
-        # weights (zero weights add nothing) into images k * B + b
-        Y = self._events_at_centres(motion, xs, ev, centres)
-        wsrc = src.to(xs.dtype)
-        img = splat_slices(Y, wsrc, ev.b, B, ev.height, ev.width, self.sigma)
-        per_kb = count_keys(ev.b, B, wsrc).to(xs.dtype)  # sources per (slice, batch)
+    def _density(self, st: dict, motion):
+        """The setup's events at every evaluated slice centre, splatted with their source masks as weights
+        (zero weights add nothing) into images k * B + b; and the sources per (slice, batch)."""
+        ev, B = st["ev"], st["ev"].batch_size
+        Y = self._events_at_centres(motion, st["xs"], st["t"], st["b"], st["centres"])
+        wsrc = st["src"].to(st["xs"].dtype)
+        img = splat_slices(Y, wsrc, st["b"], B, ev.height, ev.width, self.sigma)
+        return img, count_keys(st["b"], B, wsrc).to(st["xs"].dtype)
 
+    def _scores(self, st: dict, motion, img, per_kb, counts, ai, ka):
+        """Log scores of the anchors ``ai`` (slice ranks ``ka``) against the full density stack ``img`` and
+        source counts ``per_kb``; ``counts``: the window's exposure-check slice counts."""
+        ev, B, xs, xsm = st["ev"], st["ev"].batch_size, st["xs"], st["xsm"]
+        xa, ta, ba, ca = xsm[ai], st["t"][ai], st["b"][ai], st["centres"][ka]
         # anchor records at their slice centres: [x +- d e_x, x +- d e_y,] a [, unsmoothed copy]
-        xa, ta, ba, ca = xsm[ai], ev.t[ai], ev.b[ai], centres[ka]
         recs = []
         if self.logdet:
             d = 0.5  # Motion.transport_logdet's default step (atl/motion/base.py:43)
@@ -407,21 +431,20 @@ class AnchoredSliced(Objective):
                                    ba.repeat_interleave(P)).reshape(-1, P, 2)
         img_a = ka * B + ba
         val = gather(img, pos[:, ia], img_a)
-        src_a = src[ka, ai].to(val.dtype)
+        src_a = st["src"][ka, ai].to(val.dtype)
         cnt = per_kb[ka, ba] - src_a
         vis = None
         if self.visibility:
-            vis = visible_fraction(motion, xa.detach(), ta, ba, ev, self.tau, counts=slice_counts(ev))
-        ls = _SlicedScore.apply(pos, val, cnt, vis, src_a, (P, ia, io, 0 if self.logdet else -1), self.sigma,
-                                0.5, eps, ev.height, ev.width)
-        return ls, ai
+            vis = visible_fraction(motion, xa.detach(), ta, ba, ev, self.tau, counts=counts)
+        return _SlicedScore.apply(pos, val, cnt, vis, src_a, (P, ia, io, 0 if self.logdet else -1), self.sigma,
+                                  0.5, st["eps"], ev.height, ev.width)
 
     @staticmethod
-    def _events_at_centres(motion, xs, ev: EventPacket, centres):
-        """(Sp, N, 2): every event at every centre.  Trajectories: one kernel, one origin solve per event;
+    def _events_at_centres(motion, xs, t, b, centres):
+        """(Sp, n, 2): every event at every centre.  Trajectories: one kernel, one origin solve per event;
         linear vector fields: each velocity once, x + v (c - t) (the reference's warp); other models: their
         transport of every (event, centre) pair."""
-        t, b, n, Sp = ev.t, ev.b, ev.n, centres.shape[0]
+        n, Sp = t.shape[0], centres.shape[0]
         if hasattr(motion, "transport_targets") and motion._device_transport(xs, t):
             return motion.transport_targets(xs, t, centres, b)
         if _fused_kind(motion) >= 0:

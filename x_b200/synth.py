@@ -30,7 +30,7 @@ def _gen(seed: int) -> torch.Generator:
 
 
 def _normalised_sorted_times(n: int, duration: float, g) -> torch.Tensor:
-    t = torch.sort(torch.rand(n, generator=g, dtype=torch.float64) * duration).values
+    t = torch.sort(torch.rand(n, generator=g, dtype=torch.float64, device=g.device) * duration).values
     if n > 0:
         t0, t1 = t.min(), t.max()
         t = (t - t0) / torch.clamp(t1 - t0, min=1e-12)
@@ -38,7 +38,7 @@ def _normalised_sorted_times(n: int, duration: float, g) -> torch.Tensor:
 
 
 def _polarity(n, g):
-    return torch.where(torch.rand(n, generator=g) > 0.5, 1.0, -1.0).to(torch.float32)
+    return torch.where(torch.rand(n, generator=g, device=g.device) > 0.5, 1.0, -1.0).to(torch.float32)
 
 
 def uniform_window(n: int, H: int, W: int, duration: float = 0.05, seed: int = 0, device="cpu") -> EventPacket:
@@ -68,21 +68,27 @@ def _gauss_blur(img: torch.Tensor, sigma: float) -> torch.Tensor:
 
 
 def textured_window(n: int, H: int, W: int, duration: float = 0.1, seed: int = 0, texture_sigma: float = 2.0,
-                    batch: int = 1, device="cpu") -> EventPacket:
-    """``batch`` windows of ``n`` events each, density proportional to |grad texture| (integer pixels)."""
-    g = _gen(seed)
+                    batch: int = 1, device="cpu", draw_on_device: bool = False) -> EventPacket:
+    """``batch`` windows of ``n`` events each, density proportional to |grad texture| (integer pixels).
+    ``draw_on_device``: draw with a seeded generator of ``device`` instead of the CPU one (other numbers,
+    same distributions; for windows of tens of millions of events)."""
+    if draw_on_device:
+        g = torch.Generator(device=device).manual_seed(int(seed))
+        dev = torch.device(device)
+    else:
+        g, dev = _gen(seed), torch.device("cpu")
     xs, ts, ps, bs = [], [], [], []
     for k in range(batch):
-        tex = _gauss_blur(torch.randn(1, H, W, generator=g), texture_sigma)[0]
+        tex = _gauss_blur(torch.randn(1, H, W, generator=g, device=dev), texture_sigma)[0]
         gx = torch.zeros_like(tex); gy = torch.zeros_like(tex)
         gx[:, 1:-1] = 0.5 * (tex[:, 2:] - tex[:, :-2])
         gy[1:-1, :] = 0.5 * (tex[2:, :] - tex[:-2, :])
         w = torch.sqrt(gx * gx + gy * gy).reshape(-1) + 1e-6
         idx = torch.multinomial(w / w.sum(), n, replacement=True, generator=g)
-        xs.append(torch.stack([(idx % W).float(), (idx // W).float()], 1))
+        xs.append(torch.stack([(idx % W).float(), (idx // W).float()], 1).to(dev))
         ts.append(_normalised_sorted_times(n, duration, g))
         ps.append(_polarity(n, g))
-        bs.append(torch.full((n,), k, dtype=torch.long))
+        bs.append(torch.full((n,), k, dtype=torch.long, device=dev))
     return EventPacket(torch.cat(xs), torch.cat(ts), torch.cat(ps), torch.cat(bs), batch, H, W).to(device)
 
 
