@@ -205,8 +205,8 @@ __global__ void __launch_bounds__(kThreads) k_order_count(PlanConsts P, const fl
 __global__ void __launch_bounds__(kThreads) k_order_scatter(PlanConsts P, const float4* __restrict__ ev4,
                                                             const float* __restrict__ t,
                                                             const long long* __restrict__ b, long long N,
-                                                            long long id0, const int* __restrict__ ostart,
-                                                            int* __restrict__ ocursor, float4* __restrict__ XVo,
+                                                            long long id0, int* __restrict__ ocursor,
+                                                            float4* __restrict__ XVo,
                                                             int4* __restrict__ TBo) {
   const long long stride = (long long)gridDim.x * blockDim.x;
   for (long long j = blockIdx.x * (long long)blockDim.x + threadIdx.x; j < N; j += stride) {
@@ -214,7 +214,7 @@ __global__ void __launch_bounds__(kThreads) k_order_scatter(PlanConsts P, const 
     const float tj = t[j];
     const int bj = (int)b[j];
     const int key = order_key(P, e, tj, bj);
-    const int pos = ostart[key] + atomicAdd(ocursor + key, 1);
+    const int pos = atomicAdd(ocursor + key, 1);  // the cursors start at the offsets
     XVo[pos] = e;
     TBo[pos] = make_int4(__float_as_int(tj), bj, (int)(id0 + j), 0);
   }
@@ -254,11 +254,11 @@ __global__ void __launch_bounds__(kThreads) k_fast_count_ordered(PlanConsts P, c
 }
 
 // Entries of the ordered events: the count pass's keys, one cursor atomic per distinct cell of a warp, and
-// the lanes of a cell writing consecutive slots.  One event per lane, its slices in an inner loop.
+// the lanes of a cell writing consecutive slots.  One event per lane, its slices in an inner loop.  The
+// cursors start at the cells' offsets (the scan sets them so), so an atomic returns an absolute slot.
 __global__ void __launch_bounds__(kThreads) k_fast_scatter_ordered(PlanConsts P, const float4* __restrict__ XVo,
                                                                    const int4* __restrict__ TBo, long long N,
                                                                    const int* __restrict__ KEY,
-                                                                   const int* __restrict__ start,
                                                                    int* __restrict__ cursor, float4* __restrict__ YV,
                                                                    float2* __restrict__ TI) {
   const int lane = threadIdx.x & 31;
@@ -294,10 +294,7 @@ __global__ void __launch_bounds__(kThreads) k_fast_scatter_ordered(PlanConsts P,
       }
 #pragma unroll
       for (int u = 0; u < kSB; ++u) {
-        const int leader = __ffs(grp[u]) - 1;
-        int b = 0;
-        if (key[u] >= 0 && lane == leader) b = start[key[u]] + base[u];
-        b = __shfl_sync(0xffffffffu, b, leader);
+        const int b = __shfl_sync(0xffffffffu, base[u], __ffs(grp[u]) - 1);
         if (key[u] >= 0) {
           float yx, yy;
           transported(P, e.x, e.y, e.z, e.w, tj, s0 + u, &yx, &yy);
@@ -344,7 +341,6 @@ __global__ void __launch_bounds__(kThreads) k_fast_anchor_scatter(PlanConsts P, 
                                                                   const long long* __restrict__ anc_b, long long M,
                                                                   const float4* __restrict__ ev4,
                                                                   const float* __restrict__ SC,
-                                                                  const int* __restrict__ start,
                                                                   int* __restrict__ cursor, float4* __restrict__ XT,
                                                                   int4* __restrict__ XK) {
   const long long stride = (long long)gridDim.x * blockDim.x;
@@ -354,7 +350,7 @@ __global__ void __launch_bounds__(kThreads) k_fast_anchor_scatter(PlanConsts P, 
     int g, fy, fx, cx, cy;
     const long long key = fast_anchor_key(P, a, ba, &g, &fy, &fx, &cx, &cy);
     if (key < 0) continue;
-    const int p = start[key] + atomicAdd(cursor + key, 1);
+    const int p = atomicAdd(cursor + key, 1);  // the cursors start at the offsets
     const int s = (int)(g - ba * P.S);
     const float self = self_term(P, C, ev4, __float_as_int(a.w), a.x, a.y, a.z, sub_rn(a.z, SC[s]), (int)ba, s, cx, cy);
     XT[p] = make_float4(a.x, a.y, a.z, self);
@@ -837,22 +833,20 @@ int exact_forward(const atlb_exact_cfg& c, const float* t, const long long* b, l
     const float4* ev = (const float4*)ev4 + j0;
     cudaMemsetAsync(w.ocount, 0, (size_t)nkey * 4, s);
     launch(k_order_count, grid_for(ns), kThreads, 0, s, P, ev, t + j0, b + j0, ns, w.ocount);
-    exclusive_scan<int>(w.ocount, nkey, w.partials, w.ostart, s);
-    launch(k_order_scatter, grid_for(ns), kThreads, 0, s, P, ev, t + j0, b + j0, ns, j0, (const int*)w.ostart,
-           w.ocount, w.XVo, w.TBo);
+    exclusive_scan<int>(w.ocount, nkey, w.partials, w.ostart, s, /*cursors=*/true);
+    launch(k_order_scatter, grid_for(ns), kThreads, 0, s, P, ev, t + j0, b + j0, ns, j0, w.ocount, w.XVo, w.TBo);
     launch(k_fast_count_ordered, grid_for(ns), kThreads, 0, s, P, (const float4*)w.XVo, (const int4*)w.TBo,
            ns, w.counts, w.KEY);
   }
   if (M > 0) launch(k_fast_anchor_count, grid_for(M), kThreads, 0, s, P, (const float4*)anc4, anc_b, M, w.acounts);
-  exclusive_scan<int>(w.counts, ncell, w.partials, w.start, s);
+  exclusive_scan<int>(w.counts, ncell, w.partials, w.start, s, /*cursors=*/true);
   if (ns > 0)
     launch(k_fast_scatter_ordered, grid_for(ns), kThreads, 0, s, P, (const float4*)w.XVo, (const int4*)w.TBo,
-           ns, (const int*)w.KEY, (const int*)w.start, w.counts, w.YV, w.TI);
-  exclusive_scan<int>(w.acounts, ncell, w.partials, w.astart, s);
+           ns, (const int*)w.KEY, w.counts, w.YV, w.TI);
+  exclusive_scan<int>(w.acounts, ncell, w.partials, w.astart, s, /*cursors=*/true);
   if (M > 0)
     launch(k_fast_anchor_scatter, grid_for(M), kThreads, 0, s, P, make_pair_consts(c.h, c.tau, c.cut),
-           (const float4*)anc4, anc_b, M, (const float4*)ev4, (const float*)w.SC, (const int*)w.astart, w.acounts,
-           w.XT, w.XK);
+           (const float4*)anc4, anc_b, M, (const float4*)ev4, (const float*)w.SC, w.acounts, w.XT, w.XK);
   if (side) {  // the pair kernels below read den
     cudaEventRecord(side->join, norm_s);
     cudaStreamWaitEvent(s, side->join, 0);

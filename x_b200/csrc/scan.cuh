@@ -83,8 +83,9 @@ __global__ void __launch_bounds__(kScanThreads) k_scan_partials_scan(long long* 
   if (threadIdx.x == 0) partials[nchunks] = carry;
 }
 
-// offsets[i] = exclusive prefix (OutT = long long or int); offsets[n] = total; counts[i] = 0.
-template <typename OutT>
+// offsets[i] = exclusive prefix (OutT = long long or int); offsets[n] = total; counts[i] = 0, or (CURSORS)
+// counts[i] = offsets[i], so that a scatter's atomicAdd on counts returns absolute slots.
+template <typename OutT, bool CURSORS = false>
 __global__ void __launch_bounds__(kScanThreads) k_scan_final(int* __restrict__ counts, long long n,
                                                              const long long* __restrict__ partials,
                                                              OutT* __restrict__ offsets) {
@@ -98,14 +99,14 @@ __global__ void __launch_bounds__(kScanThreads) k_scan_final(int* __restrict__ c
       ((reinterpret_cast<uintptr_t>(counts) & 15) == 0)) {
     const int o0 = (int)ex, o1 = o0 + v[0], o2 = o1 + v[1], o3 = o2 + v[2];
     *reinterpret_cast<int4*>(offsets + base) = make_int4(o0, o1, o2, o3);
-    *reinterpret_cast<int4*>(counts + base) = make_int4(0, 0, 0, 0);
+    *reinterpret_cast<int4*>(counts + base) = CURSORS ? make_int4(o0, o1, o2, o3) : make_int4(0, 0, 0, 0);
   } else {
 #pragma unroll
     for (int q = 0; q < kScanItems; ++q) {
       const long long i = base + q;
       if (i < n) {
         offsets[i] = (OutT)ex;
-        counts[i] = 0;
+        counts[i] = CURSORS ? (int)ex : 0;
       }
       ex += v[q];
     }
@@ -113,9 +114,11 @@ __global__ void __launch_bounds__(kScanThreads) k_scan_final(int* __restrict__ c
   if (blockIdx.x == 0 && threadIdx.x == 0) offsets[n] = (OutT)partials[gridDim.x];
 }
 
-// counts[0..n) -> offsets[0..n] (exclusive, offsets[n] = total); counts zeroed.
+// counts[0..n) -> offsets[0..n] (exclusive, offsets[n] = total); counts zeroed, or (cursors) set to the
+// offsets (int offsets only).
 template <typename OutT>
-inline void exclusive_scan(int* counts, long long n, long long* partials, OutT* offsets, cudaStream_t s) {
+inline void exclusive_scan(int* counts, long long n, long long* partials, OutT* offsets, cudaStream_t s,
+                           bool cursors = false) {
   const long long nch = scan_nchunks(n);
   if (nch == 0) {
     cudaMemsetAsync(offsets, 0, sizeof(OutT), s);
@@ -123,7 +126,10 @@ inline void exclusive_scan(int* counts, long long n, long long* partials, OutT* 
   }
   launch(k_scan_partials, (unsigned)nch, kScanThreads, 0, s, counts, n, partials);
   launch(k_scan_partials_scan, 1, kScanThreads, 0, s, partials, nch);
-  launch(k_scan_final<OutT>, (unsigned)nch, kScanThreads, 0, s, counts, n, partials, offsets);
+  if (cursors)
+    launch(k_scan_final<OutT, true>, (unsigned)nch, kScanThreads, 0, s, counts, n, partials, offsets);
+  else
+    launch(k_scan_final<OutT, false>, (unsigned)nch, kScanThreads, 0, s, counts, n, partials, offsets);
 }
 
 }  // namespace
