@@ -90,10 +90,16 @@ __global__ void __launch_bounds__(kGThreads) k_gtile_count(GTiles T, const float
     for (int i = threadIdx.x; i < T.ntiles; i += blockDim.x) hist[i] = 0;
   __syncthreads();
   const long long n0 = blockIdx.x * chunk, n1 = min(n0 + chunk, N);
-  for (long long n = n0 + threadIdx.x; n < n1; n += blockDim.x) {
-    const float2 p = P[n];
-    const long long key = gauss_tile(T, p.x, p.y, mul_rn(Wt[n], norm), Bi[n], skip_zero);
-    if (key >= 0) atomicAdd(sm ? hist + key : counts + key, 1);
+  const int lane = threadIdx.x & 31;
+  for (long long nb = n0; nb < n1; nb += blockDim.x) {  // warp-uniform: one atomic per distinct tile of a warp
+    const long long n = nb + threadIdx.x;
+    long long key = -1;
+    if (n < n1) {
+      const float2 p = P[n];
+      key = gauss_tile(T, p.x, p.y, mul_rn(Wt[n], norm), Bi[n], skip_zero);
+    }
+    const unsigned grp = __match_any_sync(0xffffffffu, key);
+    if (key >= 0 && lane == __ffs(grp) - 1) atomicAdd(sm ? hist + key : counts + key, __popc(grp));
   }
   __syncthreads();
   if (sm)
@@ -114,10 +120,15 @@ __global__ void __launch_bounds__(kGThreads) k_gtile_scatter(GTiles T, const flo
   if (sm) {
     for (int i = threadIdx.x; i < T.ntiles; i += blockDim.x) hist[i] = 0;
     __syncthreads();
-    for (long long n = n0 + threadIdx.x; n < n1; n += blockDim.x) {
-      const float2 p = P[n];
-      const long long key = gauss_tile(T, p.x, p.y, mul_rn(Wt[n], norm), Bi[n], skip_zero);
-      if (key >= 0) atomicAdd(hist + key, 1);
+    for (long long nb = n0; nb < n1; nb += blockDim.x) {  // warp-uniform, as in k_gtile_count
+      const long long n = nb + threadIdx.x;
+      long long key = -1;
+      if (n < n1) {
+        const float2 p = P[n];
+        key = gauss_tile(T, p.x, p.y, mul_rn(Wt[n], norm), Bi[n], skip_zero);
+      }
+      const unsigned grp = __match_any_sync(0xffffffffu, key);
+      if (key >= 0 && (threadIdx.x & 31) == __ffs(grp) - 1) atomicAdd(hist + key, __popc(grp));
     }
     __syncthreads();
     for (int i = threadIdx.x; i < T.ntiles; i += blockDim.x) {
@@ -126,13 +137,25 @@ __global__ void __launch_bounds__(kGThreads) k_gtile_scatter(GTiles T, const flo
     }
     __syncthreads();
   }
-  for (long long n = n0 + threadIdx.x; n < n1; n += blockDim.x) {
-    const float2 p = P[n];
-    const float w = Wt[n];
-    const long long key = gauss_tile(T, p.x, p.y, mul_rn(w, norm), Bi[n], skip_zero);
+  const int lane = threadIdx.x & 31;
+  for (long long nb = n0; nb < n1; nb += blockDim.x) {  // warp-uniform: the lanes of a tile take consecutive slots
+    const long long n = nb + threadIdx.x;
+    long long key = -1;
+    float2 p = make_float2(0.f, 0.f);
+    float w = 0.f;
+    if (n < n1) {
+      p = P[n];
+      w = Wt[n];
+      key = gauss_tile(T, p.x, p.y, mul_rn(w, norm), Bi[n], skip_zero);
+    }
+    const unsigned grp = __match_any_sync(0xffffffffu, key);
+    const int leader = __ffs(grp) - 1;
+    int base = 0;
+    if (key >= 0 && lane == leader)
+      base = sm ? atomicAdd(hist + key, __popc(grp)) : start[key] + atomicAdd(cursor + key, __popc(grp));
+    base = __shfl_sync(0xffffffffu, base, leader);
     if (key < 0) continue;
-    const int slot = sm ? atomicAdd(hist + key, 1) : start[key] + atomicAdd(cursor + key, 1);
-    EV[slot] = make_float4(p.x, p.y, w, __int_as_float((int)n));
+    EV[base + __popc(grp & ((1u << lane) - 1u))] = make_float4(p.x, p.y, w, __int_as_float((int)n));
   }
 }
 

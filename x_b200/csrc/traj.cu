@@ -7,9 +7,11 @@
 //
 // The coefficients are read channels-last (B, Hq, Wq, 2K) with channels [y_1..y_K, x_1..x_K], so one tap of
 // a sample is 2K consecutive floats (16-byte vector loads when 2K is a multiple of 4).  The kernels are
-// instantiated per K (1..16) so that the per-event basis and channel sums live in registers.  Sums follow
-// the reference's order (taps in order, then over k); the basis powers are products (t^k by repeated
-// multiplication instead of pow), so values differ from the reference's in the last bits.
+// instantiated per K (1..16) so that the per-event basis and channel sums live in registers.  The final
+// sample follows the reference's order (the coefficient sample, taps in order, then the sum over k); the
+// fixed-point iterations sum tap by tap with fused multiply-adds (traj_disp_it, half the arithmetic); the
+// basis powers are products (t^k by repeated multiplication instead of pow).  Values differ from the
+// reference's in the last bits.
 // The backward recomputes the iterates and runs reverse mode through them: dL/dp_i = -J_d(p_i)^T dL/dp_{i+1}.
 // The coefficient gradient w_tap * g_k(t) * dL/dp of the samples of one coefficient cell is accumulated per
 // tap (the iterates of one event rarely leave their cell) and leaves with vector reds when the cell changes.
@@ -88,10 +90,9 @@ __device__ __forceinline__ void load_tap(const float* __restrict__ p, float (&f)
   }
 }
 
-// displacement d(p, t) = sum_k (cx_k, cy_k) g_k with c the bilinear sample at p (taps summed in order)
+// The coefficient sample at the taps T: c = sum_q w_q c_q (taps summed in order, as sample_grid does).
 template <int K>
-__device__ __forceinline__ float2 traj_disp(const TrajView& V, const Taps& T, const float (&g)[K]) {
-  float c[2 * K];
+__device__ __forceinline__ void traj_sample(const TrajView& V, const Taps& T, float (&c)[2 * K]) {
 #pragma unroll
   for (int ch = 0; ch < 2 * K; ++ch) c[ch] = 0.f;
 #pragma unroll
@@ -101,11 +102,68 @@ __device__ __forceinline__ float2 traj_disp(const TrajView& V, const Taps& T, co
 #pragma unroll
     for (int ch = 0; ch < 2 * K; ++ch) c[ch] = add_rn(c[ch], mul_rn(f[ch], T.w[q]));
   }
+}
+
+// sum_k (cx_k, cy_k) g_k of a coefficient sample
+template <int K>
+__device__ __forceinline__ float2 traj_dot(const float (&c)[2 * K], const float (&g)[K]) {
   float dx = 0.f, dy = 0.f;
 #pragma unroll
   for (int k = 0; k < K; ++k) {
     dx = add_rn(dx, mul_rn(c[K + k], g[k]));
     dy = add_rn(dy, mul_rn(c[k], g[k]));
+  }
+  return make_float2(dx, dy);
+}
+
+// displacement d(p, t) = sum_k (cx_k, cy_k) g_k with c the bilinear sample at p (the final sample of a
+// transport; a caller moving one point to several times samples once and takes one dot per time)
+template <int K>
+__device__ __forceinline__ float2 traj_disp(const TrajView& V, const Taps& T, const float (&g)[K]) {
+  float c[2 * K];
+  traj_sample<K>(V, T, c);
+  return traj_dot<K>(c, g);
+}
+
+// The displacement inside the fixed-point iterations, tap-major with fused multiply-adds:
+// d = sum_q w_q(p) D_q, D_q = sum_k c_{q,k} g_k (x and y channels) -- half the arithmetic of traj_disp (which
+// forms the coefficient sample first, as the reference's sample_grid does); the iterates differ from that
+// order in the last bits only.  D depends on the cell (the four taps) and the basis only, and the iterates
+// of one event rarely leave their cell, so D is kept in a CellDisp and the taps are read again only when
+// the cell changes.  Every kernel iterates with this function, so a backward that solves the iterates
+// again, and the records / targets kernels, reproduce the forward's iterates exactly.
+struct CellDisp {
+  long long base0;     // first tap of the cell whose sums are held; -1: none
+  float dx[4], dy[4];  // per tap q: D_q for the x and the y channels
+};
+
+template <int K>
+__device__ __forceinline__ void cell_fill(const TrajView& V, const Taps& T, const float (&g)[K], CellDisp& D) {
+  if (D.base0 == T.base[0]) return;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    float f[2 * K];
+    load_tap<K>(V.C + T.base[q], f);
+    float sx = 0.f, sy = 0.f;
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      sx = fmaf(f[K + k], g[k], sx);
+      sy = fmaf(f[k], g[k], sy);
+    }
+    D.dx[q] = sx;
+    D.dy[q] = sy;
+  }
+  D.base0 = T.base[0];
+}
+
+template <int K>
+__device__ __forceinline__ float2 traj_disp_it(const TrajView& V, const Taps& T, const float (&g)[K], CellDisp& D) {
+  cell_fill<K>(V, T, g, D);
+  float dx = 0.f, dy = 0.f;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    dx = fmaf(T.w[q], D.dx[q], dx);
+    dy = fmaf(T.w[q], D.dy[q], dy);
   }
   return make_float2(dx, dy);
 }
@@ -129,8 +187,10 @@ __global__ void __launch_bounds__(kTThreads) k_traj_fwd(TrajView V, int mode, co
     float px = x.x, py = x.y;
     if (mode != 2) {
       traj_basis<K>(V, t[n], g);
+      CellDisp D;
+      D.base0 = -1;
       for (int i = 0; i < V.n_fp; ++i) {
-        const float2 d = traj_disp<K>(V, traj_taps(V, bb, px, py), g);
+        const float2 d = traj_disp_it<K>(V, traj_taps(V, bb, px, py), g, D);
         px = sub_rn(x.x, d.x);
         py = sub_rn(x.y, d.y);
       }
@@ -145,26 +205,62 @@ __global__ void __launch_bounds__(kTThreads) k_traj_fwd(TrajView V, int mode, co
   }
 }
 
+// J_d(p)^T for per-channel weights (Ux_k, Uy_k) (the transposed bilinear Jacobian; the clamp passes
+// gradient inside its range, floor none): (sum_q dw_q/dpx s_q, sum_q dw_q/dpy s_q) / tile with
+// s_q = sum_k (Ux_k cx_{q,k} + Uy_k cy_{q,k}).
+template <int K>
+__device__ __forceinline__ float2 traj_jt_u(const TrajView& V, const Taps& T, const float (&Ux)[K],
+                                            const float (&Uy)[K]) {
+  const float oax = 1.f - T.ax, oay = 1.f - T.ay;
+  const float dwx[4] = {-oay, oay, -T.ay, T.ay}, dwy[4] = {-oax, -T.ax, oax, T.ax};
+  float jx = 0.f, jy = 0.f;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    float f[2 * K];
+    load_tap<K>(V.C + T.base[q], f);
+    float sq = 0.f;
+#pragma unroll
+    for (int k = 0; k < K; ++k) sq += Ux[k] * f[K + k] + Uy[k] * f[k];
+    jx += dwx[q] * sq;
+    jy += dwy[q] * sq;
+  }
+  const float sx = T.gx_in ? 1.f / V.tile : 0.f, sy = T.gy_in ? 1.f / V.tile : 0.f;
+  return make_float2(jx * sx, jy * sy);
+}
+
 // J_d(p)^T (ux, uy) for one sample of d at p with basis g (the transposed bilinear Jacobian; the clamp passes
-// gradient inside its range, floor none).
+// gradient inside its range, floor none).  d = sum_q w_q(p) sum_k g_k c_{q,k}, so with
+// s_q = sum_k g_k (ux cx_{q,k} + uy cy_{q,k}) the result is (sum_q dw_q/dpx s_q, sum_q dw_q/dpy s_q) / tile:
+// one tap's coefficients are live at a time.
 template <int K>
 __device__ __forceinline__ float2 traj_jt(const TrajView& V, const Taps& T, const float (&g)[K], float ux,
                                           float uy) {
-  float f[4][2 * K];
-#pragma unroll
-  for (int q = 0; q < 4; ++q) load_tap<K>(V.C + T.base[q], f[q]);
-  float jxx = 0.f, jxy = 0.f, jyx = 0.f, jyy = 0.f;  // J = [[d dx/d px, d dx/d py], [d dy/d px, d dy/d py]]
-  const float oax = 1.f - T.ax, oay = 1.f - T.ay;
+  float Ux[K], Uy[K];
 #pragma unroll
   for (int k = 0; k < K; ++k) {
-    const int X = K + k;
-    jxx += g[k] * ((f[1][X] - f[0][X]) * oay + (f[3][X] - f[2][X]) * T.ay);
-    jxy += g[k] * ((f[2][X] - f[0][X]) * oax + (f[3][X] - f[1][X]) * T.ax);
-    jyx += g[k] * ((f[1][k] - f[0][k]) * oay + (f[3][k] - f[2][k]) * T.ay);
-    jyy += g[k] * ((f[2][k] - f[0][k]) * oax + (f[3][k] - f[1][k]) * T.ax);
+    Ux[k] = g[k] * ux;
+    Uy[k] = g[k] * uy;
+  }
+  return traj_jt_u<K>(V, T, Ux, Uy);
+}
+
+// traj_jt for the basis of a CellDisp (the iterations' basis g), from its per-tap sums:
+// s_q = ux Dx_q + uy Dy_q; the taps are read only when the cell changes.
+template <int K>
+__device__ __forceinline__ float2 traj_jt_it(const TrajView& V, const Taps& T, const float (&g)[K], CellDisp& D,
+                                             float ux, float uy) {
+  cell_fill<K>(V, T, g, D);
+  const float oax = 1.f - T.ax, oay = 1.f - T.ay;
+  const float dwx[4] = {-oay, oay, -T.ay, T.ay}, dwy[4] = {-oax, -T.ax, oax, T.ax};
+  float jx = 0.f, jy = 0.f;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const float sq = ux * D.dx[q] + uy * D.dy[q];
+    jx += dwx[q] * sq;
+    jy += dwy[q] * sq;
   }
   const float sx = T.gx_in ? 1.f / V.tile : 0.f, sy = T.gy_in ? 1.f / V.tile : 0.f;
-  return make_float2((jxx * ux + jyx * uy) * sx, (jxy * ux + jyy * uy) * sy);
+  return make_float2(jx * sx, jy * sy);
 }
 
 // Coefficient gradient of the samples that fall in one coefficient cell.  For samples with basis g the
@@ -255,8 +351,10 @@ __global__ void __launch_bounds__(kTThreads) k_traj_bwd(TrajView V, int mode, co
     float P[kTrajKMax + 1][2];  // iterates p_0 .. p_n (n_fp <= kTrajKMax), as the forward computes them
     P[0][0] = x.x;
     P[0][1] = x.y;
+    CellDisp D;
+    D.base0 = -1;
     for (int i = 0; i < nfp; ++i) {
-      const float2 d = traj_disp<K>(V, traj_taps(V, bb, P[i][0], P[i][1]), g);
+      const float2 d = traj_disp_it<K>(V, traj_taps(V, bb, P[i][0], P[i][1]), g, D);
       P[i + 1][0] = sub_rn(x.x, d.x);
       P[i + 1][1] = sub_rn(x.y, d.y);
     }
@@ -274,7 +372,7 @@ __global__ void __launch_bounds__(kTThreads) k_traj_bwd(TrajView V, int mode, co
     for (int i = nfp - 1; i >= 0; --i) {
       const Taps T = traj_taps(V, bb, P[i][0], P[i][1]);
       acc_add<K>(A, T, false, -gpx, -gpy, g, gd, gC);
-      const float2 j = traj_jt<K>(V, T, g, -gpx, -gpy);
+      const float2 j = traj_jt_it<K>(V, T, g, D, -gpx, -gpy);
       gpx = j.x;
       gpy = j.y;
     }
@@ -305,18 +403,21 @@ __global__ void __launch_bounds__(kTThreads) k_traj_vis(TrajView V, const float2
     float g[K];
     traj_basis<K>(V, t, g);
     float px = x.x, py = x.y;
+    CellDisp D;
+    D.base0 = -1;
     for (int it = 0; it < V.n_fp; ++it) {
-      const float2 d = traj_disp<K>(V, traj_taps(V, bb, px, py), g);
+      const float2 d = traj_disp_it<K>(V, traj_taps(V, bb, px, py), g, D);
       px = sub_rn(x.x, d.x);
       py = sub_rn(x.y, d.y);
     }
-    const Taps T = traj_taps(V, bb, px, py);
+    float cs[2 * K];  // the coefficient sample at the origin, shared by every check time
+    traj_sample<K>(V, traj_taps(V, bb, px, py), cs);
     float vis = 0.f, tot = 0.f;
     for (int k = 0; k < n_check; ++k) {
       const float c = __ldg(centres + k);
       const float near = fabsf(sub_rn(t, c)) <= tau ? 1.f : 0.f;
       traj_basis<K>(V, c, g);
-      const float2 d = traj_disp<K>(V, T, g);
+      const float2 d = traj_dot<K>(cs, g);
       const float yx = add_rn(px, d.x), yy = add_rn(py, d.y);
       const float inside = (yx >= 0.f && yx <= wmax && yy >= 0.f && yy <= hmax) ? 1.f : 0.f;
       const float w = mul_rn(__ldg(counts + (long long)bb * n_check + k), near);
@@ -353,8 +454,10 @@ __global__ void __launch_bounds__(kTThreads) k_traj_records_fwd(TrajView V, int 
     traj_basis<K>(V, t[n], g);
     const float2 x = xy[i];
     float px = x.x, py = x.y;
+    CellDisp D;
+    D.base0 = -1;
     for (int it = 0; it < V.n_fp; ++it) {
-      const float2 d = traj_disp<K>(V, traj_taps(V, bb, px, py), g);
+      const float2 d = traj_disp_it<K>(V, traj_taps(V, bb, px, py), g, D);
       px = sub_rn(x.x, d.x);
       py = sub_rn(x.y, d.y);
       if (iters) iters[(long long)it * NR + i] = make_float2(px, py);  // iterate-major: coalesced
@@ -392,6 +495,8 @@ __global__ void __launch_bounds__(kTThreads) k_traj_records_bwd(TrajView V, int 
       float P[kTrajKMax + 1][2];
       P[0][0] = x.x;
       P[0][1] = x.y;
+      CellDisp D;
+      D.base0 = -1;
       for (int it = 0; it < V.n_fp; ++it) {
         if (iters) {  // the forward's iterates
           const float2 q = iters[(long long)it * NR + i];
@@ -399,7 +504,7 @@ __global__ void __launch_bounds__(kTThreads) k_traj_records_bwd(TrajView V, int 
           P[it + 1][1] = q.y;
           continue;
         }
-        const float2 d = traj_disp<K>(V, traj_taps(V, bb, P[it][0], P[it][1]), g);
+        const float2 d = traj_disp_it<K>(V, traj_taps(V, bb, P[it][0], P[it][1]), g, D);
         P[it + 1][0] = sub_rn(x.x, d.x);
         P[it + 1][1] = sub_rn(x.y, d.y);
       }
@@ -410,7 +515,7 @@ __global__ void __launch_bounds__(kTThreads) k_traj_records_bwd(TrajView V, int 
       for (int it = V.n_fp - 1; it >= 0; --it) {
         const Taps Ti = traj_taps(V, bb, P[it][0], P[it][1]);
         acc_add<K>(A, Ti, false, -gpx, -gpy, g, gd, gC);
-        const float2 j = traj_jt<K>(V, Ti, g, -gpx, -gpy);
+        const float2 j = traj_jt_it<K>(V, Ti, g, D, -gpx, -gpy);
         gpx = j.x;
         gpy = j.y;
       }
@@ -479,23 +584,16 @@ __global__ void __launch_bounds__(kTThreads) k_traj_targets_fwd(TrajView V, cons
     float g[K];
     traj_basis<K>(V, t[n], g);
     float px = x.x, py = x.y;
+    CellDisp D;
+    D.base0 = -1;
     for (int i = 0; i < V.n_fp; ++i) {
-      const float2 d = traj_disp<K>(V, traj_taps(V, bb, px, py), g);
+      const float2 d = traj_disp_it<K>(V, traj_taps(V, bb, px, py), g, D);
       px = sub_rn(x.x, d.x);
       py = sub_rn(x.y, d.y);
     }
-    // the coefficient sample at the origin (taps summed in order, as traj_disp sums them)
-    const Taps Tp = traj_taps(V, bb, px, py);
+    // the coefficient sample at the origin (as traj_disp forms it), one dot product per target
     float c[2 * K];
-#pragma unroll
-    for (int ch = 0; ch < 2 * K; ++ch) c[ch] = 0.f;
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      float f[2 * K];
-      load_tap<K>(V.C + Tp.base[q], f);
-#pragma unroll
-      for (int ch = 0; ch < 2 * K; ++ch) c[ch] = add_rn(c[ch], mul_rn(f[ch], Tp.w[q]));
-    }
+    traj_sample<K>(V, traj_taps(V, bb, px, py), c);
     for (int j = 0; j < T; ++j) {
       const float* gd = s_gd + j * K;
       float dx = 0.f, dy = 0.f;
@@ -549,29 +647,17 @@ __global__ void __launch_bounds__(kTThreads) k_traj_targets_bwd(TrajView V, cons
     float P[kTrajKMax + 1][2];
     P[0][0] = x.x;
     P[0][1] = x.y;
+    CellDisp D;
+    D.base0 = -1;
     for (int i = 0; i < V.n_fp; ++i) {
-      const float2 d = traj_disp<K>(V, traj_taps(V, bb, P[i][0], P[i][1]), g);
+      const float2 d = traj_disp_it<K>(V, traj_taps(V, bb, P[i][0], P[i][1]), g, D);
       P[i + 1][0] = sub_rn(x.x, d.x);
       P[i + 1][1] = sub_rn(x.y, d.y);
     }
     const Taps Tp = traj_taps(V, bb, P[V.n_fp][0], P[V.n_fp][1]);
     // final samples: coefficient gradient w_q U_k, and dL/dp = sum_j u_j + J^T(U)
-    float jx = 0.f, jy = 0.f;
-    {
-      float f[4][2 * K];
-#pragma unroll
-      for (int q = 0; q < 4; ++q) load_tap<K>(V.C + Tp.base[q], f[q]);
-      const float oax = 1.f - Tp.ax, oay = 1.f - Tp.ay;
-#pragma unroll
-      for (int k = 0; k < K; ++k) {
-        const int X = K + k;
-        jx += Ux[k] * ((f[1][X] - f[0][X]) * oay + (f[3][X] - f[2][X]) * Tp.ay) +
-              Uy[k] * ((f[1][k] - f[0][k]) * oay + (f[3][k] - f[2][k]) * Tp.ay);
-        jy += Ux[k] * ((f[2][X] - f[0][X]) * oax + (f[3][X] - f[1][X]) * Tp.ax) +
-              Uy[k] * ((f[2][k] - f[0][k]) * oax + (f[3][k] - f[1][k]) * Tp.ax);
-      }
-    }
-    float gpx = sux + (Tp.gx_in ? jx / V.tile : 0.f), gpy = suy + (Tp.gy_in ? jy / V.tile : 0.f);
+    const float2 jU = traj_jt_u<K>(V, Tp, Ux, Uy);
+    float gpx = sux + jU.x, gpy = suy + jU.y;
     // the fixed-point part accumulates per tap (basis g); the final samples' w_q U_k joins the flush of the
     // origin's cell (the cell of the last iterate, where the reverse pass starts)
     CellAcc A;
@@ -623,7 +709,7 @@ __global__ void __launch_bounds__(kTThreads) k_traj_targets_bwd(TrajView V, cons
         A.a[q][0] -= Ti.w[q] * gpx;
         A.a[q][1] -= Ti.w[q] * gpy;
       }
-      const float2 j = traj_jt<K>(V, Ti, g, -gpx, -gpy);
+      const float2 j = traj_jt_it<K>(V, Ti, g, D, -gpx, -gpy);
       gpx = j.x;
       gpy = j.y;
     }

@@ -259,6 +259,21 @@ class AnchoredExact(Objective):
         return {"loss": -s, "score": s.detach()}
 
 
+def _spatial_order(motion, xy: torch.Tensor, b: torch.Tensor) -> Optional[torch.Tensor]:
+    """For trajectory motions evaluated on the device: a permutation of the points that sorts them by
+    (batch, coefficient tile of their position), so that the lanes of a warp read the same coefficient
+    samples; None for other motions (their transports read no per-position coefficients)."""
+    if not (hasattr(motion, "transport_targets") and motion._device_transport(xy, xy[:, 0])):
+        return None
+    if xy.shape[0] < 2:
+        return None
+    tile, Hq, Wq = float(motion.tile), motion.Hq, motion.Wq
+    cx = torch.clamp(torch.floor(xy[:, 0] / tile), 0, Wq - 1).to(torch.int32)
+    cy = torch.clamp(torch.floor(xy[:, 1] / tile), 0, Hq - 1).to(torch.int32)
+    key = (b.to(torch.int32) * Hq + cy) * Wq + cx
+    return torch.sort(key).indices
+
+
 class _SlicedScore(torch.autograd.Function):
     """AnchoredSliced's per-anchor score from the transported anchor records (atlb_sliced_score / _bwd):
     ls = log(eps + max(val - src loo(a, own), 0) / max(cnt vis, 1)) + log|det J| (ats.py:154-169),
@@ -400,14 +415,26 @@ class AnchoredSliced(Objective):
         """The setup's events at every evaluated slice centre, splatted with their source masks as weights
         (zero weights add nothing) into images k * B + b; and the sources per (slice, batch)."""
         ev, B = st["ev"], st["ev"].batch_size
-        Y = self._events_at_centres(motion, st["xs"], st["t"], st["b"], st["centres"])
-        wsrc = st["src"].to(st["xs"].dtype)
-        img = splat_slices(Y, wsrc, st["b"], B, ev.height, ev.width, self.sigma)
-        return img, count_keys(st["b"], B, wsrc).to(st["xs"].dtype)
+        xs, t, b, wsrc = st["xs"], st["t"], st["b"], st["src"].to(st["xs"].dtype)
+        per_kb = count_keys(b, B, wsrc).to(xs.dtype)
+        order = _spatial_order(motion, xs, b)
+        if order is not None:  # the events in coefficient-tile order: neighbouring lanes share their samples
+            xs, t, b, wsrc = xs[order], t[order], b[order], wsrc[:, order]
+        Y = self._events_at_centres(motion, xs, t, b, st["centres"])
+        return splat_slices(Y, wsrc, b, B, ev.height, ev.width, self.sigma), per_kb
 
     def _scores(self, st: dict, motion, img, per_kb, counts, ai, ka):
         """Log scores of the anchors ``ai`` (slice ranks ``ka``) against the full density stack ``img`` and
         source counts ``per_kb``; ``counts``: the window's exposure-check slice counts."""
+        order = _spatial_order(motion, st["xsm"][ai], st["b"][ai])
+        if order is not None:  # evaluated in coefficient-tile order, returned in the reference's order
+            inv = torch.empty_like(order)
+            inv[order] = torch.arange(order.numel(), device=order.device)
+            ls = self._scores_in_order(st, motion, img, per_kb, counts, ai[order], ka[order])
+            return ls.index_select(0, inv)  # (its backward scatters without sorting)
+        return self._scores_in_order(st, motion, img, per_kb, counts, ai, ka)
+
+    def _scores_in_order(self, st: dict, motion, img, per_kb, counts, ai, ka):
         ev, B, xs, xsm = st["ev"], st["ev"].batch_size, st["xs"], st["xsm"]
         xa, ta, ba, ca = xsm[ai], st["t"][ai], st["b"][ai], st["centres"][ka]
         # anchor records at their slice centres: [x +- d e_x, x +- d e_y,] a [, unsmoothed copy]
