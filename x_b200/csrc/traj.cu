@@ -469,7 +469,7 @@ __global__ void __launch_bounds__(kTThreads) k_traj_records_fwd(TrajView V, int 
 }
 
 template <int K>
-__global__ void __launch_bounds__(kTThreads) k_traj_records_bwd(TrajView V, int R, const float2* __restrict__ gy,
+__global__ void __launch_bounds__(kTThreads, 3) k_traj_records_bwd(TrajView V, int R, const float2* __restrict__ gy,
                                                                 const float2* __restrict__ xy,
                                                                 const float* __restrict__ t,
                                                                 const float* __restrict__ tdst, float tdst_s,
@@ -608,7 +608,7 @@ __global__ void __launch_bounds__(kTThreads) k_traj_targets_fwd(TrajView V, cons
 }
 
 template <int K>
-__global__ void __launch_bounds__(kTThreads) k_traj_targets_bwd(TrajView V, const float2* __restrict__ gy,
+__global__ void __launch_bounds__(kTThreads, 2) k_traj_targets_bwd(TrajView V, const float2* __restrict__ gy,
                                                                 const float2* __restrict__ xy,
                                                                 const float* __restrict__ t,
                                                                 const long long* __restrict__ b, long long N,

@@ -393,7 +393,8 @@ class AnchoredSliced(Objective):
         """Anchors (indices into the setup's events) and their slice ranks, in the reference's order."""
         Sp, rank, dev = st["Sp"], st["rank"], st["t"].device
         n_anc = count_keys(rank, Sp).tolist()  # the one read-back of the step
-        rank_sorted, order = torch.sort(rank, stable=True)
+        rank_sorted, order = torch.sort(rank.to(torch.int32), stable=True)  # 32-bit keys: a shorter radix sort
+        rank_sorted = rank_sorted.long()
         pieces, ranks, off = [], [], 0
         for k in range(Sp):
             ai = order[off:off + n_anc[k]]
@@ -437,20 +438,19 @@ class AnchoredSliced(Objective):
     def _scores_in_order(self, st: dict, motion, img, per_kb, counts, ai, ka):
         ev, B, xs, xsm = st["ev"], st["ev"].batch_size, st["xs"], st["xsm"]
         xa, ta, ba, ca = xsm[ai], st["t"][ai], st["b"][ai], st["centres"][ka]
-        # anchor records at their slice centres: [x +- d e_x, x +- d e_y,] a [, unsmoothed copy]
-        recs = []
-        if self.logdet:
-            d = 0.5  # Motion.transport_logdet's default step (atl/motion/base.py:43)
-            ex, ey = xa.new_tensor([d, 0.0]), xa.new_tensor([0.0, d])
-            recs += [xa + ex, xa - ex, xa + ey, xa - ey]
-        ia = len(recs)
-        recs.append(xa)
-        io = -1
+        # anchor records at their slice centres: [x +- d e_x, x +- d e_y,] a [, unsmoothed copy], the probes
+        # x + (d, 0), x - (d, 0), x + (0, d), x - (0, d) of Motion.transport_logdet (atl/motion/base.py:43-50,
+        # d = 0.5) made with one broadcast add
+        d = 0.5
+        offs = [[d, 0.0], [-d, 0.0], [0.0, d], [0.0, -d]] if self.logdet else []
+        ia = len(offs)
+        offs.append([0.0, 0.0])
+        io = ia + 1 if self.smooth_anchors else -1
+        P = len(offs) + (1 if self.smooth_anchors else 0)
+        rec = torch.empty(xa.shape[0], P, 2, dtype=xa.dtype, device=xa.device)
+        torch.add(xa[:, None, :], xa.new_tensor(offs)[None], out=rec[:, :ia + 1])
         if self.smooth_anchors:
-            io = len(recs)
-            recs.append(xs[ai])
-        P = len(recs)
-        rec = torch.stack(recs, 1)
+            rec[:, io] = xs[ai]
         if hasattr(motion, "transport_records") and motion._device_transport(xa, ta):
             pos = motion.transport_records(rec, ta, ca, ba)
         else:
