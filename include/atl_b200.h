@@ -232,8 +232,10 @@ int atlb_visible_fraction(int kind, const float* theta, int64_t B, int64_t Hg, i
  * layout) for gy = dL/dout into gcoeff.
  * ---------------------------------------------------------------------------------------------- */
 /* mode 0: out = transport(xy, t -> t_dst); 1: out = the origin p (the fixed point; t_dst unused);
- * 2: xy holds origins, out = p + d(p, t_dst) (t unused).  Modes 1 then 2 reproduce mode 0 exactly, so a
- * caller moving the same events to several times solves each origin once. */
+ * 2: xy holds origins, out = p + d(p, t_dst) (t unused); 3: out = the first coefficient pair (c_x1, c_y1)
+ * sampled at the origin, PixelTrajectories.velocity (atl/motion/trajectories.py:79-83) of the degree-1
+ * polynomial trajectories (t_dst unused).  Modes 1 then 2 reproduce mode 0 exactly, so a caller moving
+ * the same events to several times solves each origin once. */
 int atlb_traj_transport(int mode, const float* coeff, int64_t B, int64_t Hq, int64_t Wq, int64_t K, int basis,
                         const float* bezier_c, double offset, double tile, int64_t n_fp, const float* xy,
                         const float* t, const float* t_dst, double t_dst_s, const int64_t* b, int64_t N, float* out,
@@ -246,8 +248,8 @@ int atlb_traj_visible_fraction(const float* coeff, int64_t B, int64_t Hq, int64_
                                const float* ta, const int64_t* ba, int64_t M, const float* counts,
                                const float* centres, int64_t n_check, double tau, int64_t H, int64_t W, float* out,
                                atlb_stream_t stream);
-/* Backward of the same mode for gy = dL/dout: adds dL/dcoeff into gcoeff; mode 2 also writes gp (N,2) =
- * dL/d(its input origins). */
+/* Backward of the same mode (0..3) for gy = dL/dout: adds dL/dcoeff into gcoeff; mode 2 also writes
+ * gp (N,2) = dL/d(its input origins). */
 int atlb_traj_transport_bwd(int mode, const float* gy, const float* coeff, int64_t B, int64_t Hq, int64_t Wq,
                             int64_t K, int basis, const float* bezier_c, double offset, double tile, int64_t n_fp,
                             const float* xy, const float* t, const float* t_dst, double t_dst_s, const int64_t* b,
@@ -358,6 +360,16 @@ int atlb_flow_exact(int kind, const float* theta, int64_t B, int64_t H, int64_t 
 int atlb_flow_exact_bwd(int kind, const float* gy, const float* theta, int64_t B, int64_t H, int64_t W,
                         const float* xy, const float* t, const float* t_dst, double t_dst_s, const int64_t* b,
                         int64_t N, float* gtheta, float* gxy, atlb_stream_t stream);
+/* Exact transport of the dense velocity grid, DenseLinearFlow.transport with mode="exact"
+ * (atl/motion/parametric.py:72-80): `steps` classic RK4 steps (1..64) of the grid's bilinear field
+ * (theta (B, 2, Hg, Wg), the field of atlb_velocity) over dt = t_dst - t, rounded as the reference's torch
+ * ops.  The backward overwrites gtheta (B, 2, Hg, Wg) with dL/dtheta for gy = dL/dout. */
+int atlb_flow_rk4(const float* theta, int64_t B, int64_t Hg, int64_t Wg, int64_t H, int64_t W, const float* xy,
+                  const float* t, const float* t_dst, double t_dst_s, const int64_t* b, int64_t N, int steps,
+                  float* out, atlb_stream_t stream);
+int atlb_flow_rk4_bwd(const float* gy, const float* theta, int64_t B, int64_t Hg, int64_t Wg, int64_t H, int64_t W,
+                      const float* xy, const float* t, const float* t_dst, double t_dst_s, const int64_t* b,
+                      int64_t N, int steps, float* gtheta, atlb_stream_t stream);
 
 /* ----------------------------------------------------------------------------------------------
  * Opt-in device draws of the objective's noise.  No counterpart in the reference, which draws the

@@ -64,10 +64,10 @@ def test_anchored_exact_pixel_trajectories_k1_vs_reference():
     assert e["max_over_max"] <= 1e-5, e
 
 
-def _torch_transport(m, xy, t, t_dst, b):
-    from x_b200.motion import as_time
-    p = m.origin(xy, t, b)
-    return p + m.displacement(p, b, as_time(t_dst, t))
+def _torch_transport(coeff, K, basis, xy, t, t_dst, b, velocity=False):
+    from tests.torch_reference import trajectory_transport
+    td = t_dst if torch.is_tensor(t_dst) else torch.full_like(t, float(t_dst))
+    return trajectory_transport(coeff, K, basis, 4, 6, xy, t, td, b, velocity=velocity)
 
 
 @pytest.mark.parametrize("K,basis,per_event", [(10, "bezier", False), (3, "polynomial", True), (1, "polynomial", False),
@@ -88,8 +88,7 @@ def test_traj_transport_matches_torch(K, basis, per_event):
     y1 = m1.transport(xy, t, t_dst, b)
     (y1 * w).sum().backward()
     c2 = coeff.clone().requires_grad_(True)
-    m2 = PixelTrajectories(c2, K, basis_kind=basis, tile=4)
-    y2 = _torch_transport(m2, xy, t, t_dst, b)
+    y2 = _torch_transport(c2, K, basis, xy, t, t_dst, b)  # the torch statement of tests/torch_reference.py
     (y2 * w).sum().backward()
     np.testing.assert_allclose(y1.detach().cpu().numpy(), y2.detach().cpu().numpy(), rtol=1e-5, atol=1e-5)
     g1, g2 = c1.grad.cpu().numpy(), c2.grad.cpu().numpy()
@@ -98,9 +97,10 @@ def test_traj_transport_matches_torch(K, basis, per_event):
 
 
 def test_traj_visible_fraction_matches_torch():
-    """The fused exposure correction (origin solved once per anchor) against the torch loop of
-    atl/objectives/ats.py:31-50 over the same trajectories.  The inside test on positions that differ in the
-    last bits can flip for an anchor exactly on the image border, so a tiny share may differ."""
+    """The fused exposure correction (origin solved once per anchor, one coefficient sample for the 16 check
+    times) against the generic computation of atl/objectives/ats.py:31-50 over the same trajectories (16
+    transports per anchor, torch sums).  The check positions are identical; a tiny share may differ only if
+    an anchor sat exactly on the image border."""
     from x_b200 import synth
     from x_b200.motion import PixelTrajectories
     from x_b200.objectives import visible_fraction
@@ -109,8 +109,11 @@ def test_traj_visible_fraction_matches_torch():
     ev = synth.textured_window(20000, H, W, duration=0.1, seed=98, batch=B).to("cuda")
     coeff = (torch.nn.functional.avg_pool2d(torch.randn(B, 2 * K, H, W, generator=g), 9, 1, 4) * 4).cuda()
     m1 = PixelTrajectories(coeff, K, basis_kind="bezier", tile=4)
-    m2 = PixelTrajectories(coeff, K, basis_kind="bezier", tile=4)
-    m2._device_transport = lambda xy, t: False  # the torch transport
+
+    class Moved:  # the same trajectories seen only through transport: visible_fraction's generic path
+        def transport(self, xy, t, t_dst, b):
+            return m1.transport(xy, t, t_dst, b)
+    m2 = Moved()
     xa = ev.xy + torch.randn(ev.xy.shape, generator=g).cuda()
     for tau in (1.0, 0.3):
         v1 = visible_fraction(m1, xa, ev.t, ev.b, ev, tau).cpu().numpy()
@@ -183,4 +186,26 @@ def test_traj_records_and_targets_equal_transport(K, basis):
     assert torch.equal(yr1, yr2)
     assert torch.equal(yt1, yt2)
     e = assert_grad_parity(g2, g1, what=f"records / targets coefficient gradient (K={K})")
+    assert e["max_over_max"] <= 1e-5, e
+
+
+def test_traj_velocity_matches_torch():
+    """PixelTrajectories(K=1, polynomial).velocity on the device (mode 3: c_1 at the trajectory origin) against
+    the torch statement, values within 1e-5 and the coefficient gradient within 1e-5 norm-wise."""
+    from x_b200.motion import PixelTrajectories
+    g = torch.Generator().manual_seed(77)
+    B, H, W, n = 2, 48, 64, 20000
+    coeff = (torch.nn.functional.avg_pool2d(torch.randn(B, 2, H, W, generator=g), 9, 1, 4) * 30).cuda()
+    xy = torch.stack([torch.rand(n, generator=g) * (W + 16) - 8, torch.rand(n, generator=g) * (H + 16) - 8], 1).cuda()
+    t = torch.rand(n, generator=g).cuda()
+    b = torch.randint(0, B, (n,), generator=g).cuda()
+    w = torch.randn(n, 2, generator=g).cuda()
+    c1 = coeff.clone().requires_grad_(True)
+    v1 = PixelTrajectories(c1, 1, basis_kind="polynomial", tile=4).velocity(xy, t, b)
+    (v1 * w).sum().backward()
+    c2 = coeff.clone().requires_grad_(True)
+    v2 = _torch_transport(c2, 1, "polynomial", xy, t, 0.0, b, velocity=True)
+    (v2 * w).sum().backward()
+    np.testing.assert_allclose(v1.detach().cpu().numpy(), v2.detach().cpu().numpy(), rtol=1e-5, atol=1e-5)
+    e = assert_grad_parity(c1.grad.cpu().numpy(), c2.grad.cpu().numpy(), what="velocity coefficient gradient")
     assert e["max_over_max"] <= 1e-5, e

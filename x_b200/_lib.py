@@ -56,6 +56,9 @@ _SIGS = {
                                      _i64, _i64, _vp, _vp, _vp]),
     "atlb_flow_exact": (_int, [_int, _vp, _i64, _i64, _i64, _vp, _vp, _vp, _dbl, _vp, _i64, _vp, _vp]),
     "atlb_flow_exact_bwd": (_int, [_int, _vp, _vp, _i64, _i64, _i64, _vp, _vp, _vp, _dbl, _vp, _i64, _vp, _vp, _vp]),
+    "atlb_flow_rk4": (_int, [_vp, _i64, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _dbl, _vp, _i64, _int, _vp, _vp]),
+    "atlb_flow_rk4_bwd": (_int, [_vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _dbl, _vp, _i64, _int, _vp,
+                                 _vp]),
     "atlb_rng_uniform2": (_int, [ctypes.c_uint64, ctypes.c_uint64, _i64, _vp, _vp]),
     "atlb_rng_normal2": (_int, [ctypes.c_uint64, ctypes.c_uint64, _i64, _vp, _vp]),
     "atlb_kernel_launches": (ctypes.c_uint64, []),

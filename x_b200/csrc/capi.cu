@@ -52,6 +52,11 @@ int flow_exact(int kind, const float* theta, long long B, long long H, long long
 int flow_exact_bwd(int kind, const float* gy, const float* theta, long long B, long long H, long long W,
                    const float* xy, const float* t, const float* t_dst, double t_dst_s, const long long* b, long long N,
                    float* gtheta, float* gxy, cudaStream_t s);
+int flow_rk4_steps_max();
+int flow_rk4(const MotionView&, const float*, const float*, const float*, float, const long long*, long long, int,
+             float*, cudaStream_t);
+int flow_rk4_bwd(const MotionView&, const float*, const float*, const float*, const float*, float, const long long*,
+                 long long, int, float*, cudaStream_t);
 int rng_draw2(bool normal, unsigned long long seed, unsigned long long call, long long n, float* out,
               cudaStream_t s);
 int pair_fwd_noalloc(const float*, const float*, const float*, const long long*, const long long*, const float*,
@@ -629,7 +634,7 @@ int atlb_traj_transport(int mode, const float* coeff, int64_t B, int64_t Hq, int
   clear();
   NONNEG(N);
   NEED(xy, N); NEED(t, N); NEED(b, N); NEED(out, N);
-  if (mode < 0 || mode > 2) { set_error("%s: mode %d", __func__, mode); return ATLB_ERR_ARG; }
+  if (mode < 0 || mode > 3) { set_error("%s: mode %d", __func__, mode); return ATLB_ERR_ARG; }
   TrajView V;
   if (int st = make_traj(coeff, B, Hq, Wq, K, basis, bezier_c, offset, tile, n_fp, &V, __func__)) return st;
   return traj_transport(V, mode, xy, t, t_dst, (float)t_dst_s, LL(b), N, out, STREAM(stream));
@@ -642,7 +647,7 @@ int atlb_traj_transport_bwd(int mode, const float* gy, const float* coeff, int64
   clear();
   NONNEG(N);
   NEED(gy, N); NEED(xy, N); NEED(t, N); NEED(b, N);
-  if (mode < 0 || mode > 2) { set_error("%s: mode %d", __func__, mode); return ATLB_ERR_ARG; }
+  if (mode < 0 || mode > 3) { set_error("%s: mode %d", __func__, mode); return ATLB_ERR_ARG; }
   if (mode == 2) NEED(gp, N);
   if (!gcoeff) { set_error("%s: gcoeff is NULL", __func__); return ATLB_ERR_ARG; }
   TrajView V;
@@ -774,3 +779,36 @@ int atlb_count_keys(const int64_t* key, int64_t N, int64_t nbins, const float* m
   NEED(key, N); NEED(out, nbins * R);
   return count_keys(LL(key), N, nbins, mask, R, LLW(out), STREAM(stream));
 }
+
+static int check_rk4(int64_t B, int64_t Hg, int64_t Wg, int64_t H, int64_t W, int steps, const char* fn) {
+  if (B < 1 || Hg < 1 || Wg < 1 || H < 1 || W < 1 || steps < 1 || steps > flow_rk4_steps_max()) {
+    set_error("%s: grid %lld x %lld x %lld, image %lld x %lld, steps %d (1..%d)", fn, (long long)B, (long long)Hg,
+              (long long)Wg, (long long)H, (long long)W, steps, flow_rk4_steps_max());
+    return ATLB_ERR_ARG;
+  }
+  return ATLB_OK;
+}
+
+int atlb_flow_rk4(const float* theta, int64_t B, int64_t Hg, int64_t Wg, int64_t H, int64_t W, const float* xy,
+                  const float* t, const float* t_dst, double t_dst_s, const int64_t* b, int64_t N, int steps,
+                  float* out, atlb_stream_t stream) {
+  clear();
+  NONNEG(N);
+  if (int st = check_rk4(B, Hg, Wg, H, W, steps, __func__)) return st;
+  NEED(theta, B); NEED(xy, N); NEED(t, N); NEED(b, N); NEED(out, N);
+  return flow_rk4(make_motion_view(ATLB_MOTION_DENSE, theta, B, Hg, Wg, H, W), xy, t, t_dst, (float)t_dst_s, LL(b), N,
+                  steps, out, STREAM(stream));
+}
+
+int atlb_flow_rk4_bwd(const float* gy, const float* theta, int64_t B, int64_t Hg, int64_t Wg, int64_t H, int64_t W,
+                      const float* xy, const float* t, const float* t_dst, double t_dst_s, const int64_t* b,
+                      int64_t N, int steps, float* gtheta, atlb_stream_t stream) {
+  clear();
+  NONNEG(N);
+  if (int st = check_rk4(B, Hg, Wg, H, W, steps, __func__)) return st;
+  NEED(gy, N); NEED(theta, B); NEED(xy, N); NEED(t, N); NEED(b, N);
+  if (!gtheta) { set_error("%s: gtheta is NULL", __func__); return ATLB_ERR_ARG; }
+  return flow_rk4_bwd(make_motion_view(ATLB_MOTION_DENSE, theta, B, Hg, Wg, H, W), gy, xy, t, t_dst, (float)t_dst_s,
+                      LL(b), N, steps, gtheta, STREAM(stream));
+}
+

@@ -169,7 +169,10 @@ __device__ __forceinline__ float2 traj_disp_it(const TrajView& V, const Taps& T,
 }
 
 // mode 0: x -> transport(x, t -> t');  1: x -> origin p (the fixed point, t' unused);  2: p -> p + d(p, t')
-// (the input is an origin; t unused).  Modes 1 then 2 give exactly the values of mode 0.
+// (the input is an origin; t unused);  3: x -> the velocity of the degree-1 trajectory, the first coefficient
+// pair c_1 sampled at the origin (trajectories.py:79-83; t' unused), with the origin iterated in the
+// reference's order (traj_disp), so that the velocity -- which decides the exact path's pair tests -- is the
+// reference's to the bit.  Modes 1 then 2 give exactly mode 0.
 template <int K>
 __global__ void __launch_bounds__(kTThreads) k_traj_fwd(TrajView V, int mode, const float2* __restrict__ xy,
                                                         const float* __restrict__ t, const float* __restrict__ tdst,
@@ -190,13 +193,21 @@ __global__ void __launch_bounds__(kTThreads) k_traj_fwd(TrajView V, int mode, co
       CellDisp D;
       D.base0 = -1;
       for (int i = 0; i < V.n_fp; ++i) {
-        const float2 d = traj_disp_it<K>(V, traj_taps(V, bb, px, py), g, D);
+        // the velocity feeds the exact pair test, so its origin is iterated in the reference's own order
+        const Taps T = traj_taps(V, bb, px, py);
+        const float2 d = mode == 3 ? traj_disp<K>(V, T, g) : traj_disp_it<K>(V, T, g, D);
         px = sub_rn(x.x, d.x);
         py = sub_rn(x.y, d.y);
       }
     }
     if (mode == 1) {
       out[n] = make_float2(px, py);
+      continue;
+    }
+    if (mode == 3) {  // the first coefficient pair sampled at the origin (the basis e_1: c_1 exactly)
+#pragma unroll
+      for (int k = 0; k < K; ++k) g[k] = k == 0 ? 1.f : 0.f;
+      out[n] = traj_disp<K>(V, traj_taps(V, bb, px, py), g);
       continue;
     }
     traj_basis<K>(V, tdst ? tdst[n] : tdst_s, g);
@@ -341,7 +352,10 @@ __global__ void __launch_bounds__(kTThreads) k_traj_bwd(TrajView V, int mode, co
     float g[K], gd[K];
     const int nfp = mode == 2 ? 0 : V.n_fp;
     if (mode != 2) traj_basis<K>(V, t[n], g);
-    if (mode != 1) traj_basis<K>(V, tdst ? tdst[n] : tdst_s, gd);
+    if (mode == 0 || mode == 2) traj_basis<K>(V, tdst ? tdst[n] : tdst_s, gd);
+    if (mode == 3)  // out = d(p, e_1): the final basis is e_1 and there is no identity term
+#pragma unroll
+      for (int k = 0; k < K; ++k) gd[k] = k == 0 ? 1.f : 0.f;
     if (mode == 2)
 #pragma unroll
       for (int k = 0; k < K; ++k) g[k] = 0.f;
@@ -354,19 +368,20 @@ __global__ void __launch_bounds__(kTThreads) k_traj_bwd(TrajView V, int mode, co
     CellDisp D;
     D.base0 = -1;
     for (int i = 0; i < nfp; ++i) {
-      const float2 d = traj_disp_it<K>(V, traj_taps(V, bb, P[i][0], P[i][1]), g, D);
+      const Taps T = traj_taps(V, bb, P[i][0], P[i][1]);
+      const float2 d = mode == 3 ? traj_disp<K>(V, T, g) : traj_disp_it<K>(V, T, g, D);  // as the forward
       P[i + 1][0] = sub_rn(x.x, d.x);
       P[i + 1][1] = sub_rn(x.y, d.y);
     }
     CellAcc A;
     A.live = false;
     float gpx = u.x, gpy = u.y;
-    if (mode != 1) {  // y = p_n + d(p_n, t')
+    if (mode != 1) {  // y = p_n + d(p_n, t')  (mode 3: y = d(p_n, e_1))
       const Taps T = traj_taps(V, bb, P[nfp][0], P[nfp][1]);
       acc_add<K>(A, T, true, u.x, u.y, g, gd, gC);
       const float2 jt = traj_jt<K>(V, T, gd, u.x, u.y);
-      gpx = u.x + jt.x;
-      gpy = u.y + jt.y;
+      gpx = (mode == 3 ? 0.f : u.x) + jt.x;
+      gpy = (mode == 3 ? 0.f : u.y) + jt.y;
     }
     // p_{i+1} = x - d(p_i, t)
     for (int i = nfp - 1; i >= 0; --i) {

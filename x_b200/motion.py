@@ -1,11 +1,13 @@
-"""Motion models of stage 1 -- mirror of atl/motion/{base,parametric}.py for the models on the path.
+"""Motion models of stage 1 -- mirror of atl/motion/{base,parametric,trajectories}.py for the models on the path.
 
 ``Translation``, ``Affine`` and ``DenseLinearFlow`` evaluate their velocity field (and its gradient
 w.r.t. ``theta`` / the flow grid) in libatlb200 kernels that round exactly like the reference's torch
 CPU ops, so the pair plan built from the velocities is bit-identical.  ``transport`` in
-``mode="linear"`` is x + v(x) (t' - t); ``mode="exact"`` keeps the reference's closed-form matrix
-exponential (affine fields) or RK4 (dense fields) in torch ops on the device.  ``PixelTrajectories``
-(atl/motion/trajectories.py) keeps its torch transport (fixed-point inversion on the tile coefficients).
+``mode="linear"`` is x + v(x) (t' - t); ``mode="exact"`` is the closed-form flow of the affine fields
+(atlb_flow_exact) or RK4 of the dense grid (atlb_flow_rk4), both kernels.  ``PixelTrajectories``
+(atl/motion/trajectories.py) transports, solves origins and evaluates velocities in the trajectory
+kernels (atlb_traj_*).  There is no torch or CPU path: positions are data (no gradient), the
+parameters are CUDA tensors.
 """
 from __future__ import annotations
 
@@ -107,6 +109,38 @@ class _FlowExactFn(torch.autograd.Function):
         return gth.to(tdt), (None if gxy is None else gxy.to(xdt)), None, None, None, None, None, None
 
 
+class _FlowRK4Fn(torch.autograd.Function):
+    """RK4 transport of the dense velocity grid on the device (atlb_flow_rk4 / _bwd), differentiable w.r.t. the
+    grid (positions are data)."""
+
+    @staticmethod
+    def forward(ctx, grid, xy, t, t_dst, b, H, W, steps):
+        g = grid.detach().float().contiguous()
+        xyc, tc, bl = xy.detach().float().contiguous(), t.detach().float().contiguous(), b.contiguous().long()
+        if torch.is_tensor(t_dst) and t_dst.dim() > 0:
+            td, tds = t_dst.detach().float().contiguous().expand_as(tc).contiguous(), 0.0
+        else:
+            td, tds = None, float(t_dst)
+        B, _, Hg, Wg = g.shape
+        out = torch.empty_like(xyc)
+        L.check(L.lib().atlb_flow_rk4(L.ptr(g), B, Hg, Wg, H, W, L.ptr(xyc), L.ptr(tc), L.ptr(td), tds, L.ptr(bl),
+                                      tc.shape[0], int(steps), L.ptr(out), L.stream()), "flow_rk4")
+        ctx.save_for_backward(g, xyc, tc, bl, td if td is not None else tc.new_empty(0))
+        ctx.meta = (H, W, tds, td is not None, int(steps), grid.dtype, xy.dtype)
+        return out.to(xy.dtype)
+
+    @staticmethod
+    def backward(ctx, gy):
+        g, xyc, tc, bl, td = ctx.saved_tensors
+        H, W, tds, per_event, steps, gdt, _ = ctx.meta
+        B, _, Hg, Wg = g.shape
+        gg = torch.empty_like(g)
+        L.check(L.lib().atlb_flow_rk4_bwd(L.ptr(gy.contiguous().float()), L.ptr(g), B, Hg, Wg, H, W, L.ptr(xyc),
+                                          L.ptr(tc), L.ptr(td if per_event else None), tds, L.ptr(bl), tc.shape[0],
+                                          steps, L.ptr(gg), L.stream()), "flow_rk4_bwd")
+        return gg.to(gdt), None, None, None, None, None, None, None
+
+
 class VectorFieldMotion(Motion):
     """Autonomous velocity field v(x; theta) (parametric.py:84-145)."""
     n_params: int = 0
@@ -141,38 +175,15 @@ class VectorFieldMotion(Motion):
         if self.mode == "linear":
             dt = as_time(t_dst, t) - t
             return xy + self.field(xy, b) * dt[:, None]
-        if self.kind in (L.MOTION_TRANSLATION, L.MOTION_AFFINE) and xy.is_cuda:
+        if self.kind in (L.MOTION_TRANSLATION, L.MOTION_AFFINE):
             return _FlowExactFn.apply(self.theta, xy, t, t_dst, b, self.kind, self.H, self.W)
-        return self._runge_kutta(xy, as_time(t_dst, t) - t, b)
-
-    def _runge_kutta(self, x, dt, b):
-        """rk4_steps classic RK4 steps of dx/ds = v(x) over dt (per event): stage slopes at the start, twice at the
-        midpoint and at the end, combined with weights 1/6, 1/3, 1/3, 1/6."""
-        step = (dt / self.rk4_steps)[:, None]
-        half = 0.5 * step
-        for _ in range(self.rk4_steps):
-            s1 = self._field_any(x, b)
-            s2 = self._field_any(x + half * s1, b)
-            s3 = self._field_any(x + half * s2, b)
-            s4 = self._field_any(x + step * s3, b)
-            x = x + step * (s1 + 2 * s2 + 2 * s3 + s4) / 6
-        return x
-
-    def _field_any(self, xy, b):
-        """Field at positions that may carry autograd history (RK4 stages): evaluated with torch ops."""
-        return self.field(xy, b) if not xy.requires_grad else self.field_torch(xy, b)
-
-    def field_torch(self, xy, b):
-        raise NotImplementedError
+        return _FlowRK4Fn.apply(self.theta, xy, t, t_dst, b, self.H, self.W, self.rk4_steps)
 
 
 class Translation(VectorFieldMotion):
     """v = (tx, ty) (parametric.py:148-157)."""
     n_params = 2
     kind = L.MOTION_TRANSLATION
-
-    def field_torch(self, xy, b):
-        return self.theta[b]
 
     def affine_parts(self, b):
         z = self.theta.new_zeros(b.numel(), 2, 2)
@@ -188,9 +199,6 @@ class Affine(VectorFieldMotion):
         th = self.theta[b]
         return th[:, 2:6].view(-1, 2, 2), th[:, :2]
 
-    def field_torch(self, xy, b):
-        A, tr = self.affine_parts(b)
-        return tr + torch.bmm(A, (xy - self.c.to(xy))[..., None])[..., 0]
 
 
 class DenseLinearFlow(VectorFieldMotion):
@@ -208,11 +216,6 @@ class DenseLinearFlow(VectorFieldMotion):
     def theta(self):
         return self.grid
 
-    def field_torch(self, xy, b):
-        Hg, Wg = self.grid.shape[-2:]
-        gx = xy[:, 0] / max(self.W - 1, 1) * (Wg - 1)
-        gy = xy[:, 1] / max(self.H - 1, 1) * (Hg - 1)
-        return sample_grid(self.grid, torch.stack([gx, gy], 1), b)
 
     def upsample(self, factor: int = 2):
         """Refine the velocity grid by ``factor`` (parametric.py:282-289)."""
@@ -224,42 +227,11 @@ class DenseLinearFlow(VectorFieldMotion):
         return self
 
 
-def sample_grid(field: torch.Tensor, gpos: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
-    """Bilinear sample of a (B, C, Hg, Wg) field at grid coordinates, border clamp (parametric.py:296-312).
-    Torch ops; used for positions that carry autograd history (RK4 stages of ``mode='exact'``)."""
-    B, C, Hg, Wg = field.shape
-    gx = gpos[:, 0].clamp(0, Wg - 1)
-    gy = gpos[:, 1].clamp(0, Hg - 1)
-    x0 = torch.floor(gx).clamp(max=max(Wg - 2, 0)); y0 = torch.floor(gy).clamp(max=max(Hg - 2, 0))
-    ax, ay = gx - x0, gy - y0
-    x0, y0 = x0.long(), y0.long()
-    x1, y1 = (x0 + 1).clamp(max=Wg - 1), (y0 + 1).clamp(max=Hg - 1)
-    f = field.permute(0, 2, 3, 1).reshape(-1, C)
-    base = b * (Hg * Wg)
-
-    def at(yy, xx):
-        return f[base + yy * Wg + xx]
-    return (at(y0, x0) * ((1 - ax) * (1 - ay))[:, None] + at(y0, x1) * (ax * (1 - ay))[:, None] +
-            at(y1, x0) * ((1 - ax) * ay)[:, None] + at(y1, x1) * (ax * ay)[:, None])
-
-
-def basis(t: torch.Tensor, K: int, kind: str = "polynomial") -> torch.Tensor:
-    """(..., K) trajectory basis g_k(t) - g_k(0) (atl/motion/trajectories.py:26-37): t^k, or the degree-K
-    Bernstein polynomials B_{k,K}(t), k = 1..K (Bezier with the first control point pinned to the start)."""
-    t = t[..., None]
-    k = torch.arange(1, K + 1, device=t.device, dtype=t.dtype)
-    if kind == "polynomial":
-        return t ** k
-    if kind == "bezier":
-        logc = (math.lgamma(K + 1) - torch.lgamma(k + 1) - torch.lgamma(K - k + 1))
-        return torch.exp(logc) * t ** k * (1 - t) ** (K - k)
-    raise ValueError(kind)
-
-
 class _TrajTransport(torch.autograd.Function):
     """PixelTrajectories transport on the device (atlb_traj_transport), differentiable w.r.t. the tile
     coefficients.  mode 0: xy -> transport to t_dst; 1: xy -> trajectory origin; 2: xy are origins ->
-    position at t_dst (also differentiable w.r.t. those origins).  Event positions and times are data."""
+    position at t_dst (also differentiable w.r.t. those origins); 3: xy -> velocity of the degree-1
+    trajectories.  Event positions and times are data."""
 
     @staticmethod
     def forward(ctx, tile_c, xy, t, t_dst, b, model, mode):
@@ -390,27 +362,9 @@ class PixelTrajectories(Motion):
         self._bc = torch.exp(math.lgamma(K + 1) - torch.lgamma(k + 1) - torch.lgamma(K - k + 1)).contiguous()
         self._basis_id = {"polynomial": 0, "bezier": 1}.get(basis_kind, -1)
 
-    def _coeff_at(self, p, b):
-        g = (p - self.offset) / self.tile
-        c = sample_grid(self.tile_c, g, b)
-        cy, cx = c[:, :self.K], c[:, self.K:]
-        return torch.stack([cx, cy], -1)
-
-    def displacement(self, p, b, t):
-        g = basis(t, self.K, self.basis_kind)
-        return (self._coeff_at(p, b) * g[..., None]).sum(1)
-
-    def origin(self, xy, t, b):
-        p = xy
-        for _ in range(self.n_fp):
-            p = xy - self.displacement(p, b, t)
-        return p
-
     def transport(self, xy, t, t_dst, b):
-        if self._device_transport(xy, t):
-            return _TrajTransport.apply(self.tile_c, xy, t, t_dst, b, self, 0)
-        p = self.origin(xy, t, b)
-        return p + self.displacement(p, b, as_time(t_dst, t))
+        self._require_device(xy, t)
+        return _TrajTransport.apply(self.tile_c, xy, t, t_dst, b, self, 0)
 
     def origin_on_device(self, xy, t, b):
         """The trajectory origins of events (xy, t) (the fixed point of :meth:`origin`), on the device."""
@@ -437,11 +391,19 @@ class PixelTrajectories(Motion):
         return (self.tile_c.is_cuda and xy.is_cuda and self.assign == "invert" and self._basis_id >= 0
                 and self.K <= 16 and self.n_fp <= 16 and not xy.requires_grad and not t.requires_grad)
 
+    def _require_device(self, xy, t):
+        if not self._device_transport(xy, t):
+            raise NotImplementedError(
+                "x_b200 PixelTrajectories: the trajectory kernels need CUDA tensors, assign='invert', a polynomial or "
+                "Bezier basis, K <= 16, n_fixed_point <= 16 and positions without gradient (there is no torch path)")
+
     def velocity(self, xy, t, b):
+        """v = c_1 sampled at the trajectory origin of (xy, t) (trajectories.py:79-83), for the degree-1
+        polynomial trajectories (the only ones linear at the event), in the trajectory kernel's mode 3."""
         if not self.linear_at_event:
             raise NotImplementedError("per-event velocity only for the degree-1 polynomial prior")
-        p = self.origin(xy, t, b)
-        return self._coeff_at(p, b)[:, 0]
+        self._require_device(xy, t)
+        return _TrajTransport.apply(self.tile_c, xy, t, 0.0, b, self, 3)
 
     @torch.no_grad()
     def visible_fraction(self, xa, ta, ba, counts, centres, tau, H, W):
@@ -457,25 +419,6 @@ class PixelTrajectories(Motion):
                                                    centres.shape[0], float(tau), H, W, L.ptr(out), L.stream()),
                 "traj_visible_fraction")
         return out.to(ta.dtype)
-
-    def tile_trajectories(self, times: torch.Tensor) -> torch.Tensor:
-        """Positions (B, n_t, n_tiles, 2) of every tile trajectory at the given times."""
-        B, Hq, Wq, K = self.B, self.Hq, self.Wq, self.K
-        dev = self.tile_c.device
-        ys = torch.arange(Hq, device=dev, dtype=torch.float32) * self.tile + self.offset
-        xs = torch.arange(Wq, device=dev, dtype=torch.float32) * self.tile + self.offset
-        gy, gx = torch.meshgrid(ys, xs, indexing="ij")
-        p = torch.stack([gx, gy], -1).reshape(1, 1, -1, 2)
-        c = self.tile_c.reshape(B, 2, K, Hq * Wq)
-        cxy = torch.stack([c[:, 1], c[:, 0]], -1)
-        g = basis(times, K, self.basis_kind)
-        return p + torch.einsum("tk,bknc->btnc", g, cxy)
-
-    def flow_field(self, B, H, W, t0=0.0, t1=1.0):
-        times = torch.tensor([t0, t1], device=self.tile_c.device, dtype=torch.float32)
-        tr = self.tile_trajectories(times)
-        f = (tr[:, 1] - tr[:, 0]).reshape(self.B, self.Hq, self.Wq, 2).permute(0, 3, 1, 2)
-        return torch.nn.functional.interpolate(f, size=(H, W), mode="bilinear", align_corners=False)
 
     def regulariser_fields(self, B, H, W):
         return self.tile_c
