@@ -49,10 +49,11 @@ def parse():
     ap.add_argument("--dropin", action="store_true",
                     help="config2 through the stage-by-stage drop-in ops (device plan + ats_pair_fwd/bwd extension "
                          "calls, as atl's objective makes them) instead of the fused pipeline")
-    ap.add_argument("--workload", default="config2", choices=["config2", "config3", "config5", "splat"],
+    ap.add_argument("--workload", default="config2", choices=["config2", "config3", "config5", "splat", "tiles"],
                     help="config2: one 1M-event window per GPU (the headline); config5: one 64M-event window "
                          "on 1280x720 shared by all GPUs (sources split across ranks, NCCL all-reduce); splat: the "
-                         "Gaussian splat forward + backward of one slice of configuration 3 (sigma 1.5, 8 x 2M)")
+                         "Gaussian splat forward + backward of one slice of configuration 3 (sigma 1.5, 8 x 2M); "
+                         "tiles: the bilinear splat, gather and voxel grid on 1M points")
     ap.add_argument("--no-strong", action="store_true",
                     help="leave out the strong-scaling legs of the default line (configuration 5a and 3 sharded "
                          "over the --gpus ranks)")
@@ -843,6 +844,72 @@ def splat_arm(args):
     }))
 
 
+# ------------------------------------------------------------------------------------------------ tiled ops
+def tiles_arm(args):
+    """The tiled bilinear ops on a configuration-2-sized input (--windows windows of --events points on
+    640x480, weights 1): bilinear splat forward + backward, bilinear gather forward + backward (the image
+    tiles staged by TMA), and the 5-bin voxel grid.  value = points per second through all five ops."""
+    import torch
+    from x_b200 import _lib, get_ext, synth
+    n = args.events
+    B, C = args.windows if args.windows != 8 else 1, 5
+    ev = synth.textured_window(n, H, W, duration=0.1, seed=4000, batch=B)
+    g = torch.Generator().manual_seed(4001)
+    pos = (ev.xy + (torch.rand(ev.xy.shape, generator=g) - 0.5)).cuda()
+    w = torch.ones(pos.shape[0], device="cuda")
+    b, t, p = ev.b.cuda(), ev.t.cuda(), ev.p.cuda()
+    img = torch.randn(B, H, W, generator=g).cuda()
+    gval = torch.randn(pos.shape[0], generator=g).cuda()
+    ext = get_ext()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    ops = {
+        "splat_bilinear_fwd": lambda: ext.splat_bilinear_fwd(pos, w, b, B, H, W),
+        "splat_bilinear_bwd": lambda: ext.splat_bilinear_bwd(img, pos, w, b),
+        "gather_bilinear_fwd": lambda: ext.gather_bilinear_fwd(img, pos, b),
+        "gather_bilinear_bwd": lambda: ext.gather_bilinear_bwd(gval, img, pos, b),
+        "voxel_grid": lambda: ext.voxel_grid(pos, t, p, b, B, C, H, W),
+    }
+    # algorithmic bytes per point: positions 8, batch index 8, plus weight / value / time / polarity 4 each and
+    # the per-point outputs; the images are L2-resident (one read or write of B x H x W floats per call)
+    per_pt = {"splat_bilinear_fwd": 20, "splat_bilinear_bwd": 20 + 12, "gather_bilinear_fwd": 16 + 4,
+              "gather_bilinear_bwd": 20 + 8, "voxel_grid": 24}
+    for _ in range(max(args.warmup, 3)):
+        for f in ops.values():
+            f()
+    torch.cuda.synchronize()
+    L = _lib.load_library()
+    launches0 = L.atlb_kernel_launches()
+    per_op = {k: 0.0 for k in ops}
+    with ClockSampler(0) as clk:
+        clk.mark()
+        for i in range(args.steps):
+            for k, f in ops.items():
+                flush.zero_()
+                a, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record()
+                f()
+                e.record()
+                e.synchronize()
+                per_op[k] += a.elapsed_time(e)
+        clk.mark(end=True)
+    launches = L.atlb_kernel_launches() - launches0
+    per_op = {k: v / args.steps for k, v in per_op.items()}
+    ms = sum(per_op.values())
+    npts = pos.shape[0]
+    peak, peak_kind = measured_peak()
+    print(json.dumps({
+        "metric": "tiled bilinear ops (splat fwd+bwd, gather fwd+bwd, voxel grid) points/s", "value": npts / (ms / 1000),
+        "unit": "points/s", "n_gpus": 1, "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"tiles: {B} window(s) x {n} points, 640x480, voxel bins {C}",
+                   "l2": "flushed (256 MB write) before every op"},
+        "ops_ms": per_op,
+        "ops_gbs_of_algorithmic_bytes": {k: npts * per_pt[k] / (v / 1000) / 1e9 for k, v in per_op.items()},
+        "hbm_peak_gbs": peak, "peak_source": peak_kind,
+        "gpu_launches": int(launches), "clocks": clk.summary(),
+    }))
+
+
 # ------------------------------------------------------------------------------------------------ config 3
 def config3_arm(args):
     """Configuration 3: AnchoredSliced(n_slices=10, sigma=1.5) + Bezier PixelTrajectories (K = 10 control
@@ -917,6 +984,8 @@ def main():
         config5_arm(args)
     elif args.workload == "splat":
         splat_arm(args)
+    elif args.workload == "tiles":
+        tiles_arm(args)
     elif args.workload == "config3":
         config3_arm(args)
     else:

@@ -74,14 +74,14 @@ __device__ __forceinline__ long long bil_tile(const BTiles& T, float x, float y,
 // The value stored with a point: its weight (w), the upstream gradient (g) or its time and polarity (voxel).
 __global__ void __launch_bounds__(kThreads) k_btile_count(BTiles T, const float2* __restrict__ P,
                                                           const long long* __restrict__ Bi, long long N,
-                                                          const float* __restrict__ skip_zero,
+                                                          long long chunk, const float* __restrict__ skip_zero,
                                                           int* __restrict__ counts) {
   extern __shared__ int hist[];
   const bool sm = T.ntiles <= kSmemTiles;
   if (sm)
     for (int i = threadIdx.x; i < T.ntiles; i += blockDim.x) hist[i] = 0;
   __syncthreads();
-  const long long n0 = blockIdx.x * kChunk, n1 = min(n0 + kChunk, N);
+  const long long n0 = blockIdx.x * chunk, n1 = min(n0 + chunk, N);
   for (long long n = n0 + threadIdx.x; n < n1; n += blockDim.x) {
     if (skip_zero && skip_zero[n] == 0.f) continue;
     const float2 p = P[n];
@@ -97,14 +97,14 @@ __global__ void __launch_bounds__(kThreads) k_btile_count(BTiles T, const float2
 // REC[slot] = (x, y, v0, v1): v0 = val0[n] (or 0), v1 = val1[n] (voxel) or the index bits.
 __global__ void __launch_bounds__(kThreads) k_btile_scatter(BTiles T, const float2* __restrict__ P,
                                                             const long long* __restrict__ Bi, long long N,
-                                                            const float* __restrict__ skip_zero,
+                                                            long long chunk, const float* __restrict__ skip_zero,
                                                             const float* __restrict__ val0,
                                                             const float* __restrict__ val1,
                                                             const int* __restrict__ start, int* __restrict__ cursor,
                                                             float4* __restrict__ REC) {
   extern __shared__ int hist[];
   const bool sm = T.ntiles <= kSmemTiles;
-  const long long n0 = blockIdx.x * kChunk, n1 = min(n0 + kChunk, N);
+  const long long n0 = blockIdx.x * chunk, n1 = min(n0 + chunk, N);
   if (sm) {
     for (int i = threadIdx.x; i < T.ntiles; i += blockDim.x) hist[i] = 0;
     __syncthreads();
@@ -489,13 +489,19 @@ inline size_t bucket_smem(const BTiles& T) { return T.ntiles <= kSmemTiles ? (si
 void bucket(const BTiles& T, const float* pos, const long long* b, long long N, const float* skip_zero,
             const float* val0, const float* val1, const TileWs& w, cudaStream_t s) {
   cudaMemsetAsync(w.counts, 0, (size_t)T.ntiles * 4, s);
-  const unsigned grid = (unsigned)((N + kChunk - 1) / kChunk);
+  // enough CTAs to fill the GPU (8 per SM), each with a contiguous chunk of at least kChunk / 16 points so its
+  // shared histogram is reused: with a fixed chunk of kChunk points a 1M-point call had 61 CTAs
+  long long grid_l = (N + kChunk / 16 - 1) / (kChunk / 16);
+  grid_l = grid_l < 148LL * 8 ? grid_l : 148LL * 8;
+  const unsigned grid = (unsigned)(grid_l > 0 ? grid_l : 1);
+  const long long chunk = (N + grid - 1) / grid;
   if (N > 0)
-    launch(k_btile_count, grid, kThreads, bucket_smem(T), s, T, (const float2*)pos, b, N, skip_zero, w.counts);
+    launch(k_btile_count, grid, kThreads, bucket_smem(T), s, T, (const float2*)pos, b, N, chunk, skip_zero,
+           w.counts);
   exclusive_scan<int>(w.counts, T.ntiles, w.partials, w.start, s);
   if (N > 0)
-    launch(k_btile_scatter, grid, kThreads, bucket_smem(T), s, T, (const float2*)pos, b, N, skip_zero, val0, val1,
-           (const int*)w.start, w.counts, w.rec);
+    launch(k_btile_scatter, grid, kThreads, bucket_smem(T), s, T, (const float2*)pos, b, N, chunk, skip_zero, val0,
+           val1, (const int*)w.start, w.counts, w.rec);
 }
 
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no link dependency on libcuda).
