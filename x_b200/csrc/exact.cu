@@ -605,6 +605,7 @@ struct ExactWs {
   float2* TI;
   int* acounts;
   int* astart;
+  long long* apartials;  // scan scratch of the anchor buckets (their scan runs on the second stream)
   float4* XT;
   int4* XK;      // (original index, plane, sub-cell row, sub-cell column) of the bucketed anchors
   int* slice_hist;
@@ -639,6 +640,7 @@ size_t ws_layout(long long N, long long M, long long ncell, long long S, long lo
   x.TI = (float2*)take((size_t)nent * 8);
   x.acounts = (int*)take((size_t)ncell * 4);
   x.astart = (int*)take((size_t)(ncell + 1) * 4);
+  x.apartials = (long long*)take(scan_partials_bytes(ncell));
   x.XT = (float4*)take((size_t)M * 16);
   x.XK = (int4*)take((size_t)M * 16);
   x.slice_hist = (int*)take((size_t)(B * n_check) * 4);
@@ -795,8 +797,10 @@ int exact_forward(const atlb_exact_cfg& c, const float* t, const long long* b, l
   PlanConsts P = make_plan_consts(g, c.tau, c.B);
   P.src0 = j0;
   P.src1 = j1;
-  // normaliser (window counts, exposure correction): depends on the prepared events and anchors only, so it
-  // runs on a second stream beside the plan build below
+  // slice centres: read by the anchor records and the pair kernels
+  launch(k_slice_centres, (unsigned)((c.B * g.S + 127) / 128), 128, 0, s, P, w.SC, w.SCg);
+  // the normaliser (window counts, exposure correction) and the anchor buckets depend on the prepared events
+  // and anchors only, so they run on a second stream beside the entry plan build below
   SideStream* side = side_stream();
   const cudaStream_t norm_s = side ? side->s : s;
   if (side) {
@@ -829,10 +833,16 @@ int exact_forward(const atlb_exact_cfg& c, const float* t, const long long* b, l
   if (M > 0)
     launch(k_exact_norm, grid_for(M), kThreads, 0, norm_s, Mv, K, (const float4*)anc4, anc_b, M, t, b, N,
            whole_batch ? (const long long*)w.bstart : nullptr, (const int*)w.slice_hist, den_out);
-  // slice centres, entries and anchors
-  launch(k_slice_centres, (unsigned)((c.B * g.S + 127) / 128), 128, 0, s, P, w.SC, w.SCg);
+  // anchors into sub-cells, each with its own pair value (second stream)
+  cudaMemsetAsync(w.acounts, 0, (size_t)ncell * 4, norm_s);
+  if (M > 0)
+    launch(k_fast_anchor_count, grid_for(M), kThreads, 0, norm_s, P, (const float4*)anc4, anc_b, M, w.acounts);
+  exclusive_scan<int>(w.acounts, ncell, w.apartials, w.astart, norm_s, /*cursors=*/true);
+  if (M > 0)
+    launch(k_fast_anchor_scatter, grid_for(M), kThreads, 0, norm_s, P, make_pair_consts(c.h, c.tau, c.cut),
+           (const float4*)anc4, anc_b, M, (const float4*)ev4, (const float*)w.SC, w.acounts, w.XT, w.XK);
+  // entries
   cudaMemsetAsync(w.counts, 0, (size_t)ncell * 4, s);
-  cudaMemsetAsync(w.acounts, 0, (size_t)ncell * 4, s);
   if (ns > 0) {  // source events in mid-slice cell order (see k_order_count)
     const long long nkey = c.B * g.GH * g.GW * kFine * kFine;  // mid-slice sub-cells
     const float4* ev = (const float4*)ev4 + j0;
@@ -843,16 +853,11 @@ int exact_forward(const atlb_exact_cfg& c, const float* t, const long long* b, l
     launch(k_fast_count_ordered, grid_for(ns), kThreads, 0, s, P, (const float4*)w.XVo, (const int4*)w.TBo,
            ns, w.counts, w.KEY);
   }
-  if (M > 0) launch(k_fast_anchor_count, grid_for(M), kThreads, 0, s, P, (const float4*)anc4, anc_b, M, w.acounts);
   exclusive_scan<int>(w.counts, ncell, w.partials, w.start, s);  // relative cursors: measured faster here
   if (ns > 0)
     launch(k_fast_scatter_ordered, grid_for(ns), kThreads, 0, s, P, (const float4*)w.XVo, (const int4*)w.TBo,
            ns, (const int*)w.KEY, (const int*)w.start, w.counts, w.YV, w.TI);
-  exclusive_scan<int>(w.acounts, ncell, w.partials, w.astart, s, /*cursors=*/true);
-  if (M > 0)
-    launch(k_fast_anchor_scatter, grid_for(M), kThreads, 0, s, P, make_pair_consts(c.h, c.tau, c.cut),
-           (const float4*)anc4, anc_b, M, (const float4*)ev4, (const float*)w.SC, w.acounts, w.XT, w.XK);
-  if (side) {  // the pair kernels below read den
+  if (side) {  // the pair kernels below read den and the anchor buckets
     cudaEventRecord(side->join, norm_s);
     cudaStreamWaitEvent(s, side->join, 0);
   }
