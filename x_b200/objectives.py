@@ -421,12 +421,23 @@ class AnchoredSliced(Objective):
         order = _spatial_order(motion, xs, b)
         if order is not None:  # the events in coefficient-tile order: neighbouring lanes share their samples
             xs, t, b, wsrc = xs[order], t[order], b[order], wsrc[:, order]
+            st["order"] = order  # kept for the anchors (_scores) with the gathered times and batch indices
+            st["in_order"] = {"t": t, "b": b}
         Y = self._events_at_centres(motion, xs, t, b, st["centres"])
         return splat_slices(Y, wsrc, b, B, ev.height, ev.width, self.sigma), per_kb
 
     def _scores(self, st: dict, motion, img, per_kb, counts, ai, ka):
         """Log scores of the anchors ``ai`` (slice ranks ``ka``) against the full density stack ``img`` and
         source counts ``per_kb``; ``counts``: the window's exposure-check slice counts."""
+        n = st["t"].shape[0]
+        if "order" in st and ai.numel() == n:
+            # every event is an anchor: evaluate them in the events' coefficient-tile order (the density's), and
+            # return them in the reference's order (ai)
+            order = st["order"]
+            pos = torch.empty_like(order)
+            pos[order] = torch.arange(n, device=order.device)
+            ls = self._scores_in_order(st, motion, img, per_kb, counts, order, st["rank"][order], reuse=True)
+            return ls.index_select(0, pos[ai])  # (its backward scatters without sorting)
         order = _spatial_order(motion, st["xsm"][ai], st["b"][ai])
         if order is not None:  # evaluated in coefficient-tile order, returned in the reference's order
             inv = torch.empty_like(order)
@@ -435,9 +446,13 @@ class AnchoredSliced(Objective):
             return ls.index_select(0, inv)  # (its backward scatters without sorting)
         return self._scores_in_order(st, motion, img, per_kb, counts, ai, ka)
 
-    def _scores_in_order(self, st: dict, motion, img, per_kb, counts, ai, ka):
+    def _scores_in_order(self, st: dict, motion, img, per_kb, counts, ai, ka, reuse: bool = False):
         ev, B, xs, xsm = st["ev"], st["ev"].batch_size, st["xs"], st["xsm"]
-        xa, ta, ba, ca = xsm[ai], st["t"][ai], st["b"][ai], st["centres"][ka]
+        if reuse:  # ai is the density's event order: its times and batch indices are gathered already
+            ta, ba = st["in_order"]["t"], st["in_order"]["b"]
+        else:
+            ta, ba = st["t"][ai], st["b"][ai]
+        xa, ca = xsm[ai], st["centres"][ka]
         # anchor records at their slice centres: [x +- d e_x, x +- d e_y,] a [, unsmoothed copy], the probes
         # x + (d, 0), x - (d, 0), x + (0, d), x - (0, d) of Motion.transport_logdet (atl/motion/base.py:43-50,
         # d = 0.5) made with one broadcast add
