@@ -478,25 +478,21 @@ __global__ void __launch_bounds__(kThreads) k_exact_ls(const float* __restrict__
 
 
 // dL/dS in bucket order from the upstream dL/dls (torch's LogBackward then DivBackward).
-// The backward's anchor records in bucket order: AB = (x, y, t - c_s, t - c_s) and GT = (dL/dS / h^2, t), with
-// dL/dS = dL/dls / (eps + S / den) / den (the Log then Div backward of ls = log(eps + S / den)) (s = the anchor's slice, as in anchor_cell).
-__global__ void __launch_bounds__(kThreads) k_exact_gs_records(PlanConsts P, const float4* __restrict__ XT,
+// The backward's anchor records in bucket order: AB = (x, y, t, dL/dS / h^2), with
+// dL/dS = dL/dls / (eps + S / den) / den (the Log then Div backward of ls = log(eps + S / den)).
+__global__ void __launch_bounds__(kThreads) k_exact_gs_records(const float4* __restrict__ XT,
                                                                const int4* __restrict__ XK, long long M,
                                                                const float* __restrict__ grad_ls,
                                                                const float* __restrict__ S,
                                                                const float* __restrict__ den, float eps, float invh2,
-                                                               const float* __restrict__ SC,
-                                                               float4* __restrict__ AB, float2* __restrict__ GT) {
+                                                               float4* __restrict__ AB) {
   const long long stride = (long long)gridDim.x * blockDim.x;
   for (long long p = blockIdx.x * (long long)blockDim.x + threadIdx.x; p < M; p += stride) {
     const int i = XK[p].x;
     const float q = div_rn(S[i], den[i]);
     const float g = div_rn(div_rn(grad_ls[i], add_rn(eps, q)), den[i]);
     const float4 a = XT[p];
-    const int sa = (int)clampf(floorf(div_rn(a.z, P.delta_f)), 0.f, (float)(P.S - 1));
-    const float dts = sub_rn(a.z, SC[sa]);
-    AB[p] = make_float4(a.x, a.y, dts, dts);
-    GT[p] = make_float2(g * invh2, a.z);
+    AB[p] = make_float4(a.x, a.y, a.z, g * invh2);
   }
 }
 
@@ -613,8 +609,7 @@ struct ExactWs {
   float* SCg;    // slice centre of every plane (B S)
   long long* bstart;  // first event of each batch (B + 1)
   int* KEY;      // cell key of each (slice, source event) of the count pass, -1 = no entry
-  float4* AB;    // backward anchor records (x, y, t - c_s, t), bucket order
-  float2* GT;    // (dL/dS / h^2, t), bucket order
+  float4* AB;    // backward anchor records (x, y, t, dL/dS / h^2), bucket order
   int* ocount;   // events per mid-slice cell (B*GH*GW), then the order cursor
   int* ostart;
   float4* XVo;   // events in spatial order: (x, y, vx, vy)
@@ -649,7 +644,6 @@ size_t ws_layout(long long N, long long M, long long ncell, long long S, long lo
   x.bstart = (long long*)take((size_t)(B + 1) * 8);
   x.KEY = (int*)take((size_t)nent * 4);
   x.AB = (float4*)take((size_t)M * 16);
-  x.GT = (float2*)take((size_t)M * 8);
   x.ocount = (int*)take((size_t)nkey * 4);
   x.ostart = (int*)take((size_t)(nkey + 1) * 4);
   x.XVo = (float4*)take((size_t)N * 16);
@@ -900,17 +894,17 @@ int exact_backward(const atlb_exact_cfg& c, const float* grad_ls, const long lon
   const PairConsts C = make_pair_consts(c.h, c.tau, c.cut);
   if (M > 0 && ncell > 0) {
     const PlanConsts P = make_plan_consts(g, c.tau, c.B);
-    launch(k_exact_gs_records, grid_for(M), kThreads, 0, s, P, (const float4*)w.XT, (const int4*)w.XK, M, grad_ls, S,
-           den, eps, C.invh2, (const float*)w.SC, w.AB, w.GT);
+    launch(k_exact_gs_records, grid_for(M), kThreads, 0, s, (const float4*)w.XT, (const int4*)w.XK, M, grad_ls, S,
+           den, eps, C.invh2, w.AB);
     const FineConsts F = fine_consts(c, g, P);
     const int nrows = (int)(c.B * g.S * g.GH);  // plan cell rows of all planes
     const dim3 grid((unsigned)((g.GW + kBwdWarps - 1) / kBwdWarps), (unsigned)min(nrows, 65535));
     cudaEvent_t e0 = timing_begin(s);
     if (tau_covers(g, c.tau))
-      launch(k_pair_bwd_fine<true>, grid, kBwdWarps * 32, 0, s, E, (const float4*)w.AB, (const float2*)w.GT,
+      launch(k_pair_bwd_fine<true>, grid, kBwdWarps * 32, 0, s, E, (const float4*)w.AB, (const float*)w.SCg,
              (const int*)w.astart, (const int*)w.start, F, (int)g.GW, nrows, C, N, gv);
     else
-      launch(k_pair_bwd_fine<false>, grid, kBwdWarps * 32, 0, s, E, (const float4*)w.AB, (const float2*)w.GT,
+      launch(k_pair_bwd_fine<false>, grid, kBwdWarps * 32, 0, s, E, (const float4*)w.AB, (const float*)w.SCg,
              (const int*)w.astart, (const int*)w.start, F, (int)g.GW, nrows, C, N, gv);
     timing_end("k_pair_bwd", s, e0);
   }

@@ -196,23 +196,24 @@ __global__ void __launch_bounds__(kFwdWarps * 32, 12) k_pair_fwd_fine(FastEntrie
 // copied into the warp's shared memory and padded to a multiple of 4 with far-away records that no test
 // accepts, so the lanes -- one entry each, or several per entry for a short last chunk -- walk it 4 at a time
 // without bounds checks.  Grid: x = groups of kBwdWarps cells of a cell row, y = cell rows of all planes
-// (grid-stride).  AB = (x, y, t - c_s, t - c_s), GT = (dL/dS / h^2, t) in anchor bucket order.
+// (grid-stride).  AB = (x, y, t, dL/dS / h^2) in anchor bucket order.
 constexpr int kBwdList = 128;  // anchor records a warp holds at a time
 
 // Gradient of one entry over the anchors i = g, g + G, ... of the padded list (na a multiple of 4 when G = 1).
+// ab[i] = (x, y, t, dL/dS / h^2); cs = the centre of the plane's slice, so t - c_s is the value the anchor
+// records of the forward hold (the same rounded difference).
 template <bool TAU_ALL, bool STRIDED>
-__device__ __forceinline__ float2 bwd_entry_fine(const float4* ab, const float2* gt, int na, f32x2 y, f32x2 v,
-                                                 float st, int g, int G, float r2max, float k2, float tau) {
+__device__ __forceinline__ float2 bwd_entry_fine(const float4* ab, int na, f32x2 y, f32x2 v, float st, float cs,
+                                                 int g, int G, float r2max, float k2, float tau) {
   float gx = 0.f, gy = 0.f;
   auto one = [&](int i) {
-    const float4 a = ab[i];  // (x, y, t - c_s, t - c_s)
-    const float2 q = gt[i];  // (dL/dS / h^2, t)
+    const float4 a = ab[i];
     float2 rr;
-    const float d2 = residual2(pk2(a.x, a.y), pk2(a.z, a.w), y, v, &rr);
-    const float dt = sub_rn(q.y, st);
+    const float d2 = residual2s(pk2(a.x, a.y), sub_rn(a.z, cs), y, v, &rr);
+    const float dt = sub_rn(a.z, st);
     bool ok = !(d2 > r2max);
     if (!TAU_ALL) ok = ok && !(fabsf(dt) > tau);
-    const float f = ok ? q.x * ex2_approx(-d2 * k2) * dt : 0.f;  // gS k dt / h^2
+    const float f = ok ? a.w * ex2_approx(-d2 * k2) * dt : 0.f;  // gS k dt / h^2
     gx = fmaf(f, rr.x, gx);
     gy = fmaf(f, rr.y, gy);
   };
@@ -231,19 +232,17 @@ __device__ __forceinline__ float2 bwd_entry_fine(const float4* ab, const float2*
 
 template <bool TAU_ALL>
 __global__ void __launch_bounds__(kBwdWarps * 32, 6) k_pair_bwd_fine(FastEntries E, const float4* __restrict__ AB,
-                                                                     const float2* __restrict__ GT,
+                                                                     const float* __restrict__ SCg,
                                                                      const int* __restrict__ astart,
                                                                      const int* __restrict__ cstart, FineConsts F,
                                                                      int GW, int nrows, PairConsts C, long long N,
                                                                      float* __restrict__ gv) {
   __shared__ float4 s_ab[kBwdWarps][kBwdList];
-  __shared__ float2 s_gt[kBwdWarps][kBwdList];
   __shared__ int s_row[kBwdWarps][2][kMaxWinRows];  // per window row: first flat index, first bucket position
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const int cx = blockIdx.x * kBwdWarps + w;
   if (cx >= GW) return;  // warp-uniform; no CTA-wide barrier follows
   float4* ab = s_ab[w];
-  float2* gt = s_gt[w];
   int* rex = s_row[w][0];
   int* rlo = s_row[w][1];
   const float r2max = C.r2max, k2 = C.k2, tau = C.tau;
@@ -252,6 +251,7 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 6) k_pair_bwd_fine(FastEntries
   for (int crow = blockIdx.y; crow < nrows; crow += gridDim.y) {  // crow = g * GH + cy
     const int cy = crow % GHc;
     const int prow = (crow - cy) * kFine;  // the plane's first sub-cell row
+    const float cs = __ldg(SCg + crow / GHc);  // the plane's slice centre
     const int fys = cy * kFine;             // the cell's first sub-cell row
     // the cell's entries: kFine ranges (its sub-cell rows), flattened
     int elo = 0, elen = 0;
@@ -316,10 +316,8 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 6) k_pair_bwd_fine(FastEntries
           for (int q = 1; q < kMaxWinRows; ++q) rsel += f >= rex[q] ? 1 : 0;
           const int p = rlo[rsel] + (f - rex[rsel]);
           ab[i] = __ldg(AB + p);
-          gt[i] = __ldg(GT + p);
-        } else {  // padding: a residual of ~1e30 fails the test, and 0 * 1e30 adds nothing
+        } else {  // padding: a residual of ~1e30 fails the test, and its dL/dS is 0
           ab[i] = make_float4(1e30f, 1e30f, 0.f, 0.f);
-          gt[i] = make_float2(0.f, 0.f);
         }
       }
       __syncwarp();
@@ -338,9 +336,10 @@ __global__ void __launch_bounds__(kBwdWarps * 32, 6) k_pair_bwd_fine(FastEntries
         E.load(k, sy, sv, st, sid);
         float2 gr;
         if (big) {
-          gr = bwd_entry_fine<TAU_ALL, false>(ab, gt, na4, pk2(sy.x, sy.y), pk2(sv.x, sv.y), st, 0, 1, r2max, k2, tau);
+          gr = bwd_entry_fine<TAU_ALL, false>(ab, na4, pk2(sy.x, sy.y), pk2(sv.x, sv.y), st, cs, 0, 1, r2max, k2,
+                                              tau);
         } else {
-          gr = bwd_entry_fine<TAU_ALL, true>(ab, gt, valid ? na : 0, pk2(sy.x, sy.y), pk2(sv.x, sv.y), st, gsub, G,
+          gr = bwd_entry_fine<TAU_ALL, true>(ab, valid ? na : 0, pk2(sy.x, sy.y), pk2(sv.x, sv.y), st, cs, gsub, G,
                                              r2max, k2, tau);
           for (int d = 1; d < G; d <<= 1) {
             const float ox = __shfl_down_sync(0xffffffffu, gr.x, d), oy = __shfl_down_sync(0xffffffffu, gr.y, d);

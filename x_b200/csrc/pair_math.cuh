@@ -97,5 +97,14 @@ __device__ __forceinline__ float residual2(f32x2 xi, f32x2 dti2, f32x2 y, f32x2 
   const float2 sq = upk2(mul2(rr, rr));
   return add_rn(sq.x, sq.y);
 }
+// The same with the time difference dti as one scalar.
+__device__ __forceinline__ float residual2s(f32x2 xi, float dti, f32x2 y, f32x2 v, float2* r) {
+  const float2 vv = upk2(v);
+  const f32x2 vd = pk2(__fmul_rn(vv.x, dti), __fmul_rn(vv.y, dti));
+  const f32x2 rr = sub2(xi, add2(y, vd));
+  *r = upk2(rr);
+  const float2 sq = upk2(mul2(rr, rr));
+  return add_rn(sq.x, sq.y);
+}
 
 }  // namespace atlb
