@@ -228,8 +228,8 @@ int atlb_visible_fraction(int kind, const float* theta, int64_t B, int64_t Hg, i
  *          exp(lgamma(K+1) - lgamma(k+1) - lgamma(K-k+1)) as the reference computes them in fp32)
  *   the coefficients at p are the bilinear (border-clamped) sample at (p - offset) / tile; the origin is
  *   the fixed point of p = x - d(p, t) after n_fp iterations; t_dst (N) per event, or NULL for t_dst_s.
- * K <= 16 and n_fp <= 16.  Events with b outside [0, B) get NaN.  The backward ADDS dL/dcoeff (same
- * layout) for gy = dL/dout into gcoeff.
+ * K <= 16, n_fp <= 16 and B Hq Wq 2K < 2^31 floats.  Events with b outside [0, B) get NaN.  The
+ * backward ADDS dL/dcoeff (same layout) for gy = dL/dout into gcoeff.
  * ---------------------------------------------------------------------------------------------- */
 /* mode 0: out = transport(xy, t -> t_dst); 1: out = the origin p (the fixed point; t_dst unused);
  * 2: xy holds origins, out = p + d(p, t_dst) (t unused); 3: out = the first coefficient pair (c_x1, c_y1)

@@ -609,7 +609,7 @@ int atlb_exact_backward(const atlb_exact_cfg* cfg, const float* grad_ls, const i
 static int make_traj(const float* coeff, int64_t B, int64_t Hq, int64_t Wq, int64_t K, int basis, const float* bc,
                      double offset, double tile, int64_t n_fp, TrajView* V, const char* fn) {
   if (!coeff || B < 1 || Hq < 1 || Wq < 1 || K < 1 || K > kTrajKMax || n_fp < 0 || n_fp > kTrajKMax ||
-      !(tile > 0) || (basis != 0 && basis != 1) || (basis == 1 && !bc) || B * Hq * Wq * 2 * K > (1LL << 40)) {
+      !(tile > 0) || (basis != 0 && basis != 1) || (basis == 1 && !bc) || B * Hq * Wq * 2 * K >= (1LL << 31)) {
     set_error("%s: invalid trajectory grid (B %lld, %lld x %lld, K %lld, basis %d, n_fp %lld, tile %g)", fn,
               (long long)B, (long long)Hq, (long long)Wq, (long long)K, basis, (long long)n_fp, tile);
     return ATLB_ERR_ARG;

@@ -42,7 +42,7 @@ __device__ __forceinline__ void traj_basis(const TrajView& V, float t, float (&g
 }
 
 struct Taps {
-  long long base[4];  // offsets of the four taps (channels-last)
+  int base[4];  // element offsets of the four taps (channels-last; the grid holds < 2^31 floats)
   float w[4];         // bilinear weights (1-ax)(1-ay), ax(1-ay), (1-ax)ay, ax ay
   float ax, ay;
   bool gx_in, gy_in;  // inside the clamp range (the clamp passes gradient)
@@ -59,11 +59,11 @@ __device__ __forceinline__ Taps traj_taps(const TrajView& V, int b, float px, fl
   T.ax = sub_rn(gx, x0);
   T.ay = sub_rn(gy, y0);
   const int ix0 = (int)x0, iy0 = (int)y0, ix1 = min(ix0 + 1, V.Wq - 1), iy1 = min(iy0 + 1, V.Hq - 1);
-  const long long C2 = 2LL * V.K, plane = (long long)b * V.Hq * V.Wq;
-  T.base[0] = (plane + (long long)iy0 * V.Wq + ix0) * C2;
-  T.base[1] = (plane + (long long)iy0 * V.Wq + ix1) * C2;
-  T.base[2] = (plane + (long long)iy1 * V.Wq + ix0) * C2;
-  T.base[3] = (plane + (long long)iy1 * V.Wq + ix1) * C2;
+  const int C2 = 2 * V.K, plane = b * V.Hq * V.Wq;
+  T.base[0] = (plane + iy0 * V.Wq + ix0) * C2;
+  T.base[1] = (plane + iy0 * V.Wq + ix1) * C2;
+  T.base[2] = (plane + iy1 * V.Wq + ix0) * C2;
+  T.base[3] = (plane + iy1 * V.Wq + ix1) * C2;
   const float oax = sub_rn(1.f, T.ax), oay = sub_rn(1.f, T.ay);
   T.w[0] = mul_rn(oax, oay);
   T.w[1] = mul_rn(T.ax, oay);
@@ -133,7 +133,7 @@ __device__ __forceinline__ float2 traj_disp(const TrajView& V, const Taps& T, co
 // the cell changes.  Every kernel iterates with this function, so a backward that solves the iterates
 // again, and the records / targets kernels, reproduce the forward's iterates exactly.
 struct CellDisp {
-  long long base0;     // first tap of the cell whose sums are held; -1: none
+  int base0;           // first tap of the cell whose sums are held; -1: none
   float dx[4], dy[4];  // per tap q: D_q for the x and the y channels
 };
 
@@ -279,7 +279,7 @@ __device__ __forceinline__ float2 traj_jt_it(const TrajView& V, const Taps& T, c
 // a_q = sum_i w_q u_i (basis of the origin iterations) and f_q (basis of the final sample) are kept; they are
 // flushed as g_k a_q + gd_k f_q into the 2K channels of each tap (vector reds) when the cell changes.
 struct CellAcc {
-  long long base[4];
+  int base[4];
   float a[4][2], f[4][2];  // [tap][x, y]
   bool live;
 };
@@ -483,7 +483,9 @@ __global__ void __launch_bounds__(kTThreads) k_traj_records_fwd(TrajView V, int 
   }
 }
 
-template <int K>
+// STORED: the forward's iterates are read back from `iters` inside the reverse loop (no per-thread array of
+// iterates, which would live in local memory); otherwise the iterates are solved again into such an array.
+template <int K, bool STORED>
 __global__ void __launch_bounds__(kTThreads, 3) k_traj_records_bwd(TrajView V, int R, const float2* __restrict__ gy,
                                                                 const float2* __restrict__ xy,
                                                                 const float* __restrict__ t,
@@ -507,32 +509,46 @@ __global__ void __launch_bounds__(kTThreads, 3) k_traj_records_bwd(TrajView V, i
       traj_basis<K>(V, t[n], g);
       traj_basis<K>(V, tdst ? tdst[n] : tdst_s, gd);
       const float2 x = xy[i];
-      float P[kTrajKMax + 1][2];
-      P[0][0] = x.x;
-      P[0][1] = x.y;
       CellDisp D;
       D.base0 = -1;
-      for (int it = 0; it < V.n_fp; ++it) {
-        if (iters) {  // the forward's iterates
-          const float2 q = iters[(long long)it * NR + i];
-          P[it + 1][0] = q.x;
-          P[it + 1][1] = q.y;
-          continue;
+      if constexpr (STORED) {
+        // iterate k (k = 1..n_fp) sits at iters[(k - 1) NR + i]; iterate 0 is x
+        const float2 pn = V.n_fp > 0 ? iters[(long long)(V.n_fp - 1) * NR + i] : x;
+        const Taps T = traj_taps(V, bb, pn.x, pn.y);
+        acc_add<K>(A, T, true, u.x, u.y, g, gd, gC);
+        const float2 jt = traj_jt<K>(V, T, gd, u.x, u.y);
+        float gpx = u.x + jt.x, gpy = u.y + jt.y;
+        float2 p = V.n_fp > 1 ? iters[(long long)(V.n_fp - 2) * NR + i] : x;
+        for (int it = V.n_fp - 1; it >= 0; --it) {
+          // the next (earlier) iterate is loaded before this one's work
+          const float2 pnext = it > 1 ? iters[(long long)(it - 2) * NR + i] : x;
+          const Taps Ti = traj_taps(V, bb, p.x, p.y);
+          acc_add<K>(A, Ti, false, -gpx, -gpy, g, gd, gC);
+          const float2 j = traj_jt_it<K>(V, Ti, g, D, -gpx, -gpy);
+          gpx = j.x;
+          gpy = j.y;
+          p = pnext;
         }
-        const float2 d = traj_disp_it<K>(V, traj_taps(V, bb, P[it][0], P[it][1]), g, D);
-        P[it + 1][0] = sub_rn(x.x, d.x);
-        P[it + 1][1] = sub_rn(x.y, d.y);
-      }
-      const Taps T = traj_taps(V, bb, P[V.n_fp][0], P[V.n_fp][1]);
-      acc_add<K>(A, T, true, u.x, u.y, g, gd, gC);
-      const float2 jt = traj_jt<K>(V, T, gd, u.x, u.y);
-      float gpx = u.x + jt.x, gpy = u.y + jt.y;
-      for (int it = V.n_fp - 1; it >= 0; --it) {
-        const Taps Ti = traj_taps(V, bb, P[it][0], P[it][1]);
-        acc_add<K>(A, Ti, false, -gpx, -gpy, g, gd, gC);
-        const float2 j = traj_jt_it<K>(V, Ti, g, D, -gpx, -gpy);
-        gpx = j.x;
-        gpy = j.y;
+      } else {
+        float P[kTrajKMax + 1][2];
+        P[0][0] = x.x;
+        P[0][1] = x.y;
+        for (int it = 0; it < V.n_fp; ++it) {
+          const float2 d = traj_disp_it<K>(V, traj_taps(V, bb, P[it][0], P[it][1]), g, D);
+          P[it + 1][0] = sub_rn(x.x, d.x);
+          P[it + 1][1] = sub_rn(x.y, d.y);
+        }
+        const Taps T = traj_taps(V, bb, P[V.n_fp][0], P[V.n_fp][1]);
+        acc_add<K>(A, T, true, u.x, u.y, g, gd, gC);
+        const float2 jt = traj_jt<K>(V, T, gd, u.x, u.y);
+        float gpx = u.x + jt.x, gpy = u.y + jt.y;
+        for (int it = V.n_fp - 1; it >= 0; --it) {
+          const Taps Ti = traj_taps(V, bb, P[it][0], P[it][1]);
+          acc_add<K>(A, Ti, false, -gpx, -gpy, g, gd, gC);
+          const float2 j = traj_jt_it<K>(V, Ti, g, D, -gpx, -gpy);
+          gpx = j.x;
+          gpy = j.y;
+        }
       }
     }
     // runs of neighbouring lanes with the same event and the same open cell add up their per-tap sums
@@ -806,8 +822,12 @@ int traj_records_bwd(const TrajView& V, int R, const float* gy, const float* xy,
     cudaEvent_t e0 = timing_begin(s);
     dispatch_k(V.K, [&](auto kc) {
       constexpr int K = decltype(kc)::value;
-      launch(k_traj_records_bwd<K>, tgrid(N * R), kTThreads, 0, s, V, R, (const float2*)gy, (const float2*)xy, t,
-             tdst, tdst_s, b, N, (const float2*)iters, gC);
+      if (iters)
+        launch(k_traj_records_bwd<K, true>, tgrid(N * R), kTThreads, 0, s, V, R, (const float2*)gy,
+               (const float2*)xy, t, tdst, tdst_s, b, N, (const float2*)iters, gC);
+      else
+        launch(k_traj_records_bwd<K, false>, tgrid(N * R), kTThreads, 0, s, V, R, (const float2*)gy,
+               (const float2*)xy, t, tdst, tdst_s, b, N, (const float2*)nullptr, gC);
     });
     timing_end("k_traj_records_bwd", s, e0);
   }
