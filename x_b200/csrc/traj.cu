@@ -451,7 +451,7 @@ __global__ void __launch_bounds__(kTThreads) k_traj_vis(TrajView V, const float2
 // sums of neighbouring lanes of one event and one coefficient cell (segmented shuffle reduction) before a
 // single lane flushes them.
 template <int K>
-__global__ void __launch_bounds__(kTThreads) k_traj_records_fwd(TrajView V, int R, const float2* __restrict__ xy,
+__global__ void __launch_bounds__(kTThreads, 4) k_traj_records_fwd(TrajView V, int R, const float2* __restrict__ xy,
                                                                 const float* __restrict__ t,
                                                                 const float* __restrict__ tdst, float tdst_s,
                                                                 const long long* __restrict__ b, long long N,
