@@ -623,6 +623,10 @@ static int make_traj(const float* coeff, int64_t B, int64_t Hq, int64_t Wq, int6
   V->basis = basis;
   V->offset = (float)offset;
   V->tile = (float)tile;
+  volatile float one = 1.f;  // an fp32 division on the host: RN(1 / tile), the device's 1.f / tile
+  V->rtile = one / V->tile;
+  int e2 = 0;
+  V->tile_pow2 = std::frexp(V->tile, &e2) == 0.5f ? 1 : 0;
   for (int k = 0; k < kTrajKMax; ++k) V->bc[k] = (basis == 1 && k < K) ? bc[k] : 0.f;
   return ATLB_OK;
 }

@@ -50,7 +50,10 @@ struct Taps {
 
 __device__ __forceinline__ Taps traj_taps(const TrajView& V, int b, float px, float py) {
   Taps T;
-  const float gxr = div_rn(sub_rn(px, V.offset), V.tile), gyr = div_rn(sub_rn(py, V.offset), V.tile);
+  // (p - offset) / tile; for a power-of-two tile the product with its reciprocal is the same number
+  const float ox = sub_rn(px, V.offset), oy = sub_rn(py, V.offset);
+  const float gxr = V.tile_pow2 ? mul_rn(ox, V.rtile) : div_rn(ox, V.tile);
+  const float gyr = V.tile_pow2 ? mul_rn(oy, V.rtile) : div_rn(oy, V.tile);
   const float wq = (float)(V.Wq - 1), hq = (float)(V.Hq - 1);
   T.gx_in = gxr >= 0.f && gxr <= wq;
   T.gy_in = gyr >= 0.f && gyr <= hq;
@@ -235,7 +238,7 @@ __device__ __forceinline__ float2 traj_jt_u(const TrajView& V, const Taps& T, co
     jx += dwx[q] * sq;
     jy += dwy[q] * sq;
   }
-  const float sx = T.gx_in ? 1.f / V.tile : 0.f, sy = T.gy_in ? 1.f / V.tile : 0.f;
+  const float sx = T.gx_in ? V.rtile : 0.f, sy = T.gy_in ? V.rtile : 0.f;
   return make_float2(jx * sx, jy * sy);
 }
 
@@ -270,7 +273,7 @@ __device__ __forceinline__ float2 traj_jt_it(const TrajView& V, const Taps& T, c
     jx += dwx[q] * sq;
     jy += dwy[q] * sq;
   }
-  const float sx = T.gx_in ? 1.f / V.tile : 0.f, sy = T.gy_in ? 1.f / V.tile : 0.f;
+  const float sx = T.gx_in ? V.rtile : 0.f, sy = T.gy_in ? V.rtile : 0.f;
   return make_float2(jx * sx, jy * sy);
 }
 
