@@ -631,8 +631,8 @@ size_t ws_layout(long long N, long long M, long long ncell, long long S, long lo
   x.counts = (int*)take((size_t)ncell * 4);
   x.start = (int*)take((size_t)(ncell + 1) * 4);
   x.partials = (long long*)take(scan_partials_bytes(ncell));
-  x.YV = (float4*)take((size_t)nent * 16);
-  x.TI = (float2*)take((size_t)nent * 8);
+  x.YV = (float4*)take((size_t)(nent + kFwdPad) * 16);  // padding: read, never used, by k_pair_fwd_fine
+  x.TI = (float2*)take((size_t)(nent + kFwdPad) * 8);
   x.acounts = (int*)take((size_t)ncell * 4);
   x.astart = (int*)take((size_t)(ncell + 1) * 4);
   x.apartials = (long long*)take(scan_partials_bytes(ncell));

@@ -63,24 +63,27 @@ __device__ __forceinline__ float fwd_candidate(const FastEntries& E, int k, f32x
   const float kv = ex2_approx(-d2 * C.k2);
   return ok ? kv : 0.f;
 }
-// The same without a branch: k is clamped to a valid entry (kmax = Ns - 1 >= 0) and the value masked by on.
+// The same without a branch: the value of k is masked by on.  k may run up to kFwdPad - 1 entries past the
+// last entry; the entry arrays carry kFwdPad entries of padding, so the load stays in the buffer.
 template <bool TAU_ALL>
-__device__ __forceinline__ float fwd_candidate_masked(const FastEntries& E, int k, bool on, int kmax, f32x2 axy,
-                                                      f32x2 adt2, float at, const PairConsts& C) {
-  const int kk = min(k, kmax);
-  const float4 e = E.yv(kk);
+__device__ __forceinline__ float fwd_candidate_masked(const FastEntries& E, int k, bool on, f32x2 axy, f32x2 adt2,
+                                                      float at, const PairConsts& C) {
+  const float4 e = E.yv(k);
   float2 rr;
   const float d2 = residual2(axy, adt2, pk2(e.x, e.y), pk2(e.z, e.w), &rr);
   bool ok = on && !(d2 > C.r2max);
-  if (!TAU_ALL) ok = ok && !(fabsf(sub_rn(at, E.t(kk))) > C.tau);
+  if (!TAU_ALL) ok = ok && !(fabsf(sub_rn(at, E.t(k))) > C.tau);
   const float kv = ex2_approx(-d2 * C.k2);
   return ok ? kv : 0.f;
 }
 
 constexpr int kFwdLanes = 8;  // lanes per anchor (measured against 16 and 32 at configuration 2: fastest)
 constexpr int kFwdPerWarp = 32 / kFwdLanes;
+constexpr int kFwdPad = 32;   // entries of padding after the entry arrays: the predicated chunks of a row read
+                              // up to 4 x kFwdLanes - 1 entries past its end
 
-// Grid: (sub-cell tiles along x, tiles along y, planes g = b * S + s).  Ns >= 1 (the caller skips empty plans).
+// Grid: (sub-cell tiles along x, tiles along y, planes g = b * S + s).  Ns >= 1 (the caller skips empty plans);
+// the entry arrays hold at least Ns + kFwdPad entries.
 template <bool TAU_ALL>
 __global__ void __launch_bounds__(kFwdWarps * 32, 12) k_pair_fwd_fine(FastEntries E, const float4* __restrict__ XT,
                                                                   const int4* __restrict__ XK,
@@ -94,7 +97,6 @@ __global__ void __launch_bounds__(kFwdWarps * 32, 12) k_pair_fwd_fine(FastEntrie
   const int nx = min(kFwdTileX, F.GWf - fx0), ny = min(kFwdTileY, F.GHf - fy0);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int grp = lane / kFwdLanes, lg = lane % kFwdLanes;
-  const int kmax = Ns - 1;
   if (warp == 0) {  // the tile's anchors: one contiguous bucket range per sub-cell row
     int lo = 0, len = 0;
     if (lane < ny) {
@@ -172,16 +174,19 @@ __global__ void __launch_bounds__(kFwdWarps * 32, 12) k_pair_fwd_fine(FastEntrie
     float acc = 0.f;
     for (int r = 0; r < rmax; ++r) {  // warp-uniform
       const int src = grp * kFwdLanes + (r % kFwdLanes);
-      int l = __shfl_sync(0xffffffffu, lo[0], src), h = __shfl_sync(0xffffffffu, hi[0], src);
-      if (kFwdLanes < kMaxWinRows) {
-        const int l2 = __shfl_sync(0xffffffffu, lo[1], src), h2 = __shfl_sync(0xffffffffu, hi[1], src);
-        if (r >= kFwdLanes) { l = l2; h = h2; }
+      int l, h;
+      if (kFwdLanes < kMaxWinRows && r >= kFwdLanes) {  // warp-uniform: rows past the group's lanes
+        l = __shfl_sync(0xffffffffu, lo[1], src);
+        h = __shfl_sync(0xffffffffu, hi[1], src);
+      } else {
+        l = __shfl_sync(0xffffffffu, lo[0], src);
+        h = __shfl_sync(0xffffffffu, hi[0], src);
       }
       constexpr int kChunks = 32 / kFwdLanes;  // predicated chunks of kFwdLanes entries, then a loop for longer rows
       int k = l + lg;
 #pragma unroll
       for (int c = 0; c < kChunks; ++c, k += kFwdLanes)
-        acc += fwd_candidate_masked<TAU_ALL>(E, k, k < h, kmax, axy, adt2, a.z, C);
+        acc += fwd_candidate_masked<TAU_ALL>(E, k, k < h, axy, adt2, a.z, C);
       for (; k < h; k += kFwdLanes) acc += fwd_candidate<TAU_ALL>(E, k, axy, adt2, a.z, C);
     }
 #pragma unroll
