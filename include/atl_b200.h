@@ -38,7 +38,7 @@ enum {
 const char* atlb_last_error(void);
 /* ABI version of this header (bumped on incompatible changes). */
 int atlb_abi_version(void);
-#define ATLB_ABI_VERSION 11
+#define ATLB_ABI_VERSION 12
 /* Number of kernels this library has launched in the calling process (instrumentation; no reference
  * counterpart). */
 uint64_t atlb_kernel_launches(void);
@@ -344,6 +344,17 @@ int atlb_exact_forward(const atlb_exact_cfg* cfg, const float* t, const int64_t*
                        const float* ev4, const float* anc4, const int64_t* anc_b, const atlb_plan_geom* geom,
                        void* workspace, size_t workspace_bytes, float* S_out, float* den_out, float* ls_out,
                        atlb_stream_t stream);
+/* atlb_exact_prepare then atlb_exact_forward in one call, for a caller that sized the workspace ahead (for
+ * instance from the previous window's atlb_exact_workspace_bytes): the forward's kernels follow the geometry
+ * read-back with no return to the caller in between, so the device does not wait on the caller's code there.
+ * If the workspace is smaller than this window's plan needs, the prepare outputs (ev4, anc4, anc_b, geom_out)
+ * are written and ATLB_ERR_WORKSPACE is returned: size the workspace from geom_out and call
+ * atlb_exact_forward.  Replaces the same steps of AnchoredExact.log_scores (atl/objectives/ats.py:75-96). */
+int atlb_exact_prepare_forward(const atlb_exact_cfg* cfg, const float* xy, const float* u, const float* t,
+                               const int64_t* b, int64_t N, const int64_t* anchors, const float* z, int64_t M,
+                               float* ev4, float* anc4, int64_t* anc_b, void* scratch, atlb_plan_geom* geom_out,
+                               void* workspace, size_t workspace_bytes, float* S_out, float* den_out, float* ls_out,
+                               atlb_stream_t stream);
 int atlb_exact_backward(const atlb_exact_cfg* cfg, const float* grad_ls, const int64_t* b, int64_t N, int64_t M,
                         const float* ev4, const atlb_plan_geom* geom, void* workspace, size_t workspace_bytes,
                         const float* S, const float* den, float* gv, float* gtheta, atlb_stream_t stream);

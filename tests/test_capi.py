@@ -33,7 +33,7 @@ def test_binding_covers_header_exactly():
 
 def test_abi_version_and_counter():
     L = _lib.load_library()
-    assert L.atlb_abi_version() == 11
+    assert L.atlb_abi_version() == 12
     assert L.atlb_kernel_launches() >= 0
 
 

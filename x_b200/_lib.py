@@ -114,6 +114,8 @@ _SIGS = {
                                   ctypes.POINTER(PlanGeom), _vp, _size, _vp, _vp, _vp, _vp]),
     "atlb_exact_backward": (_int, [ctypes.POINTER(ExactCfg), _vp, _vp, _i64, _i64, _vp, ctypes.POINTER(PlanGeom), _vp,
                                    _size, _vp, _vp, _vp, _vp, _vp]),
+    "atlb_exact_prepare_forward": (_int, [ctypes.POINTER(ExactCfg), _vp, _vp, _vp, _vp, _i64, _vp, _vp, _i64, _vp,
+                                          _vp, _vp, _vp, ctypes.POINTER(PlanGeom), _vp, _size, _vp, _vp, _vp, _vp]),
 }
 
 _LIB = None

@@ -588,6 +588,23 @@ int atlb_exact_forward(const atlb_exact_cfg* cfg, const float* t, const int64_t*
                        STREAM(stream));
 }
 
+int atlb_exact_prepare_forward(const atlb_exact_cfg* cfg, const float* xy, const float* u, const float* t,
+                               const int64_t* b, int64_t N, const int64_t* anchors, const float* z, int64_t M,
+                               float* ev4, float* anc4, int64_t* anc_b, void* scratch, atlb_plan_geom* geom_out,
+                               void* workspace, size_t workspace_bytes, float* S_out, float* den_out, float* ls_out,
+                               atlb_stream_t stream) {
+  if (int st = atlb_exact_prepare(cfg, xy, u, t, b, N, anchors, z, M, ev4, anc4, anc_b, scratch, geom_out, stream))
+    return st;
+  // the forward's kernels are launched right after the geometry read-back, with no return to the caller between
+  if (!workspace || workspace_bytes < exact_workspace_bytes(*cfg, N, M, *geom_out)) {
+    set_error("atlb_exact_prepare_forward: workspace too small for this window's plan (prepared; size it with "
+              "atlb_exact_workspace_bytes and call atlb_exact_forward)");
+    return ATLB_ERR_WORKSPACE;
+  }
+  return atlb_exact_forward(cfg, t, b, N, M, ev4, anc4, anc_b, geom_out, workspace, workspace_bytes, S_out, den_out,
+                            ls_out, stream);
+}
+
 int atlb_exact_backward(const atlb_exact_cfg* cfg, const float* grad_ls, const int64_t* b, int64_t N, int64_t M,
                         const float* ev4, const atlb_plan_geom* geom, void* workspace, size_t workspace_bytes,
                         const float* S, const float* den, float* gv, float* gtheta, atlb_stream_t stream) {

@@ -96,6 +96,11 @@ def visible_fraction(motion, xa, ta, ba, ev: EventPacket, tau: float, n_check: i
     return (vis / tot.clamp(min=1)).clamp(min=1e-3)
 
 
+# Workspace bytes for the fused pipeline's next window, per (device, motion kind, B, H, W, slices): the last
+# window's need and a little slack.
+_WS_HINT: dict = {}
+
+
 class _FusedExact(torch.autograd.Function):
     """AnchoredExact.log_scores (ats.py:84-96) as one libatlb200 pipeline (atlb_exact_*), differentiable
     w.r.t. the motion parameters."""
@@ -121,18 +126,31 @@ class _FusedExact(torch.autograd.Function):
         anc4 = torch.empty(M, 4, dtype=torch.float32, device=dev)
         anc_b = torch.empty(M, dtype=torch.int64, device=dev)
         scratch = torch.empty(64, dtype=torch.uint8, device=dev)
-        geom = L.PlanGeom()
-        L.check(lib.atlb_exact_prepare(ctypes.byref(cfg), L.ptr(xyc), L.ptr(uc), L.ptr(tc), L.ptr(bc), N, L.ptr(anc),
-                                       L.ptr(zc), M, L.ptr(ev4), L.ptr(anc4), L.ptr(anc_b), L.ptr(scratch),
-                                       ctypes.byref(geom), L.stream()), "exact_prepare")
-        nb = lib.atlb_exact_workspace_bytes(ctypes.byref(cfg), N, M, ctypes.byref(geom))
-        ws = L.workspace(nb, dev)
         Sv = torch.empty(M, dtype=torch.float32, device=dev)
         den = torch.empty(M, dtype=torch.float32, device=dev)
         ls = torch.empty(M, dtype=torch.float32, device=dev)
-        L.check(lib.atlb_exact_forward(ctypes.byref(cfg), L.ptr(tc), L.ptr(bc), N, M, L.ptr(ev4), L.ptr(anc4),
-                                       L.ptr(anc_b), ctypes.byref(geom), L.ptr(ws), nb, L.ptr(Sv), L.ptr(den),
-                                       L.ptr(ls), L.stream()), "exact_forward")
+        geom = L.PlanGeom()
+        # The plan's workspace depends on the window's geometry, known only after the prepare kernels.  A workspace
+        # sized from the previous window of this kind lets prepare and forward run as one call (no return to Python
+        # between the geometry read-back and the forward's kernels); a short one falls back to two calls.
+        key = (dev.index, kind, B, H, W, S)
+        hint = _WS_HINT.get(key, 0)
+        ws = L.workspace(hint, dev) if hint else None
+        st = lib.atlb_exact_prepare_forward(ctypes.byref(cfg), L.ptr(xyc), L.ptr(uc), L.ptr(tc), L.ptr(bc), N,
+                                            L.ptr(anc), L.ptr(zc), M, L.ptr(ev4), L.ptr(anc4), L.ptr(anc_b),
+                                            L.ptr(scratch), ctypes.byref(geom), L.ptr(ws), hint, L.ptr(Sv),
+                                            L.ptr(den), L.ptr(ls), L.stream())
+        nb = hint
+        if st in (L.ATLB_OK, L.ATLB_ERR_WORKSPACE):
+            need = lib.atlb_exact_workspace_bytes(ctypes.byref(cfg), N, M, ctypes.byref(geom))
+            _WS_HINT[key] = need + need // 32  # this window's size and a little slack for the next one
+            if st == L.ATLB_ERR_WORKSPACE:
+                nb = _WS_HINT[key]
+                ws = L.workspace(nb, dev)
+                st = lib.atlb_exact_forward(ctypes.byref(cfg), L.ptr(tc), L.ptr(bc), N, M, L.ptr(ev4), L.ptr(anc4),
+                                            L.ptr(anc_b), ctypes.byref(geom), L.ptr(ws), nb, L.ptr(Sv), L.ptr(den),
+                                            L.ptr(ls), L.stream())
+        L.check(st, "exact_prepare_forward")
         ctx.save_for_backward(th, bc, ev4, ws, Sv, den)
         ctx.meta = (cfg, geom, nb, N, M, theta.dtype, tuple(theta.shape))
         ctx.S, ctx.den = Sv, den
