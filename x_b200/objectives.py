@@ -404,12 +404,21 @@ class AnchoredSliced(Objective):
         src = (t[None, :] - centres[:, None]).abs() <= torch.tensor(self.tau + delta / 2, dtype=t.dtype, device=dev)
         if source_mask is not None:
             src = src & cut(source_mask)[None, :]
+        # every event an anchor candidate of an evaluated slice: the anchors are all of them, no count needed
+        every = anchor_mask is None and Sp == S
         return dict(ev=ev, xy=xy, t=t, b=b, xs=xs, xsm=xsm, Sp=Sp, rank=rank, centres=centres, src=src,
-                    eps=self.eps_frac / (ev.height * ev.width))
+                    eps=self.eps_frac / (ev.height * ev.width), every=every)
 
     def _pick(self, st: dict):
         """Anchors (indices into the setup's events) and their slice ranks, in the reference's order."""
         Sp, rank, dev = st["Sp"], st["rank"], st["t"].device
+        if st.get("every") and self.nap is None:
+            # every slice evaluated, no anchor mask, no per-slice subsets: every event is an anchor, in slice order,
+            # so the step needs no per-slice counts on the host (and no synchronisation)
+            if rank.numel() == 0:
+                return None
+            rank_sorted, order = torch.sort(rank.to(torch.int32), stable=True)
+            return order, rank_sorted.long()
         n_anc = count_keys(rank, Sp).tolist()  # the one read-back of the step
         rank_sorted, order = torch.sort(rank.to(torch.int32), stable=True)  # 32-bit keys: a shorter radix sort
         rank_sorted = rank_sorted.long()
