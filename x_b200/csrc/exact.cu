@@ -746,6 +746,28 @@ static MotionView motion_of(const atlb_exact_cfg& c) {
   return make_motion_view(c.kind, c.theta, c.Bt, c.Hg, c.Wg, c.H, c.W);
 }
 
+// The prepare's read-back buffer: 64 bytes of pinned host memory per host thread, allocated on the thread's first
+// call and kept for the thread (null if pinned memory cannot be had: the caller then copies into its stack).  A
+// copy into pageable memory is staged by the driver and handed to the stream only once the stream reaches it;
+// into pinned memory it is an ordinary stream operation queued right behind the prepare kernels.
+static int* pinned_readback() {
+  thread_local struct Holder {
+    int* p = nullptr;
+    bool tried = false;
+    ~Holder() {
+      if (p) cudaFreeHost(p);  // at thread exit; an error during process teardown is of no consequence
+    }
+  } h;
+  if (!h.tried) {
+    h.tried = true;
+    if (cudaHostAlloc((void**)&h.p, 64, cudaHostAllocPortable) != cudaSuccess) {
+      cudaGetLastError();  // not sticky: clear it, the stack buffer is used instead
+      h.p = nullptr;
+    }
+  }
+  return h.p;
+}
+
 int exact_prepare(const atlb_exact_cfg& c, const float* xy, const float* u, const float* t, const long long* b,
                   long long N, const long long* anchors, const float* z, long long M, float* ev4, float* anc4,
                   long long* anc_b, void* scratch, atlb_plan_geom* geom, cudaStream_t s) {
@@ -760,8 +782,10 @@ int exact_prepare(const atlb_exact_cfg& c, const float* xy, const float* u, cons
   if (M > 0)
     launch(k_exact_anchors, grid_for(M), kThreads, 0, s, (const float4*)ev4, t, b, N, anchors, (const float2*)z,
            rng_z, K, (float)c.h, M, (float4*)anc4, anc_b, r);
-  int host[10];
-  if (cudaMemcpyAsync(host, r, sizeof(host), cudaMemcpyDeviceToHost, s) != cudaSuccess)
+  int stack_host[10];
+  int* pinned = pinned_readback();
+  int* host = pinned ? pinned : stack_host;
+  if (cudaMemcpyAsync(host, r, sizeof(stack_host), cudaMemcpyDeviceToHost, s) != cudaSuccess)
     return launch_status("exact_prepare copy");
   if (cudaStreamSynchronize(s) != cudaSuccess) return launch_status("exact_prepare sync");
   if (int st = launch_status("exact_prepare")) return st;
