@@ -53,7 +53,8 @@ __global__ void k_exact_init(int* r) {
 }
 
 // rng: u == NULL and rng set -> the dequantisation jitter is drawn on the device (stream 0 of rng.cuh)
-__global__ void __launch_bounds__(kThreads) k_exact_events(MotionView Mv, const float2* __restrict__ xy,
+// 5 CTAs per SM (51 registers, no spills; 4 at the uncapped 64): the kernel waits on its loads and the flow taps
+__global__ void __launch_bounds__(kThreads, 5) k_exact_events(MotionView Mv, const float2* __restrict__ xy,
                                                            const float2* __restrict__ u, const float* __restrict__ t,
                                                            const long long* __restrict__ b, long long N, long long B,
                                                            bool rng, RngKey K, float4* __restrict__ ev4, int* r) {
