@@ -54,20 +54,22 @@ __global__ void k_exact_init(int* r) {
 
 // rng: u == NULL and rng set -> the dequantisation jitter is drawn on the device (stream 0 of rng.cuh)
 // 5 CTAs per SM (51 registers, no spills; 4 at the uncapped 64): the kernel waits on its loads and the flow taps
+template <bool RNG>  // compiled with and without the device draw, which needs registers of its own
 __global__ void __launch_bounds__(kThreads, 5) k_exact_events(MotionView Mv, const float2* __restrict__ xy,
                                                            const float2* __restrict__ u, const float* __restrict__ t,
                                                            const long long* __restrict__ b, long long N, long long B,
-                                                           bool rng, RngKey K, float4* __restrict__ ev4, int* r) {
+                                                           RngKey K, float4* __restrict__ ev4, int* r) {
   float vm = 0.f;
   int unsorted = 0, badb = 0, tmn = 0x7fffffff, tmx = (int)0x80000000;
   const long long stride = (long long)gridDim.x * blockDim.x;
+#pragma unroll 1
   for (long long j = blockIdx.x * (long long)blockDim.x + threadIdx.x; j < N; j += stride) {
     const int ot = float_to_ordered(t[j]);
     tmn = min(tmn, ot);
     tmx = max(tmx, ot);
     float2 p = xy[j];
-    if (u || rng) {  // ats.py:84-85: xs = xy + (u - 0.5)
-      const float2 q = u ? u[j] : rng_uniform2(K, (unsigned long long)j);
+    if (u || RNG) {  // ats.py:84-85: xs = xy + (u - 0.5)
+      const float2 q = (RNG && !u) ? rng_uniform2(K, (unsigned long long)j) : u[j];
       p = make_float2(add_rn(p.x, sub_rn(q.x, 0.5f)), add_rn(p.y, sub_rn(q.y, 0.5f)));
     }
     const long long bj = b[j];
@@ -118,16 +120,18 @@ __global__ void __launch_bounds__(kThreads, 5) k_exact_events(MotionView Mv, con
   }
 }
 
+template <bool RNG>  // compiled with and without the device draw, as k_exact_events
 __global__ void __launch_bounds__(kThreads) k_exact_anchors(const float4* __restrict__ ev4,
                                                             const float* __restrict__ t,
                                                             const long long* __restrict__ b, long long N,
                                                             const long long* __restrict__ anchors,
-                                                            const float2* __restrict__ z, bool rng, RngKey K,
+                                                            const float2* __restrict__ z, RngKey K,
                                                             float h_f, long long M,
                                                             float4* __restrict__ anc4, long long* __restrict__ anc_b,
                                                             int* r) {
   int mnx = 0x7fffffff, mny = 0x7fffffff, mxx = (int)0x80000000, mxy = (int)0x80000000, bad = 0;
   const long long stride = (long long)gridDim.x * blockDim.x;
+#pragma unroll 1
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < M; i += stride) {
     const long long a = anchors ? anchors[i] : i;
     if (a < 0 || a >= N) {
@@ -138,8 +142,8 @@ __global__ void __launch_bounds__(kThreads) k_exact_anchors(const float4* __rest
     }
     const float4 e = ev4[a];
     float xa = e.x, ya = e.y;
-    if (z || rng) {  // ats.py:87-88: xa = xs[a] + h * z (z drawn on the device: stream 1 of rng.cuh)
-      const float2 q = z ? z[i] : rng_normal2(K, (unsigned long long)i);
+    if (z || RNG) {  // ats.py:87-88: xa = xs[a] + h * z (z drawn on the device: stream 1 of rng.cuh)
+      const float2 q = (RNG && !z) ? rng_normal2(K, (unsigned long long)i) : z[i];
       xa = add_rn(xa, mul_rn(h_f, q.x));
       ya = add_rn(ya, mul_rn(h_f, q.y));
     }
@@ -197,6 +201,7 @@ __global__ void __launch_bounds__(kThreads) k_order_count(PlanConsts P, const fl
                                                           const long long* __restrict__ b, long long N,
                                                           int* __restrict__ ocount) {
   const long long stride = (long long)gridDim.x * blockDim.x;
+#pragma unroll 1
   for (long long j = blockIdx.x * (long long)blockDim.x + threadIdx.x; j < N; j += stride)
     atomicAdd(ocount + order_key(P, ev4[j], t[j], (int)b[j]), 1);
 }
@@ -210,6 +215,7 @@ __global__ void __launch_bounds__(kThreads) k_order_scatter(PlanConsts P, const 
                                                             float4* __restrict__ XVo,
                                                             int4* __restrict__ TBo) {
   const long long stride = (long long)gridDim.x * blockDim.x;
+#pragma unroll 1
   for (long long j = blockIdx.x * (long long)blockDim.x + threadIdx.x; j < N; j += stride) {
     const float4 e = ev4[j];
     const float tj = t[j];
@@ -230,6 +236,7 @@ __global__ void __launch_bounds__(kThreads) k_fast_count_ordered(PlanConsts P, c
   const int lane = threadIdx.x & 31;
   const long long stride = (long long)gridDim.x * blockDim.x;
   const long long first = blockIdx.x * (long long)blockDim.x + (threadIdx.x & ~31);
+#pragma unroll 1
   for (long long i0 = first; i0 < N; i0 += stride) {  // warp-uniform loop
     const long long i = i0 + lane;
     const bool live = i < N;
@@ -268,6 +275,7 @@ __global__ void __launch_bounds__(kThreads) k_fast_scatter_ordered(PlanConsts P,
   const unsigned below = (1u << lane) - 1u;
   const long long stride = (long long)gridDim.x * blockDim.x;
   const long long first = blockIdx.x * (long long)blockDim.x + (threadIdx.x & ~31);
+#pragma unroll 1
   for (long long i0 = first; i0 < N; i0 += stride) {  // warp-uniform loop
     const long long i = i0 + lane;
     const bool live = i < N;
@@ -332,6 +340,7 @@ __global__ void __launch_bounds__(kThreads) k_fast_anchor_count(PlanConsts P, co
                                                                 const long long* __restrict__ anc_b, long long M,
                                                                 int* __restrict__ counts) {
   const long long stride = (long long)gridDim.x * blockDim.x;
+#pragma unroll 1
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < M; i += stride) {
     int g, fy, fx, cx, cy;
     const long long key = fast_anchor_key(P, anc4[i], anc_b[i], &g, &fy, &fx, &cx, &cy);
@@ -350,6 +359,7 @@ __global__ void __launch_bounds__(kThreads) k_fast_anchor_scatter(PlanConsts P, 
                                                                   int* __restrict__ cursor, float4* __restrict__ XT,
                                                                   int4* __restrict__ XK) {
   const long long stride = (long long)gridDim.x * blockDim.x;
+#pragma unroll 1
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < M; i += stride) {
     const float4 a = anc4[i];
     const long long ba = anc_b[i];
@@ -416,6 +426,7 @@ __device__ __forceinline__ float visible_fraction_tab(float2 v, float xa, float 
 __global__ void __launch_bounds__(kThreads) k_batch_bounds(const long long* __restrict__ b, long long N, long long B,
                                                            long long* __restrict__ bstart) {
   const long long stride = (long long)gridDim.x * blockDim.x;
+#pragma unroll 1
   for (long long j = blockIdx.x * (long long)blockDim.x + threadIdx.x; j <= N; j += stride) {
     const long long lo = j == 0 ? 0 : b[j - 1] + 1, hi = j == N ? B : b[j];
     for (long long k = lo; k <= hi && k <= B; ++k) bstart[k] = j;
@@ -440,6 +451,7 @@ __global__ void __launch_bounds__(kThreads) k_exact_norm(MotionView Mv, NormCons
   }
   __syncthreads();
   const long long stride = (long long)gridDim.x * blockDim.x;
+#pragma unroll 1
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < M; i += stride) {
     const float4 a = anc4[i];
     const int ai = __float_as_int(a.w);
@@ -473,6 +485,7 @@ __global__ void __launch_bounds__(kThreads) k_exact_norm(MotionView Mv, NormCons
 __global__ void __launch_bounds__(kThreads) k_exact_ls(const float* __restrict__ S, const float* __restrict__ den,
                                                        float eps, long long M, float* __restrict__ ls) {
   const long long stride = (long long)gridDim.x * blockDim.x;
+#pragma unroll 1
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < M; i += stride)
     ls[i] = logf(add_rn(eps, div_rn(S[i], den[i])));  // log(eps + S / den)
 }
@@ -488,6 +501,7 @@ __global__ void __launch_bounds__(kThreads) k_exact_gs_records(const float4* __r
                                                                const float* __restrict__ den, float eps, float invh2,
                                                                float4* __restrict__ AB) {
   const long long stride = (long long)gridDim.x * blockDim.x;
+#pragma unroll 1
   for (long long p = blockIdx.x * (long long)blockDim.x + threadIdx.x; p < M; p += stride) {
     const int i = XK[p].x;
     const float q = div_rn(S[i], den[i]);
@@ -507,6 +521,7 @@ __global__ void __launch_bounds__(kThreads) k_slice_hist(const float* __restrict
     for (long long i = threadIdx.x; i < nbins; i += blockDim.x) hist[i] = 0;
   __syncthreads();
   const long long stride = (long long)gridDim.x * blockDim.x;
+#pragma unroll 1
   for (long long j = blockIdx.x * (long long)blockDim.x + threadIdx.x; j < N; j += stride) {
     const long long bj = b[j];
     if (bj < 0 || bj >= B) continue;
@@ -535,6 +550,7 @@ __global__ void __launch_bounds__(kThreads) k_exact_vbwd_dense(MotionView Mv, co
                                                                float* __restrict__ ggrid) {
   const long long stride = (long long)gridDim.x * blockDim.x;
   const long long plane = Mv.Hg * Mv.Wg;
+#pragma unroll 1
   for (long long j = blockIdx.x * (long long)blockDim.x + threadIdx.x; j < N; j += stride) {
     const float2 g = gv[j];
     if ((g.x == 0.f && g.y == 0.f) || b[j] < 0 || b[j] >= Mv.B) continue;
@@ -570,6 +586,7 @@ __global__ void __launch_bounds__(kThreads) k_exact_vbwd_param(MotionView Mv, co
   // (B, 2|6) parameters after a warp reduction over runs of equal batch index
   const int np = Mv.kind == ATLB_MOTION_TRANSLATION ? 2 : 6;
   const long long stride = (long long)gridDim.x * blockDim.x;
+#pragma unroll 1
   for (long long j0 = blockIdx.x * (long long)blockDim.x; j0 < N; j0 += stride) {
     const long long j = j0 + threadIdx.x;
     float c[6] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
@@ -778,11 +795,11 @@ int exact_prepare(const atlb_exact_cfg& c, const float* xy, const float* u, cons
   const bool rng_u = (c.rng & 1) != 0, rng_z = (c.rng & 2) != 0;
   const RngKey K = make_rng_key(c.rng_seed, c.rng_call);
   if (N > 0)
-    launch(k_exact_events, grid_for(N), kThreads, 0, s, Mv, (const float2*)xy, (const float2*)u, t, b, N, c.B, rng_u,
-           K, (float4*)ev4, r);
+    launch(rng_u ? k_exact_events<true> : k_exact_events<false>, grid_for(N), kThreads, 0, s, Mv, (const float2*)xy,
+           (const float2*)u, t, b, N, c.B, K, (float4*)ev4, r);
   if (M > 0)
-    launch(k_exact_anchors, grid_for(M), kThreads, 0, s, (const float4*)ev4, t, b, N, anchors, (const float2*)z,
-           rng_z, K, (float)c.h, M, (float4*)anc4, anc_b, r);
+    launch(rng_z ? k_exact_anchors<true> : k_exact_anchors<false>, grid_for(M), kThreads, 0, s, (const float4*)ev4, t,
+           b, N, anchors, (const float2*)z, K, (float)c.h, M, (float4*)anc4, anc_b, r);
   int stack_host[10];
   int* pinned = pinned_readback();
   int* host = pinned ? pinned : stack_host;
